@@ -1,0 +1,415 @@
+// The C ABI: contexts, workspace, error reporting, and the orchestration of one MoE layer.
+//
+// cwx_moe_forward is the resident branch of StreamedMoe::forward
+// (crates/engine/src/experts.rs:2562-2614) plus SharedExpert::forward
+// (crates/engine/src/model_next.rs:731-741): router logits, route, piles, gate/up products with
+// the activation, down products, weighted combine, shared expert, optional residual
+// (model_next.rs:1437). Everything is stream-ordered; nothing synchronises.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "cwx_common.cuh"
+#include "kernels.cuh"
+
+namespace cwx {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+}
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return e == cudaErrorMemoryAllocation ? CWX_ENOMEM : CWX_ECUDA;
+}
+
+// Bump allocator over the context workspace.
+struct Carve {
+    uint8_t* base;
+    size_t off;
+    template <typename T>
+    T* take(size_t count) {
+        off = (off + 255) & ~(size_t)255;
+        T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+        off += count * sizeof(T);
+        return p;
+    }
+};
+
+static int ensure_ws(cwx_ctx* ctx, size_t bytes, cudaStream_t st) {
+    if (bytes <= ctx->ws_bytes) return CWX_OK;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cap);
+    if (cap != cudaStreamCaptureStatusNone)
+        return fail(CWX_EINVAL, "workspace too small during stream capture: call cwx_ctx_reserve first");
+    size_t nb = ((bytes + (1 << 20) - 1) >> 20) << 20;  // 1 MB rounding, as the reference arena does
+    if (ctx->ws) {
+        cudaError_t e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) return cuda_fail(e, "workspace grow");
+        cudaFree(ctx->ws);
+        ctx->ws = nullptr;
+        ctx->ws_bytes = 0;
+    }
+    CWX_CUDA(cudaMalloc(&ctx->ws, nb));
+    ctx->ws_bytes = nb;
+    return CWX_OK;
+}
+
+static int act_mode_of(const cwx_bank* b, int policy) { return act_mode_for(b->L.fmt, policy); }
+
+struct LayerPlan {
+    int H, E, K, I, Is, T;
+    int mgu, msgu, md, msd;  // activation modes
+    // workspace pointers
+    float* logits;
+    float* sgate;
+    uint32_t* ids;
+    float* w;
+    uint32_t* heads;
+    uint32_t* pairs;
+    uint32_t* used3;
+    uint32_t* n_used;
+    uint32_t* perm;
+    __half* xh[3];
+    __half* xl[3];
+    float* h;
+    float* hs;
+    __half *hh, *hl, *hsh, *hsl;
+    float* y;
+    float* ys;
+    size_t bytes;
+};
+
+static int validate_layer(const cwx_moe_layer* L) {
+    if (!L) return fail(CWX_EINVAL, "cwx_moe_forward: null layer");
+    if (!L->router_w || !L->gate || !L->up || !L->down) return fail(CWX_EINVAL, "cwx_moe_forward: missing router or expert bank");
+    if (L->top_k < 1 || L->top_k > 16 || L->top_k > L->n_experts)
+        return fail(CWX_EINVAL, "cwx_moe_forward: top_k %d out of range (1..16, <= experts)", L->top_k);
+    if (L->n_experts < 1 || L->n_experts > 1024) return fail(CWX_EUNSUPPORTED, "cwx_moe_forward: %d experts (max 1024)", L->n_experts);
+    const Layout &g = L->gate->L, &u = L->up->L, &d = L->down->L;
+    if (g.n != L->inter || g.k != L->hidden || u.n != L->inter || u.k != L->hidden || d.n != L->hidden || d.k != L->inter)
+        return fail(CWX_EINVAL, "cwx_moe_forward: bank shapes do not match hidden=%d inter=%d", L->hidden, L->inter);
+    if (g.n_experts != L->n_experts || u.n_experts != L->n_experts || d.n_experts != L->n_experts)
+        return fail(CWX_EINVAL, "cwx_moe_forward: banks hold a different number of experts than %d", L->n_experts);
+    if (L->hidden % 64 || L->inter % 64) return fail(CWX_EUNSUPPORTED, "cwx_moe_forward: hidden and inter must be multiples of 64");
+    if (act_mode_of(L->gate, L->act_mode) != act_mode_of(L->up, L->act_mode))
+        return fail(CWX_EUNSUPPORTED, "cwx_moe_forward: gate and up need different activation quantisation");
+    if (L->sh_gate || L->sh_up || L->sh_down) {
+        if (!L->sh_gate || !L->sh_up || !L->sh_down || !L->sh_gate_inp)
+            return fail(CWX_EINVAL, "cwx_moe_forward: incomplete shared expert");
+        const Layout &sg = L->sh_gate->L, &su = L->sh_up->L, &sd = L->sh_down->L;
+        if (sg.k != L->hidden || su.k != L->hidden || sg.n != su.n || sd.n != L->hidden || sd.k != sg.n ||
+            sg.n_experts != 1 || su.n_experts != 1 || sd.n_experts != 1)
+            return fail(CWX_EINVAL, "cwx_moe_forward: shared expert shapes do not match");
+        if (sg.n % 64) return fail(CWX_EUNSUPPORTED, "cwx_moe_forward: shared inter must be a multiple of 64");
+        if (act_mode_of(L->sh_gate, L->act_mode) != act_mode_of(L->sh_up, L->act_mode))
+            return fail(CWX_EUNSUPPORTED, "cwx_moe_forward: shared gate and up need different activation quantisation");
+    }
+    if (L->act != CWX_ACT_SILU && L->act != CWX_ACT_CLAMPED_SWIGLU) return fail(CWX_EINVAL, "cwx_moe_forward: unknown act %d", L->act);
+    return CWX_OK;
+}
+
+static void plan_layer(const cwx_moe_layer* L, int T, uint8_t* base, LayerPlan* p) {
+    p->H = L->hidden;
+    p->E = L->n_experts;
+    p->K = L->top_k;
+    p->I = L->inter;
+    p->Is = L->sh_gate ? (int)L->sh_gate->L.n : 0;
+    p->T = T;
+    p->mgu = act_mode_of(L->gate, L->act_mode);
+    p->md = act_mode_of(L->down, L->act_mode);
+    p->msgu = L->sh_gate ? act_mode_of(L->sh_gate, L->act_mode) : -1;
+    p->msd = L->sh_down ? act_mode_of(L->sh_down, L->act_mode) : -1;
+    int64_t n = (int64_t)T * p->K;
+    Carve c{base, 0};
+    p->logits = c.take<float>((size_t)T * p->E);
+    p->sgate = c.take<float>((size_t)T + 1);
+    p->ids = c.take<uint32_t>((size_t)n + 1);
+    p->w = c.take<float>((size_t)n + 1);
+    p->heads = c.take<uint32_t>((size_t)3 * p->E);
+    p->pairs = c.take<uint32_t>((size_t)n + 1);
+    p->used3 = c.take<uint32_t>((size_t)3 * p->E);
+    p->n_used = c.take<uint32_t>(4);
+    p->perm = c.take<uint32_t>(perm_scratch_bytes(n, p->E) / 4);
+    for (int m = 0; m < 3; ++m) {
+        bool need = (m == p->mgu) || (m == p->msgu);
+        p->xh[m] = need ? c.take<__half>((size_t)T * p->H) : nullptr;
+        p->xl[m] = need ? c.take<__half>((size_t)T * p->H) : nullptr;
+    }
+    p->h = c.take<float>((size_t)n * p->I);
+    p->hh = c.take<__half>((size_t)n * p->I);
+    p->hl = c.take<__half>((size_t)n * p->I);
+    p->hs = c.take<float>((size_t)T * p->Is);
+    p->hsh = c.take<__half>((size_t)T * p->Is);
+    p->hsl = c.take<__half>((size_t)T * p->Is);
+    p->y = c.take<float>((size_t)n * p->H);
+    p->ys = c.take<float>((size_t)T * p->H);
+    p->bytes = c.off + 256;
+}
+
+}  // namespace cwx
+
+using namespace cwx;
+
+extern "C" const char* cwx_last_error(void) { return g_err; }
+extern "C" int cwx_version(void) { return 1; }
+
+extern "C" int cwx_ctx_create(int device, cwx_ctx** out) {
+    if (!out) return fail(CWX_EINVAL, "cwx_ctx_create: null output pointer");
+    *out = nullptr;
+    int ndev = 0;
+    CWX_CUDA(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(CWX_EINVAL, "cwx_ctx_create: device %d of %d", device, ndev);
+    CWX_CUDA(cudaSetDevice(device));
+    cwx_ctx* c = new cwx_ctx();
+    memset(c, 0, sizeof *c);
+    c->device = device;
+    cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
+    cudaError_t e = cudaMalloc(&c->d_err, 16);
+    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, 16);
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "cwx_ctx_create");
+    }
+    *out = c;
+    return CWX_OK;
+}
+
+extern "C" int cwx_ctx_destroy(cwx_ctx* c) {
+    if (!c) return CWX_OK;
+    cudaSetDevice(c->device);
+    if (c->ws) cudaFree(c->ws);
+    if (c->d_err) cudaFree(c->d_err);
+    if (c->d_iq3s_map) cudaFree(c->d_iq3s_map);
+    if (c->d_iq2s_map) cudaFree(c->d_iq2s_map);
+    delete c;
+    return CWX_OK;
+}
+
+extern "C" int cwx_ctx_status(cwx_ctx* c, void* stream) {
+    if (!c) return fail(CWX_EINVAL, "cwx_ctx_status: null context");
+    CWX_CUDA(cudaSetDevice(c->device));
+    CWX_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    int h = 0;
+    CWX_CUDA(cudaMemcpy(&h, c->d_err, 4, cudaMemcpyDeviceToHost));
+    if (h == DE_OK) return CWX_OK;
+    CWX_CUDA(cudaMemset(c->d_err, 0, 4));
+    if (h == DE_TIMEOUT) return fail(CWX_ETIMEOUT, "a device-side wait gave up (bulk copy did not complete)");
+    if (h == DE_BAD_ID) return fail(CWX_EDEVICE, "an expert id was out of range");
+    return fail(CWX_EDEVICE, "device error %d", h);
+}
+
+extern "C" int cwx_ctx_reserve(cwx_ctx* c, const void* layer, int32_t tokens) {
+    if (!c || !layer) return fail(CWX_EINVAL, "cwx_ctx_reserve: null argument");
+    const cwx_moe_layer* L = (const cwx_moe_layer*)layer;
+    int rc = validate_layer(L);
+    if (rc) return rc;
+    CWX_CUDA(cudaSetDevice(c->device));
+    LayerPlan p;
+    plan_layer(L, tokens, nullptr, &p);
+    return ensure_ws(c, p.bytes, 0);
+}
+
+extern "C" int cwx_route(cwx_ctx* c, const float* logits, int32_t T, int32_t E, int32_t K, int32_t norm, uint32_t* ids,
+                         float* w, void* stream) {
+    if (!c || (!logits && T) || (!ids && T) || (!w && T)) return fail(CWX_EINVAL, "cwx_route: null argument");
+    if (T < 0 || E < 1 || E > 1024) return fail(CWX_EINVAL, "cwx_route: %d experts (1..1024)", E);
+    if (K < 1 || K > 16 || K > E) return fail(CWX_EINVAL, "cwx_route: top_k %d (1..16, <= experts)", K);
+    CWX_CUDA(cudaSetDevice(c->device));
+    return launch_route(logits, T, E, K, norm, ids, w, nullptr, nullptr, 0, nullptr, (cudaStream_t)stream);
+}
+
+extern "C" int cwx_permute(cwx_ctx* c, const uint32_t* ids, int32_t T, int32_t K, int32_t E, uint32_t* pairs,
+                           uint32_t* heads, void* stream) {
+    if (!c || (!ids && T) || !heads || (!pairs && T)) return fail(CWX_EINVAL, "cwx_permute: null argument");
+    if (T < 0 || K < 1 || E < 1 || E > 12288) return fail(CWX_EINVAL, "cwx_permute: bad sizes");
+    CWX_CUDA(cudaSetDevice(c->device));
+    cudaStream_t st = (cudaStream_t)stream;
+    int64_t n = (int64_t)T * K;
+    Carve cv{nullptr, 0};
+    cv.take<uint32_t>((size_t)3 * E);
+    cv.take<uint32_t>(4);
+    cv.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
+    int rc = ensure_ws(c, cv.off + 256, st);
+    if (rc) return rc;
+    Carve w{c->ws, 0};
+    uint32_t* used3 = w.take<uint32_t>((size_t)3 * E);
+    uint32_t* n_used = w.take<uint32_t>(4);
+    uint32_t* scratch = w.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
+    return launch_permute(ids, n, E, pairs, heads, used3, n_used, scratch, c->d_err, st);
+}
+
+static MatRef mref(const cwx_bank* b) { return MatRef{b ? b->d : nullptr, b ? b->L : Layout{}}; }
+
+extern "C" int cwx_expert_matmul(cwx_ctx* c, const cwx_bank* bank, const float* x, int32_t rows_per_expert,
+                                 const uint32_t* ids, int32_t tokens, int32_t nei0, int32_t act_mode, float* out,
+                                 void* stream) {
+    if (!c || !bank || (tokens && (!x || !ids || !out))) return fail(CWX_EINVAL, "cwx_expert_matmul: null argument");
+    if (tokens < 0 || nei0 < 1) return fail(CWX_EINVAL, "cwx_expert_matmul: bad sizes tokens=%d nei0=%d", tokens, nei0);
+    if (bank->L.k % 64 || bank->L.n % 16)
+        return fail(CWX_EUNSUPPORTED, "cwx_expert_matmul: k must be a multiple of 64 and n of 16 (k=%lld n=%lld)",
+                    (long long)bank->L.k, (long long)bank->L.n);
+    if (bank->L.n_experts > 12288) return fail(CWX_EUNSUPPORTED, "cwx_expert_matmul: too many experts");
+    if (tokens == 0) return CWX_OK;
+    CWX_CUDA(cudaSetDevice(c->device));
+    cudaStream_t st = (cudaStream_t)stream;
+    int E = (int)bank->L.n_experts;
+    int64_t n = (int64_t)tokens * nei0;
+    int64_t xrows = rows_per_expert ? n : tokens;
+    int64_t K = bank->L.k;
+    int mode = act_mode_of(bank, act_mode);
+    Carve cv{nullptr, 0};
+    cv.take<uint32_t>((size_t)n);
+    cv.take<uint32_t>((size_t)3 * E);
+    cv.take<uint32_t>((size_t)3 * E);
+    cv.take<uint32_t>(4);
+    cv.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
+    cv.take<__half>((size_t)(xrows * K));
+    cv.take<__half>((size_t)(xrows * K));
+    int rc = ensure_ws(c, cv.off + 256, st);
+    if (rc) return rc;
+    Carve w{c->ws, 0};
+    uint32_t* pairs = w.take<uint32_t>((size_t)n);
+    uint32_t* heads = w.take<uint32_t>((size_t)3 * E);
+    uint32_t* used3 = w.take<uint32_t>((size_t)3 * E);
+    uint32_t* n_used = w.take<uint32_t>(4);
+    uint32_t* scratch = w.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
+    __half* xh = w.take<__half>((size_t)(xrows * K));
+    __half* xl = w.take<__half>((size_t)(xrows * K));
+    if ((rc = launch_permute(ids, n, E, pairs, heads, used3, n_used, scratch, c->d_err, st))) return rc;
+    if ((rc = launch_prep(x, xrows, K, mode, xh, xl, st))) return rc;
+    GemvArgs a;
+    memset(&a, 0, sizeof a);
+    a.two = 0;
+    a.ra = mref(bank);
+    a.rbh = xh;
+    a.rbl = xl;
+    a.r_bstride = K;
+    a.r_bdiv = rows_per_expert ? 1 : nei0;
+    a.rout = out;
+    a.r_ostride = bank->L.n;
+    a.pairs = pairs;
+    a.used3 = used3;
+    a.n_used = n_used;
+    a.err = c->d_err;
+    int64_t tiles = (bank->L.n + TILE_ROWS - 1) / TILE_ROWS;
+    int64_t max_items = tiles * (n < E ? n : E);
+    return launch_gemv(a, max_items, c->device, c->sm_count, st);
+}
+
+extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, void* stream) {
+    if (!c || !A) return fail(CWX_EINVAL, "cwx_moe_forward: null argument");
+    int rc = validate_layer(L);
+    if (rc) return rc;
+    int T = A->tokens;
+    if (T < 0) return fail(CWX_EINVAL, "cwx_moe_forward: tokens %d", T);
+    if (T == 0) return CWX_OK;
+    if (!A->x || !A->out) return fail(CWX_EINVAL, "cwx_moe_forward: null x or out");
+    CWX_CUDA(cudaSetDevice(c->device));
+    cudaStream_t st = (cudaStream_t)stream;
+    LayerPlan p;
+    plan_layer(L, T, nullptr, &p);
+    if ((rc = ensure_ws(c, p.bytes, st))) return rc;
+    plan_layer(L, T, c->ws, &p);
+    const int H = p.H, E = p.E, K = p.K, I = p.I, Is = p.Is;
+    const int64_t n = (int64_t)T * K;
+    const bool shared = L->sh_gate != nullptr;
+
+    if ((rc = launch_router(A->x, L->router_w, L->router_b, T, H, E, p.logits, st))) return rc;
+    if ((rc = launch_route(p.logits, T, E, K, L->norm_topk_prob, p.ids, p.w, A->x, shared ? L->sh_gate_inp : nullptr,
+                           H, shared ? p.sgate : nullptr, st)))
+        return rc;
+    if ((rc = launch_permute(p.ids, n, E, p.pairs, p.heads, p.used3, p.n_used, p.perm, c->d_err, st))) return rc;
+    for (int m = 0; m < 3; ++m)
+        if (p.xh[m] && (rc = launch_prep(A->x, T, H, m, p.xh[m], p.xl[m], st))) return rc;
+
+    // gate/up (+ activation): routed piles and the shared expert's tiles in one launch
+    GemvArgs a;
+    memset(&a, 0, sizeof a);
+    a.two = 1;
+    a.ra = mref(L->gate);
+    a.rb = mref(L->up);
+    a.rbh = p.xh[p.mgu];
+    a.rbl = p.xl[p.mgu];
+    a.r_bstride = H;
+    a.r_bdiv = K;
+    a.rout = p.h;
+    a.r_ostride = I;
+    a.pairs = p.pairs;
+    a.used3 = p.used3;
+    a.n_used = p.n_used;
+    a.has_shared = shared;
+    if (shared) {
+        a.sa = mref(L->sh_gate);
+        a.sb = mref(L->sh_up);
+        a.sbh = p.xh[p.msgu];
+        a.sbl = p.xl[p.msgu];
+        a.s_bstride = H;
+        a.sout = p.hs;
+        a.s_ostride = Is;
+        a.s_count = T;
+    }
+    a.act = L->act;
+    a.alpha = L->alpha;
+    a.limit = L->limit;
+    a.gate_b = L->gate_b;
+    a.up_b = L->up_b;
+    a.err = c->d_err;
+    int64_t used_max = n < E ? n : E;
+    int64_t max_items = ((I + TILE_ROWS - 1) / TILE_ROWS) * used_max + (shared ? (Is + TILE_ROWS - 1) / TILE_ROWS : 0);
+    if ((rc = launch_gemv(a, max_items, c->device, c->sm_count, st))) return rc;
+
+    if ((rc = launch_prep(p.h, n, I, p.md, p.hh, p.hl, st))) return rc;
+    if (shared && (rc = launch_prep(p.hs, T, Is, p.msd, p.hsh, p.hsl, st))) return rc;
+
+    // down
+    GemvArgs d;
+    memset(&d, 0, sizeof d);
+    d.two = 0;
+    d.ra = mref(L->down);
+    d.rbh = p.hh;
+    d.rbl = p.hl;
+    d.r_bstride = I;
+    d.r_bdiv = 1;
+    d.rout = p.y;
+    d.r_ostride = H;
+    d.pairs = p.pairs;
+    d.used3 = p.used3;
+    d.n_used = p.n_used;
+    d.has_shared = shared;
+    if (shared) {
+        d.sa = mref(L->sh_down);
+        d.sbh = p.hsh;
+        d.sbl = p.hsl;
+        d.s_bstride = Is;
+        d.sout = p.ys;
+        d.s_ostride = H;
+        d.s_count = T;
+    }
+    d.act = L->act;
+    d.down_b = L->act == CWX_ACT_CLAMPED_SWIGLU ? L->down_b : nullptr;
+    d.err = c->d_err;
+    max_items = ((H + TILE_ROWS - 1) / TILE_ROWS) * (used_max + (shared ? 1 : 0));
+    if ((rc = launch_gemv(d, max_items, c->device, c->sm_count, st))) return rc;
+
+    if ((rc = launch_combine(p.y, p.w, T, K, H, shared ? p.ys : nullptr, p.sgate, A->residual, A->out, st))) return rc;
+
+    if (A->ids_out) CWX_CUDA(cudaMemcpyAsync(A->ids_out, p.ids, n * 4, cudaMemcpyDeviceToDevice, st));
+    if (A->weights_out) CWX_CUDA(cudaMemcpyAsync(A->weights_out, p.w, n * 4, cudaMemcpyDeviceToDevice, st));
+    if (A->pairs_out) CWX_CUDA(cudaMemcpyAsync(A->pairs_out, p.pairs, n * 4, cudaMemcpyDeviceToDevice, st));
+    if (A->heads_out) CWX_CUDA(cudaMemcpyAsync(A->heads_out, p.heads, (size_t)3 * E * 4, cudaMemcpyDeviceToDevice, st));
+    return CWX_OK;
+}

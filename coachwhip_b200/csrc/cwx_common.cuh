@@ -1,0 +1,230 @@
+// Shared definitions of the cwx CUDA library: formats, the tiled bank layout, error state and
+// the inline PTX used by the kernels (bulk copies, mbarriers, ldmatrix, mma).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/cwx.h"
+
+namespace cwx {
+
+// ---------------------------------------------------------------- formats (GGUF type ids)
+enum Fmt : int {
+    F_Q8_0 = CWX_TYPE_Q8_0,
+    F_Q4_K = CWX_TYPE_Q4_K,
+    F_Q6_K = CWX_TYPE_Q6_K,
+    F_IQ3_S = CWX_TYPE_IQ3_S,
+    F_IQ2_S = CWX_TYPE_IQ2_S,
+    F_MXFP4 = CWX_TYPE_MXFP4,
+};
+
+__host__ __device__ inline int fmt_block_elems(int t) {
+    switch (t) {
+        case F_Q8_0: case F_MXFP4: return 32;
+        case F_Q4_K: case F_Q6_K: case F_IQ2_S: case F_IQ3_S: return 256;
+        default: return 0;
+    }
+}
+__host__ __device__ inline int fmt_block_bytes(int t) {
+    switch (t) {
+        case F_Q8_0: return 34;
+        case F_MXFP4: return 17;
+        case F_Q4_K: return 144;
+        case F_Q6_K: return 210;
+        case F_IQ2_S: return 82;
+        case F_IQ3_S: return 110;
+        default: return 0;
+    }
+}
+
+// Activation mode of a matrix product: which input the weights are multiplied with.
+enum ActMode : int {
+    AM_F32 = 0,   // f32 activations (Metal semantics; the only mode of the IQ formats)
+    AM_Q8_K = 1,  // activations quantised to Q8_K per 256 (candle CPU VecDotType of K-quants)
+    AM_Q8_0 = 2,  // activations quantised to Q8_0 per 32 (candle CPU VecDotType of Q8_0, MXFP4)
+};
+__host__ __device__ inline int act_mode_for(int fmt, int policy) {
+    if (policy == CWX_ACT_MODE_F32) return AM_F32;
+    switch (fmt) {
+        case F_Q4_K: case F_Q6_K: return AM_Q8_K;
+        case F_Q8_0: case F_MXFP4: return AM_Q8_0;
+        default: return AM_F32;
+    }
+}
+
+// ---------------------------------------------------------------- tiled bank layout
+// A bank (E experts x n rows x k columns) is stored expert-major; inside an expert, 64-row tiles;
+// inside a tile, K-pieces of up to 256 columns; inside a piece, the tile's rows one after the
+// other, each row's quant blocks of that K range. A piece is one contiguous run of bytes padded
+// to 16, so one bulk copy brings a (64 rows x 256 K) slab into shared memory. The quant blocks
+// themselves are the GGUF bytes, unchanged.
+constexpr int TILE_ROWS = 64;
+constexpr int PIECE_K = 256;
+
+__host__ __device__ inline int64_t pad16(int64_t x) { return (x + 15) & ~(int64_t)15; }
+
+struct Layout {
+    int fmt;
+    int64_t n, k, n_experts;
+    int64_t row_bytes;     // GGUF bytes of one row
+    int n_kp;              // K-pieces per row
+    int64_t kp_row_bytes;  // bytes of one row inside a full piece (256 K)
+    int64_t last_kp_row_bytes;
+    int64_t full_tile_bytes;
+    int64_t expert_bytes;  // tiled bytes of one expert, padded to 256
+};
+
+__host__ __device__ inline int64_t piece_row_bytes(const Layout& L, int kp) {
+    return kp == L.n_kp - 1 ? L.last_kp_row_bytes : L.kp_row_bytes;
+}
+__host__ __device__ inline int tile_rows(const Layout& L, int64_t rt) {
+    int64_t r = L.n - rt * TILE_ROWS;
+    return (int)(r < TILE_ROWS ? r : TILE_ROWS);
+}
+// Offset of piece (rt, kp) inside an expert, and its size.
+__host__ __device__ inline int64_t piece_offset(const Layout& L, int64_t rt, int kp) {
+    int rows = tile_rows(L, rt);
+    int64_t off = rt * L.full_tile_bytes;
+    int64_t full = pad16((int64_t)rows * L.kp_row_bytes);
+    return off + (int64_t)kp * full;
+}
+__host__ __device__ inline int64_t piece_bytes(const Layout& L, int64_t rt, int kp) {
+    return pad16((int64_t)tile_rows(L, rt) * piece_row_bytes(L, kp));
+}
+
+inline bool make_layout(int fmt, int64_t n, int64_t k, int64_t e, Layout* L) {
+    int be = fmt_block_elems(fmt), bb = fmt_block_bytes(fmt);
+    if (be == 0 || n <= 0 || k <= 0 || e <= 0 || k % be) return false;
+    L->fmt = fmt;
+    L->n = n;
+    L->k = k;
+    L->n_experts = e;
+    L->row_bytes = k / be * bb;
+    L->n_kp = (int)((k + PIECE_K - 1) / PIECE_K);
+    L->kp_row_bytes = (int64_t)(PIECE_K < k ? PIECE_K : k) / be * bb;
+    int64_t last_k = k - (int64_t)(L->n_kp - 1) * PIECE_K;
+    L->last_kp_row_bytes = last_k / be * bb;
+    L->full_tile_bytes = 0;
+    for (int kp = 0; kp < L->n_kp; ++kp)
+        L->full_tile_bytes += pad16((int64_t)TILE_ROWS * (kp == L->n_kp - 1 ? L->last_kp_row_bytes : L->kp_row_bytes));
+    int64_t full_tiles = n / TILE_ROWS;
+    int64_t eb = full_tiles * L->full_tile_bytes;
+    if (n % TILE_ROWS) {
+        int rows = (int)(n % TILE_ROWS);
+        for (int kp = 0; kp < L->n_kp; ++kp)
+            eb += pad16((int64_t)rows * (kp == L->n_kp - 1 ? L->last_kp_row_bytes : L->kp_row_bytes));
+    }
+    L->expert_bytes = (eb + 255) & ~(int64_t)255;
+    return true;
+}
+// Note for partial tiles: every piece of a tile has the same padded size except the tail piece,
+// so piece_offset() is exact for full pieces before the tail; tiles are laid out back to back.
+
+}  // namespace cwx
+
+struct cwx_bank {
+    int device;
+    cwx::Layout L;
+    uint8_t* d;  // tiled bytes, E * expert_bytes
+    int64_t bytes_per_expert_gguf;
+};
+
+struct cwx_ctx {
+    int device;
+    int sm_count;
+    uint8_t* ws;  // workspace
+    size_t ws_bytes;
+    int* d_err;   // device error word (first error code wins)
+    int* h_err;   // pinned mirror
+    uint16_t* d_iq3s_map;  // encoder maps for synthetic banks (built on first use)
+    uint16_t* d_iq2s_map;
+};
+
+namespace cwx {
+
+// ---------------------------------------------------------------- error reporting
+void set_error(const char* fmt, ...);
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+
+#define CWX_CUDA(call)                                 \
+    do {                                               \
+        cudaError_t _e = (call);                       \
+        if (_e != cudaSuccess) return cuda_fail(_e, #call); \
+    } while (0)
+
+// Device error codes written to cwx_ctx::d_err.
+enum DevErr : int { DE_OK = 0, DE_TIMEOUT = 1, DE_BAD_ID = 2, DE_SHAPE = 3 };
+
+__device__ inline void dev_error(int* err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ inline uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ inline void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ inline void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ inline void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// Bounded wait on an mbarrier phase. Returns false (and records DE_TIMEOUT) when the phase has
+// not completed after `limit` polls, so a lost copy ends the kernel instead of hanging the GPU.
+__device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, uint32_t limit = (1u << 26)) {
+    uint32_t a = smem_u32(bar);
+    for (uint32_t i = 0; i < limit; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    dev_error(err, DE_TIMEOUT);
+    return false;
+}
+
+// 1-D bulk copy global -> shared, completion signalled on `bar` (bytes and addresses 16-aligned).
+__device__ inline void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ inline void ldmatrix_x4(uint32_t* r, const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+
+// D += A (16x16 f16, row) * B (16x8 f16, col), f32 accumulate.
+__device__ inline void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ inline uint32_t pack_half2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// f32 -> (hi, lo) f16 pair with hi + lo = x to about 2^-22 relative.
+__device__ inline void split_f16(float x, __half* hi, __half* lo) {
+    __half h = __float2half_rn(x);
+    *hi = h;
+    *lo = __float2half_rn(__fsub_rn(x, __half2float(h)));
+}
+
+}  // namespace cwx

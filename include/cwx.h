@@ -1,0 +1,165 @@
+/* cwx: B200-native mixture-of-experts layer for coachwhip -- C ABI.
+ *
+ * The drop-in boundary for coachwhip's resident MoE path. Every entry point takes plain
+ * pointers and sizes; device pointers are CUDA device addresses, `stream` is a cudaStream_t
+ * passed as void* (NULL = the legacy default stream). Calls are stream-ordered and do not
+ * synchronise unless documented. No call throws or aborts: each returns a cwx status code and
+ * cwx_last_error() gives a thread-local message for the last failure.
+ *
+ * Reference interfaces replaced (paths inside the coachwhip tree):
+ *   cwx_bank_create / cwx_bank_destroy
+ *       ExpertStore::resident_op + exact_load   crates/engine/src/experts.rs:1949-1998, 98-119
+ *   cwx_expert_matmul
+ *       MoeMatvec::metal_fwd (CustomOp2)         crates/engine/src/experts.rs:2183-2309
+ *   cwx_route
+ *       route() / fuse_kernel::route             crates/engine/src/experts.rs:2364-2372,
+ *                                                crates/engine/src/fuse_kernel.rs:20-75, 347-352
+ *   cwx_permute
+ *       fuse_kernel::piles (cw_pile)             crates/engine/src/fuse_kernel.rs:180-202, 567-582
+ *   cwx_moe_forward
+ *       StreamedMoe::forward, resident branch    crates/engine/src/experts.rs:2539-2614
+ *       + SharedExpert::forward                  crates/engine/src/model_next.rs:731-741
+ */
+#ifndef CWX_H
+#define CWX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define CWX_OK 0
+#define CWX_EINVAL 1       /* bad argument: shape, null pointer, out-of-range value */
+#define CWX_EUNSUPPORTED 2 /* quant type or shape this build does not handle */
+#define CWX_ECUDA 3        /* a CUDA runtime call failed */
+#define CWX_ETIMEOUT 4     /* a bounded device-side wait gave up (see cwx_ctx_status) */
+#define CWX_ENOMEM 5       /* device or host allocation failed */
+#define CWX_EDEVICE 6      /* a kernel recorded an error (bad expert id, shape) */
+
+/* GGUF tensor type ids (ggml_type) of the supported expert formats. */
+#define CWX_TYPE_F32 0
+#define CWX_TYPE_Q8_0 8
+#define CWX_TYPE_Q4_K 12
+#define CWX_TYPE_Q6_K 14
+#define CWX_TYPE_IQ3_S 21
+#define CWX_TYPE_IQ2_S 22
+#define CWX_TYPE_MXFP4 39
+
+/* Activation policy of the expert products.
+ * CANDLE: a matrix whose format has a CPU dot product in the reference (Q4_K, Q6_K: Q8_K;
+ *         Q8_0, MXFP4: Q8_0) is multiplied with its activations quantised exactly as candle's
+ *         CPU QMatMul does (k_quants.rs:2595-2603); IQ formats use f32 activations.
+ * F32:    every matrix is multiplied with f32 activations (the reference's Metal semantics). */
+#define CWX_ACT_MODE_CANDLE 0
+#define CWX_ACT_MODE_F32 1
+
+/* Expert activation (ExpertAct, crates/engine/src/experts.rs:2376-2385). */
+#define CWX_ACT_SILU 0
+#define CWX_ACT_CLAMPED_SWIGLU 1
+
+typedef struct cwx_bank cwx_bank; /* one (n_experts, n, k) quantised expert matrix in HBM */
+typedef struct cwx_ctx cwx_ctx;   /* a device binding: workspace, error word; one per thread */
+
+/* Description of one expert matrix as stored in a GGUF file: n_experts x n rows x k columns,
+ * rows = output features, each row k/block_elems quant blocks; bytes_per_expert = n * row bytes.
+ * host_ptr points at n_experts * bytes_per_expert bytes (the tensor's data, verbatim). */
+typedef struct {
+    int32_t ggml_type;
+    int64_t n;
+    int64_t k;
+    int64_t n_experts;
+    int64_t bytes_per_expert;
+    const void* host_ptr;
+} cwx_matrix_desc;
+
+const char* cwx_last_error(void);
+int cwx_version(void);
+
+/* Context: binds `device`, owns a growing workspace and a device error word. */
+int cwx_ctx_create(int device, cwx_ctx** out);
+int cwx_ctx_destroy(cwx_ctx* ctx);
+/* Grow the workspace for up to `tokens` tokens of `layer` (call before stream capture). */
+int cwx_ctx_reserve(cwx_ctx* ctx, const void* layer, int32_t tokens);
+/* Synchronises `stream`, returns CWX_OK or the first device-side error recorded (and clears it). */
+int cwx_ctx_status(cwx_ctx* ctx, void* stream);
+
+/* Bank: copy a GGUF expert tensor into HBM (replaces ExpertStore::resident_op's exact_load). */
+int cwx_bank_create(int device, const cwx_matrix_desc* desc, cwx_bank** out);
+/* Bank filled on the device with the synthetic N(0, std^2) weights of stream `key`
+ * (test and benchmark workloads; same values as the CPU generator). */
+int cwx_bank_synth(cwx_ctx* ctx, int32_t ggml_type, int64_t n, int64_t k, int64_t n_experts, uint64_t key,
+                   float std_, cwx_bank** out);
+int cwx_bank_destroy(cwx_bank* bank);
+/* out[i] = std * N(0,1) element (offset + i) of stream `key`, i < n (synthetic router weights,
+ * biases and inputs; same values as the CPU generator). */
+int cwx_synth_normal(cwx_ctx* ctx, uint64_t key, uint64_t offset, int64_t n, float std_, float* out, void* stream);
+/* Shape of a bank (host_ptr of the result is NULL). */
+int cwx_bank_desc(const cwx_bank* bank, cwx_matrix_desc* out);
+/* GGUF bytes of experts [e0, e0+ne) back into host memory (blocking). */
+int cwx_bank_download(const cwx_bank* bank, int64_t e0, int64_t ne, void* host_dst);
+/* Dequantised f32 rows of one expert, (n, k), into device memory. */
+int cwx_bank_dequantize(const cwx_bank* bank, int64_t expert, float* out, void* stream);
+
+/* route(): logits (tokens, n_experts) f32 -> ids (tokens, top_k) u32 best first (ties: lowest
+ * id), weights (tokens, top_k) f32 = softmax over all experts, renormalised over the picks when
+ * norm != 0. n_experts <= 1024, top_k <= 16. All device pointers. */
+int cwx_route(cwx_ctx* ctx, const float* logits, int32_t tokens, int32_t n_experts, int32_t top_k, int32_t norm,
+              uint32_t* ids, float* weights, void* stream);
+
+/* Expert piles: ids (tokens, top_k) -> pairs (tokens*top_k) = flat pick indices t*top_k + j
+ * grouped by expert, ascending pick index within an expert; heads (3*n_experts) = (e, first
+ * pair, count) for every expert. Device pointers. An id >= n_experts records CWX_EDEVICE. */
+int cwx_permute(cwx_ctx* ctx, const uint32_t* ids, int32_t tokens, int32_t top_k, int32_t n_experts,
+                uint32_t* pairs, uint32_t* heads, void* stream);
+
+/* MoeMatvec: out (tokens, nei0, n) f32 = for each token t and pick j, one input row times the
+ * bank matrix of expert ids[t][j]. x is (tokens, k) f32 when rows_per_expert == 0, else
+ * (tokens*nei0, k) with one row per pick. act_mode: CWX_ACT_MODE_*. Device pointers. */
+int cwx_expert_matmul(cwx_ctx* ctx, const cwx_bank* bank, const float* x, int32_t rows_per_expert,
+                      const uint32_t* ids, int32_t tokens, int32_t nei0, int32_t act_mode, float* out,
+                      void* stream);
+
+/* One MoE layer's weights (all device pointers; banks from cwx_bank_*). */
+typedef struct {
+    int32_t hidden, n_experts, top_k, inter, norm_topk_prob;
+    const float* router_w; /* (n_experts, hidden) f32 */
+    const float* router_b; /* (n_experts) or NULL */
+    const cwx_bank* gate;  /* (n_experts, inter, hidden) */
+    const cwx_bank* up;    /* (n_experts, inter, hidden) */
+    const cwx_bank* down;  /* (n_experts, hidden, inter) */
+    int32_t act;           /* CWX_ACT_SILU / CWX_ACT_CLAMPED_SWIGLU */
+    float alpha, limit;    /* clamped SwiGLU constants (1.702, 7.0 for gpt-oss) */
+    const float* gate_b;   /* (n_experts, inter) or NULL */
+    const float* up_b;     /* (n_experts, inter) or NULL */
+    const float* down_b;   /* (n_experts, hidden) or NULL */
+    const cwx_bank* sh_gate; /* shared expert (1, shared_inter, hidden), or NULL for none */
+    const cwx_bank* sh_up;
+    const cwx_bank* sh_down; /* (1, hidden, shared_inter) */
+    const float* sh_gate_inp; /* (hidden) f32: sigmoid gate of the shared expert */
+    int32_t act_mode;         /* CWX_ACT_MODE_* */
+} cwx_moe_layer;
+
+/* Per-call tensors (device pointers). x, out: (tokens, hidden) f32. residual: optional
+ * (tokens, hidden) added to out. ids/weights/pairs/heads: optional taps of the routing. */
+typedef struct {
+    const float* x;
+    int32_t tokens;
+    float* out;
+    const float* residual;
+    uint32_t* ids_out;
+    float* weights_out;
+    uint32_t* pairs_out;
+    uint32_t* heads_out;
+} cwx_moe_args;
+
+/* out = routed experts (weighted) + shared expert * sigmoid(x . sh_gate_inp) (+ residual). */
+int cwx_moe_forward(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_moe_args* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CWX_H */

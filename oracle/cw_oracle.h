@@ -1,0 +1,106 @@
+// CPU oracle for the MoE hot path -- TEST INFRASTRUCTURE ONLY.
+//
+// A C++ restatement of the reference's arithmetic (candle CPU path and the Metal shader
+// dequant for IQ types), used only by tests/, __graft_entry__.smoke() and bench.py's CPU
+// baseline as the checker. The product library (coachwhip_b200) never links or calls it.
+//
+// Two oracles, one per semantic the reference has:
+//   O1 "candle CPU" (mode CWO_MODE_CANDLE): per matrix, activations quantised to the format's
+//      VecDotType (Q8_K for K-quants, Q8_0 for Q8_0/MXFP4) and integer block dots
+//      (vendor/candle-core/src/quantized/k_quants.rs:2551-2668). IQ types have no CPU path in
+//      the reference (k_quants.rs:2955-2993 panic), so their matrices use O2 arithmetic.
+//      Expert contributions summed in ascending expert order (experts.rs:2500-2537).
+//   O2 "reference GPU" (mode CWO_MODE_F32): weights dequantised bit-exactly, f32 activations,
+//      dot products accumulated in f64 and rounded once; picks summed in pick order
+//      (fuse_kernel.rs:277-291).
+//
+// Parity pins: route() known answers from crates/engine/tests/router.rs and rank() order from
+// crates/engine/tests/lookahead.rs; dequantisation of every format against ggml's gguf Python
+// package (an independent implementation of the same formats). Quantisers (from_float) are
+// restated from candle and unpinned by any reference test vector.
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    CWO_F32 = 0,
+    CWO_Q8_0 = 8,
+    CWO_Q4_K = 12,
+    CWO_Q6_K = 14,
+    CWO_Q8_K = 15,
+    CWO_IQ3_S = 21,
+    CWO_IQ2_S = 22,
+    CWO_MXFP4 = 39,
+};
+
+enum { CWO_MODE_CANDLE = 0, CWO_MODE_F32 = 1 };
+enum { CWO_ACT_SILU = 0, CWO_ACT_CLAMPED_SWIGLU = 1 };
+
+int cwo_block_elems(int type);
+int cwo_block_bytes(int type);
+int64_t cwo_row_bytes(int type, int64_t k);
+
+// from_float for Q4_K, Q6_K, Q8_0, Q8_K, MXFP4 (candle); own encoder for IQ2_S, IQ3_S.
+int cwo_quantize(int type, const float* x, int64_t n, void* out);
+// to_float, bit-exact restatement.
+int cwo_dequantize(int type, const void* blocks, int64_t n, float* y);
+// vec_dot_unopt of one weight row against one row of activation blocks (the VecDotType).
+float cwo_vec_dot(int type, int64_t n, const void* w_blocks, const void* act_blocks);
+// VecDotType of a weight type (CWO_Q8_K, CWO_Q8_0) or CWO_F32 when the reference has no CPU dot.
+int cwo_vec_dot_type(int type);
+
+// Synthetic data (the same generator the library's bank synthesis uses).
+uint64_t cwo_stream(uint32_t seed, uint32_t layer, uint32_t tensor);
+void cwo_normal(uint64_t key, uint64_t offset, int64_t n, float std_, float* out);
+// Quantised bytes of experts [e0, e0+ne) of an (E, n, k) tensor drawn N(0, std^2) from key.
+int cwo_synth_matrix(int type, uint64_t key, int64_t e0, int64_t ne, int64_t n, int64_t k, float std_, void* out);
+
+// Router logits (T, E) = x (T, H) . W (E, H)^T (+ b), products exact, f64 accumulation.
+void cwo_router(const float* x, const float* w, const float* b, int T, int H, int E, float* logits);
+// route(): softmax over all E, stable descending order, top k, renormalised when norm.
+int cwo_route(const float* logits, int T, int E, int k, int norm, uint32_t* ids, float* w);
+// Expert piles: pairs = flat pick indices i = t*k + j grouped stably by expert,
+// heads[3e] = e, heads[3e+1] = first pair, heads[3e+2] = count, for every e < E.
+int cwo_permute(const uint32_t* ids, int T, int k, int E, uint32_t* pairs, uint32_t* heads);
+
+// out (rows, n) = x (rows, k) . W_e^T for expert e of a bank; mode CWO_MODE_CANDLE / _F32.
+int cwo_matmul(int type, int mode, const void* bank, int64_t n, int64_t k, int64_t bytes_per_expert,
+               uint32_t expert, const float* x, int rows, float* out);
+
+typedef struct {
+    int hidden, n_experts, top_k, inter, norm_topk_prob;
+    const float* router_w;  // (E, H)
+    const float* router_b;  // (E) or NULL
+    int gate_type, up_type, down_type;
+    const void* gate_bank;  // (E, inter, hidden) quantised
+    const void* up_bank;
+    const void* down_bank;  // (E, hidden, inter)
+    int act;                // CWO_ACT_*
+    float alpha, limit;
+    const float* gate_b;  // (E, inter) or NULL
+    const float* up_b;
+    const float* down_b;  // (E, hidden)
+    int shared_inter;     // 0 = no shared expert
+    int sh_gate_type, sh_up_type, sh_down_type;
+    const void* sh_gate;
+    const void* sh_up;
+    const void* sh_down;
+    const float* sh_gate_inp;  // (H)
+} cwo_moe_layer;
+
+// One MoE layer. routed (T, H) and shared (T, H) may be NULL; ids/w (T, k) may be NULL.
+// out (T, H) = routed + shared contribution.
+int cwo_moe_forward(const cwo_moe_layer* L, const float* x, int T, int mode, float* out, float* routed,
+                    float* shared, uint32_t* ids, float* w);
+
+// Threads used by the OpenMP regions (0 = runtime default).
+void cwo_set_threads(int n);
+int cwo_get_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
