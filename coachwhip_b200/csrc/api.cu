@@ -362,6 +362,11 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
         a.s_ostride = Is;
         a.s_count = T;
     }
+    // Products whose results are re-quantised downstream (the down matrix takes Q8 activations)
+    // carry their weights to ~22 bits, so the hidden state matches the CPU path closely enough
+    // that its Q8 codes do not flip at rounding boundaries.
+    a.split_r = p.md != AM_F32;
+    a.split_s = shared && p.msd != AM_F32;
     a.act = L->act;
     a.alpha = L->alpha;
     a.limit = L->limit;

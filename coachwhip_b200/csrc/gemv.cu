@@ -103,21 +103,33 @@ __device__ __forceinline__ void issue_step(const GemvArgs& a, const Cursor& c, u
 }
 
 // Dequantise unit (row = lane % 16, 32-column unit (2*ss + lane/16)) of the warp's 16 rows and
-// store it as f16 into the warp's 16 x 64 tile (16-byte chunks XOR-swizzled by row).
+// store it as f16 into the warp's 16 x 64 tile (16-byte chunks XOR-swizzled by row). With a `lo`
+// tile, the weights are stored as an f16 pair hi + lo carrying ~22 bits of the exact f32 value.
 __device__ __forceinline__ void stage_a(int fmt, const uint8_t* piece, int64_t prb, int row0, int ss, int lane,
-                                        __half* abuf, const Tables& t) {
+                                        __half* abuf, __half* abuf_lo, const Tables& t) {
     int r = lane & 15, uh = lane >> 4;
     float w[32];
     decode_unit(fmt, piece + (int64_t)(row0 + r) * prb, 2 * ss + uh, w, t);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-        uint4 v;
-        v.x = pack_half2(w[8 * q + 0], w[8 * q + 1]);
-        v.y = pack_half2(w[8 * q + 2], w[8 * q + 3]);
-        v.z = pack_half2(w[8 * q + 4], w[8 * q + 5]);
-        v.w = pack_half2(w[8 * q + 6], w[8 * q + 7]);
+        uint4 v, vl;
+        uint32_t* pv = reinterpret_cast<uint32_t*>(&v);
+        uint32_t* pl = reinterpret_cast<uint32_t*>(&vl);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float a = w[8 * q + 2 * i], b = w[8 * q + 2 * i + 1];
+            __half2 h = __floats2half2_rn(a, b);
+            pv[i] = *reinterpret_cast<uint32_t*>(&h);
+            if (abuf_lo) {
+                float2 hf = __half22float2(h);
+                __half2 l = __floats2half2_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y));
+                pl[i] = *reinterpret_cast<uint32_t*>(&l);
+            }
+        }
         int chunk = 4 * uh + q;
-        *reinterpret_cast<uint4*>(abuf + r * 64 + ((chunk ^ (r & 7)) * 8)) = v;
+        int off = r * 64 + ((chunk ^ (r & 7)) * 8);
+        *reinterpret_cast<uint4*>(abuf + off) = v;
+        if (abuf_lo) *reinterpret_cast<uint4*>(abuf_lo + off) = vl;
     }
 }
 
@@ -135,8 +147,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);  // nst mbarriers
     uint64_t* s_iq2s = reinterpret_cast<uint64_t*>(smem + 128);
     uint32_t* s_iq3s = reinterpret_cast<uint32_t*>(smem + 128 + 8192);
-    __half* abufs = reinterpret_cast<__half*>(smem + 128 + 8192 + 2048);  // 4 warps x 2 x 16 x 64
-    uint8_t* stages = smem + 128 + 8192 + 2048 + GEMV_WARPS * 2 * 16 * 64 * 2;
+    __half* abufs = reinterpret_cast<__half*>(smem + 128 + 8192 + 2048);  // 4 warps x 4 x 16 x 64
+    uint8_t* stages = smem + 128 + 8192 + 2048 + GEMV_WARPS * 4 * 16 * 64 * 2;
     __shared__ int s_abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -161,8 +173,10 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
         }
     }
 
-    __half* abuf0 = abufs + (warp * 2 + 0) * 16 * 64;
-    __half* abuf1 = abufs + (warp * 2 + 1) * 16 * 64;
+    __half* abuf0 = abufs + (warp * 4 + 0) * 16 * 64;
+    __half* abuf1 = abufs + (warp * 4 + 1) * 16 * 64;
+    __half* abuf0l = abufs + (warp * 4 + 2) * 16 * 64;
+    __half* abuf1l = abufs + (warp * 4 + 3) * 16 * 64;
     float acc0[NT][4], acc1[NT][4];
     int64_t boff[NT];
     int ntok = 0;
@@ -206,16 +220,21 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
         const int64_t kbase = (int64_t)cc.kp * PIECE_K;
         const int klen = (int)(m0.L.k - kbase < PIECE_K ? m0.L.k - kbase : PIECE_K);
         const int n_nt = (ntok + 7) >> 3;
+        const bool split = it.shared ? a.split_s : a.split_r;
         if (row0 < rows) {
             for (int ss = 0; ss < klen / 64; ++ss) {
-                stage_a(m0.L.fmt, st, prb0, row0, ss, lane, abuf0, tb);
-                if (a.two) stage_a(m1.L.fmt, st + a.stage_b_off, prb1, row0, ss, lane, abuf1, tb);
+                stage_a(m0.L.fmt, st, prb0, row0, ss, lane, abuf0, split ? abuf0l : nullptr, tb);
+                if (a.two) stage_a(m1.L.fmt, st + a.stage_b_off, prb1, row0, ss, lane, abuf1, split ? abuf1l : nullptr, tb);
                 __syncwarp();
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    uint32_t af0[4], af1[4];
+                    uint32_t af0[4], af1[4], al0[4], al1[4];
                     load_a_frag(abuf0, kk, lane, af0);
                     if (a.two) load_a_frag(abuf1, kk, lane, af1);
+                    if (split) {
+                        load_a_frag(abuf0l, kk, lane, al0);
+                        if (a.two) load_a_frag(abuf1l, kk, lane, al1);
+                    }
                     int64_t kg = kbase + ss * 64 + kk * 16 + 2 * c4;
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
@@ -231,9 +250,11 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
                             }
                             mma_16816(acc0[nt], af0, h0, h1);
                             mma_16816(acc0[nt], af0, l0, l1);
+                            if (split) mma_16816(acc0[nt], al0, h0, h1);
                             if (a.two) {
                                 mma_16816(acc1[nt], af1, h0, h1);
                                 mma_16816(acc1[nt], af1, l0, l1);
+                                if (split) mma_16816(acc1[nt], al1, h0, h1);
                             }
                         }
                     }
@@ -423,7 +444,7 @@ int launch_gemv(GemvArgs a, int64_t max_items, int device, int sm_count, cudaStr
     }
     a.stage_b_off = (int)pad16(b0);
     a.stage_bytes = (int)pad16(b0 + b1 + 15);
-    const int fixed = 128 + 8192 + 2048 + GEMV_WARPS * 2 * 16 * 64 * 2;
+    const int fixed = 128 + 8192 + 2048 + GEMV_WARPS * 4 * 16 * 64 * 2;
     int max_smem = 227 * 1024 - 1024;
     int nst = (max_smem - fixed) / a.stage_bytes;
     if (nst > 6) nst = 6;

@@ -35,6 +35,7 @@ struct GemvArgs {
     const float* gate_b;
     const float* up_b;
     const float* down_b;
+    int split_r, split_s;  // weights carried as an f16 hi + lo pair (routed, shared items)
     int* err;
     int stage_bytes;  // set by launch_gemv
     int stage_b_off;

@@ -187,7 +187,7 @@ def test_expert_matmul_shape_errors():
     with pytest.raises(ValueError, match="ids per token"):
         op(torch.zeros((1, 256), device=DEV), torch.zeros((1, 3), dtype=torch.int32, device=DEV))
     with pytest.raises(ValueError, match="needs contiguous"):
-        op(torch.zeros((256, 1), device=DEV).t(), torch.zeros((1, 2), dtype=torch.int32, device=DEV))
+        op(torch.zeros((2, 512), device=DEV)[:, ::2], torch.zeros((2, 2), dtype=torch.int32, device=DEV))
     with pytest.raises(ValueError, match="x must be f32"):
         op(torch.zeros((1, 256), device=DEV, dtype=torch.float64), torch.zeros((1, 2), dtype=torch.int32, device=DEV))
 
