@@ -19,7 +19,9 @@ EXPORTS = [
     "cwx_last_error", "cwx_version", "cwx_ctx_create", "cwx_ctx_destroy", "cwx_ctx_reserve", "cwx_ctx_status",
     "cwx_bank_create", "cwx_bank_synth", "cwx_bank_destroy", "cwx_bank_desc", "cwx_bank_download",
     "cwx_bank_dequantize", "cwx_synth_normal", "cwx_route", "cwx_permute", "cwx_expert_matmul", "cwx_moe_forward",
+    "cwx_ctx_set_profiling", "cwx_ctx_read_profile", "cwx_ctx_reset_profile", "cwx_ctx_launches",
 ]
+PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine"]
 
 
 class CwxError(RuntimeError):
@@ -88,6 +90,10 @@ def lib() -> ctypes.CDLL:
             "cwx_permute": (I32, [P, P, I32, I32, I32, P, P, P]),
             "cwx_expert_matmul": (I32, [P, P, P, I32, P, I32, I32, I32, P, P]),
             "cwx_moe_forward": (I32, [P, ctypes.POINTER(MoeLayer), ctypes.POINTER(MoeArgs), P]),
+            "cwx_ctx_set_profiling": (I32, [P, I32]),
+            "cwx_ctx_read_profile": (I32, [P, P, P]),
+            "cwx_ctx_reset_profile": (I32, [P]),
+            "cwx_ctx_launches": (I64, [P]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -119,3 +125,11 @@ def ctx(device: int) -> ctypes.c_void_p:
 def status(device: int, stream: int | None = None) -> None:
     """Synchronise and raise if a kernel recorded a device-side error."""
     check(lib().cwx_ctx_status(ctx(device), stream))
+
+
+def read_profile(device: int) -> tuple[list[float], list[int]]:
+    """Per-phase (milliseconds, counts) recorded on this thread's context (see PHASES)."""
+    ms = (ctypes.c_double * len(PHASES))()
+    cnt = (ctypes.c_int64 * len(PHASES))()
+    check(lib().cwx_ctx_read_profile(ctx(device), ctypes.byref(ms), ctypes.byref(cnt)))
+    return list(ms), list(cnt)

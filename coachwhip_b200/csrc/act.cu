@@ -1,0 +1,156 @@
+// Activation preparation for the expert products, and the weighted combine.
+//
+//   activation       ExpertAct::hidden crates/engine/src/experts.rs:2389-2406 (SiLU; gpt-oss clamped
+//                    SwiGLU with per-expert biases), cw_silu_mul crates/engine/src/fuse_kernel.rs:77-96
+//   Q8 activations   BlockQ8K::from_float vendor/candle-core/src/quantized/k_quants.rs:2495-2534,
+//                    BlockQ8_0::from_float k_quants.rs:784-820 (the VecDotType quantisation candle's
+//                    CPU QMatMul applies to its left-hand side, k_quants.rs:2595-2603)
+//   combine          cw_weighted_sum fuse_kernel.rs:277-291 (pick order) + shared expert
+//                    crates/engine/src/model_next.rs:731-741 + residual model_next.rs:1437
+//
+// Packed activation rows: per 256-column piece, 64 chunks of 8 f16 values; chunk
+// ((ss*2 + q)*2 + h)*4 + c holds columns 64c + 16ss + 8q + 0..7, hi part (h = 0) or lo part
+// (h = 1). This is the order in which the grouped products' threads read them (gemv.cu).
+#include "cwx_common.cuh"
+#include "kernels.cuh"
+
+namespace cwx {
+
+__device__ __forceinline__ float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
+
+// One warp per (row, 256 columns); lane l takes columns 8l..8l+7 of the block.
+__global__ void __launch_bounds__(256) k_prep(PrepArgs p) {
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = (p.K + 255) / 256;
+    if (w >= p.R * nb) return;
+    const int64_t r = w / nb, b = w % nb;
+    const int64_t c0 = b * 256;
+    const int len = (int)(p.K - c0 < 256 ? p.K - c0 : 256);
+    const int k0 = 8 * lane;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (k0 + j < len) ? p.src[r * p.K + c0 + k0 + j] : 0.f;
+    if (p.up) {
+        if (p.act == CWX_ACT_SILU) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (k0 + j < len) v[j] = __fmul_rn(silu_f(v[j]), p.up[r * p.K + c0 + k0 + j]);
+        } else {
+            const int64_t e = p.ids ? (int64_t)p.ids[r] : 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (k0 + j >= len) continue;
+                const int64_t col = c0 + k0 + j;
+                float gv = v[j], uv = p.up[r * p.K + col];
+                if (p.gate_b) gv = __fadd_rn(gv, p.gate_b[e * p.K + col]);
+                gv = fminf(gv, p.limit);
+                if (p.up_b) uv = __fadd_rn(uv, p.up_b[e * p.K + col]);
+                uv = fminf(fmaxf(uv, -p.limit), p.limit);
+                const float z = __fmul_rn(gv, p.alpha);
+                const float sg = __fdiv_rn(1.0f, __fadd_rn(expf(-z), 1.0f));
+                v[j] = __fmul_rn(__fadd_rn(uv, 1.0f), __fmul_rn(gv, sg));
+            }
+        }
+    }
+    if (p.mode == AM_Q8_K) {
+        // max |x| with the lowest index among equals, and the signed value there
+        float am = -1.f, mv = 0.f;
+        int ai = 1 << 30;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float f = fabsf(v[j]);
+            if (f > am) {
+                am = f;
+                ai = k0 + j;
+                mv = v[j];
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float oa = __shfl_xor_sync(0xffffffffu, am, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, ai, o);
+            const float ov = __shfl_xor_sync(0xffffffffu, mv, o);
+            if (oa > am || (oa == am && oi < ai)) {
+                am = oa;
+                ai = oi;
+                mv = ov;
+            }
+        }
+        if (am == 0.f) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = 0.f;
+        } else {
+            const float iscale = __fdiv_rn(-127.f, mv);
+            const float d = __fdiv_rn(1.0f, iscale);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float qv = roundf(__fmul_rn(iscale, v[j]));
+                qv = fminf(fmaxf(qv, -128.f), 127.f);
+                v[j] = __fmul_rn(d, qv);
+            }
+        }
+    } else if (p.mode == AM_Q8_0) {
+        // 32-column blocks: lanes 4i..4i+3 hold block i
+        float am = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(v[j]));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        const float d = __fdiv_rn(am, 127.f);
+        const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
+        const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float qv = roundf(__fmul_rn(v[j], id));
+            qv = fminf(fmaxf(qv, -128.f), 127.f);
+            v[j] = __fmul_rn(qv, dh);
+        }
+    }
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+        const float2 hf = __half22float2(h);
+        const __half2 l = __floats2half2_rn(__fsub_rn(v[2 * j], hf.x), __fsub_rn(v[2 * j + 1], hf.y));
+        hi[j] = *reinterpret_cast<const uint32_t*>(&h);
+        lo[j] = *reinterpret_cast<const uint32_t*>(&l);
+    }
+    const int c = k0 >> 6, ss = (k0 >> 4) & 3, q = (k0 >> 3) & 1;
+    uint8_t* piece = p.out + r * packed_row_bytes(p.K) + b * 1024;
+    *reinterpret_cast<uint4*>(piece + 16 * (((ss * 2 + q) * 2 + 0) * 4 + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(piece + 16 * (((ss * 2 + q) * 2 + 1) * 4 + c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
+// out[t] = sum_j w[t][j] * rows[t*K + j] (pick order, from 0) + sgate[t] * shared[t] + residual[t]
+__global__ void __launch_bounds__(256) k_combine(const float* __restrict__ rows, const float* __restrict__ w,
+                                                 int T, int K, int H, const float* __restrict__ shared,
+                                                 const float* __restrict__ sgate, const float* __restrict__ residual,
+                                                 float* __restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)T * H) return;
+    const int64_t t = i / H, c = i % H;
+    float acc = 0.f;
+    for (int j = 0; j < K; ++j) acc = __fadd_rn(acc, __fmul_rn(rows[(t * K + j) * H + c], w[t * K + j]));
+    if (shared) acc = __fadd_rn(acc, __fmul_rn(shared[t * H + c], sgate[t]));
+    if (residual) acc = __fadd_rn(acc, residual[i]);
+    out[i] = acc;
+}
+
+int launch_prep(const PrepArgs& p, cudaStream_t st) {
+    if (p.R == 0) return CWX_OK;
+    const int64_t warps = p.R * ((p.K + 255) / 256);
+    k_prep<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_prep");
+}
+
+int launch_combine(const float* rows, const float* w, int T, int K, int H, const float* shared, const float* sgate,
+                   const float* residual, float* out, cudaStream_t st) {
+    if (T == 0) return CWX_OK;
+    const int64_t n = (int64_t)T * H;
+    k_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, w, T, K, H, shared, sgate, residual, out);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_combine");
+}
+
+}  // namespace cwx

@@ -1,13 +1,16 @@
-// The C ABI: contexts, workspace, error reporting, and the orchestration of one MoE layer.
+// The C ABI: contexts, workspace, error reporting, profiling, and the orchestration of one MoE
+// layer.
 //
 // cwx_moe_forward is the resident branch of StreamedMoe::forward
 // (crates/engine/src/experts.rs:2562-2614) plus SharedExpert::forward
-// (crates/engine/src/model_next.rs:731-741): router logits, route, piles, gate/up products with
-// the activation, down products, weighted combine, shared expert, optional residual
+// (crates/engine/src/model_next.rs:731-741): router logits, route, piles, gate/up products, the
+// activation, down products, weighted combine, shared expert, optional residual
 // (model_next.rs:1437). Everything is stream-ordered; nothing synchronises.
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
+
+#include <vector>
 
 #include "cwx_common.cuh"
 #include "kernels.cuh"
@@ -55,7 +58,7 @@ static int ensure_ws(cwx_ctx* ctx, size_t bytes, cudaStream_t st) {
     cudaStreamIsCapturing(st, &cap);
     if (cap != cudaStreamCaptureStatusNone)
         return fail(CWX_EINVAL, "workspace too small during stream capture: call cwx_ctx_reserve first");
-    size_t nb = ((bytes + (1 << 20) - 1) >> 20) << 20;  // 1 MB rounding, as the reference arena does
+    const size_t nb = ((bytes + (1 << 20) - 1) >> 20) << 20;  // 1 MB rounding, as the reference arena does
     if (ctx->ws) {
         cudaError_t e = cudaStreamSynchronize(st);
         if (e != cudaSuccess) return cuda_fail(e, "workspace grow");
@@ -68,12 +71,52 @@ static int ensure_ws(cwx_ctx* ctx, size_t bytes, cudaStream_t st) {
     return CWX_OK;
 }
 
+// ---------------------------------------------------------------- profiling
+struct ProfEvent {
+    int phase;
+    cudaEvent_t a, b;
+};
+using ProfLog = std::vector<ProfEvent>;
+
+// Inside stream capture the events are recorded as graph nodes (cudaEventRecordExternal), so each
+// replay of the graph records them again.
+static void record_event(cudaEvent_t e, cudaStream_t st) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cap);
+    if (cap == cudaStreamCaptureStatusActive) cudaEventRecordWithFlags(e, st, cudaEventRecordExternal);
+    else cudaEventRecord(e, st);
+}
+
+// Event pair around one phase of a call (no-op unless profiling is on).
+struct PhaseTimer {
+    cwx_ctx* c;
+    cudaStream_t st;
+    int phase;
+    cudaEvent_t a = nullptr;
+    PhaseTimer(cwx_ctx* c_, cudaStream_t s_, int ph) : c(c_), st(s_), phase(ph) {
+        if (!c->profiling) return;
+        if (cudaEventCreate(&a) == cudaSuccess) record_event(a, st);
+        else a = nullptr;
+    }
+    void end() {
+        if (!a) return;
+        cudaEvent_t b;
+        if (cudaEventCreate(&b) == cudaSuccess) {
+            record_event(b, st);
+            static_cast<ProfLog*>(c->prof)->push_back({phase, a, b});
+        } else {
+            cudaEventDestroy(a);
+        }
+        a = nullptr;
+    }
+};
+
+// ---------------------------------------------------------------- layer plan
 static int act_mode_of(const cwx_bank* b, int policy) { return act_mode_for(b->L.fmt, policy); }
 
 struct LayerPlan {
     int H, E, K, I, Is, T;
     int mgu, msgu, md, msd;  // activation modes
-    // workspace pointers
     float* logits;
     float* sgate;
     uint32_t* ids;
@@ -83,11 +126,9 @@ struct LayerPlan {
     uint32_t* used3;
     uint32_t* n_used;
     uint32_t* perm;
-    __half* xh[3];
-    __half* xl[3];
-    float* h;
-    float* hs;
-    __half *hh, *hl, *hsh, *hsl;
+    uint8_t* xpk[3];         // packed activation rows of x per activation mode
+    float *g, *u, *gs, *us;  // gate / up outputs (routed by pick, shared by token)
+    uint8_t *hpk, *hspk;     // packed hidden rows (routed, shared)
     float* y;
     float* ys;
     size_t bytes;
@@ -133,7 +174,7 @@ static void plan_layer(const cwx_moe_layer* L, int T, uint8_t* base, LayerPlan* 
     p->md = act_mode_of(L->down, L->act_mode);
     p->msgu = L->sh_gate ? act_mode_of(L->sh_gate, L->act_mode) : -1;
     p->msd = L->sh_down ? act_mode_of(L->sh_down, L->act_mode) : -1;
-    int64_t n = (int64_t)T * p->K;
+    const int64_t n = (int64_t)T * p->K;
     Carve c{base, 0};
     p->logits = c.take<float>((size_t)T * p->E);
     p->sgate = c.take<float>((size_t)T + 1);
@@ -145,19 +186,48 @@ static void plan_layer(const cwx_moe_layer* L, int T, uint8_t* base, LayerPlan* 
     p->n_used = c.take<uint32_t>(4);
     p->perm = c.take<uint32_t>(perm_scratch_bytes(n, p->E) / 4);
     for (int m = 0; m < 3; ++m) {
-        bool need = (m == p->mgu) || (m == p->msgu);
-        p->xh[m] = need ? c.take<__half>((size_t)T * p->H) : nullptr;
-        p->xl[m] = need ? c.take<__half>((size_t)T * p->H) : nullptr;
+        const bool need = (m == p->mgu) || (m == p->msgu);
+        p->xpk[m] = need ? c.take<uint8_t>((size_t)(T * packed_row_bytes(p->H))) : nullptr;
     }
-    p->h = c.take<float>((size_t)n * p->I);
-    p->hh = c.take<__half>((size_t)n * p->I);
-    p->hl = c.take<__half>((size_t)n * p->I);
-    p->hs = c.take<float>((size_t)T * p->Is);
-    p->hsh = c.take<__half>((size_t)T * p->Is);
-    p->hsl = c.take<__half>((size_t)T * p->Is);
+    p->g = c.take<float>((size_t)n * p->I);
+    p->u = c.take<float>((size_t)n * p->I);
+    p->gs = c.take<float>((size_t)T * p->Is);
+    p->us = c.take<float>((size_t)T * p->Is);
+    p->hpk = c.take<uint8_t>((size_t)(n * packed_row_bytes(p->I)));
+    p->hspk = c.take<uint8_t>((size_t)(T * packed_row_bytes(p->Is)));
     p->y = c.take<float>((size_t)n * p->H);
     p->ys = c.take<float>((size_t)T * p->H);
     p->bytes = c.off + 256;
+}
+
+static MatRef mref(const cwx_bank* b) { return MatRef{b ? b->d : nullptr, b ? b->L : Layout{}}; }
+
+static GemvJob job(const cwx_bank* b, int shared, const uint8_t* act, int64_t k, int bdiv, float* out, int64_t ostride,
+                   int split, const float* bias) {
+    GemvJob j;
+    j.m = mref(b);
+    j.shared = shared;
+    j.b = act;
+    j.bstride = packed_row_bytes(k);
+    j.bdiv = bdiv;
+    j.out = out;
+    j.ostride = ostride;
+    j.split = split;
+    j.bias = bias;
+    return j;
+}
+
+static PrepArgs prep(const float* src, const float* up, int64_t R, int64_t K, int mode, uint8_t* out) {
+    PrepArgs a;
+    memset(&a, 0, sizeof a);
+    a.src = src;
+    a.up = up;
+    a.R = R;
+    a.K = K;
+    a.mode = mode;
+    a.act = CWX_ACT_SILU;
+    a.out = out;
+    return a;
 }
 
 }  // namespace cwx
@@ -177,14 +247,29 @@ extern "C" int cwx_ctx_create(int device, cwx_ctx** out) {
     cwx_ctx* c = new cwx_ctx();
     memset(c, 0, sizeof *c);
     c->device = device;
+    c->prof = new ProfLog();
     cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
     cudaError_t e = cudaMalloc(&c->d_err, 16);
     if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, 16);
     if (e != cudaSuccess) {
+        delete static_cast<ProfLog*>(c->prof);
         delete c;
         return cuda_fail(e, "cwx_ctx_create");
     }
     *out = c;
+    return CWX_OK;
+}
+
+extern "C" int cwx_ctx_reset_profile(cwx_ctx* c) {
+    if (!c) return fail(CWX_EINVAL, "cwx_ctx_reset_profile: null context");
+    ProfLog* log = static_cast<ProfLog*>(c->prof);
+    if (!log) return CWX_OK;
+    cudaSetDevice(c->device);
+    for (const ProfEvent& e : *log) {
+        cudaEventDestroy(e.a);
+        cudaEventDestroy(e.b);
+    }
+    log->clear();
     return CWX_OK;
 }
 
@@ -195,9 +280,32 @@ extern "C" int cwx_ctx_destroy(cwx_ctx* c) {
     if (c->d_err) cudaFree(c->d_err);
     if (c->d_iq3s_map) cudaFree(c->d_iq3s_map);
     if (c->d_iq2s_map) cudaFree(c->d_iq2s_map);
+    cwx_ctx_reset_profile(c);
+    delete static_cast<ProfLog*>(c->prof);
     delete c;
     return CWX_OK;
 }
+
+extern "C" int cwx_ctx_set_profiling(cwx_ctx* c, int enabled) {
+    if (!c) return fail(CWX_EINVAL, "cwx_ctx_set_profiling: null context");
+    c->profiling = enabled ? 1 : 0;
+    return CWX_OK;
+}
+
+extern "C" int cwx_ctx_read_profile(cwx_ctx* c, double* ms, int64_t* count) {
+    if (!c) return fail(CWX_EINVAL, "cwx_ctx_read_profile: null context");
+    CWX_CUDA(cudaSetDevice(c->device));
+    CWX_CUDA(cudaDeviceSynchronize());
+    for (const ProfEvent& e : *static_cast<ProfLog*>(c->prof)) {
+        float t = 0.f;
+        CWX_CUDA(cudaEventElapsedTime(&t, e.a, e.b));
+        if (ms) ms[e.phase] += t;
+        if (count) count[e.phase] += 1;
+    }
+    return CWX_OK;
+}
+
+extern "C" int64_t cwx_ctx_launches(const cwx_ctx* c) { return c ? c->launches : 0; }
 
 extern "C" int cwx_ctx_status(cwx_ctx* c, void* stream) {
     if (!c) return fail(CWX_EINVAL, "cwx_ctx_status: null context");
@@ -229,6 +337,7 @@ extern "C" int cwx_route(cwx_ctx* c, const float* logits, int32_t T, int32_t E, 
     if (T < 0 || E < 1 || E > 1024) return fail(CWX_EINVAL, "cwx_route: %d experts (1..1024)", E);
     if (K < 1 || K > 16 || K > E) return fail(CWX_EINVAL, "cwx_route: top_k %d (1..16, <= experts)", K);
     CWX_CUDA(cudaSetDevice(c->device));
+    c->launches += T > 0 ? 1 : 0;
     return launch_route(logits, T, E, K, norm, ids, w, nullptr, nullptr, 0, nullptr, (cudaStream_t)stream);
 }
 
@@ -238,7 +347,7 @@ extern "C" int cwx_permute(cwx_ctx* c, const uint32_t* ids, int32_t T, int32_t K
     if (T < 0 || K < 1 || E < 1 || E > 12288) return fail(CWX_EINVAL, "cwx_permute: bad sizes");
     CWX_CUDA(cudaSetDevice(c->device));
     cudaStream_t st = (cudaStream_t)stream;
-    int64_t n = (int64_t)T * K;
+    const int64_t n = (int64_t)T * K;
     Carve cv{nullptr, 0};
     cv.take<uint32_t>((size_t)3 * E);
     cv.take<uint32_t>(4);
@@ -249,10 +358,9 @@ extern "C" int cwx_permute(cwx_ctx* c, const uint32_t* ids, int32_t T, int32_t K
     uint32_t* used3 = w.take<uint32_t>((size_t)3 * E);
     uint32_t* n_used = w.take<uint32_t>(4);
     uint32_t* scratch = w.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
+    c->launches += 3;
     return launch_permute(ids, n, E, pairs, heads, used3, n_used, scratch, c->d_err, st);
 }
-
-static MatRef mref(const cwx_bank* b) { return MatRef{b ? b->d : nullptr, b ? b->L : Layout{}}; }
 
 extern "C" int cwx_expert_matmul(cwx_ctx* c, const cwx_bank* bank, const float* x, int32_t rows_per_expert,
                                  const uint32_t* ids, int32_t tokens, int32_t nei0, int32_t act_mode, float* out,
@@ -266,19 +374,18 @@ extern "C" int cwx_expert_matmul(cwx_ctx* c, const cwx_bank* bank, const float* 
     if (tokens == 0) return CWX_OK;
     CWX_CUDA(cudaSetDevice(c->device));
     cudaStream_t st = (cudaStream_t)stream;
-    int E = (int)bank->L.n_experts;
-    int64_t n = (int64_t)tokens * nei0;
-    int64_t xrows = rows_per_expert ? n : tokens;
-    int64_t K = bank->L.k;
-    int mode = act_mode_of(bank, act_mode);
+    const int E = (int)bank->L.n_experts;
+    const int64_t n = (int64_t)tokens * nei0;
+    const int64_t xrows = rows_per_expert ? n : tokens;
+    const int64_t K = bank->L.k;
+    const int mode = act_mode_of(bank, act_mode);
     Carve cv{nullptr, 0};
     cv.take<uint32_t>((size_t)n);
     cv.take<uint32_t>((size_t)3 * E);
     cv.take<uint32_t>((size_t)3 * E);
     cv.take<uint32_t>(4);
     cv.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
-    cv.take<__half>((size_t)(xrows * K));
-    cv.take<__half>((size_t)(xrows * K));
+    cv.take<uint8_t>((size_t)(xrows * packed_row_bytes(K)));
     int rc = ensure_ws(c, cv.off + 256, st);
     if (rc) return rc;
     Carve w{c->ws, 0};
@@ -287,34 +394,26 @@ extern "C" int cwx_expert_matmul(cwx_ctx* c, const cwx_bank* bank, const float* 
     uint32_t* used3 = w.take<uint32_t>((size_t)3 * E);
     uint32_t* n_used = w.take<uint32_t>(4);
     uint32_t* scratch = w.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
-    __half* xh = w.take<__half>((size_t)(xrows * K));
-    __half* xl = w.take<__half>((size_t)(xrows * K));
+    uint8_t* xpk = w.take<uint8_t>((size_t)(xrows * packed_row_bytes(K)));
     if ((rc = launch_permute(ids, n, E, pairs, heads, used3, n_used, scratch, c->d_err, st))) return rc;
-    if ((rc = launch_prep(x, xrows, K, mode, xh, xl, st))) return rc;
+    if ((rc = launch_prep(prep(x, nullptr, xrows, K, mode, xpk), st))) return rc;
     GemvArgs a;
     memset(&a, 0, sizeof a);
-    a.two = 0;
-    a.ra = mref(bank);
-    a.rbh = xh;
-    a.rbl = xl;
-    a.r_bstride = K;
-    a.r_bdiv = rows_per_expert ? 1 : nei0;
-    a.rout = out;
-    a.r_ostride = bank->L.n;
+    a.njobs = 1;
+    a.job[0] = job(bank, 0, xpk, K, rows_per_expert ? 1 : nei0, out, bank->L.n, 0, nullptr);
     a.pairs = pairs;
     a.used3 = used3;
     a.n_used = n_used;
     a.err = c->d_err;
-    int64_t tiles = (bank->L.n + TILE_ROWS - 1) / TILE_ROWS;
-    int64_t max_items = tiles * (n < E ? n : E);
-    return launch_gemv(a, max_items, c->device, c->sm_count, st);
+    c->launches += 5;
+    return launch_gemv(a, n < E ? n : E, c->device, c->sm_count, st);
 }
 
 extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, void* stream) {
     if (!c || !A) return fail(CWX_EINVAL, "cwx_moe_forward: null argument");
     int rc = validate_layer(L);
     if (rc) return rc;
-    int T = A->tokens;
+    const int T = A->tokens;
     if (T < 0) return fail(CWX_EINVAL, "cwx_moe_forward: tokens %d", T);
     if (T == 0) return CWX_OK;
     if (!A->x || !A->out) return fail(CWX_EINVAL, "cwx_moe_forward: null x or out");
@@ -328,89 +427,93 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
     const int64_t n = (int64_t)T * K;
     const bool shared = L->sh_gate != nullptr;
 
-    if ((rc = launch_router(A->x, L->router_w, L->router_b, T, H, E, p.logits, st))) return rc;
-    if ((rc = launch_route(p.logits, T, E, K, L->norm_topk_prob, p.ids, p.w, A->x, shared ? L->sh_gate_inp : nullptr,
-                           H, shared ? p.sgate : nullptr, st)))
-        return rc;
-    if ((rc = launch_permute(p.ids, n, E, p.pairs, p.heads, p.used3, p.n_used, p.perm, c->d_err, st))) return rc;
-    for (int m = 0; m < 3; ++m)
-        if (p.xh[m] && (rc = launch_prep(A->x, T, H, m, p.xh[m], p.xl[m], st))) return rc;
-
-    // gate/up (+ activation): routed piles and the shared expert's tiles in one launch
-    GemvArgs a;
-    memset(&a, 0, sizeof a);
-    a.two = 1;
-    a.ra = mref(L->gate);
-    a.rb = mref(L->up);
-    a.rbh = p.xh[p.mgu];
-    a.rbl = p.xl[p.mgu];
-    a.r_bstride = H;
-    a.r_bdiv = K;
-    a.rout = p.h;
-    a.r_ostride = I;
-    a.pairs = p.pairs;
-    a.used3 = p.used3;
-    a.n_used = p.n_used;
-    a.has_shared = shared;
-    if (shared) {
-        a.sa = mref(L->sh_gate);
-        a.sb = mref(L->sh_up);
-        a.sbh = p.xh[p.msgu];
-        a.sbl = p.xl[p.msgu];
-        a.s_bstride = H;
-        a.sout = p.hs;
-        a.s_ostride = Is;
+    {
+        PhaseTimer t(c, st, CWX_PHASE_ROUTER);
+        if ((rc = launch_router(A->x, L->router_w, L->router_b, T, H, E, p.logits, st))) return rc;
+        t.end();
+    }
+    {
+        PhaseTimer t(c, st, CWX_PHASE_ROUTE);
+        if ((rc = launch_route(p.logits, T, E, K, L->norm_topk_prob, p.ids, p.w, A->x,
+                               shared ? L->sh_gate_inp : nullptr, H, shared ? p.sgate : nullptr, st)))
+            return rc;
+        t.end();
+    }
+    {
+        PhaseTimer t(c, st, CWX_PHASE_PILES);
+        if ((rc = launch_permute(p.ids, n, E, p.pairs, p.heads, p.used3, p.n_used, p.perm, c->d_err, st))) return rc;
+        t.end();
+    }
+    c->launches += 5;
+    {
+        PhaseTimer t(c, st, CWX_PHASE_PREP);
+        for (int m = 0; m < 3; ++m) {
+            if (!p.xpk[m]) continue;
+            if ((rc = launch_prep(prep(A->x, nullptr, T, H, m, p.xpk[m]), st))) return rc;
+            c->launches += 1;
+        }
+        t.end();
+    }
+    const int64_t used_max = n < E ? n : E;
+    // gate and up: routed piles and the shared expert, four matrix jobs in one launch. A product
+    // whose result is re-quantised downstream (the down matrix takes Q8 activations) carries its
+    // weights to ~22 bits, so the hidden state matches the CPU path closely enough that its Q8
+    // codes do not flip at rounding boundaries.
+    {
+        GemvArgs a;
+        memset(&a, 0, sizeof a);
+        const int split_r = p.md != AM_F32, split_s = shared && p.msd != AM_F32;
+        a.job[a.njobs++] = job(L->gate, 0, p.xpk[p.mgu], H, K, p.g, I, split_r, nullptr);
+        a.job[a.njobs++] = job(L->up, 0, p.xpk[p.mgu], H, K, p.u, I, split_r, nullptr);
+        if (shared) {
+            a.job[a.njobs++] = job(L->sh_gate, 1, p.xpk[p.msgu], H, 1, p.gs, Is, split_s, nullptr);
+            a.job[a.njobs++] = job(L->sh_up, 1, p.xpk[p.msgu], H, 1, p.us, Is, split_s, nullptr);
+        }
+        a.pairs = p.pairs;
+        a.used3 = p.used3;
+        a.n_used = p.n_used;
         a.s_count = T;
+        a.err = c->d_err;
+        PhaseTimer t(c, st, CWX_PHASE_GATE_UP);
+        if ((rc = launch_gemv(a, used_max, c->device, c->sm_count, st))) return rc;
+        t.end();
     }
-    // Products whose results are re-quantised downstream (the down matrix takes Q8 activations)
-    // carry their weights to ~22 bits, so the hidden state matches the CPU path closely enough
-    // that its Q8 codes do not flip at rounding boundaries.
-    a.split_r = p.md != AM_F32;
-    a.split_s = shared && p.msd != AM_F32;
-    a.act = L->act;
-    a.alpha = L->alpha;
-    a.limit = L->limit;
-    a.gate_b = L->gate_b;
-    a.up_b = L->up_b;
-    a.err = c->d_err;
-    int64_t used_max = n < E ? n : E;
-    int64_t max_items = ((I + TILE_ROWS - 1) / TILE_ROWS) * used_max + (shared ? (Is + TILE_ROWS - 1) / TILE_ROWS : 0);
-    if ((rc = launch_gemv(a, max_items, c->device, c->sm_count, st))) return rc;
-
-    if ((rc = launch_prep(p.h, n, I, p.md, p.hh, p.hl, st))) return rc;
-    if (shared && (rc = launch_prep(p.hs, T, Is, p.msd, p.hsh, p.hsl, st))) return rc;
-
-    // down
-    GemvArgs d;
-    memset(&d, 0, sizeof d);
-    d.two = 0;
-    d.ra = mref(L->down);
-    d.rbh = p.hh;
-    d.rbl = p.hl;
-    d.r_bstride = I;
-    d.r_bdiv = 1;
-    d.rout = p.y;
-    d.r_ostride = H;
-    d.pairs = p.pairs;
-    d.used3 = p.used3;
-    d.n_used = p.n_used;
-    d.has_shared = shared;
-    if (shared) {
-        d.sa = mref(L->sh_down);
-        d.sbh = p.hsh;
-        d.sbl = p.hsl;
-        d.s_bstride = Is;
-        d.sout = p.ys;
-        d.s_ostride = H;
+    {
+        PhaseTimer t(c, st, CWX_PHASE_PREP);
+        PrepArgs pa = prep(p.g, p.u, n, I, p.md, p.hpk);
+        pa.act = L->act;
+        pa.alpha = L->alpha;
+        pa.limit = L->limit;
+        pa.gate_b = L->gate_b;
+        pa.up_b = L->up_b;
+        pa.ids = p.ids;
+        if ((rc = launch_prep(pa, st))) return rc;
+        if (shared && (rc = launch_prep(prep(p.gs, p.us, T, Is, p.msd, p.hspk), st))) return rc;
+        t.end();
+    }
+    c->launches += 2 + (shared ? 1 : 0);
+    {
+        GemvArgs d;
+        memset(&d, 0, sizeof d);
+        d.job[d.njobs++] = job(L->down, 0, p.hpk, I, 1, p.y, H, 0,
+                               L->act == CWX_ACT_CLAMPED_SWIGLU ? L->down_b : nullptr);
+        if (shared) d.job[d.njobs++] = job(L->sh_down, 1, p.hspk, Is, 1, p.ys, H, 0, nullptr);
+        d.pairs = p.pairs;
+        d.used3 = p.used3;
+        d.n_used = p.n_used;
         d.s_count = T;
+        d.err = c->d_err;
+        PhaseTimer t(c, st, CWX_PHASE_DOWN);
+        if ((rc = launch_gemv(d, used_max, c->device, c->sm_count, st))) return rc;
+        t.end();
     }
-    d.act = L->act;
-    d.down_b = L->act == CWX_ACT_CLAMPED_SWIGLU ? L->down_b : nullptr;
-    d.err = c->d_err;
-    max_items = ((H + TILE_ROWS - 1) / TILE_ROWS) * (used_max + (shared ? 1 : 0));
-    if ((rc = launch_gemv(d, max_items, c->device, c->sm_count, st))) return rc;
-
-    if ((rc = launch_combine(p.y, p.w, T, K, H, shared ? p.ys : nullptr, p.sgate, A->residual, A->out, st))) return rc;
+    {
+        PhaseTimer t(c, st, CWX_PHASE_COMBINE);
+        if ((rc = launch_combine(p.y, p.w, T, K, H, shared ? p.ys : nullptr, p.sgate, A->residual, A->out, st)))
+            return rc;
+        t.end();
+    }
+    c->launches += 2;
 
     if (A->ids_out) CWX_CUDA(cudaMemcpyAsync(A->ids_out, p.ids, n * 4, cudaMemcpyDeviceToDevice, st));
     if (A->weights_out) CWX_CUDA(cudaMemcpyAsync(A->weights_out, p.w, n * 4, cudaMemcpyDeviceToDevice, st));

@@ -27,48 +27,44 @@ namespace cwx {
 // One warp per (expert, row): move the row's bytes between GGUF order and the tiled layout.
 __global__ void k_repack(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, Layout L, int64_t e0,
                          int64_t ne, int to_tiled) {
-    int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int lane = threadIdx.x & 31;
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
     if (w >= ne * L.n) return;
-    int64_t e = w / L.n, r = w % L.n;
-    int64_t rt = r / TILE_ROWS, rr = r % TILE_ROWS;
-    const uint8_t* g = nullptr;
-    uint8_t* gd = nullptr;
-    int64_t gguf_row = e * (L.n * L.row_bytes) + r * L.row_bytes;
+    const int64_t e = w / L.n, r = w % L.n;
+    const int64_t rt = r / TILE_ROWS, rr = r % TILE_ROWS;
+    const int64_t gguf_row = e * (L.n * L.row_bytes) + r * L.row_bytes;
+    const int64_t ebase = (e0 + e) * L.expert_bytes;
     for (int kp = 0; kp < L.n_kp; ++kp) {
-        int64_t prb = piece_row_bytes(L, kp);
-        int64_t toff = (e0 + e) * L.expert_bytes + piece_offset(L, rt, kp) + rr * prb;
-        int64_t goff = gguf_row + (int64_t)kp * L.kp_row_bytes;
-        if (to_tiled) {
-            g = src + goff;
-            gd = dst + toff;
-        } else {
-            g = src + toff;
-            gd = dst + goff;
+        const int64_t prb = piece_row_bytes(L, kp);
+        for (int64_t i = lane; i < prb; i += 32) {
+            const int64_t goff = gguf_row + (int64_t)kp * L.kp_row_bytes + i;
+            const int64_t toff = ebase + tiled_offset(L, rt, rr, kp, i);
+            if (to_tiled) dst[toff] = src[goff];
+            else dst[goff] = src[toff];
         }
-        for (int64_t i = lane; i < prb; i += 32) gd[i] = g[i];
     }
 }
 
-// f32 rows of one expert.
+// f32 rows of one expert: one thread per (row, 16 columns).
 __global__ void k_dequant(const uint8_t* __restrict__ bank, Layout L, int64_t e, float* __restrict__ out) {
-    __shared__ uint64_t s2[1024];
-    __shared__ uint32_t s3[512];
-    load_tables(s2, s3);
+    extern __shared__ __align__(16) uint8_t tsm[];
+    load_htables(reinterpret_cast<uint4*>(tsm), reinterpret_cast<uint2*>(tsm + 16384),
+                 reinterpret_cast<uint4*>(tsm + 20480));
     __syncthreads();
-    Tables t{s2, s3};
-    int64_t units_per_row = L.k / 32;
-    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const HTables t{reinterpret_cast<const uint4*>(tsm), reinterpret_cast<const uint2*>(tsm + 16384),
+                    reinterpret_cast<const uint4*>(tsm + 20480)};
+    const int64_t units_per_row = L.k / 16;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= L.n * units_per_row) return;
-    int64_t r = i / units_per_row, uk = i % units_per_row;
-    int kp = (int)(uk / 8), u = (int)(uk % 8);
-    int64_t rt = r / TILE_ROWS, rr = r % TILE_ROWS;
-    const uint8_t* row = bank + e * L.expert_bytes + piece_offset(L, rt, kp) + rr * piece_row_bytes(L, kp);
-    float w[32];
-    decode_unit(L.fmt, row, u, w, t);
-    float* o = out + r * L.k + uk * 32;
+    const int64_t r = i / units_per_row, uk = i % units_per_row;
+    const int kp = (int)(uk / 16), kofs = (int)(uk % 16) * 16;
+    const int64_t rt = r / TILE_ROWS, rr = r % TILE_ROWS;
+    const uint8_t* piece = bank + e * L.expert_bytes + piece_offset(L, rt, kp);
+    float w[16];
+    dec16_exact(L.fmt, piece, (int)rr, piece_row_bytes(L, kp), kofs, w, t);
+    float* o = out + r * L.k + uk * 16;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) o[j] = w[j];
+    for (int j = 0; j < 16; ++j) o[j] = w[j];
 }
 
 // ---------------------------------------------------------------- device quantisers
@@ -353,7 +349,8 @@ __global__ void k_synth(uint8_t* __restrict__ bank, Layout L, int64_t e0, int64_
     int64_t e = er / L.n + e0, r = er % L.n;
     int64_t rt = r / TILE_ROWS, rr = r % TILE_ROWS;
     int64_t prb = piece_row_bytes(L, kp);
-    uint8_t* dst = bank + (e - e0) * L.expert_bytes + piece_offset(L, rt, kp) + rr * prb;
+    uint8_t blk[272];  // the row's bytes of this piece, written to the tiled layout below
+    uint8_t* dst = blk;
     int64_t c0 = (int64_t)kp * PIECE_K;
     int64_t klen = L.k - c0 < PIECE_K ? L.k - c0 : PIECE_K;
     float x[256];
@@ -371,6 +368,8 @@ __global__ void k_synth(uint8_t* __restrict__ bank, Layout L, int64_t e0, int64_
             for (int b = 0; b < klen / 32; ++b) mxfp4_from_float_d(x + 32 * b, dst + 17 * b);
             break;
     }
+    uint8_t* ebank = bank + (e - e0) * L.expert_bytes;
+    for (int64_t b = 0; b < prb; ++b) ebank[tiled_offset(L, rt, rr, kp, b)] = blk[b];
 }
 
 __global__ void k_normal(float* __restrict__ out, int64_t n, uint64_t key, uint64_t offset, float std_) {
@@ -534,10 +533,11 @@ extern "C" int cwx_bank_download(const cwx_bank* b, int64_t e0, int64_t ne, void
 extern "C" int cwx_bank_dequantize(const cwx_bank* b, int64_t expert, float* out, void* stream) {
     if (!b || !out) return fail(CWX_EINVAL, "cwx_bank_dequantize: null argument");
     if (expert < 0 || expert >= b->L.n_experts) return fail(CWX_EINVAL, "cwx_bank_dequantize: expert out of range");
-    if (b->L.k % 32) return fail(CWX_EUNSUPPORTED, "cwx_bank_dequantize: k must be a multiple of 32");
+    if (b->L.k % 16) return fail(CWX_EUNSUPPORTED, "cwx_bank_dequantize: k must be a multiple of 16");
     CWX_CUDA(cudaSetDevice(b->device));
-    int64_t units = b->L.n * (b->L.k / 32);
-    k_dequant<<<(unsigned)((units + 127) / 128), 128, 0, (cudaStream_t)stream>>>(b->d, b->L, expert, out);
+    int64_t units = b->L.n * (b->L.k / 16);
+    k_dequant<<<(unsigned)((units + 127) / 128), 128, HTABLES_BYTES, (cudaStream_t)stream>>>(b->d, b->L, expert,
+                                                                                              out);
     CWX_CUDA(cudaGetLastError());
     return CWX_OK;
 }

@@ -121,6 +121,41 @@ inline bool make_layout(int fmt, int64_t n, int64_t k, int64_t e, Layout* L) {
 // Note for partial tiles: every piece of a tile has the same padded size except the tail piece,
 // so piece_offset() is exact for full pieces before the tail; tiles are laid out back to back.
 
+// IQ2_S and IQ3_S pieces (one 256-column block per row) are stored as groups of 16 rows, each
+// group field by field (all rows' qs, then signs, qh, scales, d), so every field a thread reads is
+// aligned for a vector load. Same bytes, reordered; other formats keep whole rows.
+__host__ __device__ inline bool fmt_soa(int fmt) { return fmt == F_IQ2_S || fmt == F_IQ3_S; }
+
+// Where byte b of a GGUF block goes inside a 16-row group: the field's first GGUF byte, its bytes
+// per row, and its offset in the group. IQ2_S block = d(2) qs(32) signs(32) qh(8) scales(8);
+// IQ3_S block = d(2) qs(64) qh(8) signs(32) scales(4).
+struct SoaField {
+    int gguf_off, bytes, group_off;
+};
+__host__ __device__ inline SoaField soa_field(int fmt, int b) {
+    if (fmt == F_IQ2_S) {
+        if (b < 2) return {0, 2, 1280};
+        if (b < 34) return {2, 32, 0};
+        if (b < 66) return {34, 32, 512};
+        if (b < 74) return {66, 8, 1024};
+        return {74, 8, 1152};
+    }
+    if (b < 2) return {0, 2, 1728};
+    if (b < 66) return {2, 64, 0};
+    if (b < 74) return {66, 8, 1536};
+    if (b < 106) return {74, 32, 1024};
+    return {106, 4, 1664};
+}
+
+// Byte b of row rr (row inside its 64-row tile rt) of piece kp -> offset inside the expert.
+__host__ __device__ inline int64_t tiled_offset(const Layout& L, int64_t rt, int64_t rr, int kp, int64_t b) {
+    const int64_t prb = piece_row_bytes(L, kp);
+    const int64_t base = piece_offset(L, rt, kp);
+    if (!fmt_soa(L.fmt)) return base + rr * prb + b;
+    const SoaField f = soa_field(L.fmt, (int)b);
+    return base + (rr / 16) * 16 * prb + f.group_off + (rr % 16) * f.bytes + (b - f.gguf_off);
+}
+
 }  // namespace cwx
 
 struct cwx_bank {
@@ -139,6 +174,9 @@ struct cwx_ctx {
     int* h_err;   // pinned mirror
     uint16_t* d_iq3s_map;  // encoder maps for synthetic banks (built on first use)
     uint16_t* d_iq2s_map;
+    int profiling;     // record per-phase events (cwx_ctx_set_profiling)
+    void* prof;        // recorded (phase, start, end) events
+    int64_t launches;  // kernel launches issued through this context
 };
 
 namespace cwx {
@@ -174,11 +212,19 @@ __device__ inline void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                  : "memory");
 }
 
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
 // Bounded wait on an mbarrier phase. Returns false (and records DE_TIMEOUT) when the phase has
-// not completed after `limit` polls, so a lost copy ends the kernel instead of hanging the GPU.
-__device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, uint32_t limit = (1u << 26)) {
-    uint32_t a = smem_u32(bar);
-    for (uint32_t i = 0; i < limit; ++i) {
+// not completed within `limit_ns` of wall-clock time (try_wait may suspend the thread, so the
+// bound is on time, not on polls): a lost copy ends the kernel instead of hanging the GPU.
+__device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, uint64_t limit_ns = 2000000000ull) {
+    const uint32_t a = smem_u32(bar);
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
         uint32_t done;
         asm volatile(
             "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -186,9 +232,15 @@ __device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, uint3
             : "r"(a), "r"(parity)
             : "memory");
         if (done) return true;
+        if (i == 0) t0 = globaltimer_ns();
+        else if ((i & 255) == 0 && globaltimer_ns() - t0 > limit_ns) break;
     }
     dev_error(err, DE_TIMEOUT);
     return false;
+}
+
+__device__ inline void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // 1-D bulk copy global -> shared, completion signalled on `bar` (bytes and addresses 16-aligned).

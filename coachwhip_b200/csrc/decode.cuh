@@ -1,26 +1,36 @@
-// Device dequantisation of GGUF quant blocks, 32 consecutive weights of one row at a time.
+// Device dequantisation of GGUF quant blocks.
 //
-// Each routine reproduces the reference's to_float arithmetic operation for operation (the
-// products and differences use the _rn intrinsics so no FMA contraction changes a rounding),
-// so the f32 values are bit-identical to the CPU restatement:
+// The exact routines reproduce the reference's to_float arithmetic operation for operation (the
+// products and differences use the _rn intrinsics so no FMA contraction changes a rounding), so
+// the f32 values are bit-identical to the CPU restatement:
 //   Q4_K  vendor/candle-core/src/quantized/k_quants.rs:1821-1848
 //   Q6_K  k_quants.rs:2420-2451          Q8_0 k_quants.rs:766-782
 //   MXFP4 k_quants.rs:673-691 (+ e8m0_to_f32_half 642-649)
 //   IQ3_S vendor/candle-metal-kernels/src/metal_src/quantized.metal:6892-6915
 //   IQ2_S quantized.metal:6917-6934
-// `row` points at one row's bytes of one 256-column K-piece (see the tiled layout in
-// cwx_common.cuh); `u` is the 32-column unit inside the piece (0..7).
+// The fast IQ paths produce f16 pairs for the tensor cores: the codebook values are exact in f16,
+// the per-16/32-column scale is rounded to f16 (about 2^-11 relative per weight).
+//
+// Row addressing (see the tiled layout in cwx_common.cuh): K-quants, Q8_0 and MXFP4 rows are
+// whole (row r of a piece at r * piece_row_bytes); IQ2_S / IQ3_S pieces are 16-row groups stored
+// field by field, addressed through IqRow.
 #pragma once
 #include "cwx_common.cuh"
 #include "iq_grids.h"
 
 namespace cwx {
 
-struct Tables {
-    const uint64_t* iq2s;  // 1024 entries, 8 grid bytes each
-    const uint32_t* iq3s;  // 512 entries, 4 grid bytes each
+// f16 codebooks and sign masks in shared memory (codebook values are small integers, exact in f16).
+struct HTables {
+    const uint4* g2;   // IQ2_S: 1024 entries x 8 halves
+    const uint2* g3;   // IQ3_S: 512 entries x 4 halves
+    const uint4* sgn;  // sign byte -> f16 sign bits of 8 values (4 words of 2 halves)
 };
+constexpr int HTABLES_BYTES = 16384 + 4096 + 4096;
 
+__device__ __forceinline__ float half_at(const void* p, int j) {
+    return __half2float(reinterpret_cast<const __half*>(p)[j]);
+}
 __device__ __forceinline__ float h2f_bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 __device__ __forceinline__ uint16_t ld_u16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
 
@@ -34,124 +44,222 @@ __device__ __forceinline__ void get_scale_min_k4(int j, const uint8_t* q, int* d
     }
 }
 
-__device__ __forceinline__ void dec_q4k(const uint8_t* b, int u, float* w) {
-    float d = h2f_bits(ld_u16(b)), mn = h2f_bits(ld_u16(b + 2));
-    const uint8_t* scales = b + 4;
-    const uint8_t* q = b + 16 + 32 * (u >> 1);
-    int sc, m;
-    get_scale_min_k4(u, scales, &sc, &m);
-    float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(mn, (float)m);
-    int shift = (u & 1) * 4;
-#pragma unroll
-    for (int l = 0; l < 32; ++l) w[l] = __fsub_rn(__fmul_rn(d1, (float)((q[l] >> shift) & 0xF)), m1);
-}
-
-__device__ __forceinline__ void dec_q6k(const uint8_t* b, int u, float* w) {
-    const uint8_t* ql = b;
-    const uint8_t* qh = b + 128;
-    const int8_t* sc = (const int8_t*)(b + 192);
-    float d = h2f_bits(ld_u16(b + 208));
-    int half = u >> 2, v = u & 3;
-    ql += 64 * half;
-    qh += 32 * half;
-    sc += 8 * half;
-#pragma unroll
-    for (int l = 0; l < 32; ++l) {
-        int q;
-        if (v == 0) q = (ql[l] & 0xF) | ((qh[l] & 3) << 4);
-        else if (v == 1) q = (ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4);
-        else if (v == 2) q = (ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4);
-        else q = (ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4);
-        w[l] = __fmul_rn(__fmul_rn(d, (float)sc[l / 16 + 2 * v]), (float)(q - 32));
-    }
-}
-
-__device__ __forceinline__ void dec_q8_0(const uint8_t* b, int u, float* w) {
-    b += 34 * u;
-    float d = h2f_bits(ld_u16(b));
-    const int8_t* qs = (const int8_t*)(b + 2);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) w[j] = __fmul_rn((float)qs[j], d);
-}
-
 __device__ __forceinline__ float e8m0_to_f32_half(uint8_t e) {
     uint32_t bits = e < 2 ? (0x00200000u << e) : ((uint32_t)(e - 1) << 23);
     return __uint_as_float(bits);
 }
 
-__device__ __forceinline__ void dec_mxfp4(const uint8_t* b, int u, float* w) {
-    b += 17 * u;
-    float d = e8m0_to_f32_half(b[0]);
-    const int8_t kv[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        uint8_t q = b[1 + j];
-        w[j] = __fmul_rn((float)kv[q & 0xF], d);
-        w[j + 16] = __fmul_rn((float)kv[q >> 4], d);
-    }
+// One row's fields of an IQ2_S / IQ3_S block inside a 16-row group.
+struct IqRow {
+    const uint8_t *qs, *signs, *qh, *sc, *d;
+};
+__device__ __forceinline__ IqRow iq_row(int fmt, const uint8_t* group, int rg) {
+    if (fmt == F_IQ2_S)
+        return {group + rg * 32, group + 512 + rg * 32, group + 1024 + rg * 8, group + 1152 + rg * 8, group + 1280 + rg * 2};
+    return {group + rg * 64, group + 1024 + rg * 32, group + 1536 + rg * 8, group + 1664 + rg * 4, group + 1728 + rg * 2};
+}
+// Row rr of a piece (or of rows staged from it, starting at a 16-row boundary), rows prb bytes.
+__device__ __forceinline__ IqRow iq_row_in(int fmt, const uint8_t* piece, int rr, int64_t prb) {
+    return iq_row(fmt, piece + (int64_t)(rr >> 4) * 16 * prb, rr & 15);
 }
 
-__device__ __forceinline__ void dec_iq3s(const uint8_t* b, int ib, float* w, const uint32_t* grid) {
-    float d = h2f_bits(ld_u16(b));
-    const uint8_t* qs = b + 2 + 8 * ib;
-    uint8_t qh = b[66 + ib];
-    const uint8_t* signs = b + 74 + 4 * ib;
-    uint8_t scb = b[106 + ib / 2];
-    float dl = __fmul_rn(d, (float)(1 + 2 * ((scb >> (4 * (ib & 1))) & 0xF)));
+// ---------------------------------------------------------------- exact 16-column runs
+// 16 consecutive columns [kofs, kofs+16) of one row's 256-column piece, bit-exact f32.
+__device__ __forceinline__ void dec16_iq_exact(int fmt, const IqRow& r, int kofs, float* v, const HTables& t) {
+    const int ib = kofs >> 5;
+    const float d = h2f_bits(*reinterpret_cast<const uint16_t*>(r.d));
+    const uint8_t qh = r.qh[ib];
+    if (fmt == F_IQ2_S) {
+        const int g0 = (kofs & 16) >> 3;  // 2 groups of 8
+        const float dl = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)((r.sc[ib] >> (4 * (g0 >> 1))) & 0xF))), 0.25f);
 #pragma unroll
-    for (int g = 0; g < 8; ++g) {
-        uint32_t gv = grid[qs[g] | (((qh >> g) & 1) << 8)];
-        uint8_t s = signs[g >> 1] >> (4 * (g & 1));
+        for (int gi = 0; gi < 2; ++gi) {
+            const int g = g0 + gi;
+            const uint4* gv = &t.g2[r.qs[4 * ib + g] | (((qh >> (2 * g)) & 3) << 8)];
+            const uint8_t sg = r.signs[4 * ib + g];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            float v = __fmul_rn(dl, (float)((gv >> (8 * j)) & 0xFF));
-            w[4 * g + j] = ((s >> j) & 1) ? -v : v;
+            for (int j = 0; j < 8; ++j) {
+                const float x = __fmul_rn(dl, half_at(gv, j));
+                v[8 * gi + j] = ((sg >> j) & 1) ? -x : x;
+            }
+        }
+    } else {
+        const int g0 = (kofs & 16) >> 2;  // 4 groups of 4
+        const float dl = __fmul_rn(d, (float)(1 + 2 * ((r.sc[ib >> 1] >> (4 * (ib & 1))) & 0xF)));
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi) {
+            const int g = g0 + gi;
+            const uint2* gv = &t.g3[r.qs[8 * ib + g] | (((qh >> g) & 1) << 8)];
+            const uint8_t sg = r.signs[4 * ib + (g >> 1)] >> (4 * (g & 1));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float x = __fmul_rn(dl, half_at(gv, j));
+                v[4 * gi + j] = ((sg >> j) & 1) ? -x : x;
+            }
         }
     }
 }
 
-__device__ __forceinline__ void dec_iq2s(const uint8_t* b, int ib, float* w, const uint64_t* grid) {
-    float d = h2f_bits(ld_u16(b));
-    const uint8_t* qs = b + 2 + 4 * ib;
-    const uint8_t* signs = b + 34 + 4 * ib;
-    uint8_t qh = b[66 + ib];
-    uint8_t scb = b[74 + ib];
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-        float dl = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)((scb >> (4 * (g >> 1))) & 0xF))), 0.25f);
-        uint64_t gv = grid[qs[g] | (((qh >> (2 * g)) & 3) << 8)];
-        uint8_t s = signs[g];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float v = __fmul_rn(dl, (float)((gv >> (8 * j)) & 0xFF));
-            w[8 * g + j] = ((s >> j) & 1) ? -v : v;
-        }
-    }
-}
-
-// 32 weights of unit u of one row of a K-piece, bit-exact f32.
-__device__ __forceinline__ void decode_unit(int fmt, const uint8_t* row, int u, float* w, const Tables& t) {
+// Whole-row formats: `b` is the row's bytes of its piece.
+__device__ __forceinline__ void dec16_row_exact(int fmt, const uint8_t* b, int kofs, float* v) {
     switch (fmt) {
-        case F_Q4_K: dec_q4k(row, u, w); break;
-        case F_Q6_K: dec_q6k(row, u, w); break;
-        case F_Q8_0: dec_q8_0(row, u, w); break;
-        case F_MXFP4: dec_mxfp4(row, u, w); break;
-        case F_IQ3_S: dec_iq3s(row, u, w, t.iq3s); break;
-        case F_IQ2_S: dec_iq2s(row, u, w, t.iq2s); break;
+        case F_Q4_K: {
+            const float d = h2f_bits(ld_u16(b)), mn = h2f_bits(ld_u16(b + 2));
+            const int j = kofs >> 5, l0 = kofs & 16;
+            int sc, m;
+            get_scale_min_k4(j, b + 4, &sc, &m);
+            const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(mn, (float)m);
+            const uint8_t* q = b + 16 + 32 * (j >> 1) + l0;
+            const int sh = (j & 1) * 4;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __fsub_rn(__fmul_rn(d1, (float)((q[i] >> sh) & 0xF)), m1);
+            break;
+        }
+        case F_Q6_K: {
+            const int half = kofs >> 7, u = (kofs >> 5) & 3, l0 = kofs & 16;
+            const uint8_t* ql = b + 64 * half;
+            const uint8_t* qh = b + 128 + 32 * half;
+            const int8_t* sc = (const int8_t*)(b + 192) + 8 * half;
+            const float d = h2f_bits(ld_u16(b + 208));
+            const float ds = __fmul_rn(d, (float)sc[(l0 >> 4) + 2 * u]);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int l = l0 + i;
+                int q;
+                if (u == 0) q = (ql[l] & 0xF) | ((qh[l] & 3) << 4);
+                else if (u == 1) q = (ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4);
+                else if (u == 2) q = (ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4);
+                else q = (ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4);
+                v[i] = __fmul_rn(ds, (float)(q - 32));
+            }
+            break;
+        }
+        case F_Q8_0: {
+            const uint8_t* blk = b + 34 * (kofs >> 5);
+            const float d = h2f_bits(ld_u16(blk));
+            const int8_t* qs = (const int8_t*)(blk + 2) + (kofs & 16);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __fmul_rn((float)qs[i], d);
+            break;
+        }
+        case F_MXFP4: {
+            const uint8_t* blk = b + 17 * (kofs >> 5);
+            const float d = e8m0_to_f32_half(blk[0]);
+            const int8_t kv[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+            const int sh = (kofs & 16) ? 4 : 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __fmul_rn((float)kv[(blk[1 + i] >> sh) & 0xF], d);
+            break;
+        }
         default:
 #pragma unroll
-            for (int j = 0; j < 32; ++j) w[j] = 0.f;
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
     }
 }
 
+// Any format: row rr of a piece whose rows are prb bytes.
+__device__ __forceinline__ void dec16_exact(int fmt, const uint8_t* piece, int rr, int64_t prb, int kofs, float* v,
+                                            const HTables& t) {
+    if (fmt_soa(fmt)) dec16_iq_exact(fmt, iq_row_in(fmt, piece, rr, prb), kofs, v, t);
+    else dec16_row_exact(fmt, piece + (int64_t)rr * prb, kofs, v);
+}
+
+// ---------------------------------------------------------------- fast f16 IQ paths
+__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, __half2 s) {
+    __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), s);
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// A thread's 64 columns [64c, 64c+64) of one row of an IQ piece: the metadata is loaded once,
+// then each 16-column run (ss = 0..3) is produced as 8 f16 pairs.
+struct IqRun {
+    uint64_t qs0, qs1;  // IQ2_S: 8 code bytes (qs0); IQ3_S: 16 code bytes
+    uint64_t sg;        // sign bits of the 64 columns
+    uint32_t qh;        // two qh bytes
+    uint32_t sc;        // IQ2_S: two scale bytes; IQ3_S: one
+    float d;
+};
+
+__device__ __forceinline__ IqRun iq_run_load(int fmt, const IqRow& r, int c) {
+    IqRun q;
+    q.d = h2f_bits(*reinterpret_cast<const uint16_t*>(r.d));
+    q.qh = *reinterpret_cast<const uint16_t*>(r.qh + 2 * c);
+    q.sg = *reinterpret_cast<const uint64_t*>(r.signs + 8 * c);
+    if (fmt == F_IQ2_S) {
+        q.qs0 = *reinterpret_cast<const uint64_t*>(r.qs + 8 * c);
+        q.qs1 = 0;
+        q.sc = *reinterpret_cast<const uint16_t*>(r.sc + 2 * c);
+    } else {
+        const uint4 v = *reinterpret_cast<const uint4*>(r.qs + 16 * c);
+        q.qs0 = ((uint64_t)v.y << 32) | v.x;
+        q.qs1 = ((uint64_t)v.w << 32) | v.z;
+        q.sc = r.sc[c];
+    }
+    return q;
+}
+
+// Columns 64c + 16ss .. +16 as 8 f16 pairs.
+__device__ __forceinline__ void iq_run_pairs(int fmt, const IqRun& q, int ss, uint32_t* p, const HTables& t) {
+    if (fmt == F_IQ2_S) {
+        const float dl = __fmul_rn(__fmul_rn(q.d, __fadd_rn(0.5f, (float)((q.sc >> (4 * ss)) & 0xF))), 0.25f);
+        const __half2 s2 = __float2half2_rn(dl);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int gi = 2 * ss + h;
+            const uint32_t e = (uint32_t)((q.qs0 >> (8 * gi)) & 0xFF) | (((q.qh >> (2 * gi)) & 3) << 8);
+            const uint4 gv = t.g2[e];
+            const uint4 m = t.sgn[(q.sg >> (8 * gi)) & 0xFF];
+            p[4 * h + 0] = hmul2_u(gv.x ^ m.x, s2);
+            p[4 * h + 1] = hmul2_u(gv.y ^ m.y, s2);
+            p[4 * h + 2] = hmul2_u(gv.z ^ m.z, s2);
+            p[4 * h + 3] = hmul2_u(gv.w ^ m.w, s2);
+        }
+    } else {
+        const float dl = __fmul_rn(q.d, (float)(1 + 2 * ((q.sc >> (4 * (ss >> 1))) & 0xF)));
+        const __half2 s2 = __float2half2_rn(dl);
+        const uint64_t qsw = ss < 2 ? q.qs0 : q.qs1;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const int gi = 4 * ss + h;
+            const uint32_t e = (uint32_t)((qsw >> (8 * (gi & 7))) & 0xFF) | (((q.qh >> gi) & 1) << 8);
+            const uint2 gv = t.g3[e];
+            const uint4 m = t.sgn[(q.sg >> (4 * gi)) & 0xF];
+            p[2 * h + 0] = hmul2_u(gv.x ^ m.x, s2);
+            p[2 * h + 1] = hmul2_u(gv.y ^ m.y, s2);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- tables
 static __device__ const uint16_t d_iq2s_codes[1024] = CWX_IQ2S_CODES;
 static __device__ const uint16_t d_iq3s_codes[512] = CWX_IQ3S_CODES;
 
-// Expand the packed codebooks into shared memory (called by every thread of a CTA; the caller
-// synchronises before use).
-__device__ __forceinline__ void load_tables(uint64_t* s_iq2s, uint32_t* s_iq3s) {
-    for (int i = threadIdx.x; i < 1024; i += blockDim.x) s_iq2s[i] = cwx_iq2s_expand(d_iq2s_codes[i]);
-    for (int i = threadIdx.x; i < 512; i += blockDim.x) s_iq3s[i] = cwx_iq3s_expand(d_iq3s_codes[i]);
+// Expand the packed codebooks into f16 tables in shared memory (every thread of the CTA calls
+// this; the caller synchronises before use).
+__device__ __forceinline__ void load_htables(uint4* g2, uint2* g3, uint4* sgn) {
+    for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
+        const uint64_t v = cwx_iq2s_expand(d_iq2s_codes[i]);
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            __half2 h = __floats2half2_rn((float)((v >> (16 * j)) & 0xFF), (float)((v >> (16 * j + 8)) & 0xFF));
+            w[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        g2[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+        const uint32_t v = cwx_iq3s_expand(d_iq3s_codes[i]);
+        __half2 a = __floats2half2_rn((float)(v & 0xFF), (float)((v >> 8) & 0xFF));
+        __half2 b = __floats2half2_rn((float)((v >> 16) & 0xFF), (float)(v >> 24));
+        g3[i] = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+    }
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            w[j] = (((i >> (2 * j)) & 1) ? 0x8000u : 0u) | (((i >> (2 * j + 1)) & 1) ? 0x80000000u : 0u);
+        sgn[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
 }
 
 }  // namespace cwx

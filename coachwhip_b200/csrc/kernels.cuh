@@ -1,4 +1,5 @@
-// Argument blocks and host launchers of the cwx kernels (route.cu, gemv.cu), used by api.cu.
+// Argument blocks and host launchers of the cwx kernels (route.cu, gemv.cu, act.cu), used by
+// api.cu.
 #pragma once
 #include "cwx_common.cuh"
 
@@ -9,38 +10,33 @@ struct MatRef {
     Layout L;
 };
 
-// One grouped-product launch: routed piles of one or two matrices (+ optional shared expert).
+// One matrix of a grouped-product launch.
+struct GemvJob {
+    MatRef m;
+    int shared;         // 0: routed piles (rows by pick); 1: every token (the shared expert)
+    const uint8_t* b;   // packed activation rows (act.cu), bstride bytes apart
+    int64_t bstride;
+    int bdiv;           // routed: activation row = pick index / bdiv
+    float* out;         // output rows: pick index (routed) or token (shared)
+    int64_t ostride;
+    int split;          // weights carried as an f16 hi + lo pair
+    const float* bias;  // (n_experts, n) added to the outputs, or NULL
+};
+
 struct GemvArgs {
-    int two;  // 1: gate and up (+ activation) -> hidden rows; 0: one matrix -> output rows
-    MatRef ra, rb;
-    const __half* rbh;  // activation rows (hi part), f16, (rows, K)
-    const __half* rbl;  // activation rows (lo part)
-    int64_t r_bstride;
-    int r_bdiv;  // activation row = pick index / r_bdiv
-    float* rout;
-    int64_t r_ostride;
+    int njobs;
+    GemvJob job[4];
     const uint32_t* pairs;
     const uint32_t* used3;  // (expert, first pair, count) per used expert
     const uint32_t* n_used;
-    int has_shared;
-    MatRef sa, sb;
-    const __half* sbh;
-    const __half* sbl;
-    int64_t s_bstride;
-    float* sout;
-    int64_t s_ostride;
-    int s_count;
-    int act;
-    float alpha, limit;
-    const float* gate_b;
-    const float* up_b;
-    const float* down_b;
-    int split_r, split_s;  // weights carried as an f16 hi + lo pair (routed, shared items)
+    int s_count;  // tokens of the shared jobs
     int* err;
-    int stage_bytes;  // set by launch_gemv
-    int stage_b_off;
+    int stage_bytes;  // set by the launcher
     int nst;
 };
+
+// Bytes of one packed activation row of k columns (1024 per 256-column piece).
+__host__ __device__ inline int64_t packed_row_bytes(int64_t k) { return (k + PIECE_K - 1) / PIECE_K * 1024; }
 
 int launch_router(const float* x, const float* w, const float* b, int T, int H, int E, float* logits,
                   cudaStream_t st);
@@ -49,9 +45,26 @@ int launch_route(const float* logits, int T, int E, int K, int norm, uint32_t* i
 size_t perm_scratch_bytes(int64_t n, int E);
 int launch_permute(const uint32_t* ids, int64_t n, int E, uint32_t* pairs, uint32_t* heads, uint32_t* used3,
                    uint32_t* n_used, uint32_t* scratch, int* err, cudaStream_t st);
-int launch_prep(const float* src, int64_t R, int64_t K, int mode, __half* hi, __half* lo, cudaStream_t st);
+
+// Activation preparation: rows (R, K) -> packed f16 hi/lo rows in the order the grouped products
+// read. With `up` set, the input is the activation of (gate, up): SiLU, or clamped SwiGLU with
+// per-expert biases (expert of row r = ids[r], rows being pick indices).
+struct PrepArgs {
+    const float* src;  // (R, K) f32: x, or gate outputs
+    const float* up;   // (R, K) up outputs, or NULL
+    int64_t R, K;
+    int mode;          // ActMode
+    int act;           // CWX_ACT_* when up is set
+    float alpha, limit;
+    const float* gate_b;
+    const float* up_b;
+    const uint32_t* ids;
+    uint8_t* out;
+};
+int launch_prep(const PrepArgs& p, cudaStream_t st);
 int launch_combine(const float* rows, const float* w, int T, int K, int H, const float* shared, const float* sgate,
                    const float* residual, float* out, cudaStream_t st);
-int launch_gemv(GemvArgs a, int64_t max_items, int device, int sm_count, cudaStream_t st);
+// experts_est: the number of experts expected to have picks (sizes the grid and the K split).
+int launch_gemv(const GemvArgs& a, int64_t experts_est, int device, int sm_count, cudaStream_t st);
 
 }  // namespace cwx

@@ -37,8 +37,8 @@ __device__ __forceinline__ float avx_lane_tree(float acc) {
     return __shfl_sync(0xffffffffu, r, 0);
 }
 
-// logits (T, E): one warp per (expert, K quarter), tokens in chunks of 8, f64 partial sums
-// reduced in a fixed order. Block = 8 warps = 2 experts.
+// logits (T, E): one warp per (expert, K quarter), 8 tokens per block row (blockIdx.y), f64
+// partial sums reduced in a fixed order. Block = 8 warps = 2 experts.
 __global__ void __launch_bounds__(256) k_router(const float* __restrict__ x, const float* __restrict__ w,
                                                 const float* __restrict__ bias, int T, int H, int E,
                                                 float* __restrict__ logits) {
@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(256) k_router(const float* __restrict__ x, con
     int kq = (H + 3) / 4;
     int k0 = q * kq, k1 = min(H, k0 + kq);
     const float* wr = w + (int64_t)(e < E ? e : 0) * H;
-    for (int t0 = 0; t0 < T; t0 += 8) {
+    for (int t0 = 8 * blockIdx.y; t0 < T; t0 += 8 * gridDim.y) {
         double acc[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[j] = 0.0;
@@ -308,7 +308,9 @@ __global__ void __launch_bounds__(1024) k_perm_scatter(const uint32_t* __restric
 int launch_router(const float* x, const float* w, const float* b, int T, int H, int E, float* logits,
                   cudaStream_t st) {
     if (T == 0) return CWX_OK;
-    k_router<<<(E + 1) / 2, 256, 0, st>>>(x, w, b, T, H, E, logits);
+    int ty = (T + 7) / 8;
+    if (ty > 64) ty = 64;
+    k_router<<<dim3((E + 1) / 2, ty), 256, 0, st>>>(x, w, b, T, H, E, logits);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_router");
 }

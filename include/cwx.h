@@ -158,6 +158,28 @@ typedef struct {
 /* out = routed experts (weighted) + shared expert * sigmoid(x . sh_gate_inp) (+ residual). */
 int cwx_moe_forward(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_moe_args* args, void* stream);
 
+/* Per-phase timing of cwx_moe_forward, the analogue of the reference's --profile Stats
+ * (crates/engine/src/experts.rs:2541-2552): with profiling on, each call records a CUDA event
+ * pair around every phase on its stream (also inside stream capture, where the events become
+ * graph nodes and record again on every replay). */
+#define CWX_PHASE_ROUTER 0  /* router logits */
+#define CWX_PHASE_ROUTE 1   /* softmax, top-k, shared gate */
+#define CWX_PHASE_PILES 2   /* permutation */
+#define CWX_PHASE_PREP 3    /* activation preparation (all prep launches) */
+#define CWX_PHASE_GATE_UP 4 /* gate/up expert products */
+#define CWX_PHASE_DOWN 5    /* down expert products */
+#define CWX_PHASE_COMBINE 6 /* weighted combine + shared expert + residual */
+#define CWX_N_PHASES 7
+int cwx_ctx_set_profiling(cwx_ctx* ctx, int enabled);
+/* Synchronises the device; adds each recorded phase's elapsed milliseconds into ms[phase] and
+ * its occurrences into count[phase] (arrays of CWX_N_PHASES; either may be NULL); keeps the
+ * recorded events, so a replayed graph can be read again after each replay. */
+int cwx_ctx_read_profile(cwx_ctx* ctx, double* ms, int64_t* count);
+/* Drops the recorded events. */
+int cwx_ctx_reset_profile(cwx_ctx* ctx);
+/* Kernel launches issued through this context since creation. */
+int64_t cwx_ctx_launches(const cwx_ctx* ctx);
+
 #ifdef __cplusplus
 }
 #endif

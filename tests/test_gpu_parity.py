@@ -208,6 +208,10 @@ SPECS = {
     "q6k": Spec(hidden=512, n_experts=16, top_k=2, inter=256, gate_type=O.Q6_K, up_type=O.Q6_K, down_type=O.Q6_K,
                 norm=False),
     "q8_0": Spec(hidden=256, n_experts=8, top_k=3, inter=128, gate_type=O.Q8_0, up_type=O.Q8_0, down_type=O.Q8_0),
+    # full config-1 width (hidden 2048: eight 256-column pieces), few experts: small batches take
+    # the K-split (4 and 8 slices per item) paths of the grouped products
+    "iq_wide": Spec(hidden=2048, n_experts=16, top_k=2, inter=512, gate_type=O.IQ2_S, up_type=O.IQ2_S,
+                    down_type=O.IQ3_S, shared_inter=512, seed=2),
 }
 
 
