@@ -18,7 +18,7 @@ ACT_SILU, ACT_CLAMPED_SWIGLU = 0, 1
 EXPORTS = [
     "cwx_last_error", "cwx_version", "cwx_ctx_create", "cwx_ctx_destroy", "cwx_ctx_reserve", "cwx_ctx_status",
     "cwx_bank_create", "cwx_bank_synth", "cwx_bank_destroy", "cwx_bank_desc", "cwx_bank_download",
-    "cwx_bank_dequantize", "cwx_synth_normal", "cwx_route", "cwx_permute", "cwx_expert_matmul", "cwx_moe_forward",
+    "cwx_bank_dequantize", "cwx_synth_normal", "cwx_route", "cwx_permute", "cwx_permute_noalloc", "cwx_expert_matmul", "cwx_moe_forward",
     "cwx_ctx_set_profiling", "cwx_ctx_read_profile", "cwx_ctx_reset_profile", "cwx_ctx_launches",
 ]
 PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine"]
@@ -88,6 +88,7 @@ def lib() -> ctypes.CDLL:
             "cwx_synth_normal": (I32, [P, U64, U64, I64, F, P, P]),
             "cwx_route": (I32, [P, P, I32, I32, I32, I32, P, P, P]),
             "cwx_permute": (I32, [P, P, I32, I32, I32, P, P, P]),
+            "cwx_permute_noalloc": (I32, [P, I32, I32, I32, P, P, P, P]),
             "cwx_expert_matmul": (I32, [P, P, P, I32, P, I32, I32, I32, P, P]),
             "cwx_moe_forward": (I32, [P, ctypes.POINTER(MoeLayer), ctypes.POINTER(MoeArgs), P]),
             "cwx_ctx_set_profiling": (I32, [P, I32]),

@@ -115,6 +115,21 @@ int cwx_route(cwx_ctx* ctx, const float* logits, int32_t tokens, int32_t n_exper
 int cwx_permute(cwx_ctx* ctx, const uint32_t* ids, int32_t tokens, int32_t top_k, int32_t n_experts,
                 uint32_t* pairs, uint32_t* heads, void* stream);
 
+/* cwx_permute for callers that must not allocate (no counterpart in the reference; it has no
+ * such constraint). For code that cannot let a call allocate device memory: inside CUDA stream
+ * capture, under a caller-owned memory pool, or without a cwx_ctx. Same pairs and heads as
+ * cwx_permute; the scratch is a fixed 1 MiB device array of this library, so the call makes no
+ * allocation. Limits: n_experts <= 4096 and
+ * ceil(tokens*top_k / 1024) * n_experts + 3 * n_experts + 8 <= CWX_NOALLOC_SCRATCH_WORDS;
+ * larger calls return CWX_EINVAL. Runs on the current device (stream must belong to it). The
+ * array is shared per device, so calls on one device must not overlap (one stream, or ordered
+ * streams); overlapping calls race. The first call on a device looks up the array's address:
+ * make it outside stream capture. dev_status (optional device int) receives 0, or nonzero when
+ * an id was >= n_experts. */
+#define CWX_NOALLOC_SCRATCH_WORDS 262144
+int cwx_permute_noalloc(const uint32_t* ids, int32_t tokens, int32_t top_k, int32_t n_experts, uint32_t* pairs,
+                        uint32_t* heads, int32_t* dev_status, void* stream);
+
 /* MoeMatvec: out (tokens, nei0, n) f32 = for each token t and pick j, one input row times the
  * bank matrix of expert ids[t][j]. x is (tokens, k) f32 when rows_per_expert == 0, else
  * (tokens*nei0, k) with one row per pick. act_mode: CWX_ACT_MODE_*. Device pointers. */
