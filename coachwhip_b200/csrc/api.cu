@@ -404,6 +404,7 @@ extern "C" int cwx_expert_matmul(cwx_ctx* c, const cwx_bank* bank, const float* 
     a.pairs = pairs;
     a.used3 = used3;
     a.n_used = n_used;
+    a.tok_est = tokens;
     a.err = c->d_err;
     c->launches += 5;
     return launch_gemv(a, n < E ? n : E, c->device, c->sm_count, st);
@@ -473,6 +474,7 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
         a.used3 = p.used3;
         a.n_used = p.n_used;
         a.s_count = T;
+        a.tok_est = T;
         a.err = c->d_err;
         PhaseTimer t(c, st, CWX_PHASE_GATE_UP);
         if ((rc = launch_gemv(a, used_max, c->device, c->sm_count, st))) return rc;
@@ -502,6 +504,7 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
         d.used3 = p.used3;
         d.n_used = p.n_used;
         d.s_count = T;
+        d.tok_est = T;
         d.err = c->d_err;
         PhaseTimer t(c, st, CWX_PHASE_DOWN);
         if ((rc = launch_gemv(d, used_max, c->device, c->sm_count, st))) return rc;

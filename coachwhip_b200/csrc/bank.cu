@@ -61,7 +61,7 @@ __global__ void k_dequant(const uint8_t* __restrict__ bank, Layout L, int64_t e,
     const int64_t rt = r / TILE_ROWS, rr = r % TILE_ROWS;
     const uint8_t* piece = bank + e * L.expert_bytes + piece_offset(L, rt, kp);
     float w[16];
-    dec16_exact(L.fmt, piece, (int)rr, piece_row_bytes(L, kp), kofs, w, t);
+    dec16_exact<true>(L.fmt, piece, (int)rr, piece_row_bytes(L, kp), kofs, w, t);
     float* o = out + r * L.k + uk * 16;
 #pragma unroll
     for (int j = 0; j < 16; ++j) o[j] = w[j];

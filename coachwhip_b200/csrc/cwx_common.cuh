@@ -122,29 +122,33 @@ inline bool make_layout(int fmt, int64_t n, int64_t k, int64_t e, Layout* L) {
 // so piece_offset() is exact for full pieces before the tail; tiles are laid out back to back.
 
 // IQ2_S and IQ3_S pieces (one 256-column block per row) are stored as groups of 16 rows, each
-// group field by field (all rows' qs, then signs, qh, scales, d), so every field a thread reads is
-// aligned for a vector load. Same bytes, reordered; other formats keep whole rows.
+// group field by field, so that what one thread of the grouped products reads (a row's fields
+// for 64 consecutive columns, c4 = which 64) is one aligned vector. Same bytes, reordered; other
+// formats keep whole rows.
+//   IQ2_S group (16 x 82 = 1312 B): per (row, c4) a 16-byte record [qs 8 B | signs 8 B] at
+//     (row*4 + c4)*16; per (row, c4) a 4-byte record [qh 2 B | scales 2 B] at 1024 + (row*4+c4)*4;
+//     d at 1280 + row*2.
+//   IQ3_S group (16 x 110 = 1760 B): qs at row*64, signs at 1024 + row*32, qh at 1536 + row*8,
+//     scales at 1664 + row*4, d at 1728 + row*2.
+// GGUF blocks: IQ2_S = d(2) qs(32) signs(32) qh(8) scales(8); IQ3_S = d(2) qs(64) qh(8) signs(32)
+// scales(4).
 __host__ __device__ inline bool fmt_soa(int fmt) { return fmt == F_IQ2_S || fmt == F_IQ3_S; }
 
-// Where byte b of a GGUF block goes inside a 16-row group: the field's first GGUF byte, its bytes
-// per row, and its offset in the group. IQ2_S block = d(2) qs(32) signs(32) qh(8) scales(8);
-// IQ3_S block = d(2) qs(64) qh(8) signs(32) scales(4).
-struct SoaField {
-    int gguf_off, bytes, group_off;
-};
-__host__ __device__ inline SoaField soa_field(int fmt, int b) {
+// Offset inside a 16-row group of byte b of the GGUF block of row rg (0..15).
+__host__ __device__ inline int soa_offset(int fmt, int rg, int b) {
     if (fmt == F_IQ2_S) {
-        if (b < 2) return {0, 2, 1280};
-        if (b < 34) return {2, 32, 0};
-        if (b < 66) return {34, 32, 512};
-        if (b < 74) return {66, 8, 1024};
-        return {74, 8, 1152};
+        if (b < 2) return 1280 + rg * 2 + b;
+        if (b < 34) { const int j = b - 2; return (rg * 4 + (j >> 3)) * 16 + (j & 7); }
+        if (b < 66) { const int j = b - 34; return (rg * 4 + (j >> 3)) * 16 + 8 + (j & 7); }
+        if (b < 74) { const int j = b - 66; return 1024 + (rg * 4 + (j >> 1)) * 4 + (j & 1); }
+        const int j = b - 74;
+        return 1024 + (rg * 4 + (j >> 1)) * 4 + 2 + (j & 1);
     }
-    if (b < 2) return {0, 2, 1728};
-    if (b < 66) return {2, 64, 0};
-    if (b < 74) return {66, 8, 1536};
-    if (b < 106) return {74, 32, 1024};
-    return {106, 4, 1664};
+    if (b < 2) return 1728 + rg * 2 + b;
+    if (b < 66) return rg * 64 + (b - 2);
+    if (b < 74) return 1536 + rg * 8 + (b - 66);
+    if (b < 106) return 1024 + rg * 32 + (b - 74);
+    return 1664 + rg * 4 + (b - 106);
 }
 
 // Byte b of row rr (row inside its 64-row tile rt) of piece kp -> offset inside the expert.
@@ -152,8 +156,7 @@ __host__ __device__ inline int64_t tiled_offset(const Layout& L, int64_t rt, int
     const int64_t prb = piece_row_bytes(L, kp);
     const int64_t base = piece_offset(L, rt, kp);
     if (!fmt_soa(L.fmt)) return base + rr * prb + b;
-    const SoaField f = soa_field(L.fmt, (int)b);
-    return base + (rr / 16) * 16 * prb + f.group_off + (rr % 16) * f.bytes + (b - f.gguf_off);
+    return base + (rr / 16) * 16 * prb + soa_offset(L.fmt, (int)(rr % 16), (int)b);
 }
 
 }  // namespace cwx
@@ -225,15 +228,17 @@ __device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, uint6
     const uint32_t a = smem_u32(bar);
     uint64_t t0 = 0;
     for (uint32_t i = 0;; ++i) {
+        // the suspend-time hint lets a waiting warp sleep until the phase completes (or 20 us
+        // pass) instead of spinning on issue slots that the working warps of its SM need
         uint32_t done;
         asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(done)
-            : "r"(a), "r"(parity)
+            : "r"(a), "r"(parity), "r"(20000u)
             : "memory");
         if (done) return true;
         if (i == 0) t0 = globaltimer_ns();
-        else if ((i & 255) == 0 && globaltimer_ns() - t0 > limit_ns) break;
+        else if (globaltimer_ns() - t0 > limit_ns) break;
     }
     dev_error(err, DE_TIMEOUT);
     return false;

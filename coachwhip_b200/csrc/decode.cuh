@@ -49,51 +49,63 @@ __device__ __forceinline__ float e8m0_to_f32_half(uint8_t e) {
     return __uint_as_float(bits);
 }
 
-// One row's fields of an IQ2_S / IQ3_S block inside a 16-row group.
+// One row of an IQ2_S / IQ3_S 16-row group (layout in cwx_common.cuh); byte b of its GGUF block.
 struct IqRow {
-    const uint8_t *qs, *signs, *qh, *sc, *d;
+    const uint8_t* grp;
+    int rg;
 };
-__device__ __forceinline__ IqRow iq_row(int fmt, const uint8_t* group, int rg) {
-    if (fmt == F_IQ2_S)
-        return {group + rg * 32, group + 512 + rg * 32, group + 1024 + rg * 8, group + 1152 + rg * 8, group + 1280 + rg * 2};
-    return {group + rg * 64, group + 1024 + rg * 32, group + 1536 + rg * 8, group + 1664 + rg * 4, group + 1728 + rg * 2};
-}
+__device__ __forceinline__ uint8_t iq_byte(int fmt, const IqRow& r, int b) { return r.grp[soa_offset(fmt, r.rg, b)]; }
 // Row rr of a piece (or of rows staged from it, starting at a 16-row boundary), rows prb bytes.
-__device__ __forceinline__ IqRow iq_row_in(int fmt, const uint8_t* piece, int rr, int64_t prb) {
-    return iq_row(fmt, piece + (int64_t)(rr >> 4) * 16 * prb, rr & 15);
+__device__ __forceinline__ IqRow iq_row_in(const uint8_t* piece, int rr, int64_t prb) {
+    return IqRow{piece + (int64_t)(rr >> 4) * 16 * prb, rr & 15};
+}
+
+// Codebook value j of grid entry idx: from the shared-memory f16 tables, or from the packed
+// codebooks in global memory when no tables are staged.
+static __device__ const uint16_t d_iq2s_codes[1024] = CWX_IQ2S_CODES;
+static __device__ const uint16_t d_iq3s_codes[512] = CWX_IQ3S_CODES;
+template <bool SMEM>
+__device__ __forceinline__ float iq_grid(int fmt, const HTables& t, int idx, int j) {
+    if (SMEM) return fmt == F_IQ2_S ? half_at(&t.g2[idx], j) : half_at(&t.g3[idx], j);
+    if (fmt == F_IQ2_S) return (float)((cwx_iq2s_expand(d_iq2s_codes[idx]) >> (8 * j)) & 0xFF);
+    return (float)((cwx_iq3s_expand(d_iq3s_codes[idx]) >> (8 * j)) & 0xFF);
 }
 
 // ---------------------------------------------------------------- exact 16-column runs
 // 16 consecutive columns [kofs, kofs+16) of one row's 256-column piece, bit-exact f32.
+template <bool SMEM>
 __device__ __forceinline__ void dec16_iq_exact(int fmt, const IqRow& r, int kofs, float* v, const HTables& t) {
     const int ib = kofs >> 5;
-    const float d = h2f_bits(*reinterpret_cast<const uint16_t*>(r.d));
-    const uint8_t qh = r.qh[ib];
+    const float d = h2f_bits((uint16_t)(iq_byte(fmt, r, 0) | (iq_byte(fmt, r, 1) << 8)));
     if (fmt == F_IQ2_S) {
+        const uint8_t qh = iq_byte(fmt, r, 66 + ib);
         const int g0 = (kofs & 16) >> 3;  // 2 groups of 8
-        const float dl = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)((r.sc[ib] >> (4 * (g0 >> 1))) & 0xF))), 0.25f);
+        const uint8_t sc = iq_byte(fmt, r, 74 + ib);
+        const float dl = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)((sc >> (4 * (g0 >> 1))) & 0xF))), 0.25f);
 #pragma unroll
         for (int gi = 0; gi < 2; ++gi) {
             const int g = g0 + gi;
-            const uint4* gv = &t.g2[r.qs[4 * ib + g] | (((qh >> (2 * g)) & 3) << 8)];
-            const uint8_t sg = r.signs[4 * ib + g];
+            const int idx = iq_byte(fmt, r, 2 + 4 * ib + g) | (((qh >> (2 * g)) & 3) << 8);
+            const uint8_t sg = iq_byte(fmt, r, 34 + 4 * ib + g);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const float x = __fmul_rn(dl, half_at(gv, j));
+                const float x = __fmul_rn(dl, iq_grid<SMEM>(fmt, t, idx, j));
                 v[8 * gi + j] = ((sg >> j) & 1) ? -x : x;
             }
         }
     } else {
+        const uint8_t qh = iq_byte(fmt, r, 66 + ib);
         const int g0 = (kofs & 16) >> 2;  // 4 groups of 4
-        const float dl = __fmul_rn(d, (float)(1 + 2 * ((r.sc[ib >> 1] >> (4 * (ib & 1))) & 0xF)));
+        const uint8_t sc = iq_byte(fmt, r, 106 + (ib >> 1));
+        const float dl = __fmul_rn(d, (float)(1 + 2 * ((sc >> (4 * (ib & 1))) & 0xF)));
 #pragma unroll
         for (int gi = 0; gi < 4; ++gi) {
             const int g = g0 + gi;
-            const uint2* gv = &t.g3[r.qs[8 * ib + g] | (((qh >> g) & 1) << 8)];
-            const uint8_t sg = r.signs[4 * ib + (g >> 1)] >> (4 * (g & 1));
+            const int idx = iq_byte(fmt, r, 2 + 8 * ib + g) | (((qh >> g) & 1) << 8);
+            const uint8_t sg = iq_byte(fmt, r, 74 + 4 * ib + (g >> 1)) >> (4 * (g & 1));
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const float x = __fmul_rn(dl, half_at(gv, j));
+                const float x = __fmul_rn(dl, iq_grid<SMEM>(fmt, t, idx, j));
                 v[4 * gi + j] = ((sg >> j) & 1) ? -x : x;
             }
         }
@@ -157,83 +169,16 @@ __device__ __forceinline__ void dec16_row_exact(int fmt, const uint8_t* b, int k
     }
 }
 
-// Any format: row rr of a piece whose rows are prb bytes.
+// Any format: row rr of a piece whose rows are prb bytes. SMEM: IQ codebooks from the
+// shared-memory tables (load_htables) rather than from global memory.
+template <bool SMEM>
 __device__ __forceinline__ void dec16_exact(int fmt, const uint8_t* piece, int rr, int64_t prb, int kofs, float* v,
                                             const HTables& t) {
-    if (fmt_soa(fmt)) dec16_iq_exact(fmt, iq_row_in(fmt, piece, rr, prb), kofs, v, t);
+    if (fmt_soa(fmt)) dec16_iq_exact<SMEM>(fmt, iq_row_in(piece, rr, prb), kofs, v, t);
     else dec16_row_exact(fmt, piece + (int64_t)rr * prb, kofs, v);
 }
 
-// ---------------------------------------------------------------- fast f16 IQ paths
-__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, __half2 s) {
-    __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), s);
-    return *reinterpret_cast<uint32_t*>(&r);
-}
-
-// A thread's 64 columns [64c, 64c+64) of one row of an IQ piece: the metadata is loaded once,
-// then each 16-column run (ss = 0..3) is produced as 8 f16 pairs.
-struct IqRun {
-    uint64_t qs0, qs1;  // IQ2_S: 8 code bytes (qs0); IQ3_S: 16 code bytes
-    uint64_t sg;        // sign bits of the 64 columns
-    uint32_t qh;        // two qh bytes
-    uint32_t sc;        // IQ2_S: two scale bytes; IQ3_S: one
-    float d;
-};
-
-__device__ __forceinline__ IqRun iq_run_load(int fmt, const IqRow& r, int c) {
-    IqRun q;
-    q.d = h2f_bits(*reinterpret_cast<const uint16_t*>(r.d));
-    q.qh = *reinterpret_cast<const uint16_t*>(r.qh + 2 * c);
-    q.sg = *reinterpret_cast<const uint64_t*>(r.signs + 8 * c);
-    if (fmt == F_IQ2_S) {
-        q.qs0 = *reinterpret_cast<const uint64_t*>(r.qs + 8 * c);
-        q.qs1 = 0;
-        q.sc = *reinterpret_cast<const uint16_t*>(r.sc + 2 * c);
-    } else {
-        const uint4 v = *reinterpret_cast<const uint4*>(r.qs + 16 * c);
-        q.qs0 = ((uint64_t)v.y << 32) | v.x;
-        q.qs1 = ((uint64_t)v.w << 32) | v.z;
-        q.sc = r.sc[c];
-    }
-    return q;
-}
-
-// Columns 64c + 16ss .. +16 as 8 f16 pairs.
-__device__ __forceinline__ void iq_run_pairs(int fmt, const IqRun& q, int ss, uint32_t* p, const HTables& t) {
-    if (fmt == F_IQ2_S) {
-        const float dl = __fmul_rn(__fmul_rn(q.d, __fadd_rn(0.5f, (float)((q.sc >> (4 * ss)) & 0xF))), 0.25f);
-        const __half2 s2 = __float2half2_rn(dl);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int gi = 2 * ss + h;
-            const uint32_t e = (uint32_t)((q.qs0 >> (8 * gi)) & 0xFF) | (((q.qh >> (2 * gi)) & 3) << 8);
-            const uint4 gv = t.g2[e];
-            const uint4 m = t.sgn[(q.sg >> (8 * gi)) & 0xFF];
-            p[4 * h + 0] = hmul2_u(gv.x ^ m.x, s2);
-            p[4 * h + 1] = hmul2_u(gv.y ^ m.y, s2);
-            p[4 * h + 2] = hmul2_u(gv.z ^ m.z, s2);
-            p[4 * h + 3] = hmul2_u(gv.w ^ m.w, s2);
-        }
-    } else {
-        const float dl = __fmul_rn(q.d, (float)(1 + 2 * ((q.sc >> (4 * (ss >> 1))) & 0xF)));
-        const __half2 s2 = __float2half2_rn(dl);
-        const uint64_t qsw = ss < 2 ? q.qs0 : q.qs1;
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-            const int gi = 4 * ss + h;
-            const uint32_t e = (uint32_t)((qsw >> (8 * (gi & 7))) & 0xFF) | (((q.qh >> gi) & 1) << 8);
-            const uint2 gv = t.g3[e];
-            const uint4 m = t.sgn[(q.sg >> (4 * gi)) & 0xF];
-            p[2 * h + 0] = hmul2_u(gv.x ^ m.x, s2);
-            p[2 * h + 1] = hmul2_u(gv.y ^ m.y, s2);
-        }
-    }
-}
-
 // ---------------------------------------------------------------- tables
-static __device__ const uint16_t d_iq2s_codes[1024] = CWX_IQ2S_CODES;
-static __device__ const uint16_t d_iq3s_codes[512] = CWX_IQ3S_CODES;
-
 // Expand the packed codebooks into f16 tables in shared memory (every thread of the CTA calls
 // this; the caller synchronises before use).
 __device__ __forceinline__ void load_htables(uint4* g2, uint2* g3, uint4* sgn) {

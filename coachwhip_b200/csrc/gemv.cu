@@ -5,39 +5,64 @@
 //              vendor/candle-metal-kernels/src/metal_src/quantized.metal:7668-7766, 7868-7911).
 //
 // A launch runs up to four matrix jobs (routed gate, routed up, shared gate, shared up; or routed
-// down, shared down). Work items are (job, expert, R-row tile) over the experts that have picks
-// (the used list the pile kernels build) and (job, tile, pass) for the shared expert, walked by a
-// persistent grid. A CTA has 8 consumer warps and one producer warp. Consumer warp w owns rows
-// 16*(w % (R/16)) of the tile and K-slice w / (R/16) (KS slices, R = 128/KS, so small batches
-// split K across warps and still fill the GPU). The producer runs ahead through the CTA's steps:
-// for each it writes a small header (item, pass, the pass's output rows) into a free stage and
+// down, shared down). Work items are (job, expert, row tile) over the experts that have picks
+// (the used list the pile kernels build) and (job, row tile, pass) for the shared expert, walked
+// by a persistent grid of one CTA per SM: 16 consumer warps and one producer warp. Consumer warp
+// w owns the 16 rows 16*(w % MT) of the tile and K-slice w / MT (KS slices, MT = 16 / KS, so small
+// batches split K across warps and still fill the GPU). The producer resolves the CTA's items 32
+// at a time (one per lane, so their loads of the used list and the piles overlap) into a small
+// ring in shared memory, then runs ahead through the steps without touching global memory: for
+// each it writes a small header (item, pass, the pass's output rows) into a free stage and
 // brings, in one mbarrier phase, the tile's quantised bytes for KS pieces of 256 columns
-// (cp.async.bulk from the tiled bank layout) and the pile's packed activation rows for those
-// columns. Producer and consumers meet only on full/empty mbarriers.
+// (cp.async.bulk from the tiled bank layout) and the pass's packed activation rows for those
+// columns. Producer and consumers meet only on full/empty mbarriers whose waits are bounded.
 //
-// Each thread dequantises two rows x 64 contiguous columns of a piece straight into mma.sync
-// m16n8k16 A registers, 16 columns per sub-step. The reduction index of an MMA step is permuted
-// (thread c of a quad contributes 4 of its own columns), legal because A and B use the same
-// permutation; the activation rows arrive packed in exactly that order (act.cu), so every thread
-// reads its 16 activation columns with four conflict-free 16-byte loads. Activations are an f16
-// hi + lo pair (~22 bits); weights are f16 (IQ formats, F32 policy) or an f16 hi + lo pair when
-// the result is re-quantised downstream. f32 accumulation; K-slices summed in a fixed order.
+// Each thread takes two rows x 64 contiguous columns of a piece into mma.sync m16n8k16 A
+// registers, 16 columns per sub-step; the reduction index of an MMA step is permuted (thread c of
+// a quad contributes 4 of its own columns), legal because A and B use the same permutation, and
+// the activation rows arrive packed in exactly that order (act.cu).
+//
+// IQ2_S / IQ3_S fast path (the routed format of the launch): the codebooks live in shared memory
+// replicated (8 copies of the IQ2_S table, 16 of the IQ3_S one) and interleaved so that the lanes
+// sharing a shared-memory wavefront read different banks whatever entries they ask for. The
+// weights go to the tensor cores as exact f16 integers, codebook value x sign x (2 * scale + 1);
+// the block scale d (and the 1/8 of IQ2_S) multiplies the f32 partial sum of each 256-column
+// piece, so no weight is rounded. Activations: f16 (hi), plus the lo part when the job asks for
+// ~22-bit products (its outputs are re-quantised downstream).
+// Other formats (and any job of another format in the same launch): exact f32 dequantisation
+// rounded to f16 (hi + lo pairs when the job asks for it), activations hi + lo.
 #include "cwx_common.cuh"
 #include "decode.cuh"
 #include "kernels.cuh"
 
 namespace cwx {
 
-constexpr int GEMV_THREADS = 256;  // consumer threads (the producer warp comes on top)
-// K-slice partial sums: slices 1..KS-1 of every m-tile, one 16x8 fragment (128 floats) each;
-// (KS - 1) * (R / 16) * 128 <= 7 * 128 floats for every KS, double-buffered by pass parity.
-constexpr int RED_FLOATS = 7 * 128;
-constexpr int RED_BYTES = 2 * RED_FLOATS * 4;
+constexpr int NCW = 16;                      // consumer warps
+constexpr int GEMV_THREADS = NCW * 32 + 32;  // + the producer warp
+constexpr int RED_FLOATS = 14 * 128;         // (KS - 1) * MT fragments of 128 floats, KS * MT = 16, KS <= 8
+constexpr int BAR_BYTES = 256;
+constexpr int HDR_BYTES = 128;
+constexpr int MAX_TOKCAP = 8;
+constexpr int SMEM_LIMIT = 227 * 1024;
+constexpr int RING_BYTES = 4096;  // the producer's look-ahead ring (PRing)
+
+template <int FMT>
+struct Tbl {  // replicated codebook bytes in shared memory
+    static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 128 : FMT == F_IQ3_S ? 512 * 128 : 0;
+};
+
+template <int KS>
+struct Cfg {
+    static constexpr int MT = NCW / KS;            // m-tiles (16 rows) per item
+    static constexpr int R = 16 * MT;              // rows of a routed item
+    static constexpr int BROW = KS * 1024 + 64;    // shared bytes of one staged activation row
+    static_assert((KS - 1) * MT * 128 <= RED_FLOATS, "K-slice reduction buffer");
+};
 
 struct Item {
     int job;
     uint32_t e, first, count;
-    int64_t rt;  // tile index in R-row units
+    int64_t rt;  // row tile index (in units of the job's rows per item)
     int rows;    // rows of this tile (multiple of 16)
     int n_kp;    // 256-column pieces per row
     int nsk;     // steps per pass (ceil(n_kp / KS))
@@ -45,31 +70,18 @@ struct Item {
     int passes;  // passes this item runs
 };
 
-template <int KS>
-struct Cfg {
-    static constexpr int R = 128 / KS;           // rows per item
-    static constexpr int MT = R / 16;            // m-tiles per item
-    static constexpr int TOKCAP = 8;             // picks per pass (one n-tile)
-    static constexpr int BROW = KS * 1024 + 64;  // smem bytes of one activation row (bank-spread)
-    static_assert((KS - 1) * MT * 128 <= RED_FLOATS, "K-slice reduction buffer");
-};
-
-template <int KS>
-__device__ __forceinline__ int64_t tiles(const GemvJob& j) {
-    return (j.m.L.n + Cfg<KS>::R - 1) / Cfg<KS>::R;
-}
+__device__ __forceinline__ int64_t job_tiles(const GemvJob& j) { return (j.m.L.n + j.rows - 1) / j.rows; }
 
 // Item `it` of the launch: the shared jobs' (tile, pass) items first, then per used expert the
 // tiles of every routed job (expert-major, so one expert's jobs reuse its activation rows in L2).
 template <int KS>
 __device__ __forceinline__ bool get_item(const GemvArgs& a, int64_t it, uint32_t n_used, Item* o) {
-    using C = Cfg<KS>;
     int64_t routed_tiles = 0;
-    const int64_t sp = (a.s_count + C::TOKCAP - 1) / C::TOKCAP;  // passes of a shared tile
+    const int64_t sp = (a.s_count + a.tokcap - 1) / a.tokcap;  // passes of a shared tile
     for (int j = 0; j < a.njobs; ++j) {
         const GemvJob& jb = a.job[j];
         if (jb.shared) {
-            const int64_t t = tiles<KS>(jb) * sp;
+            const int64_t t = job_tiles(jb) * sp;
             if (it < t) {
                 o->job = j;
                 o->e = 0;
@@ -82,7 +94,7 @@ __device__ __forceinline__ bool get_item(const GemvArgs& a, int64_t it, uint32_t
             }
             it -= t;
         } else {
-            routed_tiles += tiles<KS>(jb);
+            routed_tiles += job_tiles(jb);
         }
     }
     if (routed_tiles == 0) return false;
@@ -93,7 +105,7 @@ __device__ __forceinline__ bool get_item(const GemvArgs& a, int64_t it, uint32_t
         for (int j = 0; j < a.njobs; ++j) {
             const GemvJob& jb = a.job[j];
             if (jb.shared) continue;
-            const int64_t t = tiles<KS>(jb);
+            const int64_t t = job_tiles(jb);
             if (r < t) {
                 o->job = j;
                 o->rt = r;
@@ -105,41 +117,16 @@ __device__ __forceinline__ bool get_item(const GemvArgs& a, int64_t it, uint32_t
         o->first = a.used3[3 * u + 1];
         o->count = a.used3[3 * u + 2];
         o->pass0 = 0;
-        o->passes = (int)((o->count + C::TOKCAP - 1) / C::TOKCAP);
+        o->passes = (int)((o->count + a.tokcap - 1) / a.tokcap);
         if (o->passes < 1) o->passes = 1;
     }
 found:
-    const Layout& L = a.job[o->job].m.L;
-    const int64_t left = L.n - o->rt * C::R;
-    o->rows = (int)(left < C::R ? left : C::R);
-    o->n_kp = L.n_kp;
-    o->nsk = (L.n_kp + KS - 1) / KS;
+    const GemvJob& jb = a.job[o->job];
+    const int64_t left = jb.m.L.n - o->rt * jb.rows;
+    o->rows = (int)(left < jb.rows ? left : jb.rows);
+    o->n_kp = jb.m.L.n_kp;
+    o->nsk = (jb.m.L.n_kp + KS - 1) / KS;
     return true;
-}
-
-struct Cursor {
-    int64_t j;
-    int pass, sk;
-    Item item;
-    bool valid;
-};
-
-template <int KS>
-__device__ __forceinline__ void cursor_init(const GemvArgs& a, uint32_t n_used, Cursor* c) {
-    c->j = 0;
-    c->sk = 0;
-    c->valid = get_item<KS>(a, blockIdx.x, n_used, &c->item);
-    c->pass = c->valid ? c->item.pass0 : 0;
-}
-template <int KS>
-__device__ __forceinline__ void cursor_next(const GemvArgs& a, uint32_t n_used, Cursor* c) {
-    if (!c->valid) return;
-    if (++c->sk < c->item.nsk) return;
-    c->sk = 0;
-    if (++c->pass < c->item.pass0 + c->item.passes) return;
-    c->j++;
-    c->valid = get_item<KS>(a, (int64_t)blockIdx.x + c->j * gridDim.x, n_used, &c->item);
-    c->pass = c->valid ? c->item.pass0 : 0;
 }
 
 // What consumers need to know about a step, written by the producer at the head of its stage.
@@ -149,31 +136,53 @@ struct StepHdr {
     int64_t rt;
     int rows, n_kp, kp0, pass_start, pass_end;
     uint32_t ntok;
-    uint32_t orow[8];  // output row of each slot of the pass (pick index, or token)
+    uint32_t orow[MAX_TOKCAP];  // output row of each slot of the pass (pick index, or token)
 };
-constexpr int HDR_BYTES = 128;
 static_assert(sizeof(StepHdr) <= HDR_BYTES, "step header");
 
-// Stage layout of one step: [header][KS weight slots of R rows x piece bytes][TOKCAP activation rows].
-template <int KS>
-__host__ __device__ __forceinline__ int64_t slot_bytes(const Layout& L) {
-    return pad16((int64_t)Cfg<KS>::R * L.kp_row_bytes);
+__device__ __forceinline__ uint32_t pass_tokens(const Item& it, int pass, int tokcap) {
+    const uint32_t done = (uint32_t)pass * (uint32_t)tokcap;
+    const uint32_t left = it.count - done;
+    return left < (uint32_t)tokcap ? left : (uint32_t)tokcap;
 }
 
-// Issue step c into a stage (all lanes of the producer warp): the tile's rows of KS pieces, and
-// the pass's activation rows for those columns.
+// Slot t of a pass: its activation row and its output row (pick index, or token).
+__device__ __forceinline__ void pass_rows(const GemvArgs& a, const Item& it, int pass, uint32_t t, uint32_t* arow,
+                                          uint32_t* orow) {
+    const GemvJob& jb = a.job[it.job];
+    const uint32_t ip = (uint32_t)pass * (uint32_t)a.tokcap + t;
+    if (jb.shared) {
+        *arow = ip;
+        *orow = ip;
+    } else {
+        const uint32_t p = a.pairs[it.first + ip];
+        *arow = p / (uint32_t)jb.bdiv;
+        *orow = p;
+    }
+}
+
+// The producer's look-ahead: the CTA's items resolved 32 at a time (lane L resolves one, so
+// their global loads overlap), with the token rows of each item's first pass. Steps then need
+// no global load.
+constexpr int PBATCH = 32;
+struct PRing {
+    Item it[PBATCH];
+    uint32_t arow[PBATCH][MAX_TOKCAP];
+    uint32_t orow[PBATCH][MAX_TOKCAP];
+};
+static_assert(sizeof(PRing) <= RING_BYTES, "producer ring");
+
+// Issue one step into a stage (all lanes of the producer warp): the tile's rows of KS pieces
+// from sk * KS on, and the pass's activation rows for those columns (lane t < ntok holds row t).
 template <int KS>
-__device__ __forceinline__ void issue_step(const GemvArgs& a, const Cursor& c, uint8_t* stage, uint64_t* bar,
-                                           int lane) {
+__device__ __forceinline__ void issue_step(const GemvArgs& a, const Item& it, int sk, uint32_t ntok, uint32_t arow,
+                                           uint8_t* stage, uint64_t* bar, int lane) {
     using C = Cfg<KS>;
-    const Item& it = c.item;
     const GemvJob& jb = a.job[it.job];
     const Layout& L = jb.m.L;
-    const int kp0 = c.sk * KS;
+    const int kp0 = sk * KS;
     const int nk = it.n_kp - kp0 < KS ? it.n_kp - kp0 : KS;
-    uint32_t ntok = it.count - (uint32_t)c.pass * C::TOKCAP;
-    if (ntok > (uint32_t)C::TOKCAP) ntok = C::TOKCAP;
-    const int64_t row0 = it.rt * C::R, rowe = row0 + it.rows;
+    const int64_t row0 = it.rt * jb.rows, rowe = row0 + it.rows;
     uint32_t total = 0;
     for (int q = 0; q < nk; ++q) total += (uint32_t)(it.rows * piece_row_bytes(L, kp0 + q));
     const uint32_t bbytes = (uint32_t)nk * 1024;
@@ -185,7 +194,7 @@ __device__ __forceinline__ void issue_step(const GemvArgs& a, const Cursor& c, u
     for (int q = 0; q < nk; ++q) {
         const int kp = kp0 + q;
         const int64_t prb = piece_row_bytes(L, kp);
-        uint8_t* dst = stage + q * slot_bytes<KS>(L);
+        uint8_t* dst = stage + q * a.slot_bytes;
         for (int64_t r = row0; r < rowe;) {
             const int64_t lt = r / TILE_ROWS, rr = r % TILE_ROWS;
             const int64_t rend = (lt + 1) * TILE_ROWS < rowe ? (lt + 1) * TILE_ROWS : rowe;
@@ -195,52 +204,227 @@ __device__ __forceinline__ void issue_step(const GemvArgs& a, const Cursor& c, u
             r = rend;
         }
     }
-    uint8_t* bdst = stage + KS * slot_bytes<KS>(L);
-    for (uint32_t t = lane; t < ntok; t += 32) {
-        const uint32_t ip = (uint32_t)c.pass * C::TOKCAP + t;
-        const int64_t row = jb.shared ? (int64_t)ip : (int64_t)(a.pairs[it.first + ip] / (uint32_t)jb.bdiv);
-        bulk_g2s(bdst + t * C::BROW, jb.b + row * jb.bstride + (int64_t)kp0 * 1024, bbytes, bar);
+    if ((uint32_t)lane < ntok)
+        bulk_g2s(stage + KS * a.slot_bytes + lane * C::BROW, jb.b + (int64_t)arow * jb.bstride + (int64_t)kp0 * 1024,
+                 bbytes, bar);
+}
+
+// ---------------------------------------------------------------- fast IQ decode
+__device__ __forceinline__ __half2 u2h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+__device__ __forceinline__ uint32_t h22u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// Sign bits q and q+1 of s8 onto the f16 sign bits (15, 31) of a value pair.
+__device__ __forceinline__ uint32_t sign_pair(uint32_t s8, int q, uint32_t g) {
+    const uint32_t m = s8 * ((1u << (15 - q)) + (1u << (30 - q)));
+    return (m & 0x80008000u) ^ g;
+}
+// n in 0..15 -> (2n + 1, 2n + 1) in f16, exact (from the f16 bits of 1024 + 2n + 1).
+__device__ __forceinline__ __half2 odd2(uint32_t n) {
+    return __hsub2(u2h2(n * 0x00020002u + 0x64016401u), __floats2half2_rn(1024.f, 1024.f));
+}
+
+// IQ2_S: columns 16ss .. 16ss+15 of the thread's 64 (groups 2ss, 2ss+1) of one row as 8 f16
+// pairs of exact integers g * sign * (2n + 1). Q = [qs 8 B | signs 8 B], H = [qh 2 B | scales 2 B]
+// of the row's 64 columns; tl = this lane's copy of the table.
+__device__ __forceinline__ void iq2s_pairs(const uint4& Q, uint32_t H, int ss, const uint8_t* tl, uint32_t* p) {
+    const __half2 od = odd2((H >> (16 + 4 * ss)) & 0xFu);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int gi = 2 * ss + h;
+        const uint32_t qw = gi < 4 ? Q.x : Q.y, sw = gi < 4 ? Q.z : Q.w;
+        const uint32_t b = __byte_perm(qw, 0u, 0x4440 | (gi & 3));
+        const uint32_t off = (b << 7) | (((H >> (2 * gi)) & 3u) << 15);
+        const uint4 G = *reinterpret_cast<const uint4*>(tl + off);
+        const uint32_t s8 = __byte_perm(sw, 0u, 0x4440 | (gi & 3));
+        p[4 * h + 0] = h22u(__hmul2(u2h2(sign_pair(s8, 0, G.x)), od));
+        p[4 * h + 1] = h22u(__hmul2(u2h2(sign_pair(s8, 2, G.y)), od));
+        p[4 * h + 2] = h22u(__hmul2(u2h2(sign_pair(s8, 4, G.z)), od));
+        p[4 * h + 3] = h22u(__hmul2(u2h2(sign_pair(s8, 6, G.w)), od));
     }
 }
 
-// Header of step c (lanes of the producer warp; lane t < ntok fills output row t).
-template <int KS>
-__device__ __forceinline__ void write_hdr(const GemvArgs& a, const Cursor& c, StepHdr* h, int lane) {
-    using C = Cfg<KS>;
-    const Item& it = c.item;
-    uint32_t ntok = it.count - (uint32_t)c.pass * C::TOKCAP;
-    if (ntok > (uint32_t)C::TOKCAP) ntok = C::TOKCAP;
-    if (lane == 0) {
-        h->job = it.job;
-        h->e = it.e;
-        h->rt = it.rt;
-        h->rows = it.rows;
-        h->n_kp = it.n_kp;
-        h->kp0 = c.sk * KS;
-        h->pass_start = c.sk == 0;
-        h->pass_end = c.sk == it.nsk - 1;
-        h->ntok = ntok;
-    }
-    if ((uint32_t)lane < ntok) {
-        const uint32_t ip = (uint32_t)c.pass * C::TOKCAP + lane;
-        h->orow[lane] = a.job[it.job].shared ? ip : a.pairs[it.first + ip];
+// IQ3_S: the same 16 columns (lookups 4ss .. 4ss+3 of 4 values). Qs = 16 index bytes, S = 64
+// sign bits, qh = 16 high index bits, sc = two scale nibbles (per 32 columns).
+__device__ __forceinline__ void iq3s_pairs(const uint4& Qs, const uint2& S, uint32_t qh, uint32_t sc, int ss,
+                                           const uint8_t* tl, uint32_t* p) {
+    const __half2 od = odd2((sc >> (4 * (ss >> 1))) & 0xFu);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+        const int j = 4 * ss + h;
+        const uint32_t qw = j < 4 ? Qs.x : j < 8 ? Qs.y : j < 12 ? Qs.z : Qs.w;
+        const uint32_t b = __byte_perm(qw, 0u, 0x4440 | (j & 3));
+        const uint32_t off = (b << 7) | (((qh >> j) & 1u) << 15);
+        const uint2 G = *reinterpret_cast<const uint2*>(tl + off);
+        const uint32_t s8 = __byte_perm(j < 8 ? S.x : S.y, 0u, 0x4440 | ((j >> 1) & 3));
+        const int q = 4 * (j & 1);
+        p[2 * h + 0] = h22u(__hmul2(u2h2(sign_pair(s8, q, G.x)), od));
+        p[2 * h + 1] = h22u(__hmul2(u2h2(sign_pair(s8, q + 2, G.y)), od));
     }
 }
 
-template <int KS>
-__global__ void __launch_bounds__(GEMV_THREADS + 32, 2) k_gemv(GemvArgs a) {
+// Activation chunks of sub-step ss for this thread's token slot: hi columns 0-7 / 8-15 (and lo).
+__device__ __forceinline__ void load_b(const uint8_t* brow, int ss, bool has_tok, bool lo, uint32_t* hb,
+                                       uint32_t* lb) {
+    uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0, l0 = h0, l1 = h0;
+    if (has_tok) {
+        h0 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 0));
+        h1 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 2));
+        if (lo) {
+            l0 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 1));
+            l1 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 3));
+        }
+    }
+    hb[0] = h0.x; hb[1] = h0.y; hb[2] = h0.z; hb[3] = h0.w;
+    hb[4] = h1.x; hb[5] = h1.y; hb[6] = h1.z; hb[7] = h1.w;
+    lb[0] = l0.x; lb[1] = l0.y; lb[2] = l0.z; lb[3] = l0.w;
+    lb[4] = l1.x; lb[5] = l1.y; lb[6] = l1.z; lb[7] = l1.w;
+}
+
+// One step of a fast-path job: this warp's 16 rows x 256 columns; the piece's partial sums are
+// scaled by the rows' block scales and added to acc.
+template <int FMT>
+__device__ __forceinline__ void fast_step(const uint8_t* wsl, int mt, int g, int c4, const uint8_t* tl,
+                                          const uint8_t* brow, bool has_tok, bool lo, float* acc) {
+    float t[4] = {0.f, 0.f, 0.f, 0.f};
+    float dA, dB;
+    if (FMT == F_IQ2_S) {
+        const uint8_t* grp = wsl + mt * (16 * 82);
+        const uint4 QA = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 16);
+        const uint4 QB = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 16);
+        const uint32_t HA = *reinterpret_cast<const uint32_t*>(grp + 1024 + (g * 4 + c4) * 4);
+        const uint32_t HB = *reinterpret_cast<const uint32_t*>(grp + 1024 + ((g + 8) * 4 + c4) * 4);
+        dA = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1280 + 2 * g)), 0.125f);
+        dB = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1280 + 2 * (g + 8))), 0.125f);
+#pragma unroll
+        for (int ss = 0; ss < 4; ++ss) {
+            uint32_t pa[8], pb[8], hb[8], lb[8];
+            iq2s_pairs(QA, HA, ss, tl, pa);
+            iq2s_pairs(QB, HB, ss, tl, pb);
+            load_b(brow, ss, has_tok, lo, hb, lb);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
+                mma_16816(t, af, hb[2 * kk], hb[2 * kk + 1]);
+                if (lo) mma_16816(t, af, lb[2 * kk], lb[2 * kk + 1]);
+            }
+        }
+    } else {
+        const uint8_t* grp = wsl + mt * (16 * 110);
+        const uint4 QA = *reinterpret_cast<const uint4*>(grp + g * 64 + 16 * c4);
+        const uint4 QB = *reinterpret_cast<const uint4*>(grp + (g + 8) * 64 + 16 * c4);
+        const uint2 SA = *reinterpret_cast<const uint2*>(grp + 1024 + g * 32 + 8 * c4);
+        const uint2 SB = *reinterpret_cast<const uint2*>(grp + 1024 + (g + 8) * 32 + 8 * c4);
+        const uint32_t qhA = *reinterpret_cast<const uint16_t*>(grp + 1536 + g * 8 + 2 * c4);
+        const uint32_t qhB = *reinterpret_cast<const uint16_t*>(grp + 1536 + (g + 8) * 8 + 2 * c4);
+        const uint32_t scA = grp[1664 + g * 4 + c4], scB = grp[1664 + (g + 8) * 4 + c4];
+        dA = h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1728 + 2 * g));
+        dB = h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1728 + 2 * (g + 8)));
+#pragma unroll
+        for (int ss = 0; ss < 4; ++ss) {
+            uint32_t pa[8], pb[8], hb[8], lb[8];
+            iq3s_pairs(QA, SA, qhA, scA, ss, tl, pa);
+            iq3s_pairs(QB, SB, qhB, scB, ss, tl, pb);
+            load_b(brow, ss, has_tok, lo, hb, lb);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
+                mma_16816(t, af, hb[2 * kk], hb[2 * kk + 1]);
+                if (lo) mma_16816(t, af, lb[2 * kk], lb[2 * kk + 1]);
+            }
+        }
+    }
+    acc[0] = __fmaf_rn(t[0], dA, acc[0]);
+    acc[1] = __fmaf_rn(t[1], dA, acc[1]);
+    acc[2] = __fmaf_rn(t[2], dB, acc[2]);
+    acc[3] = __fmaf_rn(t[3], dB, acc[3]);
+}
+
+// One step of any format: exact f32 dequantisation rounded to f16 (hi + lo weights when split),
+// activations hi + lo.
+__device__ __forceinline__ void generic_step(const Layout& L, int kp, const uint8_t* wsl, int mt, int g, int c4,
+                                             const uint8_t* brow, bool has_tok, bool split, float* acc) {
+    const int64_t prb = piece_row_bytes(L, kp);
+    const int64_t kleft = L.k - (int64_t)kp * PIECE_K;
+    const int klen = (int)(kleft < PIECE_K ? kleft : PIECE_K);
+    const bool active = 64 * c4 < klen;  // this thread's 64 columns exist in the piece
+    const int rA = 16 * mt + g, rB = rA + 8;
+    const HTables none{nullptr, nullptr, nullptr};
+#pragma unroll 1
+    for (int ss = 0; ss < 4; ++ss) {
+        uint32_t af[4][4], al[4][4];
+        if (!active) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                af[kk][0] = af[kk][1] = af[kk][2] = af[kk][3] = 0u;
+                al[kk][0] = al[kk][1] = al[kk][2] = al[kk][3] = 0u;
+            }
+        } else {
+            float v0[16], v1[16];
+            const int kofs = 64 * c4 + 16 * ss;
+            dec16_exact<false>(L.fmt, wsl, rA, prb, kofs, v0, none);
+            dec16_exact<false>(L.fmt, wsl, rB, prb, kofs, v1, none);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {  // hh = 0: columns 4kk, 4kk+1; 1: 4kk+2, 4kk+3
+                    const int i = 4 * kk + 2 * hh;
+                    const __half2 x0 = __floats2half2_rn(v0[i], v0[i + 1]);
+                    const __half2 x1 = __floats2half2_rn(v1[i], v1[i + 1]);
+                    af[kk][2 * hh] = h22u(x0);
+                    af[kk][2 * hh + 1] = h22u(x1);
+                    const float2 f0 = __half22float2(x0), f1 = __half22float2(x1);
+                    al[kk][2 * hh] = h22u(__floats2half2_rn(__fsub_rn(v0[i], f0.x), __fsub_rn(v0[i + 1], f0.y)));
+                    al[kk][2 * hh + 1] = h22u(__floats2half2_rn(__fsub_rn(v1[i], f1.x), __fsub_rn(v1[i + 1], f1.y)));
+                }
+            }
+        }
+        uint32_t hb[8], lb[8];
+        load_b(brow, ss, has_tok, true, hb, lb);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            mma_16816(acc, af[kk], hb[2 * kk], hb[2 * kk + 1]);
+            mma_16816(acc, af[kk], lb[2 * kk], lb[2 * kk + 1]);
+            if (split) mma_16816(acc, al[kk], hb[2 * kk], hb[2 * kk + 1]);
+        }
+    }
+}
+
+// Replicated f16 codebooks (every consumer thread; the caller synchronises the consumers).
+template <int FMT>
+__device__ __forceinline__ void build_tables(uint8_t* tbl, int tid) {
+    if (FMT == F_IQ2_S) {
+        for (int e = tid; e < 1024; e += NCW * 32) {
+            const uint64_t v = cwx_iq2s_expand(d_iq2s_codes[e]);
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                w[j] = h22u(__floats2half2_rn((float)((v >> (16 * j)) & 0xFF), (float)((v >> (16 * j + 8)) & 0xFF)));
+            const uint4 q = make_uint4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(tbl + e * 128 + c * 16) = q;
+        }
+    } else if (FMT == F_IQ3_S) {
+        for (int e = tid; e < 512; e += NCW * 32) {
+            const uint32_t v = cwx_iq3s_expand(d_iq3s_codes[e]);
+            const uint2 q = make_uint2(h22u(__floats2half2_rn((float)(v & 0xFF), (float)((v >> 8) & 0xFF))),
+                                       h22u(__floats2half2_rn((float)((v >> 16) & 0xFF), (float)(v >> 24))));
+#pragma unroll
+            for (int c = 0; c < 16; ++c) *reinterpret_cast<uint2*>(tbl + e * 128 + c * 8) = q;
+        }
+    }
+}
+
+template <int FMT, int KS>
+__global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
     using C = Cfg<KS>;
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);                 // 8 x 8 B
-    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + 64);           // 8 x 8 B
-    uint4* h_g2 = reinterpret_cast<uint4*>(smem + 128);                 // 16 KB
-    uint2* h_g3 = reinterpret_cast<uint2*>(smem + 128 + 16384);         // 4 KB
-    uint4* h_sg = reinterpret_cast<uint4*>(smem + 128 + 20480);         // 4 KB
-    float* red = reinterpret_cast<float*>(smem + 128 + HTABLES_BYTES);  // 2 x RED_FLOATS
-    uint8_t* stages = smem + 128 + HTABLES_BYTES + RED_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);        // 8 x 8 B
+    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + 64);  // 8 x 8 B
+    uint8_t* tbl = smem + BAR_BYTES;
+    float* red = reinterpret_cast<float*>(smem + BAR_BYTES + Tbl<FMT>::BYTES);
+    uint8_t* stages = smem + BAR_BYTES + Tbl<FMT>::BYTES + RED_FLOATS * 4 + RING_BYTES;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    constexpr int NCW = GEMV_THREADS / 32;  // consumer warps
     if (tid == 0) {
         for (int s = 0; s < a.nst; ++s) {
             mbar_init(&full[s], 1);
@@ -248,43 +432,91 @@ __global__ void __launch_bounds__(GEMV_THREADS + 32, 2) k_gemv(GemvArgs a) {
         }
         fence_mbar_init();
     }
-    load_htables(h_g2, h_g3, h_sg);
     __syncthreads();
 
     if (warp == NCW) {
         // ---------------- producer
+        PRing* ring = reinterpret_cast<PRing*>(smem + BAR_BYTES + Tbl<FMT>::BYTES + RED_FLOATS * 4);
         const uint32_t n_used = *a.n_used;
-        Cursor pc;
-        cursor_init<KS>(a, n_used, &pc);
-        for (int64_t q = 0;; ++q) {
-            const int s = (int)(q % a.nst);
-            if (q >= a.nst && !mbar_wait(&empty[s], (uint32_t)(((q / a.nst) + 1) & 1), a.err)) return;
-            uint8_t* stage = stages + (int64_t)s * a.stage_bytes;
-            StepHdr* h = reinterpret_cast<StepHdr*>(stage);
-            if (!pc.valid) {
-                if (lane == 0) {
-                    h->job = -1;
-                    mbar_arrive(&full[s]);
-                }
-                return;
+        int s = 0;        // stage of the next step (step q uses stage q mod nst)
+        uint32_t ph = 0;  // parity of the current round of the ring of stages
+        int64_t q = 0;
+        for (int64_t base = 0;; base += PBATCH) {
+            Item mine;
+            const bool ok = get_item<KS>(a, (int64_t)blockIdx.x + (base + lane) * gridDim.x, n_used, &mine);
+            if (ok) {
+                ring->it[lane] = mine;
+                const uint32_t n0 = pass_tokens(mine, mine.pass0, a.tokcap);
+                for (uint32_t t = 0; t < n0; ++t)
+                    pass_rows(a, mine, mine.pass0, t, &ring->arow[lane][t], &ring->orow[lane][t]);
             }
-            write_hdr<KS>(a, pc, h, lane);
+            const uint32_t okm = __ballot_sync(0xffffffffu, ok);
             __syncwarp();
-            issue_step<KS>(a, pc, stage + HDR_BYTES, &full[s], lane);
-            cursor_next<KS>(a, n_used, &pc);
+            const int nitems = __popc(okm);  // items are consecutive: the valid ones come first
+            for (int li = 0; li < nitems; ++li) {
+                const Item it = ring->it[li];
+                for (int pass = it.pass0; pass < it.pass0 + it.passes; ++pass) {
+                    const uint32_t ntok = pass_tokens(it, pass, a.tokcap);
+                    uint32_t arow = 0, orow = 0;
+                    if ((uint32_t)lane < ntok) {
+                        if (pass == it.pass0) {
+                            arow = ring->arow[li][lane];
+                            orow = ring->orow[li][lane];
+                        } else {
+                            pass_rows(a, it, pass, lane, &arow, &orow);
+                        }
+                    }
+                    for (int sk = 0; sk < it.nsk; ++sk) {
+                        if (q >= a.nst && !mbar_wait(&empty[s], ph ^ 1u, a.err)) return;
+                        uint8_t* stage = stages + s * a.stage_bytes;
+                        StepHdr* h = reinterpret_cast<StepHdr*>(stage);
+                        if (lane == 0) {
+                            h->job = it.job;
+                            h->e = it.e;
+                            h->rt = it.rt;
+                            h->rows = it.rows;
+                            h->n_kp = it.n_kp;
+                            h->kp0 = sk * KS;
+                            h->pass_start = sk == 0;
+                            h->pass_end = sk == it.nsk - 1;
+                            h->ntok = ntok;
+                        }
+                        if ((uint32_t)lane < ntok) h->orow[lane] = orow;
+                        __syncwarp();
+                        issue_step<KS>(a, it, sk, ntok, arow, stage + HDR_BYTES, &full[s], lane);
+                        ++q;
+                        if (++s == a.nst) {
+                            s = 0;
+                            ph ^= 1u;
+                        }
+                    }
+                }
+            }
+            __syncwarp();  // the ring is refilled by the next batch
+            if (okm != 0xffffffffu) break;
         }
+        if (q >= a.nst && !mbar_wait(&empty[s], ph ^ 1u, a.err)) return;
+        if (lane == 0) {
+            reinterpret_cast<StepHdr*>(stages + s * a.stage_bytes)->job = -1;
+            mbar_arrive(&full[s]);
+        }
+        return;
     }
 
     // ---------------- consumers
-    const HTables ht{h_g2, h_g3, h_sg};
+    if (FMT != 0) {
+        build_tables<FMT>(tbl, tid);
+        asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
+    }
+    const uint8_t* tl = tbl + (FMT == F_IQ2_S ? (lane & 7) * 16 : (lane & 15) * 8);
     const int mt = warp % C::MT, ks = warp / C::MT;
     const int g = lane >> 2, c4 = lane & 3;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    int red_parity = 0;
-    for (int64_t q = 0;; ++q) {
-        const int s = (int)(q % a.nst);
-        if (!mbar_wait(&full[s], (uint32_t)((q / a.nst) & 1), a.err)) return;
-        const uint8_t* stage = stages + (int64_t)s * a.stage_bytes;
+    int s = 0;
+    uint32_t ph = 0;
+    for (;;) {
+        if (!mbar_wait(&full[s], ph, a.err)) return;
+        const uint8_t* stage = stages + s * a.stage_bytes;
         const StepHdr* h = reinterpret_cast<const StepHdr*>(stage);
         const int jobi = h->job;
         if (jobi < 0) return;
@@ -295,80 +527,12 @@ __global__ void __launch_bounds__(GEMV_THREADS + 32, 2) k_gemv(GemvArgs a) {
         const uint8_t* st = stage + HDR_BYTES;
         const int kp = h->kp0 + ks;
         if (kp < h->n_kp && 16 * mt < h->rows) {
-            const int64_t prb = piece_row_bytes(L, kp);
-            const uint8_t* wsl = st + ks * slot_bytes<KS>(L);
-            const int64_t kleft = L.k - (int64_t)kp * PIECE_K;
-            const int klen = (int)(kleft < PIECE_K ? kleft : PIECE_K);
-            const bool active = 64 * c4 < klen;  // this thread's 64 columns exist in the piece
-            const int rA = 16 * mt + g, rB = rA + 8;
+            const uint8_t* wsl = st + ks * a.slot_bytes;
             // this thread's activation row (slot g of the pass), its chunk of this K-slice
-            const uint8_t* brow = st + KS * slot_bytes<KS>(L) + g * C::BROW + ks * 1024 + 16 * c4;
+            const uint8_t* brow = st + KS * a.slot_bytes + g * C::BROW + ks * 1024 + 16 * c4;
             const bool has_tok = (uint32_t)g < ntok;
-            const bool split = jb.split;
-            const bool fast = !split && fmt_soa(L.fmt);
-            IqRun qa, qb;
-            if (fast && active) {
-                qa = iq_run_load(L.fmt, iq_row_in(L.fmt, wsl, rA, prb), c4);
-                qb = iq_run_load(L.fmt, iq_row_in(L.fmt, wsl, rB, prb), c4);
-            }
-#pragma unroll
-            for (int ss = 0; ss < 4; ++ss) {
-                uint32_t af[4][4], al[4][4];
-                if (!active) {
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) af[kk][0] = af[kk][1] = af[kk][2] = af[kk][3] = 0u;
-                } else if (fast) {
-                    uint32_t p0[8], p1[8];
-                    iq_run_pairs(L.fmt, qa, ss, p0, ht);
-                    iq_run_pairs(L.fmt, qb, ss, p1, ht);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        af[kk][0] = p0[2 * kk];
-                        af[kk][1] = p1[2 * kk];
-                        af[kk][2] = p0[2 * kk + 1];
-                        af[kk][3] = p1[2 * kk + 1];
-                    }
-                } else {
-                    float v0[16], v1[16];
-                    const int kofs = 64 * c4 + 16 * ss;
-                    dec16_exact(L.fmt, wsl, rA, prb, kofs, v0, ht);
-                    dec16_exact(L.fmt, wsl, rB, prb, kofs, v1, ht);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-                        for (int hh = 0; hh < 2; ++hh) {  // hh = 0: columns 4kk, 4kk+1; 1: 4kk+2, 4kk+3
-                            const int i = 4 * kk + 2 * hh;
-                            __half2 x0 = __floats2half2_rn(v0[i], v0[i + 1]);
-                            __half2 x1 = __floats2half2_rn(v1[i], v1[i + 1]);
-                            af[kk][2 * hh] = *reinterpret_cast<uint32_t*>(&x0);
-                            af[kk][2 * hh + 1] = *reinterpret_cast<uint32_t*>(&x1);
-                            if (split) {
-                                const float2 f0 = __half22float2(x0), f1 = __half22float2(x1);
-                                __half2 l0 = __floats2half2_rn(__fsub_rn(v0[i], f0.x), __fsub_rn(v0[i + 1], f0.y));
-                                __half2 l1 = __floats2half2_rn(__fsub_rn(v1[i], f1.x), __fsub_rn(v1[i + 1], f1.y));
-                                al[kk][2 * hh] = *reinterpret_cast<uint32_t*>(&l0);
-                                al[kk][2 * hh + 1] = *reinterpret_cast<uint32_t*>(&l1);
-                            }
-                        }
-                    }
-                }
-                // activation chunks (ss, q, h, c): hi cols 0-7, lo 0-7, hi 8-15, lo 8-15
-                uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0, l0 = h0, l1 = h0;
-                if (has_tok) {
-                    h0 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 0));
-                    l0 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 1));
-                    h1 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 2));
-                    l1 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 3));
-                }
-                const uint32_t hb[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-                const uint32_t lb[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    mma_16816(acc, af[kk], hb[2 * kk], hb[2 * kk + 1]);
-                    mma_16816(acc, af[kk], lb[2 * kk], lb[2 * kk + 1]);
-                    if (split) mma_16816(acc, al[kk], hb[2 * kk], hb[2 * kk + 1]);
-                }
-            }
+            if (FMT != 0 && L.fmt == FMT) fast_step<FMT>(wsl, mt, g, c4, tl, brow, has_tok, jb.split != 0, acc);
+            else generic_step(L, kp, wsl, mt, g, c4, brow, has_tok, jb.split != 0, acc);
         }
         // copy what the epilogue needs out of the stage, then hand the stage back
         const bool pass_end = h->pass_end;
@@ -382,29 +546,32 @@ __global__ void __launch_bounds__(GEMV_THREADS + 32, 2) k_gemv(GemvArgs a) {
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == a.nst) {
+            s = 0;
+            ph ^= 1u;
+        }
         if (KS > 1 && pass_end) {
             // K-slices 1..KS-1 hand their partial sums to slice 0 (summed in slice order)
-            float* rb0 = red + red_parity * RED_FLOATS;
             if (ks > 0) {
-                float* rb = rb0 + ((ks - 1) * C::MT + mt) * 128;
+                float* rb = red + ((ks - 1) * C::MT + mt) * 128;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) rb[lane * 4 + i] = acc[i];
             }
-            asm volatile("bar.sync 1, %0;" ::"n"(GEMV_THREADS) : "memory");
+            asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
             if (ks == 0)
                 for (int k2 = 1; k2 < KS; ++k2) {
-                    const float* rb = rb0 + ((k2 - 1) * C::MT + mt) * 128;
+                    const float* rb = red + ((k2 - 1) * C::MT + mt) * 128;
 #pragma unroll
                     for (int i = 0; i < 4; ++i) acc[i] = __fadd_rn(acc[i], rb[lane * 4 + i]);
                 }
-            red_parity ^= 1;
+            asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
         }
         if (pass_end && ks == 0 && 16 * mt < rows) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const uint32_t slot = 2 * c4 + (i & 1);
                 if (slot < ntok) {
-                    const int64_t feat = rt * C::R + 16 * mt + g + ((i >> 1) ? 8 : 0);
+                    const int64_t feat = rt * jb.rows + 16 * mt + g + ((i >> 1) ? 8 : 0);
                     const int64_t orow = (i & 1) ? orow1 : orow0;
                     float v = acc[i];
                     if (jb.bias) v = __fadd_rn(v, jb.bias[(int64_t)e * L.n + feat]);
@@ -416,80 +583,93 @@ __global__ void __launch_bounds__(GEMV_THREADS + 32, 2) k_gemv(GemvArgs a) {
 }
 
 // ---------------------------------------------------------------- host side
-static constexpr int FIXED_SMEM = 128 + HTABLES_BYTES + RED_BYTES;  // barriers, tables, K-slice sums
-
-template <int KS>
-static int launch_ks(GemvArgs a, int64_t max_items, int device, int sm_count, cudaStream_t st) {
+template <int FMT, int KS>
+static int launch_fk(GemvArgs a, int64_t experts_est, int device, int sm_count, cudaStream_t st) {
     using C = Cfg<KS>;
-    int64_t wb = 0;
+    // K-slice bytes of a stage: a routed tile of the fast format at full height (every job at
+    // full height when there is no fast format), and at least 16 rows of every other job; jobs of
+    // other formats get the rows that fit.
+    int64_t slot = 0;
     for (int j = 0; j < a.njobs; ++j) {
-        const int64_t b = KS * slot_bytes<KS>(a.job[j].m.L);
-        if (b > wb) wb = b;
+        const Layout& L = a.job[j].m.L;
+        const int64_t want = (FMT == 0 || L.fmt == FMT) ? (int64_t)C::R : 16;
+        const int64_t b = pad16(want * L.kp_row_bytes);
+        if (b > slot) slot = b;
     }
-    a.stage_bytes = (int)pad16(HDR_BYTES + wb + (int64_t)C::TOKCAP * C::BROW);
-    // two CTAs per SM when the stages allow three or more steps in flight each
-    int per_cta = (228 * 1024) / 2 - 1024 - FIXED_SMEM;
-    int nst = per_cta / a.stage_bytes;
-    int ctas_per_sm = 2;
-    if (nst < 3) {
-        per_cta = 227 * 1024 - 1024 - FIXED_SMEM;
-        nst = per_cta / a.stage_bytes;
-        ctas_per_sm = 1;
+    a.slot_bytes = (int)slot;
+    int64_t items = 0;
+    const int64_t sp = (a.s_count + a.tokcap - 1) / a.tokcap;
+    for (int j = 0; j < a.njobs; ++j) {
+        GemvJob& jb = a.job[j];
+        int64_t rows = slot / jb.m.L.kp_row_bytes / 16 * 16;
+        if (rows > C::R) rows = C::R;
+        jb.rows = (int)rows;
+        const int64_t t = (jb.m.L.n + rows - 1) / rows;
+        items += jb.shared ? t * sp : t * experts_est;
     }
+    a.stage_bytes = (int)((HDR_BYTES + KS * slot + (int64_t)a.tokcap * C::BROW + 127) & ~(int64_t)127);
+    const int fixed = BAR_BYTES + Tbl<FMT>::BYTES + RED_FLOATS * 4 + RING_BYTES;
+    int nst = (SMEM_LIMIT - fixed) / a.stage_bytes;
     if (nst > 8) nst = 8;
     if (nst < 2) return fail(CWX_EUNSUPPORTED, "expert pieces too large for shared memory");
     a.nst = nst;
-    const int smem = FIXED_SMEM + nst * a.stage_bytes;
-    static int attr_set[64][4] = {{0}};
+    const int smem = fixed + nst * a.stage_bytes;
+    static int attr_set[64][3][4] = {{{0}}};
+    const int fidx = FMT == 0 ? 0 : FMT == F_IQ2_S ? 1 : 2;
     const int kidx = KS == 1 ? 0 : KS == 2 ? 1 : KS == 4 ? 2 : 3;
-    if (device < 0 || device >= 64 || attr_set[device][kidx] < smem) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemv<KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (device < 0 || device >= 64 || attr_set[device][fidx][kidx] < smem) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemv<FMT, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_gemv)");
-        if (device >= 0 && device < 64) attr_set[device][kidx] = smem;
+        if (device >= 0 && device < 64) attr_set[device][fidx][kidx] = smem;
     }
-    int64_t grid = (int64_t)sm_count * ctas_per_sm;
-    if (grid > max_items) grid = max_items;
+    int64_t grid = sm_count;
+    if (grid > items) grid = items;
     if (grid < 1) return CWX_OK;
-    k_gemv<KS><<<(unsigned)grid, GEMV_THREADS + 32, smem, st>>>(a);
+    k_gemv<FMT, KS><<<(unsigned)grid, GEMV_THREADS, smem, st>>>(a);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_gemv");
 }
 
-// K-slices per item: the largest split (up to the pieces per row) whose items still fill the GPU
-// twice, chosen from the expected number of experts with picks.
-static int choose_ks(const GemvArgs& a, int64_t experts_est, int sm_count) {
-    int n_kp = 1 << 30;
-    int64_t rows = 0;
-    for (int j = 0; j < a.njobs; ++j)
-        if (!a.job[j].shared) {
-            if (a.job[j].m.L.n_kp < n_kp) n_kp = a.job[j].m.L.n_kp;
-            rows += a.job[j].m.L.n;
-        }
-    if (rows == 0) return 1;
-    int ks = 1;
-    while (ks < 8 && ks * 2 <= n_kp) {
-        const int64_t items = experts_est * ((rows + 128 / ks - 1) / (128 / ks));
-        if (items >= 2 * sm_count) break;
-        ks *= 2;
+template <int FMT>
+static int launch_f(const GemvArgs& a, int ks, int64_t experts_est, int device, int sm_count, cudaStream_t st) {
+    switch (ks) {
+        case 1: return launch_fk<FMT, 1>(a, experts_est, device, sm_count, st);
+        case 2: return launch_fk<FMT, 2>(a, experts_est, device, sm_count, st);
+        case 4: return launch_fk<FMT, 4>(a, experts_est, device, sm_count, st);
+        default: return launch_fk<FMT, 8>(a, experts_est, device, sm_count, st);
     }
-    return ks;
 }
 
-int launch_gemv(const GemvArgs& a, int64_t experts_est, int device, int sm_count, cudaStream_t st) {
-    const int ks = choose_ks(a, experts_est, sm_count);
-    const int64_t R = 128 / ks;
-    const int64_t sp = (a.s_count + 7) / 8;
-    int64_t items = 0;
+int launch_gemv(const GemvArgs& in, int64_t experts_est, int device, int sm_count, cudaStream_t st) {
+    GemvArgs a = in;
+    // picks per pass: the expected largest pile, a power of two up to 8
+    int tc = 1;
+    while (tc < MAX_TOKCAP && tc < a.tok_est) tc *= 2;
+    a.tokcap = tc;
+    // the routed format, when every routed job shares one IQ format
+    int fmt = -1, n_kp = 1 << 30;
+    int64_t rows = 0;
     for (int j = 0; j < a.njobs; ++j) {
-        const int64_t t = (a.job[j].m.L.n + R - 1) / R;
-        items += a.job[j].shared ? t * sp : t * experts_est;
+        const Layout& L = a.job[j].m.L;
+        if (a.job[j].shared) continue;
+        fmt = fmt == -1 ? L.fmt : (fmt == L.fmt ? fmt : 0);
+        if (L.n_kp < n_kp) n_kp = L.n_kp;
+        rows += L.n;
     }
-    switch (ks) {
-        case 1: return launch_ks<1>(a, items, device, sm_count, st);
-        case 2: return launch_ks<2>(a, items, device, sm_count, st);
-        case 4: return launch_ks<4>(a, items, device, sm_count, st);
-        default: return launch_ks<8>(a, items, device, sm_count, st);
-    }
+    if (fmt != F_IQ2_S && fmt != F_IQ3_S) fmt = 0;
+    // K-slices: the smallest split (up to the pieces per row, and 8 staged activation pieces per
+    // stage) whose items still fill the GPU twice
+    int ks = 1;
+    if (rows > 0)
+        while (ks < 8 && ks * 2 <= n_kp && ks * 2 * tc <= MAX_TOKCAP) {
+            const int64_t r = 16 * (NCW / ks);
+            const int64_t items = experts_est * ((rows + r - 1) / r);
+            if (items >= 2 * sm_count) break;
+            ks *= 2;
+        }
+    if (fmt == F_IQ2_S) return launch_f<F_IQ2_S>(a, ks, experts_est, device, sm_count, st);
+    if (fmt == F_IQ3_S) return launch_f<F_IQ3_S>(a, ks, experts_est, device, sm_count, st);
+    return launch_f<0>(a, ks, experts_est, device, sm_count, st);
 }
 
 }  // namespace cwx

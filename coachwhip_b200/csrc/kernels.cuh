@@ -19,8 +19,9 @@ struct GemvJob {
     int bdiv;           // routed: activation row = pick index / bdiv
     float* out;         // output rows: pick index (routed) or token (shared)
     int64_t ostride;
-    int split;          // weights carried as an f16 hi + lo pair
+    int split;          // products carried to ~22 bits (weights and activations as f16 hi + lo)
     const float* bias;  // (n_experts, n) added to the outputs, or NULL
+    int rows;           // rows per work item (set by the launcher)
 };
 
 struct GemvArgs {
@@ -30,8 +31,12 @@ struct GemvArgs {
     const uint32_t* used3;  // (expert, first pair, count) per used expert
     const uint32_t* n_used;
     int s_count;  // tokens of the shared jobs
+    int tok_est;  // expected largest number of picks of one expert (sizes the passes)
     int* err;
-    int stage_bytes;  // set by the launcher
+    // set by the launcher
+    int tokcap;      // picks per pass
+    int slot_bytes;  // weight bytes of one K-slice of a stage
+    int stage_bytes;
     int nst;
 };
 
