@@ -226,6 +226,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // bound is on time, not on polls): a lost copy ends the kernel instead of hanging the GPU.
 __device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, uint64_t limit_ns = 2000000000ull) {
     const uint32_t a = smem_u32(bar);
+    {  // already complete: a plain test costs a fraction of a suspending try_wait
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
     uint64_t t0 = 0;
     for (uint32_t i = 0;; ++i) {
         // the suspend-time hint lets a waiting warp sleep until the phase completes (or 20 us

@@ -37,8 +37,9 @@
 
 namespace cwx {
 
-constexpr int NCW = 16;                      // consumer warps
-constexpr int GEMV_THREADS = NCW * 32 + 32;  // + the producer warp
+constexpr int NCW = 16;                            // consumer warps
+constexpr int NPW = 4;                             // producer warps (one per SM sub-partition)
+constexpr int GEMV_THREADS = (NCW + NPW) * 32;
 constexpr int RED_FLOATS = 14 * 128;         // (KS - 1) * MT fragments of 128 floats, KS * MT = 16, KS <= 8
 constexpr int BAR_BYTES = 256;
 constexpr int HDR_BYTES = 128;
@@ -75,13 +76,13 @@ __device__ __forceinline__ int64_t job_tiles(const GemvJob& j) { return (j.m.L.n
 // Item `it` of the launch: the shared jobs' (tile, pass) items first, then per used expert the
 // tiles of every routed job (expert-major, so one expert's jobs reuse its activation rows in L2).
 template <int KS>
-__device__ __forceinline__ bool get_item(const GemvArgs& a, int64_t it, uint32_t n_used, Item* o) {
-    int64_t routed_tiles = 0;
-    const int64_t sp = (a.s_count + a.tokcap - 1) / a.tokcap;  // passes of a shared tile
+__device__ __forceinline__ bool get_item(const GemvArgs& a, uint32_t it, uint32_t n_used, Item* o) {
+    uint32_t routed_tiles = 0;
+    const uint32_t sp = ((uint32_t)a.s_count + a.tokcap - 1) / (uint32_t)a.tokcap;  // passes of a shared tile
     for (int j = 0; j < a.njobs; ++j) {
         const GemvJob& jb = a.job[j];
         if (jb.shared) {
-            const int64_t t = job_tiles(jb) * sp;
+            const uint32_t t = (uint32_t)job_tiles(jb) * sp;
             if (it < t) {
                 o->job = j;
                 o->e = 0;
@@ -94,18 +95,18 @@ __device__ __forceinline__ bool get_item(const GemvArgs& a, int64_t it, uint32_t
             }
             it -= t;
         } else {
-            routed_tiles += job_tiles(jb);
+            routed_tiles += (uint32_t)job_tiles(jb);
         }
     }
     if (routed_tiles == 0) return false;
     {
-        const int64_t u = it / routed_tiles;
+        const uint32_t u = it / routed_tiles;
         if (u >= n_used) return false;
-        int64_t r = it % routed_tiles;
+        uint32_t r = it - u * routed_tiles;
         for (int j = 0; j < a.njobs; ++j) {
             const GemvJob& jb = a.job[j];
             if (jb.shared) continue;
-            const int64_t t = job_tiles(jb);
+            const uint32_t t = (uint32_t)job_tiles(jb);
             if (r < t) {
                 o->job = j;
                 o->rt = r;
@@ -117,7 +118,7 @@ __device__ __forceinline__ bool get_item(const GemvArgs& a, int64_t it, uint32_t
         o->first = a.used3[3 * u + 1];
         o->count = a.used3[3 * u + 2];
         o->pass0 = 0;
-        o->passes = (int)((o->count + a.tokcap - 1) / a.tokcap);
+        o->passes = (int)((o->count + a.tokcap - 1) / (uint32_t)a.tokcap);
         if (o->passes < 1) o->passes = 1;
     }
 found:
@@ -161,52 +162,81 @@ __device__ __forceinline__ void pass_rows(const GemvArgs& a, const Item& it, int
     }
 }
 
-// The producer's look-ahead: the CTA's items resolved 32 at a time (lane L resolves one, so
+// A producer warp's look-ahead: the CTA's items resolved 8 at a time (lane L resolves one, so
 // their global loads overlap), with the token rows of each item's first pass. Steps then need
 // no global load.
-constexpr int PBATCH = 32;
+constexpr int PBATCH = 8;
 struct PRing {
     Item it[PBATCH];
     uint32_t arow[PBATCH][MAX_TOKCAP];
     uint32_t orow[PBATCH][MAX_TOKCAP];
 };
-static_assert(sizeof(PRing) <= RING_BYTES, "producer ring");
+static_assert(NPW * sizeof(PRing) <= RING_BYTES, "producer rings");
 
-// Issue one step into a stage (all lanes of the producer warp): the tile's rows of KS pieces
-// from sk * KS on, and the pass's activation rows for those columns (lane t < ntok holds row t).
+// The copies of the current item, one per lane: lane l < KS * nseg brings the 64-row-tile segment
+// l % nseg of the item's rows for piece sk * KS + l / nseg of every step, so a step is an address
+// add and one bulk copy per lane. Full pieces of a tile are pstride bytes apart; a shorter last
+// piece (k not a multiple of 256) is addressed on its own.
+struct CopyPlan {
+    const uint8_t* src;  // the segment in piece 0
+    int64_t pstride;     // bytes from one full piece of the segment's tile to the next
+    const uint8_t* tile; // the segment's tile
+    int32_t rel;         // the segment's first row inside its tile
+    int32_t drow;        // its first row inside the item
+    int32_t nrows;       // its rows
+    int32_t cq;          // piece of the step (0..KS-1), -1: lane idle
+};
+
 template <int KS>
-__device__ __forceinline__ void issue_step(const GemvArgs& a, const Item& it, int sk, uint32_t ntok, uint32_t arow,
-                                           uint8_t* stage, uint64_t* bar, int lane) {
-    using C = Cfg<KS>;
+__device__ __forceinline__ CopyPlan plan_copies(const GemvArgs& a, const Item& it, int lane) {
     const GemvJob& jb = a.job[it.job];
     const Layout& L = jb.m.L;
+    const int64_t row0 = it.rt * jb.rows, rowe = row0 + it.rows;
+    const int64_t lt0 = row0 / TILE_ROWS, nseg = (rowe - 1) / TILE_ROWS - lt0 + 1;
+    CopyPlan c;
+    c.cq = -1;
+    if (lane < KS * nseg) {
+        const int64_t lt = lt0 + lane % nseg;
+        const int64_t ra = lt * TILE_ROWS > row0 ? lt * TILE_ROWS : row0;
+        const int64_t rb = (lt + 1) * TILE_ROWS < rowe ? (lt + 1) * TILE_ROWS : rowe;
+        c.cq = lane / (int)nseg;
+        c.tile = jb.m.base + (int64_t)it.e * L.expert_bytes + lt * L.full_tile_bytes;
+        c.rel = (int32_t)(ra - lt * TILE_ROWS);
+        c.drow = (int32_t)(ra - row0);
+        c.nrows = (int32_t)(rb - ra);
+        c.pstride = pad16((int64_t)tile_rows(L, lt) * L.kp_row_bytes);
+        c.src = c.tile + c.rel * L.kp_row_bytes;
+    }
+    return c;
+}
+
+// Issue step sk of the current item: the item's rows of KS pieces into a weight slot (completing
+// on wbar) and the pass's activation rows for those columns into an activation slot (completing
+// on bbar; lane t < ntok holds the row of slot t).
+template <int KS>
+__device__ __forceinline__ void issue_step(const GemvArgs& a, const Item& it, const CopyPlan& c, int64_t prb,
+                                           int64_t lprb, int sk, uint32_t ntok, const uint8_t* brow, uint8_t* wslot,
+                                           uint64_t* wbar, uint8_t* bslot, uint64_t* bbar, int lane) {
+    using C = Cfg<KS>;
     const int kp0 = sk * KS;
     const int nk = it.n_kp - kp0 < KS ? it.n_kp - kp0 : KS;
-    const int64_t row0 = it.rt * jb.rows, rowe = row0 + it.rows;
-    uint32_t total = 0;
-    for (int q = 0; q < nk; ++q) total += (uint32_t)(it.rows * piece_row_bytes(L, kp0 + q));
-    const uint32_t bbytes = (uint32_t)nk * 1024;
-    total += ntok * bbytes;
-    if (lane == 0) mbar_expect_tx(bar, total);
+    const bool last_short = kp0 + nk == it.n_kp && lprb != prb;
+    const uint32_t wbytes = (uint32_t)(it.rows * (prb * (nk - (last_short ? 1 : 0)) + (last_short ? lprb : 0)));
+    if (lane == 0) {
+        mbar_expect_tx(wbar, wbytes);
+        mbar_expect_tx(bbar, ntok * (uint32_t)nk * 1024);
+    }
     __syncwarp();
-    int idx = 0;
-    const uint8_t* ebase = jb.m.base + (int64_t)it.e * L.expert_bytes;
-    for (int q = 0; q < nk; ++q) {
-        const int kp = kp0 + q;
-        const int64_t prb = piece_row_bytes(L, kp);
-        uint8_t* dst = stage + q * a.slot_bytes;
-        for (int64_t r = row0; r < rowe;) {
-            const int64_t lt = r / TILE_ROWS, rr = r % TILE_ROWS;
-            const int64_t rend = (lt + 1) * TILE_ROWS < rowe ? (lt + 1) * TILE_ROWS : rowe;
-            if ((idx++ & 31) == lane)
-                bulk_g2s(dst + (r - row0) * prb, ebase + piece_offset(L, lt, kp) + rr * prb,
-                         (uint32_t)((rend - r) * prb), bar);
-            r = rend;
-        }
+    if (c.cq >= 0 && c.cq < nk) {
+        const int kp = kp0 + c.cq;
+        uint8_t* dst = wslot + c.cq * a.slot_bytes;
+        if (kp == it.n_kp - 1 && lprb != prb)
+            bulk_g2s(dst + c.drow * lprb, c.tile + kp * c.pstride + c.rel * lprb, (uint32_t)(c.nrows * lprb), wbar);
+        else
+            bulk_g2s(dst + c.drow * prb, c.src + kp * c.pstride, (uint32_t)(c.nrows * prb), wbar);
     }
     if ((uint32_t)lane < ntok)
-        bulk_g2s(stage + KS * a.slot_bytes + lane * C::BROW, jb.b + (int64_t)arow * jb.bstride + (int64_t)kp0 * 1024,
-                 bbytes, bar);
+        bulk_g2s(bslot + HDR_BYTES + lane * C::BROW, brow + (int64_t)kp0 * 1024, (uint32_t)nk * 1024, bbar);
 }
 
 // ---------------------------------------------------------------- fast IQ decode
@@ -339,6 +369,68 @@ __device__ __forceinline__ void fast_step(const uint8_t* wsl, int mt, int g, int
     acc[3] = __fmaf_rn(t[3], dB, acc[3]);
 }
 
+// Early-release form of a fast step (f16 activations only): the rows' index, sign and scale bytes
+// and block scales are copied from the weight slot into registers first, so the slot can go back
+// to the producer before the decode and the MMAs run (from these registers, the codebook tables
+// and the activation slot).
+struct FastIn {
+    uint4 QA, QB;     // IQ2_S: [qs | signs]; IQ3_S: qs
+    uint2 SA, SB;     // IQ3_S: signs
+    uint32_t HA, HB;  // IQ2_S: [qh | scales]; IQ3_S: qh | scales << 16
+    float dA, dB;     // block scales of the two rows (times 1/8 for IQ2_S)
+};
+
+template <int FMT>
+__device__ __forceinline__ void fast_load(const uint8_t* wsl, int mt, int g, int c4, FastIn& in) {
+    if (FMT == F_IQ2_S) {
+        const uint8_t* grp = wsl + mt * (16 * 82);
+        in.QA = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 16);
+        in.QB = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 16);
+        in.HA = *reinterpret_cast<const uint32_t*>(grp + 1024 + (g * 4 + c4) * 4);
+        in.HB = *reinterpret_cast<const uint32_t*>(grp + 1024 + ((g + 8) * 4 + c4) * 4);
+        in.dA = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1280 + 2 * g)), 0.125f);
+        in.dB = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1280 + 2 * (g + 8))), 0.125f);
+    } else {
+        const uint8_t* grp = wsl + mt * (16 * 110);
+        in.QA = *reinterpret_cast<const uint4*>(grp + g * 64 + 16 * c4);
+        in.QB = *reinterpret_cast<const uint4*>(grp + (g + 8) * 64 + 16 * c4);
+        in.SA = *reinterpret_cast<const uint2*>(grp + 1024 + g * 32 + 8 * c4);
+        in.SB = *reinterpret_cast<const uint2*>(grp + 1024 + (g + 8) * 32 + 8 * c4);
+        in.HA = *reinterpret_cast<const uint16_t*>(grp + 1536 + g * 8 + 2 * c4) | ((uint32_t)grp[1664 + g * 4 + c4] << 16);
+        in.HB = *reinterpret_cast<const uint16_t*>(grp + 1536 + (g + 8) * 8 + 2 * c4) |
+                ((uint32_t)grp[1664 + (g + 8) * 4 + c4] << 16);
+        in.dA = h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1728 + 2 * g));
+        in.dB = h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1728 + 2 * (g + 8)));
+    }
+}
+
+template <int FMT>
+__device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl, const uint8_t* brow, bool has_tok,
+                                             float* acc) {
+    float t[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ss = 0; ss < 4; ++ss) {
+        uint32_t pa[8], pb[8], hb[8], lb[8];
+        if (FMT == F_IQ2_S) {
+            iq2s_pairs(in.QA, in.HA, ss, tl, pa);
+            iq2s_pairs(in.QB, in.HB, ss, tl, pb);
+        } else {
+            iq3s_pairs(in.QA, in.SA, in.HA & 0xFFFFu, in.HA >> 16, ss, tl, pa);
+            iq3s_pairs(in.QB, in.SB, in.HB & 0xFFFFu, in.HB >> 16, ss, tl, pb);
+        }
+        load_b(brow, ss, has_tok, false, hb, lb);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
+            mma_16816(t, af, hb[2 * kk], hb[2 * kk + 1]);
+        }
+    }
+    acc[0] = __fmaf_rn(t[0], in.dA, acc[0]);
+    acc[1] = __fmaf_rn(t[1], in.dA, acc[1]);
+    acc[2] = __fmaf_rn(t[2], in.dB, acc[2]);
+    acc[3] = __fmaf_rn(t[3], in.dB, acc[3]);
+}
+
 // One step of any format: exact f32 dequantisation rounded to f16 (hi + lo weights when split),
 // activations hi + lo.
 __device__ __forceinline__ void generic_step(const Layout& L, int kp, const uint8_t* wsl, int mt, int g, int c4,
@@ -418,32 +510,44 @@ template <int FMT, int KS>
 __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
     using C = Cfg<KS>;
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);        // 8 x 8 B
-    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + 64);  // 8 x 8 B
+    // two rings: weight slots (released as soon as the warps hold their bytes in registers, on
+    // the fast path) and activation slots with the step header (released after the math)
+    uint64_t* full_w = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty_w = full_w + 8;
+    uint64_t* full_b = full_w + 16;
+    uint64_t* empty_b = full_w + 24;
     uint8_t* tbl = smem + BAR_BYTES;
     float* red = reinterpret_cast<float*>(smem + BAR_BYTES + Tbl<FMT>::BYTES);
-    uint8_t* stages = smem + BAR_BYTES + Tbl<FMT>::BYTES + RED_FLOATS * 4 + RING_BYTES;
+    uint8_t* wslots = smem + BAR_BYTES + Tbl<FMT>::BYTES + RED_FLOATS * 4 + RING_BYTES;
+    uint8_t* bslots = wslots + a.nst * a.wslot_bytes;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < a.nst; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NCW);
+            mbar_init(&full_w[s], 1);
+            mbar_init(&empty_w[s], NCW);
+            mbar_init(&full_b[s], 1);
+            mbar_init(&empty_b[s], NCW);
         }
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == NCW) {
-        // ---------------- producer
-        PRing* ring = reinterpret_cast<PRing*>(smem + BAR_BYTES + Tbl<FMT>::BYTES + RED_FLOATS * 4);
+    if (warp >= NCW) {
+        // ---------------- producers: all four walk the same sequence of steps; producer warp pw
+        // fills the slots s with s % NPW == pw, so every slot has one writer, which has issued the
+        // slot's previous step itself (its empty barriers are never more than a phase behind), and
+        // each producer has several step-times to issue one step
+        const int pw = warp - NCW;
+        PRing* ring = reinterpret_cast<PRing*>(smem + BAR_BYTES + Tbl<FMT>::BYTES + RED_FLOATS * 4) + pw;
         const uint32_t n_used = *a.n_used;
-        int s = 0;        // stage of the next step (step q uses stage q mod nst)
-        uint32_t ph = 0;  // parity of the current round of the ring of stages
+        int s = 0;        // slot of step q (q mod nst in both rings)
+        uint32_t ph = 0;  // parity of the current round of the rings
         int64_t q = 0;
         for (int64_t base = 0;; base += PBATCH) {
             Item mine;
-            const bool ok = get_item<KS>(a, (int64_t)blockIdx.x + (base + lane) * gridDim.x, n_used, &mine);
+            const bool ok = lane < PBATCH &&
+                            get_item<KS>(a, (uint32_t)(blockIdx.x + (base + lane) * gridDim.x), n_used, &mine);
             if (ok) {
                 ring->it[lane] = mine;
                 const uint32_t n0 = pass_tokens(mine, mine.pass0, a.tokcap);
@@ -455,6 +559,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
             const int nitems = __popc(okm);  // items are consecutive: the valid ones come first
             for (int li = 0; li < nitems; ++li) {
                 const Item it = ring->it[li];
+                const GemvJob& jb = a.job[it.job];
+                const CopyPlan cp = plan_copies<KS>(a, it, lane);
+                const int64_t prb = jb.m.L.kp_row_bytes, lprb = jb.m.L.last_kp_row_bytes;
                 for (int pass = it.pass0; pass < it.pass0 + it.passes; ++pass) {
                     const uint32_t ntok = pass_tokens(it, pass, a.tokcap);
                     uint32_t arow = 0, orow = 0;
@@ -466,24 +573,30 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
                             pass_rows(a, it, pass, lane, &arow, &orow);
                         }
                     }
+                    const uint8_t* brow = jb.b + (int64_t)arow * jb.bstride;
                     for (int sk = 0; sk < it.nsk; ++sk) {
-                        if (q >= a.nst && !mbar_wait(&empty[s], ph ^ 1u, a.err)) return;
-                        uint8_t* stage = stages + s * a.stage_bytes;
-                        StepHdr* h = reinterpret_cast<StepHdr*>(stage);
-                        if (lane == 0) {
-                            h->job = it.job;
-                            h->e = it.e;
-                            h->rt = it.rt;
-                            h->rows = it.rows;
-                            h->n_kp = it.n_kp;
-                            h->kp0 = sk * KS;
-                            h->pass_start = sk == 0;
-                            h->pass_end = sk == it.nsk - 1;
-                            h->ntok = ntok;
+                        if (s % NPW == pw) {
+                            if (q >= a.nst && (!mbar_wait(&empty_w[s], ph ^ 1u, a.err) ||
+                                               !mbar_wait(&empty_b[s], ph ^ 1u, a.err)))
+                                return;
+                            uint8_t* bslot = bslots + s * a.bslot_bytes;
+                            StepHdr* h = reinterpret_cast<StepHdr*>(bslot);
+                            if (lane == 0) {
+                                h->job = it.job;
+                                h->e = it.e;
+                                h->rt = it.rt;
+                                h->rows = it.rows;
+                                h->n_kp = it.n_kp;
+                                h->kp0 = sk * KS;
+                                h->pass_start = sk == 0;
+                                h->pass_end = sk == it.nsk - 1;
+                                h->ntok = ntok;
+                            }
+                            if ((uint32_t)lane < ntok) h->orow[lane] = orow;
+                            __syncwarp();
+                            issue_step<KS>(a, it, cp, prb, lprb, sk, ntok, brow, wslots + s * a.wslot_bytes,
+                                           &full_w[s], bslot, &full_b[s], lane);
                         }
-                        if ((uint32_t)lane < ntok) h->orow[lane] = orow;
-                        __syncwarp();
-                        issue_step<KS>(a, it, sk, ntok, arow, stage + HDR_BYTES, &full[s], lane);
                         ++q;
                         if (++s == a.nst) {
                             s = 0;
@@ -493,12 +606,14 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
                 }
             }
             __syncwarp();  // the ring is refilled by the next batch
-            if (okm != 0xffffffffu) break;
+            if (okm != (1u << PBATCH) - 1u) break;
         }
-        if (q >= a.nst && !mbar_wait(&empty[s], ph ^ 1u, a.err)) return;
-        if (lane == 0) {
-            reinterpret_cast<StepHdr*>(stages + s * a.stage_bytes)->job = -1;
-            mbar_arrive(&full[s]);
+        if (s % NPW == pw) {  // the end marker, after the last step
+            if (q >= a.nst && !mbar_wait(&empty_b[s], ph ^ 1u, a.err)) return;
+            if (lane == 0) {
+                reinterpret_cast<StepHdr*>(bslots + s * a.bslot_bytes)->job = -1;
+                mbar_arrive(&full_b[s]);
+            }
         }
         return;
     }
@@ -515,37 +630,49 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
     int s = 0;
     uint32_t ph = 0;
     for (;;) {
-        if (!mbar_wait(&full[s], ph, a.err)) return;
-        const uint8_t* stage = stages + s * a.stage_bytes;
-        const StepHdr* h = reinterpret_cast<const StepHdr*>(stage);
+        if (!mbar_wait(&full_b[s], ph, a.err)) return;
+        const uint8_t* bslot = bslots + s * a.bslot_bytes;
+        const StepHdr* h = reinterpret_cast<const StepHdr*>(bslot);
         const int jobi = h->job;
         if (jobi < 0) return;
         const GemvJob& jb = a.job[jobi];
         const Layout& L = jb.m.L;
+        // the header into registers
         const uint32_t ntok = h->ntok;
-        if (h->pass_start) acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-        const uint8_t* st = stage + HDR_BYTES;
-        const int kp = h->kp0 + ks;
-        if (kp < h->n_kp && 16 * mt < h->rows) {
-            const uint8_t* wsl = st + ks * a.slot_bytes;
-            // this thread's activation row (slot g of the pass), its chunk of this K-slice
-            const uint8_t* brow = st + KS * a.slot_bytes + g * C::BROW + ks * 1024 + 16 * c4;
-            const bool has_tok = (uint32_t)g < ntok;
-            if (FMT != 0 && L.fmt == FMT) fast_step<FMT>(wsl, mt, g, c4, tl, brow, has_tok, jb.split != 0, acc);
-            else generic_step(L, kp, wsl, mt, g, c4, brow, has_tok, jb.split != 0, acc);
-        }
-        // copy what the epilogue needs out of the stage, then hand the stage back
-        const bool pass_end = h->pass_end;
+        const bool pass_start = h->pass_start, pass_end = h->pass_end;
         const uint32_t e = h->e;
         const int64_t rt = h->rt;
         const int rows = h->rows;
+        const int kp = h->kp0 + ks;
         uint32_t orow0 = 0, orow1 = 0;
         if (pass_end) {
             orow0 = h->orow[2 * c4];
             orow1 = h->orow[2 * c4 + 1];
         }
+        if (pass_start) acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+        const bool active = kp < h->n_kp && 16 * mt < rows;
+        const bool lo = jb.split != 0;
+        const uint8_t* wsl = wslots + s * a.wslot_bytes + ks * a.slot_bytes;
+        // this thread's activation row (slot g of the pass), its chunk of this K-slice
+        const uint8_t* brow = bslot + HDR_BYTES + g * C::BROW + ks * 1024 + 16 * c4;
+        const bool has_tok = (uint32_t)g < ntok;
+        if (!mbar_wait(&full_w[s], ph, a.err)) return;
+        if (FMT != 0 && L.fmt == FMT && !lo) {
+            FastIn in;
+            if (active) fast_load<FMT>(wsl, mt, g, c4, in);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_w[s]);  // the weights go back before the math
+            if (active) fast_compute<FMT>(in, tl, brow, has_tok, acc);
+        } else {
+            if (active) {
+                if (FMT != 0 && L.fmt == FMT) fast_step<FMT>(wsl, mt, g, c4, tl, brow, has_tok, true, acc);
+                else generic_step(L, kp, wsl, mt, g, c4, brow, has_tok, lo, acc);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_w[s]);
+        }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        if (lane == 0) mbar_arrive(&empty_b[s]);
         if (++s == a.nst) {
             s = 0;
             ph ^= 1u;
@@ -607,13 +734,14 @@ static int launch_fk(GemvArgs a, int64_t experts_est, int device, int sm_count, 
         const int64_t t = (jb.m.L.n + rows - 1) / rows;
         items += jb.shared ? t * sp : t * experts_est;
     }
-    a.stage_bytes = (int)((HDR_BYTES + KS * slot + (int64_t)a.tokcap * C::BROW + 127) & ~(int64_t)127);
+    a.wslot_bytes = (int)((KS * slot + 127) & ~(int64_t)127);
+    a.bslot_bytes = (int)((HDR_BYTES + (int64_t)a.tokcap * C::BROW + 127) & ~(int64_t)127);
     const int fixed = BAR_BYTES + Tbl<FMT>::BYTES + RED_FLOATS * 4 + RING_BYTES;
-    int nst = (SMEM_LIMIT - fixed) / a.stage_bytes;
+    int nst = (SMEM_LIMIT - fixed) / (a.wslot_bytes + a.bslot_bytes);
     if (nst > 8) nst = 8;
     if (nst < 2) return fail(CWX_EUNSUPPORTED, "expert pieces too large for shared memory");
     a.nst = nst;
-    const int smem = fixed + nst * a.stage_bytes;
+    const int smem = fixed + nst * (a.wslot_bytes + a.bslot_bytes);
     static int attr_set[64][3][4] = {{{0}}};
     const int fidx = FMT == 0 ? 0 : FMT == F_IQ2_S ? 1 : 2;
     const int kidx = KS == 1 ? 0 : KS == 2 ? 1 : KS == 4 ? 2 : 3;

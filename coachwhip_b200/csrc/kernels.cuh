@@ -35,9 +35,10 @@ struct GemvArgs {
     int* err;
     // set by the launcher
     int tokcap;      // picks per pass
-    int slot_bytes;  // weight bytes of one K-slice of a stage
-    int stage_bytes;
-    int nst;
+    int slot_bytes;   // weight bytes of one K-slice of a step
+    int wslot_bytes;  // one weight slot (KS K-slices)
+    int bslot_bytes;  // one activation slot (step header + activation rows)
+    int nst;          // slots per ring
 };
 
 // Bytes of one packed activation row of k columns (1024 per 256-column piece).
