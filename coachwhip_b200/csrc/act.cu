@@ -18,8 +18,13 @@ namespace cwx {
 
 __device__ __forceinline__ float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
 
-// One warp per (row, 256 columns); lane l takes columns 8l..8l+7 of the block.
-__global__ void __launch_bounds__(256) k_prep(PrepArgs p) {
+// One warp per (row, 256 columns); lane l takes columns 8l..8l+7 of the block. Up to two
+// independent preparations per launch (blockIdx.y picks one).
+struct PrepPair {
+    PrepArgs p[2];
+};
+__global__ void __launch_bounds__(256) k_prep(PrepPair pp) {
+    const PrepArgs& p = pp.p[blockIdx.y];
     const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int64_t nb = (p.K + 255) / 256;
@@ -136,13 +141,23 @@ __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ rows,
     out[i] = acc;
 }
 
-int launch_prep(const PrepArgs& p, cudaStream_t st) {
-    if (p.R == 0) return CWX_OK;
-    const int64_t warps = p.R * ((p.K + 255) / 256);
-    k_prep<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(p);
+int launch_prep2(const PrepArgs* p, int njobs, cudaStream_t st) {
+    PrepPair pp;
+    int64_t warps = 0;
+    int nj = 0;
+    for (int j = 0; j < njobs; ++j) {
+        if (p[j].R == 0) continue;
+        pp.p[nj++] = p[j];
+        const int64_t wj = p[j].R * ((p[j].K + 255) / 256);
+        if (wj > warps) warps = wj;
+    }
+    if (nj == 0) return CWX_OK;
+    k_prep<<<dim3((unsigned)((warps * 32 + 255) / 256), nj), 256, 0, st>>>(pp);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_prep");
 }
+
+int launch_prep(const PrepArgs& p, cudaStream_t st) { return launch_prep2(&p, 1, st); }
 
 int launch_combine(const float* rows, const float* w, int T, int K, int H, const float* shared, const float* sgate,
                    const float* residual, float* out, cudaStream_t st) {

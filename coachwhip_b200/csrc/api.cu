@@ -358,7 +358,7 @@ extern "C" int cwx_permute(cwx_ctx* c, const uint32_t* ids, int32_t T, int32_t K
     uint32_t* used3 = w.take<uint32_t>((size_t)3 * E);
     uint32_t* n_used = w.take<uint32_t>(4);
     uint32_t* scratch = w.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
-    c->launches += 3;
+    c->launches += perm_launches(n, E);
     return launch_permute(ids, n, E, pairs, heads, used3, n_used, scratch, c->d_err, st);
 }
 
@@ -406,7 +406,7 @@ extern "C" int cwx_expert_matmul(cwx_ctx* c, const cwx_bank* bank, const float* 
     a.n_used = n_used;
     a.tok_est = tokens;
     a.err = c->d_err;
-    c->launches += 5;
+    c->launches += perm_launches(n, E) + 2;
     return launch_gemv(a, n < E ? n : E, c->device, c->sm_count, st);
 }
 
@@ -445,14 +445,15 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
         if ((rc = launch_permute(p.ids, n, E, p.pairs, p.heads, p.used3, p.n_used, p.perm, c->d_err, st))) return rc;
         t.end();
     }
-    c->launches += 5;
+    c->launches += 2 + perm_launches(n, E);
     {
         PhaseTimer t(c, st, CWX_PHASE_PREP);
-        for (int m = 0; m < 3; ++m) {
-            if (!p.xpk[m]) continue;
-            if ((rc = launch_prep(prep(A->x, nullptr, T, H, m, p.xpk[m]), st))) return rc;
-            c->launches += 1;
-        }
+        PrepArgs px[2];
+        int nx = 0;
+        for (int m = 0; m < 3; ++m)
+            if (p.xpk[m]) px[nx++] = prep(A->x, nullptr, T, H, m, p.xpk[m]);
+        if ((rc = launch_prep2(px, nx, st))) return rc;
+        c->launches += 1;
         t.end();
     }
     const int64_t used_max = n < E ? n : E;
@@ -489,11 +490,11 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
         pa.gate_b = L->gate_b;
         pa.up_b = L->up_b;
         pa.ids = p.ids;
-        if ((rc = launch_prep(pa, st))) return rc;
-        if (shared && (rc = launch_prep(prep(p.gs, p.us, T, Is, p.msd, p.hspk), st))) return rc;
+        PrepArgs ph[2] = {pa, shared ? prep(p.gs, p.us, T, Is, p.msd, p.hspk) : PrepArgs{}};
+        if ((rc = launch_prep2(ph, shared ? 2 : 1, st))) return rc;
         t.end();
     }
-    c->launches += 2 + (shared ? 1 : 0);
+    c->launches += 2;
     {
         GemvArgs d;
         memset(&d, 0, sizeof d);

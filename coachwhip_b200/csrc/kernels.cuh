@@ -49,6 +49,7 @@ int launch_router(const float* x, const float* w, const float* b, int T, int H, 
 int launch_route(const float* logits, int T, int E, int K, int norm, uint32_t* ids, float* w, const float* x,
                  const float* g_inp, int H, float* sgate, cudaStream_t st);
 size_t perm_scratch_bytes(int64_t n, int E);
+int perm_launches(int64_t n, int E);  // kernels launch_permute issues
 int launch_permute(const uint32_t* ids, int64_t n, int E, uint32_t* pairs, uint32_t* heads, uint32_t* used3,
                    uint32_t* n_used, uint32_t* scratch, int* err, cudaStream_t st);
 
@@ -68,6 +69,7 @@ struct PrepArgs {
     uint8_t* out;
 };
 int launch_prep(const PrepArgs& p, cudaStream_t st);
+int launch_prep2(const PrepArgs* p, int njobs, cudaStream_t st);  // up to two preparations in one launch
 int launch_combine(const float* rows, const float* w, int T, int K, int H, const float* shared, const float* sgate,
                    const float* residual, float* out, cudaStream_t st);
 // experts_est: the number of experts expected to have picks (sizes the grid and the K split).

@@ -37,64 +37,73 @@ __device__ __forceinline__ float avx_lane_tree(float acc) {
     return __shfl_sync(0xffffffffu, r, 0);
 }
 
-// logits (T, E): one warp per (expert, K quarter), 8 tokens per block row (blockIdx.y), f64
-// partial sums reduced in a fixed order. Block = 8 warps = 2 experts.
+// Router logits on the FP64 tensor cores: block = 8 warps on a tile of 8 experts x 8 tokens,
+// warp w taking the w-th eighth of K; each warp accumulates its slice with mma m8n8k4 f64 (the
+// products of f32 inputs are exact in f64), the eight slices are added in warp order and the sum is
+// rounded once to f32 (+ the bias).
+__device__ __forceinline__ void dmma_8x8x4(double* c, double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+                 : "+d"(c[0]), "+d"(c[1])
+                 : "d"(a), "d"(b));
+}
+
 __global__ void __launch_bounds__(256) k_router(const float* __restrict__ x, const float* __restrict__ w,
                                                 const float* __restrict__ bias, int T, int H, int E,
                                                 float* __restrict__ logits) {
-    __shared__ double part[8][8];
-    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int e = blockIdx.x * 2 + (warp >> 2);
-    int q = warp & 3;
-    int kq = (H + 3) / 4;
-    int k0 = q * kq, k1 = min(H, k0 + kq);
-    const float* wr = w + (int64_t)(e < E ? e : 0) * H;
-    for (int t0 = 8 * blockIdx.y; t0 < T; t0 += 8 * gridDim.y) {
-        double acc[8];
+    __shared__ double red[8][64];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e0 = blockIdx.x * 8, t0 = blockIdx.y * 8;
+    const int r = lane >> 2, kq = lane & 3;
+    const int ks = (H + 7) / 8, k0 = warp * ks, k1 = min(H, k0 + ks);
+    // A[r][k] = w[e0 + r][k], B[k][n] = x[t0 + n][k]: each lane reads row r at k = 4j + kq
+    const bool ea = e0 + r < E, tb = t0 + r < T;
+    const float* wr = w + (int64_t)(ea ? e0 + r : 0) * H;
+    const float* xr = x + (int64_t)(tb ? t0 + r : 0) * H;
+    double c[2] = {0.0, 0.0};
+    int k = k0;
+    for (; k + 16 <= k1; k += 16) {  // four k4 steps with their loads issued together
+        float av[4], bv[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = 0.0;
-        if (e < E) {
-            for (int k = k0 + lane; k < k1; k += 32) {
-                double wv = (double)__ldg(wr + k);
+        for (int j = 0; j < 4; ++j) {
+            av[j] = ea ? __ldg(wr + k + 4 * j + kq) : 0.f;
+            bv[j] = tb ? __ldg(xr + k + 4 * j + kq) : 0.f;
+        }
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    if (t0 + j < T) acc[j] = fma(wv, (double)__ldg(x + (int64_t)(t0 + j) * H + k), acc[j]);
+        for (int j = 0; j < 4; ++j) dmma_8x8x4(c, (double)av[j], (double)bv[j]);
+    }
+    for (; k < k1; k += 4) {
+        const bool in = k + kq < k1;
+        const float av = ea && in ? __ldg(wr + k + kq) : 0.f, bv = tb && in ? __ldg(xr + k + kq) : 0.f;
+        dmma_8x8x4(c, (double)av, (double)bv);
+    }
+    // C[r][2kq], C[r][2kq+1]
+    red[warp][r * 8 + 2 * kq] = c[0];
+    red[warp][r * 8 + 2 * kq + 1] = c[1];
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int idx = lane * 2 + h, er = idx >> 3, tn = idx & 7;
+            double v = red[0][idx];
+            for (int q = 1; q < 8; ++q) v += red[q][idx];
+            const int e = e0 + er, t = t0 + tn;
+            if (e < E && t < T) {
+                float l = (float)v;
+                if (bias) l = __fadd_rn(l, bias[e]);
+                logits[(int64_t)t * E + e] = l;
             }
         }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            double v = acc[j];
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            acc[j] = v;
-        }
-        if (lane < 8) {
-            double v = acc[0];
-#pragma unroll
-            for (int j = 1; j < 8; ++j)
-                if (lane == j) v = acc[j];
-            part[warp][lane] = v;
-        }
-        __syncthreads();
-        if ((warp & 3) == 0 && lane < 8 && e < E && t0 + lane < T) {
-            double s = ((part[warp][lane] + part[warp + 1][lane]) + part[warp + 2][lane]) + part[warp + 3][lane];
-            float l = (float)s;
-            if (bias) l = __fadd_rn(l, bias[e]);
-            logits[(int64_t)(t0 + lane) * E + e] = l;
-        }
-        __syncthreads();
     }
 }
 
 // One warp per token: softmax over E (<= 1024), k picks (<= 32) best first with ties to the
 // lowest id, weights renormalised over the picks when norm. Optionally the shared-expert gate
 // sigmoid(sum_keepdim(x * gate_inp)) in candle's AVX summation order.
-__global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits, int T, int E, int K, int norm,
-                                               uint32_t* __restrict__ ids, float* __restrict__ wout,
+__global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits, int T, int E, int K, int norm, uint32_t* __restrict__ ids, float* __restrict__ wout,
                                                const float* __restrict__ x, const float* __restrict__ g_inp,
                                                int H, float* __restrict__ sgate) {
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
-    const float* l = logits + (int64_t)warp * E;
     const int NV = 32;  // up to 1024 experts
     float v[NV];
     int nv = (E + 31) / 32;
@@ -102,8 +111,12 @@ __global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits,
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         int e = 32 * i + lane;
-        v[i] = (i < nv && e < E) ? l[e] : -INFINITY;
-        if (i < nv && e < E) mx = fmaxf(mx, v[i]);
+        if (i < nv && e < E) {
+            v[i] = logits[(int64_t)warp * E + e];
+            mx = fmaxf(mx, v[i]);
+        } else {
+            v[i] = -INFINITY;
+        }
     }
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     int whole = E / 32;  // whole 32-element steps
@@ -168,7 +181,16 @@ __global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits,
         const float* xr = x + (int64_t)warp * H;
         int wholeh = H / 32;
         float a = 0.f;
-        for (int i = 0; i < wholeh; ++i) a = __fadd_rn(a, __fmul_rn(xr[32 * i + lane], g_inp[32 * i + lane]));
+        // loads issued 16 at a time ahead of the in-order sum (the sum's order is fixed)
+        for (int i0 = 0; i0 < wholeh; i0 += 16) {
+            float pr[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                pr[j] = i0 + j < wholeh ? __fmul_rn(__ldg(xr + 32 * (i0 + j) + lane), __ldg(g_inp + 32 * (i0 + j) + lane)) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (i0 + j < wholeh) a = __fadd_rn(a, pr[j]);
+        }
         float sum = avx_lane_tree(a);
         for (int j = wholeh * 32; j < H; ++j) sum = __fadd_rn(sum, __fmul_rn(xr[j], g_inp[j]));
         if (lane == 0) sgate[warp] = __fdiv_rn(1.0f, __fadd_rn(exp_cr(-sum), 1.0f));
@@ -304,13 +326,92 @@ __global__ void __launch_bounds__(1024) k_perm_scatter(const uint32_t* __restric
     }
 }
 
+// Small piles in one block (n <= 2048 picks, E <= 1024 experts): counts, the exclusive scan,
+// heads and the used list, then one thread per expert writes its own picks in pick order (stable
+// by construction). Replaces the three launches of the general path for decode-sized batches.
+constexpr int PERM_SMALL_N = 2048;
+__global__ void __launch_bounds__(1024) k_perm_small(const uint32_t* __restrict__ ids, int n, int E,
+                                                     uint32_t* __restrict__ pairs, uint32_t* __restrict__ heads,
+                                                     uint32_t* __restrict__ used3, uint32_t* __restrict__ n_used,
+                                                     int* err) {
+    __shared__ uint32_t sid[PERM_SMALL_N];
+    __shared__ uint32_t cnt[1024];
+    __shared__ uint32_t wsum[32], wusum[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    cnt[tid] = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += 1024) {
+        const uint32_t id = ids[i];
+        sid[i] = id;
+        if (id < (uint32_t)E) atomicAdd(&cnt[id], 1u);
+        else dev_error(err, DE_BAD_ID);
+    }
+    __syncthreads();
+    const uint32_t c = tid < E ? cnt[tid] : 0u, u = c > 0u ? 1u : 0u;
+    uint32_t ic = c, iu = u;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t a = __shfl_up_sync(0xffffffffu, ic, o), b = __shfl_up_sync(0xffffffffu, iu, o);
+        if (lane >= o) {
+            ic += a;
+            iu += b;
+        }
+    }
+    if (lane == 31) {
+        wsum[warp] = ic;
+        wusum[warp] = iu;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t a = wsum[lane], b = wusum[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t x = __shfl_up_sync(0xffffffffu, a, o), y = __shfl_up_sync(0xffffffffu, b, o);
+            if (lane >= o) {
+                a += x;
+                b += y;
+            }
+        }
+        wsum[lane] = a;
+        wusum[lane] = b;
+    }
+    __syncthreads();
+    const uint32_t first = (warp ? wsum[warp - 1] : 0u) + ic - c;
+    const uint32_t uf = (warp ? wusum[warp - 1] : 0u) + iu - u;
+    if (tid == 0) *n_used = wusum[31];
+    if (tid < E) {
+        heads[3 * tid] = (uint32_t)tid;
+        heads[3 * tid + 1] = first;
+        heads[3 * tid + 2] = c;
+        if (u) {
+            used3[3 * uf] = (uint32_t)tid;
+            used3[3 * uf + 1] = first;
+            used3[3 * uf + 2] = c;
+        }
+        cnt[tid] = first;  // running write position of this expert's pile
+    }
+    __syncthreads();
+    // stable scatter: warp 0 takes the picks 32 at a time, in order; lanes with the same expert are
+    // ranked by lane, and the expert's position advances by their number
+    if (warp == 0)
+        for (int i0 = 0; i0 < n; i0 += 32) {
+            const int i = i0 + lane;
+            const uint32_t id = i < n ? sid[i] : 0xffffffffu;
+            const bool valid = id < (uint32_t)E;
+            const uint32_t peers = __match_any_sync(0xffffffffu, valid ? id : 0xffffffffu);
+            const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
+            if (valid) pairs[cnt[id] + rank] = (uint32_t)i;
+            __syncwarp();
+            if (valid && rank == 0) cnt[id] += __popc(peers);
+            __syncwarp();
+        }
+}
+
 // ---------------------------------------------------------------- host launchers
 int launch_router(const float* x, const float* w, const float* b, int T, int H, int E, float* logits,
                   cudaStream_t st) {
     if (T == 0) return CWX_OK;
-    int ty = (T + 7) / 8;
-    if (ty > 64) ty = 64;
-    k_router<<<dim3((E + 1) / 2, ty), 256, 0, st>>>(x, w, b, T, H, E, logits);
+    k_router<<<dim3((E + 7) / 8, (T + 7) / 8), 256, 0, st>>>(x, w, b, T, H, E, logits);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_router");
 }
@@ -325,6 +426,8 @@ int launch_route(const float* logits, int T, int E, int K, int norm, uint32_t* i
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_route");
 }
 
+int perm_launches(int64_t n, int E) { return n <= PERM_SMALL_N && E <= 1024 ? 1 : 3; }
+
 size_t perm_scratch_bytes(int64_t n, int E) {
     int64_t ntiles = (n + PERM_TILE - 1) / PERM_TILE;
     return (size_t)(ntiles > 0 ? ntiles : 1) * E * 4;
@@ -332,6 +435,11 @@ size_t perm_scratch_bytes(int64_t n, int E) {
 
 int launch_permute(const uint32_t* ids, int64_t n, int E, uint32_t* pairs, uint32_t* heads, uint32_t* used3,
                    uint32_t* n_used, uint32_t* scratch, int* err, cudaStream_t st) {
+    if (n <= PERM_SMALL_N && E <= 1024) {
+        k_perm_small<<<1, 1024, 0, st>>>(ids, (int)n, E, pairs, heads, used3, n_used, err);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_perm_small");
+    }
     int ntiles = (int)((n + PERM_TILE - 1) / PERM_TILE);
     if (ntiles == 0) ntiles = 1;
     size_t sh = (size_t)E * 4;
