@@ -431,6 +431,91 @@ __device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl
     acc[3] = __fmaf_rn(t[3], in.dB, acc[3]);
 }
 
+// Q4_K: y = d * sc * q - dmin * m per 32-column sub-block (sub-blocks 2c and 2c+1 are the low
+// and high nibbles of the same 32 bytes of 64-column chunk c). Two exact-integer products on the
+// tensor cores: A1 = sc * q (<= 945, exact in f16) and A2 = m (constant over a sub-block), both
+// against the same activation fragments; per piece acc += d * t1 - dmin * t2 in f32.
+struct Q4Row {
+    uint4 qlo, qhi;  // the chunk's 32 quant bytes
+    float d, dmin;
+    uint32_t sc01;   // sc of sub-blocks 2c, 2c+1 as f16 pair halves (sc, sc) in two words
+    __half2 s0, s1, m0, m1;
+};
+
+__device__ __forceinline__ Q4Row q4_row(const uint8_t* row, int c4) {
+    Q4Row r;
+    const uint4 h = *reinterpret_cast<const uint4*>(row);  // d, dmin, scales[12]
+    r.qlo = *reinterpret_cast<const uint4*>(row + 16 + 32 * c4);
+    r.qhi = *reinterpret_cast<const uint4*>(row + 32 + 32 * c4);
+    r.d = h2f_bits((uint16_t)(h.x & 0xFFFF));
+    r.dmin = h2f_bits((uint16_t)(h.x >> 16));
+    const uint32_t sw[3] = {h.y, h.z, h.w};  // scale bytes 0..11
+    auto sb = [&](int i) -> uint32_t { return (sw[i >> 2] >> (8 * (i & 3))) & 0xFFu; };
+    uint32_t sc[2], mn[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const int j = 2 * c4 + t;  // get_scale_min_k4 (vendor/candle-core/src/quantized/utils.rs:50)
+        if (j < 4) {
+            sc[t] = sb(j) & 63u;
+            mn[t] = sb(j + 4) & 63u;
+        } else {
+            sc[t] = (sb(j + 4) & 0xFu) | ((sb(j - 4) >> 6) << 4);
+            mn[t] = (sb(j + 4) >> 4) | ((sb(j) >> 6) << 4);
+        }
+    }
+    r.s0 = __floats2half2_rn((float)sc[0], (float)sc[0]);
+    r.s1 = __floats2half2_rn((float)sc[1], (float)sc[1]);
+    r.m0 = __floats2half2_rn((float)mn[0], (float)mn[0]);
+    r.m1 = __floats2half2_rn((float)mn[1], (float)mn[1]);
+    return r;
+}
+
+// Columns 16ss..16ss+15 of the thread's 64 as 8 f16 pairs sc * q.
+__device__ __forceinline__ void q4_pairs(const Q4Row& r, int ss, uint32_t* p) {
+    const uint4 q = (ss & 1) ? r.qhi : r.qlo;
+    const __half2 sc = ss < 2 ? r.s0 : r.s1;
+    const __half2 bias = __hmul2(sc, __floats2half2_rn(-1024.f, -1024.f));
+    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi) {
+        const uint32_t nib = (ss < 2 ? w4[wi] : (w4[wi] >> 4)) & 0x0F0F0F0Fu;
+        // (1024 + q) as f16 from each nibble byte, then (1024 + q) * sc - 1024 * sc = q * sc exactly
+        const uint32_t h0 = __byte_perm(nib, 0x64646464u, 0x4140), h1 = __byte_perm(nib, 0x64646464u, 0x4342);
+        p[2 * wi] = h22u(__hfma2(u2h2(h0), sc, bias));
+        p[2 * wi + 1] = h22u(__hfma2(u2h2(h1), sc, bias));
+    }
+}
+
+__device__ __forceinline__ void q4k_step(const uint8_t* wsl, int mt, int g, int c4, const uint8_t* brow, bool has_tok,
+                                         bool lo, float* acc) {
+    const Q4Row A = q4_row(wsl + (16 * mt + g) * 144, c4);
+    const Q4Row Bq = q4_row(wsl + (16 * mt + g + 8) * 144, c4);
+    float t1[4] = {0.f, 0.f, 0.f, 0.f}, t2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ss = 0; ss < 4; ++ss) {
+        uint32_t pa[8], pb[8], hb[8], lb[8];
+        q4_pairs(A, ss, pa);
+        q4_pairs(Bq, ss, pb);
+        load_b(brow, ss, has_tok, lo, hb, lb);
+        const uint32_t ma = h22u(ss < 2 ? A.m0 : A.m1), mb = h22u(ss < 2 ? Bq.m0 : Bq.m1);
+        const uint32_t am[4] = {ma, mb, ma, mb};
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
+            mma_16816(t1, af, hb[2 * kk], hb[2 * kk + 1]);
+            mma_16816(t2, am, hb[2 * kk], hb[2 * kk + 1]);
+            if (lo) {
+                mma_16816(t1, af, lb[2 * kk], lb[2 * kk + 1]);
+                mma_16816(t2, am, lb[2 * kk], lb[2 * kk + 1]);
+            }
+        }
+    }
+    acc[0] = __fmaf_rn(-t2[0], A.dmin, __fmaf_rn(t1[0], A.d, acc[0]));
+    acc[1] = __fmaf_rn(-t2[1], A.dmin, __fmaf_rn(t1[1], A.d, acc[1]));
+    acc[2] = __fmaf_rn(-t2[2], Bq.dmin, __fmaf_rn(t1[2], Bq.d, acc[2]));
+    acc[3] = __fmaf_rn(-t2[3], Bq.dmin, __fmaf_rn(t1[3], Bq.d, acc[3]));
+}
+
 // One step of any format: exact f32 dequantisation rounded to f16 (hi + lo weights when split),
 // activations hi + lo.
 __device__ __forceinline__ void generic_step(const Layout& L, int kp, const uint8_t* wsl, int mt, int g, int c4,
@@ -666,6 +751,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
         } else {
             if (active) {
                 if (FMT != 0 && L.fmt == FMT) fast_step<FMT>(wsl, mt, g, c4, tl, brow, has_tok, true, acc);
+                else if (L.fmt == F_Q4_K && L.kp_row_bytes == 144) q4k_step(wsl, mt, g, c4, brow, has_tok, lo, acc);
                 else generic_step(L, kp, wsl, mt, g, c4, brow, has_tok, lo, acc);
             }
             __syncwarp();
