@@ -247,7 +247,7 @@ __device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, uint6
             : "memory");
         if (done) return true;
         if (i == 0) t0 = globaltimer_ns();
-        else if (globaltimer_ns() - t0 > limit_ns) break;
+        else if ((i & 63) == 0 && globaltimer_ns() - t0 > limit_ns) break;
     }
     dev_error(err, DE_TIMEOUT);
     return false;

@@ -210,22 +210,18 @@ __device__ __forceinline__ CopyPlan plan_copies(const GemvArgs& a, const Item& i
     return c;
 }
 
-// Issue step sk of the current item: the item's rows of KS pieces into a weight slot (completing
-// on wbar) and the pass's activation rows for those columns into an activation slot (completing
-// on bbar; lane t < ntok holds the row of slot t).
+// Step sk of the current item, in two parts: the item's rows of KS pieces into a weight slot
+// (completing on wbar), issued as soon as that slot's previous weights have been taken; and the
+// pass's activation rows for those columns into an activation slot (completing on bbar; lane
+// t < ntok holds the row of slot t), issued once that slot's previous step has finished.
 template <int KS>
-__device__ __forceinline__ void issue_step(const GemvArgs& a, const Item& it, const CopyPlan& c, int64_t prb,
-                                           int64_t lprb, int sk, uint32_t ntok, const uint8_t* brow, uint8_t* wslot,
-                                           uint64_t* wbar, uint8_t* bslot, uint64_t* bbar, int lane) {
-    using C = Cfg<KS>;
+__device__ __forceinline__ void issue_weights(const GemvArgs& a, const Item& it, const CopyPlan& c, int64_t prb,
+                                              int64_t lprb, int sk, uint8_t* wslot, uint64_t* wbar, int lane) {
     const int kp0 = sk * KS;
     const int nk = it.n_kp - kp0 < KS ? it.n_kp - kp0 : KS;
     const bool last_short = kp0 + nk == it.n_kp && lprb != prb;
     const uint32_t wbytes = (uint32_t)(it.rows * (prb * (nk - (last_short ? 1 : 0)) + (last_short ? lprb : 0)));
-    if (lane == 0) {
-        mbar_expect_tx(wbar, wbytes);
-        mbar_expect_tx(bbar, ntok * (uint32_t)nk * 1024);
-    }
+    if (lane == 0) mbar_expect_tx(wbar, wbytes);
     __syncwarp();
     if (c.cq >= 0 && c.cq < nk) {
         const int kp = kp0 + c.cq;
@@ -235,6 +231,16 @@ __device__ __forceinline__ void issue_step(const GemvArgs& a, const Item& it, co
         else
             bulk_g2s(dst + c.drow * prb, c.src + kp * c.pstride, (uint32_t)(c.nrows * prb), wbar);
     }
+}
+
+template <int KS>
+__device__ __forceinline__ void issue_acts(const GemvArgs& a, const Item& it, int sk, uint32_t ntok, const uint8_t* brow,
+                                           uint8_t* bslot, uint64_t* bbar, int lane) {
+    using C = Cfg<KS>;
+    const int kp0 = sk * KS;
+    const int nk = it.n_kp - kp0 < KS ? it.n_kp - kp0 : KS;
+    if (lane == 0) mbar_expect_tx(bbar, ntok * (uint32_t)nk * 1024);
+    __syncwarp();
     if ((uint32_t)lane < ntok)
         bulk_g2s(bslot + HDR_BYTES + lane * C::BROW, brow + (int64_t)kp0 * 1024, (uint32_t)nk * 1024, bbar);
 }
@@ -293,16 +299,16 @@ __device__ __forceinline__ void iq3s_pairs(const uint4& Qs, const uint2& S, uint
 }
 
 // Activation chunks of sub-step ss for this thread's token slot: hi columns 0-7 / 8-15 (and lo).
-__device__ __forceinline__ void load_b(const uint8_t* brow, int ss, bool has_tok, bool lo, uint32_t* hb,
-                                       uint32_t* lb) {
-    uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0, l0 = h0, l1 = h0;
-    if (has_tok) {
-        h0 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 0));
-        h1 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 2));
-        if (lo) {
-            l0 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 1));
-            l1 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 3));
-        }
+// Slots past the pass's tokens read whatever the slot holds: an MMA output column depends only on
+// its own activation column, and those columns are never stored, so no branch or zeroing is needed
+// (brow always points inside the activation slot).
+__device__ __forceinline__ void load_b(const uint8_t* brow, int ss, bool lo, uint32_t* hb, uint32_t* lb) {
+    const uint4 h0 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 0));
+    const uint4 h1 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 2));
+    uint4 l0 = make_uint4(0, 0, 0, 0), l1 = l0;
+    if (lo) {
+        l0 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 1));
+        l1 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 3));
     }
     hb[0] = h0.x; hb[1] = h0.y; hb[2] = h0.z; hb[3] = h0.w;
     hb[4] = h1.x; hb[5] = h1.y; hb[6] = h1.z; hb[7] = h1.w;
@@ -330,7 +336,7 @@ __device__ __forceinline__ void fast_step(const uint8_t* wsl, int mt, int g, int
             uint32_t pa[8], pb[8], hb[8], lb[8];
             iq2s_pairs(QA, HA, ss, tl, pa);
             iq2s_pairs(QB, HB, ss, tl, pb);
-            load_b(brow, ss, has_tok, lo, hb, lb);
+            load_b(brow, ss, lo, hb, lb);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
                 const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
@@ -354,7 +360,7 @@ __device__ __forceinline__ void fast_step(const uint8_t* wsl, int mt, int g, int
             uint32_t pa[8], pb[8], hb[8], lb[8];
             iq3s_pairs(QA, SA, qhA, scA, ss, tl, pa);
             iq3s_pairs(QB, SB, qhB, scB, ss, tl, pb);
-            load_b(brow, ss, has_tok, lo, hb, lb);
+            load_b(brow, ss, lo, hb, lb);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
                 const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
@@ -418,7 +424,7 @@ __device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl
             iq3s_pairs(in.QA, in.SA, in.HA & 0xFFFFu, in.HA >> 16, ss, tl, pa);
             iq3s_pairs(in.QB, in.SB, in.HB & 0xFFFFu, in.HB >> 16, ss, tl, pb);
         }
-        load_b(brow, ss, has_tok, false, hb, lb);
+        load_b(brow, ss, false, hb, lb);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
             const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
@@ -496,7 +502,7 @@ __device__ __forceinline__ void q4k_step(const uint8_t* wsl, int mt, int g, int 
         uint32_t pa[8], pb[8], hb[8], lb[8];
         q4_pairs(A, ss, pa);
         q4_pairs(Bq, ss, pb);
-        load_b(brow, ss, has_tok, lo, hb, lb);
+        load_b(brow, ss, lo, hb, lb);
         const uint32_t ma = h22u(ss < 2 ? A.m0 : A.m1), mb = h22u(ss < 2 ? Bq.m0 : Bq.m1);
         const uint32_t am[4] = {ma, mb, ma, mb};
 #pragma unroll
@@ -556,7 +562,7 @@ __device__ __forceinline__ void generic_step(const Layout& L, int kp, const uint
             }
         }
         uint32_t hb[8], lb[8];
-        load_b(brow, ss, has_tok, true, hb, lb);
+        load_b(brow, ss, true, hb, lb);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
             mma_16816(acc, af[kk], hb[2 * kk], hb[2 * kk + 1]);
@@ -661,9 +667,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
                     const uint8_t* brow = jb.b + (int64_t)arow * jb.bstride;
                     for (int sk = 0; sk < it.nsk; ++sk) {
                         if (s % NPW == pw) {
-                            if (q >= a.nst && (!mbar_wait(&empty_w[s], ph ^ 1u, a.err) ||
-                                               !mbar_wait(&empty_b[s], ph ^ 1u, a.err)))
-                                return;
+                            if (q >= a.nst && !mbar_wait(&empty_w[s], ph ^ 1u, a.err)) return;
+                            issue_weights<KS>(a, it, cp, prb, lprb, sk, wslots + s * a.wslot_bytes, &full_w[s], lane);
+                            if (q >= a.nst && !mbar_wait(&empty_b[s], ph ^ 1u, a.err)) return;
                             uint8_t* bslot = bslots + s * a.bslot_bytes;
                             StepHdr* h = reinterpret_cast<StepHdr*>(bslot);
                             if (lane == 0) {
@@ -679,8 +685,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
                             }
                             if ((uint32_t)lane < ntok) h->orow[lane] = orow;
                             __syncwarp();
-                            issue_step<KS>(a, it, cp, prb, lprb, sk, ntok, brow, wslots + s * a.wslot_bytes,
-                                           &full_w[s], bslot, &full_b[s], lane);
+                            issue_acts<KS>(a, it, sk, ntok, brow, bslot, &full_b[s], lane);
                         }
                         ++q;
                         if (++s == a.nst) {
@@ -738,8 +743,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
         const bool active = kp < h->n_kp && 16 * mt < rows;
         const bool lo = jb.split != 0;
         const uint8_t* wsl = wslots + s * a.wslot_bytes + ks * a.slot_bytes;
-        // this thread's activation row (slot g of the pass), its chunk of this K-slice
-        const uint8_t* brow = bslot + HDR_BYTES + g * C::BROW + ks * 1024 + 16 * c4;
+        // this thread's activation row (slot g of the pass; rows past the slot's capacity read row 0),
+        // its chunk of this K-slice
+        const uint8_t* brow = bslot + HDR_BYTES + (g < a.tokcap ? g : 0) * C::BROW + ks * 1024 + 16 * c4;
         const bool has_tok = (uint32_t)g < ntok;
         if (!mbar_wait(&full_w[s], ph, a.err)) return;
         if (FMT != 0 && L.fmt == FMT && !lo) {
