@@ -61,15 +61,29 @@ __global__ void __launch_bounds__(256) k_router(const float* __restrict__ x, con
     const float* xr = x + (int64_t)(tb ? t0 + r : 0) * H;
     double c[2] = {0.0, 0.0};
     int k = k0;
-    for (; k + 16 <= k1; k += 16) {  // four k4 steps with their loads issued together
-        float av[4], bv[4];
+    // chunks of four k4 steps; the next chunk's loads are in flight while this one multiplies
+    float av[4], bv[4];
+    if (k + 16 <= k1)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             av[j] = ea ? __ldg(wr + k + 4 * j + kq) : 0.f;
             bv[j] = tb ? __ldg(xr + k + 4 * j + kq) : 0.f;
         }
+    for (; k + 16 <= k1; k += 16) {
+        float an[4], bn[4];
+        const bool more = k + 32 <= k1;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            an[j] = more && ea ? __ldg(wr + k + 16 + 4 * j + kq) : 0.f;
+            bn[j] = more && tb ? __ldg(xr + k + 16 + 4 * j + kq) : 0.f;
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) dmma_8x8x4(c, (double)av[j], (double)bv[j]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            av[j] = an[j];
+            bv[j] = bn[j];
+        }
     }
     for (; k < k1; k += 4) {
         const bool in = k + kq < k1;
@@ -96,90 +110,134 @@ __global__ void __launch_bounds__(256) k_router(const float* __restrict__ x, con
     }
 }
 
-// One warp per token: softmax over E (<= 1024), k picks (<= 32) best first with ties to the
-// lowest id, weights renormalised over the picks when norm. Optionally the shared-expert gate
-// sigmoid(sum_keepdim(x * gate_inp)) in candle's AVX summation order.
-__global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits, int T, int E, int K, int norm, uint32_t* __restrict__ ids, float* __restrict__ wout,
+// One block (8 warps) per token: softmax over E (<= 1024, up to 4 experts per thread), K picks
+// (<= 16) best first with ties to the lowest id, weights renormalised over the picks when norm.
+// The softmax denominator keeps candle's AVX order: lane L of one warp sums elements 32i + L over
+// the whole 32-element steps in order, the lanes are reduced in the AVX tree, and a tail is added
+// element by element. Top-k: each warp selects the best K of its experts, warp 0 merges the 8
+// candidate lists. Optionally (warp 1, meanwhile) the shared-expert gate
+// sigmoid(sum_keepdim(x * gate_inp)) in the same AVX summation order.
+__global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits, int T, int E, int K, int norm,
+                                               uint32_t* __restrict__ ids, float* __restrict__ wout,
                                                const float* __restrict__ x, const float* __restrict__ g_inp,
                                                int H, float* __restrict__ sgate) {
-    int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= T) return;
-    const int NV = 32;  // up to 1024 experts
-    float v[NV];
-    int nv = (E + 31) / 32;
+    __shared__ float pv[1024];
+    __shared__ float wred[8];
+    __shared__ float s_sum;
+    __shared__ float cv[8][16];
+    __shared__ int ci[8][16];
+    const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float v[4];
     float mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        int e = 32 * i + lane;
-        if (i < nv && e < E) {
-            v[i] = logits[(int64_t)warp * E + e];
-            mx = fmaxf(mx, v[i]);
-        } else {
-            v[i] = -INFINITY;
-        }
+    for (int j = 0; j < 4; ++j) {
+        const int e = tid + 256 * j;
+        v[j] = e < E ? logits[(int64_t)t * E + e] : -INFINITY;
+        if (e < E) mx = fmaxf(mx, v[j]);
     }
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    int whole = E / 32;  // whole 32-element steps
-    float acc = 0.f;
+    if (lane == 0) wred[warp] = mx;
+    __syncthreads();
+    mx = wred[0];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        int e = 32 * i + lane;
-        if (i < nv && e < E) v[i] = exp_cr(__fsub_rn(v[i], mx));
-        if (i < whole) acc = __fadd_rn(acc, v[i]);
-    }
-    float s = avx_lane_tree(acc);
-    if (E % 32) {  // tail elements added one by one, in order
-        float tail = 0.f;
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, wred[w]);
 #pragma unroll
-        for (int i = 0; i < NV; ++i)
-            if (i == whole) tail = v[i];
-        for (int j = 0; j < E % 32; ++j) s = __fadd_rn(s, __shfl_sync(0xffffffffu, tail, j));
+    for (int j = 0; j < 4; ++j) {
+        const int e = tid + 256 * j;
+        if (e < E) {
+            v[j] = exp_cr(__fsub_rn(v[j], mx));
+            pv[e] = v[j];
+        }
     }
+    __syncthreads();
+    if (warp == 0) {
+        const int whole = E / 32;  // whole 32-element steps
+        float acc = 0.f;
+        for (int i = 0; i < whole; ++i) acc = __fadd_rn(acc, pv[32 * i + lane]);
+        float sum = avx_lane_tree(acc);
+        for (int j = whole * 32; j < E; ++j) sum = __fadd_rn(sum, pv[j]);  // tail in order
+        if (lane == 0) s_sum = sum;
+    }
+    __syncthreads();
+    const float ssum = s_sum;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        int e = 32 * i + lane;
-        v[i] = (i < nv && e < E) ? __fdiv_rn(v[i], s) : -1.0f;  // probabilities; -1 marks padding
+    for (int j = 0; j < 4; ++j) {
+        const int e = tid + 256 * j;
+        v[j] = e < E ? __fdiv_rn(v[j], ssum) : -1.0f;  // probabilities; -1 marks padding
     }
-    float pw[32];
-    uint32_t pid[32];
-    for (int j = 0; j < K; ++j) {
+    // this warp's best K of its experts (ascending id within a thread: the first wins ties)
+    for (int r = 0; r < K; ++r) {
         float bv = -2.0f;
         int bi = 0x7fffffff;
 #pragma unroll
-        for (int i = 0; i < NV; ++i) {
-            int e = 32 * i + lane;
-            if (i < nv && e < E && v[i] > bv) {  // ascending e within a lane: first wins ties
-                bv = v[i];
-                bi = e;
+        for (int j = 0; j < 4; ++j)
+            if (v[j] > bv) {
+                bv = v[j];
+                bi = tid + 256 * j;
             }
-        }
         for (int o = 16; o > 0; o >>= 1) {
-            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (ov > bv || (ov == bv && oi < bi)) {
                 bv = ov;
                 bi = oi;
             }
         }
-        if (bi >= E) bi = E - 1;  // only when every candidate is NaN: keep ids in range
-        pw[j] = bv;
-        pid[j] = (uint32_t)bi;
-#pragma unroll
-        for (int i = 0; i < NV; ++i)
-            if (32 * i + lane == bi) v[i] = -3.0f;  // taken
-    }
-    if (lane == 0) {
-        float tot = 0.f;
-        if (norm)
-            for (int j = 0; j < K; ++j) tot = __fadd_rn(tot, pw[j]);
-        for (int j = 0; j < K; ++j) {
-            ids[(int64_t)warp * K + j] = pid[j];
-            wout[(int64_t)warp * K + j] = norm ? __fdiv_rn(pw[j], tot) : pw[j];
+        if (lane == 0) {
+            cv[warp][r] = bv;
+            ci[warp][r] = bi;
         }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (tid + 256 * j == bi) v[j] = -3.0f;  // taken
     }
-    if (sgate) {
-        const float* xr = x + (int64_t)warp * H;
-        int wholeh = H / 32;
+    __syncthreads();
+    if (warp == 0) {
+        // merge: lane l holds candidates l, l + 32, ... of the 8 x K list
+        const int nc = 8 * K;
+        float mv[4];
+        int mi[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c = lane + 32 * j;
+            mv[j] = c < nc ? cv[c / K][c % K] : -2.0f;
+            mi[j] = c < nc ? ci[c / K][c % K] : 0x7fffffff;
+        }
+        float tot = 0.f;
+        for (int r = 0; r < K; ++r) {
+            float bv = -2.0f;
+            int bi = 0x7fffffff, bj = -1;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (mv[j] > bv || (mv[j] == bv && mi[j] < bi)) {
+                    bv = mv[j];
+                    bi = mi[j];
+                    bj = j;
+                }
+            int owner = lane;
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                const int oo = __shfl_xor_sync(0xffffffffu, owner, o);
+                if (ov > bv || (ov == bv && oi < bi)) {
+                    bv = ov;
+                    bi = oi;
+                    owner = oo;
+                }
+            }
+            if (owner == lane && bj >= 0) mv[bj] = -3.0f;  // taken
+            if (bi >= E) bi = E - 1;  // only when every candidate is NaN: keep ids in range
+            if (lane == 0) {
+                ids[(int64_t)t * K + r] = (uint32_t)bi;
+                wout[(int64_t)t * K + r] = bv;
+                if (norm) tot = __fadd_rn(tot, bv);
+            }
+        }
+        if (lane == 0 && norm)
+            for (int r = 0; r < K; ++r) wout[(int64_t)t * K + r] = __fdiv_rn(wout[(int64_t)t * K + r], tot);
+    } else if (warp == 1 && sgate) {
+        const float* xr = x + (int64_t)t * H;
+        const int wholeh = H / 32;
         float a = 0.f;
         // loads issued 16 at a time ahead of the in-order sum (the sum's order is fixed)
         for (int i0 = 0; i0 < wholeh; i0 += 16) {
@@ -193,7 +251,7 @@ __global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits,
         }
         float sum = avx_lane_tree(a);
         for (int j = wholeh * 32; j < H; ++j) sum = __fadd_rn(sum, __fmul_rn(xr[j], g_inp[j]));
-        if (lane == 0) sgate[warp] = __fdiv_rn(1.0f, __fadd_rn(exp_cr(-sum), 1.0f));
+        if (lane == 0) sgate[t] = __fdiv_rn(1.0f, __fadd_rn(exp_cr(-sum), 1.0f));
     }
 }
 
@@ -419,9 +477,7 @@ int launch_router(const float* x, const float* w, const float* b, int T, int H, 
 int launch_route(const float* logits, int T, int E, int K, int norm, uint32_t* ids, float* w, const float* x,
                  const float* g_inp, int H, float* sgate, cudaStream_t st) {
     if (T == 0) return CWX_OK;
-    int warps_per_block = 8;
-    k_route<<<(T + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, st>>>(logits, T, E, K, norm, ids,
-                                                                                          w, x, g_inp, H, sgate);
+    k_route<<<T, 256, 0, st>>>(logits, T, E, K, norm, ids, w, x, g_inp, H, sgate);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_route");
 }
