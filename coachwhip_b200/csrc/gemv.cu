@@ -31,6 +31,8 @@
 // ~22-bit products (its outputs are re-quantised downstream).
 // Other formats (and any job of another format in the same launch): exact f32 dequantisation
 // rounded to f16 (hi + lo pairs when the job asks for it), activations hi + lo.
+#include <cstddef>
+
 #include "cwx_common.cuh"
 #include "decode.cuh"
 #include "kernels.cuh"
@@ -46,6 +48,12 @@ constexpr int HDR_BYTES = 128;
 constexpr int MAX_TOKCAP = 8;
 constexpr int SMEM_LIMIT = 227 * 1024;
 constexpr int RING_BYTES = 4096;  // the producer's look-ahead ring (PRing)
+// Register split: the kernel launches with 96 registers per thread (640 threads fill the 64 K
+// register file of an SM); the producer warpgroup then drops to PROD_REGS and the four consumer
+// warpgroups rise to CONS_REGS, the decode's lookups and MMAs need more than 96 to overlap.
+// 4 warps x 32 x PROD_REGS + 16 warps x 32 x CONS_REGS = 640 x 96 exactly.
+constexpr int LAUNCH_REGS = 96, PROD_REGS = 40, CONS_REGS = 104;
+static_assert(NPW * PROD_REGS + NCW * CONS_REGS <= (NCW + NPW) * LAUNCH_REGS, "register split");
 
 template <int FMT>
 struct Tbl {  // replicated codebook bytes in shared memory
@@ -131,15 +139,27 @@ found:
 }
 
 // What consumers need to know about a step, written by the producer at the head of its stage.
-struct StepHdr {
-    int job;  // -1: no more steps
+// Everything the consumers of a fast-path step need is in it, so they read it with a few 16-byte
+// loads instead of indexing the launch's job table.
+struct __align__(16) StepHdr {
+    int job;    // -1: no more steps
+    int flags;  // HF_* below, and the job's format in bits 8..15
+    int kp0, n_kp;
+    int rows, ntok;
+    int feat0;  // first output feature of the tile
+    int n;      // the job's rows (bias stride)
+    float* out;
+    int ostride;
     uint32_t e;
-    int64_t rt;
-    int rows, n_kp, kp0, pass_start, pass_end;
-    uint32_t ntok;
+    const float* bias;
+    int pad[2];
     uint32_t orow[MAX_TOKCAP];  // output row of each slot of the pass (pick index, or token)
 };
 static_assert(sizeof(StepHdr) <= HDR_BYTES, "step header");
+static_assert(offsetof(StepHdr, rows) == 16 && offsetof(StepHdr, out) == 32 && offsetof(StepHdr, ostride) == 40 &&
+                  offsetof(StepHdr, e) == 44 && offsetof(StepHdr, bias) == 48 && offsetof(StepHdr, orow) == 64,
+              "step header words as the consumers read them");
+constexpr int HF_PASS_START = 1, HF_PASS_END = 2, HF_SPLIT = 4;
 
 __device__ __forceinline__ uint32_t pass_tokens(const Item& it, int pass, int tokcap) {
     const uint32_t done = (uint32_t)pass * (uint32_t)tokcap;
@@ -625,6 +645,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
     __syncthreads();
 
     if (warp >= NCW) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(PROD_REGS));
         // ---------------- producers: all four walk the same sequence of steps; producer warp pw
         // fills the slots s with s % NPW == pw, so every slot has one writer, which has issued the
         // slot's previous step itself (its empty barriers are never more than a phase behind), and
@@ -673,15 +694,15 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
                             uint8_t* bslot = bslots + s * a.bslot_bytes;
                             StepHdr* h = reinterpret_cast<StepHdr*>(bslot);
                             if (lane == 0) {
-                                h->job = it.job;
+                                const int flags = (sk == 0 ? HF_PASS_START : 0) | (sk == it.nsk - 1 ? HF_PASS_END : 0) |
+                                                  (jb.split ? HF_SPLIT : 0) | (jb.m.L.fmt << 8);
+                                uint4* hv = reinterpret_cast<uint4*>(h);
+                                hv[0] = make_uint4((uint32_t)it.job, (uint32_t)flags, (uint32_t)(sk * KS), (uint32_t)it.n_kp);
+                                hv[1] = make_uint4((uint32_t)it.rows, ntok, (uint32_t)(it.rt * jb.rows), (uint32_t)jb.m.L.n);
+                                h->out = jb.out;
+                                h->ostride = (int)jb.ostride;
                                 h->e = it.e;
-                                h->rt = it.rt;
-                                h->rows = it.rows;
-                                h->n_kp = it.n_kp;
-                                h->kp0 = sk * KS;
-                                h->pass_start = sk == 0;
-                                h->pass_end = sk == it.nsk - 1;
-                                h->ntok = ntok;
+                                h->bias = jb.bias;
                             }
                             if ((uint32_t)lane < ntok) h->orow[lane] = orow;
                             __syncwarp();
@@ -709,6 +730,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
     }
 
     // ---------------- consumers
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(CONS_REGS));
     if (FMT != 0) {
         build_tables<FMT>(tbl, tid);
         asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
@@ -723,32 +745,31 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
         if (!mbar_wait(&full_b[s], ph, a.err)) return;
         const uint8_t* bslot = bslots + s * a.bslot_bytes;
         const StepHdr* h = reinterpret_cast<const StepHdr*>(bslot);
-        const int jobi = h->job;
+        const uint4 h0 = reinterpret_cast<const uint4*>(h)[0], h1 = reinterpret_cast<const uint4*>(h)[1];
+        const int jobi = (int)h0.x;
         if (jobi < 0) return;
-        const GemvJob& jb = a.job[jobi];
-        const Layout& L = jb.m.L;
-        // the header into registers
-        const uint32_t ntok = h->ntok;
-        const bool pass_start = h->pass_start, pass_end = h->pass_end;
-        const uint32_t e = h->e;
-        const int64_t rt = h->rt;
-        const int rows = h->rows;
-        const int kp = h->kp0 + ks;
-        uint32_t orow0 = 0, orow1 = 0;
-        if (pass_end) {
-            orow0 = h->orow[2 * c4];
-            orow1 = h->orow[2 * c4 + 1];
-        }
+        const int flags = (int)h0.y, fmt = (flags >> 8) & 0xFF;
+        const bool pass_start = flags & HF_PASS_START, pass_end = flags & HF_PASS_END, lo = flags & HF_SPLIT;
+        const int kp = (int)h0.z + ks, n_kp = (int)h0.w;
+        const int rows = (int)h1.x;
+        const uint32_t ntok = h1.y;
         if (pass_start) acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-        const bool active = kp < h->n_kp && 16 * mt < rows;
-        const bool lo = jb.split != 0;
+        const bool active = kp < n_kp && 16 * mt < rows;
+        // what the pass's epilogue needs, taken out of the slot before the slot is handed back
+        uint4 h2 = make_uint4(0, 0, 0, 0), h3 = h2;
+        uint2 orw = make_uint2(0, 0);
+        if (pass_end) {
+            h2 = reinterpret_cast<const uint4*>(h)[2];
+            h3 = reinterpret_cast<const uint4*>(h)[3];
+            orw = *reinterpret_cast<const uint2*>(&h->orow[2 * c4]);
+        }
         const uint8_t* wsl = wslots + s * a.wslot_bytes + ks * a.slot_bytes;
         // this thread's activation row (slot g of the pass; rows past the slot's capacity read row 0),
         // its chunk of this K-slice
         const uint8_t* brow = bslot + HDR_BYTES + (g < a.tokcap ? g : 0) * C::BROW + ks * 1024 + 16 * c4;
         const bool has_tok = (uint32_t)g < ntok;
         if (!mbar_wait(&full_w[s], ph, a.err)) return;
-        if (FMT != 0 && L.fmt == FMT && !lo) {
+        if (FMT != 0 && fmt == FMT && !lo) {
             FastIn in;
             if (active) fast_load<FMT>(wsl, mt, g, c4, in);
             __syncwarp();
@@ -756,6 +777,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
             if (active) fast_compute<FMT>(in, tl, brow, has_tok, acc);
         } else {
             if (active) {
+                const Layout& L = a.job[jobi].m.L;
                 if (FMT != 0 && L.fmt == FMT) fast_step<FMT>(wsl, mt, g, c4, tl, brow, has_tok, true, acc);
                 else if (L.fmt == F_Q4_K && L.kp_row_bytes == 144) q4k_step(wsl, mt, g, c4, brow, has_tok, lo, acc);
                 else generic_step(L, kp, wsl, mt, g, c4, brow, has_tok, lo, acc);
@@ -786,15 +808,21 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
             asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
         }
         if (pass_end && ks == 0 && 16 * mt < rows) {
+            // header words 2 and 3: out, ostride, e; bias
+            float* out = reinterpret_cast<float*>(((uint64_t)h2.y << 32) | h2.x);
+            const int64_t ostride = (int)h2.z;
+            const uint32_t e = h2.w;
+            const float* bias = reinterpret_cast<const float*>(((uint64_t)h3.y << 32) | h3.x);
+            const int feat0 = (int)h1.z, n = (int)h1.w;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const uint32_t slot = 2 * c4 + (i & 1);
                 if (slot < ntok) {
-                    const int64_t feat = rt * jb.rows + 16 * mt + g + ((i >> 1) ? 8 : 0);
-                    const int64_t orow = (i & 1) ? orow1 : orow0;
+                    const int64_t feat = feat0 + 16 * mt + g + ((i >> 1) ? 8 : 0);
+                    const int64_t orow = (i & 1) ? orw.y : orw.x;
                     float v = acc[i];
-                    if (jb.bias) v = __fadd_rn(v, jb.bias[(int64_t)e * L.n + feat]);
-                    jb.out[orow * jb.ostride + feat] = v;
+                    if (bias) v = __fadd_rn(v, bias[(int64_t)e * n + feat]);
+                    out[orow * ostride + feat] = v;
                 }
             }
         }
@@ -834,6 +862,21 @@ static int launch_fk(GemvArgs a, int64_t experts_est, int device, int sm_count, 
     if (nst < 2) return fail(CWX_EUNSUPPORTED, "expert pieces too large for shared memory");
     a.nst = nst;
     const int smem = fixed + nst * (a.wslot_bytes + a.bslot_bytes);
+    // the register split above assumes the launch allocates LAUNCH_REGS per thread (allocation is
+    // in steps of 8): a kernel compiled with fewer would make the consumers' increase wait forever
+    static int regs_ok[3][4] = {{0}};
+    {
+        const int fi = FMT == 0 ? 0 : FMT == F_IQ2_S ? 1 : 2, ki = KS == 1 ? 0 : KS == 2 ? 1 : KS == 4 ? 2 : 3;
+        if (!regs_ok[fi][ki]) {
+            cudaFuncAttributes fa;
+            cudaError_t e = cudaFuncGetAttributes(&fa, k_gemv<FMT, KS>);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes(k_gemv)");
+            if ((fa.numRegs + 7) / 8 * 8 != LAUNCH_REGS)
+                return fail(CWX_EUNSUPPORTED, "k_gemv compiled with %d registers, the register split needs %d",
+                            fa.numRegs, LAUNCH_REGS);
+            regs_ok[fi][ki] = 1;
+        }
+    }
     static int attr_set[64][3][4] = {{{0}}};
     const int fidx = FMT == 0 ? 0 : FMT == F_IQ2_S ? 1 : 2;
     const int kidx = KS == 1 ? 0 : KS == 2 ? 1 : KS == 4 ? 2 : 3;
