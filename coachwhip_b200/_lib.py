@@ -20,6 +20,7 @@ EXPORTS = [
     "cwx_bank_create", "cwx_bank_synth", "cwx_bank_destroy", "cwx_bank_desc", "cwx_bank_download",
     "cwx_bank_dequantize", "cwx_synth_normal", "cwx_route", "cwx_permute", "cwx_permute_noalloc", "cwx_expert_matmul", "cwx_moe_forward",
     "cwx_ctx_set_profiling", "cwx_ctx_read_profile", "cwx_ctx_reset_profile", "cwx_ctx_launches",
+    "cwx_ctx_set_mma_min_pile",
 ]
 PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine"]
 
@@ -95,6 +96,7 @@ def lib() -> ctypes.CDLL:
             "cwx_ctx_read_profile": (I32, [P, P, P]),
             "cwx_ctx_reset_profile": (I32, [P]),
             "cwx_ctx_launches": (I64, [P]),
+            "cwx_ctx_set_mma_min_pile": (I32, [P, I32]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -126,6 +128,11 @@ def ctx(device: int) -> ctypes.c_void_p:
 def status(device: int, stream: int | None = None) -> None:
     """Synchronise and raise if a kernel recorded a device-side error."""
     check(lib().cwx_ctx_status(ctx(device), stream))
+
+
+def set_mma_min_pile(device: int, min_pile: int) -> None:
+    """Average picks per expert from which IQ layers use the tensor-core products (0: never)."""
+    check(lib().cwx_ctx_set_mma_min_pile(ctx(device), min_pile))
 
 
 def read_profile(device: int) -> tuple[list[float], list[int]]:

@@ -8,9 +8,13 @@
 //   combine          cw_weighted_sum fuse_kernel.rs:277-291 (pick order) + shared expert
 //                    crates/engine/src/model_next.rs:731-741 + residual model_next.rs:1437
 //
-// Packed activation rows: per 256-column piece, 64 chunks of 8 f16 values; chunk
-// ((ss*2 + q)*2 + h)*4 + c holds columns 64c + 16ss + 8q + 0..7, hi part (h = 0) or lo part
-// (h = 1). This is the order in which the grouped products' threads read them (gemv.cu).
+// Packed activation rows: per 256-column piece, 1024 bytes: first the 32 hi chunks, then the 32 lo
+// chunks, each chunk 8 f16 values; chunk (ss*2 + q)*4 + c of a half holds columns
+// 64c + 16ss + 8q + 0..7. This is the order in which the grouped products' threads read them
+// (gemv.cu), and a product that needs only the hi parts copies the first 528 bytes of a piece.
+// Q8_K rows (one Q8_K block per piece) hold the block's codes as exact f16 integers in the hi
+// chunks and the block scale d as an f32 at byte 512 (the rest of the lo half is zero): the
+// products sum code x weight per piece and scale the sum by d once.
 #include "cwx_common.cuh"
 #include "kernels.cuh"
 
@@ -81,19 +85,31 @@ __global__ void __launch_bounds__(256) k_prep(PrepPair pp) {
                 mv = ov;
             }
         }
+        float d = 0.f;
         if (am == 0.f) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) v[j] = 0.f;
         } else {
             const float iscale = __fdiv_rn(-127.f, mv);
-            const float d = __fdiv_rn(1.0f, iscale);
+            d = __fdiv_rn(1.0f, iscale);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 float qv = roundf(__fmul_rn(iscale, v[j]));
-                qv = fminf(fmaxf(qv, -128.f), 127.f);
-                v[j] = __fmul_rn(d, qv);
+                v[j] = fminf(fmaxf(qv, -128.f), 127.f);
             }
         }
+        uint32_t hi[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+            hi[j] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        const int c = k0 >> 6, ss = (k0 >> 4) & 3, q = (k0 >> 3) & 1;
+        uint8_t* piece = p.out + r * packed_row_bytes(p.K) + b * 1024;
+        const int ch = (ss * 2 + q) * 4 + c;
+        *reinterpret_cast<uint4*>(piece + 16 * ch) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(piece + 512 + 16 * ch) = make_uint4(ch == 0 ? __float_as_uint(d) : 0u, 0u, 0u, 0u);
+        return;
     } else if (p.mode == AM_Q8_0) {
         // 32-column blocks: lanes 4i..4i+3 hold block i
         float am = 0.f;
@@ -122,8 +138,8 @@ __global__ void __launch_bounds__(256) k_prep(PrepPair pp) {
     }
     const int c = k0 >> 6, ss = (k0 >> 4) & 3, q = (k0 >> 3) & 1;
     uint8_t* piece = p.out + r * packed_row_bytes(p.K) + b * 1024;
-    *reinterpret_cast<uint4*>(piece + 16 * (((ss * 2 + q) * 2 + 0) * 4 + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4*>(piece + 16 * (((ss * 2 + q) * 2 + 1) * 4 + c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(piece + 16 * ((ss * 2 + q) * 4 + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(piece + 512 + 16 * ((ss * 2 + q) * 4 + c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
 // out[t] = sum_j w[t][j] * rows[t*K + j] (pick order, from 0) + sgate[t] * shared[t] + residual[t]

@@ -131,8 +131,24 @@ struct LayerPlan {
     uint8_t *hpk, *hspk;     // packed hidden rows (routed, shared)
     float* y;
     float* ys;
+    int mma;           // routed products on the tensor cores (IQ banks, large piles)
+    __half* x16;       // (T, H) f16 rows of x
+    __half* h16;       // (n, I) f16 hidden rows per pick
     size_t bytes;
 };
+
+// Whether a layer's routed products run on the tensor cores: IQ2_S / IQ3_S banks (f32 activations
+// under every policy), SiLU, whole 256-column pieces, and piles large enough on average.
+static bool mma_layer(const cwx_ctx* c, const cwx_moe_layer* L, int T) {
+    if (!c || c->mma_min_pile <= 0 || L->act != CWX_ACT_SILU) return false;
+    const int64_t pile = ((int64_t)T * L->top_k + L->n_experts - 1) / L->n_experts;
+    if (pile < c->mma_min_pile) return false;
+    const cwx_bank* bs[3] = {L->gate, L->up, L->down};
+    for (const cwx_bank* b : bs)
+        if (b->L.fmt != F_IQ2_S && b->L.fmt != F_IQ3_S) return false;
+    if (L->gate->L.fmt != L->up->L.fmt) return false;
+    return L->hidden % 256 == 0 && L->inter % 256 == 0;
+}
 
 static int validate_layer(const cwx_moe_layer* L) {
     if (!L) return fail(CWX_EINVAL, "cwx_moe_forward: null layer");
@@ -163,7 +179,7 @@ static int validate_layer(const cwx_moe_layer* L) {
     return CWX_OK;
 }
 
-static void plan_layer(const cwx_moe_layer* L, int T, uint8_t* base, LayerPlan* p) {
+static void plan_layer(const cwx_moe_layer* L, int T, int mma, uint8_t* base, LayerPlan* p) {
     p->H = L->hidden;
     p->E = L->n_experts;
     p->K = L->top_k;
@@ -186,26 +202,31 @@ static void plan_layer(const cwx_moe_layer* L, int T, uint8_t* base, LayerPlan* 
     p->n_used = c.take<uint32_t>(4);
     p->perm = c.take<uint32_t>(perm_scratch_bytes(n, p->E) / 4);
     for (int m = 0; m < 3; ++m) {
-        const bool need = (m == p->mgu) || (m == p->msgu);
+        const bool need = (m == p->mgu && !mma) || (m == p->msgu);
         p->xpk[m] = need ? c.take<uint8_t>((size_t)(T * packed_row_bytes(p->H))) : nullptr;
     }
-    p->g = c.take<float>((size_t)n * p->I);
-    p->u = c.take<float>((size_t)n * p->I);
+    const size_t nr = mma ? 0 : (size_t)n;  // the tensor-core products write h directly
+    p->g = c.take<float>(nr * p->I);
+    p->u = c.take<float>(nr * p->I);
     p->gs = c.take<float>((size_t)T * p->Is);
     p->us = c.take<float>((size_t)T * p->Is);
-    p->hpk = c.take<uint8_t>((size_t)(n * packed_row_bytes(p->I)));
+    p->hpk = c.take<uint8_t>((size_t)(nr * packed_row_bytes(p->I)));
     p->hspk = c.take<uint8_t>((size_t)(T * packed_row_bytes(p->Is)));
     p->y = c.take<float>((size_t)n * p->H);
     p->ys = c.take<float>((size_t)T * p->H);
+    p->mma = mma;
+    p->x16 = mma ? c.take<__half>((size_t)T * p->H) : nullptr;
+    p->h16 = mma ? c.take<__half>((size_t)n * p->I) : nullptr;
     p->bytes = c.off + 256;
 }
 
 static MatRef mref(const cwx_bank* b) { return MatRef{b ? b->d : nullptr, b ? b->L : Layout{}}; }
 
-static GemvJob job(const cwx_bank* b, int shared, const uint8_t* act, int64_t k, int bdiv, float* out, int64_t ostride,
-                   int split, const float* bias) {
+static GemvJob job(const cwx_bank* b, int shared, const uint8_t* act, int mode, int64_t k, int bdiv, float* out,
+                   int64_t ostride, int split, const float* bias) {
     GemvJob j;
     j.m = mref(b);
+    j.qint = mode == AM_Q8_K;
     j.shared = shared;
     j.b = act;
     j.bstride = packed_row_bytes(k);
@@ -247,6 +268,7 @@ extern "C" int cwx_ctx_create(int device, cwx_ctx** out) {
     cwx_ctx* c = new cwx_ctx();
     memset(c, 0, sizeof *c);
     c->device = device;
+    c->mma_min_pile = 32;
     c->prof = new ProfLog();
     cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
     cudaError_t e = cudaMalloc(&c->d_err, 16);
@@ -283,6 +305,13 @@ extern "C" int cwx_ctx_destroy(cwx_ctx* c) {
     cwx_ctx_reset_profile(c);
     delete static_cast<ProfLog*>(c->prof);
     delete c;
+    return CWX_OK;
+}
+
+extern "C" int cwx_ctx_set_mma_min_pile(cwx_ctx* c, int min_pile) {
+    if (!c) return fail(CWX_EINVAL, "cwx_ctx_set_mma_min_pile: null context");
+    if (min_pile < 0) return fail(CWX_EINVAL, "cwx_ctx_set_mma_min_pile: %d is negative", min_pile);
+    c->mma_min_pile = min_pile;
     return CWX_OK;
 }
 
@@ -326,9 +355,11 @@ extern "C" int cwx_ctx_reserve(cwx_ctx* c, const void* layer, int32_t tokens) {
     int rc = validate_layer(L);
     if (rc) return rc;
     CWX_CUDA(cudaSetDevice(c->device));
-    LayerPlan p;
-    plan_layer(L, tokens, nullptr, &p);
-    return ensure_ws(c, p.bytes, 0);
+    // the larger of the two plans (tensor-core products or not), so any batch up to `tokens` fits
+    LayerPlan p, q;
+    plan_layer(L, tokens, 0, nullptr, &p);
+    plan_layer(L, tokens, mma_layer(c, L, tokens) ? 1 : 0, nullptr, &q);
+    return ensure_ws(c, p.bytes > q.bytes ? p.bytes : q.bytes, 0);
 }
 
 extern "C" int cwx_route(cwx_ctx* c, const float* logits, int32_t T, int32_t E, int32_t K, int32_t norm, uint32_t* ids,
@@ -400,52 +431,25 @@ extern "C" int cwx_expert_matmul(cwx_ctx* c, const cwx_bank* bank, const float* 
     GemvArgs a;
     memset(&a, 0, sizeof a);
     a.njobs = 1;
-    a.job[0] = job(bank, 0, xpk, K, rows_per_expert ? 1 : nei0, out, bank->L.n, 0, nullptr);
+    a.job[0] = job(bank, 0, xpk, mode, K, rows_per_expert ? 1 : nei0, out, bank->L.n, 0, nullptr);
     a.pairs = pairs;
     a.used3 = used3;
     a.n_used = n_used;
     a.tok_est = tokens;
+    a.pile_est = (int)((n + E - 1) / E);
     a.err = c->d_err;
     c->launches += perm_launches(n, E) + 2;
     return launch_gemv(a, n < E ? n : E, c->device, c->sm_count, st);
 }
 
-extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, void* stream) {
-    if (!c || !A) return fail(CWX_EINVAL, "cwx_moe_forward: null argument");
-    int rc = validate_layer(L);
-    if (rc) return rc;
-    const int T = A->tokens;
-    if (T < 0) return fail(CWX_EINVAL, "cwx_moe_forward: tokens %d", T);
-    if (T == 0) return CWX_OK;
-    if (!A->x || !A->out) return fail(CWX_EINVAL, "cwx_moe_forward: null x or out");
-    CWX_CUDA(cudaSetDevice(c->device));
-    cudaStream_t st = (cudaStream_t)stream;
-    LayerPlan p;
-    plan_layer(L, T, nullptr, &p);
-    if ((rc = ensure_ws(c, p.bytes, st))) return rc;
-    plan_layer(L, T, c->ws, &p);
-    const int H = p.H, E = p.E, K = p.K, I = p.I, Is = p.Is;
+// Gate/up, activation and down products on the grouped mma.sync products (every format, any
+// batch; the shared expert in the same launches).
+static int moe_gemv(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, const LayerPlan& p, cudaStream_t st) {
+    const int T = p.T, H = p.H, E = p.E, K = p.K, I = p.I, Is = p.Is;
     const int64_t n = (int64_t)T * K;
     const bool shared = L->sh_gate != nullptr;
-
-    {
-        PhaseTimer t(c, st, CWX_PHASE_ROUTER);
-        if ((rc = launch_router(A->x, L->router_w, L->router_b, T, H, E, p.logits, st))) return rc;
-        t.end();
-    }
-    {
-        PhaseTimer t(c, st, CWX_PHASE_ROUTE);
-        if ((rc = launch_route(p.logits, T, E, K, L->norm_topk_prob, p.ids, p.w, A->x,
-                               shared ? L->sh_gate_inp : nullptr, H, shared ? p.sgate : nullptr, st)))
-            return rc;
-        t.end();
-    }
-    {
-        PhaseTimer t(c, st, CWX_PHASE_PILES);
-        if ((rc = launch_permute(p.ids, n, E, p.pairs, p.heads, p.used3, p.n_used, p.perm, c->d_err, st))) return rc;
-        t.end();
-    }
-    c->launches += 2 + perm_launches(n, E);
+    int rc;
+    const int64_t used_max = n < E ? n : E;
     {
         PhaseTimer t(c, st, CWX_PHASE_PREP);
         PrepArgs px[2];
@@ -456,7 +460,6 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
         c->launches += 1;
         t.end();
     }
-    const int64_t used_max = n < E ? n : E;
     // gate and up: routed piles and the shared expert, four matrix jobs in one launch. A product
     // whose result is re-quantised downstream (the down matrix takes Q8 activations) carries its
     // weights to ~22 bits, so the hidden state matches the CPU path closely enough that its Q8
@@ -465,17 +468,18 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
         GemvArgs a;
         memset(&a, 0, sizeof a);
         const int split_r = p.md != AM_F32, split_s = shared && p.msd != AM_F32;
-        a.job[a.njobs++] = job(L->gate, 0, p.xpk[p.mgu], H, K, p.g, I, split_r, nullptr);
-        a.job[a.njobs++] = job(L->up, 0, p.xpk[p.mgu], H, K, p.u, I, split_r, nullptr);
+        a.job[a.njobs++] = job(L->gate, 0, p.xpk[p.mgu], p.mgu, H, K, p.g, I, split_r, nullptr);
+        a.job[a.njobs++] = job(L->up, 0, p.xpk[p.mgu], p.mgu, H, K, p.u, I, split_r, nullptr);
         if (shared) {
-            a.job[a.njobs++] = job(L->sh_gate, 1, p.xpk[p.msgu], H, 1, p.gs, Is, split_s, nullptr);
-            a.job[a.njobs++] = job(L->sh_up, 1, p.xpk[p.msgu], H, 1, p.us, Is, split_s, nullptr);
+            a.job[a.njobs++] = job(L->sh_gate, 1, p.xpk[p.msgu], p.msgu, H, 1, p.gs, Is, split_s, nullptr);
+            a.job[a.njobs++] = job(L->sh_up, 1, p.xpk[p.msgu], p.msgu, H, 1, p.us, Is, split_s, nullptr);
         }
         a.pairs = p.pairs;
         a.used3 = p.used3;
         a.n_used = p.n_used;
         a.s_count = T;
         a.tok_est = T;
+        a.pile_est = (int)((n + E - 1) / E);
         a.err = c->d_err;
         PhaseTimer t(c, st, CWX_PHASE_GATE_UP);
         if ((rc = launch_gemv(a, used_max, c->device, c->sm_count, st))) return rc;
@@ -498,18 +502,156 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
     {
         GemvArgs d;
         memset(&d, 0, sizeof d);
-        d.job[d.njobs++] = job(L->down, 0, p.hpk, I, 1, p.y, H, 0,
+        d.job[d.njobs++] = job(L->down, 0, p.hpk, p.md, I, 1, p.y, H, 0,
                                L->act == CWX_ACT_CLAMPED_SWIGLU ? L->down_b : nullptr);
-        if (shared) d.job[d.njobs++] = job(L->sh_down, 1, p.hspk, Is, 1, p.ys, H, 0, nullptr);
+        if (shared) d.job[d.njobs++] = job(L->sh_down, 1, p.hspk, p.msd, Is, 1, p.ys, H, 0, nullptr);
         d.pairs = p.pairs;
         d.used3 = p.used3;
         d.n_used = p.n_used;
         d.s_count = T;
         d.tok_est = T;
+        d.pile_est = (int)((n + E - 1) / E);
         d.err = c->d_err;
         PhaseTimer t(c, st, CWX_PHASE_DOWN);
         if ((rc = launch_gemv(d, used_max, c->device, c->sm_count, st))) return rc;
         t.end();
+    }
+    c->launches += 1;
+    return CWX_OK;
+}
+
+// The shared expert's products alone (the routed ones run on the tensor cores).
+static int shared_gemv(cwx_ctx* c, const cwx_moe_layer* L, const LayerPlan& p, int down, cudaStream_t st) {
+    const int T = p.T, H = p.H, Is = p.Is;
+    GemvArgs a;
+    memset(&a, 0, sizeof a);
+    const int split_s = p.msd != AM_F32;
+    if (!down) {
+        a.job[a.njobs++] = job(L->sh_gate, 1, p.xpk[p.msgu], p.msgu, H, 1, p.gs, Is, split_s, nullptr);
+        a.job[a.njobs++] = job(L->sh_up, 1, p.xpk[p.msgu], p.msgu, H, 1, p.us, Is, split_s, nullptr);
+    } else {
+        a.job[a.njobs++] = job(L->sh_down, 1, p.hspk, p.msd, Is, 1, p.ys, H, 0, nullptr);
+    }
+    a.pairs = p.pairs;
+    a.used3 = p.used3;
+    a.n_used = p.n_used;
+    a.s_count = T;
+    a.tok_est = T;
+    a.pile_est = T;
+    a.err = c->d_err;
+    return launch_gemv(a, 0, c->device, c->sm_count, st);
+}
+
+// Routed products on the tensor cores (mma.cu): x as f16 rows; fused gate/up writing h = silu(g)
+// * u as f16 rows per pick; down from those rows. The shared expert stays on the mma.sync
+// products, one launch per stage.
+static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, const LayerPlan& p, cudaStream_t st) {
+    const int T = p.T, H = p.H, K = p.K, I = p.I, Is = p.Is;
+    const bool shared = L->sh_gate != nullptr;
+    int rc;
+    {
+        PhaseTimer t(c, st, CWX_PHASE_PREP);
+        if ((rc = launch_f16rows(A->x, (int64_t)T * H, p.x16, st))) return rc;
+        c->launches += 1;
+        if (shared) {
+            if ((rc = launch_prep(prep(A->x, nullptr, T, H, p.msgu, p.xpk[p.msgu]), st))) return rc;
+            c->launches += 1;
+        }
+        t.end();
+    }
+    MmaArgs m;
+    memset(&m, 0, sizeof m);
+    m.pairs = p.pairs;
+    m.used3 = p.used3;
+    m.n_used = p.n_used;
+    m.err = c->d_err;
+    {
+        PhaseTimer t(c, st, CWX_PHASE_GATE_UP);
+        MmaArgs g = m;
+        g.a0 = mref(L->gate);
+        g.a1 = mref(L->up);
+        g.fused = 1;
+        g.b = reinterpret_cast<const uint8_t*>(p.x16);
+        g.bstride = (int64_t)H * 2;
+        g.bdiv = K;
+        g.hout = p.h16;
+        g.ostride = I;
+        if ((rc = launch_mma(g, c->device, c->sm_count, st))) return rc;
+        c->launches += 1;
+        if (shared) {
+            if ((rc = shared_gemv(c, L, p, 0, st))) return rc;
+            c->launches += 1;
+        }
+        t.end();
+    }
+    if (shared) {
+        PhaseTimer t(c, st, CWX_PHASE_PREP);
+        if ((rc = launch_prep(prep(p.gs, p.us, T, Is, p.msd, p.hspk), st))) return rc;
+        c->launches += 1;
+        t.end();
+    }
+    {
+        PhaseTimer t(c, st, CWX_PHASE_DOWN);
+        MmaArgs d = m;
+        d.a0 = mref(L->down);
+        d.fused = 0;
+        d.b = reinterpret_cast<const uint8_t*>(p.h16);
+        d.bstride = (int64_t)I * 2;
+        d.bdiv = 1;
+        d.out = p.y;
+        d.ostride = H;
+        if ((rc = launch_mma(d, c->device, c->sm_count, st))) return rc;
+        c->launches += 1;
+        if (shared) {
+            if ((rc = shared_gemv(c, L, p, 1, st))) return rc;
+            c->launches += 1;
+        }
+        t.end();
+    }
+    return CWX_OK;
+}
+
+extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, void* stream) {
+    if (!c || !A) return fail(CWX_EINVAL, "cwx_moe_forward: null argument");
+    int rc = validate_layer(L);
+    if (rc) return rc;
+    const int T = A->tokens;
+    if (T < 0) return fail(CWX_EINVAL, "cwx_moe_forward: tokens %d", T);
+    if (T == 0) return CWX_OK;
+    if (!A->x || !A->out) return fail(CWX_EINVAL, "cwx_moe_forward: null x or out");
+    CWX_CUDA(cudaSetDevice(c->device));
+    cudaStream_t st = (cudaStream_t)stream;
+    LayerPlan p;
+    const int mma = mma_layer(c, L, T) ? 1 : 0;
+    plan_layer(L, T, mma, nullptr, &p);
+    if ((rc = ensure_ws(c, p.bytes, st))) return rc;
+    plan_layer(L, T, mma, c->ws, &p);
+    const int H = p.H, E = p.E, K = p.K, I = p.I, Is = p.Is;
+    const int64_t n = (int64_t)T * K;
+    const bool shared = L->sh_gate != nullptr;
+
+    {
+        PhaseTimer t(c, st, CWX_PHASE_ROUTER);
+        if ((rc = launch_router(A->x, L->router_w, L->router_b, T, H, E, p.logits, st))) return rc;
+        t.end();
+    }
+    {
+        PhaseTimer t(c, st, CWX_PHASE_ROUTE);
+        if ((rc = launch_route(p.logits, T, E, K, L->norm_topk_prob, p.ids, p.w, A->x,
+                               shared ? L->sh_gate_inp : nullptr, H, shared ? p.sgate : nullptr, st)))
+            return rc;
+        t.end();
+    }
+    {
+        PhaseTimer t(c, st, CWX_PHASE_PILES);
+        if ((rc = launch_permute(p.ids, n, E, p.pairs, p.heads, p.used3, p.n_used, p.perm, c->d_err, st))) return rc;
+        t.end();
+    }
+    c->launches += 2 + perm_launches(n, E);
+    if (p.mma) {
+        if ((rc = moe_mma(c, L, A, p, st))) return rc;
+    } else {
+        if ((rc = moe_gemv(c, L, A, p, st))) return rc;
     }
     {
         PhaseTimer t(c, st, CWX_PHASE_COMBINE);
@@ -517,7 +659,7 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
             return rc;
         t.end();
     }
-    c->launches += 2;
+    c->launches += 1;
 
     if (A->ids_out) CWX_CUDA(cudaMemcpyAsync(A->ids_out, p.ids, n * 4, cudaMemcpyDeviceToDevice, st));
     if (A->weights_out) CWX_CUDA(cudaMemcpyAsync(A->weights_out, p.w, n * 4, cudaMemcpyDeviceToDevice, st));

@@ -180,6 +180,7 @@ struct cwx_ctx {
     int profiling;     // record per-phase events (cwx_ctx_set_profiling)
     void* prof;        // recorded (phase, start, end) events
     int64_t launches;  // kernel launches issued through this context
+    int mma_min_pile;  // average picks per expert from which IQ layers take the tensor-core products (0: never)
 };
 
 namespace cwx {

@@ -44,15 +44,16 @@ constexpr int NPW = 4;                             // producer warps (one per SM
 constexpr int GEMV_THREADS = (NCW + NPW) * 32;
 constexpr int RED_FLOATS = 14 * 128;         // (KS - 1) * MT fragments of 128 floats, KS * MT = 16, KS <= 8
 constexpr int BAR_BYTES = 256;
-constexpr int HDR_BYTES = 128;
-constexpr int MAX_TOKCAP = 8;
+constexpr int HDR_BYTES = 256;
+constexpr int MAX_TOKCAP = 32;  // picks per pass: 8 per n-tile of the MMA, up to 4 n-tiles
+constexpr int RING_TOK = 8;      // first-pass rows kept in the producer ring (passes of up to 8 picks)
 constexpr int SMEM_LIMIT = 227 * 1024;
 constexpr int RING_BYTES = 4096;  // the producer's look-ahead ring (PRing)
 // Register split: the kernel launches with 96 registers per thread (640 threads fill the 64 K
 // register file of an SM); the producer warpgroup then drops to PROD_REGS and the four consumer
 // warpgroups rise to CONS_REGS, the decode's lookups and MMAs need more than 96 to overlap.
 // 4 warps x 32 x PROD_REGS + 16 warps x 32 x CONS_REGS = 640 x 96 exactly.
-constexpr int LAUNCH_REGS = 96, PROD_REGS = 40, CONS_REGS = 104;
+constexpr int LAUNCH_REGS = 96, PROD_REGS = 64, CONS_REGS = 104;
 static_assert(NPW * PROD_REGS + NCW * CONS_REGS <= (NCW + NPW) * LAUNCH_REGS, "register split");
 
 template <int FMT>
@@ -64,7 +65,6 @@ template <int KS>
 struct Cfg {
     static constexpr int MT = NCW / KS;            // m-tiles (16 rows) per item
     static constexpr int R = 16 * MT;              // rows of a routed item
-    static constexpr int BROW = KS * 1024 + 64;    // shared bytes of one staged activation row
     static_assert((KS - 1) * MT * 128 <= RED_FLOATS, "K-slice reduction buffer");
 };
 
@@ -159,7 +159,7 @@ static_assert(sizeof(StepHdr) <= HDR_BYTES, "step header");
 static_assert(offsetof(StepHdr, rows) == 16 && offsetof(StepHdr, out) == 32 && offsetof(StepHdr, ostride) == 40 &&
                   offsetof(StepHdr, e) == 44 && offsetof(StepHdr, bias) == 48 && offsetof(StepHdr, orow) == 64,
               "step header words as the consumers read them");
-constexpr int HF_PASS_START = 1, HF_PASS_END = 2, HF_SPLIT = 4;
+constexpr int HF_PASS_START = 1, HF_PASS_END = 2, HF_SPLIT = 4, HF_QINT = 8;
 
 __device__ __forceinline__ uint32_t pass_tokens(const Item& it, int pass, int tokcap) {
     const uint32_t done = (uint32_t)pass * (uint32_t)tokcap;
@@ -188,8 +188,8 @@ __device__ __forceinline__ void pass_rows(const GemvArgs& a, const Item& it, int
 constexpr int PBATCH = 8;
 struct PRing {
     Item it[PBATCH];
-    uint32_t arow[PBATCH][MAX_TOKCAP];
-    uint32_t orow[PBATCH][MAX_TOKCAP];
+    uint32_t arow[PBATCH][RING_TOK];
+    uint32_t orow[PBATCH][RING_TOK];
 };
 static_assert(NPW * sizeof(PRing) <= RING_BYTES, "producer rings");
 
@@ -256,13 +256,14 @@ __device__ __forceinline__ void issue_weights(const GemvArgs& a, const Item& it,
 template <int KS>
 __device__ __forceinline__ void issue_acts(const GemvArgs& a, const Item& it, int sk, uint32_t ntok, const uint8_t* brow,
                                            uint8_t* bslot, uint64_t* bbar, int lane) {
-    using C = Cfg<KS>;
     const int kp0 = sk * KS;
     const int nk = it.n_kp - kp0 < KS ? it.n_kp - kp0 : KS;
-    if (lane == 0) mbar_expect_tx(bbar, ntok * (uint32_t)nk * 1024);
+    // the hi halves and a Q8_K piece's scale (KS == 1) when no job of the launch reads the lo parts
+    const uint32_t bytes = a.bhi ? 528u : (uint32_t)nk * 1024;
+    if (lane == 0) mbar_expect_tx(bbar, ntok * bytes);
     __syncwarp();
     if ((uint32_t)lane < ntok)
-        bulk_g2s(bslot + HDR_BYTES + lane * C::BROW, brow + (int64_t)kp0 * 1024, (uint32_t)nk * 1024, bbar);
+        bulk_g2s(bslot + HDR_BYTES + lane * a.brow, brow + (int64_t)kp0 * 1024, bytes, bbar);
 }
 
 // ---------------------------------------------------------------- fast IQ decode
@@ -318,17 +319,18 @@ __device__ __forceinline__ void iq3s_pairs(const uint4& Qs, const uint2& S, uint
     }
 }
 
-// Activation chunks of sub-step ss for this thread's token slot: hi columns 0-7 / 8-15 (and lo).
+// Activation chunks of sub-step ss for this thread's token slot: hi columns 0-7 / 8-15 (and lo;
+// a piece's 32 hi chunks come first, then its 32 lo chunks).
 // Slots past the pass's tokens read whatever the slot holds: an MMA output column depends only on
 // its own activation column, and those columns are never stored, so no branch or zeroing is needed
 // (brow always points inside the activation slot).
 __device__ __forceinline__ void load_b(const uint8_t* brow, int ss, bool lo, uint32_t* hb, uint32_t* lb) {
-    const uint4 h0 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 0));
-    const uint4 h1 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 2));
+    const uint4 h0 = *reinterpret_cast<const uint4*>(brow + 128 * ss);
+    const uint4 h1 = *reinterpret_cast<const uint4*>(brow + 128 * ss + 64);
     uint4 l0 = make_uint4(0, 0, 0, 0), l1 = l0;
     if (lo) {
-        l0 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 1));
-        l1 = *reinterpret_cast<const uint4*>(brow + 64 * (4 * ss + 3));
+        l0 = *reinterpret_cast<const uint4*>(brow + 512 + 128 * ss);
+        l1 = *reinterpret_cast<const uint4*>(brow + 512 + 128 * ss + 64);
     }
     hb[0] = h0.x; hb[1] = h0.y; hb[2] = h0.z; hb[3] = h0.w;
     hb[4] = h1.x; hb[5] = h1.y; hb[6] = h1.z; hb[7] = h1.w;
@@ -336,63 +338,68 @@ __device__ __forceinline__ void load_b(const uint8_t* brow, int ss, bool lo, uin
     lb[4] = l1.x; lb[5] = l1.y; lb[6] = l1.z; lb[7] = l1.w;
 }
 
-// One step of a fast-path job: this warp's 16 rows x 256 columns; the piece's partial sums are
-// scaled by the rows' block scales and added to acc.
-template <int FMT>
+// One step of a fast-path job (late release): this warp's 16 rows x 256 columns against NT n-tiles
+// of 8 activation rows (bnt bytes apart); the piece's partial sums are scaled by the rows' block
+// scales and added to acc[nt * 4 + i].
+template <int FMT, int NT>
 __device__ __forceinline__ void fast_step(const uint8_t* wsl, int mt, int g, int c4, const uint8_t* tl,
-                                          const uint8_t* brow, bool has_tok, bool lo, float* acc) {
-    float t[4] = {0.f, 0.f, 0.f, 0.f};
+                                          const uint8_t* brow, int bnt, bool lo, float* acc) {
+    float t[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) t[nt][0] = t[nt][1] = t[nt][2] = t[nt][3] = 0.f;
     float dA, dB;
+    uint4 QA, QB;
+    uint2 SA = make_uint2(0, 0), SB = SA;
+    uint32_t HA, HB;
     if (FMT == F_IQ2_S) {
         const uint8_t* grp = wsl + mt * (16 * 82);
-        const uint4 QA = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 16);
-        const uint4 QB = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 16);
-        const uint32_t HA = *reinterpret_cast<const uint32_t*>(grp + 1024 + (g * 4 + c4) * 4);
-        const uint32_t HB = *reinterpret_cast<const uint32_t*>(grp + 1024 + ((g + 8) * 4 + c4) * 4);
+        QA = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 16);
+        QB = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 16);
+        HA = *reinterpret_cast<const uint32_t*>(grp + 1024 + (g * 4 + c4) * 4);
+        HB = *reinterpret_cast<const uint32_t*>(grp + 1024 + ((g + 8) * 4 + c4) * 4);
         dA = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1280 + 2 * g)), 0.125f);
         dB = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1280 + 2 * (g + 8))), 0.125f);
-#pragma unroll
-        for (int ss = 0; ss < 4; ++ss) {
-            uint32_t pa[8], pb[8], hb[8], lb[8];
-            iq2s_pairs(QA, HA, ss, tl, pa);
-            iq2s_pairs(QB, HB, ss, tl, pb);
-            load_b(brow, ss, lo, hb, lb);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
-                mma_16816(t, af, hb[2 * kk], hb[2 * kk + 1]);
-                if (lo) mma_16816(t, af, lb[2 * kk], lb[2 * kk + 1]);
-            }
-        }
     } else {
         const uint8_t* grp = wsl + mt * (16 * 110);
-        const uint4 QA = *reinterpret_cast<const uint4*>(grp + g * 64 + 16 * c4);
-        const uint4 QB = *reinterpret_cast<const uint4*>(grp + (g + 8) * 64 + 16 * c4);
-        const uint2 SA = *reinterpret_cast<const uint2*>(grp + 1024 + g * 32 + 8 * c4);
-        const uint2 SB = *reinterpret_cast<const uint2*>(grp + 1024 + (g + 8) * 32 + 8 * c4);
-        const uint32_t qhA = *reinterpret_cast<const uint16_t*>(grp + 1536 + g * 8 + 2 * c4);
-        const uint32_t qhB = *reinterpret_cast<const uint16_t*>(grp + 1536 + (g + 8) * 8 + 2 * c4);
-        const uint32_t scA = grp[1664 + g * 4 + c4], scB = grp[1664 + (g + 8) * 4 + c4];
+        QA = *reinterpret_cast<const uint4*>(grp + g * 64 + 16 * c4);
+        QB = *reinterpret_cast<const uint4*>(grp + (g + 8) * 64 + 16 * c4);
+        SA = *reinterpret_cast<const uint2*>(grp + 1024 + g * 32 + 8 * c4);
+        SB = *reinterpret_cast<const uint2*>(grp + 1024 + (g + 8) * 32 + 8 * c4);
+        HA = *reinterpret_cast<const uint16_t*>(grp + 1536 + g * 8 + 2 * c4) | ((uint32_t)grp[1664 + g * 4 + c4] << 16);
+        HB = *reinterpret_cast<const uint16_t*>(grp + 1536 + (g + 8) * 8 + 2 * c4) |
+             ((uint32_t)grp[1664 + (g + 8) * 4 + c4] << 16);
         dA = h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1728 + 2 * g));
         dB = h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1728 + 2 * (g + 8)));
+    }
 #pragma unroll
-        for (int ss = 0; ss < 4; ++ss) {
-            uint32_t pa[8], pb[8], hb[8], lb[8];
-            iq3s_pairs(QA, SA, qhA, scA, ss, tl, pa);
-            iq3s_pairs(QB, SB, qhB, scB, ss, tl, pb);
-            load_b(brow, ss, lo, hb, lb);
+    for (int ss = 0; ss < 4; ++ss) {
+        uint32_t pa[8], pb[8];
+        if (FMT == F_IQ2_S) {
+            iq2s_pairs(QA, HA, ss, tl, pa);
+            iq2s_pairs(QB, HB, ss, tl, pb);
+        } else {
+            iq3s_pairs(QA, SA, HA & 0xFFFFu, HA >> 16, ss, tl, pa);
+            iq3s_pairs(QB, SB, HB & 0xFFFFu, HB >> 16, ss, tl, pb);
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            uint32_t hb[8], lb[8];
+            load_b(brow + nt * bnt, ss, lo, hb, lb);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
                 const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
-                mma_16816(t, af, hb[2 * kk], hb[2 * kk + 1]);
-                if (lo) mma_16816(t, af, lb[2 * kk], lb[2 * kk + 1]);
+                mma_16816(t[nt], af, hb[2 * kk], hb[2 * kk + 1]);
+                if (lo) mma_16816(t[nt], af, lb[2 * kk], lb[2 * kk + 1]);
             }
         }
     }
-    acc[0] = __fmaf_rn(t[0], dA, acc[0]);
-    acc[1] = __fmaf_rn(t[1], dA, acc[1]);
-    acc[2] = __fmaf_rn(t[2], dB, acc[2]);
-    acc[3] = __fmaf_rn(t[3], dB, acc[3]);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        acc[nt * 4 + 0] = __fmaf_rn(t[nt][0], dA, acc[nt * 4 + 0]);
+        acc[nt * 4 + 1] = __fmaf_rn(t[nt][1], dA, acc[nt * 4 + 1]);
+        acc[nt * 4 + 2] = __fmaf_rn(t[nt][2], dB, acc[nt * 4 + 2]);
+        acc[nt * 4 + 3] = __fmaf_rn(t[nt][3], dB, acc[nt * 4 + 3]);
+    }
 }
 
 // Early-release form of a fast step (f16 activations only): the rows' index, sign and scale bytes
@@ -430,13 +437,15 @@ __device__ __forceinline__ void fast_load(const uint8_t* wsl, int mt, int g, int
     }
 }
 
-template <int FMT>
-__device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl, const uint8_t* brow, bool has_tok,
+template <int FMT, int NT>
+__device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl, const uint8_t* brow, int bnt,
                                              float* acc) {
-    float t[4] = {0.f, 0.f, 0.f, 0.f};
+    float t[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) t[nt][0] = t[nt][1] = t[nt][2] = t[nt][3] = 0.f;
 #pragma unroll
     for (int ss = 0; ss < 4; ++ss) {
-        uint32_t pa[8], pb[8], hb[8], lb[8];
+        uint32_t pa[8], pb[8];
         if (FMT == F_IQ2_S) {
             iq2s_pairs(in.QA, in.HA, ss, tl, pa);
             iq2s_pairs(in.QB, in.HB, ss, tl, pb);
@@ -444,17 +453,24 @@ __device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl
             iq3s_pairs(in.QA, in.SA, in.HA & 0xFFFFu, in.HA >> 16, ss, tl, pa);
             iq3s_pairs(in.QB, in.SB, in.HB & 0xFFFFu, in.HB >> 16, ss, tl, pb);
         }
-        load_b(brow, ss, false, hb, lb);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
-            mma_16816(t, af, hb[2 * kk], hb[2 * kk + 1]);
+        for (int nt = 0; nt < NT; ++nt) {
+            uint32_t hb[8], lb[8];
+            load_b(brow + nt * bnt, ss, false, hb, lb);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
+                mma_16816(t[nt], af, hb[2 * kk], hb[2 * kk + 1]);
+            }
         }
     }
-    acc[0] = __fmaf_rn(t[0], in.dA, acc[0]);
-    acc[1] = __fmaf_rn(t[1], in.dA, acc[1]);
-    acc[2] = __fmaf_rn(t[2], in.dB, acc[2]);
-    acc[3] = __fmaf_rn(t[3], in.dB, acc[3]);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        acc[nt * 4 + 0] = __fmaf_rn(t[nt][0], in.dA, acc[nt * 4 + 0]);
+        acc[nt * 4 + 1] = __fmaf_rn(t[nt][1], in.dA, acc[nt * 4 + 1]);
+        acc[nt * 4 + 2] = __fmaf_rn(t[nt][2], in.dB, acc[nt * 4 + 2]);
+        acc[nt * 4 + 3] = __fmaf_rn(t[nt][3], in.dB, acc[nt * 4 + 3]);
+    }
 }
 
 // Q4_K: y = d * sc * q - dmin * m per 32-column sub-block (sub-blocks 2c and 2c+1 are the low
@@ -512,40 +528,80 @@ __device__ __forceinline__ void q4_pairs(const Q4Row& r, int ss, uint32_t* p) {
     }
 }
 
-__device__ __forceinline__ void q4k_step(const uint8_t* wsl, int mt, int g, int c4, const uint8_t* brow, bool has_tok,
-                                         bool lo, float* acc) {
+// Activation scales of the thread's two output columns in each n-tile, for Q8_K rows (qi): the
+// f32 at byte 512 of the piece in rows dx0 and dx1 (byte offsets from the slot's rows) and
+// n-tile nt bnt bytes further.
+struct DxAt {
+    const uint8_t* p0;
+    const uint8_t* p1;
+};
+__device__ __forceinline__ float dx_of(const DxAt& x, int nt, int bnt, int i) {
+    return *reinterpret_cast<const float*>(((i & 1) ? x.p1 : x.p0) + nt * bnt);
+}
+
+template <int NT>
+__device__ __forceinline__ void q4k_step(const uint8_t* wsl, int mt, int g, int c4, const uint8_t* brow, int bnt, bool lo,
+                                         bool qi, const DxAt& dx, float* acc) {
     const Q4Row A = q4_row(wsl + (16 * mt + g) * 144, c4);
     const Q4Row Bq = q4_row(wsl + (16 * mt + g + 8) * 144, c4);
-    float t1[4] = {0.f, 0.f, 0.f, 0.f}, t2[4] = {0.f, 0.f, 0.f, 0.f};
+    float t1[NT][4], t2[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) t1[nt][i] = t2[nt][i] = 0.f;
 #pragma unroll
     for (int ss = 0; ss < 4; ++ss) {
-        uint32_t pa[8], pb[8], hb[8], lb[8];
+        uint32_t pa[8], pb[8];
         q4_pairs(A, ss, pa);
         q4_pairs(Bq, ss, pb);
-        load_b(brow, ss, lo, hb, lb);
         const uint32_t ma = h22u(ss < 2 ? A.m0 : A.m1), mb = h22u(ss < 2 ? Bq.m0 : Bq.m1);
         const uint32_t am[4] = {ma, mb, ma, mb};
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
-            mma_16816(t1, af, hb[2 * kk], hb[2 * kk + 1]);
-            mma_16816(t2, am, hb[2 * kk], hb[2 * kk + 1]);
-            if (lo) {
-                mma_16816(t1, af, lb[2 * kk], lb[2 * kk + 1]);
-                mma_16816(t2, am, lb[2 * kk], lb[2 * kk + 1]);
+        for (int nt = 0; nt < NT; ++nt) {
+            uint32_t hb[8], lb[8];
+            // Q8_K rows have no lo halves (and are copied without them)
+            load_b(brow + nt * bnt, ss, lo && !qi, hb, lb);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
+                mma_16816(t1[nt], af, hb[2 * kk], hb[2 * kk + 1]);
+                mma_16816(t2[nt], am, hb[2 * kk], hb[2 * kk + 1]);
+                if (lo && !qi) {
+                    mma_16816(t1[nt], af, lb[2 * kk], lb[2 * kk + 1]);
+                    mma_16816(t2[nt], am, lb[2 * kk], lb[2 * kk + 1]);
+                }
             }
         }
     }
-    acc[0] = __fmaf_rn(-t2[0], A.dmin, __fmaf_rn(t1[0], A.d, acc[0]));
-    acc[1] = __fmaf_rn(-t2[1], A.dmin, __fmaf_rn(t1[1], A.d, acc[1]));
-    acc[2] = __fmaf_rn(-t2[2], Bq.dmin, __fmaf_rn(t1[2], Bq.d, acc[2]));
-    acc[3] = __fmaf_rn(-t2[3], Bq.dmin, __fmaf_rn(t1[3], Bq.d, acc[3]));
+    if (qi) {  // integer codes: the piece's sums times the rows' scales, then the code scale d
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const Q4Row& R = i < 2 ? A : Bq;
+                const float r = __fmaf_rn(-t2[nt][i], R.dmin, __fmul_rn(t1[nt][i], R.d));
+                acc[nt * 4 + i] = __fmaf_rn(r, dx_of(dx, nt, bnt, i), acc[nt * 4 + i]);
+            }
+    } else {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            acc[nt * 4 + 0] = __fmaf_rn(-t2[nt][0], A.dmin, __fmaf_rn(t1[nt][0], A.d, acc[nt * 4 + 0]));
+            acc[nt * 4 + 1] = __fmaf_rn(-t2[nt][1], A.dmin, __fmaf_rn(t1[nt][1], A.d, acc[nt * 4 + 1]));
+            acc[nt * 4 + 2] = __fmaf_rn(-t2[nt][2], Bq.dmin, __fmaf_rn(t1[nt][2], Bq.d, acc[nt * 4 + 2]));
+            acc[nt * 4 + 3] = __fmaf_rn(-t2[nt][3], Bq.dmin, __fmaf_rn(t1[nt][3], Bq.d, acc[nt * 4 + 3]));
+        }
+    }
 }
 
 // One step of any format: exact f32 dequantisation rounded to f16 (hi + lo weights when split),
-// activations hi + lo.
+// activations hi + lo, or Q8_K codes (qi) whose piece sums are scaled by the rows' d.
+template <int NT>
 __device__ __forceinline__ void generic_step(const Layout& L, int kp, const uint8_t* wsl, int mt, int g, int c4,
-                                             const uint8_t* brow, bool has_tok, bool split, float* acc) {
+                                             const uint8_t* brow, int bnt, bool split, bool qi, const DxAt& dx,
+                                             float* acc) {
+    float t[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) t[nt][0] = t[nt][1] = t[nt][2] = t[nt][3] = 0.f;
     const int64_t prb = piece_row_bytes(L, kp);
     const int64_t kleft = L.k - (int64_t)kp * PIECE_K;
     const int klen = (int)(kleft < PIECE_K ? kleft : PIECE_K);
@@ -581,15 +637,24 @@ __device__ __forceinline__ void generic_step(const Layout& L, int kp, const uint
                 }
             }
         }
-        uint32_t hb[8], lb[8];
-        load_b(brow, ss, true, hb, lb);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            mma_16816(acc, af[kk], hb[2 * kk], hb[2 * kk + 1]);
-            mma_16816(acc, af[kk], lb[2 * kk], lb[2 * kk + 1]);
-            if (split) mma_16816(acc, al[kk], hb[2 * kk], hb[2 * kk + 1]);
+        for (int nt = 0; nt < NT; ++nt) {
+            uint32_t hb[8], lb[8];
+            load_b(brow + nt * bnt, ss, !qi, hb, lb);
+            float* d = qi ? t[nt] : acc + nt * 4;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                mma_16816(d, af[kk], hb[2 * kk], hb[2 * kk + 1]);
+                if (!qi) mma_16816(d, af[kk], lb[2 * kk], lb[2 * kk + 1]);
+                if (split) mma_16816(d, al[kk], hb[2 * kk], hb[2 * kk + 1]);
+            }
         }
     }
+    if (qi)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[nt * 4 + i] = __fmaf_rn(t[nt][i], dx_of(dx, nt, bnt, i), acc[nt * 4 + i]);
 }
 
 // Replicated f16 codebooks (every consumer thread; the caller synchronises the consumers).
@@ -617,9 +682,10 @@ __device__ __forceinline__ void build_tables(uint8_t* tbl, int tid) {
     }
 }
 
-template <int FMT, int KS>
+template <int FMT, int KS, int NT>
 __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
     using C = Cfg<KS>;
+    static_assert(KS == 1 || NT == 1, "n-tiles per pass only without K-slices");
     extern __shared__ __align__(128) uint8_t smem[];
     // two rings: weight slots (released as soon as the warps hold their bytes in registers, on
     // the fast path) and activation slots with the step header (released after the math)
@@ -662,9 +728,11 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
                             get_item<KS>(a, (uint32_t)(blockIdx.x + (base + lane) * gridDim.x), n_used, &mine);
             if (ok) {
                 ring->it[lane] = mine;
-                const uint32_t n0 = pass_tokens(mine, mine.pass0, a.tokcap);
-                for (uint32_t t = 0; t < n0; ++t)
-                    pass_rows(a, mine, mine.pass0, t, &ring->arow[lane][t], &ring->orow[lane][t]);
+                if (a.tokcap <= RING_TOK) {
+                    const uint32_t n0 = pass_tokens(mine, mine.pass0, a.tokcap);
+                    for (uint32_t t = 0; t < n0; ++t)
+                        pass_rows(a, mine, mine.pass0, t, &ring->arow[lane][t], &ring->orow[lane][t]);
+                }
             }
             const uint32_t okm = __ballot_sync(0xffffffffu, ok);
             __syncwarp();
@@ -678,7 +746,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
                     const uint32_t ntok = pass_tokens(it, pass, a.tokcap);
                     uint32_t arow = 0, orow = 0;
                     if ((uint32_t)lane < ntok) {
-                        if (pass == it.pass0) {
+                        if (pass == it.pass0 && a.tokcap <= RING_TOK) {
                             arow = ring->arow[li][lane];
                             orow = ring->orow[li][lane];
                         } else {
@@ -695,7 +763,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
                             StepHdr* h = reinterpret_cast<StepHdr*>(bslot);
                             if (lane == 0) {
                                 const int flags = (sk == 0 ? HF_PASS_START : 0) | (sk == it.nsk - 1 ? HF_PASS_END : 0) |
-                                                  (jb.split ? HF_SPLIT : 0) | (jb.m.L.fmt << 8);
+                                                  (jb.split ? HF_SPLIT : 0) | (jb.qint ? HF_QINT : 0) |
+                                                  (jb.m.L.fmt << 8);
                                 uint4* hv = reinterpret_cast<uint4*>(h);
                                 hv[0] = make_uint4((uint32_t)it.job, (uint32_t)flags, (uint32_t)(sk * KS), (uint32_t)it.n_kp);
                                 hv[1] = make_uint4((uint32_t)it.rows, ntok, (uint32_t)(it.rt * jb.rows), (uint32_t)jb.m.L.n);
@@ -738,7 +807,16 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
     const uint8_t* tl = tbl + (FMT == F_IQ2_S ? (lane & 7) * 16 : (lane & 15) * 8);
     const int mt = warp % C::MT, ks = warp / C::MT;
     const int g = lane >> 2, c4 = lane & 3;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    // this thread's activation row (slot g of n-tile 0; with one n-tile, passes of fewer than 8
+    // slots read row 0 past their capacity), its chunk of this K-slice; n-tile nt is bnt further
+    const int bnt = 8 * a.brow;
+    const int brow_off = HDR_BYTES + (NT == 1 && g >= a.tokcap ? 0 : g) * a.brow + ks * 1024 + 16 * c4;
+    // the rows of this thread's output columns 2 c4 and 2 c4 + 1 (Q8_K scales), row 0 past capacity
+    const int dx0_off = HDR_BYTES + (2 * c4 < a.tokcap ? 2 * c4 : 0) * a.brow + ks * 1024 + 512;
+    const int dx1_off = HDR_BYTES + (2 * c4 + 1 < a.tokcap ? 2 * c4 + 1 : 0) * a.brow + ks * 1024 + 512;
+    float acc[4 * NT];
+#pragma unroll
+    for (int i = 0; i < 4 * NT; ++i) acc[i] = 0.f;
     int s = 0;
     uint32_t ph = 0;
     for (;;) {
@@ -750,40 +828,46 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
         if (jobi < 0) return;
         const int flags = (int)h0.y, fmt = (flags >> 8) & 0xFF;
         const bool pass_start = flags & HF_PASS_START, pass_end = flags & HF_PASS_END, lo = flags & HF_SPLIT;
+        const bool qi = flags & HF_QINT;
         const int kp = (int)h0.z + ks, n_kp = (int)h0.w;
         const int rows = (int)h1.x;
         const uint32_t ntok = h1.y;
-        if (pass_start) acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-        const bool active = kp < n_kp && 16 * mt < rows;
-        // what the pass's epilogue needs, taken out of the slot before the slot is handed back
-        uint4 h2 = make_uint4(0, 0, 0, 0), h3 = h2;
-        uint2 orw = make_uint2(0, 0);
-        if (pass_end) {
-            h2 = reinterpret_cast<const uint4*>(h)[2];
-            h3 = reinterpret_cast<const uint4*>(h)[3];
-            orw = *reinterpret_cast<const uint2*>(&h->orow[2 * c4]);
+        if (pass_start) {
+#pragma unroll
+            for (int i = 0; i < 4 * NT; ++i) acc[i] = 0.f;
         }
+        const bool active = kp < n_kp && 16 * mt < rows;
         const uint8_t* wsl = wslots + s * a.wslot_bytes + ks * a.slot_bytes;
-        // this thread's activation row (slot g of the pass; rows past the slot's capacity read row 0),
-        // its chunk of this K-slice
-        const uint8_t* brow = bslot + HDR_BYTES + (g < a.tokcap ? g : 0) * C::BROW + ks * 1024 + 16 * c4;
-        const bool has_tok = (uint32_t)g < ntok;
+        const uint8_t* brow = bslot + brow_off;
         if (!mbar_wait(&full_w[s], ph, a.err)) return;
-        if (FMT != 0 && fmt == FMT && !lo) {
+        if (FMT != 0 && fmt == FMT && !lo && !qi) {
             FastIn in;
             if (active) fast_load<FMT>(wsl, mt, g, c4, in);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty_w[s]);  // the weights go back before the math
-            if (active) fast_compute<FMT>(in, tl, brow, has_tok, acc);
+            if (active) fast_compute<FMT, NT>(in, tl, brow, bnt, acc);
         } else {
             if (active) {
                 const Layout& L = a.job[jobi].m.L;
-                if (FMT != 0 && L.fmt == FMT) fast_step<FMT>(wsl, mt, g, c4, tl, brow, has_tok, true, acc);
-                else if (L.fmt == F_Q4_K && L.kp_row_bytes == 144) q4k_step(wsl, mt, g, c4, brow, has_tok, lo, acc);
-                else generic_step(L, kp, wsl, mt, g, c4, brow, has_tok, lo, acc);
+                const DxAt dx{bslot + dx0_off, bslot + dx1_off};
+                if (FMT != 0 && L.fmt == FMT && !qi) fast_step<FMT, NT>(wsl, mt, g, c4, tl, brow, bnt, true, acc);
+                else if (L.fmt == F_Q4_K && L.kp_row_bytes == 144) q4k_step<NT>(wsl, mt, g, c4, brow, bnt, lo, qi, dx, acc);
+                else generic_step<NT>(L, kp, wsl, mt, g, c4, brow, bnt, lo, qi, dx, acc);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty_w[s]);
+        }
+        // what the pass's epilogue needs, taken out of the slot before the slot is handed back (after
+        // the math, so these registers are not held through it)
+        uint4 h2 = make_uint4(0, 0, 0, 0), h3 = h2;
+        uint2 orw[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) orw[nt] = make_uint2(0, 0);
+        if (pass_end) {
+            h2 = reinterpret_cast<const uint4*>(h)[2];
+            h3 = reinterpret_cast<const uint4*>(h)[3];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) orw[nt] = *reinterpret_cast<const uint2*>(&h->orow[8 * nt + 2 * c4]);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_b[s]);
@@ -815,100 +899,118 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
             const float* bias = reinterpret_cast<const float*>(((uint64_t)h3.y << 32) | h3.x);
             const int feat0 = (int)h1.z, n = (int)h1.w;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t slot = 2 * c4 + (i & 1);
-                if (slot < ntok) {
-                    const int64_t feat = feat0 + 16 * mt + g + ((i >> 1) ? 8 : 0);
-                    const int64_t orow = (i & 1) ? orw.y : orw.x;
-                    float v = acc[i];
-                    if (bias) v = __fadd_rn(v, bias[(int64_t)e * n + feat]);
-                    out[orow * ostride + feat] = v;
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t slot = 8 * nt + 2 * c4 + (i & 1);
+                    if (slot < ntok) {
+                        const int64_t feat = feat0 + 16 * mt + g + ((i >> 1) ? 8 : 0);
+                        const int64_t orow = (i & 1) ? orw[nt].y : orw[nt].x;
+                        float v = acc[nt * 4 + i];
+                        if (bias) v = __fadd_rn(v, bias[(int64_t)e * n + feat]);
+                        out[orow * ostride + feat] = v;
+                    }
                 }
-            }
         }
     }
 }
 
 // ---------------------------------------------------------------- host side
-template <int FMT, int KS>
-static int launch_fk(GemvArgs a, int64_t experts_est, int device, int sm_count, cudaStream_t st) {
-    using C = Cfg<KS>;
-    // K-slice bytes of a stage: a routed tile of the fast format at full height (every job at
-    // full height when there is no fast format), and at least 16 rows of every other job; jobs of
-    // other formats get the rows that fit.
+static int tbl_bytes(int fmt) {
+    return fmt == F_IQ2_S ? Tbl<F_IQ2_S>::BYTES : fmt == F_IQ3_S ? Tbl<F_IQ3_S>::BYTES : 0;
+}
+
+// Stage sizes of a launch with routed format fmt (0: none), ks K-slices and a.tokcap picks per
+// pass: the weight bytes of a K-slice (a routed tile of the fast format at full height, every job
+// at full height when there is no fast format, and at least 16 rows of every other job; jobs of
+// other formats get the rows that fit), the activation row stride (the hi halves only when one
+// K-slice is copied and no job reads the lo parts), and how many stages fit in shared memory.
+// Returns the stage count (below 2: the configuration does not fit).
+static int size_stages(GemvArgs& a, int fmt, int ks, int64_t experts_est, int64_t* items, int* smem) {
+    const int64_t R = 16 * (NCW / ks);
     int64_t slot = 0;
+    bool hi_only = ks == 1;
     for (int j = 0; j < a.njobs; ++j) {
-        const Layout& L = a.job[j].m.L;
-        const int64_t want = (FMT == 0 || L.fmt == FMT) ? (int64_t)C::R : 16;
+        const GemvJob& jb = a.job[j];
+        const Layout& L = jb.m.L;
+        const int64_t want = (fmt == 0 || L.fmt == fmt) ? R : 16;
         const int64_t b = pad16(want * L.kp_row_bytes);
         if (b > slot) slot = b;
+        // which products read the activations' lo halves: the exact path of any format, and
+        // split products, unless the rows hold Q8_K codes
+        const bool fast = fmt != 0 && L.fmt == fmt, q4 = L.fmt == F_Q4_K && L.kp_row_bytes == 144;
+        if (!jb.qint && (jb.split || !(fast || q4))) hi_only = false;
     }
     a.slot_bytes = (int)slot;
-    int64_t items = 0;
+    *items = 0;
     const int64_t sp = (a.s_count + a.tokcap - 1) / a.tokcap;
     for (int j = 0; j < a.njobs; ++j) {
         GemvJob& jb = a.job[j];
         int64_t rows = slot / jb.m.L.kp_row_bytes / 16 * 16;
-        if (rows > C::R) rows = C::R;
+        if (rows > R) rows = R;
         jb.rows = (int)rows;
         const int64_t t = (jb.m.L.n + rows - 1) / rows;
-        items += jb.shared ? t * sp : t * experts_est;
+        *items += jb.shared ? t * sp : t * experts_est;
     }
-    a.wslot_bytes = (int)((KS * slot + 127) & ~(int64_t)127);
-    a.bslot_bytes = (int)((HDR_BYTES + (int64_t)a.tokcap * C::BROW + 127) & ~(int64_t)127);
-    const int fixed = BAR_BYTES + Tbl<FMT>::BYTES + RED_FLOATS * 4 + RING_BYTES;
+    // rows of a slot 64 bytes past a multiple of 128, so the 8 rows one load instruction touches
+    // fall in different banks
+    a.bhi = hi_only ? 1 : 0;
+    a.brow = (hi_only ? 512 : ks * 1024) + 64;
+    a.wslot_bytes = (int)((ks * slot + 127) & ~(int64_t)127);
+    a.bslot_bytes = (int)((HDR_BYTES + (int64_t)a.tokcap * a.brow + 127) & ~(int64_t)127);
+    const int fixed = BAR_BYTES + tbl_bytes(fmt) + RED_FLOATS * 4 + RING_BYTES;
     int nst = (SMEM_LIMIT - fixed) / (a.wslot_bytes + a.bslot_bytes);
     if (nst > 8) nst = 8;
-    if (nst < 2) return fail(CWX_EUNSUPPORTED, "expert pieces too large for shared memory");
     a.nst = nst;
-    const int smem = fixed + nst * (a.wslot_bytes + a.bslot_bytes);
-    // the register split above assumes the launch allocates LAUNCH_REGS per thread (allocation is
-    // in steps of 8): a kernel compiled with fewer would make the consumers' increase wait forever
-    static int regs_ok[3][4] = {{0}};
-    {
-        const int fi = FMT == 0 ? 0 : FMT == F_IQ2_S ? 1 : 2, ki = KS == 1 ? 0 : KS == 2 ? 1 : KS == 4 ? 2 : 3;
-        if (!regs_ok[fi][ki]) {
-            cudaFuncAttributes fa;
-            cudaError_t e = cudaFuncGetAttributes(&fa, k_gemv<FMT, KS>);
-            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes(k_gemv)");
-            if ((fa.numRegs + 7) / 8 * 8 != LAUNCH_REGS)
-                return fail(CWX_EUNSUPPORTED, "k_gemv compiled with %d registers, the register split needs %d",
-                            fa.numRegs, LAUNCH_REGS);
-            regs_ok[fi][ki] = 1;
-        }
+    *smem = fixed + nst * (a.wslot_bytes + a.bslot_bytes);
+    return nst;
+}
+
+template <int FMT, int KS, int NT>
+static int launch_fk(const GemvArgs& a, int64_t items, int smem, int device, int sm_count, cudaStream_t st) {
+    constexpr int fi = FMT == 0 ? 0 : FMT == F_IQ2_S ? 1 : 2;
+    constexpr int ki = (KS == 1 ? 0 : KS == 2 ? 1 : KS == 4 ? 2 : 3) + (NT == 2 ? 4 : NT == 4 ? 5 : 0);
+    // the register split assumes the launch allocates LAUNCH_REGS per thread (allocation is in
+    // steps of 8): a kernel compiled with fewer would make the consumers' increase wait forever
+    static int regs_ok[3][6] = {{0}};
+    if (!regs_ok[fi][ki]) {
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaFuncGetAttributes(&fa, k_gemv<FMT, KS, NT>);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes(k_gemv)");
+        if ((fa.numRegs + 7) / 8 * 8 != LAUNCH_REGS)
+            return fail(CWX_EUNSUPPORTED, "k_gemv compiled with %d registers, the register split needs %d",
+                        fa.numRegs, LAUNCH_REGS);
+        regs_ok[fi][ki] = 1;
     }
-    static int attr_set[64][3][4] = {{{0}}};
-    const int fidx = FMT == 0 ? 0 : FMT == F_IQ2_S ? 1 : 2;
-    const int kidx = KS == 1 ? 0 : KS == 2 ? 1 : KS == 4 ? 2 : 3;
-    if (device < 0 || device >= 64 || attr_set[device][fidx][kidx] < smem) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemv<FMT, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    static int attr_set[64][3][6] = {{{0}}};
+    if (device < 0 || device >= 64 || attr_set[device][fi][ki] < smem) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemv<FMT, KS, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_gemv)");
-        if (device >= 0 && device < 64) attr_set[device][fidx][kidx] = smem;
+        if (device >= 0 && device < 64) attr_set[device][fi][ki] = smem;
     }
     int64_t grid = sm_count;
     if (grid > items) grid = items;
     if (grid < 1) return CWX_OK;
-    k_gemv<FMT, KS><<<(unsigned)grid, GEMV_THREADS, smem, st>>>(a);
+    k_gemv<FMT, KS, NT><<<(unsigned)grid, GEMV_THREADS, smem, st>>>(a);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_gemv");
 }
 
 template <int FMT>
-static int launch_f(const GemvArgs& a, int ks, int64_t experts_est, int device, int sm_count, cudaStream_t st) {
+static int launch_f(const GemvArgs& a, int ks, int nt, int64_t items, int smem, int device, int sm_count,
+                    cudaStream_t st) {
+    if (nt == 4) return launch_fk<FMT, 1, 4>(a, items, smem, device, sm_count, st);
+    if (nt == 2) return launch_fk<FMT, 1, 2>(a, items, smem, device, sm_count, st);
     switch (ks) {
-        case 1: return launch_fk<FMT, 1>(a, experts_est, device, sm_count, st);
-        case 2: return launch_fk<FMT, 2>(a, experts_est, device, sm_count, st);
-        case 4: return launch_fk<FMT, 4>(a, experts_est, device, sm_count, st);
-        default: return launch_fk<FMT, 8>(a, experts_est, device, sm_count, st);
+        case 1: return launch_fk<FMT, 1, 1>(a, items, smem, device, sm_count, st);
+        case 2: return launch_fk<FMT, 2, 1>(a, items, smem, device, sm_count, st);
+        case 4: return launch_fk<FMT, 4, 1>(a, items, smem, device, sm_count, st);
+        default: return launch_fk<FMT, 8, 1>(a, items, smem, device, sm_count, st);
     }
 }
 
 int launch_gemv(const GemvArgs& in, int64_t experts_est, int device, int sm_count, cudaStream_t st) {
     GemvArgs a = in;
-    // picks per pass: the expected largest pile, a power of two up to 8
-    int tc = 1;
-    while (tc < MAX_TOKCAP && tc < a.tok_est) tc *= 2;
-    a.tokcap = tc;
     // the routed format, when every routed job shares one IQ format
     int fmt = -1, n_kp = 1 << 30;
     int64_t rows = 0;
@@ -920,19 +1022,38 @@ int launch_gemv(const GemvArgs& in, int64_t experts_est, int device, int sm_coun
         rows += L.n;
     }
     if (fmt != F_IQ2_S && fmt != F_IQ3_S) fmt = 0;
+    int64_t items = 0;
+    int smem = 0;
+    // large piles (on average 24 or 10 picks and more): 32 or 16 picks per pass (4 or 2 n-tiles of
+    // 8 per decoded weight fragment), one K-slice, when two stages of that fit
+    for (int nt = 4; nt >= 2; nt /= 2)
+        if (a.pile_est >= (nt == 4 ? 24 : 10) && a.tok_est > 8) {
+            a.tokcap = 8 * nt;
+            if (size_stages(a, fmt, 1, experts_est, &items, &smem) >= 2) {
+                if (fmt == F_IQ2_S) return launch_f<F_IQ2_S>(a, 1, nt, items, smem, device, sm_count, st);
+                if (fmt == F_IQ3_S) return launch_f<F_IQ3_S>(a, 1, nt, items, smem, device, sm_count, st);
+                return launch_f<0>(a, 1, nt, items, smem, device, sm_count, st);
+            }
+        }
+    // otherwise passes of the expected largest pile, a power of two up to 8
+    int tc = 1;
+    while (tc < 8 && tc < a.tok_est) tc *= 2;
+    a.tokcap = tc;
     // K-slices: the smallest split (up to the pieces per row, and 8 staged activation pieces per
     // stage) whose items still fill the GPU twice
     int ks = 1;
     if (rows > 0)
-        while (ks < 8 && ks * 2 <= n_kp && ks * 2 * tc <= MAX_TOKCAP) {
+        while (ks < 8 && ks * 2 <= n_kp && ks * 2 * tc <= 8) {
             const int64_t r = 16 * (NCW / ks);
-            const int64_t items = experts_est * ((rows + r - 1) / r);
-            if (items >= 2 * sm_count) break;
+            const int64_t it = experts_est * ((rows + r - 1) / r);
+            if (it >= 2 * sm_count) break;
             ks *= 2;
         }
-    if (fmt == F_IQ2_S) return launch_f<F_IQ2_S>(a, ks, experts_est, device, sm_count, st);
-    if (fmt == F_IQ3_S) return launch_f<F_IQ3_S>(a, ks, experts_est, device, sm_count, st);
-    return launch_f<0>(a, ks, experts_est, device, sm_count, st);
+    if (size_stages(a, fmt, ks, experts_est, &items, &smem) < 2)
+        return fail(CWX_EUNSUPPORTED, "expert pieces too large for shared memory");
+    if (fmt == F_IQ2_S) return launch_f<F_IQ2_S>(a, ks, 1, items, smem, device, sm_count, st);
+    if (fmt == F_IQ3_S) return launch_f<F_IQ3_S>(a, ks, 1, items, smem, device, sm_count, st);
+    return launch_f<0>(a, ks, 1, items, smem, device, sm_count, st);
 }
 
 }  // namespace cwx

@@ -20,6 +20,7 @@ struct GemvJob {
     float* out;         // output rows: pick index (routed) or token (shared)
     int64_t ostride;
     int split;          // products carried to ~22 bits (weights and activations as f16 hi + lo)
+    int qint;           // activation rows hold Q8_K codes (f16 integers) and each piece's f32 scale
     const float* bias;  // (n_experts, n) added to the outputs, or NULL
     int rows;           // rows per work item (set by the launcher)
 };
@@ -31,7 +32,8 @@ struct GemvArgs {
     const uint32_t* used3;  // (expert, first pair, count) per used expert
     const uint32_t* n_used;
     int s_count;  // tokens of the shared jobs
-    int tok_est;  // expected largest number of picks of one expert (sizes the passes)
+    int tok_est;   // upper bound on the picks of one expert (sizes the passes of small batches)
+    int pile_est;  // average picks per expert (large piles take passes of 16 or 32 picks)
     int* err;
     // set by the launcher
     int tokcap;      // picks per pass
@@ -39,6 +41,8 @@ struct GemvArgs {
     int wslot_bytes;  // one weight slot (KS K-slices)
     int bslot_bytes;  // one activation slot (step header + activation rows)
     int nst;          // slots per ring
+    int bhi;          // activation copies carry the hi halves only
+    int brow;         // bytes from one activation row of a slot to the next
 };
 
 // Bytes of one packed activation row of k columns (1024 per 256-column piece).
@@ -74,5 +78,25 @@ int launch_combine(const float* rows, const float* w, int T, int K, int H, const
                    const float* residual, float* out, cudaStream_t st);
 // experts_est: the number of experts expected to have picks (sizes the grid and the K split).
 int launch_gemv(const GemvArgs& a, int64_t experts_est, int device, int sm_count, cudaStream_t st);
+
+// Tensor-core (tcgen05) expert products for large piles (mma.cu).
+struct MmaArgs {
+    MatRef a0, a1;       // weights; a1: the up matrix of a fused gate/up launch
+    int fused;           // 1: gate/up rows side by side, SwiGLU epilogue writing f16 h rows
+    const uint8_t* b;    // activation rows (f16), bstride bytes apart
+    int64_t bstride;
+    int bdiv;            // activation row = pair / bdiv
+    const uint32_t* pairs;
+    const uint32_t* used3;
+    const uint32_t* n_used;
+    float* out;          // plain: f32 output rows per pick
+    __half* hout;        // fused: f16 h rows per pick
+    int64_t ostride;     // elements between output rows
+    int* err;
+    int mtiles;          // row tiles per expert (set by the launcher)
+};
+bool mma_supports(const MmaArgs& a);
+int launch_mma(const MmaArgs& a, int device, int sm_count, cudaStream_t st);
+int launch_f16rows(const float* x, int64_t n, __half* y, cudaStream_t st);
 
 }  // namespace cwx

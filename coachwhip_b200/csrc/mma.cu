@@ -1,0 +1,559 @@
+// Grouped expert products for large piles (prefill) on the 5th-generation tensor cores.
+//
+//   reference  MoeMatvec on prefill-sized batches (crates/engine/src/experts.rs:2183-2309), which
+//              ends in kernel_mul_mm_idg_* (crates/engine/src/mv_id.rs:220-384,
+//              vendor/candle-metal-kernels/src/metal_src/quantized.metal:7868-7911): per expert, the
+//              picks routed to it times the expert's dequantised matrix.
+//
+// One persistent CTA per SM walks work items (used expert, row tile of 128 outputs, column tile of
+// up to 256 picks). Per item the CTA streams the tile's quantised pieces (256 columns) into shared
+// memory with bulk copies, decodes them 64 columns at a time into f16 A tiles, gathers the picks'
+// activation rows (f16) into B tiles with cp.async, and one thread issues tcgen05.mma
+// (M = 128, N = the tile's picks rounded up to 16, K = 16 per instruction) into a TMEM
+// accumulator. Two accumulators (TMEM columns 0-255 and 256-511) let the epilogue of one item run
+// while the next one multiplies.
+//
+// Operand layout (both K-major, 128-byte swizzle): a tile row holds 64 f16 (128 bytes), rows are
+// 128 bytes apart, 16-byte chunk c of row r sits at chunk position c ^ (r % 8), and 8-row groups
+// are 1024 bytes apart (the smem descriptor's stride byte offset). The MMA for columns
+// 16 kk .. 16 kk + 15 of a stage starts 32 kk bytes into the tile.
+//
+// Weights: IQ2_S / IQ3_S codebook values times sign times (2 s + 1) are exact f16 integers; one
+// f16 multiply by the block scale d (d / 8 for IQ2_S, exact in f16) rounds each weight once, so
+// the A tiles hold the exact dequantised weight rounded to f16.
+//
+// Two forms of a launch:
+//   fused gate/up: A rows 0-63 are gate rows f0 .. f0+63, rows 64-127 the up rows of the same
+//     features; the epilogue writes h = silu(gate) * up as f16 rows (one per pick), the B operand
+//     of the down products;
+//   plain: A rows are 128 consecutive rows of one matrix; the epilogue writes f32 rows per pick.
+//
+// Roles (18 warps): 0-3 epilogue (TMEM lanes 32w .. 32w+31), 4 MMA issue and TMEM allocation,
+// 5 quantised-piece copies, 6-9 activation gathers, 10-17 decode. Every wait is bounded; a role
+// that gives up records DE_TIMEOUT and leaves its loop, and the CTA still meets at the final
+// barrier, where the TMEM is freed.
+#include "cwx_common.cuh"
+#include "decode.cuh"
+#include "kernels.cuh"
+
+namespace cwx {
+
+namespace mm {
+
+constexpr int NS = 3;             // operand stages (64 columns each)
+constexpr int NQ = 2;             // quantised-piece stages (256 columns each)
+constexpr int NMAX = 256;         // picks per column tile
+constexpr int A_BYTES = 128 * 128;
+constexpr int B_BYTES = NMAX * 128;
+constexpr int Q_BYTES = 128 * 110;  // 128 rows of the largest piece (IQ3_S)
+constexpr int XCH_BYTES = 32 * 64 * 4;
+constexpr int THREADS = 18 * 32;
+constexpr int W_MMA = 4, W_QCOPY = 5, W_GATHER = 6, N_GATHER = 4, W_DEC = 10, N_DEC = 8;
+constexpr int TMEM_COLS = 512;
+
+template <int FMT>
+struct Tab {
+    static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 16 : 512 * 8;
+};
+
+// shared memory: barriers, then 1024-aligned A and B stages, quantised stages, codebook, exchange
+struct Smem {
+    static constexpr int BAR = 0;
+    static constexpr int A = 1024;
+    static constexpr int B = A + NS * A_BYTES;
+    static constexpr int Q = B + NS * B_BYTES;
+    static constexpr int TAB = Q + NQ * Q_BYTES;
+    template <int FMT>
+    static constexpr int xch() { return TAB + Tab<FMT>::BYTES; }
+    template <int FMT>
+    static constexpr int total() { return xch<FMT>() + XCH_BYTES; }
+};
+
+struct Bars {
+    uint64_t full_q[NQ], empty_q[NQ];
+    uint64_t full_a[NS], full_b[NS], empty_s[NS];
+    uint64_t acc_full[2], acc_empty[2];
+    uint64_t mma_done;
+    uint32_t tmem;
+};
+static_assert(sizeof(Bars) <= 1024, "barrier block");
+
+// ---------------------------------------------------------------- tcgen05 / async-copy PTX
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem]^T, f16 inputs, f32 accumulate; acc = 0 overwrites D.
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// The mbarrier completes once every tcgen05 operation this thread issued before it has finished.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// 32 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// Arrives on bar once this thread's earlier cp.async copies have landed (counts toward the
+// barrier's expected arrivals).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sdesc(const void* p) {
+    const uint32_t a = smem_u32(p);
+    return (uint64_t)((a >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
+           ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, M = 128, N.
+__host__ __device__ constexpr uint32_t idesc_f16(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+// ---------------------------------------------------------------- work items
+// Items in order: per used expert, per column tile of NMAX picks, per row tile.
+struct Iter {
+    uint32_t u = 0xFFFFFFFFu;  // current used expert (none loaded yet)
+    uint32_t base = 0;         // items before expert u
+    uint32_t n_items = 0;      // items of expert u
+    uint32_t e = 0, first = 0, count = 0;
+};
+struct MItem {
+    uint32_t e, first, n0, ntok;
+    int mt;
+};
+
+__device__ __forceinline__ bool next_item(const MmaArgs& a, Iter& st, uint32_t i, uint32_t n_used, MItem* o) {
+    while (st.u == 0xFFFFFFFFu || i >= st.base + st.n_items) {
+        if (st.u != 0xFFFFFFFFu) st.base += st.n_items;
+        st.u = st.u == 0xFFFFFFFFu ? 0 : st.u + 1;
+        if (st.u >= n_used) return false;
+        st.e = a.used3[3 * st.u];
+        st.first = a.used3[3 * st.u + 1];
+        st.count = a.used3[3 * st.u + 2];
+        st.n_items = (st.count + NMAX - 1) / NMAX * (uint32_t)a.mtiles;
+    }
+    const uint32_t local = i - st.base;
+    const uint32_t nt = local / (uint32_t)a.mtiles;
+    o->mt = (int)(local % (uint32_t)a.mtiles);
+    o->e = st.e;
+    o->first = st.first;
+    o->n0 = nt * NMAX;
+    const uint32_t left = st.count - o->n0;
+    o->ntok = left < (uint32_t)NMAX ? left : (uint32_t)NMAX;
+    return true;
+}
+
+// Source of A rows 0-63 (half 0) and 64-127 (half 1) of row tile mt, piece kp.
+__device__ __forceinline__ const uint8_t* half_src(const MmaArgs& a, int half, uint32_t e, int mt, int kp) {
+    const MatRef& m = half == 0 || !a.fused ? a.a0 : a.a1;
+    const int64_t t = a.fused ? mt : 2 * mt + half;
+    const Layout& L = m.L;
+    return m.base + (int64_t)e * L.expert_bytes + t * L.full_tile_bytes + (int64_t)kp * pad16(64 * L.kp_row_bytes);
+}
+
+// ---------------------------------------------------------------- decode
+// 8 consecutive weights (chunk gi of the 64-column slice c4) of row r of a staged piece, as f16
+// (exact dequantised value rounded once), 16 bytes.
+__device__ __forceinline__ uint32_t u_h2(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 h2_u(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+__device__ __forceinline__ uint32_t sgn_pair(uint32_t s8, int q, uint32_t g) {
+    const uint32_t m = s8 * ((1u << (15 - q)) + (1u << (30 - q)));
+    return (m & 0x80008000u) ^ g;
+}
+// n in 0..15 -> (2n + 1) as an f16 pair, exact.
+__device__ __forceinline__ __half2 odd_h2(uint32_t n) {
+    return __hsub2(h2_u(n * 0x00020002u + 0x64016401u), __floats2half2_rn(1024.f, 1024.f));
+}
+
+template <int FMT>
+__device__ __forceinline__ uint4 dec_chunk(const uint8_t* q, int r, int c4, int gi, const uint8_t* tab) {
+    if (FMT == F_IQ2_S) {
+        const uint8_t* grp = q + (r >> 4) * (16 * 82);
+        const int rg = r & 15;
+        const uint4 Q = *reinterpret_cast<const uint4*>(grp + (rg * 4 + c4) * 16);
+        const uint32_t H = *reinterpret_cast<const uint32_t*>(grp + 1024 + (rg * 4 + c4) * 4);
+        const __half dh = __ushort_as_half(*reinterpret_cast<const uint16_t*>(grp + 1280 + 2 * rg));
+        const __half2 d2 = __half2half2(__hmul(dh, __float2half_rn(0.125f)));
+        const uint32_t qw = gi < 4 ? Q.x : Q.y, sw = gi < 4 ? Q.z : Q.w;
+        const uint32_t b = __byte_perm(qw, 0u, 0x4440 | (gi & 3));
+        const uint32_t idx = b | (((H >> (2 * gi)) & 3u) << 8);
+        const uint4 G = *reinterpret_cast<const uint4*>(tab + idx * 16);
+        const uint32_t s8 = __byte_perm(sw, 0u, 0x4440 | (gi & 3));
+        const __half2 od = odd_h2((H >> (16 + 4 * (gi >> 1))) & 0xFu);
+        uint4 o;
+        o.x = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 0, G.x)), od), d2));
+        o.y = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 2, G.y)), od), d2));
+        o.z = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 4, G.z)), od), d2));
+        o.w = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 6, G.w)), od), d2));
+        return o;
+    } else {
+        const uint8_t* grp = q + (r >> 4) * (16 * 110);
+        const int rg = r & 15;
+        const uint16_t qs2 = *reinterpret_cast<const uint16_t*>(grp + rg * 64 + 16 * c4 + 2 * gi);
+        const uint8_t s8 = grp[1024 + rg * 32 + 8 * c4 + gi];
+        const uint16_t qh = *reinterpret_cast<const uint16_t*>(grp + 1536 + rg * 8 + 2 * c4);
+        const uint8_t sc = grp[1664 + rg * 4 + c4];
+        const __half2 d2 = __half2half2(__ushort_as_half(*reinterpret_cast<const uint16_t*>(grp + 1728 + 2 * rg)));
+        const __half2 od = odd_h2((sc >> (4 * (gi >> 2))) & 0xFu);
+        const uint32_t i0 = (qs2 & 0xFFu) | (((qh >> (2 * gi)) & 1u) << 8);
+        const uint32_t i1 = (qs2 >> 8) | (((qh >> (2 * gi + 1)) & 1u) << 8);
+        const uint2 G0 = *reinterpret_cast<const uint2*>(tab + i0 * 8);
+        const uint2 G1 = *reinterpret_cast<const uint2*>(tab + i1 * 8);
+        uint4 o;
+        o.x = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 0, G0.x)), od), d2));
+        o.y = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 2, G0.y)), od), d2));
+        o.z = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 4, G1.x)), od), d2));
+        o.w = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 6, G1.y)), od), d2));
+        return o;
+    }
+}
+
+__device__ __forceinline__ float silu(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
+
+}  // namespace mm
+
+template <int FMT>
+__global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
+    using namespace mm;
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-aligned base (the swizzled operand tiles need it)
+    uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    Bars* bars = reinterpret_cast<Bars*>(smem + Smem::BAR);
+    uint8_t* sa = smem + Smem::A;
+    uint8_t* sb = smem + Smem::B;
+    uint8_t* sq = smem + Smem::Q;
+    uint8_t* tab = smem + Smem::TAB;
+    float* xch = reinterpret_cast<float*>(smem + Smem::xch<FMT>());
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < NQ; ++i) {
+            mbar_init(&bars->full_q[i], 1);
+            mbar_init(&bars->empty_q[i], N_DEC);
+        }
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&bars->full_a[i], N_DEC);
+            mbar_init(&bars->full_b[i], N_GATHER * 32);
+            mbar_init(&bars->empty_s[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bars->acc_full[i], 1);
+            mbar_init(&bars->acc_empty[i], 4);
+        }
+        mbar_init(&bars->mma_done, 1);
+        fence_mbar_init();
+    }
+    if (warp == W_MMA) {
+        tmem_alloc(&bars->tmem, TMEM_COLS);
+        tmem_relinquish();
+    }
+    if (warp >= W_DEC) {  // the codebook as f16 values: IQ2_S 8 per entry, IQ3_S 4
+        const int t = tid - W_DEC * 32;
+        if (FMT == F_IQ2_S) {
+            for (int e = t; e < 1024; e += N_DEC * 32) {
+                const uint64_t v = cwx_iq2s_expand(d_iq2s_codes[e]);
+                uint4 o;
+                o.x = u_h2(__floats2half2_rn((float)(v & 0xFF), (float)((v >> 8) & 0xFF)));
+                o.y = u_h2(__floats2half2_rn((float)((v >> 16) & 0xFF), (float)((v >> 24) & 0xFF)));
+                o.z = u_h2(__floats2half2_rn((float)((v >> 32) & 0xFF), (float)((v >> 40) & 0xFF)));
+                o.w = u_h2(__floats2half2_rn((float)((v >> 48) & 0xFF), (float)(v >> 56)));
+                *reinterpret_cast<uint4*>(tab + e * 16) = o;
+            }
+        } else {
+            for (int e = t; e < 512; e += N_DEC * 32) {
+                const uint32_t v = cwx_iq3s_expand(d_iq3s_codes[e]);
+                *reinterpret_cast<uint2*>(tab + e * 8) =
+                    make_uint2(u_h2(__floats2half2_rn((float)(v & 0xFF), (float)((v >> 8) & 0xFF))),
+                               u_h2(__floats2half2_rn((float)((v >> 16) & 0xFF), (float)(v >> 24))));
+            }
+        }
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    const uint32_t tmem = bars->tmem;
+    const uint32_t n_used = *a.n_used;
+    const int n_kp = a.a0.L.n_kp;
+    const int nks = 4 * n_kp;  // 64-column stages per item
+
+    if (warp == W_MMA) {
+        // ---------------- MMA issue (one thread)
+        if (lane == 0) {
+            Iter it;
+            MItem m;
+            uint32_t c = 0;  // stage counter
+            bool ok = true;
+            int li = 0;
+            for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m); i += gridDim.x, ++li) {
+                const int buf = li & 1;
+                const uint32_t use = (uint32_t)li >> 1;
+                if (use > 0 && !mbar_wait(&bars->acc_empty[buf], (use - 1) & 1, a.err)) {
+                    ok = false;
+                    break;
+                }
+                tc_after();
+                const int npad = ((int)m.ntok + 15) & ~15;
+                const uint32_t idesc = idesc_f16(npad);
+                const uint32_t d = tmem + (uint32_t)buf * 256;
+                for (int ks = 0; ks < nks; ++ks, ++c) {
+                    const int s = (int)(c % NS);
+                    const uint32_t ph = (c / NS) & 1;
+                    if (!mbar_wait(&bars->full_a[s], ph, a.err) || !mbar_wait(&bars->full_b[s], ph, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_after();
+                    fence_async_smem();  // the gathered activations were written by cp.async
+                    const uint8_t* at = sa + s * A_BYTES;
+                    const uint8_t* bt = sb + s * B_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma(d, sdesc(at + 32 * kk), sdesc(bt + 32 * kk), idesc, (ks | kk) != 0);
+                    tc_commit(&bars->empty_s[s]);
+                }
+                if (!ok) break;
+                tc_commit(&bars->acc_full[buf]);
+            }
+            // every MMA issued has finished before the TMEM is freed
+            tc_commit(&bars->mma_done);
+            mbar_wait(&bars->mma_done, 0, a.err);
+        }
+        __syncwarp();
+    } else if (warp == W_QCOPY) {
+        // ---------------- quantised pieces: two 64-row halves per piece, one bulk copy each
+        Iter it;
+        MItem m;
+        uint32_t p = 0;
+        const int64_t hb0 = 64 * a.a0.L.kp_row_bytes, hb1 = 64 * (a.fused ? a.a1 : a.a0).L.kp_row_bytes;
+        bool ok = true;
+        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m); i += gridDim.x) {
+            for (int kp = 0; kp < n_kp; ++kp, ++p) {
+                const int s = (int)(p % NQ);
+                const uint32_t use = p / NQ;
+                if (use > 0 && !mbar_wait(&bars->empty_q[s], (use - 1) & 1, a.err)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) mbar_expect_tx(&bars->full_q[s], (uint32_t)(hb0 + hb1));
+                __syncwarp();
+                uint8_t* dst = sq + s * Q_BYTES;
+                if (lane == 0) bulk_g2s(dst, half_src(a, 0, m.e, m.mt, kp), (uint32_t)hb0, &bars->full_q[s]);
+                if (lane == 1) bulk_g2s(dst + hb0, half_src(a, 1, m.e, m.mt, kp), (uint32_t)hb1, &bars->full_q[s]);
+            }
+        }
+        // the copies in flight land before the CTA ends
+        for (uint32_t q = p > NQ ? p - NQ : 0; q < p; ++q) mbar_wait(&bars->full_q[q % NQ], (q / NQ) & 1, a.err);
+    } else if (warp >= W_GATHER && warp < W_GATHER + N_GATHER) {
+        // ---------------- activation rows: chunk i = t + 128 j (j < 16) of a stage is row i / 8,
+        // 16-byte chunk i % 8 (so 8 threads read one row's 128 contiguous bytes)
+        const int t = tid - W_GATHER * 32;
+        Iter it;
+        MItem m;
+        uint32_t c = 0;
+        bool ok = true;
+        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m); i += gridDim.x) {
+            const uint8_t* src[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const uint32_t n = (uint32_t)(t >> 3) + 16 * j;
+                src[j] = nullptr;
+                if (n < m.ntok) {
+                    const uint32_t p = a.pairs[m.first + m.n0 + n];
+                    src[j] = a.b + (int64_t)(p / (uint32_t)a.bdiv) * a.bstride + 16 * (t & 7);
+                }
+            }
+            for (int ks = 0; ks < nks; ++ks, ++c) {
+                const int s = (int)(c % NS);
+                const uint32_t use = c / NS;
+                if (lane == 0 && use > 0 && !mbar_wait(&bars->empty_s[s], (use - 1) & 1, a.err)) ok = false;
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                uint8_t* bt = sb + s * B_BYTES;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int n = (t >> 3) + 16 * j, ch = t & 7;
+                    if (src[j]) cp_async16(bt + n * 128 + ((ch ^ (n & 7)) << 4), src[j] + (int64_t)ks * 128);
+                }
+                cp_async_arrive(&bars->full_b[s]);
+            }
+        }
+        cp_async_wait_all();
+    } else if (warp >= W_DEC) {
+        // ---------------- decode: chunk i = t + 256 j (j < 4) of a stage is row i / 8, chunk i % 8
+        const int t = tid - W_DEC * 32;
+        Iter it;
+        MItem m;
+        uint32_t c = 0, p = 0;
+        bool ok = true;
+        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m); i += gridDim.x) {
+            for (int kp = 0; kp < n_kp && ok; ++kp, ++p) {
+                const int qs = (int)(p % NQ);
+                if (!mbar_wait(&bars->full_q[qs], (p / NQ) & 1, a.err)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* q = sq + qs * Q_BYTES;
+                for (int c4 = 0; c4 < 4; ++c4, ++c) {
+                    const int s = (int)(c % NS);
+                    const uint32_t use = c / NS;
+                    if (lane == 0 && use > 0 && !mbar_wait(&bars->empty_s[s], (use - 1) & 1, a.err)) ok = false;
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) break;
+                    uint8_t* at = sa + s * A_BYTES;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int r = (t >> 3) + 32 * j, gi = t & 7;
+                        const uint4 w = dec_chunk<FMT>(q, r, c4, gi, tab);
+                        *reinterpret_cast<uint4*>(at + r * 128 + ((gi ^ (r & 7)) << 4)) = w;
+                    }
+                    fence_async_smem();  // the tensor cores read the tile through the async proxy
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->full_a[s]);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->empty_q[qs]);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 0-3: TMEM lanes 32 w .. 32 w + 31 = A rows)
+        Iter it;
+        MItem m;
+        int li = 0;
+        for (uint32_t i = blockIdx.x; next_item(a, it, i, n_used, &m); i += gridDim.x, ++li) {
+            const int buf = li & 1;
+            if (!mbar_wait(&bars->acc_full[buf], ((uint32_t)li >> 1) & 1, a.err)) break;
+            tc_after();
+            const uint32_t* pk = a.pairs + m.first + m.n0;
+            const int nch = ((int)m.ntok + 31) >> 5;
+            for (int cc = 0; cc < nch; ++cc) {
+                uint32_t r[32];
+                tc_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(buf * 256 + cc * 32), r);
+                tc_wait_ld();
+                if (a.fused) {
+                    // up rows (lanes 64-127) go through shared memory to the gate rows' threads
+                    if (warp >= 2)
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) xch[j * 64 + (warp - 2) * 32 + lane] = __uint_as_float(r[j]);
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    if (warp < 2) {
+                        const int64_t f = (int64_t)m.mt * 64 + warp * 32 + lane;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int col = cc * 32 + j;
+                            if (col < (int)m.ntok) {
+                                const float g = __uint_as_float(r[j]);
+                                const float u = xch[j * 64 + warp * 32 + lane];
+                                const float h = __fmul_rn(silu(g), u);
+                                a.hout[(int64_t)pk[col] * a.ostride + f] = __float2half_rn(h);
+                            }
+                        }
+                    }
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                } else {
+                    const int64_t f = (int64_t)m.mt * 128 + warp * 32 + lane;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int col = cc * 32 + j;
+                        if (col < (int)m.ntok) a.out[(int64_t)pk[col] * a.ostride + f] = __uint_as_float(r[j]);
+                    }
+                }
+            }
+            tc_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
+        }
+    }
+    tc_before();
+    __syncthreads();
+    tc_after();
+    if (warp == W_MMA) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// x (R, K) f32 -> f16 rows (the activation rows of the fused gate/up products).
+__global__ void __launch_bounds__(256) k_f16rows(const float* __restrict__ x, int64_t n, __half* __restrict__ y) {
+    const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i + 3 < n) {
+        const float4 v = *reinterpret_cast<const float4*>(x + i);
+        *reinterpret_cast<__half2*>(y + i) = __floats2half2_rn(v.x, v.y);
+        *reinterpret_cast<__half2*>(y + i + 2) = __floats2half2_rn(v.z, v.w);
+    } else {
+        for (int64_t j = i; j < n; ++j) y[j] = __float2half_rn(x[j]);
+    }
+}
+
+int launch_f16rows(const float* x, int64_t n, __half* y, cudaStream_t st) {
+    if (n <= 0) return CWX_OK;
+    const int64_t blocks = (n / 4 + 255) / 256 + 1;
+    k_f16rows<<<(unsigned)blocks, 256, 0, st>>>(x, n, y);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_f16rows");
+}
+
+// Which launches can take the tensor-core path: IQ2_S / IQ3_S weights in full 64-row tiles and
+// whole 256-column pieces, gate and up of one format and shape.
+bool mma_supports(const MmaArgs& a) {
+    const Layout& L = a.a0.L;
+    if (L.fmt != F_IQ2_S && L.fmt != F_IQ3_S) return false;
+    if (L.k % PIECE_K || L.n % (a.fused ? 64 : 128)) return false;
+    if (a.fused) {
+        const Layout& U = a.a1.L;
+        if (U.fmt != L.fmt || U.n != L.n || U.k != L.k) return false;
+    }
+    if (a.bstride % 16 || ((uintptr_t)a.b & 15)) return false;
+    return true;
+}
+
+int launch_mma(const MmaArgs& in, int device, int sm_count, cudaStream_t st) {
+    MmaArgs a = in;
+    if (!mma_supports(a)) return fail(CWX_EUNSUPPORTED, "tensor-core expert products: unsupported layout");
+    a.mtiles = (int)(a.fused ? a.a0.L.n / 64 : a.a0.L.n / 128);
+    const int fmt = a.a0.L.fmt;
+    const int smem = (fmt == F_IQ2_S ? mm::Smem::total<F_IQ2_S>() : mm::Smem::total<F_IQ3_S>()) + 1024;
+    static int attr_set[64][2] = {{0}};
+    const int fi = fmt == F_IQ2_S ? 0 : 1;
+    if (device < 0 || device >= 64 || !attr_set[device][fi]) {
+        cudaError_t e = fmt == F_IQ2_S
+                            ? cudaFuncSetAttribute(k_mma<F_IQ2_S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
+                            : cudaFuncSetAttribute(k_mma<F_IQ3_S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_mma)");
+        if (device >= 0 && device < 64) attr_set[device][fi] = 1;
+    }
+    const unsigned grid = (unsigned)(sm_count > 0 ? sm_count : 1);
+    if (fmt == F_IQ2_S) k_mma<F_IQ2_S><<<grid, mm::THREADS, smem, st>>>(a);
+    else k_mma<F_IQ3_S><<<grid, mm::THREADS, smem, st>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_mma");
+}
+
+}  // namespace cwx

@@ -186,6 +186,11 @@ int cwx_moe_forward(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_moe_args
 #define CWX_PHASE_COMBINE 6 /* weighted combine + shared expert + residual */
 #define CWX_N_PHASES 7
 int cwx_ctx_set_profiling(cwx_ctx* ctx, int enabled);
+/* Layers whose routed banks are all IQ2_S / IQ3_S (SiLU, hidden and inter multiples of 256) run
+ * their routed products on the tensor cores (tcgen05) when the batch gives at least min_pile
+ * picks per expert on average (tokens * top_k / n_experts, rounded up); smaller batches use the
+ * grouped mma.sync products. Default 32; 0 keeps every batch on the mma.sync products. */
+int cwx_ctx_set_mma_min_pile(cwx_ctx* ctx, int min_pile);
 /* Synchronises the device; adds each recorded phase's elapsed milliseconds into ms[phase] and
  * its occurrences into count[phase] (arrays of CWX_N_PHASES; either may be NULL); keeps the
  * recorded events, so a replayed graph can be read again after each replay. */

@@ -28,8 +28,12 @@ def _lib():
     from coachwhip_b200 import _lib
 
     _lib.lib()
+    # this module covers the grouped mma.sync products at every batch size; the tensor-core
+    # products of large IQ piles have their own module (test_mma.py)
+    _lib.set_mma_min_pile(0, 0)
     yield
     _lib.status(0)
+    _lib.set_mma_min_pile(0, 32)
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
@@ -215,10 +219,22 @@ SPECS = {
 }
 
 
+# T = 256 and 1500: piles of 16 and more picks on average take passes of 16 or 32 picks (two or
+# four n-tiles per decoded weight fragment); 1500 leaves ragged last passes
 @pytest.mark.parametrize("name", list(SPECS))
-@pytest.mark.parametrize("T", [1, 5, 64])
+@pytest.mark.parametrize("T", [1, 5, 64, 256])
 @pytest.mark.parametrize("mode", [O.MODE_CANDLE, O.MODE_F32])
 def test_moe_forward_matches_oracle(name, T, mode):
+    _moe_case(name, T, mode)
+
+
+@pytest.mark.parametrize("name", ["iq_mix", "iq3_q4k", "mxfp4_gptoss"])
+@pytest.mark.parametrize("mode", [O.MODE_CANDLE, O.MODE_F32])
+def test_moe_forward_prefill_piles(name, mode):
+    _moe_case(name, 1500, mode)
+
+
+def _moe_case(name, T, mode):
     s = SPECS[name]
     L = build_cpu(s)
     x = make_input(s, T)
