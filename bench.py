@@ -51,6 +51,7 @@ def parse():
     p.add_argument("--layers", type=int, default=LAYERS)
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--no-prefill", action="store_true")
     return p.parse_args()
 
 
@@ -291,6 +292,50 @@ def impl_reference(a, rank, world):
     print(json.dumps(line), flush=True)
 
 
+PREFILL_T = [1500, 4096]
+
+
+def layer_flops(T):
+    """Multiply-add FLOPs of one config-1 layer on T tokens: routed gate/up/down, shared expert, router."""
+    return 2 * T * K * 3 * H * I + 2 * T * 3 * H * I_S + 2 * T * H * E
+
+
+def prefill_runs(mods, Ts, a, dev, pk, maxall, barrier, world):
+    """Config 2: the 40-layer stack on 1500 and 4096 tokens (CUDA graphs), with the per-phase event
+    times of one replay; the routed products run on the tensor-core kernel (k_mma)."""
+    import torch
+
+    from coachwhip_b200 import _lib
+
+    out = {}
+    ctx = _lib.ctx(dev.index)
+    # the products run inside a long step: the sustained (power-capped) dense bf16 figure
+    tpk = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    for T in Ts:
+        x = synth_f32(T * H, stream(3, 0, T_IN), 1.0, dev).view(1, T, H)
+        g, _ = capture(mods, x, dev)
+        barrier()
+        ms = maxall(time_graph(g, max(3, a.steps // 4), a.warmup, dev))
+        del g
+        _lib.lib().cwx_ctx_reset_profile(ctx)
+        _lib.lib().cwx_ctx_set_profiling(ctx, 1)
+        run_stack(mods, x)
+        _lib.lib().cwx_ctx_set_profiling(ctx, 0)
+        msv, _ = _lib.read_profile(dev.index)
+        _lib.lib().cwx_ctx_reset_profile(ctx)
+        ph = {n: msv[i] for i, n in enumerate(_lib.PHASES)}
+        fl = len(mods) * layer_flops(T)
+        prod_fl = len(mods) * (2 * T * K * 3 * H * I + 2 * T * 3 * H * I_S)
+        prod_ms = ph["gate_up"] + ph["down"]
+        out[str(T)] = {"tokens_per_s": world * T / (ms / 1e3), "ms_per_step": ms, "layers": len(mods),
+                       "tflops": fl / (ms / 1e3) / 1e12, "frac_bf16_sustained_peak": fl / (ms / 1e3) / 1e12 / tpk,
+                       "products_tflops": prod_fl / (prod_ms / 1e3) / 1e12, "phase_ms_eager": ph,
+                       "path": "tcgen05 grouped products (k_mma) for the routed experts, mma.sync for the shared expert"}
+        print(f"[bench] prefill {T}: {ms:.3f} ms/step, {out[str(T)]['tokens_per_s']:.0f} tokens/s, "
+              f"{out[str(T)]['tflops']:.1f} TFLOP/s", file=sys.stderr, flush=True)
+    return out
+
+
 def main():
     a = parse()
     rank, world, local = dist_setup()
@@ -325,8 +370,9 @@ def main():
         return float(t.item())
 
     batches = [a.batch] if a.no_sweep else sorted({1, 4, 16, 64, a.batch})
+    prefill_T = [] if a.no_prefill else PREFILL_T
     for m in mods:
-        m.reserve(max(batches))  # one workspace for every captured graph
+        m.reserve(max(batches + prefill_T))  # one workspace for every captured graph
     sweep, graphs = {}, {}
     head = None
     ctx = _lib.ctx(local)
@@ -427,6 +473,8 @@ def main():
     e2e_ms = maxall(e0.elapsed_time(e1) / e_steps)
     _lib.status(local)
 
+    prefill = prefill_runs(mods, prefill_T, a, dev, pk, maxall, barrier, world)
+
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
         cpu = cpu_baseline(store, T)
@@ -442,7 +490,8 @@ def main():
                         "path": "StreamedMoe.forward x 40 via ctypes -> cwx_moe_forward"},
                 "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
                 "gpu_launches": int(launches_per_step * a.steps),
-                "decode_sweep": {str(b): d for b, d in sweep.items()}}
+                "decode_sweep": {str(b): d for b, d in sweep.items()},
+                "prefill": prefill}
         print(json.dumps(line), flush=True)
     graphs.clear()
     if world > 1:

@@ -20,7 +20,7 @@ EXPORTS = [
     "cwx_bank_create", "cwx_bank_synth", "cwx_bank_destroy", "cwx_bank_desc", "cwx_bank_download",
     "cwx_bank_dequantize", "cwx_synth_normal", "cwx_route", "cwx_permute", "cwx_permute_noalloc", "cwx_expert_matmul", "cwx_moe_forward",
     "cwx_ctx_set_profiling", "cwx_ctx_read_profile", "cwx_ctx_reset_profile", "cwx_ctx_launches",
-    "cwx_ctx_set_mma_min_pile",
+    "cwx_ctx_set_mma_min_pile", "cwx_ep_dispatch", "cwx_ep_experts", "cwx_ep_combine",
 ]
 PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine"]
 
@@ -47,6 +47,10 @@ class MoeLayer(ctypes.Structure):
         ("sh_gate", ctypes.c_void_p), ("sh_up", ctypes.c_void_p), ("sh_down", ctypes.c_void_p),
         ("sh_gate_inp", ctypes.c_void_p), ("act_mode", ctypes.c_int32),
     ]
+
+
+class EpGroup(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("experts_per_rank", ctypes.c_int32)]
 
 
 class MoeArgs(ctypes.Structure):
@@ -97,6 +101,10 @@ def lib() -> ctypes.CDLL:
             "cwx_ctx_reset_profile": (I32, [P]),
             "cwx_ctx_launches": (I64, [P]),
             "cwx_ctx_set_mma_min_pile": (I32, [P, I32]),
+            "cwx_ep_dispatch": (I32, [P, ctypes.POINTER(MoeLayer), ctypes.POINTER(EpGroup), P, I32, P, P, P, P, P, P,
+                                      P, P]),
+            "cwx_ep_experts": (I32, [P, ctypes.POINTER(MoeLayer), ctypes.POINTER(EpGroup), P, P, I32, P, P]),
+            "cwx_ep_combine": (I32, [P, ctypes.POINTER(MoeLayer), P, I32, P, P, P, P, P, P, P]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)

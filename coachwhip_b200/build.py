@@ -15,7 +15,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libcwx.so")
-SOURCES = ["api.cu", "bank.cu", "route.cu", "gemv.cu", "act.cu", "noalloc.cu", "mma.cu"]
+SOURCES = ["api.cu", "bank.cu", "route.cu", "gemv.cu", "act.cu", "noalloc.cu", "mma.cu", "ep.cu"]
 NO_FMA = {"bank.cu"}
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

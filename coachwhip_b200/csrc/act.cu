@@ -143,15 +143,19 @@ __global__ void __launch_bounds__(256) k_prep(PrepPair pp) {
 }
 
 // out[t] = sum_j w[t][j] * rows[t*K + j] (pick order, from 0) + sgate[t] * shared[t] + residual[t]
-__global__ void __launch_bounds__(256) k_combine(const float* __restrict__ rows, const float* __restrict__ w,
-                                                 int T, int K, int H, const float* __restrict__ shared,
-                                                 const float* __restrict__ sgate, const float* __restrict__ residual,
-                                                 float* __restrict__ out) {
+// rows are indexed by pick (t*K + j), or through idx (row of pick p = idx[p]) when idx is set.
+__global__ void __launch_bounds__(256) k_combine(const float* __restrict__ rows, const uint32_t* __restrict__ idx,
+                                                 const float* __restrict__ w, int T, int K, int H,
+                                                 const float* __restrict__ shared, const float* __restrict__ sgate,
+                                                 const float* __restrict__ residual, float* __restrict__ out) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)T * H) return;
     const int64_t t = i / H, c = i % H;
     float acc = 0.f;
-    for (int j = 0; j < K; ++j) acc = __fadd_rn(acc, __fmul_rn(rows[(t * K + j) * H + c], w[t * K + j]));
+    for (int j = 0; j < K; ++j) {
+        const int64_t p = t * K + j, r = idx ? (int64_t)idx[p] : p;
+        acc = __fadd_rn(acc, __fmul_rn(rows[r * H + c], w[p]));
+    }
     if (shared) acc = __fadd_rn(acc, __fmul_rn(shared[t * H + c], sgate[t]));
     if (residual) acc = __fadd_rn(acc, residual[i]);
     out[i] = acc;
@@ -176,10 +180,10 @@ int launch_prep2(const PrepArgs* p, int njobs, cudaStream_t st) {
 int launch_prep(const PrepArgs& p, cudaStream_t st) { return launch_prep2(&p, 1, st); }
 
 int launch_combine(const float* rows, const float* w, int T, int K, int H, const float* shared, const float* sgate,
-                   const float* residual, float* out, cudaStream_t st) {
+                   const float* residual, float* out, cudaStream_t st, const uint32_t* idx) {
     if (T == 0) return CWX_OK;
     const int64_t n = (int64_t)T * H;
-    k_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, w, T, K, H, shared, sgate, residual, out);
+    k_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, idx, w, T, K, H, shared, sgate, residual, out);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_combine");
 }

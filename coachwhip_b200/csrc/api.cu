@@ -573,6 +573,7 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
         g.fused = 1;
         g.b = reinterpret_cast<const uint8_t*>(p.x16);
         g.bstride = (int64_t)H * 2;
+        g.brows = T;
         g.bdiv = K;
         g.hout = p.h16;
         g.ostride = I;
@@ -597,6 +598,7 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
         d.fused = 0;
         d.b = reinterpret_cast<const uint8_t*>(p.h16);
         d.bstride = (int64_t)I * 2;
+        d.brows = (int64_t)T * K;
         d.bdiv = 1;
         d.out = p.y;
         d.ostride = H;
@@ -665,5 +667,166 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
     if (A->weights_out) CWX_CUDA(cudaMemcpyAsync(A->weights_out, p.w, n * 4, cudaMemcpyDeviceToDevice, st));
     if (A->pairs_out) CWX_CUDA(cudaMemcpyAsync(A->pairs_out, p.pairs, n * 4, cudaMemcpyDeviceToDevice, st));
     if (A->heads_out) CWX_CUDA(cudaMemcpyAsync(A->heads_out, p.heads, (size_t)3 * E * 4, cudaMemcpyDeviceToDevice, st));
+    return CWX_OK;
+}
+
+// ---------------------------------------------------------------- expert parallelism
+// The three per-rank steps of an expert-parallel layer; the caller moves the rows between them
+// with two all-to-all exchanges (counts first, so every rank knows its receive sizes).
+
+static int ep_check(const cwx_moe_layer* L, const cwx_ep_group* g, const char* who) {
+    if (!L || !g) return fail(CWX_EINVAL, "%s: null layer or group", who);
+    if (g->world < 1 || g->rank < 0 || g->rank >= g->world || g->experts_per_rank < 1)
+        return fail(CWX_EINVAL, "%s: bad group (world %d, rank %d, %d experts per rank)", who, g->world, g->rank,
+                    g->experts_per_rank);
+    if ((int64_t)g->world * g->experts_per_rank != L->n_experts)
+        return fail(CWX_EINVAL, "%s: %d ranks x %d experts do not cover n_experts=%d", who, g->world,
+                    g->experts_per_rank, L->n_experts);
+    if (!L->gate || !L->up || !L->down || L->gate->L.n_experts != g->experts_per_rank ||
+        L->up->L.n_experts != g->experts_per_rank || L->down->L.n_experts != g->experts_per_rank)
+        return fail(CWX_EINVAL, "%s: the banks must hold this rank's %d experts", who, g->experts_per_rank);
+    return CWX_OK;
+}
+
+extern "C" int cwx_ep_dispatch(cwx_ctx* c, const cwx_moe_layer* L, const cwx_ep_group* g, const float* x,
+                               int32_t tokens, uint32_t* ids, float* weights, uint32_t* pairs, float* sgate,
+                               float* send_rows, uint32_t* send_eids, int32_t* send_counts, void* stream) {
+    if (!c) return fail(CWX_EINVAL, "cwx_ep_dispatch: null context");
+    int rc = ep_check(L, g, "cwx_ep_dispatch");
+    if (rc) return rc;
+    if (!L->router_w || L->top_k < 1 || L->top_k > 16 || L->top_k > L->n_experts || L->n_experts > 1024)
+        return fail(CWX_EINVAL, "cwx_ep_dispatch: router or top_k out of range");
+    if (tokens < 0) return fail(CWX_EINVAL, "cwx_ep_dispatch: tokens %d", tokens);
+    if (!send_counts || (tokens && (!x || !ids || !weights || !pairs || !send_rows || !send_eids)))
+        return fail(CWX_EINVAL, "cwx_ep_dispatch: null argument");
+    const bool shared = L->sh_gate != nullptr;
+    if (shared && tokens && !sgate) return fail(CWX_EINVAL, "cwx_ep_dispatch: the shared expert needs sgate");
+    CWX_CUDA(cudaSetDevice(c->device));
+    cudaStream_t st = (cudaStream_t)stream;
+    const int T = tokens, H = L->hidden, E = L->n_experts, K = L->top_k;
+    const int64_t n = (int64_t)T * K;
+    Carve cv{nullptr, 0};
+    for (int pass = 0; pass < 2; ++pass) {
+        cv = Carve{pass ? c->ws : nullptr, 0};
+        cv.take<float>((size_t)T * E + 1);
+        cv.take<uint32_t>((size_t)3 * E);
+        cv.take<uint32_t>((size_t)3 * E);
+        cv.take<uint32_t>(4);
+        cv.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
+        if (!pass && (rc = ensure_ws(c, cv.off + 256, st))) return rc;
+    }
+    Carve w{c->ws, 0};
+    float* logits = w.take<float>((size_t)T * E + 1);
+    uint32_t* heads = w.take<uint32_t>((size_t)3 * E);
+    uint32_t* used3 = w.take<uint32_t>((size_t)3 * E);
+    uint32_t* n_used = w.take<uint32_t>(4);
+    uint32_t* perm = w.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
+    if (T > 0) {
+        if ((rc = launch_router(x, L->router_w, L->router_b, T, H, E, logits, st))) return rc;
+        if ((rc = launch_route(logits, T, E, K, L->norm_topk_prob, ids, weights, x,
+                               shared ? L->sh_gate_inp : nullptr, H, shared ? sgate : nullptr, st)))
+            return rc;
+        if ((rc = launch_permute(ids, n, E, pairs, heads, used3, n_used, perm, c->d_err, st))) return rc;
+        c->launches += 2 + perm_launches(n, E);
+    } else {
+        CWX_CUDA(cudaMemsetAsync(heads, 0, (size_t)3 * E * 4, st));
+    }
+    if ((rc = launch_ep_counts(heads, E, g->experts_per_rank, g->world, send_counts, st))) return rc;
+    if ((rc = launch_ep_pack(x, H, K, ids, pairs, n, g->experts_per_rank, send_rows, send_eids, st))) return rc;
+    c->launches += n > 0 ? 2 : 1;
+    return CWX_OK;
+}
+
+extern "C" int cwx_ep_experts(cwx_ctx* c, const cwx_moe_layer* L, const cwx_ep_group* g, const float* rows,
+                              const uint32_t* eids, int32_t n_rows, float* y_rows, void* stream) {
+    if (!c) return fail(CWX_EINVAL, "cwx_ep_experts: null context");
+    int rc = ep_check(L, g, "cwx_ep_experts");
+    if (rc) return rc;
+    if (n_rows < 0) return fail(CWX_EINVAL, "cwx_ep_experts: n_rows %d", n_rows);
+    if (n_rows == 0) return CWX_OK;
+    if (!rows || !eids || !y_rows) return fail(CWX_EINVAL, "cwx_ep_experts: null argument");
+    // this rank's experts as a layer of their own: one pick per row, no router, no shared expert
+    cwx_moe_layer lc = *L;
+    lc.n_experts = g->experts_per_rank;
+    lc.top_k = 1;
+    lc.sh_gate = lc.sh_up = lc.sh_down = nullptr;
+    lc.sh_gate_inp = nullptr;
+    if ((rc = validate_layer(&lc))) return rc;
+    CWX_CUDA(cudaSetDevice(c->device));
+    cudaStream_t st = (cudaStream_t)stream;
+    const int mma = mma_layer(c, &lc, n_rows) ? 1 : 0;
+    LayerPlan p;
+    plan_layer(&lc, n_rows, mma, nullptr, &p);
+    if ((rc = ensure_ws(c, p.bytes, st))) return rc;
+    plan_layer(&lc, n_rows, mma, c->ws, &p);
+    p.ids = const_cast<uint32_t*>(eids);  // per-row expert (the clamped SwiGLU biases index it)
+    p.y = y_rows;                          // down rows straight into the caller's buffer
+    if ((rc = launch_permute(eids, n_rows, lc.n_experts, p.pairs, p.heads, p.used3, p.n_used, p.perm, c->d_err, st)))
+        return rc;
+    c->launches += perm_launches(n_rows, lc.n_experts);
+    cwx_moe_args a;
+    memset(&a, 0, sizeof a);
+    a.x = rows;
+    a.tokens = n_rows;
+    return p.mma ? moe_mma(c, &lc, &a, p, st) : moe_gemv(c, &lc, &a, p, st);
+}
+
+extern "C" int cwx_ep_combine(cwx_ctx* c, const cwx_moe_layer* L, const float* x, int32_t tokens,
+                              const float* weights, const uint32_t* pairs, const float* back_rows, const float* sgate,
+                              const float* residual, float* out, void* stream) {
+    if (!c || !L) return fail(CWX_EINVAL, "cwx_ep_combine: null argument");
+    if (tokens < 0) return fail(CWX_EINVAL, "cwx_ep_combine: tokens %d", tokens);
+    if (tokens == 0) return CWX_OK;
+    if (!x || !weights || !pairs || !back_rows || !out) return fail(CWX_EINVAL, "cwx_ep_combine: null argument");
+    const bool shared = L->sh_gate != nullptr;
+    if (shared && (!sgate || !L->sh_up || !L->sh_down || !L->sh_gate_inp))
+        return fail(CWX_EINVAL, "cwx_ep_combine: incomplete shared expert");
+    CWX_CUDA(cudaSetDevice(c->device));
+    cudaStream_t st = (cudaStream_t)stream;
+    const int T = tokens, H = L->hidden, K = L->top_k;
+    const int64_t n = (int64_t)T * K;
+    LayerPlan p;
+    memset(&p, 0, sizeof p);
+    p.T = T;
+    p.H = H;
+    p.K = K;
+    p.Is = shared ? (int)L->sh_gate->L.n : 0;
+    p.msgu = shared ? act_mode_of(L->sh_gate, L->act_mode) : -1;
+    p.msd = shared ? act_mode_of(L->sh_down, L->act_mode) : -1;
+    size_t need = 0;
+    for (int pass = 0; pass < 2; ++pass) {
+        Carve w{pass ? c->ws : nullptr, 0};
+        uint32_t* inv = w.take<uint32_t>((size_t)n);
+        p.n_used = w.take<uint32_t>(4);
+        p.used3 = w.take<uint32_t>(4);
+        p.pairs = p.n_used;
+        if (shared) {
+            p.xpk[p.msgu] = w.take<uint8_t>((size_t)(T * packed_row_bytes(H)));
+            p.gs = w.take<float>((size_t)T * p.Is);
+            p.us = w.take<float>((size_t)T * p.Is);
+            p.hspk = w.take<uint8_t>((size_t)(T * packed_row_bytes(p.Is)));
+            p.ys = w.take<float>((size_t)T * H);
+        }
+        if (!pass) {
+            need = w.off + 256;
+            int rc = ensure_ws(c, need, st);
+            if (rc) return rc;
+            continue;
+        }
+        int rc;
+        CWX_CUDA(cudaMemsetAsync(p.n_used, 0, 16, st));  // the shared-only product launches read it
+        if ((rc = launch_inverse(pairs, n, inv, st))) return rc;
+        c->launches += 1;
+        if (shared) {
+            if ((rc = launch_prep(prep(x, nullptr, T, H, p.msgu, p.xpk[p.msgu]), st))) return rc;
+            if ((rc = shared_gemv(c, L, p, 0, st))) return rc;
+            if ((rc = launch_prep(prep(p.gs, p.us, T, p.Is, p.msd, p.hspk), st))) return rc;
+            if ((rc = shared_gemv(c, L, p, 1, st))) return rc;
+            c->launches += 4;
+        }
+        if ((rc = launch_combine(back_rows, weights, T, K, H, shared ? p.ys : nullptr, sgate, residual, out, st, inv)))
+            return rc;
+        c->launches += 1;
+    }
     return CWX_OK;
 }

@@ -1,6 +1,8 @@
 // Argument blocks and host launchers of the cwx kernels (route.cu, gemv.cu, act.cu), used by
 // api.cu.
 #pragma once
+#include <cuda.h>
+
 #include "cwx_common.cuh"
 
 namespace cwx {
@@ -75,16 +77,26 @@ struct PrepArgs {
 int launch_prep(const PrepArgs& p, cudaStream_t st);
 int launch_prep2(const PrepArgs* p, int njobs, cudaStream_t st);  // up to two preparations in one launch
 int launch_combine(const float* rows, const float* w, int T, int K, int H, const float* shared, const float* sgate,
-                   const float* residual, float* out, cudaStream_t st);
+                   const float* residual, float* out, cudaStream_t st, const uint32_t* idx = nullptr);
+
+// Expert parallelism (ep.cu): the picks in pile order grouped by the rank that owns their expert.
+// send_rows[pos] = x[pairs[pos] / K], send_eids[pos] = the expert's index on its rank.
+int launch_ep_pack(const float* x, int H, int K, const uint32_t* ids, const uint32_t* pairs, int64_t n, int epr,
+                   float* send_rows, uint32_t* send_eids, cudaStream_t st);
+// counts[d] = picks for rank d (from the pile heads); inv[pairs[pos]] = pos.
+int launch_ep_counts(const uint32_t* heads, int E, int epr, int world, int32_t* counts, cudaStream_t st);
+int launch_inverse(const uint32_t* pairs, int64_t n, uint32_t* inv, cudaStream_t st);
 // experts_est: the number of experts expected to have picks (sizes the grid and the K split).
 int launch_gemv(const GemvArgs& a, int64_t experts_est, int device, int sm_count, cudaStream_t st);
 
 // Tensor-core (tcgen05) expert products for large piles (mma.cu).
 struct MmaArgs {
+    CUtensorMap bmap;    // activation rows as a 2-D tensor (set by the launcher)
     MatRef a0, a1;       // weights; a1: the up matrix of a fused gate/up launch
     int fused;           // 1: gate/up rows side by side, SwiGLU epilogue writing f16 h rows
     const uint8_t* b;    // activation rows (f16), bstride bytes apart
     int64_t bstride;
+    int64_t brows;       // activation rows
     int bdiv;            // activation row = pair / bdiv
     const uint32_t* pairs;
     const uint32_t* used3;

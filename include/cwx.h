@@ -173,6 +173,35 @@ typedef struct {
 /* out = routed experts (weighted) + shared expert * sigmoid(x . sh_gate_inp) (+ residual). */
 int cwx_moe_forward(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_moe_args* args, void* stream);
 
+/* Expert parallelism (no counterpart in the reference, which runs one device): the experts are
+ * split contiguously over `world` ranks, rank r owning experts [r*epr, (r+1)*epr); every rank
+ * routes its own tokens. A layer is three calls around two all-to-all exchanges the caller
+ * makes (NCCL, or any transport):
+ *   1. cwx_ep_dispatch: router, route and piles over all n_experts; the picks' rows in pile
+ *      order, which groups them by destination rank (send_counts[d] rows for rank d, in rank
+ *      order), with each pick's expert rewritten to its index on that rank (send_eids);
+ *   (exchange send_counts, then send_rows and send_eids with those split sizes)
+ *   2. cwx_ep_experts: the received rows through this rank's experts, one pick per row ->
+ *      y_rows (n_rows, hidden), in the order received;
+ *   (exchange y_rows back with the reverse split sizes: each rank gets its rows in the order it
+ *   sent them)
+ *   3. cwx_ep_combine: out = sum over picks in pick order of weight * returned row, + shared
+ *      expert (computed on the local tokens) * sgate, + residual.
+ * The layer's n_experts and router are global; its banks (and expert biases) hold this rank's
+ * epr experts. ids/weights/pairs (tokens*top_k) and sgate (tokens) are caller buffers that carry
+ * the routing from step 1 to step 3; send_counts is a device int32 array of `world`. */
+typedef struct {
+    int32_t world, rank, experts_per_rank;
+} cwx_ep_group;
+int cwx_ep_dispatch(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_ep_group* group, const float* x,
+                    int32_t tokens, uint32_t* ids, float* weights, uint32_t* pairs, float* sgate, float* send_rows,
+                    uint32_t* send_eids, int32_t* send_counts, void* stream);
+int cwx_ep_experts(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_ep_group* group, const float* rows,
+                   const uint32_t* eids, int32_t n_rows, float* y_rows, void* stream);
+int cwx_ep_combine(cwx_ctx* ctx, const cwx_moe_layer* layer, const float* x, int32_t tokens, const float* weights,
+                   const uint32_t* pairs, const float* back_rows, const float* sgate, const float* residual,
+                   float* out, void* stream);
+
 /* Per-phase timing of cwx_moe_forward, the analogue of the reference's --profile Stats
  * (crates/engine/src/experts.rs:2541-2552): with profiling on, each call records a CUDA event
  * pair around every phase on its stream (also inside stream capture, where the events become

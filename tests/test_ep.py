@@ -1,0 +1,54 @@
+"""Expert parallelism, host side: the exchange protocol of ExpertParallelMoe on two gloo ranks
+(CPU), with the per-rank steps computed by the oracle. Each rank's output must equal the
+single-process layer's output for its tokens."""
+
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from tests.layers import Spec, build_cpu, make_input, rel_l2
+
+SPEC = Spec(hidden=256, n_experts=8, top_k=2, inter=256, gate_type=O.Q4_K, up_type=O.Q4_K, down_type=O.Q4_K,
+            shared_inter=256, seed=11)
+T = 24
+
+
+def _rank(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    from coachwhip_b200.ep import ExpertParallelMoe
+    from tests.ep_common import OracleEngine
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        L = build_cpu(SPEC)
+        x = make_input(SPEC, T)
+        per = T // world
+        xl = torch.from_numpy(np.ascontiguousarray(x[rank * per:(rank + 1) * per]))
+        moe = ExpertParallelMoe(OracleEngine(L, world, rank, O.MODE_F32))
+        out = moe.forward(xl[None])[0].numpy()
+        want = O.moe_forward(L, x, O.MODE_F32)["out"][rank * per:(rank + 1) * per]
+        q.put((rank, rel_l2(out, want)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_protocol_on_two_gloo_ranks():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29611
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=180)
+    assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
+    res = dict(q.get(timeout=5) for _ in range(2))
+    assert max(res.values()) < 1e-5, res

@@ -1,0 +1,124 @@
+"""Expert parallelism on the GPU through cwx_ep_dispatch / cwx_ep_experts / cwx_ep_combine.
+
+Two ranks emulated in one process on one device (the exchanges are tensor copies between the
+two engines), and the real two-process NCCL run when two devices are present. Same bar as the
+single-device layer: expert ids bit-exact (through the routing), outputs within relative L2 1e-3
+of the oracle."""
+
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from tests.ep_common import gpu_engine
+from tests.layers import Spec, build_cpu, make_input, rel_l2
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-3
+SPECS = {
+    "iq_mix": Spec(hidden=512, n_experts=32, top_k=8, inter=256, gate_type=O.IQ2_S, up_type=O.IQ2_S,
+                   down_type=O.IQ3_S, shared_inter=256, seed=2),
+    "mxfp4_gptoss": Spec(hidden=576, n_experts=16, top_k=4, inter=576, gate_type=O.MXFP4, up_type=O.MXFP4,
+                         down_type=O.MXFP4, act=O.ACT_CLAMPED_SWIGLU, router_bias=True, expert_bias=True, seed=4),
+    "q4k": Spec(hidden=256, n_experts=8, top_k=2, inter=256, gate_type=O.Q4_K, up_type=O.Q4_K, down_type=O.Q4_K,
+                shared_inter=256, seed=11),
+}
+
+
+def _emulated(L, x, world, mode):
+    """All ranks' steps on device 0, exchanging by slicing; returns the concatenated outputs."""
+    engines = [gpu_engine(L, world, r, 0, mode) for r in range(world)]
+    T = x.shape[0]
+    per = T // world
+    xs = [torch.from_numpy(np.ascontiguousarray(x[r * per:(r + 1) * per])).cuda() for r in range(world)]
+    ds = [engines[r].dispatch(xs[r]) for r in range(world)]
+    counts = [d.send_counts.cpu().tolist() for d in ds]
+    offs = [np.concatenate([[0], np.cumsum(c)]) for c in counts]
+    ys = []
+    for dst in range(world):  # rows for rank dst, from every source in rank order
+        rows = torch.cat([ds[s].send_rows[offs[s][dst]:offs[s][dst + 1]] for s in range(world)])
+        eids = torch.cat([ds[s].send_eids[offs[s][dst]:offs[s][dst + 1]] for s in range(world)])
+        ys.append((engines[dst].experts(rows, eids), [counts[s][dst] for s in range(world)]))
+    outs = []
+    for s in range(world):  # back to each source, in the order it sent
+        parts = []
+        for dst in range(world):
+            y, rc = ys[dst]
+            o = int(np.sum(rc[:s]))
+            parts.append(y[o:o + rc[s]])
+        back = torch.cat(parts)
+        outs.append(engines[s].combine(ds[s], back, None))
+    from coachwhip_b200 import _lib
+
+    _lib.status(0)
+    return np.concatenate([o.cpu().numpy() for o in outs])
+
+
+@pytest.mark.parametrize("name,T,world", [("iq_mix", 64, 2), ("iq_mix", 512, 4), ("mxfp4_gptoss", 64, 2),
+                                          ("q4k", 24, 2), ("q4k", 8, 1)])
+@pytest.mark.parametrize("mode", [O.MODE_CANDLE, O.MODE_F32])
+def test_ep_emulated_ranks_match_oracle(name, T, world, mode):
+    s = SPECS[name]
+    L = build_cpu(s)
+    x = make_input(s, T)
+    out = _emulated(L, x, world, mode)
+    err = rel_l2(out, O.moe_forward(L, x, mode)["out"])
+    assert err < RTOL, err
+
+
+def test_ep_rank_with_no_tokens_and_no_picks():
+    # every token routes to rank 0's experts: rank 1 receives nothing, and sends nothing back
+    s = SPECS["q4k"]
+    L = build_cpu(s)
+    L["router_b"] = np.zeros(8, dtype=np.float32)
+    L["router_b"][1] = 50.0
+    L["router_b"][2] = 49.0
+    x = make_input(s, 16)
+    out = _emulated(L, x, 2, O.MODE_F32)
+    assert rel_l2(out, O.moe_forward(L, x, O.MODE_F32)["out"]) < RTOL
+
+
+def _nccl_rank(rank, world, port, q):
+    import torch.distributed as dist
+
+    from coachwhip_b200.ep import ExpertParallelMoe
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        s = SPECS["iq_mix"]
+        L = build_cpu(s)
+        T = 256
+        x = make_input(s, T)
+        per = T // world
+        moe = ExpertParallelMoe(gpu_engine(L, world, rank, rank, O.MODE_F32))
+        xl = torch.from_numpy(np.ascontiguousarray(x[rank * per:(rank + 1) * per])).cuda(rank)
+        out = moe.forward(xl[None])[0].cpu().numpy()
+        want = O.moe_forward(L, x, O.MODE_F32)["out"][rank * per:(rank + 1) * per]
+        q.put((rank, rel_l2(out, want)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two devices")
+def test_ep_nccl_two_ranks():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_nccl_rank, args=(r, 2, 29641, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
+    res = dict(q.get(timeout=5) for _ in range(2))
+    assert max(res.values()) < RTOL, res
