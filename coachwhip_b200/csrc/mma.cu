@@ -47,13 +47,19 @@ constexpr int A_BYTES = 128 * 128;
 constexpr int B_BYTES = NMAX * 128;
 constexpr int Q_BYTES = 128 * 110;  // 128 rows of the largest piece (IQ3_S)
 constexpr int XCH_BYTES = 32 * 64 * 4;
-constexpr int THREADS = 18 * 32;
-constexpr int W_MMA = 4, W_QCOPY = 5, W_GATHER = 6, N_GATHER = 4, W_DEC = 10, N_DEC = 8;
+constexpr int THREADS = 20 * 32;
+constexpr int W_MMA = 4, W_QCOPY = 5, W_GATHER = 6, N_GATHER = 4, W_DEC = 10, N_DEC = 10;
+constexpr int DEC_CHUNKS = 128 * 8;                                   // 16-byte A chunks per stage
+constexpr int DEC_PER = (DEC_CHUNKS + N_DEC * 32 - 1) / (N_DEC * 32);  // per decoder thread
+constexpr int GATHER_PER = NMAX * 8 / (N_GATHER * 32);                 // B chunks per gather thread
 constexpr int TMEM_COLS = 512;
 
+// Codebook as f16 values: IQ2_S 8 per entry, two copies (entry e of copy j at e*32 + j*16, the
+// copy picked by the lane's parity, so fewer lanes of a wavefront meet on a bank); IQ3_S 4 per
+// entry, four copies (e*32 + j*8).
 template <int FMT>
 struct Tab {
-    static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 16 : 512 * 8;
+    static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 32 : 512 * 32;
 };
 
 // shared memory: barriers, then 1024-aligned A and B stages, quantised stages, codebook, exchange
@@ -90,6 +96,14 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 __device__ __forceinline__ void tc_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+// One lane of the (converged) warp.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n .reg .b32 r;\n .reg .pred p;\n elect.sync r|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(pred));
+    return pred != 0;
+}
 __device__ __forceinline__ void tc_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -208,7 +222,7 @@ __device__ __forceinline__ uint4 dec_chunk(const uint8_t* q, int r, int c4, int 
         const uint32_t qw = gi < 4 ? Q.x : Q.y, sw = gi < 4 ? Q.z : Q.w;
         const uint32_t b = __byte_perm(qw, 0u, 0x4440 | (gi & 3));
         const uint32_t idx = b | (((H >> (2 * gi)) & 3u) << 8);
-        const uint4 G = *reinterpret_cast<const uint4*>(tab + idx * 16);
+        const uint4 G = *reinterpret_cast<const uint4*>(tab + idx * 32);
         const uint32_t s8 = __byte_perm(sw, 0u, 0x4440 | (gi & 3));
         const __half2 od = odd_h2((H >> (16 + 4 * (gi >> 1))) & 0xFu);
         uint4 o;
@@ -228,8 +242,8 @@ __device__ __forceinline__ uint4 dec_chunk(const uint8_t* q, int r, int c4, int 
         const __half2 od = odd_h2((sc >> (4 * (gi >> 2))) & 0xFu);
         const uint32_t i0 = (qs2 & 0xFFu) | (((qh >> (2 * gi)) & 1u) << 8);
         const uint32_t i1 = (qs2 >> 8) | (((qh >> (2 * gi + 1)) & 1u) << 8);
-        const uint2 G0 = *reinterpret_cast<const uint2*>(tab + i0 * 8);
-        const uint2 G1 = *reinterpret_cast<const uint2*>(tab + i1 * 8);
+        const uint2 G0 = *reinterpret_cast<const uint2*>(tab + i0 * 32);
+        const uint2 G1 = *reinterpret_cast<const uint2*>(tab + i1 * 32);
         uint4 o;
         o.x = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 0, G0.x)), od), d2));
         o.y = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 2, G0.y)), od), d2));
@@ -288,14 +302,16 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                 o.y = u_h2(__floats2half2_rn((float)((v >> 16) & 0xFF), (float)((v >> 24) & 0xFF)));
                 o.z = u_h2(__floats2half2_rn((float)((v >> 32) & 0xFF), (float)((v >> 40) & 0xFF)));
                 o.w = u_h2(__floats2half2_rn((float)((v >> 48) & 0xFF), (float)(v >> 56)));
-                *reinterpret_cast<uint4*>(tab + e * 16) = o;
+                *reinterpret_cast<uint4*>(tab + e * 32) = o;
+                *reinterpret_cast<uint4*>(tab + e * 32 + 16) = o;
             }
         } else {
             for (int e = t; e < 512; e += N_DEC * 32) {
                 const uint32_t v = cwx_iq3s_expand(d_iq3s_codes[e]);
-                *reinterpret_cast<uint2*>(tab + e * 8) =
-                    make_uint2(u_h2(__floats2half2_rn((float)(v & 0xFF), (float)((v >> 8) & 0xFF))),
-                               u_h2(__floats2half2_rn((float)((v >> 16) & 0xFF), (float)(v >> 24))));
+                const uint2 o = make_uint2(u_h2(__floats2half2_rn((float)(v & 0xFF), (float)((v >> 8) & 0xFF))),
+                                           u_h2(__floats2half2_rn((float)((v >> 16) & 0xFF), (float)(v >> 24))));
+#pragma unroll
+                for (int j = 0; j < 4; ++j) *reinterpret_cast<uint2*>(tab + e * 32 + j * 8) = o;
             }
         }
     }
@@ -308,48 +324,51 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
     const int nks = 4 * n_kp;  // 64-column stages per item
 
     if (warp == W_MMA) {
-        // ---------------- MMA issue (one thread)
-        if (lane == 0) {
-            Iter it;
-            MItem m;
-            uint32_t c = 0;  // stage counter
-            bool ok = true;
-            int li = 0;
-            for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m); i += gridDim.x, ++li) {
-                const int buf = li & 1;
-                const uint32_t use = (uint32_t)li >> 1;
-                if (use > 0 && !mbar_wait(&bars->acc_empty[buf], (use - 1) & 1, a.err)) {
+        // ---------------- MMA issue: the whole warp walks the stages (the descriptors stay
+        // warp-uniform), one elected lane issues the MMAs and commits
+        Iter it;
+        MItem m;
+        uint32_t c = 0;  // stage counter
+        bool ok = true;
+        int li = 0;
+        const bool leader = elect_one();
+        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m); i += gridDim.x, ++li) {
+            const int buf = li & 1;
+            const uint32_t use = (uint32_t)li >> 1;
+            if (use > 0 && !mbar_wait(&bars->acc_empty[buf], (use - 1) & 1, a.err)) {
+                ok = false;
+                break;
+            }
+            tc_after();
+            const int npad = ((int)m.ntok + 15) & ~15;
+            const uint32_t idesc = idesc_f16(npad);
+            const uint32_t d = tmem + (uint32_t)buf * 256;
+            for (int ks = 0; ks < nks; ++ks, ++c) {
+                const int s = (int)(c % NS);
+                const uint32_t ph = (c / NS) & 1;
+                if (!mbar_wait(&bars->full_a[s], ph, a.err) || !mbar_wait(&bars->full_b[s], ph, a.err)) {
                     ok = false;
                     break;
                 }
                 tc_after();
-                const int npad = ((int)m.ntok + 15) & ~15;
-                const uint32_t idesc = idesc_f16(npad);
-                const uint32_t d = tmem + (uint32_t)buf * 256;
-                for (int ks = 0; ks < nks; ++ks, ++c) {
-                    const int s = (int)(c % NS);
-                    const uint32_t ph = (c / NS) & 1;
-                    if (!mbar_wait(&bars->full_a[s], ph, a.err) || !mbar_wait(&bars->full_b[s], ph, a.err)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_after();
-                    fence_async_smem();  // the gathered activations were written by cp.async
-                    const uint8_t* at = sa + s * A_BYTES;
-                    const uint8_t* bt = sb + s * B_BYTES;
+                fence_async_smem();  // the gathered activations were written by cp.async
+                const uint64_t ad = sdesc(sa + s * A_BYTES), bd = sdesc(sb + s * B_BYTES);
+                if (leader) {
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        tc_mma(d, sdesc(at + 32 * kk), sdesc(bt + 32 * kk), idesc, (ks | kk) != 0);
+                    for (int kk = 0; kk < 4; ++kk)  // +32 bytes = +2 in the descriptor's address field
+                        tc_mma(d, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
                     tc_commit(&bars->empty_s[s]);
                 }
-                if (!ok) break;
-                tc_commit(&bars->acc_full[buf]);
+                __syncwarp();
             }
-            // every MMA issued has finished before the TMEM is freed
-            tc_commit(&bars->mma_done);
-            mbar_wait(&bars->mma_done, 0, a.err);
+            if (!ok) break;
+            if (leader) tc_commit(&bars->acc_full[buf]);
+            __syncwarp();
         }
+        // every MMA issued has finished before the TMEM is freed
+        if (leader) tc_commit(&bars->mma_done);
         __syncwarp();
+        mbar_wait(&bars->mma_done, 0, a.err);
     } else if (warp == W_QCOPY) {
         // ---------------- quantised pieces: two 64-row halves per piece, one bulk copy each
         Iter it;
@@ -383,15 +402,11 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
         uint32_t c = 0;
         bool ok = true;
         for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m); i += gridDim.x) {
-            const uint8_t* src[16];
+            int row[GATHER_PER];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
+            for (int j = 0; j < GATHER_PER; ++j) {
                 const uint32_t n = (uint32_t)(t >> 3) + 16 * j;
-                src[j] = nullptr;
-                if (n < m.ntok) {
-                    const uint32_t p = a.pairs[m.first + m.n0 + n];
-                    src[j] = a.b + (int64_t)(p / (uint32_t)a.bdiv) * a.bstride + 16 * (t & 7);
-                }
+                row[j] = n < m.ntok ? (int)(a.pairs[m.first + m.n0 + n] / (uint32_t)a.bdiv) : -1;
             }
             for (int ks = 0; ks < nks; ++ks, ++c) {
                 const int s = (int)(c % NS);
@@ -400,18 +415,20 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
                 uint8_t* bt = sb + s * B_BYTES;
+                const uint8_t* col = a.b + 16 * (t & 7) + (int64_t)ks * 128;
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
+                for (int j = 0; j < GATHER_PER; ++j) {
                     const int n = (t >> 3) + 16 * j, ch = t & 7;
-                    if (src[j]) cp_async16(bt + n * 128 + ((ch ^ (n & 7)) << 4), src[j] + (int64_t)ks * 128);
+                    if (row[j] >= 0) cp_async16(bt + n * 128 + ((ch ^ (n & 7)) << 4), col + (int64_t)row[j] * a.bstride);
                 }
                 cp_async_arrive(&bars->full_b[s]);
             }
         }
         cp_async_wait_all();
     } else if (warp >= W_DEC) {
-        // ---------------- decode: chunk i = t + 256 j (j < 4) of a stage is row i / 8, chunk i % 8
+        // ---------------- decode: the decoder threads share a stage's 128 rows x 8 chunks
         const int t = tid - W_DEC * 32;
+        const uint8_t* tl = tab + (FMT == F_IQ2_S ? (lane & 1) * 16 : (lane & 3) * 8);  // this lane's copy
         Iter it;
         MItem m;
         uint32_t c = 0, p = 0;
@@ -432,10 +449,13 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                     if (!ok) break;
                     uint8_t* at = sa + s * A_BYTES;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int r = (t >> 3) + 32 * j, gi = t & 7;
-                        const uint4 w = dec_chunk<FMT>(q, r, c4, gi, tab);
-                        *reinterpret_cast<uint4*>(at + r * 128 + ((gi ^ (r & 7)) << 4)) = w;
+                    for (int j = 0; j < DEC_PER; ++j) {
+                        const int ci = t + N_DEC * 32 * j;  // chunk: row ci / 8, 16-byte chunk ci % 8
+                        if (ci < DEC_CHUNKS) {
+                            const int r = ci >> 3, gi = ci & 7;
+                            const uint4 w = dec_chunk<FMT>(q, r, c4, gi, tl);
+                            *reinterpret_cast<uint4*>(at + r * 128 + ((gi ^ (r & 7)) << 4)) = w;
+                        }
                     }
                     fence_async_smem();  // the tensor cores read the tile through the async proxy
                     __syncwarp();

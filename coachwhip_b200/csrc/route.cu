@@ -13,7 +13,8 @@
 // defined: softmax sums in candle's x86 AVX order (vendor/candle-core/src/cpu/avx.rs:243-257,
 // lanes reduced as in vec_reduce 51-66), exp correctly rounded to f32 (what glibc's expf, which
 // Rust's f32::exp calls, returns), the pick order of a stable descending sort. Router logits
-// accumulate exact f32 products in f64 (T <= 64) and round once.
+// accumulate exact f32 products in f64 and round once (a decode form for small batches and a
+// tiled form with operand reuse for prefill-sized batches).
 #include "cwx_common.cuh"
 #include "kernels.cuh"
 
@@ -466,9 +467,94 @@ __global__ void __launch_bounds__(1024) k_perm_small(const uint32_t* __restrict_
 }
 
 // ---------------------------------------------------------------- host launchers
+// Tiled router for large batches: a block computes 64 experts x 64 tokens; K runs in chunks of
+// 32 columns staged in shared memory by cp.async (double-buffered, rows padded to 36 floats so
+// the fragment loads of a warp hit 32 different banks). Warp w holds experts 16 (w % 4) .. +15
+// and tokens 32 (w / 4) .. +31 as 2 x 4 m8n8k4 f64 tiles; each logit's exact products are summed
+// in f64 in K order and rounded once.
+constexpr int RT = 64, RK = 32, RPAD = 36;
+
+__device__ __forceinline__ void cp16_zfill(void* dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(256) k_router_tiled(const float* __restrict__ x, const float* __restrict__ w,
+                                                      const float* __restrict__ bias, int T, int H, int E,
+                                                      float* __restrict__ logits) {
+    __shared__ __align__(16) float ws[2][RT][RPAD];
+    __shared__ __align__(16) float xs[2][RT][RPAD];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int e0 = blockIdx.x * RT, t0 = blockIdx.y * RT;
+    const int eg = warp & 3, tg = warp >> 2;
+    const int r = lane >> 2, kq = lane & 3;
+    // staging: 64 rows x 8 pieces of 16 bytes per operand per chunk, two per thread
+    auto stage = [&](int buf, int k0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int i = tid + 256 * h, row = i >> 3, pc = i & 7;
+            const int kc = k0 + 4 * pc;
+            const int kb = H - kc > 4 ? 16 : (H - kc > 0 ? 4 * (H - kc) : 0);
+            const int e = e0 + row, t = t0 + row;
+            const bool ein = e < E, tin = t < T;
+            cp16_zfill(&ws[buf][row][4 * pc], w + (int64_t)(ein ? e : 0) * H + (kb ? kc : 0), ein ? kb : 0);
+            cp16_zfill(&xs[buf][row][4 * pc], x + (int64_t)(tin ? t : 0) * H + (kb ? kc : 0), tin ? kb : 0);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    double c[2][4][2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) c[i][j][0] = c[i][j][1] = 0.0;
+    const int nch = (H + RK - 1) / RK;
+    stage(0, 0);
+    for (int ch = 0; ch < nch; ++ch) {
+        const int buf = ch & 1;
+        if (ch + 1 < nch) {
+            stage(buf ^ 1, (ch + 1) * RK);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k4 = 0; k4 < RK / 4; ++k4) {
+            double a[2], b[4];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) a[i] = (double)ws[buf][eg * 16 + 8 * i + r][4 * k4 + kq];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = (double)xs[buf][tg * 32 + 8 * j + r][4 * k4 + kq];
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dmma_8x8x4(c[i][j], a[i], b[j]);
+        }
+        __syncthreads();  // the buffer is restaged two chunks later
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int e = e0 + eg * 16 + 8 * i + r, t = t0 + tg * 32 + 8 * j + 2 * kq + h;
+                if (e < E && t < T) {
+                    float l = (float)c[i][j][h];
+                    if (bias) l = __fadd_rn(l, bias[e]);
+                    logits[(int64_t)t * E + e] = l;
+                }
+            }
+}
+
 int launch_router(const float* x, const float* w, const float* b, int T, int H, int E, float* logits,
                   cudaStream_t st) {
     if (T == 0) return CWX_OK;
+    if (T >= 1024 && H % 4 == 0) {
+        k_router_tiled<<<dim3((E + RT - 1) / RT, (T + RT - 1) / RT), 256, 0, st>>>(x, w, b, T, H, E, logits);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_router_tiled");
+    }
     k_router<<<dim3((E + 7) / 8, (T + 7) / 8), 256, 0, st>>>(x, w, b, T, H, E, logits);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_router");
