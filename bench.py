@@ -330,7 +330,8 @@ def prefill_runs(mods, Ts, a, dev, pk, maxall, barrier, world):
         out[str(T)] = {"tokens_per_s": world * T / (ms / 1e3), "ms_per_step": ms, "layers": len(mods),
                        "tflops": fl / (ms / 1e3) / 1e12, "frac_bf16_sustained_peak": fl / (ms / 1e3) / 1e12 / tpk,
                        "products_tflops": prod_fl / (prod_ms / 1e3) / 1e12, "phase_ms_eager": ph,
-                       "path": "tcgen05 grouped products (k_mma) for the routed experts, mma.sync for the shared expert"}
+                       "act_mode": "f32 activations (O2 semantics)",
+                       "path": "tcgen05 grouped products (k_mma) for the routed and shared experts, tiled FP64 router"}
         print(f"[bench] prefill {T}: {ms:.3f} ms/step, {out[str(T)]['tokens_per_s']:.0f} tokens/s, "
               f"{out[str(T)]['tflops']:.1f} TFLOP/s", file=sys.stderr, flush=True)
     return out
@@ -473,7 +474,15 @@ def main():
     e2e_ms = maxall(e0.elapsed_time(e1) / e_steps)
     _lib.status(local)
 
-    prefill = prefill_runs(mods, prefill_T, a, dev, pk, maxall, barrier, world)
+    # prefill runs the f32-activation policy (the reference GPU path's semantics, checked against
+    # the O2 oracle): the same layers and banks, every product on the tensor cores
+    from coachwhip_b200.moe import ExpertAct, StreamedMoe
+
+    mods_f32 = [StreamedMoe(m.layer, m.gate, m.top_k, True, ExpertAct.Silu(), store, shared=m.shared,
+                            act_mode=_lib.ACT_MODE_F32) for m in mods]
+    for m in mods_f32:
+        m.reserve(max(prefill_T) if prefill_T else 1)
+    prefill = prefill_runs(mods_f32, prefill_T, a, dev, pk, maxall, barrier, world)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:

@@ -132,10 +132,27 @@ struct LayerPlan {
     float* y;
     float* ys;
     int mma;           // routed products on the tensor cores (IQ banks, large piles)
+    int sh_mma;        // the shared expert on the tensor cores too (f32 activations)
     __half* x16;       // (T, H) f16 rows of x
     __half* h16;       // (n, I) f16 hidden rows per pick
+    __half* hs16;      // (T, Is) f16 hidden rows of the shared expert
+    uint32_t* spairs;  // the shared expert's pile (every token) and used list
+    uint32_t* sused3;
+    uint32_t* snused;
     size_t bytes;
 };
+
+// The shared expert joins the tensor-core products when its activations are f32 (no Q8 codes,
+// whose per-piece scale a TMEM accumulator cannot apply) and its banks are a supported format.
+static bool shared_mma_ok(const cwx_moe_layer* L) {
+    if (!L->sh_gate) return false;
+    const Layout &g = L->sh_gate->L, &u = L->sh_up->L, &d = L->sh_down->L;
+    auto fmt_ok = [](int f) { return f == F_IQ2_S || f == F_IQ3_S || f == F_Q4_K; };
+    if (!fmt_ok(g.fmt) || !fmt_ok(d.fmt) || g.fmt != u.fmt) return false;
+    if (act_mode_of(L->sh_gate, L->act_mode) != AM_F32 || act_mode_of(L->sh_down, L->act_mode) != AM_F32)
+        return false;
+    return g.n % 256 == 0 && L->hidden % 256 == 0;
+}
 
 // Whether a layer's routed products run on the tensor cores: IQ2_S / IQ3_S banks (f32 activations
 // under every policy), SiLU, whole 256-column pieces, and piles large enough on average.
@@ -201,22 +218,29 @@ static void plan_layer(const cwx_moe_layer* L, int T, int mma, uint8_t* base, La
     p->used3 = c.take<uint32_t>((size_t)3 * p->E);
     p->n_used = c.take<uint32_t>(4);
     p->perm = c.take<uint32_t>(perm_scratch_bytes(n, p->E) / 4);
+    const int sh_mma = mma && shared_mma_ok(L) ? 1 : 0;
     for (int m = 0; m < 3; ++m) {
-        const bool need = (m == p->mgu && !mma) || (m == p->msgu);
+        const bool need = (m == p->mgu && !mma) || (m == p->msgu && !sh_mma);
         p->xpk[m] = need ? c.take<uint8_t>((size_t)(T * packed_row_bytes(p->H))) : nullptr;
     }
     const size_t nr = mma ? 0 : (size_t)n;  // the tensor-core products write h directly
     p->g = c.take<float>(nr * p->I);
     p->u = c.take<float>(nr * p->I);
-    p->gs = c.take<float>((size_t)T * p->Is);
-    p->us = c.take<float>((size_t)T * p->Is);
+    const size_t ns = sh_mma ? 0 : (size_t)T;  // the tensor-core shared expert writes h directly
+    p->gs = c.take<float>(ns * p->Is);
+    p->us = c.take<float>(ns * p->Is);
     p->hpk = c.take<uint8_t>((size_t)(nr * packed_row_bytes(p->I)));
-    p->hspk = c.take<uint8_t>((size_t)(T * packed_row_bytes(p->Is)));
+    p->hspk = c.take<uint8_t>((size_t)(ns * packed_row_bytes(p->Is)));
     p->y = c.take<float>((size_t)n * p->H);
     p->ys = c.take<float>((size_t)T * p->H);
     p->mma = mma;
+    p->sh_mma = sh_mma;
     p->x16 = mma ? c.take<__half>((size_t)T * p->H) : nullptr;
     p->h16 = mma ? c.take<__half>((size_t)n * p->I) : nullptr;
+    p->hs16 = sh_mma ? c.take<__half>((size_t)T * p->Is) : nullptr;
+    p->spairs = sh_mma ? c.take<uint32_t>((size_t)T + 1) : nullptr;
+    p->sused3 = sh_mma ? c.take<uint32_t>(4) : nullptr;
+    p->snused = sh_mma ? c.take<uint32_t>(4) : nullptr;
     p->bytes = c.off + 256;
 }
 
@@ -553,8 +577,12 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
         PhaseTimer t(c, st, CWX_PHASE_PREP);
         if ((rc = launch_f16rows(A->x, (int64_t)T * H, p.x16, st))) return rc;
         c->launches += 1;
-        if (shared) {
+        if (shared && !p.sh_mma) {
             if ((rc = launch_prep(prep(A->x, nullptr, T, H, p.msgu, p.xpk[p.msgu]), st))) return rc;
+            c->launches += 1;
+        }
+        if (p.sh_mma) {
+            if ((rc = launch_all_tokens(p.spairs, T, p.sused3, p.snused, st))) return rc;
             c->launches += 1;
         }
         t.end();
@@ -579,13 +607,25 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
         g.ostride = I;
         if ((rc = launch_mma(g, c->device, c->sm_count, st))) return rc;
         c->launches += 1;
-        if (shared) {
+        if (p.sh_mma) {
+            MmaArgs sg = g;
+            sg.a0 = mref(L->sh_gate);
+            sg.a1 = mref(L->sh_up);
+            sg.pairs = p.spairs;
+            sg.used3 = p.sused3;
+            sg.n_used = p.snused;
+            sg.bdiv = 1;
+            sg.hout = p.hs16;
+            sg.ostride = Is;
+            if ((rc = launch_mma(sg, c->device, c->sm_count, st))) return rc;
+            c->launches += 1;
+        } else if (shared) {
             if ((rc = shared_gemv(c, L, p, 0, st))) return rc;
             c->launches += 1;
         }
         t.end();
     }
-    if (shared) {
+    if (shared && !p.sh_mma) {
         PhaseTimer t(c, st, CWX_PHASE_PREP);
         if ((rc = launch_prep(prep(p.gs, p.us, T, Is, p.msd, p.hspk), st))) return rc;
         c->launches += 1;
@@ -604,7 +644,20 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
         d.ostride = H;
         if ((rc = launch_mma(d, c->device, c->sm_count, st))) return rc;
         c->launches += 1;
-        if (shared) {
+        if (p.sh_mma) {
+            MmaArgs sd = d;
+            sd.a0 = mref(L->sh_down);
+            sd.pairs = p.spairs;
+            sd.used3 = p.sused3;
+            sd.n_used = p.snused;
+            sd.b = reinterpret_cast<const uint8_t*>(p.hs16);
+            sd.bstride = (int64_t)Is * 2;
+            sd.brows = T;
+            sd.out = p.ys;
+            sd.ostride = H;
+            if ((rc = launch_mma(sd, c->device, c->sm_count, st))) return rc;
+            c->launches += 1;
+        } else if (shared) {
             if ((rc = shared_gemv(c, L, p, 1, st))) return rc;
             c->launches += 1;
         }

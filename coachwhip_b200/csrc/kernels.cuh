@@ -110,5 +110,6 @@ struct MmaArgs {
 bool mma_supports(const MmaArgs& a);
 int launch_mma(const MmaArgs& a, int device, int sm_count, cudaStream_t st);
 int launch_f16rows(const float* x, int64_t n, __half* y, cudaStream_t st);
+int launch_all_tokens(uint32_t* pairs, int T, uint32_t* used3, uint32_t* n_used, cudaStream_t st);
 
 }  // namespace cwx

@@ -45,7 +45,7 @@ constexpr int NQ = 2;             // quantised-piece stages (256 columns each)
 constexpr int NMAX = 256;         // picks per column tile
 constexpr int A_BYTES = 128 * 128;
 constexpr int B_BYTES = NMAX * 128;
-constexpr int Q_BYTES = 128 * 110;  // 128 rows of the largest piece (IQ3_S)
+constexpr int Q_BYTES = 128 * 144;  // 128 rows of the largest piece (Q4_K)
 constexpr int XCH_BYTES = 32 * 64 * 4;
 constexpr int THREADS = 20 * 32;
 constexpr int W_MMA = 4, W_QCOPY = 5, W_GATHER = 6, N_GATHER = 4, W_DEC = 10, N_DEC = 10;
@@ -59,7 +59,7 @@ constexpr int TMEM_COLS = 512;
 // entry, four copies (e*32 + j*8).
 template <int FMT>
 struct Tab {
-    static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 32 : 512 * 32;
+    static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 32 : FMT == F_IQ3_S ? 512 * 32 : 0;
 };
 
 // shared memory: barriers, then 1024-aligned A and B stages, quantised stages, codebook, exchange
@@ -212,7 +212,31 @@ __device__ __forceinline__ __half2 odd_h2(uint32_t n) {
 
 template <int FMT>
 __device__ __forceinline__ uint4 dec_chunk(const uint8_t* q, int r, int c4, int gi, const uint8_t* tab) {
-    if (FMT == F_IQ2_S) {
+    if (FMT == F_Q4_K) {
+        // y = d * sc * q - dmin * m per 32-column sub-block (candle's to_float, each operation
+        // rounded as there), then rounded to f16; sub-block 2 c4 + (gi >= 4) holds the low
+        // (gi < 4) or high nibbles of bytes 32 c4 + 8 (gi % 4) .. + 7
+        const uint8_t* row = q + r * 144;
+        const float d = h2f_bits(*reinterpret_cast<const uint16_t*>(row));
+        const float dmin = h2f_bits(*reinterpret_cast<const uint16_t*>(row + 2));
+        int sc, mn;
+        get_scale_min_k4(2 * c4 + (gi >> 2), row + 4, &sc, &mn);
+        const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
+        const uint2 b = *reinterpret_cast<const uint2*>(row + 16 + 32 * c4 + 8 * (gi & 3));
+        const uint32_t sh = gi >= 4 ? 4 : 0;
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t byte = ((j < 4 ? b.x : b.y) >> (8 * (j & 3))) & 0xFFu;
+            v[j] = __fsub_rn(__fmul_rn(d1, (float)((byte >> sh) & 0xFu)), m1);
+        }
+        uint4 o;
+        o.x = u_h2(__floats2half2_rn(v[0], v[1]));
+        o.y = u_h2(__floats2half2_rn(v[2], v[3]));
+        o.z = u_h2(__floats2half2_rn(v[4], v[5]));
+        o.w = u_h2(__floats2half2_rn(v[6], v[7]));
+        return o;
+    } else if (FMT == F_IQ2_S) {
         const uint8_t* grp = q + (r >> 4) * (16 * 82);
         const int rg = r & 15;
         const uint4 Q = *reinterpret_cast<const uint4*>(grp + (rg * 4 + c4) * 16);
@@ -294,7 +318,9 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
     }
     if (warp >= W_DEC) {  // the codebook as f16 values: IQ2_S 8 per entry, IQ3_S 4
         const int t = tid - W_DEC * 32;
-        if (FMT == F_IQ2_S) {
+        if (FMT == F_Q4_K) {
+            // no codebook
+        } else if (FMT == F_IQ2_S) {
             for (int e = t; e < 1024; e += N_DEC * 32) {
                 const uint64_t v = cwx_iq2s_expand(d_iq2s_codes[e]);
                 uint4 o;
@@ -544,7 +570,7 @@ int launch_f16rows(const float* x, int64_t n, __half* y, cudaStream_t st) {
 // whole 256-column pieces, gate and up of one format and shape.
 bool mma_supports(const MmaArgs& a) {
     const Layout& L = a.a0.L;
-    if (L.fmt != F_IQ2_S && L.fmt != F_IQ3_S) return false;
+    if (L.fmt != F_IQ2_S && L.fmt != F_IQ3_S && L.fmt != F_Q4_K) return false;
     if (L.k % PIECE_K || L.n % (a.fused ? 64 : 128)) return false;
     if (a.fused) {
         const Layout& U = a.a1.L;
@@ -554,26 +580,49 @@ bool mma_supports(const MmaArgs& a) {
     return true;
 }
 
-int launch_mma(const MmaArgs& in, int device, int sm_count, cudaStream_t st) {
-    MmaArgs a = in;
-    if (!mma_supports(a)) return fail(CWX_EUNSUPPORTED, "tensor-core expert products: unsupported layout");
-    a.mtiles = (int)(a.fused ? a.a0.L.n / 64 : a.a0.L.n / 128);
-    const int fmt = a.a0.L.fmt;
-    const int smem = (fmt == F_IQ2_S ? mm::Smem::total<F_IQ2_S>() : mm::Smem::total<F_IQ3_S>()) + 1024;
-    static int attr_set[64][2] = {{0}};
-    const int fi = fmt == F_IQ2_S ? 0 : 1;
+template <int FMT>
+static int launch_mma_f(const MmaArgs& a, int device, int sm_count, cudaStream_t st) {
+    constexpr int fi = FMT == F_IQ2_S ? 0 : FMT == F_IQ3_S ? 1 : 2;
+    const int smem = mm::Smem::total<FMT>() + 1024;
+    static int attr_set[64][3] = {{0}};
     if (device < 0 || device >= 64 || !attr_set[device][fi]) {
-        cudaError_t e = fmt == F_IQ2_S
-                            ? cudaFuncSetAttribute(k_mma<F_IQ2_S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
-                            : cudaFuncSetAttribute(k_mma<F_IQ3_S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(k_mma<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_mma)");
         if (device >= 0 && device < 64) attr_set[device][fi] = 1;
     }
     const unsigned grid = (unsigned)(sm_count > 0 ? sm_count : 1);
-    if (fmt == F_IQ2_S) k_mma<F_IQ2_S><<<grid, mm::THREADS, smem, st>>>(a);
-    else k_mma<F_IQ3_S><<<grid, mm::THREADS, smem, st>>>(a);
+    k_mma<FMT><<<grid, mm::THREADS, smem, st>>>(a);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_mma");
+}
+
+int launch_mma(const MmaArgs& in, int device, int sm_count, cudaStream_t st) {
+    MmaArgs a = in;
+    if (!mma_supports(a)) return fail(CWX_EUNSUPPORTED, "tensor-core expert products: unsupported layout");
+    a.mtiles = (int)(a.fused ? a.a0.L.n / 64 : a.a0.L.n / 128);
+    switch (a.a0.L.fmt) {
+        case F_IQ2_S: return launch_mma_f<F_IQ2_S>(a, device, sm_count, st);
+        case F_IQ3_S: return launch_mma_f<F_IQ3_S>(a, device, sm_count, st);
+        default: return launch_mma_f<F_Q4_K>(a, device, sm_count, st);
+    }
+}
+
+// The shared expert as one pile holding every token: pairs = 0 .. T-1, used list {(0, 0, T)}.
+__global__ void k_all_tokens(uint32_t* pairs, int T, uint32_t* used3, uint32_t* n_used) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < T) pairs[i] = (uint32_t)i;
+    if (i == 0) {
+        used3[0] = 0;
+        used3[1] = 0;
+        used3[2] = (uint32_t)T;
+        *n_used = T > 0 ? 1u : 0u;
+    }
+}
+
+int launch_all_tokens(uint32_t* pairs, int T, uint32_t* used3, uint32_t* n_used, cudaStream_t st) {
+    k_all_tokens<<<(T + 255) / 256 + (T == 0), 256, 0, st>>>(pairs, T, used3, n_used);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_all_tokens");
 }
 
 }  // namespace cwx
