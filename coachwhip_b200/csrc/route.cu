@@ -22,6 +22,8 @@ namespace cwx {
 
 __device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
 
+constexpr int SGATE_SMEM = 4096;  // hidden sizes up to this stage the shared gate's products
+
 // candle's AVX order for a sum whose 32-element steps live one per lane: lane L holds the sum of
 // elements 32*s + L over the whole steps, in step order. Returns the reduced value in all lanes.
 __device__ __forceinline__ float avx_lane_tree(float acc) {
@@ -62,29 +64,40 @@ __global__ void __launch_bounds__(256) k_router(const float* __restrict__ x, con
     const float* xr = x + (int64_t)(tb ? t0 + r : 0) * H;
     double c[2] = {0.0, 0.0};
     int k = k0;
-    // chunks of four k4 steps; the next chunk's loads are in flight while this one multiplies
-    float av[4], bv[4];
-    if (k + 16 <= k1)
+    // 16-column chunks with the reduction index permuted inside a chunk (the same way for both
+    // operands): step i of chunk c takes columns k0 + 16c + 4q + i (q = 0..3), so lane (r, q)
+    // holds its four steps' values as one float4 of each operand; PF chunks are in flight ahead
+    // of the multiplies
+    if ((k0 & 3) == 0 && (H & 3) == 0 && (((uintptr_t)w | (uintptr_t)x) & 15) == 0) {
+        constexpr int PF = 4;
+        const int nch = (k1 - k0) >> 4;
+        const float4* w4 = reinterpret_cast<const float4*>(wr + k0) + kq;
+        const float4* x4 = reinterpret_cast<const float4*>(xr + k0) + kq;
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 aw[PF], bx[PF];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            av[j] = ea ? __ldg(wr + k + 4 * j + kq) : 0.f;
-            bv[j] = tb ? __ldg(xr + k + 4 * j + kq) : 0.f;
+        for (int j = 0; j < PF; ++j) {
+            aw[j] = j < nch && ea ? __ldg(w4 + 4 * j) : z;
+            bx[j] = j < nch && tb ? __ldg(x4 + 4 * j) : z;
         }
-    for (; k + 16 <= k1; k += 16) {
-        float an[4], bn[4];
-        const bool more = k + 32 <= k1;
+        for (int c0 = 0; c0 < nch; c0 += PF) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            an[j] = more && ea ? __ldg(wr + k + 16 + 4 * j + kq) : 0.f;
-            bn[j] = more && tb ? __ldg(xr + k + 16 + 4 * j + kq) : 0.f;
+            for (int j = 0; j < PF; ++j) {
+                const int ch = c0 + j;
+                if (ch < nch) {
+                    const float4 a = aw[j], b = bx[j];
+                    if (ch + PF < nch) {
+                        aw[j] = ea ? __ldg(w4 + 4 * (ch + PF)) : z;
+                        bx[j] = tb ? __ldg(x4 + 4 * (ch + PF)) : z;
+                    }
+                    dmma_8x8x4(c, (double)a.x, (double)b.x);
+                    dmma_8x8x4(c, (double)a.y, (double)b.y);
+                    dmma_8x8x4(c, (double)a.z, (double)b.z);
+                    dmma_8x8x4(c, (double)a.w, (double)b.w);
+                }
+            }
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) dmma_8x8x4(c, (double)av[j], (double)bv[j]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            av[j] = an[j];
-            bv[j] = bn[j];
-        }
+        k = k0 + 16 * nch;
     }
     for (; k < k1; k += 4) {
         const bool in = k + kq < k1;
@@ -127,7 +140,11 @@ __global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits,
     __shared__ float s_sum;
     __shared__ float cv[8][16];
     __shared__ int ci[8][16];
+    __shared__ float sp[SGATE_SMEM];  // x * gate_inp for the shared gate, staged by every thread
     const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool sp_smem = sgate && H <= SGATE_SMEM;
+    if (sp_smem)
+        for (int h = tid; h < H; h += 256) sp[h] = __fmul_rn(__ldg(x + (int64_t)t * H + h), __ldg(g_inp + h));
     float v[4];
     float mx = -INFINITY;
 #pragma unroll
@@ -236,6 +253,14 @@ __global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits,
         }
         if (lane == 0 && norm)
             for (int r = 0; r < K; ++r) wout[(int64_t)t * K + r] = __fdiv_rn(wout[(int64_t)t * K + r], tot);
+    } else if (warp == 1 && sp_smem) {
+        // candle's sum_keepdim order over the staged products (staged before the first barrier)
+        const int wholeh = H / 32;
+        float a = 0.f;
+        for (int i = 0; i < wholeh; ++i) a = __fadd_rn(a, sp[32 * i + lane]);
+        float sum = avx_lane_tree(a);
+        for (int j = wholeh * 32; j < H; ++j) sum = __fadd_rn(sum, sp[j]);
+        if (lane == 0) sgate[t] = __fdiv_rn(1.0f, __fadd_rn(exp_cr(-sum), 1.0f));
     } else if (warp == 1 && sgate) {
         const float* xr = x + (int64_t)t * H;
         const int wholeh = H / 32;
