@@ -326,6 +326,9 @@ extern "C" int cwx_ctx_destroy(cwx_ctx* c) {
     if (c->d_err) cudaFree(c->d_err);
     if (c->d_iq3s_map) cudaFree(c->d_iq3s_map);
     if (c->d_iq2s_map) cudaFree(c->d_iq2s_map);
+    if (c->side) cudaStreamDestroy(c->side);
+    if (c->ev_fork) cudaEventDestroy(c->ev_fork);
+    if (c->ev_join) cudaEventDestroy(c->ev_join);
     cwx_ctx_reset_profile(c);
     delete static_cast<ProfLog*>(c->prof);
     delete c;
@@ -468,22 +471,39 @@ extern "C" int cwx_expert_matmul(cwx_ctx* c, const cwx_bank* bank, const float* 
 
 // Gate/up, activation and down products on the grouped mma.sync products (every format, any
 // batch; the shared expert in the same launches).
-static int moe_gemv(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, const LayerPlan& p, cudaStream_t st) {
+// x's packed activation rows in every mode the layer's products take (one launch).
+static int prep_x(cwx_ctx* c, const cwx_moe_args* A, const LayerPlan& p, cudaStream_t st) {
+    PhaseTimer t(c, st, CWX_PHASE_PREP);
+    PrepArgs px[2];
+    int nx = 0;
+    for (int m = 0; m < 3; ++m)
+        if (p.xpk[m]) px[nx++] = prep(A->x, nullptr, p.T, p.H, m, p.xpk[m]);
+    int rc = launch_prep2(px, nx, st);
+    if (rc) return rc;
+    c->launches += 1;
+    t.end();
+    return CWX_OK;
+}
+
+// The context's side stream and its fork/join events (created on first use, on the context's
+// device); work forked onto it is captured into a graph like the main stream's.
+static int ctx_side(cwx_ctx* c) {
+    if (c->side) return CWX_OK;
+    CWX_CUDA(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
+    CWX_CUDA(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
+    CWX_CUDA(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming));
+    return CWX_OK;
+}
+
+// prepped: x's rows were already packed (forked alongside the routing).
+static int moe_gemv(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, const LayerPlan& p, cudaStream_t st,
+                    bool prepped = false) {
     const int T = p.T, H = p.H, E = p.E, K = p.K, I = p.I, Is = p.Is;
     const int64_t n = (int64_t)T * K;
     const bool shared = L->sh_gate != nullptr;
     int rc;
     const int64_t used_max = n < E ? n : E;
-    {
-        PhaseTimer t(c, st, CWX_PHASE_PREP);
-        PrepArgs px[2];
-        int nx = 0;
-        for (int m = 0; m < 3; ++m)
-            if (p.xpk[m]) px[nx++] = prep(A->x, nullptr, T, H, m, p.xpk[m]);
-        if ((rc = launch_prep2(px, nx, st))) return rc;
-        c->launches += 1;
-        t.end();
-    }
+    if (!prepped && (rc = prep_x(c, A, p, st))) return rc;
     // gate and up: routed piles and the shared expert, four matrix jobs in one launch. A product
     // whose result is re-quantised downstream (the down matrix takes Q8 activations) carries its
     // weights to ~22 bits, so the hidden state matches the CPU path closely enough that its Q8
@@ -685,6 +705,15 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
     const int64_t n = (int64_t)T * K;
     const bool shared = L->sh_gate != nullptr;
 
+    // x's activation rows depend only on x: packed on the side stream while the routing runs
+    const bool fork = !p.mma;
+    if (fork) {
+        if ((rc = ctx_side(c))) return rc;
+        CWX_CUDA(cudaEventRecord(c->ev_fork, st));
+        CWX_CUDA(cudaStreamWaitEvent(c->side, c->ev_fork, 0));
+        if ((rc = prep_x(c, A, p, c->side))) return rc;
+        CWX_CUDA(cudaEventRecord(c->ev_join, c->side));
+    }
     {
         PhaseTimer t(c, st, CWX_PHASE_ROUTER);
         if ((rc = launch_router(A->x, L->router_w, L->router_b, T, H, E, p.logits, st))) return rc;
@@ -703,10 +732,11 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
         t.end();
     }
     c->launches += 2 + perm_launches(n, E);
+    if (fork) CWX_CUDA(cudaStreamWaitEvent(st, c->ev_join, 0));
     if (p.mma) {
         if ((rc = moe_mma(c, L, A, p, st))) return rc;
     } else {
-        if ((rc = moe_gemv(c, L, A, p, st))) return rc;
+        if ((rc = moe_gemv(c, L, A, p, st, fork))) return rc;
     }
     {
         PhaseTimer t(c, st, CWX_PHASE_COMBINE);

@@ -181,6 +181,8 @@ struct cwx_ctx {
     void* prof;        // recorded (phase, start, end) events
     int64_t launches;  // kernel launches issued through this context
     int mma_min_pile;  // average picks per expert from which IQ layers take the tensor-core products (0: never)
+    cudaStream_t side;  // forked work inside a layer (created on first use)
+    cudaEvent_t ev_fork, ev_join;
 };
 
 namespace cwx {
