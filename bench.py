@@ -52,6 +52,7 @@ def parse():
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-prefill", action="store_true")
+    p.add_argument("--no-ep", action="store_true")
     return p.parse_args()
 
 
@@ -294,6 +295,69 @@ def impl_reference(a, rank, world):
 
 PREFILL_T = [1500, 4096]
 
+# Config 4 (expert parallelism, measured when the bench runs on 2+ ranks): 48 layers of
+# H2048 / E512 / top-10 / I512, IQ3_S gate/up, Q4_K down, a Q4_K shared expert, Zipf(1.1) router
+# bias over a seeded permutation of the experts, 8192 tokens split evenly over the ranks.
+EP_H, EP_E, EP_K, EP_I, EP_IS, EP_LAYERS, EP_SEED, EP_T = 2048, 512, 10, 512, 512, 48, 5, 8192
+
+
+def ep_runs(world, rank, local, a, maxall, barrier):
+    import numpy as np
+    import torch
+
+    from coachwhip_b200 import TYPE_IQ3_S, TYPE_Q4_K, _lib
+    from coachwhip_b200.ep import CudaEngine, ExpertParallelMoe
+    from coachwhip_b200.moe import Bank, ExpertAct, SharedExpert
+
+    dev = torch.device(f"cuda:{local}")
+    epr = EP_E // world
+    r = np.random.default_rng(EP_SEED).permutation(EP_E) + 1
+    zb = (-1.1 * np.log(r) - np.log(np.sum(np.arange(1, EP_E + 1, dtype=np.float64) ** -1.1))).astype(np.float32)
+    zipf = torch.from_numpy(zb).to(dev)
+    layers = []
+    for l in range(EP_LAYERS):
+        g = Bank.synth(TYPE_IQ3_S, EP_I, EP_H, epr, stream(EP_SEED, l, T_GATE), 0.02, local, first=rank * epr)
+        u = Bank.synth(TYPE_IQ3_S, EP_I, EP_H, epr, stream(EP_SEED, l, T_UP), 0.02, local, first=rank * epr)
+        d = Bank.synth(TYPE_Q4_K, EP_H, EP_I, epr, stream(EP_SEED, l, T_DOWN), 0.02, local, first=rank * epr)
+        sh = SharedExpert(synth_f32(EP_H, stream(EP_SEED, l, T_SGI), 0.02, dev),
+                          Bank.synth(TYPE_Q4_K, EP_IS, EP_H, 1, stream(EP_SEED, l, T_SG), 0.02, local),
+                          Bank.synth(TYPE_Q4_K, EP_IS, EP_H, 1, stream(EP_SEED, l, T_SU), 0.02, local),
+                          Bank.synth(TYPE_Q4_K, EP_H, EP_IS, 1, stream(EP_SEED, l, T_SD), 0.02, local))
+        w = synth_f32(EP_E * EP_H, stream(EP_SEED, l, T_RW), 0.02, dev).view(EP_E, EP_H)
+        eng = CudaEngine(w, EP_K, True, ExpertAct.Silu(), (g, u, d), world, rank, gate_bias=zipf, shared=sh,
+                         act_mode=_lib.ACT_MODE_F32)
+        eng._keep = (g, u, d, sh, w)
+        layers.append(ExpertParallelMoe(eng))
+    per = EP_T // world
+    x = synth_f32(EP_T * EP_H, stream(EP_SEED + 1, 0, T_IN), 1.0, dev).view(EP_T, EP_H)[rank * per:(rank + 1) * per]
+    x = x.contiguous().view(1, per, EP_H)
+
+    def run():
+        h = x
+        for m in layers:
+            h = m.forward(h, residual=h)
+        return h
+
+    for _ in range(max(1, a.warmup // 2)):
+        run()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 2
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = maxall(e0.elapsed_time(e1) / reps)
+    _lib.status(local)
+    fl = EP_LAYERS * (2 * EP_T * EP_K * 3 * EP_H * EP_I + 2 * EP_T * 3 * EP_H * EP_IS + 2 * EP_T * EP_H * EP_E)
+    return {"config": "config 4: 48 x MoE(H2048, E512, top10, I512, IQ3_S gate/up, Q4_K down, Q4_K shared, "
+                      "Zipf(1.1) router bias)", "tokens": EP_T, "tokens_per_rank": per, "ranks": world,
+            "experts_per_rank": epr, "ms_per_step": ms, "tokens_per_s": EP_T / (ms / 1e3),
+            "tflops": fl / (ms / 1e3) / 1e12, "act_mode": "f32 activations (O2 semantics)",
+            "transport": "NCCL all-to-all (torch.distributed all_to_all_single), one host read of the counts "
+                         "per layer", "timing": f"CUDA events over {reps} eager passes of the 48 layers, max over ranks"}
+
 
 def layer_flops(T):
     """Multiply-add FLOPs of one config-1 layer on T tokens: routed gate/up/down, shared expert, router."""
@@ -483,6 +547,11 @@ def main():
     for m in mods_f32:
         m.reserve(max(prefill_T) if prefill_T else 1)
     prefill = prefill_runs(mods_f32, prefill_T, a, dev, pk, maxall, barrier, world)
+    del mods_f32
+    ep = None
+    if world > 1 and not a.no_ep:
+        graphs.clear()  # the decode graphs are not replayed again; release before the EP banks
+        ep = ep_runs(world, rank, local, a, maxall, barrier)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
@@ -500,7 +569,7 @@ def main():
                 "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
                 "gpu_launches": int(launches_per_step * a.steps),
                 "decode_sweep": {str(b): d for b, d in sweep.items()},
-                "prefill": prefill}
+                "prefill": prefill, "expert_parallel": ep}
         print(json.dumps(line), flush=True)
     graphs.clear()
     if world > 1:

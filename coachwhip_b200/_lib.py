@@ -20,7 +20,7 @@ EXPORTS = [
     "cwx_bank_create", "cwx_bank_synth", "cwx_bank_destroy", "cwx_bank_desc", "cwx_bank_download",
     "cwx_bank_dequantize", "cwx_synth_normal", "cwx_route", "cwx_permute", "cwx_permute_noalloc", "cwx_expert_matmul", "cwx_moe_forward",
     "cwx_ctx_set_profiling", "cwx_ctx_read_profile", "cwx_ctx_reset_profile", "cwx_ctx_launches",
-    "cwx_ctx_set_mma_min_pile", "cwx_ep_dispatch", "cwx_ep_experts", "cwx_ep_combine",
+    "cwx_ctx_set_mma_min_pile", "cwx_ep_dispatch", "cwx_ep_experts", "cwx_ep_combine", "cwx_bank_synth_experts",
 ]
 PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine"]
 
@@ -86,6 +86,7 @@ def lib() -> ctypes.CDLL:
             "cwx_ctx_status": (I32, [P, P]),
             "cwx_bank_create": (I32, [I32, ctypes.POINTER(MatrixDesc), PP]),
             "cwx_bank_synth": (I32, [P, I32, I64, I64, I64, U64, F, PP]),
+            "cwx_bank_synth_experts": (I32, [P, I32, I64, I64, I64, I64, U64, F, PP]),
             "cwx_bank_destroy": (I32, [P]),
             "cwx_bank_desc": (I32, [P, ctypes.POINTER(MatrixDesc)]),
             "cwx_bank_download": (I32, [P, I64, I64, P]),

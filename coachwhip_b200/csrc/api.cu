@@ -161,8 +161,11 @@ static bool mma_layer(const cwx_ctx* c, const cwx_moe_layer* L, int T) {
     const int64_t pile = ((int64_t)T * L->top_k + L->n_experts - 1) / L->n_experts;
     if (pile < c->mma_min_pile) return false;
     const cwx_bank* bs[3] = {L->gate, L->up, L->down};
-    for (const cwx_bank* b : bs)
-        if (b->L.fmt != F_IQ2_S && b->L.fmt != F_IQ3_S) return false;
+    for (const cwx_bank* b : bs) {
+        const int f = b->L.fmt;
+        // Q4_K only with f32 activations (its Q8_K codes carry a per-piece, per-token scale)
+        if (f != F_IQ2_S && f != F_IQ3_S && !(f == F_Q4_K && act_mode_of(b, L->act_mode) == AM_F32)) return false;
+    }
     if (L->gate->L.fmt != L->up->L.fmt) return false;
     return L->hidden % 256 == 0 && L->inter % 256 == 0;
 }

@@ -339,8 +339,10 @@ __device__ void q6k_from_float_d(const float* x, uint8_t* y) {
 }
 
 // One thread per (expert, row, K-piece): draw the piece's values and quantise them in place.
-__global__ void k_synth(uint8_t* __restrict__ bank, Layout L, int64_t e0, int64_t ne, uint64_t key, float std_,
-                        const uint16_t* __restrict__ iq3map, const uint16_t* __restrict__ iq2map) {
+// Experts e0 .. e0+ne-1 of the bank; `first` is the bank's first expert in the synthetic tensor
+// (the values follow the global expert index, so a slice equals those experts of the whole).
+__global__ void k_synth(uint8_t* __restrict__ bank, Layout L, int64_t e0, int64_t ne, int64_t first, uint64_t key,
+                        float std_, const uint16_t* __restrict__ iq3map, const uint16_t* __restrict__ iq2map) {
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     int64_t total = ne * L.n * L.n_kp;
     if (i >= total) return;
@@ -354,7 +356,7 @@ __global__ void k_synth(uint8_t* __restrict__ bank, Layout L, int64_t e0, int64_
     int64_t c0 = (int64_t)kp * PIECE_K;
     int64_t klen = L.k - c0 < PIECE_K ? L.k - c0 : PIECE_K;
     float x[256];
-    uint64_t base = (uint64_t)(e * L.n + r) * (uint64_t)L.k + (uint64_t)c0;
+    uint64_t base = (uint64_t)((e + first) * L.n + r) * (uint64_t)L.k + (uint64_t)c0;
     for (int c = 0; c < klen; ++c) x[c] = cwx_normal_std(key, base + c, std_);
     switch (L.fmt) {
         case F_Q4_K: q4k_from_float_d(x, dst); break;
@@ -462,7 +464,13 @@ extern "C" int cwx_bank_create(int device, const cwx_matrix_desc* desc, cwx_bank
 
 extern "C" int cwx_bank_synth(cwx_ctx* ctx, int32_t type, int64_t n, int64_t k, int64_t ne, uint64_t key, float std_,
                               cwx_bank** out) {
+    return cwx_bank_synth_experts(ctx, type, n, k, 0, ne, key, std_, out);
+}
+
+extern "C" int cwx_bank_synth_experts(cwx_ctx* ctx, int32_t type, int64_t n, int64_t k, int64_t first, int64_t ne,
+                                      uint64_t key, float std_, cwx_bank** out) {
     if (!ctx) return fail(CWX_EINVAL, "cwx_bank_synth: null context");
+    if (first < 0) return fail(CWX_EINVAL, "cwx_bank_synth_experts: first expert %lld", (long long)first);
     int rc = alloc_bank(ctx->device, type, n, k, ne, out);
     if (rc) return rc;
     cwx_bank* b = *out;
@@ -481,7 +489,7 @@ extern "C" int cwx_bank_synth(cwx_ctx* ctx, int32_t type, int64_t n, int64_t k, 
             int64_t cnt = ne - e0 < experts_per_launch ? ne - e0 : experts_per_launch;
             int64_t items = cnt * n * b->L.n_kp;
             k_synth<<<(unsigned)((items + threads - 1) / threads), threads>>>(
-                b->d + e0 * b->L.expert_bytes, b->L, e0, cnt, key, std_, ctx->d_iq3s_map, ctx->d_iq2s_map);
+                b->d + e0 * b->L.expert_bytes, b->L, e0, cnt, first, key, std_, ctx->d_iq3s_map, ctx->d_iq2s_map);
             e = cudaGetLastError();
         }
     }

@@ -69,9 +69,12 @@ class Bank:
         return cls(h, ggml_type, n, k, n_experts, device)
 
     @classmethod
-    def synth(cls, ggml_type: int, n: int, k: int, n_experts: int, key: int, std: float, device: int = 0) -> "Bank":
+    def synth(cls, ggml_type: int, n: int, k: int, n_experts: int, key: int, std: float, device: int = 0,
+              first: int = 0) -> "Bank":
+        """Synthetic N(0, std^2) bank of stream `key`: experts first .. first + n_experts - 1 of it."""
         h = ctypes.c_void_p()
-        check(_lib.lib().cwx_bank_synth(_lib.ctx(device), ggml_type, n, k, n_experts, key, std, ctypes.byref(h)))
+        check(_lib.lib().cwx_bank_synth_experts(_lib.ctx(device), ggml_type, n, k, first, n_experts, key, std,
+                                                ctypes.byref(h)))
         return cls(h, ggml_type, n, k, n_experts, device)
 
     @property

@@ -92,6 +92,10 @@ int cwx_bank_create(int device, const cwx_matrix_desc* desc, cwx_bank** out);
  * (test and benchmark workloads; same values as the CPU generator). */
 int cwx_bank_synth(cwx_ctx* ctx, int32_t ggml_type, int64_t n, int64_t k, int64_t n_experts, uint64_t key,
                    float std_, cwx_bank** out);
+/* Experts [first, first + n_experts) of that synthetic tensor (an expert-parallel rank's slice;
+ * the values follow the global expert index). */
+int cwx_bank_synth_experts(cwx_ctx* ctx, int32_t ggml_type, int64_t n, int64_t k, int64_t first, int64_t n_experts,
+                           uint64_t key, float std_, cwx_bank** out);
 int cwx_bank_destroy(cwx_bank* bank);
 /* out[i] = std * N(0,1) element (offset + i) of stream `key`, i < n (synthetic router weights,
  * biases and inputs; same values as the CPU generator). */

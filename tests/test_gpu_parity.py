@@ -63,6 +63,9 @@ def test_synth_bank_matches_cpu_generator(fmt):
     want = O.synth_matrix(fmt, key, 0, E, n, k, 0.02)
     got = b.download()
     assert np.array_equal(got, want)
+    # an expert-parallel rank's slice: experts 1 .. 2 of a 3-expert tensor equal those experts
+    part = Bank.synth(fmt, n, k, 2, key, 0.02, first=1).download()
+    assert np.array_equal(part, O.synth_matrix(fmt, key, 1, 2, n, k, 0.02))
 
 
 def test_synth_normal_matches_cpu_generator():

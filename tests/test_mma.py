@@ -29,6 +29,9 @@ SPECS = {
     # picks take several column tiles
     "iq_wide": Spec(hidden=2048, n_experts=16, top_k=2, inter=512, gate_type=O.IQ2_S, up_type=O.IQ2_S,
                     down_type=O.IQ3_S, shared_inter=512, seed=2),
+    # config-4 family: IQ3_S gate/up, Q4_K down (tensor cores under the f32 policy only)
+    "iq3_q4k": Spec(hidden=512, n_experts=64, top_k=10, inter=256, gate_type=O.IQ3_S, up_type=O.IQ3_S,
+                    down_type=O.Q4_K, shared_inter=256, seed=5),
 }
 
 
@@ -53,7 +56,8 @@ def _launches():
     return _lib.lib().cwx_ctx_launches(_lib.ctx(0))
 
 
-@pytest.mark.parametrize("name,T", [("iq_mix", 256), ("iq_mix", 1500), ("iq3_iq2", 700), ("iq_wide", 1500)])
+@pytest.mark.parametrize("name,T", [("iq_mix", 256), ("iq_mix", 1500), ("iq3_iq2", 700), ("iq_wide", 1500),
+                                    ("iq3_q4k", 512)])
 @pytest.mark.parametrize("mode", [O.MODE_CANDLE, O.MODE_F32])
 def test_mma_forward_matches_oracle(name, T, mode):
     from coachwhip_b200 import _lib
