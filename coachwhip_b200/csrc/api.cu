@@ -131,6 +131,8 @@ struct LayerPlan {
     uint8_t *hpk, *hspk;     // packed hidden rows (routed, shared)
     float* y;
     float* ys;
+    int64_t xrows;     // rows of x (T, unless an expert-parallel call maps picks to received rows)
+    const uint32_t* rowmap;  // when set: activation row of pick p = rowmap[p]
     int mma;           // routed products on the tensor cores (IQ banks, large piles)
     int sh_mma;        // the shared expert on the tensor cores too (f32 activations)
     __half* x16;       // (T, H) f16 rows of x
@@ -206,6 +208,8 @@ static void plan_layer(const cwx_moe_layer* L, int T, int mma, uint8_t* base, La
     p->I = L->inter;
     p->Is = L->sh_gate ? (int)L->sh_gate->L.n : 0;
     p->T = T;
+    p->xrows = T;
+    p->rowmap = nullptr;
     p->mgu = act_mode_of(L->gate, L->act_mode);
     p->md = act_mode_of(L->down, L->act_mode);
     p->msgu = L->sh_gate ? act_mode_of(L->sh_gate, L->act_mode) : -1;
@@ -258,6 +262,7 @@ static GemvJob job(const cwx_bank* b, int shared, const uint8_t* act, int mode, 
     j.b = act;
     j.bstride = packed_row_bytes(k);
     j.bdiv = bdiv;
+    j.rowmap = nullptr;
     j.out = out;
     j.ostride = ostride;
     j.split = split;
@@ -480,7 +485,7 @@ static int prep_x(cwx_ctx* c, const cwx_moe_args* A, const LayerPlan& p, cudaStr
     PrepArgs px[2];
     int nx = 0;
     for (int m = 0; m < 3; ++m)
-        if (p.xpk[m]) px[nx++] = prep(A->x, nullptr, p.T, p.H, m, p.xpk[m]);
+        if (p.xpk[m]) px[nx++] = prep(A->x, nullptr, p.xrows, p.H, m, p.xpk[m]);
     int rc = launch_prep2(px, nx, st);
     if (rc) return rc;
     c->launches += 1;
@@ -517,6 +522,7 @@ static int moe_gemv(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, c
         const int split_r = p.md != AM_F32, split_s = shared && p.msd != AM_F32;
         a.job[a.njobs++] = job(L->gate, 0, p.xpk[p.mgu], p.mgu, H, K, p.g, I, split_r, nullptr);
         a.job[a.njobs++] = job(L->up, 0, p.xpk[p.mgu], p.mgu, H, K, p.u, I, split_r, nullptr);
+        a.job[0].rowmap = a.job[1].rowmap = p.rowmap;
         if (shared) {
             a.job[a.njobs++] = job(L->sh_gate, 1, p.xpk[p.msgu], p.msgu, H, 1, p.gs, Is, split_s, nullptr);
             a.job[a.njobs++] = job(L->sh_up, 1, p.xpk[p.msgu], p.msgu, H, 1, p.us, Is, split_s, nullptr);
@@ -598,7 +604,7 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
     int rc;
     {
         PhaseTimer t(c, st, CWX_PHASE_PREP);
-        if ((rc = launch_f16rows(A->x, (int64_t)T * H, p.x16, st))) return rc;
+        if ((rc = launch_f16rows(A->x, p.xrows * H, p.x16, st))) return rc;
         c->launches += 1;
         if (shared && !p.sh_mma) {
             if ((rc = launch_prep(prep(A->x, nullptr, T, H, p.msgu, p.xpk[p.msgu]), st))) return rc;
@@ -624,8 +630,9 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
         g.fused = 1;
         g.b = reinterpret_cast<const uint8_t*>(p.x16);
         g.bstride = (int64_t)H * 2;
-        g.brows = T;
         g.bdiv = K;
+        g.rowmap = p.rowmap;
+        g.brows = p.xrows;
         g.hout = p.h16;
         g.ostride = I;
         if ((rc = launch_mma(g, c->device, c->sm_count, st))) return rc;
@@ -774,64 +781,79 @@ static int ep_check(const cwx_moe_layer* L, const cwx_ep_group* g, const char* w
     return CWX_OK;
 }
 
+// Rows travel as f16 when the routed gate/up products read f16 activations anyway (IQ banks take
+// f16 activations on both product paths), which halves the dispatch exchange at no change in the
+// result; other formats get their f32 rows.
+static bool ep_rows_f16(const cwx_moe_layer* L) {
+    const int g = L->gate->L.fmt, u = L->up->L.fmt;
+    return (g == F_IQ2_S || g == F_IQ3_S) && (u == F_IQ2_S || u == F_IQ3_S);
+}
+
+extern "C" int cwx_ep_rows_f16(const cwx_moe_layer* L) { return L && L->gate && L->up && ep_rows_f16(L) ? 1 : 0; }
+
 extern "C" int cwx_ep_dispatch(cwx_ctx* c, const cwx_moe_layer* L, const cwx_ep_group* g, const float* x,
-                               int32_t tokens, uint32_t* ids, float* weights, uint32_t* pairs, float* sgate,
-                               float* send_rows, uint32_t* send_eids, int32_t* send_counts, void* stream) {
+                               int32_t tokens, uint32_t* ids, float* weights, float* sgate, int32_t* unit_of,
+                               void* send_rows, int32_t* send_picks, int32_t* send_counts, void* stream) {
     if (!c) return fail(CWX_EINVAL, "cwx_ep_dispatch: null context");
     int rc = ep_check(L, g, "cwx_ep_dispatch");
     if (rc) return rc;
     if (!L->router_w || L->top_k < 1 || L->top_k > 16 || L->top_k > L->n_experts || L->n_experts > 1024)
         return fail(CWX_EINVAL, "cwx_ep_dispatch: router or top_k out of range");
     if (tokens < 0) return fail(CWX_EINVAL, "cwx_ep_dispatch: tokens %d", tokens);
-    if (!send_counts || (tokens && (!x || !ids || !weights || !pairs || !send_rows || !send_eids)))
+    if (!send_counts || (tokens && (!x || !ids || !weights || !unit_of || !send_rows || !send_picks)))
         return fail(CWX_EINVAL, "cwx_ep_dispatch: null argument");
+    if (L->hidden % 4 || ((uintptr_t)x & 15)) return fail(CWX_EINVAL, "cwx_ep_dispatch: x rows must be 16-byte aligned");
     const bool shared = L->sh_gate != nullptr;
     if (shared && tokens && !sgate) return fail(CWX_EINVAL, "cwx_ep_dispatch: the shared expert needs sgate");
     CWX_CUDA(cudaSetDevice(c->device));
     cudaStream_t st = (cudaStream_t)stream;
-    const int T = tokens, H = L->hidden, E = L->n_experts, K = L->top_k;
-    const int64_t n = (int64_t)T * K;
-    Carve cv{nullptr, 0};
-    for (int pass = 0; pass < 2; ++pass) {
-        cv = Carve{pass ? c->ws : nullptr, 0};
-        cv.take<float>((size_t)T * E + 1);
-        cv.take<uint32_t>((size_t)3 * E);
-        cv.take<uint32_t>((size_t)3 * E);
-        cv.take<uint32_t>(4);
-        cv.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
-        if (!pass && (rc = ensure_ws(c, cv.off + 256, st))) return rc;
-    }
+    const int T = tokens, H = L->hidden, E = L->n_experts, K = L->top_k, W = g->world;
+    Carve sz{nullptr, 0};
+    sz.take<float>((size_t)T * E + 1);
+    sz.take<int32_t>((size_t)T * W + 1);
+    sz.take<int32_t>((size_t)T * W + 1);
+    if ((rc = ensure_ws(c, sz.off + 256, st))) return rc;
     Carve w{c->ws, 0};
     float* logits = w.take<float>((size_t)T * E + 1);
-    uint32_t* heads = w.take<uint32_t>((size_t)3 * E);
-    uint32_t* used3 = w.take<uint32_t>((size_t)3 * E);
-    uint32_t* n_used = w.take<uint32_t>(4);
-    uint32_t* perm = w.take<uint32_t>(perm_scratch_bytes(n, E) / 4);
+    int32_t* cnt = w.take<int32_t>((size_t)T * W + 1);
+    int32_t* pbase = w.take<int32_t>((size_t)T * W + 1);
     if (T > 0) {
         if ((rc = launch_router(x, L->router_w, L->router_b, T, H, E, logits, st))) return rc;
         if ((rc = launch_route(logits, T, E, K, L->norm_topk_prob, ids, weights, x,
                                shared ? L->sh_gate_inp : nullptr, H, shared ? sgate : nullptr, st)))
             return rc;
-        if ((rc = launch_permute(ids, n, E, pairs, heads, used3, n_used, perm, c->d_err, st))) return rc;
-        c->launches += 2 + perm_launches(n, E);
-    } else {
-        CWX_CUDA(cudaMemsetAsync(heads, 0, (size_t)3 * E * 4, st));
+        c->launches += 2;
     }
-    if ((rc = launch_ep_counts(heads, E, g->experts_per_rank, g->world, send_counts, st))) return rc;
-    if ((rc = launch_ep_pack(x, H, K, ids, pairs, n, g->experts_per_rank, send_rows, send_eids, st))) return rc;
-    c->launches += n > 0 ? 2 : 1;
+    if ((rc = launch_ep_units(x, T, H, K, W, g->experts_per_rank, ids, weights, cnt, unit_of, pbase, send_counts,
+                              ep_rows_f16(L), send_rows, send_picks, st)))
+        return rc;
+    c->launches += T > 0 ? 3 : 0;
     return CWX_OK;
 }
 
-extern "C" int cwx_ep_experts(cwx_ctx* c, const cwx_moe_layer* L, const cwx_ep_group* g, const float* rows,
-                              const uint32_t* eids, int32_t n_rows, float* y_rows, void* stream) {
+extern "C" int cwx_ep_experts(cwx_ctx* c, const cwx_moe_layer* L, const cwx_ep_group* g, const void* rows,
+                              const int32_t* picks, int32_t n_units, int32_t n_picks, int32_t n_src,
+                              const int32_t* src_units, const int32_t* src_picks, float* y_units, void* stream) {
     if (!c) return fail(CWX_EINVAL, "cwx_ep_experts: null context");
     int rc = ep_check(L, g, "cwx_ep_experts");
     if (rc) return rc;
-    if (n_rows < 0) return fail(CWX_EINVAL, "cwx_ep_experts: n_rows %d", n_rows);
-    if (n_rows == 0) return CWX_OK;
-    if (!rows || !eids || !y_rows) return fail(CWX_EINVAL, "cwx_ep_experts: null argument");
-    // this rank's experts as a layer of their own: one pick per row, no router, no shared expert
+    if (n_units < 0 || n_picks < 0 || n_src < 1 || n_src > 64 || !src_units || !src_picks)
+        return fail(CWX_EINVAL, "cwx_ep_experts: bad sizes");
+    EpOffsets off;
+    off.n = n_src;
+    int64_t su = 0, sp = 0;
+    for (int s = 0; s < n_src; ++s) {
+        off.ustart[s] = su;
+        off.pstart[s] = sp;
+        su += src_units[s];
+        sp += src_picks[s];
+    }
+    off.ustart[n_src] = su;
+    off.pstart[n_src] = sp;
+    if (su != n_units || sp != n_picks) return fail(CWX_EINVAL, "cwx_ep_experts: per-source counts do not add up");
+    if (n_picks == 0) return CWX_OK;
+    if (!rows || !picks || !y_units) return fail(CWX_EINVAL, "cwx_ep_experts: null argument");
+    // this rank's experts as a layer of their own: one pick per record, rows through the row map
     cwx_moe_layer lc = *L;
     lc.n_experts = g->experts_per_rank;
     lc.top_k = 1;
@@ -840,79 +862,141 @@ extern "C" int cwx_ep_experts(cwx_ctx* c, const cwx_moe_layer* L, const cwx_ep_g
     if ((rc = validate_layer(&lc))) return rc;
     CWX_CUDA(cudaSetDevice(c->device));
     cudaStream_t st = (cudaStream_t)stream;
-    const int mma = mma_layer(c, &lc, n_rows) ? 1 : 0;
+    const int H = L->hidden, E = lc.n_experts;
+    const bool f16 = ep_rows_f16(L);
+    const int mma = mma_layer(c, &lc, n_picks) ? 1 : 0;
     LayerPlan p;
-    plan_layer(&lc, n_rows, mma, nullptr, &p);
-    if ((rc = ensure_ws(c, p.bytes, st))) return rc;
-    plan_layer(&lc, n_rows, mma, c->ws, &p);
-    p.ids = const_cast<uint32_t*>(eids);  // per-row expert (the clamped SwiGLU biases index it)
-    p.y = y_rows;                          // down rows straight into the caller's buffer
-    if ((rc = launch_permute(eids, n_rows, lc.n_experts, p.pairs, p.heads, p.used3, p.n_used, p.perm, c->d_err, st)))
-        return rc;
-    c->launches += perm_launches(n_rows, lc.n_experts);
+    plan_layer(&lc, n_picks, mma, nullptr, &p);
+    const size_t base = (p.bytes + 255) & ~(size_t)255;
+    Carve ex{nullptr, 0};
+    ex.take<uint32_t>((size_t)n_picks);
+    ex.take<uint32_t>((size_t)n_picks);
+    ex.take<float>((size_t)n_picks);
+    ex.take<int32_t>((size_t)n_units + 1);
+    if (f16) ex.take<float>((size_t)n_units * H);
+    if ((rc = ensure_ws(c, base + ex.off + 256, st))) return rc;
+    plan_layer(&lc, n_picks, mma, c->ws, &p);
+    Carve w{c->ws + base, 0};
+    uint32_t* rowmap = w.take<uint32_t>((size_t)n_picks);
+    uint32_t* eid = w.take<uint32_t>((size_t)n_picks);
+    float* wgt = w.take<float>((size_t)n_picks);
+    int32_t* first = w.take<int32_t>((size_t)n_units + 1);
+    float* rows32 = f16 ? w.take<float>((size_t)n_units * H) : nullptr;
+    if ((rc = launch_ep_recv(picks, n_picks, off, rowmap, eid, wgt, first, st))) return rc;
+    const float* x = reinterpret_cast<const float*>(rows);
+    if (f16) {
+        if ((rc = launch_f16_to_f32(reinterpret_cast<const __half*>(rows), (int64_t)n_units * H, rows32, st)))
+            return rc;
+        x = rows32;
+    }
+    p.xrows = n_units;
+    p.rowmap = rowmap;
+    p.ids = eid;  // per-pick expert (the clamped SwiGLU biases index it)
+    if ((rc = launch_permute(eid, n_picks, E, p.pairs, p.heads, p.used3, p.n_used, p.perm, c->d_err, st))) return rc;
+    c->launches += 1 + (f16 ? 1 : 0) + perm_launches(n_picks, E);
     cwx_moe_args a;
     memset(&a, 0, sizeof a);
-    a.x = rows;
-    a.tokens = n_rows;
-    return p.mma ? moe_mma(c, &lc, &a, p, st) : moe_gemv(c, &lc, &a, p, st);
+    a.x = x;
+    a.tokens = n_units;
+    if ((rc = p.mma ? moe_mma(c, &lc, &a, p, st) : moe_gemv(c, &lc, &a, p, st))) return rc;
+    if ((rc = launch_ep_unit_sum(p.y, wgt, first, n_units, n_picks, H, y_units, st))) return rc;
+    c->launches += 1;
+    return CWX_OK;
 }
 
-extern "C" int cwx_ep_combine(cwx_ctx* c, const cwx_moe_layer* L, const float* x, int32_t tokens,
-                              const float* weights, const uint32_t* pairs, const float* back_rows, const float* sgate,
+// The shared expert on the local tokens into ys (T, H): the tensor-core products when they apply
+// (f32 activations, large batch), else the grouped mma.sync products.
+static int ep_shared(cwx_ctx* c, const cwx_moe_layer* L, const float* x, int T, float** ys_out, cudaStream_t st) {
+    const int H = L->hidden, Is = (int)L->sh_gate->L.n;
+    LayerPlan p;
+    memset(&p, 0, sizeof p);
+    p.T = T;
+    p.xrows = T;
+    p.H = H;
+    p.K = 1;
+    p.Is = Is;
+    p.msgu = act_mode_of(L->sh_gate, L->act_mode);
+    p.msd = act_mode_of(L->sh_down, L->act_mode);
+    const bool tc = shared_mma_ok(L) && c->mma_min_pile > 0 && T >= c->mma_min_pile;
+    for (int pass = 0; pass < 2; ++pass) {
+        Carve w{pass ? c->ws : nullptr, 0};
+        p.ys = w.take<float>((size_t)T * H);
+        p.n_used = w.take<uint32_t>(4);
+        p.used3 = w.take<uint32_t>(4);
+        p.pairs = w.take<uint32_t>((size_t)T + 1);
+        if (tc) {
+            p.x16 = w.take<__half>((size_t)T * H);
+            p.hs16 = w.take<__half>((size_t)T * Is);
+        } else {
+            p.xpk[p.msgu] = w.take<uint8_t>((size_t)(T * packed_row_bytes(H)));
+            p.gs = w.take<float>((size_t)T * Is);
+            p.us = w.take<float>((size_t)T * Is);
+            p.hspk = w.take<uint8_t>((size_t)(T * packed_row_bytes(Is)));
+        }
+        if (!pass) {
+            int rc = ensure_ws(c, w.off + 256, st);
+            if (rc) return rc;
+        }
+    }
+    int rc;
+    if (tc) {
+        if ((rc = launch_f16rows(x, (int64_t)T * H, p.x16, st))) return rc;
+        if ((rc = launch_all_tokens(p.pairs, T, p.used3, p.n_used, st))) return rc;
+        MmaArgs m;
+        memset(&m, 0, sizeof m);
+        m.pairs = p.pairs;
+        m.used3 = p.used3;
+        m.n_used = p.n_used;
+        m.err = c->d_err;
+        m.bdiv = 1;
+        MmaArgs gu = m;
+        gu.a0 = mref(L->sh_gate);
+        gu.a1 = mref(L->sh_up);
+        gu.fused = 1;
+        gu.b = reinterpret_cast<const uint8_t*>(p.x16);
+        gu.bstride = (int64_t)H * 2;
+        gu.brows = T;
+        gu.hout = p.hs16;
+        gu.ostride = Is;
+        if ((rc = launch_mma(gu, c->device, c->sm_count, st))) return rc;
+        MmaArgs dn = m;
+        dn.a0 = mref(L->sh_down);
+        dn.b = reinterpret_cast<const uint8_t*>(p.hs16);
+        dn.bstride = (int64_t)Is * 2;
+        dn.brows = T;
+        dn.out = p.ys;
+        dn.ostride = H;
+        if ((rc = launch_mma(dn, c->device, c->sm_count, st))) return rc;
+        c->launches += 4;
+    } else {
+        CWX_CUDA(cudaMemsetAsync(p.n_used, 0, 16, st));  // the shared-only product launches read it
+        if ((rc = launch_prep(prep(x, nullptr, T, H, p.msgu, p.xpk[p.msgu]), st))) return rc;
+        if ((rc = shared_gemv(c, L, p, 0, st))) return rc;
+        if ((rc = launch_prep(prep(p.gs, p.us, T, Is, p.msd, p.hspk), st))) return rc;
+        if ((rc = shared_gemv(c, L, p, 1, st))) return rc;
+        c->launches += 4;
+    }
+    *ys_out = p.ys;
+    return CWX_OK;
+}
+
+extern "C" int cwx_ep_combine(cwx_ctx* c, const cwx_moe_layer* L, const cwx_ep_group* g, const float* x,
+                              int32_t tokens, const int32_t* unit_of, const float* back_rows, const float* sgate,
                               const float* residual, float* out, void* stream) {
-    if (!c || !L) return fail(CWX_EINVAL, "cwx_ep_combine: null argument");
+    if (!c || !L || !g) return fail(CWX_EINVAL, "cwx_ep_combine: null argument");
     if (tokens < 0) return fail(CWX_EINVAL, "cwx_ep_combine: tokens %d", tokens);
     if (tokens == 0) return CWX_OK;
-    if (!x || !weights || !pairs || !back_rows || !out) return fail(CWX_EINVAL, "cwx_ep_combine: null argument");
+    if (!x || !unit_of || !out || g->world < 1 || g->world > 64) return fail(CWX_EINVAL, "cwx_ep_combine: bad argument");
     const bool shared = L->sh_gate != nullptr;
     if (shared && (!sgate || !L->sh_up || !L->sh_down || !L->sh_gate_inp))
         return fail(CWX_EINVAL, "cwx_ep_combine: incomplete shared expert");
     CWX_CUDA(cudaSetDevice(c->device));
     cudaStream_t st = (cudaStream_t)stream;
-    const int T = tokens, H = L->hidden, K = L->top_k;
-    const int64_t n = (int64_t)T * K;
-    LayerPlan p;
-    memset(&p, 0, sizeof p);
-    p.T = T;
-    p.H = H;
-    p.K = K;
-    p.Is = shared ? (int)L->sh_gate->L.n : 0;
-    p.msgu = shared ? act_mode_of(L->sh_gate, L->act_mode) : -1;
-    p.msd = shared ? act_mode_of(L->sh_down, L->act_mode) : -1;
-    size_t need = 0;
-    for (int pass = 0; pass < 2; ++pass) {
-        Carve w{pass ? c->ws : nullptr, 0};
-        uint32_t* inv = w.take<uint32_t>((size_t)n);
-        p.n_used = w.take<uint32_t>(4);
-        p.used3 = w.take<uint32_t>(4);
-        p.pairs = p.n_used;
-        if (shared) {
-            p.xpk[p.msgu] = w.take<uint8_t>((size_t)(T * packed_row_bytes(H)));
-            p.gs = w.take<float>((size_t)T * p.Is);
-            p.us = w.take<float>((size_t)T * p.Is);
-            p.hspk = w.take<uint8_t>((size_t)(T * packed_row_bytes(p.Is)));
-            p.ys = w.take<float>((size_t)T * H);
-        }
-        if (!pass) {
-            need = w.off + 256;
-            int rc = ensure_ws(c, need, st);
-            if (rc) return rc;
-            continue;
-        }
-        int rc;
-        CWX_CUDA(cudaMemsetAsync(p.n_used, 0, 16, st));  // the shared-only product launches read it
-        if ((rc = launch_inverse(pairs, n, inv, st))) return rc;
-        c->launches += 1;
-        if (shared) {
-            if ((rc = launch_prep(prep(x, nullptr, T, H, p.msgu, p.xpk[p.msgu]), st))) return rc;
-            if ((rc = shared_gemv(c, L, p, 0, st))) return rc;
-            if ((rc = launch_prep(prep(p.gs, p.us, T, p.Is, p.msd, p.hspk), st))) return rc;
-            if ((rc = shared_gemv(c, L, p, 1, st))) return rc;
-            c->launches += 4;
-        }
-        if ((rc = launch_combine(back_rows, weights, T, K, H, shared ? p.ys : nullptr, sgate, residual, out, st, inv)))
-            return rc;
-        c->launches += 1;
-    }
+    int rc;
+    float* ys = nullptr;
+    if (shared && (rc = ep_shared(c, L, x, tokens, &ys, st))) return rc;
+    if ((rc = launch_ep_combine(back_rows, unit_of, tokens, g->world, L->hidden, ys, sgate, residual, out, st)))
+        return rc;
+    c->launches += 1;
     return CWX_OK;
 }

@@ -1,69 +1,246 @@
 // Expert parallelism: the per-rank steps around the two all-to-all exchanges.
 //
-//   reference  experts are sharded across devices by the SURVEY's EP design; the reference itself
-//              runs one device, so the layer's semantics are StreamedMoe::forward
-//              (crates/engine/src/experts.rs:2539-2614) and cw_pile's grouping (fuse_kernel.rs:180-202).
+//   reference  experts are sharded across devices by expert (one exchange each way); the reference
+//              itself runs one device, so the layer's semantics are StreamedMoe::forward
+//              (crates/engine/src/experts.rs:2539-2614): out[t] = sum over picks of w * expert(x[t]).
 //
-// Dispatch: the local tokens' picks, in pile order (grouped by expert, ascending pick index inside
-// an expert), are also grouped by destination rank, because rank d owns the contiguous experts
-// [d*epr, (d+1)*epr). One block per pick copies its token's row; the expert id is rewritten to
-// the expert's index on the destination rank.
-// Combine: the rows coming back arrive in the same pile order; inv maps a pick to its row.
+// Units: a token sends its row once to every rank that owns at least one of its picks (a unit =
+// (token, destination rank)), with one record per pick (the unit's index in the message, the
+// expert's index on the destination, the pick's weight). Units of a destination are in token
+// order, a unit's records in pick order. The destination runs the picks, sums each unit's
+// weighted rows in pick order and sends one row per unit back; the source adds its units' rows in
+// rank order. With top-k picks over W ranks a token sends min(k, W)-ish rows instead of k.
 #include "cwx_common.cuh"
 #include "kernels.cuh"
 
 namespace cwx {
 
-__global__ void __launch_bounds__(256) k_ep_pack(const float* __restrict__ x, int H, int K,
-                                                 const uint32_t* __restrict__ ids, const uint32_t* __restrict__ pairs,
-                                                 int epr, float* __restrict__ send_rows,
-                                                 uint32_t* __restrict__ send_eids) {
-    const int64_t pos = blockIdx.x;
-    const uint32_t p = pairs[pos];
-    const int64_t t = p / (uint32_t)K;
-    if (threadIdx.x == 0) send_eids[pos] = ids[p] % (uint32_t)epr;
-    const float* src = x + t * H;
-    float* dst = send_rows + pos * H;
-    if ((H & 3) == 0) {
-        for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4)
-            *reinterpret_cast<float4*>(dst + c) = *reinterpret_cast<const float4*>(src + c);
-    } else {
-        for (int c = threadIdx.x; c < H; c += blockDim.x) dst[c] = src[c];
+// Picks of each token per destination rank: cnt[t * W + d].
+__global__ void k_ep_count(const uint32_t* __restrict__ ids, int T, int K, int epr, int W, int32_t* __restrict__ cnt) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    for (int d = 0; d < W; ++d) cnt[(int64_t)t * W + d] = 0;
+    for (int j = 0; j < K; ++j) {
+        const int d = (int)(ids[(int64_t)t * K + j] / (uint32_t)epr);
+        cnt[(int64_t)t * W + d] += 1;
     }
 }
 
-__global__ void k_ep_counts(const uint32_t* __restrict__ heads, int E, int epr, int world, int32_t* __restrict__ counts) {
-    const int d = blockIdx.x * blockDim.x + threadIdx.x;
-    if (d >= world) return;
-    int64_t c = 0;
-    for (int e = d * epr; e < (d + 1) * epr && e < E; ++e) c += heads[3 * e + 2];
-    counts[d] = (int32_t)c;
+// Per destination d (one block each): exclusive scans over the tokens of [cnt > 0] (unit
+// position) and of cnt (first record), and the totals.
+__global__ void __launch_bounds__(1024) k_ep_scan(const int32_t* __restrict__ cnt, int T, int W,
+                                                  int32_t* __restrict__ upos, int32_t* __restrict__ pbase,
+                                                  int32_t* __restrict__ tot /* (W, 2): units, picks */) {
+    __shared__ int32_t su[32], sp[32];
+    __shared__ int32_t carry_u, carry_p;
+    const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) carry_u = carry_p = 0;
+    __syncthreads();
+    for (int t0 = 0; t0 < T; t0 += 1024) {
+        const int t = t0 + tid;
+        const int c = t < T ? cnt[(int64_t)t * W + d] : 0;
+        int u = c > 0, p = c;
+        // inclusive warp scans
+        for (int o = 1; o < 32; o <<= 1) {
+            const int uu = __shfl_up_sync(0xffffffffu, u, o), pp = __shfl_up_sync(0xffffffffu, p, o);
+            if (lane >= o) {
+                u += uu;
+                p += pp;
+            }
+        }
+        if (lane == 31) {
+            su[warp] = u;
+            sp[warp] = p;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            int a = su[lane], b = sp[lane];
+            for (int o = 1; o < 32; o <<= 1) {
+                const int aa = __shfl_up_sync(0xffffffffu, a, o), bb = __shfl_up_sync(0xffffffffu, b, o);
+                if (lane >= o) {
+                    a += aa;
+                    b += bb;
+                }
+            }
+            su[lane] = a;
+            sp[lane] = b;
+        }
+        __syncthreads();
+        const int wu = warp ? su[warp - 1] : 0, wp = warp ? sp[warp - 1] : 0;
+        if (t < T) {
+            upos[(int64_t)t * W + d] = c > 0 ? carry_u + wu + u - 1 : -1;
+            pbase[(int64_t)t * W + d] = carry_p + wp + p - c;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            carry_u += su[31];
+            carry_p += sp[31];
+        }
+        __syncthreads();
+    }
+    if (tid == 0) {
+        tot[2 * d] = carry_u;
+        tot[2 * d + 1] = carry_p;
+    }
 }
 
-__global__ void k_inverse(const uint32_t* __restrict__ pairs, int64_t n, uint32_t* __restrict__ inv) {
-    const int64_t pos = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (pos < n) inv[pairs[pos]] = (uint32_t)pos;
+// One block per token: its row to each destination it has picks on (f32, or f16 when the
+// destination's products take f16 activations), and its pick records. upos becomes the unit's
+// index in the whole send buffer (destination offsets added).
+template <bool F16>
+__global__ void __launch_bounds__(256) k_ep_pack_units(const float* __restrict__ x, int T, int H, int K, int W,
+                                                       int epr, const uint32_t* __restrict__ ids,
+                                                       const float* __restrict__ w, int32_t* __restrict__ upos,
+                                                       const int32_t* __restrict__ pbase,
+                                                       const int32_t* __restrict__ tot, void* __restrict__ send_rows,
+                                                       int32_t* __restrict__ send_picks) {
+    const int t = blockIdx.x;
+    __shared__ int32_t uoff[64], poff[64];
+    if (threadIdx.x == 0) {
+        int32_t a = 0, b = 0;
+        for (int d = 0; d < W; ++d) {
+            uoff[d] = a;
+            poff[d] = b;
+            a += tot[2 * d];
+            b += tot[2 * d + 1];
+        }
+    }
+    __syncthreads();
+    const float* src = x + (int64_t)t * H;
+    for (int d = 0; d < W; ++d) {
+        const int32_t u = upos[(int64_t)t * W + d];
+        if (u < 0) continue;
+        const int64_t g = (int64_t)uoff[d] + u;
+        if (F16) {
+            __half* dst = reinterpret_cast<__half*>(send_rows) + g * H;
+            for (int c = threadIdx.x * 2; c < H; c += blockDim.x * 2)
+                *reinterpret_cast<__half2*>(dst + c) = __floats2half2_rn(src[c], src[c + 1]);
+        } else {
+            float* dst = reinterpret_cast<float*>(send_rows) + g * H;
+            for (int c = threadIdx.x * 4; c < H; c += blockDim.x * 4)
+                *reinterpret_cast<float4*>(dst + c) = *reinterpret_cast<const float4*>(src + c);
+        }
+        if (threadIdx.x == 0) {
+            int32_t r = poff[d] + pbase[(int64_t)t * W + d];
+            for (int j = 0; j < K; ++j) {
+                const uint32_t e = ids[(int64_t)t * K + j];
+                if ((int)(e / (uint32_t)epr) != d) continue;
+                send_picks[3 * (int64_t)r] = u;  // unit index within the message to d
+                send_picks[3 * (int64_t)r + 1] = (int32_t)(e % (uint32_t)epr);
+                send_picks[3 * (int64_t)r + 2] = __float_as_int(w[(int64_t)t * K + j]);
+                ++r;
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)  // the unit's index in the whole send buffer, for the combine
+        for (int d = 0; d < W; ++d) {
+            const int32_t u = upos[(int64_t)t * W + d];
+            if (u >= 0) upos[(int64_t)t * W + d] = uoff[d] + u;
+        }
 }
 
-int launch_ep_pack(const float* x, int H, int K, const uint32_t* ids, const uint32_t* pairs, int64_t n, int epr,
-                   float* send_rows, uint32_t* send_eids, cudaStream_t st) {
+// Receiver: records of source s occupy [pstart[s], pstart[s+1]); their units start at ustart[s].
+// rowmap[p] = the pick's row (unit) in the received buffer, eid[p], wgt[p]; first[u] = the unit's
+// first record (units are contiguous runs of records).
+__global__ void k_ep_recv(const int32_t* __restrict__ picks, int64_t P, EpOffsets off, uint32_t* __restrict__ rowmap,
+                          uint32_t* __restrict__ eid, float* __restrict__ wgt, int32_t* __restrict__ first) {
+    const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= P) return;
+    int s = 0;
+    while (s + 1 < off.n && p >= off.pstart[s + 1]) ++s;
+    const uint32_t u = (uint32_t)(picks[3 * p] + off.ustart[s]);
+    rowmap[p] = u;
+    eid[p] = (uint32_t)picks[3 * p + 1];
+    wgt[p] = __int_as_float(picks[3 * p + 2]);
+    // a unit's records are a run inside its source's segment
+    if (p == off.pstart[s] || picks[3 * (p - 1)] != picks[3 * p]) first[u] = (int32_t)p;
+}
+
+// yu[u] = sum over the unit's records p in order of wgt[p] * y[p].
+__global__ void __launch_bounds__(256) k_ep_unit_sum(const float* __restrict__ y, const float* __restrict__ wgt,
+                                                     const int32_t* __restrict__ first, int64_t U, int64_t P, int H,
+                                                     float* __restrict__ yu) {
+    const int64_t u = blockIdx.x;
+    const int64_t p0 = first[u], p1 = u + 1 < U ? first[u + 1] : P;
+    for (int c = threadIdx.x; c < H; c += blockDim.x) {
+        float acc = 0.f;
+        for (int64_t p = p0; p < p1; ++p) acc = __fadd_rn(acc, __fmul_rn(y[p * H + c], wgt[p]));
+        yu[u * H + c] = acc;
+    }
+}
+
+// out[t] = sum over destination ranks in order of the returned unit rows + sgate * shared + residual.
+__global__ void __launch_bounds__(256) k_ep_combine(const float* __restrict__ back, const int32_t* __restrict__ unit,
+                                                    int T, int W, int H, const float* __restrict__ shared,
+                                                    const float* __restrict__ sgate,
+                                                    const float* __restrict__ residual, float* __restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)T * H) return;
+    const int64_t t = i / H, c = i % H;
+    float acc = 0.f;
+    for (int d = 0; d < W; ++d) {
+        const int32_t u = unit[t * W + d];
+        if (u >= 0) acc = __fadd_rn(acc, back[(int64_t)u * H + c]);
+    }
+    if (shared) acc = __fadd_rn(acc, __fmul_rn(shared[t * H + c], sgate[t]));
+    if (residual) acc = __fadd_rn(acc, residual[i]);
+    out[i] = acc;
+}
+
+__global__ void k_f16_to_f32(const __half* __restrict__ x, int64_t n, float* __restrict__ y) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __half2float(x[i]);
+}
+
+static int launched(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CWX_OK : cuda_fail(e, what);
+}
+
+int launch_ep_units(const float* x, int T, int H, int K, int W, int epr, const uint32_t* ids, const float* w,
+                    int32_t* cnt, int32_t* upos, int32_t* pbase, int32_t* tot, bool f16, void* send_rows,
+                    int32_t* send_picks, cudaStream_t st) {
+    if (W > 64) return fail(CWX_EUNSUPPORTED, "expert parallelism over more than 64 ranks");
+    if (T == 0) {
+        CWX_CUDA(cudaMemsetAsync(tot, 0, (size_t)2 * W * 4, st));
+        return CWX_OK;
+    }
+    k_ep_count<<<(T + 255) / 256, 256, 0, st>>>(ids, T, K, epr, W, cnt);
+    k_ep_scan<<<W, 1024, 0, st>>>(cnt, T, W, upos, pbase, tot);
+    if (f16)
+        k_ep_pack_units<true><<<T, 256, 0, st>>>(x, T, H, K, W, epr, ids, w, upos, pbase, tot, send_rows, send_picks);
+    else
+        k_ep_pack_units<false><<<T, 256, 0, st>>>(x, T, H, K, W, epr, ids, w, upos, pbase, tot, send_rows, send_picks);
+    return launched("expert-parallel dispatch kernels");
+}
+
+int launch_f16_to_f32(const __half* x, int64_t n, float* y, cudaStream_t st) {
     if (n == 0) return CWX_OK;
-    k_ep_pack<<<(unsigned)n, 256, 0, st>>>(x, H, K, ids, pairs, epr, send_rows, send_eids);
-    cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_ep_pack");
+    k_f16_to_f32<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, n, y);
+    return launched("k_f16_to_f32");
 }
 
-int launch_ep_counts(const uint32_t* heads, int E, int epr, int world, int32_t* counts, cudaStream_t st) {
-    k_ep_counts<<<(world + 127) / 128, 128, 0, st>>>(heads, E, epr, world, counts);
-    cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_ep_counts");
+int launch_ep_recv(const int32_t* picks, int64_t P, const EpOffsets& off, uint32_t* rowmap, uint32_t* eid,
+                   float* wgt, int32_t* first, cudaStream_t st) {
+    if (P == 0) return CWX_OK;
+    k_ep_recv<<<(unsigned)((P + 255) / 256), 256, 0, st>>>(picks, P, off, rowmap, eid, wgt, first);
+    return launched("k_ep_recv");
 }
 
-int launch_inverse(const uint32_t* pairs, int64_t n, uint32_t* inv, cudaStream_t st) {
-    if (n == 0) return CWX_OK;
-    k_inverse<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(pairs, n, inv);
-    cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_inverse");
+int launch_ep_unit_sum(const float* y, const float* wgt, const int32_t* first, int64_t U, int64_t P, int H, float* yu,
+                       cudaStream_t st) {
+    if (U == 0) return CWX_OK;
+    k_ep_unit_sum<<<(unsigned)U, 256, 0, st>>>(y, wgt, first, U, P, H, yu);
+    return launched("k_ep_unit_sum");
+}
+
+int launch_ep_combine(const float* back, const int32_t* unit, int T, int W, int H, const float* shared,
+                      const float* sgate, const float* residual, float* out, cudaStream_t st) {
+    if (T == 0) return CWX_OK;
+    const int64_t n = (int64_t)T * H;
+    k_ep_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(back, unit, T, W, H, shared, sgate, residual, out);
+    return launched("k_ep_combine");
 }
 
 }  // namespace cwx

@@ -177,7 +177,7 @@ __device__ __forceinline__ void pass_rows(const GemvArgs& a, const Item& it, int
         *orow = ip;
     } else {
         const uint32_t p = a.pairs[it.first + ip];
-        *arow = p / (uint32_t)jb.bdiv;
+        *arow = jb.rowmap ? jb.rowmap[p] : p / (uint32_t)jb.bdiv;
         *orow = p;
     }
 }

@@ -19,6 +19,7 @@ struct GemvJob {
     const uint8_t* b;   // packed activation rows (act.cu), bstride bytes apart
     int64_t bstride;
     int bdiv;           // routed: activation row = pick index / bdiv
+    const uint32_t* rowmap;  // or, when set: activation row = rowmap[pick index]
     float* out;         // output rows: pick index (routed) or token (shared)
     int64_t ostride;
     int split;          // products carried to ~22 bits (weights and activations as f16 hi + lo)
@@ -79,13 +80,24 @@ int launch_prep2(const PrepArgs* p, int njobs, cudaStream_t st);  // up to two p
 int launch_combine(const float* rows, const float* w, int T, int K, int H, const float* shared, const float* sgate,
                    const float* residual, float* out, cudaStream_t st, const uint32_t* idx = nullptr);
 
-// Expert parallelism (ep.cu): the picks in pile order grouped by the rank that owns their expert.
-// send_rows[pos] = x[pairs[pos] / K], send_eids[pos] = the expert's index on its rank.
-int launch_ep_pack(const float* x, int H, int K, const uint32_t* ids, const uint32_t* pairs, int64_t n, int epr,
-                   float* send_rows, uint32_t* send_eids, cudaStream_t st);
-// counts[d] = picks for rank d (from the pile heads); inv[pairs[pos]] = pos.
-int launch_ep_counts(const uint32_t* heads, int E, int epr, int world, int32_t* counts, cudaStream_t st);
-int launch_inverse(const uint32_t* pairs, int64_t n, uint32_t* inv, cudaStream_t st);
+// Expert parallelism (ep.cu): units (token, destination rank) and their pick records.
+struct EpOffsets {  // received records of source s: [pstart[s], pstart[s+1]); its units from ustart[s]
+    int n;
+    int64_t pstart[65];
+    int64_t ustart[65];
+};
+// Dispatch: cnt/upos/pbase are (T, W) scratch; upos ends as each unit's index in the send buffer
+// (-1: no picks there); tot (W, 2) = units and records per destination.
+int launch_ep_units(const float* x, int T, int H, int K, int W, int epr, const uint32_t* ids, const float* w,
+                    int32_t* cnt, int32_t* upos, int32_t* pbase, int32_t* tot, bool f16, void* send_rows,
+                    int32_t* send_picks, cudaStream_t st);
+int launch_ep_recv(const int32_t* picks, int64_t P, const EpOffsets& off, uint32_t* rowmap, uint32_t* eid,
+                   float* wgt, int32_t* first, cudaStream_t st);
+int launch_ep_unit_sum(const float* y, const float* wgt, const int32_t* first, int64_t U, int64_t P, int H, float* yu,
+                       cudaStream_t st);
+int launch_ep_combine(const float* back, const int32_t* unit, int T, int W, int H, const float* shared,
+                      const float* sgate, const float* residual, float* out, cudaStream_t st);
+int launch_f16_to_f32(const __half* x, int64_t n, float* y, cudaStream_t st);
 // experts_est: the number of experts expected to have picks (sizes the grid and the K split).
 int launch_gemv(const GemvArgs& a, int64_t experts_est, int device, int sm_count, cudaStream_t st);
 
@@ -98,6 +110,7 @@ struct MmaArgs {
     int64_t bstride;
     int64_t brows;       // activation rows
     int bdiv;            // activation row = pair / bdiv
+    const uint32_t* rowmap;  // or, when set: activation row = rowmap[pair]
     const uint32_t* pairs;
     const uint32_t* used3;
     const uint32_t* n_used;

@@ -432,7 +432,12 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
 #pragma unroll
             for (int j = 0; j < GATHER_PER; ++j) {
                 const uint32_t n = (uint32_t)(t >> 3) + 16 * j;
-                row[j] = n < m.ntok ? (int)(a.pairs[m.first + m.n0 + n] / (uint32_t)a.bdiv) : -1;
+                if (n < m.ntok) {
+                    const uint32_t pk = a.pairs[m.first + m.n0 + n];
+                    row[j] = (int)(a.rowmap ? a.rowmap[pk] : pk / (uint32_t)a.bdiv);
+                } else {
+                    row[j] = -1;
+                }
             }
             for (int ks = 0; ks < nks; ++ks, ++c) {
                 const int s = (int)(c % NS);

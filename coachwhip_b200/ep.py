@@ -4,16 +4,17 @@ The reference runs one device; this is the multi-GPU form of its layer (Streamed
 crates/engine/src/experts.rs:2539-2614) with the same output. Rank r owns experts
 [r*epr, (r+1)*epr) (epr = n_experts / world) and routes its own tokens. One layer:
 
-  1. dispatch (cwx_ep_dispatch): router, route and piles over all experts; the picks' rows in
-     pile order, which groups them by the rank that owns their expert, with each pick's expert
-     rewritten to its index on that rank;
-  2. exchange the per-rank counts, then the rows and expert indices (all-to-all with uneven
-     splits);
-  3. experts (cwx_ep_experts): the received rows through this rank's experts, one pick per row;
-  4. exchange the result rows back (the reverse splits), so every rank gets its picks' rows in
-     the order it sent them;
-  5. combine (cwx_ep_combine): weighted sum in pick order + shared expert on the local tokens +
-     residual.
+  1. dispatch (cwx_ep_dispatch): router and route over all experts; a token's row goes once to
+     each rank that owns any of its picks (a unit), with one record per pick (unit, expert index
+     on that rank, weight);
+  2. exchange the per-rank counts (units, records), then the rows and the records (all-to-all
+     with uneven splits);
+  3. experts (cwx_ep_experts): the received records through this rank's experts, each unit's
+     weighted sum in record order;
+  4. exchange the unit rows back (the reverse splits), so every rank gets its units in the order
+     it sent them;
+  5. combine (cwx_ep_combine): the units' rows summed in rank order + shared expert on the local
+     tokens + residual.
 
 The exchanges use torch.distributed (NCCL between GPUs; the steps themselves run in libcwx.so).
 The count exchange is read on the host to size the row exchange, so a layer synchronises once.
@@ -35,15 +36,14 @@ from .moe import Bank, ExpertAct, SharedExpert, _dev_index, _ptr, _stream
 
 @dataclass
 class Dispatched:
-    """What step 1 leaves for step 5 and the rows it sends."""
+    """What step 1 leaves for step 5 and what it sends."""
 
-    x: torch.Tensor          # (T, H) f32 local tokens
-    weights: torch.Tensor    # (T, k) f32
-    pairs: torch.Tensor      # (T*k,) pile order of the picks
+    x: torch.Tensor           # (T, H) f32 local tokens
+    unit_of: torch.Tensor     # (T, world) int32: the token's unit in send_rows per rank, or -1
     sgate: torch.Tensor | None
-    send_rows: torch.Tensor  # (T*k, H) f32
-    send_eids: torch.Tensor  # (T*k,) int32 expert index on the destination rank
-    send_counts: torch.Tensor  # (world,) int32
+    send_rows: torch.Tensor   # (units, H) f16 or f32, destinations in rank order
+    send_picks: torch.Tensor  # (records, 3) int32: unit in its message, expert on the rank, weight bits
+    send_counts: torch.Tensor  # (world, 2) int32: units, records per destination
 
 
 class CudaEngine:
@@ -78,38 +78,45 @@ class CudaEngine:
         L.act_mode = act_mode
         self._layer = L
         self._group = _lib.EpGroup(world, rank, self.epr)
+        self.row_dtype = torch.float16 if _lib.lib().cwx_ep_rows_f16(ctypes.byref(L)) else torch.float32
 
     def dispatch(self, x: torch.Tensor) -> Dispatched:
         T, H = x.shape
+        W = self._group.world
         n = T * self.top_k
         dev = x.device
         ids = torch.empty(n, dtype=torch.int32, device=dev)
-        w = torch.empty((T, self.top_k), dtype=torch.float32, device=dev)
-        pairs = torch.empty(n, dtype=torch.int32, device=dev)
+        w = torch.empty(n, dtype=torch.float32, device=dev)
         sgate = torch.empty(T, dtype=torch.float32, device=dev) if self.shared is not None else None
-        rows = torch.empty((n, H), dtype=torch.float32, device=dev)
-        eids = torch.empty(n, dtype=torch.int32, device=dev)
-        counts = torch.empty(self._group.world, dtype=torch.int32, device=dev)
+        unit_of = torch.empty((T, W), dtype=torch.int32, device=dev)
+        rows = torch.empty((T * min(self.top_k, W), H), dtype=self.row_dtype, device=dev)
+        picks = torch.empty((n, 3), dtype=torch.int32, device=dev)
+        counts = torch.empty((W, 2), dtype=torch.int32, device=dev)
         check(_lib.lib().cwx_ep_dispatch(_lib.ctx(_dev_index(x)), ctypes.byref(self._layer), ctypes.byref(self._group),
-                                         x.data_ptr(), T, ids.data_ptr(), w.data_ptr(), pairs.data_ptr(), _ptr(sgate),
-                                         rows.data_ptr(), eids.data_ptr(), counts.data_ptr(), _stream(dev)))
-        return Dispatched(x, w, pairs, sgate, rows, eids, counts)
+                                         x.data_ptr(), T, ids.data_ptr(), w.data_ptr(), _ptr(sgate),
+                                         unit_of.data_ptr(), rows.data_ptr(), picks.data_ptr(), counts.data_ptr(),
+                                         _stream(dev)))
+        return Dispatched(x, unit_of, sgate, rows, picks, counts)
 
-    def experts(self, rows: torch.Tensor, eids: torch.Tensor) -> torch.Tensor:
-        n = rows.shape[0]
-        y = torch.empty((n, self.hidden), dtype=torch.float32, device=rows.device)
-        if n:
+    def experts(self, rows: torch.Tensor, picks: torch.Tensor, src_units: list[int],
+                src_picks: list[int]) -> torch.Tensor:
+        nu, npk = rows.shape[0], picks.shape[0]
+        y = torch.empty((nu, self.hidden), dtype=torch.float32, device=rows.device)
+        if npk:
+            su = (ctypes.c_int32 * len(src_units))(*src_units)
+            sp = (ctypes.c_int32 * len(src_picks))(*src_picks)
             check(_lib.lib().cwx_ep_experts(_lib.ctx(_dev_index(rows)), ctypes.byref(self._layer),
-                                            ctypes.byref(self._group), rows.data_ptr(), eids.data_ptr(), n,
-                                            y.data_ptr(), _stream(rows.device)))
+                                            ctypes.byref(self._group), rows.data_ptr(), picks.data_ptr(), nu, npk,
+                                            len(src_units), su, sp, y.data_ptr(), _stream(rows.device)))
         return y
 
     def combine(self, d: Dispatched, back: torch.Tensor, residual: torch.Tensor | None) -> torch.Tensor:
         T, H = d.x.shape
         out = torch.empty((T, H), dtype=torch.float32, device=d.x.device)
-        check(_lib.lib().cwx_ep_combine(_lib.ctx(_dev_index(d.x)), ctypes.byref(self._layer), d.x.data_ptr(), T,
-                                        d.weights.data_ptr(), d.pairs.data_ptr(), back.data_ptr(), _ptr(d.sgate),
-                                        _ptr(residual), out.data_ptr(), _stream(d.x.device)))
+        check(_lib.lib().cwx_ep_combine(_lib.ctx(_dev_index(d.x)), ctypes.byref(self._layer),
+                                        ctypes.byref(self._group), d.x.data_ptr(), T, d.unit_of.data_ptr(),
+                                        back.data_ptr(), _ptr(d.sgate), _ptr(residual), out.data_ptr(),
+                                        _stream(d.x.device)))
         return out
 
 
@@ -136,7 +143,7 @@ class ExpertParallelMoe:
         x = xs.reshape(b * s, h).to(torch.float32).contiguous()
         res = None if residual is None else residual.reshape(b * s, h).to(torch.float32).contiguous()
         d = self.engine.dispatch(x)
-        # counts first: every rank learns how many rows each peer sends it
+        # counts first: every rank learns how many units and records each peer sends it
         recv_counts = torch.empty_like(d.send_counts)
         if self.world == 1:
             recv_counts.copy_(d.send_counts)
@@ -144,16 +151,16 @@ class ExpertParallelMoe:
             import torch.distributed as dist
 
             dist.all_to_all_single(recv_counts, d.send_counts, group=self.group)
-        sc = [int(v) for v in d.send_counts.tolist()]
-        rc = [int(v) for v in recv_counts.tolist()]
-        nr = sum(rc)
-        rows = torch.empty((nr, h), dtype=torch.float32, device=x.device)
-        eids = torch.empty(nr, dtype=torch.int32, device=x.device)
-        self._a2a(rows, d.send_rows, rc, sc)
-        self._a2a(eids, d.send_eids, rc, sc)
-        y = self.engine.experts(rows, eids)
-        back = torch.empty((sum(sc), h), dtype=torch.float32, device=x.device)
-        self._a2a(back, y, sc, rc)
+        sc, rc = d.send_counts.tolist(), recv_counts.tolist()
+        su, sp = [int(v[0]) for v in sc], [int(v[1]) for v in sc]
+        ru, rp = [int(v[0]) for v in rc], [int(v[1]) for v in rc]
+        rows = torch.empty((sum(ru), h), dtype=d.send_rows.dtype, device=x.device)
+        picks = torch.empty((sum(rp), 3), dtype=torch.int32, device=x.device)
+        self._a2a(rows, d.send_rows[:sum(su)], ru, su)
+        self._a2a(picks, d.send_picks[:sum(sp)], rp, sp)
+        y = self.engine.experts(rows, picks, ru, rp)
+        back = torch.empty((sum(su), h), dtype=torch.float32, device=x.device)
+        self._a2a(back, y, su, ru)
         out = self.engine.combine(d, back, res)
         return out.reshape(b, s, h).to(xs.dtype)
 

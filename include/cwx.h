@@ -179,32 +179,38 @@ int cwx_moe_forward(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_moe_args
 
 /* Expert parallelism (no counterpart in the reference, which runs one device): the experts are
  * split contiguously over `world` ranks, rank r owning experts [r*epr, (r+1)*epr); every rank
- * routes its own tokens. A layer is three calls around two all-to-all exchanges the caller
- * makes (NCCL, or any transport):
- *   1. cwx_ep_dispatch: router, route and piles over all n_experts; the picks' rows in pile
- *      order, which groups them by destination rank (send_counts[d] rows for rank d, in rank
- *      order), with each pick's expert rewritten to its index on that rank (send_eids);
- *   (exchange send_counts, then send_rows and send_eids with those split sizes)
- *   2. cwx_ep_experts: the received rows through this rank's experts, one pick per row ->
- *      y_rows (n_rows, hidden), in the order received;
- *   (exchange y_rows back with the reverse split sizes: each rank gets its rows in the order it
- *   sent them)
- *   3. cwx_ep_combine: out = sum over picks in pick order of weight * returned row, + shared
- *      expert (computed on the local tokens) * sgate, + residual.
- * The layer's n_experts and router are global; its banks (and expert biases) hold this rank's
- * epr experts. ids/weights/pairs (tokens*top_k) and sgate (tokens) are caller buffers that carry
- * the routing from step 1 to step 3; send_counts is a device int32 array of `world`. */
+ * routes its own tokens. A token sends its row once to each rank that owns any of its picks (a
+ * unit), with one record per pick: (unit index in that message, the expert's index on that rank,
+ * the pick's weight) as three int32 (the weight's f32 bits). A layer is three calls around two
+ * all-to-all exchanges the caller makes (NCCL, or any transport):
+ *   1. cwx_ep_dispatch: router and route over all n_experts; for each destination d (in rank
+ *      order) its units in token order and their records in pick order: send_counts[2d] units
+ *      and send_counts[2d+1] records; unit_of (tokens, world) receives each token's unit index in
+ *      send_rows per destination, or -1;
+ *   (exchange send_counts, then the rows (unit splits) and the records (record splits))
+ *   2. cwx_ep_experts: the received records through this rank's experts, then each unit's
+ *      weighted sum in record order -> y_units (n_units, hidden) f32, in the order received;
+ *      src_units / src_picks (host arrays of n_src) are the per-source counts received;
+ *   (exchange y_units back with the reverse unit splits: each rank gets its units in send order)
+ *   3. cwx_ep_combine: out[t] = sum over destinations in rank order of its returned unit rows,
+ *      + shared expert (on the local tokens) * sgate, + residual.
+ * Rows are f16 when cwx_ep_rows_f16(layer) (the routed gate/up products read f16 activations
+ * anyway: the result is unchanged), else f32. The layer's n_experts and router are global; its
+ * banks (and expert biases) hold this rank's epr experts. send_rows holds up to
+ * tokens * min(top_k, world) rows, send_picks tokens * top_k records. */
 typedef struct {
     int32_t world, rank, experts_per_rank;
 } cwx_ep_group;
+int cwx_ep_rows_f16(const cwx_moe_layer* layer);
 int cwx_ep_dispatch(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_ep_group* group, const float* x,
-                    int32_t tokens, uint32_t* ids, float* weights, uint32_t* pairs, float* sgate, float* send_rows,
-                    uint32_t* send_eids, int32_t* send_counts, void* stream);
-int cwx_ep_experts(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_ep_group* group, const float* rows,
-                   const uint32_t* eids, int32_t n_rows, float* y_rows, void* stream);
-int cwx_ep_combine(cwx_ctx* ctx, const cwx_moe_layer* layer, const float* x, int32_t tokens, const float* weights,
-                   const uint32_t* pairs, const float* back_rows, const float* sgate, const float* residual,
-                   float* out, void* stream);
+                    int32_t tokens, uint32_t* ids, float* weights, float* sgate, int32_t* unit_of, void* send_rows,
+                    int32_t* send_picks, int32_t* send_counts, void* stream);
+int cwx_ep_experts(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_ep_group* group, const void* rows,
+                   const int32_t* picks, int32_t n_units, int32_t n_picks, int32_t n_src, const int32_t* src_units,
+                   const int32_t* src_picks, float* y_units, void* stream);
+int cwx_ep_combine(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_ep_group* group, const float* x,
+                   int32_t tokens, const int32_t* unit_of, const float* back_rows, const float* sgate,
+                   const float* residual, float* out, void* stream);
 
 /* Per-phase timing of cwx_moe_forward, the analogue of the reference's --profile Stats
  * (crates/engine/src/experts.rs:2541-2552): with profiling on, each call records a CUDA event

@@ -16,8 +16,8 @@ def expert_bytes(L: dict, which: str) -> int:
 
 
 class OracleEngine:
-    """This rank's steps on the CPU with the oracle's primitives (router, route, piles, per-expert
-    products, layer forward for the shared expert)."""
+    """This rank's steps on the CPU with the oracle's primitives (router, route, per-expert
+    products, layer forward for the shared expert), on the same unit protocol as CudaEngine."""
 
     def __init__(self, L: dict, world: int, rank: int, mode: int):
         self.L, self.world, self.rank, self.mode = L, world, rank, mode
@@ -29,47 +29,64 @@ class OracleEngine:
 
         from coachwhip_b200.ep import Dispatched
 
-        L, K = self.L, self.K
+        L, K, W = self.L, self.K, self.world
         xn = x.numpy()
+        T = xn.shape[0]
         logits = O.router(xn, L["router_w"], L.get("router_b"))
         ids, w = O.route(logits, K, bool(L["norm_topk_prob"]))
-        pairs, _ = O.permute(ids, self.E)
-        e = ids.reshape(-1)[pairs]
-        rows = np.ascontiguousarray(xn[pairs // K])
-        counts = np.bincount(e // self.epr, minlength=self.world).astype(np.int32)
-        return Dispatched(x, torch.from_numpy(w), torch.from_numpy(pairs.astype(np.int32)), None,
-                          torch.from_numpy(rows), torch.from_numpy((e % self.epr).astype(np.int32)),
+        unit_of = -np.ones((T, W), dtype=np.int32)
+        rows, recs, counts = [], [], np.zeros((W, 2), dtype=np.int32)
+        for d in range(W):  # destinations in rank order, their units in token order
+            for t in range(T):
+                js = [j for j in range(K) if ids[t, j] // self.epr == d]
+                if not js:
+                    continue
+                u = counts[d, 0]
+                unit_of[t, d] = len(rows)
+                rows.append(xn[t])
+                for j in js:
+                    recs.append((u, ids[t, j] % self.epr, np.float32(w[t, j]).view(np.int32)))
+                counts[d, 0] += 1
+                counts[d, 1] += len(js)
+        rows = np.array(rows, dtype=np.float32).reshape(-1, self.H)
+        recs = np.array(recs, dtype=np.int32).reshape(-1, 3)
+        return Dispatched(x, torch.from_numpy(unit_of), None, torch.from_numpy(rows), torch.from_numpy(recs),
                           torch.from_numpy(counts))
 
-    def experts(self, rows, eids):
+    def experts(self, rows, picks, src_units, src_picks):
         import torch
 
         L, H, I = self.L, self.H, self.I
-        r, ei = rows.numpy(), eids.numpy()
-        y = np.zeros((r.shape[0], H), dtype=np.float32)
-        for el in np.unique(ei):
-            sel = np.nonzero(ei == el)[0]
+        r, pk = rows.numpy(), picks.numpy()
+        uoff = np.concatenate([[0], np.cumsum(src_units)])
+        poff = np.concatenate([[0], np.cumsum(src_picks)])
+        unit = np.concatenate([pk[poff[s]:poff[s + 1], 0] + uoff[s] for s in range(len(src_units))]).astype(np.int64)
+        eid, wgt = pk[:, 1], pk[:, 2].view(np.float32)
+        y = np.zeros((pk.shape[0], H), dtype=np.float32)
+        for el in np.unique(eid):
+            sel = np.nonzero(eid == el)[0]
             e = int(self.rank * self.epr + el)
-            g = O.matmul(L["gate_type"], self.mode, L["gate_bank"], I, H, expert_bytes(L, "gate"), e, r[sel])
-            u = O.matmul(L["up_type"], self.mode, L["up_bank"], I, H, expert_bytes(L, "up"), e, r[sel])
+            xr = r[unit[sel]]
+            g = O.matmul(L["gate_type"], self.mode, L["gate_bank"], I, H, expert_bytes(L, "gate"), e, xr)
+            u = O.matmul(L["up_type"], self.mode, L["up_bank"], I, H, expert_bytes(L, "up"), e, xr)
             h = (g / (np.float32(1) + np.exp(-g))) * u
             y[sel] = O.matmul(L["down_type"], self.mode, L["down_bank"], H, I, expert_bytes(L, "down"), e,
                               h.astype(np.float32))
-        return torch.from_numpy(y)
+        yu = np.zeros((r.shape[0], H), dtype=np.float32)
+        for p in range(pk.shape[0]):  # each unit's weighted sum in record order
+            yu[unit[p]] += wgt[p] * y[p]
+        return torch.from_numpy(yu)
 
     def combine(self, d, back, residual):
         import torch
 
-        K = self.K
-        pairs = d.pairs.numpy().astype(np.int64)
-        inv = np.empty_like(pairs)
-        inv[pairs] = np.arange(pairs.size)
         b = back.numpy()
-        w = d.weights.numpy()
-        T = w.shape[0]
+        uo = d.unit_of.numpy()
+        T = uo.shape[0]
         out = np.zeros((T, self.H), dtype=np.float32)
-        for j in range(K):
-            out += w[:, j:j + 1] * b[inv[np.arange(T) * K + j]]
+        for dd in range(self.world):
+            has = uo[:, dd] >= 0
+            out[has] += b[uo[has, dd]]
         out += O.moe_forward(self.L, d.x.numpy(), self.mode)["shared"]
         if residual is not None:
             out += residual.numpy()

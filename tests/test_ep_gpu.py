@@ -35,22 +35,24 @@ def _emulated(L, x, world, mode):
     per = T // world
     xs = [torch.from_numpy(np.ascontiguousarray(x[r * per:(r + 1) * per])).cuda() for r in range(world)]
     ds = [engines[r].dispatch(xs[r]) for r in range(world)]
-    counts = [d.send_counts.cpu().tolist() for d in ds]
-    offs = [np.concatenate([[0], np.cumsum(c)]) for c in counts]
+    counts = [d.send_counts.cpu().numpy() for d in ds]  # (world, 2): units, records per destination
+    uo = [np.concatenate([[0], np.cumsum(c[:, 0])]) for c in counts]
+    po = [np.concatenate([[0], np.cumsum(c[:, 1])]) for c in counts]
     ys = []
-    for dst in range(world):  # rows for rank dst, from every source in rank order
-        rows = torch.cat([ds[s].send_rows[offs[s][dst]:offs[s][dst + 1]] for s in range(world)])
-        eids = torch.cat([ds[s].send_eids[offs[s][dst]:offs[s][dst + 1]] for s in range(world)])
-        ys.append((engines[dst].experts(rows, eids), [counts[s][dst] for s in range(world)]))
+    for dst in range(world):  # units and records for rank dst, from every source in rank order
+        rows = torch.cat([ds[s].send_rows[uo[s][dst]:uo[s][dst + 1]] for s in range(world)])
+        picks = torch.cat([ds[s].send_picks[po[s][dst]:po[s][dst + 1]] for s in range(world)])
+        su = [int(counts[s][dst, 0]) for s in range(world)]
+        sp = [int(counts[s][dst, 1]) for s in range(world)]
+        ys.append((engines[dst].experts(rows, picks, su, sp), su))
     outs = []
-    for s in range(world):  # back to each source, in the order it sent
+    for s in range(world):  # unit rows back to each source, in the order it sent them
         parts = []
         for dst in range(world):
-            y, rc = ys[dst]
-            o = int(np.sum(rc[:s]))
-            parts.append(y[o:o + rc[s]])
-        back = torch.cat(parts)
-        outs.append(engines[s].combine(ds[s], back, None))
+            y, su = ys[dst]
+            o = int(np.sum(su[:s]))
+            parts.append(y[o:o + su[s]])
+        outs.append(engines[s].combine(ds[s], torch.cat(parts), None))
     from coachwhip_b200 import _lib
 
     _lib.status(0)
