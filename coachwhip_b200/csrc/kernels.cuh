@@ -1,8 +1,6 @@
 // Argument blocks and host launchers of the cwx kernels (route.cu, gemv.cu, act.cu), used by
 // api.cu.
 #pragma once
-#include <cuda.h>
-
 #include "cwx_common.cuh"
 
 namespace cwx {
@@ -103,12 +101,11 @@ int launch_gemv(const GemvArgs& a, int64_t experts_est, int device, int sm_count
 
 // Tensor-core (tcgen05) expert products for large piles (mma.cu).
 struct MmaArgs {
-    CUtensorMap bmap;    // activation rows as a 2-D tensor (set by the launcher)
     MatRef a0, a1;       // weights; a1: the up matrix of a fused gate/up launch
     int fused;           // 1: gate/up rows side by side, SwiGLU epilogue writing f16 h rows
     const uint8_t* b;    // activation rows (f16), bstride bytes apart
     int64_t bstride;
-    int64_t brows;       // activation rows
+    int64_t brows;       // activation rows (their offsets must fit 32 bits)
     int bdiv;            // activation row = pair / bdiv
     const uint32_t* rowmap;  // or, when set: activation row = rowmap[pair]
     const uint32_t* pairs;
