@@ -47,8 +47,8 @@ constexpr int A_BYTES = 128 * 128;
 constexpr int B_BYTES = NMAX * 128;
 constexpr int Q_BYTES = 128 * 144;  // 128 rows of the largest piece (Q4_K)
 constexpr int XCH_BYTES = 32 * 64 * 4;
-constexpr int THREADS = 20 * 32;
-constexpr int W_MMA = 4, W_QCOPY = 5, W_GATHER = 6, N_GATHER = 4, W_DEC = 10, N_DEC = 10;
+constexpr int THREADS = 22 * 32;
+constexpr int W_MMA = 4, W_QCOPY = 5, W_GATHER = 6, N_GATHER = 4, W_DEC = 10, N_DEC = 12;
 constexpr int DEC_CHUNKS = 128 * 8;                                   // 16-byte A chunks per stage
 constexpr int DEC_PER = (DEC_CHUNKS + N_DEC * 32 - 1) / (N_DEC * 32);  // per decoder thread
 constexpr int GATHER_PER = NMAX * 8 / (N_GATHER * 32);                 // B chunks per gather thread
