@@ -21,7 +21,7 @@ EXPORTS = [
     "cwx_bank_dequantize", "cwx_synth_normal", "cwx_route", "cwx_permute", "cwx_permute_noalloc", "cwx_expert_matmul", "cwx_moe_forward",
     "cwx_ctx_set_profiling", "cwx_ctx_read_profile", "cwx_ctx_reset_profile", "cwx_ctx_launches",
     "cwx_ctx_set_mma_min_pile", "cwx_ep_dispatch", "cwx_ep_experts", "cwx_ep_combine", "cwx_bank_synth_experts",
-    "cwx_ep_rows_f16",
+    "cwx_ep_rows_f16", "cwx_ctx_check_wait",
 ]
 PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine"]
 
@@ -104,6 +104,7 @@ def lib() -> ctypes.CDLL:
             "cwx_ctx_launches": (I64, [P]),
             "cwx_ctx_set_mma_min_pile": (I32, [P, I32]),
             "cwx_ep_rows_f16": (I32, [ctypes.POINTER(MoeLayer)]),
+            "cwx_ctx_check_wait": (I32, [P, I32, P]),
             "cwx_ep_dispatch": (I32, [P, ctypes.POINTER(MoeLayer), ctypes.POINTER(EpGroup), P, I32, P, P, P, P, P,
                                       P, P, P]),
             "cwx_ep_experts": (I32, [P, ctypes.POINTER(MoeLayer), ctypes.POINTER(EpGroup), P, P, I32, I32, I32, P, P,

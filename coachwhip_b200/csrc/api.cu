@@ -384,6 +384,27 @@ extern "C" int cwx_ctx_status(cwx_ctx* c, void* stream) {
     return fail(CWX_EDEVICE, "device error %d", h);
 }
 
+// One bounded wait on an mbarrier that nothing completes (the failure path of every kernel's
+// waits): the wait gives up after limit_ns, records DE_TIMEOUT and the kernel returns.
+__global__ void k_wait_check(int* err, uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_wait(&bar, 0, err, limit_ns);
+    }
+}
+
+extern "C" int cwx_ctx_check_wait(cwx_ctx* c, int32_t limit_us, void* stream) {
+    if (!c) return fail(CWX_EINVAL, "cwx_ctx_check_wait: null context");
+    if (limit_us < 1 || limit_us > 1000000) return fail(CWX_EINVAL, "cwx_ctx_check_wait: limit %d us", limit_us);
+    CWX_CUDA(cudaSetDevice(c->device));
+    k_wait_check<<<1, 32, 0, (cudaStream_t)stream>>>(c->d_err, (uint64_t)limit_us * 1000);
+    CWX_CUDA(cudaGetLastError());
+    c->launches += 1;
+    return CWX_OK;
+}
+
 extern "C" int cwx_ctx_reserve(cwx_ctx* c, const void* layer, int32_t tokens) {
     if (!c || !layer) return fail(CWX_EINVAL, "cwx_ctx_reserve: null argument");
     const cwx_moe_layer* L = (const cwx_moe_layer*)layer;

@@ -85,6 +85,11 @@ int cwx_ctx_destroy(cwx_ctx* ctx);
 int cwx_ctx_reserve(cwx_ctx* ctx, const void* layer, int32_t tokens);
 /* Synchronises `stream`, returns CWX_OK or the first device-side error recorded (and clears it). */
 int cwx_ctx_status(cwx_ctx* ctx, void* stream);
+/* Diagnostic of the failure path: one device-side wait, bounded like every wait of the library,
+ * on a barrier that nothing completes. After limit_us (1 .. 1e6) it gives up and records the
+ * timeout; the next cwx_ctx_status reports CWX_ETIMEOUT and clears it, and the context stays
+ * usable. */
+int cwx_ctx_check_wait(cwx_ctx* ctx, int32_t limit_us, void* stream);
 
 /* Bank: copy a GGUF expert tensor into HBM (replaces ExpertStore::resident_op's exact_load). */
 int cwx_bank_create(int device, const cwx_matrix_desc* desc, cwx_bank** out);

@@ -52,3 +52,46 @@ def test_expert_parallel_protocol_on_two_gloo_ranks():
     assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
     res = dict(q.get(timeout=5) for _ in range(2))
     assert max(res.values()) < 1e-5, res
+
+
+def _rank_dies(rank, world, port, q):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from coachwhip_b200.ep import ExpertParallelMoe
+    from tests.ep_common import OracleEngine
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=15))
+    if rank == 1:
+        os._exit(0)  # the peer dies between layers, with nothing in flight
+    L = build_cpu(SPEC)
+    x = torch.from_numpy(np.ascontiguousarray(make_input(SPEC, T)[: T // world]))
+    moe = ExpertParallelMoe(OracleEngine(L, world, rank, O.MODE_F32))
+    try:
+        moe.forward(x[None])
+        q.put("completed")
+    except Exception as e:  # the exchange reports the lost peer instead of waiting forever
+        q.put(f"raised: {type(e).__name__}")
+
+
+def test_lost_peer_is_reported_not_waited_on():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_rank_dies, args=(r, 2, 29613, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=120)
+    alive = [p.is_alive() for p in ps]
+    for p in ps:
+        if p.is_alive():
+            p.kill()
+    assert not any(alive)
+    msg = q.get(timeout=5)
+    assert msg.startswith("raised"), msg

@@ -83,6 +83,22 @@ def test_ep_rank_with_no_tokens_and_no_picks():
     assert rel_l2(out, O.moe_forward(L, x, O.MODE_F32)["out"]) < RTOL
 
 
+def test_ep_inconsistent_counts_are_refused():
+    # a receive-count list that does not add up to the rows and records handed over
+    import ctypes
+
+    from coachwhip_b200 import CwxError, _lib
+
+    s = SPECS["q4k"]
+    L = build_cpu(s)
+    eng = gpu_engine(L, 2, 0, 0, O.MODE_F32)
+    rows = torch.zeros((3, s.hidden), dtype=eng.row_dtype, device="cuda")
+    picks = torch.zeros((4, 3), dtype=torch.int32, device="cuda")
+    with pytest.raises(CwxError, match="do not add up"):
+        eng.experts(rows, picks, [1, 1], [2, 2])
+    _lib.status(0)
+
+
 def _nccl_rank(rank, world, port, q):
     import torch.distributed as dist
 
