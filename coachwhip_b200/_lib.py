@@ -21,7 +21,9 @@ EXPORTS = [
     "cwx_bank_dequantize", "cwx_synth_normal", "cwx_route", "cwx_permute", "cwx_permute_noalloc", "cwx_expert_matmul", "cwx_moe_forward",
     "cwx_ctx_set_profiling", "cwx_ctx_read_profile", "cwx_ctx_reset_profile", "cwx_ctx_launches",
     "cwx_ctx_set_mma_min_pile", "cwx_ep_dispatch", "cwx_ep_experts", "cwx_ep_combine", "cwx_bank_synth_experts",
-    "cwx_ep_rows_f16", "cwx_ctx_check_wait",
+    "cwx_ep_rows_f16", "cwx_ctx_check_wait", "cwx_gguf_open", "cwx_gguf_close", "cwx_gguf_info",
+    "cwx_gguf_tensor_info", "cwx_gguf_tensor", "cwx_bank_from_gguf", "cwx_gguf_tensor_f32", "cwx_gguf_meta_int",
+    "cwx_gguf_meta_f64", "cwx_gguf_meta_str",
 ]
 PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine"]
 
@@ -110,6 +112,16 @@ def lib() -> ctypes.CDLL:
             "cwx_ep_experts": (I32, [P, ctypes.POINTER(MoeLayer), ctypes.POINTER(EpGroup), P, P, I32, I32, I32, P, P,
                                      P, P]),
             "cwx_ep_combine": (I32, [P, ctypes.POINTER(MoeLayer), ctypes.POINTER(EpGroup), P, I32, P, P, P, P, P, P]),
+            "cwx_gguf_open": (I32, [ctypes.c_char_p, PP]),
+            "cwx_gguf_close": (I32, [P]),
+            "cwx_gguf_info": (I32, [P, P, P, P, P]),
+            "cwx_gguf_tensor_info": (I32, [P, ctypes.c_char_p, P, P, P, P]),
+            "cwx_gguf_tensor": (I32, [P, ctypes.c_char_p, ctypes.POINTER(MatrixDesc)]),
+            "cwx_bank_from_gguf": (I32, [I32, P, ctypes.c_char_p, I64, I64, PP]),
+            "cwx_gguf_tensor_f32": (I32, [P, ctypes.c_char_p, P, I64]),
+            "cwx_gguf_meta_int": (I32, [P, ctypes.c_char_p, P]),
+            "cwx_gguf_meta_f64": (I32, [P, ctypes.c_char_p, P]),
+            "cwx_gguf_meta_str": (I32, [P, ctypes.c_char_p, P, I64, P]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)

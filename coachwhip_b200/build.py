@@ -1,8 +1,8 @@
 """Builds libcwx.so (the CUDA library behind include/cwx.h) in-tree, for sm_100a.
 
-Each .cu under csrc/ is compiled separately with nvcc and linked into one shared library next to
-this file. bank.cu (synthetic-bank quantisers) is compiled with -fmad=false so its f32 arithmetic
-rounds step by step like the CPU code it mirrors.
+Each source under csrc/ is compiled separately with nvcc (gguf.cpp, host code only, as CUDA too)
+and linked into one shared library next to this file. bank.cu (synthetic-bank quantisers) is
+compiled with -fmad=false so its f32 arithmetic rounds step by step like the CPU code it mirrors.
 """
 
 from __future__ import annotations
@@ -15,7 +15,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libcwx.so")
-SOURCES = ["api.cu", "bank.cu", "route.cu", "gemv.cu", "act.cu", "noalloc.cu", "mma.cu", "ep.cu"]
+SOURCES = ["api.cu", "bank.cu", "route.cu", "gemv.cu", "act.cu", "noalloc.cu", "mma.cu", "ep.cu", "gguf.cpp"]
 NO_FMA = {"bank.cu"}
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -43,12 +43,12 @@ def build(verbose: bool = False, force: bool = False) -> str:
     objs = []
     for src in SOURCES:
         path = os.path.join(CSRC, src)
-        obj = os.path.join(objdir, src.replace(".cu", ".o"))
+        obj = os.path.join(objdir, os.path.splitext(src)[0] + ".o")
         objs.append(obj)
         if not force and not _stale(obj, [path] + headers):
             continue
         cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", inc, "-I", CSRC,
-               "--expt-relaxed-constexpr", "-c", path, "-o", obj]
+               "--expt-relaxed-constexpr", "-x", "cu", "-c", path, "-o", obj]
         if src in NO_FMA:
             cmd.insert(1, "-fmad=false")
         if verbose:

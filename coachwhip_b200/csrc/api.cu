@@ -805,9 +805,12 @@ static int ep_check(const cwx_moe_layer* L, const cwx_ep_group* g, const char* w
 // Rows travel as f16 when the routed gate/up products read f16 activations anyway (IQ banks take
 // f16 activations on both product paths), which halves the dispatch exchange at no change in the
 // result; other formats get their f32 rows.
+// f16 rows only where nothing downstream re-quantises: with a down matrix that takes Q8
+// activations, the f16 rounding of x moves the hidden state across Q8 rounding boundaries.
 static bool ep_rows_f16(const cwx_moe_layer* L) {
     const int g = L->gate->L.fmt, u = L->up->L.fmt;
-    return (g == F_IQ2_S || g == F_IQ3_S) && (u == F_IQ2_S || u == F_IQ3_S);
+    return (g == F_IQ2_S || g == F_IQ3_S) && (u == F_IQ2_S || u == F_IQ3_S) &&
+           act_mode_of(L->down, L->act_mode) == AM_F32;
 }
 
 extern "C" int cwx_ep_rows_f16(const cwx_moe_layer* L) { return L && L->gate && L->up && ep_rows_f16(L) ? 1 : 0; }

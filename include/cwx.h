@@ -112,6 +112,37 @@ int cwx_bank_download(const cwx_bank* bank, int64_t e0, int64_t ne, void* host_d
 /* Dequantised f32 rows of one expert, (n, k), into device memory. */
 int cwx_bank_dequantize(const cwx_bank* bank, int64_t expert, float* out, void* stream);
 
+/* GGUF files (replace candle's gguf_file::Content::read and tensor lookup,
+ * vendor/candle-core/src/quantized/gguf_file.rs:469-563, as used by ExpertStore::new,
+ * crates/engine/src/experts.rs:697-717, and the model loaders' metadata and dense-tensor reads,
+ * crates/engine/src/model.rs:140-175, model_next.rs:1036-1053, model_gptoss.rs:115-175).
+ * Versions 1-3; the file stays mapped read-only until cwx_gguf_close. Names are GGUF tensor
+ * names ("blk.3.ffn_gate_exps.weight"); ne[] is innermost first (ne[0] = columns). */
+typedef struct cwx_gguf cwx_gguf;
+int cwx_gguf_open(const char* path, cwx_gguf** out);
+int cwx_gguf_close(cwx_gguf* file);
+/* version, tensor count, alignment and file offset of the tensor data (each optional). */
+int cwx_gguf_info(const cwx_gguf* file, int32_t* version, int64_t* n_tensors, int64_t* alignment,
+                  int64_t* data_offset);
+/* ggml type, dimensions, ne[4] (unused dims 1) and the tensor's file offset (each optional). */
+int cwx_gguf_tensor_info(const cwx_gguf* file, const char* name, int32_t* ggml_type, int32_t* n_dims, int64_t* ne,
+                         int64_t* offset);
+/* A 2-D (n, k) or 3-D (n_experts, n, k) tensor of an expert format as a bank descriptor whose
+ * host_ptr points into the mapping (valid while the file is open). */
+int cwx_gguf_tensor(const cwx_gguf* file, const char* name, cwx_matrix_desc* out);
+/* Bank of experts [first, first + n_experts) of that tensor (n_experts < 0: through the last);
+ * an expert-parallel rank loads its own slice. */
+int cwx_bank_from_gguf(int device, const cwx_gguf* file, const char* name, int64_t first, int64_t n_experts,
+                       cwx_bank** out);
+/* An F32 / F16 / BF16 tensor of n elements as f32, into host memory (router weights and
+ * biases, expert biases, the shared expert's gate). */
+int cwx_gguf_tensor_f32(const cwx_gguf* file, const char* name, float* out, int64_t n);
+/* Metadata values: any integer type (widened), F32/F64, strings (copied NUL-terminated into
+ * buf of cap bytes, truncated to fit; *len = full length). */
+int cwx_gguf_meta_int(const cwx_gguf* file, const char* key, int64_t* out);
+int cwx_gguf_meta_f64(const cwx_gguf* file, const char* key, double* out);
+int cwx_gguf_meta_str(const cwx_gguf* file, const char* key, char* buf, int64_t cap, int64_t* len);
+
 /* route(): logits (tokens, n_experts) f32 -> ids (tokens, top_k) u32 best first (ties: lowest
  * id), weights (tokens, top_k) f32 = softmax over all experts, renormalised over the picks when
  * norm != 0. n_experts <= 1024, top_k <= 16. All device pointers. */
@@ -199,8 +230,9 @@ int cwx_moe_forward(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_moe_args
  *   (exchange y_units back with the reverse unit splits: each rank gets its units in send order)
  *   3. cwx_ep_combine: out[t] = sum over destinations in rank order of its returned unit rows,
  *      + shared expert (on the local tokens) * sgate, + residual.
- * Rows are f16 when cwx_ep_rows_f16(layer) (the routed gate/up products read f16 activations
- * anyway: the result is unchanged), else f32. The layer's n_experts and router are global; its
+ * Rows are f16 when cwx_ep_rows_f16(layer): IQ gate/up banks (their tensor-core products read
+ * f16 activations) and a down matrix that takes f32 activations; else f32 (a down matrix that
+ * re-quantises its input to Q8 would turn the f16 rounding into flipped codes). The layer's n_experts and router are global; its
  * banks (and expert biases) hold this rank's epr experts. send_rows holds up to
  * tokens * min(top_k, world) rows, send_picks tokens * top_k records. */
 typedef struct {

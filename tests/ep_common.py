@@ -126,3 +126,37 @@ def gpu_engine(L: dict, world: int, rank: int, device: int, act_mode: int):
                      gate_bias=t(L.get("router_b")), shared=shared, act_mode=act_mode)
     eng._keep = (act, shared, g, u, dn)
     return eng
+
+
+def run_emulated(engines, x):
+    """All ranks' engines stepped on device 0, the exchanges done by slicing: x (T, H) split
+    evenly over the ranks; returns the concatenated outputs."""
+    import torch
+
+    world = len(engines)
+    T = x.shape[0]
+    per = T // world
+    xs = [torch.from_numpy(np.ascontiguousarray(x[r * per:(r + 1) * per])).cuda() for r in range(world)]
+    ds = [engines[r].dispatch(xs[r]) for r in range(world)]
+    counts = [d.send_counts.cpu().numpy() for d in ds]  # (world, 2): units, records per destination
+    uo = [np.concatenate([[0], np.cumsum(c[:, 0])]) for c in counts]
+    po = [np.concatenate([[0], np.cumsum(c[:, 1])]) for c in counts]
+    ys = []
+    for dst in range(world):  # units and records for rank dst, from every source in rank order
+        rows = torch.cat([ds[s].send_rows[uo[s][dst]:uo[s][dst + 1]] for s in range(world)])
+        picks = torch.cat([ds[s].send_picks[po[s][dst]:po[s][dst + 1]] for s in range(world)])
+        su = [int(counts[s][dst, 0]) for s in range(world)]
+        sp = [int(counts[s][dst, 1]) for s in range(world)]
+        ys.append((engines[dst].experts(rows, picks, su, sp), su))
+    outs = []
+    for s in range(world):  # unit rows back to each source, in the order it sent them
+        parts = []
+        for dst in range(world):
+            y, su = ys[dst]
+            o = int(np.sum(su[:s]))
+            parts.append(y[o:o + su[s]])
+        outs.append(engines[s].combine(ds[s], torch.cat(parts), None))
+    from coachwhip_b200 import _lib
+
+    _lib.status(0)
+    return np.concatenate([o.cpu().numpy() for o in outs])

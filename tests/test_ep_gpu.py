@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from tests.ep_common import gpu_engine
+from tests.ep_common import gpu_engine, run_emulated
 from tests.layers import Spec, build_cpu, make_input, rel_l2
 
 torch = pytest.importorskip("torch")
@@ -30,33 +30,7 @@ SPECS = {
 
 def _emulated(L, x, world, mode):
     """All ranks' steps on device 0, exchanging by slicing; returns the concatenated outputs."""
-    engines = [gpu_engine(L, world, r, 0, mode) for r in range(world)]
-    T = x.shape[0]
-    per = T // world
-    xs = [torch.from_numpy(np.ascontiguousarray(x[r * per:(r + 1) * per])).cuda() for r in range(world)]
-    ds = [engines[r].dispatch(xs[r]) for r in range(world)]
-    counts = [d.send_counts.cpu().numpy() for d in ds]  # (world, 2): units, records per destination
-    uo = [np.concatenate([[0], np.cumsum(c[:, 0])]) for c in counts]
-    po = [np.concatenate([[0], np.cumsum(c[:, 1])]) for c in counts]
-    ys = []
-    for dst in range(world):  # units and records for rank dst, from every source in rank order
-        rows = torch.cat([ds[s].send_rows[uo[s][dst]:uo[s][dst + 1]] for s in range(world)])
-        picks = torch.cat([ds[s].send_picks[po[s][dst]:po[s][dst + 1]] for s in range(world)])
-        su = [int(counts[s][dst, 0]) for s in range(world)]
-        sp = [int(counts[s][dst, 1]) for s in range(world)]
-        ys.append((engines[dst].experts(rows, picks, su, sp), su))
-    outs = []
-    for s in range(world):  # unit rows back to each source, in the order it sent them
-        parts = []
-        for dst in range(world):
-            y, su = ys[dst]
-            o = int(np.sum(su[:s]))
-            parts.append(y[o:o + su[s]])
-        outs.append(engines[s].combine(ds[s], torch.cat(parts), None))
-    from coachwhip_b200 import _lib
-
-    _lib.status(0)
-    return np.concatenate([o.cpu().numpy() for o in outs])
+    return run_emulated([gpu_engine(L, world, r, 0, mode) for r in range(world)], x)
 
 
 @pytest.mark.parametrize("name,T,world", [("iq_mix", 64, 2), ("iq_mix", 512, 4), ("mxfp4_gptoss", 64, 2),
