@@ -11,6 +11,7 @@ LIB_PATH = os.path.join(HERE, "libcwx.so")
 
 OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT, ENOMEM, EDEVICE = range(7)
 TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_IQ3_S, TYPE_IQ2_S, TYPE_MXFP4 = 0, 8, 12, 14, 21, 22, 39
+TYPE_IQ2_XXS, TYPE_IQ3_XXS, TYPE_IQ4_XS = 16, 18, 23
 ACT_MODE_CANDLE, ACT_MODE_F32 = 0, 1
 ACT_SILU, ACT_CLAMPED_SWIGLU = 0, 1
 

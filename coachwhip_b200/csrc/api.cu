@@ -334,6 +334,8 @@ extern "C" int cwx_ctx_destroy(cwx_ctx* c) {
     if (c->d_err) cudaFree(c->d_err);
     if (c->d_iq3s_map) cudaFree(c->d_iq3s_map);
     if (c->d_iq2s_map) cudaFree(c->d_iq2s_map);
+    if (c->d_iq3xxs_map) cudaFree(c->d_iq3xxs_map);
+    if (c->d_iq2xxs_map) cudaFree(c->d_iq2xxs_map);
     if (c->side) cudaStreamDestroy(c->side);
     if (c->ev_fork) cudaEventDestroy(c->ev_fork);
     if (c->ev_join) cudaEventDestroy(c->ev_join);
@@ -732,7 +734,7 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
     plan_layer(L, T, mma, nullptr, &p);
     if ((rc = ensure_ws(c, p.bytes, st))) return rc;
     plan_layer(L, T, mma, c->ws, &p);
-    const int H = p.H, E = p.E, K = p.K, I = p.I, Is = p.Is;
+    const int H = p.H, E = p.E, K = p.K;
     const int64_t n = (int64_t)T * K;
     const bool shared = L->sh_gate != nullptr;
 

@@ -341,8 +341,12 @@ __device__ void q6k_from_float_d(const float* x, uint8_t* y) {
 // One thread per (expert, row, K-piece): draw the piece's values and quantise them in place.
 // Experts e0 .. e0+ne-1 of the bank; `first` is the bank's first expert in the synthetic tensor
 // (the values follow the global expert index, so a slice equals those experts of the whole).
+struct SynthMaps {
+    const uint16_t *iq3s, *iq2s, *iq3xxs, *iq2xxs;
+};
+
 __global__ void k_synth(uint8_t* __restrict__ bank, Layout L, int64_t e0, int64_t ne, int64_t first, uint64_t key,
-                        float std_, const uint16_t* __restrict__ iq3map, const uint16_t* __restrict__ iq2map) {
+                        float std_, SynthMaps maps) {
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     int64_t total = ne * L.n * L.n_kp;
     if (i >= total) return;
@@ -361,8 +365,11 @@ __global__ void k_synth(uint8_t* __restrict__ bank, Layout L, int64_t e0, int64_
     switch (L.fmt) {
         case F_Q4_K: q4k_from_float_d(x, dst); break;
         case F_Q6_K: q6k_from_float_d(x, dst); break;
-        case F_IQ3_S: cwx_encode_iq3s(x, dst, iq3map); break;
-        case F_IQ2_S: cwx_encode_iq2s(x, dst, iq2map); break;
+        case F_IQ3_S: cwx_encode_iq3s(x, dst, maps.iq3s); break;
+        case F_IQ2_S: cwx_encode_iq2s(x, dst, maps.iq2s); break;
+        case F_IQ3_XXS: cwx_encode_iq3xxs(x, dst, maps.iq3xxs); break;
+        case F_IQ2_XXS: cwx_encode_iq2xxs(x, dst, maps.iq2xxs); break;
+        case F_IQ4_XS: cwx_encode_iq4xs(x, dst); break;
         case F_Q8_0:
             for (int b = 0; b < klen / 32; ++b) q8_0_from_float_d(x + 32 * b, dst + 34 * b);
             break;
@@ -379,15 +386,23 @@ __global__ void k_normal(float* __restrict__ out, int64_t n, uint64_t key, uint6
     if (i < n) out[i] = cwx_normal_std(key, offset + (uint64_t)i, std_);
 }
 
+static int upload_map(uint16_t** dst, void (*build)(uint16_t*), int size) {
+    std::vector<uint16_t> m(size);
+    build(m.data());
+    CWX_CUDA(cudaMalloc(dst, m.size() * 2));
+    CWX_CUDA(cudaMemcpy(*dst, m.data(), m.size() * 2, cudaMemcpyHostToDevice));
+    return CWX_OK;
+}
+
+// The encoder maps of the IQ codebook formats, on the context's device (built on first use).
 static int ensure_maps(cwx_ctx* ctx) {
-    if (ctx->d_iq3s_map) return CWX_OK;
-    std::vector<uint16_t> m3(CWX_IQ3S_MAP_SIZE), m2(CWX_IQ2S_MAP_SIZE);
-    cwx_build_iq3s_map(m3.data());
-    cwx_build_iq2s_map(m2.data());
-    CWX_CUDA(cudaMalloc(&ctx->d_iq3s_map, m3.size() * 2));
-    CWX_CUDA(cudaMalloc(&ctx->d_iq2s_map, m2.size() * 2));
-    CWX_CUDA(cudaMemcpy(ctx->d_iq3s_map, m3.data(), m3.size() * 2, cudaMemcpyHostToDevice));
-    CWX_CUDA(cudaMemcpy(ctx->d_iq2s_map, m2.data(), m2.size() * 2, cudaMemcpyHostToDevice));
+    int rc;
+    if (!ctx->d_iq3s_map && (rc = upload_map(&ctx->d_iq3s_map, cwx_build_iq3s_map, CWX_IQ3S_MAP_SIZE))) return rc;
+    if (!ctx->d_iq2s_map && (rc = upload_map(&ctx->d_iq2s_map, cwx_build_iq2s_map, CWX_IQ2S_MAP_SIZE))) return rc;
+    if (!ctx->d_iq3xxs_map && (rc = upload_map(&ctx->d_iq3xxs_map, cwx_build_iq3xxs_map, CWX_IQ3XXS_MAP_SIZE)))
+        return rc;
+    if (!ctx->d_iq2xxs_map && (rc = upload_map(&ctx->d_iq2xxs_map, cwx_build_iq2xxs_map, CWX_IQ2XXS_MAP_SIZE)))
+        return rc;
     return CWX_OK;
 }
 
@@ -396,7 +411,8 @@ static int ensure_maps(cwx_ctx* ctx) {
 using namespace cwx;
 
 static int supported_type(int t) {
-    return t == F_Q8_0 || t == F_Q4_K || t == F_Q6_K || t == F_IQ3_S || t == F_IQ2_S || t == F_MXFP4;
+    return t == F_Q8_0 || t == F_Q4_K || t == F_Q6_K || t == F_IQ3_S || t == F_IQ2_S || t == F_MXFP4 ||
+           t == F_IQ2_XXS || t == F_IQ3_XXS || t == F_IQ4_XS;
 }
 
 static int alloc_bank(int device, int type, int64_t n, int64_t k, int64_t ne, cwx_bank** out) {
@@ -489,7 +505,8 @@ extern "C" int cwx_bank_synth_experts(cwx_ctx* ctx, int32_t type, int64_t n, int
             int64_t cnt = ne - e0 < experts_per_launch ? ne - e0 : experts_per_launch;
             int64_t items = cnt * n * b->L.n_kp;
             k_synth<<<(unsigned)((items + threads - 1) / threads), threads>>>(
-                b->d + e0 * b->L.expert_bytes, b->L, e0, cnt, first, key, std_, ctx->d_iq3s_map, ctx->d_iq2s_map);
+                b->d + e0 * b->L.expert_bytes, b->L, e0, cnt, first, key, std_,
+                SynthMaps{ctx->d_iq3s_map, ctx->d_iq2s_map, ctx->d_iq3xxs_map, ctx->d_iq2xxs_map});
             e = cudaGetLastError();
         }
     }

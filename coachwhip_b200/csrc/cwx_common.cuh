@@ -17,12 +17,16 @@ enum Fmt : int {
     F_IQ3_S = CWX_TYPE_IQ3_S,
     F_IQ2_S = CWX_TYPE_IQ2_S,
     F_MXFP4 = CWX_TYPE_MXFP4,
+    F_IQ2_XXS = CWX_TYPE_IQ2_XXS,
+    F_IQ3_XXS = CWX_TYPE_IQ3_XXS,
+    F_IQ4_XS = CWX_TYPE_IQ4_XS,
 };
 
 __host__ __device__ inline int fmt_block_elems(int t) {
     switch (t) {
         case F_Q8_0: case F_MXFP4: return 32;
-        case F_Q4_K: case F_Q6_K: case F_IQ2_S: case F_IQ3_S: return 256;
+        case F_Q4_K: case F_Q6_K: case F_IQ2_S: case F_IQ3_S: case F_IQ2_XXS: case F_IQ3_XXS: case F_IQ4_XS:
+            return 256;
         default: return 0;
     }
 }
@@ -34,6 +38,9 @@ __host__ __device__ inline int fmt_block_bytes(int t) {
         case F_Q6_K: return 210;
         case F_IQ2_S: return 82;
         case F_IQ3_S: return 110;
+        case F_IQ2_XXS: return 66;
+        case F_IQ3_XXS: return 98;
+        case F_IQ4_XS: return 136;
         default: return 0;
     }
 }
@@ -177,6 +184,8 @@ struct cwx_ctx {
     int* h_err;   // pinned mirror
     uint16_t* d_iq3s_map;  // encoder maps for synthetic banks (built on first use)
     uint16_t* d_iq2s_map;
+    uint16_t* d_iq3xxs_map;
+    uint16_t* d_iq2xxs_map;
     int profiling;     // record per-phase events (cwx_ctx_set_profiling)
     void* prof;        // recorded (phase, start, end) events
     int64_t launches;  // kernel launches issued through this context

@@ -8,6 +8,7 @@
 //   MXFP4 k_quants.rs:673-691 (+ e8m0_to_f32_half 642-649)
 //   IQ3_S vendor/candle-metal-kernels/src/metal_src/quantized.metal:6892-6915
 //   IQ2_S quantized.metal:6917-6934
+//   IQ2_XXS quantized.metal:6819-6842   IQ3_XXS :6862-6890   IQ4_XS :6999-7018
 // The fast IQ paths produce f16 pairs for the tensor cores: the codebook values are exact in f16,
 // the per-16/32-column scale is rounded to f16 (about 2^-11 relative per weight).
 //
@@ -33,6 +34,9 @@ __device__ __forceinline__ float half_at(const void* p, int j) {
 }
 __device__ __forceinline__ float h2f_bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 __device__ __forceinline__ uint16_t ld_u16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+__device__ __forceinline__ uint32_t ld_u32(const uint8_t* p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
 
 __device__ __forceinline__ void get_scale_min_k4(int j, const uint8_t* q, int* d, int* m) {
     if (j < 4) {
@@ -64,6 +68,8 @@ __device__ __forceinline__ IqRow iq_row_in(const uint8_t* piece, int rr, int64_t
 // codebooks in global memory when no tables are staged.
 static __device__ const uint16_t d_iq2s_codes[1024] = CWX_IQ2S_CODES;
 static __device__ const uint16_t d_iq3s_codes[512] = CWX_IQ3S_CODES;
+static __device__ const uint16_t d_iq2xxs_codes[256] = CWX_IQ2XXS_CODES;
+static __device__ const uint16_t d_iq3xxs_codes[256] = CWX_IQ3XXS_CODES;
 template <bool SMEM>
 __device__ __forceinline__ float iq_grid(int fmt, const HTables& t, int idx, int j) {
     if (SMEM) return fmt == F_IQ2_S ? half_at(&t.g2[idx], j) : half_at(&t.g3[idx], j);
@@ -161,6 +167,57 @@ __device__ __forceinline__ void dec16_row_exact(int fmt, const uint8_t* b, int k
             const int sh = (kofs & 16) ? 4 : 0;
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] = __fmul_rn((float)kv[(blk[1 + i] >> sh) & 0xF], d);
+            break;
+        }
+        case F_IQ2_XXS: {  // 8 bytes per 32 columns: 4 grid entries, then signs and scale
+            const float d = h2f_bits(ld_u16(b));
+            const uint8_t* q = b + 2 + 8 * (kofs >> 5);
+            const uint32_t aux = ld_u32(q + 4);
+            const float dl = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.25f);
+#pragma unroll
+            for (int gi = 0; gi < 2; ++gi) {
+                const int g = ((kofs & 16) >> 3) + gi;
+                const uint64_t grid = cwx_iq2s_expand(d_iq2xxs_codes[q[g]]);
+                const uint32_t sg = cwx_ksigns((aux >> (7 * g)) & 127u);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float x = __fmul_rn(dl, (float)((grid >> (8 * j)) & 0xFF));
+                    v[8 * gi + j] = ((sg >> j) & 1) ? -x : x;
+                }
+            }
+            break;
+        }
+        case F_IQ3_XXS: {  // grid entries at 2 + 8 per 32 columns; signs and scale at 66 + 4 per 32
+            const float d = h2f_bits(ld_u16(b));
+            const int ib = kofs >> 5;
+            const uint8_t* q = b + 2 + 8 * ib;
+            const uint32_t aux = ld_u32(b + 66 + 4 * ib);
+            const float dl = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.5f);
+#pragma unroll
+            for (int gi = 0; gi < 2; ++gi) {
+                const int g = ((kofs & 16) >> 3) + gi;
+                const uint32_t sg = cwx_ksigns((aux >> (7 * g)) & 127u);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t grid = cwx_iq3xxs_expand(d_iq3xxs_codes[q[2 * g + h]]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float x = __fmul_rn(dl, (float)((grid >> (8 * j)) & 0xFF));
+                        v[8 * gi + 4 * h + j] = ((sg >> (4 * h + j)) & 1) ? -x : x;
+                    }
+                }
+            }
+            break;
+        }
+        case F_IQ4_XS: {
+            const float d = h2f_bits(ld_u16(b));
+            const int ib = kofs >> 5;
+            const int ls = ((b[4 + (ib >> 1)] >> (4 * (ib & 1))) & 0xF) | (((ld_u16(b + 2) >> (2 * ib)) & 3) << 4);
+            const float dl = __fmul_rn(d, (float)(ls - 32));
+            const uint8_t* q = b + 8 + 16 * ib;
+            const int sh = (kofs & 16) ? 4 : 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(dl, (float)cwx_iq4nl((q[i] >> sh) & 0xF));
             break;
         }
         default:

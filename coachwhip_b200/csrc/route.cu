@@ -11,8 +11,9 @@
 //
 // Arithmetic chosen so the results are those of the candle CPU path bit for bit where that is
 // defined: softmax sums in candle's x86 AVX order (vendor/candle-core/src/cpu/avx.rs:243-257,
-// lanes reduced as in vec_reduce 51-66), exp correctly rounded to f32 (what glibc's expf, which
-// Rust's f32::exp calls, returns), the pick order of a stable descending sort. Router logits
+// lanes reduced as in vec_reduce 51-66), exp correctly rounded to f32 (f64 exp rounded once;
+// glibc's expf, which Rust's f32::exp calls, misrounds a few inputs next to a rounding midpoint),
+// the pick order of a stable descending sort. Router logits
 // accumulate exact f32 products in f64 and round once (a decode form for small batches and a
 // tiled form with operand reuse for prefill-sized batches).
 #include "cwx_common.cuh"

@@ -26,6 +26,7 @@ from ._lib import CwxError, check
 BLOCK = {  # ggml type -> (elements, bytes) per quant block
     _lib.TYPE_Q8_0: (32, 34), _lib.TYPE_Q4_K: (256, 144), _lib.TYPE_Q6_K: (256, 210),
     _lib.TYPE_IQ3_S: (256, 110), _lib.TYPE_IQ2_S: (256, 82), _lib.TYPE_MXFP4: (32, 17),
+    _lib.TYPE_IQ2_XXS: (256, 66), _lib.TYPE_IQ3_XXS: (256, 98), _lib.TYPE_IQ4_XS: (256, 136),
 }
 
 

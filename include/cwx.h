@@ -44,8 +44,11 @@ extern "C" {
 #define CWX_TYPE_Q8_0 8
 #define CWX_TYPE_Q4_K 12
 #define CWX_TYPE_Q6_K 14
+#define CWX_TYPE_IQ2_XXS 16
+#define CWX_TYPE_IQ3_XXS 18
 #define CWX_TYPE_IQ3_S 21
 #define CWX_TYPE_IQ2_S 22
+#define CWX_TYPE_IQ4_XS 23
 #define CWX_TYPE_MXFP4 39
 
 /* Activation policy of the expert products.

@@ -17,6 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 
 F32, Q8_0, Q4_K, Q6_K, Q8_K, IQ3_S, IQ2_S, MXFP4 = 0, 8, 12, 14, 15, 21, 22, 39
+IQ2_XXS, IQ3_XXS, IQ4_XS = 16, 18, 23
 MODE_CANDLE, MODE_F32 = 0, 1
 ACT_SILU, ACT_CLAMPED_SWIGLU = 0, 1
 

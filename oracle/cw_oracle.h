@@ -32,8 +32,11 @@ enum {
     CWO_Q4_K = 12,
     CWO_Q6_K = 14,
     CWO_Q8_K = 15,
+    CWO_IQ2_XXS = 16,
+    CWO_IQ3_XXS = 18,
     CWO_IQ3_S = 21,
     CWO_IQ2_S = 22,
+    CWO_IQ4_XS = 23,
     CWO_MXFP4 = 39,
 };
 

@@ -11,7 +11,8 @@
 //         make_qkx1_quants 227-284
 // and the Metal shader dequantisers for the IQ formats, which have no CPU code in the
 // reference:
-//   IQ3_S dequantize_iq3_s quantized.metal:6892-6915, IQ2_S dequantize_iq2_s :6917-6934.
+//   IQ3_S dequantize_iq3_s quantized.metal:6892-6915, IQ2_S dequantize_iq2_s :6917-6934,
+//   IQ2_XXS :6819-6842, IQ3_XXS :6862-6890, IQ4_XS :6999-7018.
 // Compiled with -ffp-contract=off so every f32 operation rounds where the Rust code does.
 #include <math.h>
 #include <stdlib.h>
@@ -531,6 +532,62 @@ void iq2s_to_float(const uint8_t* b, float* y) {
     }
 }
 
+// ---------------------------------------------------------------- IQ2_XXS / IQ3_XXS / IQ4_XS
+// Metal semantics: dequantize_iq2_xxs quantized.metal:6819-6842, dequantize_iq3_xxs :6862-6890,
+// dequantize_iq4_xs :6999-7018 (the reference's CPU path has no dequantisation for them,
+// k_quants.rs:2955-2993).
+
+static inline uint32_t le32(const uint8_t* p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+void iq2xxs_to_float(const uint8_t* b, float* y) {
+    float d = f16_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+    for (int ib = 0; ib < 8; ++ib) {
+        const uint8_t* q = b + 2 + 8 * ib;
+        const uint32_t aux = le32(q + 4);
+        float dl = d * (0.5f + (float)(aux >> 28)) * 0.25f;
+        for (int g = 0; g < 4; ++g) {
+            uint64_t grid = cwx_iq2s_expand(cwx_iq2xxs_codes[q[g]]);
+            uint32_t signs = cwx_ksigns((aux >> (7 * g)) & 127u);
+            for (int j = 0; j < 8; ++j)
+                y[32 * ib + 8 * g + j] = dl * (float)((grid >> (8 * j)) & 0xFF) * ((signs >> j) & 1 ? -1.f : 1.f);
+        }
+    }
+}
+
+void iq3xxs_to_float(const uint8_t* b, float* y) {
+    float d = f16_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+    for (int ib = 0; ib < 8; ++ib) {
+        const uint8_t* q = b + 2 + 8 * ib;
+        const uint32_t aux = le32(b + 66 + 4 * ib);
+        float dl = d * (0.5f + (float)(aux >> 28)) * 0.5f;
+        for (int g = 0; g < 4; ++g) {
+            uint32_t signs = cwx_ksigns((aux >> (7 * g)) & 127u);
+            for (int h = 0; h < 2; ++h) {
+                uint32_t grid = cwx_iq3xxs_expand(cwx_iq3xxs_codes[q[2 * g + h]]);
+                for (int j = 0; j < 4; ++j)
+                    y[32 * ib + 8 * g + 4 * h + j] =
+                        dl * (float)((grid >> (8 * j)) & 0xFF) * ((signs >> (4 * h + j)) & 1 ? -1.f : 1.f);
+            }
+        }
+    }
+}
+
+void iq4xs_to_float(const uint8_t* b, float* y) {
+    float d = f16_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+    const uint32_t sh = (uint32_t)(b[2] | (b[3] << 8));
+    for (int ib = 0; ib < 8; ++ib) {
+        const int ls = ((b[4 + ib / 2] >> (4 * (ib % 2))) & 0xF) | (((sh >> (2 * ib)) & 3) << 4);
+        const float dl = d * (float)(ls - 32);
+        const uint8_t* q = b + 8 + 16 * ib;
+        for (int m = 0; m < 16; ++m) {
+            y[32 * ib + m] = dl * (float)cwx_iq4nl(q[m] & 0xF);
+            y[32 * ib + 16 + m] = dl * (float)cwx_iq4nl(q[m] >> 4);
+        }
+    }
+}
+
 // Built once, on first use; function-local statics initialise thread-safely.
 const uint16_t* iq3s_map() {
     static const std::vector<uint16_t> m = [] {
@@ -548,6 +605,22 @@ const uint16_t* iq2s_map() {
     }();
     return m.data();
 }
+const uint16_t* iq3xxs_map() {
+    static const std::vector<uint16_t> m = [] {
+        std::vector<uint16_t> v(CWX_IQ3XXS_MAP_SIZE);
+        cwx_build_iq3xxs_map(v.data());
+        return v;
+    }();
+    return m.data();
+}
+const uint16_t* iq2xxs_map() {
+    static const std::vector<uint16_t> m = [] {
+        std::vector<uint16_t> v(CWX_IQ2XXS_MAP_SIZE);
+        cwx_build_iq2xxs_map(v.data());
+        return v;
+    }();
+    return m.data();
+}
 
 }  // namespace cwo
 
@@ -559,7 +632,8 @@ int cwo_block_elems(int type) {
     switch (type) {
         case CWO_F32: return 1;
         case CWO_Q8_0: case CWO_MXFP4: return 32;
-        case CWO_Q4_K: case CWO_Q6_K: case CWO_Q8_K: case CWO_IQ2_S: case CWO_IQ3_S: return 256;
+        case CWO_Q4_K: case CWO_Q6_K: case CWO_Q8_K: case CWO_IQ2_S: case CWO_IQ3_S: case CWO_IQ2_XXS:
+        case CWO_IQ3_XXS: case CWO_IQ4_XS: return 256;
         default: return 0;
     }
 }
@@ -574,6 +648,9 @@ int cwo_block_bytes(int type) {
         case CWO_Q8_K: return 292;
         case CWO_IQ2_S: return 82;
         case CWO_IQ3_S: return 110;
+        case CWO_IQ2_XXS: return 66;
+        case CWO_IQ3_XXS: return 98;
+        case CWO_IQ4_XS: return 136;
         default: return 0;
     }
 }
@@ -600,6 +677,8 @@ int cwo_quantize(int type, const float* x, int64_t n, void* out) {
     int bb = cwo_block_bytes(type);
     if (type == CWO_IQ3_S) iq3s_map();
     if (type == CWO_IQ2_S) iq2s_map();
+    if (type == CWO_IQ3_XXS) iq3xxs_map();
+    if (type == CWO_IQ2_XXS) iq2xxs_map();
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < nb; ++i) {
         const float* xi = x + i * be;
@@ -612,6 +691,9 @@ int cwo_quantize(int type, const float* x, int64_t n, void* out) {
             case CWO_MXFP4: mxfp4_from_float(xi, (BMXFP4*)yi); break;
             case CWO_IQ3_S: cwx_encode_iq3s(xi, (uint8_t*)yi, iq3s_map()); break;
             case CWO_IQ2_S: cwx_encode_iq2s(xi, (uint8_t*)yi, iq2s_map()); break;
+            case CWO_IQ2_XXS: cwx_encode_iq2xxs(xi, (uint8_t*)yi, iq2xxs_map()); break;
+            case CWO_IQ3_XXS: cwx_encode_iq3xxs(xi, (uint8_t*)yi, iq3xxs_map()); break;
+            case CWO_IQ4_XS: cwx_encode_iq4xs(xi, (uint8_t*)yi); break;
             case CWO_F32: memcpy(yi, xi, 4); break;
         }
     }
@@ -640,6 +722,9 @@ int cwo_dequantize(int type, const void* blocks, int64_t n, float* y) {
             case CWO_MXFP4: mxfp4_to_float((const BMXFP4*)bi, yi); break;
             case CWO_IQ3_S: iq3s_to_float((const uint8_t*)bi, yi); break;
             case CWO_IQ2_S: iq2s_to_float((const uint8_t*)bi, yi); break;
+            case CWO_IQ2_XXS: iq2xxs_to_float((const uint8_t*)bi, yi); break;
+            case CWO_IQ3_XXS: iq3xxs_to_float((const uint8_t*)bi, yi); break;
+            case CWO_IQ4_XS: iq4xs_to_float((const uint8_t*)bi, yi); break;
             case CWO_F32: memcpy(yi, bi, 4); break;
         }
     }

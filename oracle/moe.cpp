@@ -14,7 +14,11 @@
 //   shared expert    SharedExpert::forward model_next.rs:731-741
 // Router logits use exact f32 products accumulated in f64 and rounded once: candle's gemm
 // crate summation order is not restatable, and any correct f32 GEMV lies within its rounding.
-// exp is glibc expf, the function Rust's f32::exp calls on x86-64 Linux.
+// The softmax and the shared-expert gate take exp correctly rounded to f32, computed as exp in f64
+// rounded once: glibc's expf (what Rust's f32::exp calls on x86-64 Linux) is within 0.502 ulp but
+// misrounds some inputs next to a rounding midpoint, and the reference's own platform (Apple's
+// libm, Metal) is a third implementation, so the checker takes the one exact definition. The
+// activations (SiLU, clamped SwiGLU) use expf; their outputs are compared within a tolerance.
 #include <math.h>
 #include <omp.h>
 #include <stdlib.h>
@@ -45,16 +49,18 @@ float avx_sum(const float* x, int n) {
     return r;
 }
 
+static float exp_cr(float x) { return (float)exp((double)x); }
+
 static void softmax_row(const float* x, int n, float* p) {
     float mx = x[0];
     for (int i = 1; i < n; ++i) mx = fmaxf(mx, x[i]);
-    for (int i = 0; i < n; ++i) p[i] = expf(x[i] - mx);
+    for (int i = 0; i < n; ++i) p[i] = exp_cr(x[i] - mx);
     float s = avx_sum(p, n);
     for (int i = 0; i < n; ++i) p[i] = p[i] / s;
 }
 
 static float silu(float v) { return v / (1.0f + expf(-v)); }
-static float sigmoid(float v) { return 1.0f / (expf(-v) + 1.0f); }
+static float sigmoid(float v) { return 1.0f / (exp_cr(-v) + 1.0f); }
 
 }  // namespace cwo
 
@@ -79,6 +85,8 @@ int cwo_synth_matrix(int type, uint64_t key, int64_t e0, int64_t ne, int64_t n, 
     if (rb < 0) return -1;
     if (type == CWO_IQ3_S) iq3s_map();
     if (type == CWO_IQ2_S) iq2s_map();
+    if (type == CWO_IQ3_XXS) iq3xxs_map();
+    if (type == CWO_IQ2_XXS) iq2xxs_map();
     uint8_t* o = (uint8_t*)out;
 #pragma omp parallel
     {

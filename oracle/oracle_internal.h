@@ -41,6 +41,8 @@ void q8k_from_float(const float* x, BQ8K* y);
 void q8_0_from_float(const float* x, BQ8_0* y);
 const uint16_t* iq3s_map();
 const uint16_t* iq2s_map();
+const uint16_t* iq3xxs_map();
+const uint16_t* iq2xxs_map();
 
 // candle's x86 AVX f32 sum (vendor/candle-core/src/cpu/avx.rs:243-257 with vec_reduce 51-66):
 // 4 x 8 lanes over whole 32-element steps, the fixed pairwise lane reduction, then the tail

@@ -15,7 +15,7 @@ def _gtype(fmt: int):
     from gguf.constants import GGMLQuantizationType as G
 
     return {O.Q4_K: G.Q4_K, O.Q6_K: G.Q6_K, O.Q8_0: G.Q8_0, O.MXFP4: G.MXFP4, O.IQ2_S: G.IQ2_S,
-            O.IQ3_S: G.IQ3_S}[fmt]
+            O.IQ3_S: G.IQ3_S, O.IQ2_XXS: G.IQ2_XXS, O.IQ3_XXS: G.IQ3_XXS, O.IQ4_XS: G.IQ4_XS}[fmt]
 
 
 def _quant(w, name: str, data: np.ndarray, fmt: int, e: int | None, n: int, k: int) -> None:

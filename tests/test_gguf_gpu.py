@@ -25,6 +25,11 @@ CASES = {
                                   up_type=O.IQ2_S, down_type=O.IQ3_S, seed=21)),
     "qwen3next": ("qwen3next", Spec(hidden=512, n_experts=32, top_k=8, inter=256, gate_type=O.IQ3_S,
                                     up_type=O.IQ3_S, down_type=O.Q4_K, shared_inter=256, seed=22)),
+    # the reference's own file family (Qwen3.6 UD-IQ2_M): qwen35moe, IQ2_XXS gate/up, IQ3_XXS
+    # down, IQ4_XS shared expert
+    "qwen35moe": ("qwen35moe", Spec(hidden=512, n_experts=32, top_k=8, inter=256, gate_type=O.IQ2_XXS,
+                                    up_type=O.IQ2_XXS, down_type=O.IQ3_XXS, shared_inter=256,
+                                    sh_types=(O.IQ4_XS, O.IQ4_XS, O.IQ4_XS), seed=24)),
     "gpt-oss": ("gpt-oss", Spec(hidden=576, n_experts=16, top_k=4, inter=576, gate_type=O.MXFP4, up_type=O.MXFP4,
                                 down_type=O.MXFP4, act=O.ACT_CLAMPED_SWIGLU, router_bias=True, expert_bias=True,
                                 seed=23)),

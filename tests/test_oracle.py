@@ -6,14 +6,14 @@ import pytest
 
 import oracle as O
 
-FORMATS = [O.Q4_K, O.Q6_K, O.Q8_0, O.MXFP4, O.IQ2_S, O.IQ3_S]
+FORMATS = [O.Q4_K, O.Q6_K, O.Q8_0, O.MXFP4, O.IQ2_S, O.IQ3_S, O.IQ2_XXS, O.IQ3_XXS, O.IQ4_XS]
 
 
 def _gguf_type(fmt):
     from gguf.constants import GGMLQuantizationType as G
 
     return {O.Q4_K: G.Q4_K, O.Q6_K: G.Q6_K, O.Q8_0: G.Q8_0, O.MXFP4: G.MXFP4, O.IQ2_S: G.IQ2_S,
-            O.IQ3_S: G.IQ3_S}[fmt]
+            O.IQ3_S: G.IQ3_S, O.IQ2_XXS: G.IQ2_XXS, O.IQ3_XXS: G.IQ3_XXS, O.IQ4_XS: G.IQ4_XS}[fmt]
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
@@ -42,7 +42,8 @@ def test_quantisers_round_trip(fmt):
     x = O.normal(O.stream(1, fmt, 5), 0, 256 * 64, 0.02)
     y = O.dequantize(fmt, O.quantize(fmt, x), x.size)
     err = np.linalg.norm(y - x) / np.linalg.norm(x)
-    bound = {O.Q4_K: 0.12, O.Q6_K: 0.03, O.Q8_0: 0.01, O.MXFP4: 0.15, O.IQ2_S: 0.45, O.IQ3_S: 0.4}[fmt]
+    bound = {O.Q4_K: 0.12, O.Q6_K: 0.03, O.Q8_0: 0.01, O.MXFP4: 0.15, O.IQ2_S: 0.45, O.IQ3_S: 0.4, O.IQ2_XXS: 0.5,
+             O.IQ3_XXS: 0.3, O.IQ4_XS: 0.12}[fmt]
     assert err < bound, err
 
 
