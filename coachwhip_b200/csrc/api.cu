@@ -144,19 +144,25 @@ struct LayerPlan {
     size_t bytes;
 };
 
+// IQ formats: f32 activations under every policy (the reference runs them on Metal only), decoded
+// by both product kernels.
+static bool iq_format(int f) {
+    return f == F_IQ2_S || f == F_IQ3_S || f == F_IQ2_XXS || f == F_IQ3_XXS || f == F_IQ4_XS;
+}
+
 // The shared expert joins the tensor-core products when its activations are f32 (no Q8 codes,
 // whose per-piece scale a TMEM accumulator cannot apply) and its banks are a supported format.
 static bool shared_mma_ok(const cwx_moe_layer* L) {
     if (!L->sh_gate) return false;
     const Layout &g = L->sh_gate->L, &u = L->sh_up->L, &d = L->sh_down->L;
-    auto fmt_ok = [](int f) { return f == F_IQ2_S || f == F_IQ3_S || f == F_Q4_K; };
+    auto fmt_ok = [](int f) { return iq_format(f) || f == F_Q4_K; };
     if (!fmt_ok(g.fmt) || !fmt_ok(d.fmt) || g.fmt != u.fmt) return false;
     if (act_mode_of(L->sh_gate, L->act_mode) != AM_F32 || act_mode_of(L->sh_down, L->act_mode) != AM_F32)
         return false;
     return g.n % 256 == 0 && L->hidden % 256 == 0;
 }
 
-// Whether a layer's routed products run on the tensor cores: IQ2_S / IQ3_S banks (f32 activations
+// Whether a layer's routed products run on the tensor cores: IQ banks (f32 activations
 // under every policy), SiLU, whole 256-column pieces, and piles large enough on average.
 static bool mma_layer(const cwx_ctx* c, const cwx_moe_layer* L, int T) {
     if (!c || c->mma_min_pile <= 0 || L->act != CWX_ACT_SILU) return false;
@@ -166,7 +172,7 @@ static bool mma_layer(const cwx_ctx* c, const cwx_moe_layer* L, int T) {
     for (const cwx_bank* b : bs) {
         const int f = b->L.fmt;
         // Q4_K only with f32 activations (its Q8_K codes carry a per-piece, per-token scale)
-        if (f != F_IQ2_S && f != F_IQ3_S && !(f == F_Q4_K && act_mode_of(b, L->act_mode) == AM_F32)) return false;
+        if (!iq_format(f) && !(f == F_Q4_K && act_mode_of(b, L->act_mode) == AM_F32)) return false;
     }
     if (L->gate->L.fmt != L->up->L.fmt) return false;
     return L->hidden % 256 == 0 && L->inter % 256 == 0;
@@ -811,8 +817,7 @@ static int ep_check(const cwx_moe_layer* L, const cwx_ep_group* g, const char* w
 // activations, the f16 rounding of x moves the hidden state across Q8 rounding boundaries.
 static bool ep_rows_f16(const cwx_moe_layer* L) {
     const int g = L->gate->L.fmt, u = L->up->L.fmt;
-    return (g == F_IQ2_S || g == F_IQ3_S) && (u == F_IQ2_S || u == F_IQ3_S) &&
-           act_mode_of(L->down, L->act_mode) == AM_F32;
+    return iq_format(g) && iq_format(u) && act_mode_of(L->down, L->act_mode) == AM_F32;
 }
 
 extern "C" int cwx_ep_rows_f16(const cwx_moe_layer* L) { return L && L->gate && L->up && ep_rows_f16(L) ? 1 : 0; }

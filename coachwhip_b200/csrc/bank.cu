@@ -422,6 +422,9 @@ static int alloc_bank(int device, int type, int64_t n, int64_t k, int64_t ne, cw
     Layout L;
     if (!make_layout(type, n, k, ne, &L)) return fail(CWX_EINVAL, "cwx_bank: bad shape n=%lld k=%lld experts=%lld for type %d",
                                                       (long long)n, (long long)k, (long long)ne, type);
+    // the IQ formats are stored in groups of 16 rows (a partial group would not fit its piece)
+    if (fmt_soa(type) && n % 16)
+        return fail(CWX_EUNSUPPORTED, "cwx_bank: type %d needs a multiple of 16 rows, got n=%lld", type, (long long)n);
     CWX_CUDA(cudaSetDevice(device));
     cwx_bank* b = new cwx_bank();
     b->device = device;

@@ -137,12 +137,39 @@ inline bool make_layout(int fmt, int64_t n, int64_t k, int64_t e, Layout* L) {
 //     d at 1280 + row*2.
 //   IQ3_S group (16 x 110 = 1760 B): qs at row*64, signs at 1024 + row*32, qh at 1536 + row*8,
 //     scales at 1664 + row*4, d at 1728 + row*2.
+//   IQ2_XXS group (16 x 66 = 1056 B): per (row, c4) a 16-byte record = GGUF bytes 2 + 16 c4 ..
+//     (grid entries and signs/scale words of the two 32-column blocks) at (row*4 + c4)*16; d at
+//     1024 + row*2.
+//   IQ3_XXS group (16 x 98 = 1568 B): per (row, c4) the 16 grid-entry bytes (GGUF 2 + 16 c4 ..) at
+//     (row*4 + c4)*16 and the two signs/scale words (GGUF 66 + 8 c4 ..) at 1024 + (row*4 + c4)*8;
+//     d at 1536 + row*2.
+//   IQ4_XS group (16 x 136 = 2176 B): per (row, c4) the 32 nibble bytes (GGUF 8 + 32 c4 ..) at
+//     (row*4 + c4)*32; per row [d | scales_h | scales_l] (GGUF 0 .. 7) at 2048 + row*8.
 // GGUF blocks: IQ2_S = d(2) qs(32) signs(32) qh(8) scales(8); IQ3_S = d(2) qs(64) qh(8) signs(32)
-// scales(4).
-__host__ __device__ inline bool fmt_soa(int fmt) { return fmt == F_IQ2_S || fmt == F_IQ3_S; }
+// scales(4); IQ2_XXS = d(2) 8 x [entries(4) signs/scale(4)]; IQ3_XXS = d(2) entries(64)
+// signs/scale(32); IQ4_XS = d(2) scales_h(2) scales_l(4) qs(128).
+__host__ __device__ inline bool fmt_soa(int fmt) {
+    return fmt == F_IQ2_S || fmt == F_IQ3_S || fmt == F_IQ2_XXS || fmt == F_IQ3_XXS || fmt == F_IQ4_XS;
+}
 
 // Offset inside a 16-row group of byte b of the GGUF block of row rg (0..15).
 __host__ __device__ inline int soa_offset(int fmt, int rg, int b) {
+    if (fmt == F_IQ2_XXS) {
+        if (b < 2) return 1024 + rg * 2 + b;
+        const int j = b - 2;
+        return (rg * 4 + (j >> 4)) * 16 + (j & 15);
+    }
+    if (fmt == F_IQ3_XXS) {
+        if (b < 2) return 1536 + rg * 2 + b;
+        if (b < 66) { const int j = b - 2; return (rg * 4 + (j >> 4)) * 16 + (j & 15); }
+        const int j = b - 66;
+        return 1024 + (rg * 4 + (j >> 3)) * 8 + (j & 7);
+    }
+    if (fmt == F_IQ4_XS) {
+        if (b < 8) return 2048 + rg * 8 + b;
+        const int j = b - 8;
+        return (rg * 4 + (j >> 5)) * 32 + (j & 31);
+    }
     if (fmt == F_IQ2_S) {
         if (b < 2) return 1280 + rg * 2 + b;
         if (b < 34) { const int j = b - 2; return (rg * 4 + (j >> 3)) * 16 + (j & 7); }

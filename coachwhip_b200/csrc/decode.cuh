@@ -13,7 +13,7 @@
 // the per-16/32-column scale is rounded to f16 (about 2^-11 relative per weight).
 //
 // Row addressing (see the tiled layout in cwx_common.cuh): K-quants, Q8_0 and MXFP4 rows are
-// whole (row r of a piece at r * piece_row_bytes); IQ2_S / IQ3_S pieces are 16-row groups stored
+// whole (row r of a piece at r * piece_row_bytes); the IQ formats' pieces are 16-row groups stored
 // field by field, addressed through IqRow.
 #pragma once
 #include "cwx_common.cuh"
@@ -79,10 +79,59 @@ __device__ __forceinline__ float iq_grid(int fmt, const HTables& t, int idx, int
 
 // ---------------------------------------------------------------- exact 16-column runs
 // 16 consecutive columns [kofs, kofs+16) of one row's 256-column piece, bit-exact f32.
+__device__ __forceinline__ uint32_t iq_u32(int fmt, const IqRow& r, int b) {
+    return (uint32_t)iq_byte(fmt, r, b) | ((uint32_t)iq_byte(fmt, r, b + 1) << 8) |
+           ((uint32_t)iq_byte(fmt, r, b + 2) << 16) | ((uint32_t)iq_byte(fmt, r, b + 3) << 24);
+}
+
 template <bool SMEM>
 __device__ __forceinline__ void dec16_iq_exact(int fmt, const IqRow& r, int kofs, float* v, const HTables& t) {
     const int ib = kofs >> 5;
     const float d = h2f_bits((uint16_t)(iq_byte(fmt, r, 0) | (iq_byte(fmt, r, 1) << 8)));
+    if (fmt == F_IQ2_XXS) {  // 8 bytes per 32 columns: 4 grid entries, then signs and scale
+        const uint32_t aux = iq_u32(fmt, r, 2 + 8 * ib + 4);
+        const float dl = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.25f);
+#pragma unroll
+        for (int gi = 0; gi < 2; ++gi) {
+            const int g = ((kofs & 16) >> 3) + gi;
+            const uint64_t grid = cwx_iq2s_expand(d_iq2xxs_codes[iq_byte(fmt, r, 2 + 8 * ib + g)]);
+            const uint32_t sg = cwx_ksigns((aux >> (7 * g)) & 127u);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float x = __fmul_rn(dl, (float)((grid >> (8 * j)) & 0xFF));
+                v[8 * gi + j] = ((sg >> j) & 1) ? -x : x;
+            }
+        }
+        return;
+    }
+    if (fmt == F_IQ3_XXS) {  // grid entries at 2 + 8 per 32 columns; signs and scale at 66 + 4 per 32
+        const uint32_t aux = iq_u32(fmt, r, 66 + 4 * ib);
+        const float dl = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.5f);
+#pragma unroll
+        for (int gi = 0; gi < 2; ++gi) {
+            const int g = ((kofs & 16) >> 3) + gi;
+            const uint32_t sg = cwx_ksigns((aux >> (7 * g)) & 127u);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t grid = cwx_iq3xxs_expand(d_iq3xxs_codes[iq_byte(fmt, r, 2 + 8 * ib + 2 * g + h)]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float x = __fmul_rn(dl, (float)((grid >> (8 * j)) & 0xFF));
+                    v[8 * gi + 4 * h + j] = ((sg >> (4 * h + j)) & 1) ? -x : x;
+                }
+            }
+        }
+        return;
+    }
+    if (fmt == F_IQ4_XS) {
+        const uint32_t sh = (uint32_t)iq_byte(fmt, r, 2) | ((uint32_t)iq_byte(fmt, r, 3) << 8);
+        const int ls = ((iq_byte(fmt, r, 4 + (ib >> 1)) >> (4 * (ib & 1))) & 0xF) | (((sh >> (2 * ib)) & 3) << 4);
+        const float dl = __fmul_rn(d, (float)(ls - 32));
+        const int nsh = (kofs & 16) ? 4 : 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(dl, (float)cwx_iq4nl((iq_byte(fmt, r, 8 + 16 * ib + i) >> nsh) & 0xF));
+        return;
+    }
     if (fmt == F_IQ2_S) {
         const uint8_t qh = iq_byte(fmt, r, 66 + ib);
         const int g0 = (kofs & 16) >> 3;  // 2 groups of 8
@@ -167,57 +216,6 @@ __device__ __forceinline__ void dec16_row_exact(int fmt, const uint8_t* b, int k
             const int sh = (kofs & 16) ? 4 : 0;
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] = __fmul_rn((float)kv[(blk[1 + i] >> sh) & 0xF], d);
-            break;
-        }
-        case F_IQ2_XXS: {  // 8 bytes per 32 columns: 4 grid entries, then signs and scale
-            const float d = h2f_bits(ld_u16(b));
-            const uint8_t* q = b + 2 + 8 * (kofs >> 5);
-            const uint32_t aux = ld_u32(q + 4);
-            const float dl = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.25f);
-#pragma unroll
-            for (int gi = 0; gi < 2; ++gi) {
-                const int g = ((kofs & 16) >> 3) + gi;
-                const uint64_t grid = cwx_iq2s_expand(d_iq2xxs_codes[q[g]]);
-                const uint32_t sg = cwx_ksigns((aux >> (7 * g)) & 127u);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float x = __fmul_rn(dl, (float)((grid >> (8 * j)) & 0xFF));
-                    v[8 * gi + j] = ((sg >> j) & 1) ? -x : x;
-                }
-            }
-            break;
-        }
-        case F_IQ3_XXS: {  // grid entries at 2 + 8 per 32 columns; signs and scale at 66 + 4 per 32
-            const float d = h2f_bits(ld_u16(b));
-            const int ib = kofs >> 5;
-            const uint8_t* q = b + 2 + 8 * ib;
-            const uint32_t aux = ld_u32(b + 66 + 4 * ib);
-            const float dl = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(aux >> 28))), 0.5f);
-#pragma unroll
-            for (int gi = 0; gi < 2; ++gi) {
-                const int g = ((kofs & 16) >> 3) + gi;
-                const uint32_t sg = cwx_ksigns((aux >> (7 * g)) & 127u);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint32_t grid = cwx_iq3xxs_expand(d_iq3xxs_codes[q[2 * g + h]]);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float x = __fmul_rn(dl, (float)((grid >> (8 * j)) & 0xFF));
-                        v[8 * gi + 4 * h + j] = ((sg >> (4 * h + j)) & 1) ? -x : x;
-                    }
-                }
-            }
-            break;
-        }
-        case F_IQ4_XS: {
-            const float d = h2f_bits(ld_u16(b));
-            const int ib = kofs >> 5;
-            const int ls = ((b[4 + (ib >> 1)] >> (4 * (ib & 1))) & 0xF) | (((ld_u16(b + 2) >> (2 * ib)) & 3) << 4);
-            const float dl = __fmul_rn(d, (float)(ls - 32));
-            const uint8_t* q = b + 8 + 16 * ib;
-            const int sh = (kofs & 16) ? 4 : 0;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(dl, (float)cwx_iq4nl((q[i] >> sh) & 0xF));
             break;
         }
         default:

@@ -22,13 +22,16 @@
 // a quad contributes 4 of its own columns), legal because A and B use the same permutation, and
 // the activation rows arrive packed in exactly that order (act.cu).
 //
-// IQ2_S / IQ3_S fast path (the routed format of the launch): the codebooks live in shared memory
-// replicated (8 copies of the IQ2_S table, 16 of the IQ3_S one) and interleaved so that the lanes
-// sharing a shared-memory wavefront read different banks whatever entries they ask for. The
-// weights go to the tensor cores as exact f16 integers, codebook value x sign x (2 * scale + 1);
-// the block scale d (and the 1/8 of IQ2_S) multiplies the f32 partial sum of each 256-column
-// piece, so no weight is rounded. Activations: f16 (hi), plus the lo part when the job asks for
-// ~22-bit products (its outputs are re-quantised downstream).
+// IQ2_S / IQ3_S / IQ2_XXS / IQ3_XXS fast path (the routed format of the launch): the codebooks
+// live in shared memory replicated (8 copies of an 8-value table, 16 of a 4-value one) and
+// interleaved so that the lanes sharing a shared-memory wavefront read different banks whatever
+// entries they ask for. The weights go to the tensor cores as exact f16 integers, codebook value x
+// sign x (2 * scale + 1) (at most 62 x 31); the block scale d (and the 1/8 of IQ2_S and IQ2_XXS,
+// the 1/4 of IQ3_XXS) multiplies the f32 partial sum of each 256-column piece, so no weight is
+// rounded. IQ4_XS (no codebook): nibble pairs map through a table to level pairs, times
+// (ls - 32) of the 32-column block; exact while the product stays within 2048 (beyond, 11 bits).
+// Activations: f16 (hi), plus the lo part when the job asks for ~22-bit products (its outputs are
+// re-quantised downstream).
 // Other formats (and any job of another format in the same launch): exact f32 dequantisation
 // rounded to f16 (hi + lo pairs when the job asks for it), activations hi + lo.
 #include <cstddef>
@@ -57,9 +60,18 @@ constexpr int LAUNCH_REGS = 96, PROD_REGS = 64, CONS_REGS = 104;
 static_assert(NPW * PROD_REGS + NCW * CONS_REGS <= (NCW + NPW) * LAUNCH_REGS, "register split");
 
 template <int FMT>
-struct Tbl {  // replicated codebook bytes in shared memory
-    static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 128 : FMT == F_IQ3_S ? 512 * 128 : 0;
+struct Tbl {  // replicated codebook bytes in shared memory (128 bytes per entry)
+    static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 128
+                                 : FMT == F_IQ3_S ? 512 * 128
+                                 : (FMT == F_IQ2_XXS || FMT == F_IQ3_XXS || FMT == F_IQ4_XS) ? 256 * 128
+                                                                                               : 0;
 };
+// This lane's copy of the table: 8-value codebooks (IQ2_S, IQ2_XXS) keep 8 copies of 16 bytes per
+// entry, 4-value ones (IQ3_S, IQ3_XXS) 16 copies of 8 bytes, the IQ4_XS nibble-pair table (256
+// pairs of levels) 32 copies of 4 bytes.
+__device__ __forceinline__ int tbl_lane(int fmt, int lane) {
+    return (fmt == F_IQ2_S || fmt == F_IQ2_XXS) ? (lane & 7) * 16 : fmt == F_IQ4_XS ? (lane & 31) * 4 : (lane & 15) * 8;
+}
 
 template <int KS>
 struct Cfg {
@@ -319,6 +331,48 @@ __device__ __forceinline__ void iq3s_pairs(const uint4& Qs, const uint2& S, uint
     }
 }
 
+// IQ2_XXS / IQ3_XXS sign byte from its 7 stored bits (the eighth makes the count even).
+__device__ __forceinline__ uint32_t ksigns_d(uint32_t s7) { return s7 | ((__popc(s7) & 1u) << 7); }
+
+// IQ2_XXS: columns 16ss .. 16ss+15 of the thread's 64 as 8 f16 pairs g * sign * (2s + 1). Q =
+// [entries | signs/scale] of the 64 columns' two 32-column blocks.
+__device__ __forceinline__ void iq2xxs_pairs(const uint4& Q, int ss, const uint8_t* tl, uint32_t* p) {
+    const uint32_t qw = ss < 2 ? Q.x : Q.z, aux = ss < 2 ? Q.y : Q.w;
+    const __half2 od = odd2(aux >> 28);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int l = 2 * (ss & 1) + h;
+        const uint32_t b = __byte_perm(qw, 0u, 0x4440 | l);
+        const uint4 G = *reinterpret_cast<const uint4*>(tl + (b << 7));
+        const uint32_t s8 = ksigns_d((aux >> (7 * l)) & 127u);
+        p[4 * h + 0] = h22u(__hmul2(u2h2(sign_pair(s8, 0, G.x)), od));
+        p[4 * h + 1] = h22u(__hmul2(u2h2(sign_pair(s8, 2, G.y)), od));
+        p[4 * h + 2] = h22u(__hmul2(u2h2(sign_pair(s8, 4, G.z)), od));
+        p[4 * h + 3] = h22u(__hmul2(u2h2(sign_pair(s8, 6, G.w)), od));
+    }
+}
+
+// IQ3_XXS: the same 16 columns. Q = the 16 grid-entry bytes of the two blocks, A = their
+// signs/scale words.
+__device__ __forceinline__ void iq3xxs_pairs(const uint4& Q, const uint2& A, int ss, const uint8_t* tl, uint32_t* p) {
+    const uint32_t aux = ss < 2 ? A.x : A.y;
+    const __half2 od = odd2(aux >> 28);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int l = 2 * (ss & 1) + h;
+        const uint32_t w = ss < 2 ? (l < 2 ? Q.x : Q.y) : (l < 2 ? Q.z : Q.w);
+        const uint32_t b0 = __byte_perm(w, 0u, 0x4440 | (2 * (l & 1)));
+        const uint32_t b1 = __byte_perm(w, 0u, 0x4440 | (2 * (l & 1) + 1));
+        const uint2 G0 = *reinterpret_cast<const uint2*>(tl + (b0 << 7));
+        const uint2 G1 = *reinterpret_cast<const uint2*>(tl + (b1 << 7));
+        const uint32_t s8 = ksigns_d((aux >> (7 * l)) & 127u);
+        p[4 * h + 0] = h22u(__hmul2(u2h2(sign_pair(s8, 0, G0.x)), od));
+        p[4 * h + 1] = h22u(__hmul2(u2h2(sign_pair(s8, 2, G0.y)), od));
+        p[4 * h + 2] = h22u(__hmul2(u2h2(sign_pair(s8, 4, G1.x)), od));
+        p[4 * h + 3] = h22u(__hmul2(u2h2(sign_pair(s8, 6, G1.y)), od));
+    }
+}
+
 // Activation chunks of sub-step ss for this thread's token slot: hi columns 0-7 / 8-15 (and lo;
 // a piece's 32 hi chunks come first, then its 32 lo chunks).
 // Slots past the pass's tokens read whatever the slot holds: an MMA output column depends only on
@@ -338,84 +392,75 @@ __device__ __forceinline__ void load_b(const uint8_t* brow, int ss, bool lo, uin
     lb[4] = l1.x; lb[5] = l1.y; lb[6] = l1.z; lb[7] = l1.w;
 }
 
-// One step of a fast-path job (late release): this warp's 16 rows x 256 columns against NT n-tiles
-// of 8 activation rows (bnt bytes apart); the piece's partial sums are scaled by the rows' block
-// scales and added to acc[nt * 4 + i].
-template <int FMT, int NT>
-__device__ __forceinline__ void fast_step(const uint8_t* wsl, int mt, int g, int c4, const uint8_t* tl,
-                                          const uint8_t* brow, int bnt, bool lo, float* acc) {
-    float t[NT][4];
+// Fast-path inputs of one thread: the rows' index, sign and scale bytes and block scales, copied
+// from the weight slot into registers (so, on the early-release path, the slot can go back to the
+// producer before the decode and the MMAs run from these registers, the tables and the
+// activation slot).
+struct FastIn {
+    uint4 QA, QB;     // IQ2_S: [qs | signs]; IQ3_S: qs; IQ2_XXS: [entries | signs/scale] x 2;
+                      // IQ3_XXS: entries; IQ4_XS: the first 32-column block's nibble bytes
+    uint4 QA2, QB2;   // IQ4_XS: the second block's nibble bytes
+    uint2 SA, SB;     // IQ3_S: signs; IQ3_XXS: signs/scale words
+    uint32_t HA, HB;  // IQ2_S: [qh | scales]; IQ3_S: qh | scales << 16; IQ4_XS: (ls - 32) of the two
+                      // blocks as an f16 pair
+    float dA, dB;     // block scales of the two rows (times 1/8 for IQ2_S and IQ2_XXS, 1/4 for IQ3_XXS)
+};
+
+// IQ4_XS scales (ls - 32) of blocks 2 c4 and 2 c4 + 1 as an f16 pair (exact), from the row's
+// [d | scales_h] and scales_l words.
+__device__ __forceinline__ uint32_t iq4xs_scales(uint2 m, int c4) {
+    const uint32_t sh = m.x >> 16, sl = m.y;
+    const int l0 = (int)(((sl >> (8 * c4)) & 15u) | (((sh >> (4 * c4)) & 3u) << 4));
+    const int l1 = (int)(((sl >> (8 * c4 + 4)) & 15u) | (((sh >> (4 * c4 + 2)) & 3u) << 4));
+    return h22u(__floats2half2_rn((float)(l0 - 32), (float)(l1 - 32)));
+}
+
+// IQ4_XS: columns 16ss .. 16ss+15 of the thread's 64 (the low (ss even) or high nibbles of block
+// ss / 2's 16 bytes Q) as 8 f16 pairs level * (ls - 32): exact up to 2048 in magnitude (products of
+// the largest levels and scales beyond it round to 11 bits). tl = this lane's copy of the pair
+// table (nibble pair -> level pair).
+__device__ __forceinline__ void iq4xs_pairs(const uint4& Q, __half2 sc, int nh, const uint8_t* tl, uint32_t* p) {
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) t[nt][0] = t[nt][1] = t[nt][2] = t[nt][3] = 0.f;
-    float dA, dB;
-    uint4 QA, QB;
-    uint2 SA = make_uint2(0, 0), SB = SA;
-    uint32_t HA, HB;
-    if (FMT == F_IQ2_S) {
-        const uint8_t* grp = wsl + mt * (16 * 82);
-        QA = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 16);
-        QB = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 16);
-        HA = *reinterpret_cast<const uint32_t*>(grp + 1024 + (g * 4 + c4) * 4);
-        HB = *reinterpret_cast<const uint32_t*>(grp + 1024 + ((g + 8) * 4 + c4) * 4);
-        dA = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1280 + 2 * g)), 0.125f);
-        dB = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1280 + 2 * (g + 8))), 0.125f);
-    } else {
-        const uint8_t* grp = wsl + mt * (16 * 110);
-        QA = *reinterpret_cast<const uint4*>(grp + g * 64 + 16 * c4);
-        QB = *reinterpret_cast<const uint4*>(grp + (g + 8) * 64 + 16 * c4);
-        SA = *reinterpret_cast<const uint2*>(grp + 1024 + g * 32 + 8 * c4);
-        SB = *reinterpret_cast<const uint2*>(grp + 1024 + (g + 8) * 32 + 8 * c4);
-        HA = *reinterpret_cast<const uint16_t*>(grp + 1536 + g * 8 + 2 * c4) | ((uint32_t)grp[1664 + g * 4 + c4] << 16);
-        HB = *reinterpret_cast<const uint16_t*>(grp + 1536 + (g + 8) * 8 + 2 * c4) |
-             ((uint32_t)grp[1664 + (g + 8) * 4 + c4] << 16);
-        dA = h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1728 + 2 * g));
-        dB = h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1728 + 2 * (g + 8)));
-    }
-#pragma unroll
-    for (int ss = 0; ss < 4; ++ss) {
-        uint32_t pa[8], pb[8];
-        if (FMT == F_IQ2_S) {
-            iq2s_pairs(QA, HA, ss, tl, pa);
-            iq2s_pairs(QB, HB, ss, tl, pb);
-        } else {
-            iq3s_pairs(QA, SA, HA & 0xFFFFu, HA >> 16, ss, tl, pa);
-            iq3s_pairs(QB, SB, HB & 0xFFFFu, HB >> 16, ss, tl, pb);
-        }
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            uint32_t hb[8], lb[8];
-            load_b(brow + nt * bnt, ss, lo, hb, lb);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
-                mma_16816(t[nt], af, hb[2 * kk], hb[2 * kk + 1]);
-                if (lo) mma_16816(t[nt], af, lb[2 * kk], lb[2 * kk + 1]);
-            }
-        }
-    }
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        acc[nt * 4 + 0] = __fmaf_rn(t[nt][0], dA, acc[nt * 4 + 0]);
-        acc[nt * 4 + 1] = __fmaf_rn(t[nt][1], dA, acc[nt * 4 + 1]);
-        acc[nt * 4 + 2] = __fmaf_rn(t[nt][2], dB, acc[nt * 4 + 2]);
-        acc[nt * 4 + 3] = __fmaf_rn(t[nt][3], dB, acc[nt * 4 + 3]);
+    for (int w = 0; w < 4; ++w) {
+        const uint32_t x = w == 0 ? Q.x : w == 1 ? Q.y : w == 2 ? Q.z : Q.w;
+        const uint32_t y = (nh ? x >> 4 : x) & 0x0F0F0F0Fu;
+        const uint32_t z = y | (y >> 4);  // byte 0: nibbles 0, 1; byte 2: nibbles 2, 3
+        const uint32_t v0 = *reinterpret_cast<const uint32_t*>(tl + ((z & 0xFFu) << 7));
+        const uint32_t v1 = *reinterpret_cast<const uint32_t*>(tl + (((z >> 16) & 0xFFu) << 7));
+        p[2 * w + 0] = h22u(__hmul2(u2h2(v0), sc));
+        p[2 * w + 1] = h22u(__hmul2(u2h2(v1), sc));
     }
 }
 
-// Early-release form of a fast step (f16 activations only): the rows' index, sign and scale bytes
-// and block scales are copied from the weight slot into registers first, so the slot can go back
-// to the producer before the decode and the MMAs run (from these registers, the codebook tables
-// and the activation slot).
-struct FastIn {
-    uint4 QA, QB;     // IQ2_S: [qs | signs]; IQ3_S: qs
-    uint2 SA, SB;     // IQ3_S: signs
-    uint32_t HA, HB;  // IQ2_S: [qh | scales]; IQ3_S: qh | scales << 16
-    float dA, dB;     // block scales of the two rows (times 1/8 for IQ2_S)
-};
-
 template <int FMT>
 __device__ __forceinline__ void fast_load(const uint8_t* wsl, int mt, int g, int c4, FastIn& in) {
-    if (FMT == F_IQ2_S) {
+    if (FMT == F_IQ4_XS) {
+        const uint8_t* grp = wsl + mt * (16 * 136);
+        in.QA = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 32);
+        in.QA2 = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 32 + 16);
+        in.QB = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 32);
+        in.QB2 = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 32 + 16);
+        const uint2 mA = *reinterpret_cast<const uint2*>(grp + 2048 + 8 * g);
+        const uint2 mB = *reinterpret_cast<const uint2*>(grp + 2048 + 8 * (g + 8));
+        in.HA = iq4xs_scales(mA, c4);
+        in.HB = iq4xs_scales(mB, c4);
+        in.dA = h2f_bits((uint16_t)(mA.x & 0xFFFFu));
+        in.dB = h2f_bits((uint16_t)(mB.x & 0xFFFFu));
+    } else if (FMT == F_IQ2_XXS) {
+        const uint8_t* grp = wsl + mt * (16 * 66);
+        in.QA = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 16);
+        in.QB = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 16);
+        in.dA = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1024 + 2 * g)), 0.125f);
+        in.dB = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1024 + 2 * (g + 8))), 0.125f);
+    } else if (FMT == F_IQ3_XXS) {
+        const uint8_t* grp = wsl + mt * (16 * 98);
+        in.QA = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 16);
+        in.QB = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 16);
+        in.SA = *reinterpret_cast<const uint2*>(grp + 1024 + (g * 4 + c4) * 8);
+        in.SB = *reinterpret_cast<const uint2*>(grp + 1024 + ((g + 8) * 4 + c4) * 8);
+        in.dA = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1536 + 2 * g)), 0.25f);
+        in.dB = __fmul_rn(h2f_bits(*reinterpret_cast<const uint16_t*>(grp + 1536 + 2 * (g + 8))), 0.25f);
+    } else if (FMT == F_IQ2_S) {
         const uint8_t* grp = wsl + mt * (16 * 82);
         in.QA = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 16);
         in.QB = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 16);
@@ -437,8 +482,11 @@ __device__ __forceinline__ void fast_load(const uint8_t* wsl, int mt, int g, int
     }
 }
 
+// A fast-path step from its inputs: this warp's 16 rows x 256 columns against NT n-tiles of 8
+// activation rows (bnt bytes apart), hi activations plus the lo parts when `lo`; the piece's
+// partial sums are scaled by the rows' block scales and added to acc[nt * 4 + i].
 template <int FMT, int NT>
-__device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl, const uint8_t* brow, int bnt,
+__device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl, const uint8_t* brow, int bnt, bool lo,
                                              float* acc) {
     float t[NT][4];
 #pragma unroll
@@ -446,7 +494,18 @@ __device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl
 #pragma unroll
     for (int ss = 0; ss < 4; ++ss) {
         uint32_t pa[8], pb[8];
-        if (FMT == F_IQ2_S) {
+        if (FMT == F_IQ4_XS) {
+            const __half2 sa = ss < 2 ? __low2half2(u2h2(in.HA)) : __high2half2(u2h2(in.HA));
+            const __half2 sb = ss < 2 ? __low2half2(u2h2(in.HB)) : __high2half2(u2h2(in.HB));
+            iq4xs_pairs(ss < 2 ? in.QA : in.QA2, sa, ss & 1, tl, pa);
+            iq4xs_pairs(ss < 2 ? in.QB : in.QB2, sb, ss & 1, tl, pb);
+        } else if (FMT == F_IQ2_XXS) {
+            iq2xxs_pairs(in.QA, ss, tl, pa);
+            iq2xxs_pairs(in.QB, ss, tl, pb);
+        } else if (FMT == F_IQ3_XXS) {
+            iq3xxs_pairs(in.QA, in.SA, ss, tl, pa);
+            iq3xxs_pairs(in.QB, in.SB, ss, tl, pb);
+        } else if (FMT == F_IQ2_S) {
             iq2s_pairs(in.QA, in.HA, ss, tl, pa);
             iq2s_pairs(in.QB, in.HB, ss, tl, pb);
         } else {
@@ -456,11 +515,12 @@ __device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             uint32_t hb[8], lb[8];
-            load_b(brow + nt * bnt, ss, false, hb, lb);
+            load_b(brow + nt * bnt, ss, lo, hb, lb);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
                 const uint32_t af[4] = {pa[2 * kk], pb[2 * kk], pa[2 * kk + 1], pb[2 * kk + 1]};
                 mma_16816(t[nt], af, hb[2 * kk], hb[2 * kk + 1]);
+                if (lo) mma_16816(t[nt], af, lb[2 * kk], lb[2 * kk + 1]);
             }
         }
     }
@@ -671,6 +731,31 @@ __device__ __forceinline__ void build_tables(uint8_t* tbl, int tid) {
 #pragma unroll
             for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(tbl + e * 128 + c * 16) = q;
         }
+    } else if (FMT == F_IQ4_XS) {
+        for (int e = tid; e < 256; e += NCW * 32) {
+            const uint32_t q = h22u(__floats2half2_rn((float)cwx_iq4nl(e & 15), (float)cwx_iq4nl(e >> 4)));
+#pragma unroll
+            for (int c = 0; c < 32; ++c) *reinterpret_cast<uint32_t*>(tbl + e * 128 + c * 4) = q;
+        }
+    } else if (FMT == F_IQ2_XXS) {
+        for (int e = tid; e < 256; e += NCW * 32) {
+            const uint64_t v = cwx_iq2s_expand(d_iq2xxs_codes[e]);
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                w[j] = h22u(__floats2half2_rn((float)((v >> (16 * j)) & 0xFF), (float)((v >> (16 * j + 8)) & 0xFF)));
+            const uint4 q = make_uint4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(tbl + e * 128 + c * 16) = q;
+        }
+    } else if (FMT == F_IQ3_XXS) {
+        for (int e = tid; e < 256; e += NCW * 32) {
+            const uint32_t v = cwx_iq3xxs_expand(d_iq3xxs_codes[e]);
+            const uint2 q = make_uint2(h22u(__floats2half2_rn((float)(v & 0xFF), (float)((v >> 8) & 0xFF))),
+                                       h22u(__floats2half2_rn((float)((v >> 16) & 0xFF), (float)(v >> 24))));
+#pragma unroll
+            for (int c = 0; c < 16; ++c) *reinterpret_cast<uint2*>(tbl + e * 128 + c * 8) = q;
+        }
     } else if (FMT == F_IQ3_S) {
         for (int e = tid; e < 512; e += NCW * 32) {
             const uint32_t v = cwx_iq3s_expand(d_iq3s_codes[e]);
@@ -804,7 +889,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
         build_tables<FMT>(tbl, tid);
         asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
     }
-    const uint8_t* tl = tbl + (FMT == F_IQ2_S ? (lane & 7) * 16 : (lane & 15) * 8);
+    const uint8_t* tl = tbl + tbl_lane(FMT, lane);
     const int mt = warp % C::MT, ks = warp / C::MT;
     const int g = lane >> 2, c4 = lane & 3;
     // this thread's activation row (slot g of n-tile 0; with one n-tile, passes of fewer than 8
@@ -845,12 +930,18 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
             if (active) fast_load<FMT>(wsl, mt, g, c4, in);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty_w[s]);  // the weights go back before the math
-            if (active) fast_compute<FMT, NT>(in, tl, brow, bnt, acc);
+            if (active) fast_compute<FMT, NT>(in, tl, brow, bnt, false, acc);
         } else {
             if (active) {
                 const Layout& L = a.job[jobi].m.L;
                 const DxAt dx{bslot + dx0_off, bslot + dx1_off};
-                if (FMT != 0 && L.fmt == FMT && !qi) fast_step<FMT, NT>(wsl, mt, g, c4, tl, brow, bnt, true, acc);
+                // (late release; IQ4_XS weights above 2048 are not exact in f16, so its products
+                // that must carry ~22 bits take the exact path)
+                if (FMT != 0 && L.fmt == FMT && !qi && (FMT != F_IQ4_XS || !lo)) {
+                    FastIn in;
+                    fast_load<FMT>(wsl, mt, g, c4, in);
+                    fast_compute<FMT, NT>(in, tl, brow, bnt, lo, acc);
+                }
                 else if (L.fmt == F_Q4_K && L.kp_row_bytes == 144) q4k_step<NT>(wsl, mt, g, c4, brow, bnt, lo, qi, dx, acc);
                 else generic_step<NT>(L, kp, wsl, mt, g, c4, brow, bnt, lo, qi, dx, acc);
             }
@@ -917,7 +1008,18 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
 
 // ---------------------------------------------------------------- host side
 static int tbl_bytes(int fmt) {
-    return fmt == F_IQ2_S ? Tbl<F_IQ2_S>::BYTES : fmt == F_IQ3_S ? Tbl<F_IQ3_S>::BYTES : 0;
+    switch (fmt) {
+        case F_IQ2_S: return Tbl<F_IQ2_S>::BYTES;
+        case F_IQ3_S: return Tbl<F_IQ3_S>::BYTES;
+        case F_IQ2_XXS: return Tbl<F_IQ2_XXS>::BYTES;
+        case F_IQ3_XXS: return Tbl<F_IQ3_XXS>::BYTES;
+        case F_IQ4_XS: return Tbl<F_IQ4_XS>::BYTES;
+        default: return 0;
+    }
+}
+// Routed formats with a fast path in k_gemv.
+static bool fast_fmt(int fmt) {
+    return fmt == F_IQ2_S || fmt == F_IQ3_S || fmt == F_IQ2_XXS || fmt == F_IQ3_XXS || fmt == F_IQ4_XS;
 }
 
 // Stage sizes of a launch with routed format fmt (0: none), ks K-slices and a.tokcap picks per
@@ -968,11 +1070,11 @@ static int size_stages(GemvArgs& a, int fmt, int ks, int64_t experts_est, int64_
 
 template <int FMT, int KS, int NT>
 static int launch_fk(const GemvArgs& a, int64_t items, int smem, int device, int sm_count, cudaStream_t st) {
-    constexpr int fi = FMT == 0 ? 0 : FMT == F_IQ2_S ? 1 : 2;
+    constexpr int fi = FMT == 0 ? 0 : FMT == F_IQ2_S ? 1 : FMT == F_IQ3_S ? 2 : FMT == F_IQ2_XXS ? 3 : FMT == F_IQ3_XXS ? 4 : 5;
     constexpr int ki = (KS == 1 ? 0 : KS == 2 ? 1 : KS == 4 ? 2 : 3) + (NT == 2 ? 4 : NT == 4 ? 5 : 0);
     // the register split assumes the launch allocates LAUNCH_REGS per thread (allocation is in
     // steps of 8): a kernel compiled with fewer would make the consumers' increase wait forever
-    static int regs_ok[3][6] = {{0}};
+    static int regs_ok[6][6] = {{0}};
     if (!regs_ok[fi][ki]) {
         cudaFuncAttributes fa;
         cudaError_t e = cudaFuncGetAttributes(&fa, k_gemv<FMT, KS, NT>);
@@ -982,7 +1084,7 @@ static int launch_fk(const GemvArgs& a, int64_t items, int smem, int device, int
                         fa.numRegs, LAUNCH_REGS);
         regs_ok[fi][ki] = 1;
     }
-    static int attr_set[64][3][6] = {{{0}}};
+    static int attr_set[64][6][6] = {{{0}}};
     if (device < 0 || device >= 64 || attr_set[device][fi][ki] < smem) {
         cudaError_t e = cudaFuncSetAttribute(k_gemv<FMT, KS, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_gemv)");
@@ -1009,6 +1111,18 @@ static int launch_f(const GemvArgs& a, int ks, int nt, int64_t items, int smem, 
     }
 }
 
+static int launch_fmt(int fmt, const GemvArgs& a, int ks, int nt, int64_t items, int smem, int device, int sm_count,
+                      cudaStream_t st) {
+    switch (fmt) {
+        case F_IQ2_S: return launch_f<F_IQ2_S>(a, ks, nt, items, smem, device, sm_count, st);
+        case F_IQ3_S: return launch_f<F_IQ3_S>(a, ks, nt, items, smem, device, sm_count, st);
+        case F_IQ2_XXS: return launch_f<F_IQ2_XXS>(a, ks, nt, items, smem, device, sm_count, st);
+        case F_IQ3_XXS: return launch_f<F_IQ3_XXS>(a, ks, nt, items, smem, device, sm_count, st);
+        case F_IQ4_XS: return launch_f<F_IQ4_XS>(a, ks, nt, items, smem, device, sm_count, st);
+        default: return launch_f<0>(a, ks, nt, items, smem, device, sm_count, st);
+    }
+}
+
 int launch_gemv(const GemvArgs& in, int64_t experts_est, int device, int sm_count, cudaStream_t st) {
     GemvArgs a = in;
     // the routed format, when every routed job shares one IQ format
@@ -1021,7 +1135,7 @@ int launch_gemv(const GemvArgs& in, int64_t experts_est, int device, int sm_coun
         if (L.n_kp < n_kp) n_kp = L.n_kp;
         rows += L.n;
     }
-    if (fmt != F_IQ2_S && fmt != F_IQ3_S) fmt = 0;
+    if (!fast_fmt(fmt)) fmt = 0;
     int64_t items = 0;
     int smem = 0;
     // large piles (on average 24 or 10 picks and more): 32 or 16 picks per pass (4 or 2 n-tiles of
@@ -1030,9 +1144,7 @@ int launch_gemv(const GemvArgs& in, int64_t experts_est, int device, int sm_coun
         if (a.pile_est >= (nt == 4 ? 24 : 10) && a.tok_est > 8) {
             a.tokcap = 8 * nt;
             if (size_stages(a, fmt, 1, experts_est, &items, &smem) >= 2) {
-                if (fmt == F_IQ2_S) return launch_f<F_IQ2_S>(a, 1, nt, items, smem, device, sm_count, st);
-                if (fmt == F_IQ3_S) return launch_f<F_IQ3_S>(a, 1, nt, items, smem, device, sm_count, st);
-                return launch_f<0>(a, 1, nt, items, smem, device, sm_count, st);
+                return launch_fmt(fmt, a, 1, nt, items, smem, device, sm_count, st);
             }
         }
     // otherwise passes of the expected largest pile, a power of two up to 8
@@ -1051,9 +1163,7 @@ int launch_gemv(const GemvArgs& in, int64_t experts_est, int device, int sm_coun
         }
     if (size_stages(a, fmt, ks, experts_est, &items, &smem) < 2)
         return fail(CWX_EUNSUPPORTED, "expert pieces too large for shared memory");
-    if (fmt == F_IQ2_S) return launch_f<F_IQ2_S>(a, ks, 1, items, smem, device, sm_count, st);
-    if (fmt == F_IQ3_S) return launch_f<F_IQ3_S>(a, ks, 1, items, smem, device, sm_count, st);
-    return launch_f<0>(a, ks, 1, items, smem, device, sm_count, st);
+    return launch_fmt(fmt, a, ks, 1, items, smem, device, sm_count, st);
 }
 
 }  // namespace cwx

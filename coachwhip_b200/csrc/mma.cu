@@ -18,9 +18,12 @@
 // are 1024 bytes apart (the smem descriptor's stride byte offset). The MMA for columns
 // 16 kk .. 16 kk + 15 of a stage starts 32 kk bytes into the tile.
 //
-// Weights: IQ2_S / IQ3_S codebook values times sign times (2 s + 1) are exact f16 integers; one
-// f16 multiply by the block scale d (d / 8 for IQ2_S, exact in f16) rounds each weight once, so
-// the A tiles hold the exact dequantised weight rounded to f16.
+// Weights: IQ2_S / IQ3_S / IQ2_XXS / IQ3_XXS codebook values times sign times (2 s + 1), times 1/8
+// (IQ2_S, IQ2_XXS) or 1/4 (IQ3_XXS), are exact in f16 (at most 11 significant bits); one f16
+// multiply by the block scale d rounds each weight once, so the A tiles hold the exact dequantised
+// weight rounded to f16. (Scaling d by 1/8 first would not be exact: typical d are near the f16
+// subnormal range.) IQ4_XS: (d * (ls - 32)) * level in f32 rounded to f16 once, as the
+// reference's Metal matrix kernels store it.
 //
 // Two forms of a launch:
 //   fused gate/up: A rows 0-63 are gate rows f0 .. f0+63, rows 64-127 the up rows of the same
@@ -54,12 +57,17 @@ constexpr int DEC_PER = (DEC_CHUNKS + N_DEC * 32 - 1) / (N_DEC * 32);  // per de
 constexpr int GATHER_PER = NMAX * 8 / (N_GATHER * 32);                 // B chunks per gather thread
 constexpr int TMEM_COLS = 512;
 
-// Codebook as f16 values: IQ2_S 8 per entry, two copies (entry e of copy j at e*32 + j*16, the
-// copy picked by the lane's parity, so fewer lanes of a wavefront meet on a bank); IQ3_S 4 per
-// entry, four copies (e*32 + j*8).
+// Codebook as f16 values: IQ2_S and IQ2_XXS 8 per entry, two copies (entry e of copy j at
+// e*32 + j*16, the copy picked by the lane's parity, so fewer lanes of a wavefront meet on a bank);
+// IQ3_S and IQ3_XXS 4 per entry, four copies (e*32 + j*8); the 16 IQ4_XS levels as f32, one copy
+// per lane (level n of copy j at n*128 + j*4).
 template <int FMT>
 struct Tab {
-    static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 32 : FMT == F_IQ3_S ? 512 * 32 : 0;
+    static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 32
+                                 : FMT == F_IQ3_S ? 512 * 32
+                                 : (FMT == F_IQ2_XXS || FMT == F_IQ3_XXS) ? 256 * 32
+                                 : FMT == F_IQ4_XS ? 16 * 128
+                                                   : 0;
 };
 
 // shared memory: barriers, then 1024-aligned A and B stages, quantised stages, codebook, exchange
@@ -236,19 +244,79 @@ __device__ __forceinline__ uint4 dec_chunk(const uint8_t* q, int r, int c4, int 
         o.z = u_h2(__floats2half2_rn(v[4], v[5]));
         o.w = u_h2(__floats2half2_rn(v[6], v[7]));
         return o;
+    } else if (FMT == F_IQ4_XS) {
+        // chunk gi: block gi / 4 of the slice, its columns 8 (gi % 4) ..: the low (gi % 4 < 2) or
+        // high nibbles of bytes 8 (gi % 2) .. + 7; y = (d * (ls - 32)) * level in f32 (the
+        // reference's dequantize_iq4_xs), rounded to f16 once
+        const uint8_t* grp = q + (r >> 4) * (16 * 136);
+        const int rg = r & 15;
+        const uint2 M = *reinterpret_cast<const uint2*>(grp + 2048 + rg * 8);
+        const int ib = 2 * c4 + (gi >> 2);
+        const int ls = (int)(((M.y >> (4 * ib)) & 15u) | (((M.x >> (16 + 2 * ib)) & 3u) << 4));
+        const float ds = __fmul_rn(h2f_bits((uint16_t)(M.x & 0xFFFFu)), (float)(ls - 32));
+        const uint2 b = *reinterpret_cast<const uint2*>(grp + (rg * 4 + c4) * 32 + 16 * (gi >> 2) + 8 * (gi & 1));
+        const int sh = (gi & 2) ? 4 : 0;
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t n = (((j < 4 ? b.x : b.y) >> (8 * (j & 3) + sh)) & 15u);
+            v[j] = __fmul_rn(ds, *reinterpret_cast<const float*>(tab + n * 128));
+        }
+        uint4 o;
+        o.x = u_h2(__floats2half2_rn(v[0], v[1]));
+        o.y = u_h2(__floats2half2_rn(v[2], v[3]));
+        o.z = u_h2(__floats2half2_rn(v[4], v[5]));
+        o.w = u_h2(__floats2half2_rn(v[6], v[7]));
+        return o;
+    } else if (FMT == F_IQ2_XXS) {
+        // record (r, c4) = [entries | signs/scale] of the slice's two 32-column blocks; chunk gi is
+        // group gi % 4 of block gi / 4
+        const uint8_t* grp = q + (r >> 4) * (16 * 66);
+        const int rg = r & 15;
+        const uint4 Q = *reinterpret_cast<const uint4*>(grp + (rg * 4 + c4) * 16);
+        const __half2 d2 = __half2half2(__ushort_as_half(*reinterpret_cast<const uint16_t*>(grp + 1024 + 2 * rg)));
+        const uint32_t qw = gi < 4 ? Q.x : Q.z, aux = gi < 4 ? Q.y : Q.w;
+        const uint32_t b = __byte_perm(qw, 0u, 0x4440 | (gi & 3));
+        const uint4 G = *reinterpret_cast<const uint4*>(tab + b * 32);
+        const uint32_t s7 = (aux >> (7 * (gi & 3))) & 127u;
+        const uint32_t s8 = s7 | ((__popc(s7) & 1u) << 7);
+        const __half2 od = __hmul2(odd_h2(aux >> 28), __floats2half2_rn(0.125f, 0.125f));
+        uint4 o;
+        o.x = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 0, G.x)), od), d2));
+        o.y = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 2, G.y)), od), d2));
+        o.z = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 4, G.z)), od), d2));
+        o.w = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 6, G.w)), od), d2));
+        return o;
+    } else if (FMT == F_IQ3_XXS) {
+        // entries 2 gi, 2 gi + 1 of the slice's 16 (two per 8 columns); signs/scale word of block gi / 4
+        const uint8_t* grp = q + (r >> 4) * (16 * 98);
+        const int rg = r & 15;
+        const uint16_t e2 = *reinterpret_cast<const uint16_t*>(grp + (rg * 4 + c4) * 16 + 2 * gi);
+        const uint32_t aux = *reinterpret_cast<const uint32_t*>(grp + 1024 + (rg * 4 + c4) * 8 + 4 * (gi >> 2));
+        const __half2 d2 = __half2half2(__ushort_as_half(*reinterpret_cast<const uint16_t*>(grp + 1536 + 2 * rg)));
+        const uint32_t s7 = (aux >> (7 * (gi & 3))) & 127u;
+        const uint32_t s8 = s7 | ((__popc(s7) & 1u) << 7);
+        const __half2 od = __hmul2(odd_h2(aux >> 28), __floats2half2_rn(0.25f, 0.25f));
+        const uint2 G0 = *reinterpret_cast<const uint2*>(tab + (e2 & 0xFFu) * 32);
+        const uint2 G1 = *reinterpret_cast<const uint2*>(tab + (e2 >> 8) * 32);
+        uint4 o;
+        o.x = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 0, G0.x)), od), d2));
+        o.y = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 2, G0.y)), od), d2));
+        o.z = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 4, G1.x)), od), d2));
+        o.w = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 6, G1.y)), od), d2));
+        return o;
     } else if (FMT == F_IQ2_S) {
         const uint8_t* grp = q + (r >> 4) * (16 * 82);
         const int rg = r & 15;
         const uint4 Q = *reinterpret_cast<const uint4*>(grp + (rg * 4 + c4) * 16);
         const uint32_t H = *reinterpret_cast<const uint32_t*>(grp + 1024 + (rg * 4 + c4) * 4);
-        const __half dh = __ushort_as_half(*reinterpret_cast<const uint16_t*>(grp + 1280 + 2 * rg));
-        const __half2 d2 = __half2half2(__hmul(dh, __float2half_rn(0.125f)));
+        const __half2 d2 = __half2half2(__ushort_as_half(*reinterpret_cast<const uint16_t*>(grp + 1280 + 2 * rg)));
         const uint32_t qw = gi < 4 ? Q.x : Q.y, sw = gi < 4 ? Q.z : Q.w;
         const uint32_t b = __byte_perm(qw, 0u, 0x4440 | (gi & 3));
         const uint32_t idx = b | (((H >> (2 * gi)) & 3u) << 8);
         const uint4 G = *reinterpret_cast<const uint4*>(tab + idx * 32);
         const uint32_t s8 = __byte_perm(sw, 0u, 0x4440 | (gi & 3));
-        const __half2 od = odd_h2((H >> (16 + 4 * (gi >> 1))) & 0xFu);
+        const __half2 od = __hmul2(odd_h2((H >> (16 + 4 * (gi >> 1))) & 0xFu), __floats2half2_rn(0.125f, 0.125f));
         uint4 o;
         o.x = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 0, G.x)), od), d2));
         o.y = u_h2(__hmul2(__hmul2(h2_u(sgn_pair(s8, 2, G.y)), od), d2));
@@ -320,9 +388,12 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
         const int t = tid - W_DEC * 32;
         if (FMT == F_Q4_K) {
             // no codebook
-        } else if (FMT == F_IQ2_S) {
-            for (int e = t; e < 1024; e += N_DEC * 32) {
-                const uint64_t v = cwx_iq2s_expand(d_iq2s_codes[e]);
+        } else if (FMT == F_IQ4_XS) {
+            for (int e = t; e < 16 * 32; e += N_DEC * 32)
+                *reinterpret_cast<float*>(tab + (e >> 5) * 128 + (e & 31) * 4) = (float)cwx_iq4nl(e >> 5);
+        } else if (FMT == F_IQ2_S || FMT == F_IQ2_XXS) {
+            for (int e = t; e < (FMT == F_IQ2_S ? 1024 : 256); e += N_DEC * 32) {
+                const uint64_t v = cwx_iq2s_expand(FMT == F_IQ2_S ? d_iq2s_codes[e] : d_iq2xxs_codes[e]);
                 uint4 o;
                 o.x = u_h2(__floats2half2_rn((float)(v & 0xFF), (float)((v >> 8) & 0xFF)));
                 o.y = u_h2(__floats2half2_rn((float)((v >> 16) & 0xFF), (float)((v >> 24) & 0xFF)));
@@ -332,8 +403,8 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                 *reinterpret_cast<uint4*>(tab + e * 32 + 16) = o;
             }
         } else {
-            for (int e = t; e < 512; e += N_DEC * 32) {
-                const uint32_t v = cwx_iq3s_expand(d_iq3s_codes[e]);
+            for (int e = t; e < (FMT == F_IQ3_S ? 512 : 256); e += N_DEC * 32) {
+                const uint32_t v = FMT == F_IQ3_S ? cwx_iq3s_expand(d_iq3s_codes[e]) : cwx_iq3xxs_expand(d_iq3xxs_codes[e]);
                 const uint2 o = make_uint2(u_h2(__floats2half2_rn((float)(v & 0xFF), (float)((v >> 8) & 0xFF))),
                                            u_h2(__floats2half2_rn((float)((v >> 16) & 0xFF), (float)(v >> 24))));
 #pragma unroll
@@ -459,7 +530,10 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
     } else if (warp >= W_DEC) {
         // ---------------- decode: the decoder threads share a stage's 128 rows x 8 chunks
         const int t = tid - W_DEC * 32;
-        const uint8_t* tl = tab + (FMT == F_IQ2_S ? (lane & 1) * 16 : (lane & 3) * 8);  // this lane's copy
+        // this lane's copy of the table
+        const uint8_t* tl = tab + ((FMT == F_IQ2_S || FMT == F_IQ2_XXS) ? (lane & 1) * 16
+                                   : FMT == F_IQ4_XS                   ? lane * 4
+                                                                       : (lane & 3) * 8);
         Iter it;
         MItem m;
         uint32_t c = 0, p = 0;
@@ -571,11 +645,16 @@ int launch_f16rows(const float* x, int64_t n, __half* y, cudaStream_t st) {
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_f16rows");
 }
 
-// Which launches can take the tensor-core path: IQ2_S / IQ3_S weights in full 64-row tiles and
+// Formats the tensor-core products decode.
+bool mma_format(int fmt) {
+    return fmt == F_IQ2_S || fmt == F_IQ3_S || fmt == F_IQ2_XXS || fmt == F_IQ3_XXS || fmt == F_IQ4_XS || fmt == F_Q4_K;
+}
+
+// Which launches can take the tensor-core path: weights of those formats in full 64-row tiles and
 // whole 256-column pieces, gate and up of one format and shape.
 bool mma_supports(const MmaArgs& a) {
     const Layout& L = a.a0.L;
-    if (L.fmt != F_IQ2_S && L.fmt != F_IQ3_S && L.fmt != F_Q4_K) return false;
+    if (!mma_format(L.fmt)) return false;
     if (L.k % PIECE_K || L.n % (a.fused ? 64 : 128)) return false;
     if (a.fused) {
         const Layout& U = a.a1.L;
@@ -587,9 +666,10 @@ bool mma_supports(const MmaArgs& a) {
 
 template <int FMT>
 static int launch_mma_f(const MmaArgs& a, int device, int sm_count, cudaStream_t st) {
-    constexpr int fi = FMT == F_IQ2_S ? 0 : FMT == F_IQ3_S ? 1 : 2;
+    constexpr int fi =
+        FMT == F_IQ2_S ? 0 : FMT == F_IQ3_S ? 1 : FMT == F_IQ2_XXS ? 2 : FMT == F_IQ3_XXS ? 3 : FMT == F_IQ4_XS ? 4 : 5;
     const int smem = mm::Smem::total<FMT>() + 1024;
-    static int attr_set[64][3] = {{0}};
+    static int attr_set[64][6] = {{0}};
     if (device < 0 || device >= 64 || !attr_set[device][fi]) {
         cudaError_t e = cudaFuncSetAttribute(k_mma<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_mma)");
@@ -608,6 +688,9 @@ int launch_mma(const MmaArgs& in, int device, int sm_count, cudaStream_t st) {
     switch (a.a0.L.fmt) {
         case F_IQ2_S: return launch_mma_f<F_IQ2_S>(a, device, sm_count, st);
         case F_IQ3_S: return launch_mma_f<F_IQ3_S>(a, device, sm_count, st);
+        case F_IQ2_XXS: return launch_mma_f<F_IQ2_XXS>(a, device, sm_count, st);
+        case F_IQ3_XXS: return launch_mma_f<F_IQ3_XXS>(a, device, sm_count, st);
+        case F_IQ4_XS: return launch_mma_f<F_IQ4_XS>(a, device, sm_count, st);
         default: return launch_mma_f<F_Q4_K>(a, device, sm_count, st);
     }
 }

@@ -52,3 +52,22 @@ def test_product_does_not_import_the_oracle():
             if f.endswith((".py", ".cu", ".cuh", ".h")):
                 src = open(os.path.join(dirpath, f)).read()
                 assert "import oracle" not in src and "from oracle" not in src and "cw_oracle" not in src, f
+
+
+@pytest.mark.parametrize("fmt", [22, 21, 16, 18, 23])  # IQ2_S, IQ3_S, IQ2_XXS, IQ3_XXS, IQ4_XS
+def test_iq_banks_need_whole_16_row_groups(fmt):
+    # the IQ formats are stored in 16-row groups; other row counts are refused before any device
+    # call (so this runs without a GPU)
+    import ctypes
+
+    import numpy as np
+
+    from coachwhip_b200 import _lib
+
+    blk = {22: 82, 21: 110, 16: 66, 18: 98, 23: 136}[fmt]
+    n, k = 40, 256
+    data = np.zeros(n * blk, dtype=np.uint8)
+    d = _lib.MatrixDesc(fmt, n, k, 1, n * blk, data.ctypes.data)
+    h = ctypes.c_void_p()
+    assert _lib.lib().cwx_bank_create(0, ctypes.byref(d), ctypes.byref(h)) == _lib.EUNSUPPORTED
+    assert b"multiple of 16 rows" in _lib.lib().cwx_last_error()

@@ -1,7 +1,8 @@
 """Tensor-core (tcgen05) expert products of large piles against the CPU oracle.
 
-Layers whose routed banks are IQ2_S / IQ3_S take these products once the batch gives enough picks
-per expert; here the threshold is dropped to 1 so every case below takes them. Same bar as the
+Layers whose routed banks are codebook IQ formats (IQ2_S, IQ3_S, IQ2_XXS, IQ3_XXS) take these
+products once the batch gives enough picks per expert; here the threshold is dropped to 1 so every
+case below takes them. Same bar as the
 grouped mma.sync products: MoE output within relative L2 1e-3 of the oracle with the same
 activation semantics, expert ids and piles bit-exact.
 """
@@ -32,6 +33,14 @@ SPECS = {
     # config-4 family: IQ3_S gate/up, Q4_K down (tensor cores under the f32 policy only)
     "iq3_q4k": Spec(hidden=512, n_experts=64, top_k=10, inter=256, gate_type=O.IQ3_S, up_type=O.IQ3_S,
                     down_type=O.Q4_K, shared_inter=256, seed=5),
+    # the reference file's formats: IQ2_XXS gate/up, IQ3_XXS down; IQ4_XS shared expert (grouped
+    # mma.sync products beside the tensor-core ones)
+    "iq_xxs": Spec(hidden=512, n_experts=32, top_k=8, inter=256, gate_type=O.IQ2_XXS, up_type=O.IQ2_XXS,
+                   down_type=O.IQ3_XXS, shared_inter=256, sh_types=(O.IQ4_XS, O.IQ4_XS, O.IQ4_XS), seed=8),
+    # IQ3_XXS gate/up, IQ2_XXS down, shared expert of the same formats on the tensor cores
+    "iq3xxs_iq2xxs": Spec(hidden=768, n_experts=16, top_k=4, inter=512, gate_type=O.IQ3_XXS, up_type=O.IQ3_XXS,
+                          down_type=O.IQ2_XXS, shared_inter=512, sh_types=(O.IQ3_XXS, O.IQ3_XXS, O.IQ2_XXS),
+                          seed=10),
 }
 
 
@@ -57,7 +66,7 @@ def _launches():
 
 
 @pytest.mark.parametrize("name,T", [("iq_mix", 256), ("iq_mix", 1500), ("iq3_iq2", 700), ("iq_wide", 1500),
-                                    ("iq3_q4k", 512)])
+                                    ("iq3_q4k", 512), ("iq_xxs", 300), ("iq_xxs", 1500), ("iq3xxs_iq2xxs", 900)])
 @pytest.mark.parametrize("mode", [O.MODE_CANDLE, O.MODE_F32])
 def test_mma_forward_matches_oracle(name, T, mode):
     from coachwhip_b200 import _lib
