@@ -24,7 +24,7 @@ EXPORTS = [
     "cwx_ctx_set_mma_min_pile", "cwx_ep_dispatch", "cwx_ep_experts", "cwx_ep_combine", "cwx_bank_synth_experts",
     "cwx_ep_rows_f16", "cwx_ctx_check_wait", "cwx_gguf_open", "cwx_gguf_close", "cwx_gguf_info",
     "cwx_gguf_tensor_info", "cwx_gguf_tensor", "cwx_bank_from_gguf", "cwx_gguf_tensor_f32", "cwx_gguf_meta_int",
-    "cwx_gguf_meta_f64", "cwx_gguf_meta_str",
+    "cwx_gguf_meta_f64", "cwx_gguf_meta_str", "cwx_add_rms_norm",
 ]
 PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine"]
 
@@ -60,7 +60,8 @@ class EpGroup(ctypes.Structure):
 class MoeArgs(ctypes.Structure):
     _fields_ = [("x", ctypes.c_void_p), ("tokens", ctypes.c_int32), ("out", ctypes.c_void_p),
                 ("residual", ctypes.c_void_p), ("ids_out", ctypes.c_void_p), ("weights_out", ctypes.c_void_p),
-                ("pairs_out", ctypes.c_void_p), ("heads_out", ctypes.c_void_p)]
+                ("pairs_out", ctypes.c_void_p), ("heads_out", ctypes.c_void_p),
+                ("norm_w", ctypes.c_void_p), ("norm_eps", ctypes.c_float), ("norm_out", ctypes.c_void_p)]
 
 
 _lib = None
@@ -101,6 +102,7 @@ def lib() -> ctypes.CDLL:
             "cwx_permute_noalloc": (I32, [P, I32, I32, I32, P, P, P, P]),
             "cwx_expert_matmul": (I32, [P, P, P, I32, P, I32, I32, I32, P, P]),
             "cwx_moe_forward": (I32, [P, ctypes.POINTER(MoeLayer), ctypes.POINTER(MoeArgs), P]),
+            "cwx_add_rms_norm": (I32, [P, P, P, P, F, I64, I32, P, P, P]),
             "cwx_ctx_set_profiling": (I32, [P, I32]),
             "cwx_ctx_read_profile": (I32, [P, P, P]),
             "cwx_ctx_reset_profile": (I32, [P]),

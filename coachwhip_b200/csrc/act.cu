@@ -28,6 +28,7 @@ struct PrepPair {
     PrepArgs p[2];
 };
 __global__ void __launch_bounds__(256) k_prep(PrepPair pp) {
+    pdl_wait();
     const PrepArgs& p = pp.p[blockIdx.y];
     const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -148,6 +149,7 @@ __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ rows,
                                                  const float* __restrict__ w, int T, int K, int H,
                                                  const float* __restrict__ shared, const float* __restrict__ sgate,
                                                  const float* __restrict__ residual, float* __restrict__ out) {
+    pdl_wait();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)T * H) return;
     const int64_t t = i / H, c = i % H;
@@ -166,6 +168,7 @@ __global__ void __launch_bounds__(256) k_combine4(const float* __restrict__ rows
                                                   const float* __restrict__ w, int T, int K, int H,
                                                   const float* __restrict__ shared, const float* __restrict__ sgate,
                                                   const float* __restrict__ residual, float* __restrict__ out) {
+    pdl_wait();
     const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (i >= (int64_t)T * H) return;
     const int64_t t = i / H, c = i % H;
@@ -197,6 +200,174 @@ __global__ void __launch_bounds__(256) k_combine4(const float* __restrict__ rows
     *reinterpret_cast<float4*>(out + i) = acc;
 }
 
+// ---------------------------------------------------------------- residual add + RMSNorm
+// add_norm (crates/engine/src/fuse_kernel.rs:433-471): sum = a + b (+ c), out = rms_norm(sum) *
+// alpha, candle's RmsNorm v / sqrt(mean(v^2) + eps) * alpha. One block per row; thread t owns the
+// quads (4 consecutive columns) t, t + 256, ... in both passes, whether the row is read as float4
+// or as scalars, so the result does not depend on the pointers' alignment. The squares are exact
+// in f64 and summed in f64 in a fixed order (the thread's quads in order, an xor-shuffle tree,
+// the warps in order), then rounded once: at least as accurate as the reference's f32 sums (a
+// left-to-right sum on the CPU, a tree in the Metal kernel), so the outputs agree with either to
+// the rounding of the reference's own sum. sqrt and the divide are correctly rounded, as in Rust.
+constexpr int NORM_THREADS = 256;
+
+__device__ __forceinline__ double norm_block_sum(double v, double* red) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    double s = red[0];
+#pragma unroll
+    for (int w = 1; w < NORM_THREADS / 32; ++w) s += red[w];
+    return s;
+}
+
+__device__ __forceinline__ double sq4(float4 v) {
+    double s = (double)v.x * (double)v.x;
+    s += (double)v.y * (double)v.y;
+    s += (double)v.z * (double)v.z;
+    s += (double)v.w * (double)v.w;
+    return s;
+}
+
+// Second pass over a summed row (this thread's own writes): out = v / m * alpha.
+__device__ __forceinline__ void norm_row(double ss, const float* __restrict__ sum, const float* __restrict__ alpha,
+                                         float eps, int H, bool vec, float* __restrict__ out) {
+    __shared__ double red[NORM_THREADS / 32];
+    const double tot = norm_block_sum(ss, red);
+    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn((float)tot, (float)H), eps));
+    const int nq = (H + 3) / 4;
+    for (int q = threadIdx.x; q < nq; q += NORM_THREADS) {
+        if (vec) {
+            const float4 v = *reinterpret_cast<const float4*>(sum + 4 * q);
+            const float4 al = __ldg(reinterpret_cast<const float4*>(alpha) + q);
+            float4 r;
+            r.x = __fmul_rn(__fdiv_rn(v.x, m), al.x);
+            r.y = __fmul_rn(__fdiv_rn(v.y, m), al.y);
+            r.z = __fmul_rn(__fdiv_rn(v.z, m), al.z);
+            r.w = __fmul_rn(__fdiv_rn(v.w, m), al.w);
+            *reinterpret_cast<float4*>(out + 4 * q) = r;
+        } else {
+            for (int j = 0; j < 4 && 4 * q + j < H; ++j)
+                out[4 * q + j] = __fmul_rn(__fdiv_rn(sum[4 * q + j], m), __ldg(alpha + 4 * q + j));
+        }
+    }
+}
+
+// (a, b or c may be the sum buffer itself: each element is read before the same thread writes it)
+__global__ void __launch_bounds__(NORM_THREADS) k_add_norm(const float* a, const float* b, const float* c,
+                                                          const float* __restrict__ alpha, float eps, int H, int vec,
+                                                          float* sum, float* out) {
+    pdl_wait();
+    const int64_t o = (int64_t)blockIdx.x * H;
+    const int nq = (H + 3) / 4;
+    double ss = 0.0;
+    for (int q = threadIdx.x; q < nq; q += NORM_THREADS) {
+        const int64_t i = o + 4 * q;
+        if (vec) {
+            const float4 va = *reinterpret_cast<const float4*>(a + i), vb = *reinterpret_cast<const float4*>(b + i);
+            float4 v = make_float4(__fadd_rn(va.x, vb.x), __fadd_rn(va.y, vb.y), __fadd_rn(va.z, vb.z), __fadd_rn(va.w, vb.w));
+            if (c) {
+                const float4 vc = *reinterpret_cast<const float4*>(c + i);
+                v = make_float4(__fadd_rn(v.x, vc.x), __fadd_rn(v.y, vc.y), __fadd_rn(v.z, vc.z), __fadd_rn(v.w, vc.w));
+            }
+            *reinterpret_cast<float4*>(sum + i) = v;
+            ss += sq4(v);
+        } else {
+            for (int j = 0; j < 4 && 4 * q + j < H; ++j) {
+                float v = __fadd_rn(a[i + j], b[i + j]);
+                if (c) v = __fadd_rn(v, c[i + j]);
+                sum[i + j] = v;
+                ss += (double)v * (double)v;
+            }
+        }
+    }
+    norm_row(ss, sum + o, alpha, eps, H, vec, out + o);
+}
+
+// The combine of k_combine / k_combine4 (the same operations in the same order, so `out` is the
+// same bits) with the next layer's RMSNorm of the row fused after it: one block per token.
+__global__ void __launch_bounds__(NORM_THREADS) k_combine_norm(const float* __restrict__ rows,
+                                                              const uint32_t* __restrict__ idx,
+                                                              const float* __restrict__ w, int K, int H,
+                                                              const float* __restrict__ shared,
+                                                              const float* __restrict__ sgate,
+                                                              const float* __restrict__ residual,
+                                                              const float* __restrict__ alpha, float eps, int vec,
+                                                              float* out, float* __restrict__ norm_out) {
+    pdl_wait();
+    const int64_t t = blockIdx.x, o = t * H;
+    const int nq = (H + 3) / 4;
+    const float g = shared ? sgate[t] : 0.f;
+    double ss = 0.0;
+    for (int q = threadIdx.x; q < nq; q += NORM_THREADS) {
+        const int c = 4 * q;
+        if (vec) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int j = 0; j < K; ++j) {
+                const int64_t p = t * K + j, r = idx ? (int64_t)idx[p] : p;
+                const float4 v = *reinterpret_cast<const float4*>(rows + r * H + c);
+                const float wj = w[p];
+                acc.x = __fadd_rn(acc.x, __fmul_rn(v.x, wj));
+                acc.y = __fadd_rn(acc.y, __fmul_rn(v.y, wj));
+                acc.z = __fadd_rn(acc.z, __fmul_rn(v.z, wj));
+                acc.w = __fadd_rn(acc.w, __fmul_rn(v.w, wj));
+            }
+            if (shared) {
+                const float4 v = *reinterpret_cast<const float4*>(shared + o + c);
+                acc.x = __fadd_rn(acc.x, __fmul_rn(v.x, g));
+                acc.y = __fadd_rn(acc.y, __fmul_rn(v.y, g));
+                acc.z = __fadd_rn(acc.z, __fmul_rn(v.z, g));
+                acc.w = __fadd_rn(acc.w, __fmul_rn(v.w, g));
+            }
+            if (residual) {
+                const float4 v = *reinterpret_cast<const float4*>(residual + o + c);
+                acc.x = __fadd_rn(acc.x, v.x);
+                acc.y = __fadd_rn(acc.y, v.y);
+                acc.z = __fadd_rn(acc.z, v.z);
+                acc.w = __fadd_rn(acc.w, v.w);
+            }
+            *reinterpret_cast<float4*>(out + o + c) = acc;
+            ss += sq4(acc);
+        } else {
+            for (int jc = c; jc < c + 4 && jc < H; ++jc) {
+                float acc = 0.f;
+                for (int j = 0; j < K; ++j) {
+                    const int64_t p = t * K + j, r = idx ? (int64_t)idx[p] : p;
+                    acc = __fadd_rn(acc, __fmul_rn(rows[r * H + jc], w[p]));
+                }
+                if (shared) acc = __fadd_rn(acc, __fmul_rn(shared[o + jc], g));
+                if (residual) acc = __fadd_rn(acc, residual[o + jc]);
+                out[o + jc] = acc;
+                ss += (double)acc * (double)acc;
+            }
+        }
+    }
+    norm_row(ss, out + o, alpha, eps, H, vec, norm_out + o);
+}
+
+static bool al16(const void* p) { return !((uintptr_t)p & 15); }
+
+int launch_add_norm(const float* a, const float* b, const float* c, const float* alpha, float eps, int64_t rows,
+                    int H, float* sum, float* out, cudaStream_t st) {
+    if (rows == 0) return CWX_OK;
+    const int vec = H % 4 == 0 && al16(a) && al16(b) && (!c || al16(c)) && al16(alpha) && al16(sum) && al16(out);
+    cudaError_t e = launch_pdl(k_add_norm, dim3((unsigned)rows), dim3(NORM_THREADS), 0, st, a, b, c, alpha, eps, H, vec,
+                               sum, out);
+    return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_add_norm");
+}
+
+int launch_combine_norm(const float* rows, const float* w, int T, int K, int H, const float* shared,
+                        const float* sgate, const float* residual, const float* alpha, float eps, float* out,
+                        float* norm_out, cudaStream_t st, const uint32_t* idx) {
+    if (T == 0) return CWX_OK;
+    const int vec = H % 4 == 0 && al16(rows) && al16(out) && (!shared || al16(shared)) &&
+                    (!residual || al16(residual)) && al16(alpha) && al16(norm_out);
+    cudaError_t e = launch_pdl(k_combine_norm, dim3((unsigned)T), dim3(NORM_THREADS), 0, st, rows, idx, w, K, H, shared,
+                               sgate, residual, alpha, eps, vec, out, norm_out);
+    return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_combine_norm");
+}
+
 int launch_prep2(const PrepArgs* p, int njobs, cudaStream_t st) {
     PrepPair pp;
     int64_t warps = 0;
@@ -208,8 +379,7 @@ int launch_prep2(const PrepArgs* p, int njobs, cudaStream_t st) {
         if (wj > warps) warps = wj;
     }
     if (nj == 0) return CWX_OK;
-    k_prep<<<dim3((unsigned)((warps * 32 + 255) / 256), nj), 256, 0, st>>>(pp);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(k_prep, dim3((unsigned)((warps * 32 + 255) / 256), nj), dim3(256), 0, st, pp);
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_prep");
 }
 
@@ -220,12 +390,10 @@ int launch_combine(const float* rows, const float* w, int T, int K, int H, const
     if (T == 0) return CWX_OK;
     const int64_t n = (int64_t)T * H;
     const bool vec = H % 4 == 0 && !(((uintptr_t)rows | (uintptr_t)out | (uintptr_t)shared | (uintptr_t)residual) & 15);
-    if (vec)
-        k_combine4<<<(unsigned)((n / 4 + 255) / 256), 256, 0, st>>>(rows, idx, w, T, K, H, shared, sgate, residual,
-                                                                    out);
-    else
-        k_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rows, idx, w, T, K, H, shared, sgate, residual, out);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = vec ? launch_pdl(k_combine4, dim3((unsigned)((n / 4 + 255) / 256)), dim3(256), 0, st, rows, idx, w, T,
+                                     K, H, shared, sgate, residual, out)
+                        : launch_pdl(k_combine, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, rows, idx, w, T, K, H,
+                                     shared, sgate, residual, out);
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_combine");
 }
 

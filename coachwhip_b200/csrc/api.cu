@@ -733,6 +733,8 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
     if (T < 0) return fail(CWX_EINVAL, "cwx_moe_forward: tokens %d", T);
     if (T == 0) return CWX_OK;
     if (!A->x || !A->out) return fail(CWX_EINVAL, "cwx_moe_forward: null x or out");
+    if (A->norm_w && (!A->norm_out || A->norm_out == A->out || A->norm_out == A->x || A->norm_out == A->residual))
+        return fail(CWX_EINVAL, "cwx_moe_forward: norm_w needs a norm_out buffer of its own");
     CWX_CUDA(cudaSetDevice(c->device));
     cudaStream_t st = (cudaStream_t)stream;
     LayerPlan p;
@@ -779,8 +781,12 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
     }
     {
         PhaseTimer t(c, st, CWX_PHASE_COMBINE);
-        if ((rc = launch_combine(p.y, p.w, T, K, H, shared ? p.ys : nullptr, p.sgate, A->residual, A->out, st)))
-            return rc;
+        if (A->norm_w)
+            rc = launch_combine_norm(p.y, p.w, T, K, H, shared ? p.ys : nullptr, p.sgate, A->residual, A->norm_w,
+                                     A->norm_eps, A->out, A->norm_out, st);
+        else
+            rc = launch_combine(p.y, p.w, T, K, H, shared ? p.ys : nullptr, p.sgate, A->residual, A->out, st);
+        if (rc) return rc;
         t.end();
     }
     c->launches += 1;
@@ -790,6 +796,16 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
     if (A->pairs_out) CWX_CUDA(cudaMemcpyAsync(A->pairs_out, p.pairs, n * 4, cudaMemcpyDeviceToDevice, st));
     if (A->heads_out) CWX_CUDA(cudaMemcpyAsync(A->heads_out, p.heads, (size_t)3 * E * 4, cudaMemcpyDeviceToDevice, st));
     return CWX_OK;
+}
+
+extern "C" int cwx_add_rms_norm(const float* a, const float* b, const float* c, const float* alpha, float eps,
+                                int64_t rows, int32_t hidden, float* sum, float* out, void* stream) {
+    if (!a || !b || !alpha || !sum || !out) return fail(CWX_EINVAL, "cwx_add_rms_norm: null argument");
+    if (rows < 0 || hidden <= 0 || rows > INT32_MAX)
+        return fail(CWX_EINVAL, "cwx_add_rms_norm: rows %lld, hidden %d", (long long)rows, hidden);
+    if (out == a || out == b || (c && out == c) || out == sum)
+        return fail(CWX_EINVAL, "cwx_add_rms_norm: out must be a buffer of its own");
+    return launch_add_norm(a, b, c, alpha, eps, rows, hidden, sum, out, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------- expert parallelism

@@ -241,6 +241,34 @@ __device__ inline void dev_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// The layer's kernels run back to back on one stream; each is launched with programmatic stream
+// serialisation (launch_pdl), so its launch is processed, and its blocks scheduled as the blocks
+// of the kernel before exit, without the gap of a full grid-to-grid dependency. Every such kernel
+// calls pdl_wait() before it reads anything an earlier kernel wrote or writes anything an earlier
+// kernel reads (the wait returns once the preceding grid has completed and its writes are
+// visible; in a kernel launched without the attribute it returns at once). Work before the wait
+// touches only shared memory, kernel parameters and tables that no kernel writes. No kernel
+// signals its dependents early (griddepcontrol.launch_dependents): dependents parked on the SMs
+// beside a running grid measured 9 % slower prefill layers and no faster decode.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ---------------------------------------------------------------- PTX helpers
 __device__ inline uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

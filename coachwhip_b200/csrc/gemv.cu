@@ -803,6 +803,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
         // each producer has several step-times to issue one step
         const int pw = warp - NCW;
         PRing* ring = reinterpret_cast<PRing*>(smem + BAR_BYTES + Tbl<FMT>::BYTES + RED_FLOATS * 4) + pw;
+        pdl_wait();  // the piles and activation rows of the kernels before
         const uint32_t n_used = *a.n_used;
         int s = 0;        // slot of step q (q mod nst in both rings)
         uint32_t ph = 0;  // parity of the current round of the rings
@@ -886,9 +887,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
     // ---------------- consumers
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(CONS_REGS));
     if (FMT != 0) {
-        build_tables<FMT>(tbl, tid);
+        build_tables<FMT>(tbl, tid);  // (static tables only: runs while the kernel before ends)
         asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
     }
+    pdl_wait();  // before the first write of an output row an earlier kernel may still read
     const uint8_t* tl = tbl + tbl_lane(FMT, lane);
     const int mt = warp % C::MT, ks = warp / C::MT;
     const int g = lane >> 2, c4 = lane & 3;
@@ -1093,8 +1095,7 @@ static int launch_fk(const GemvArgs& a, int64_t items, int smem, int device, int
     int64_t grid = sm_count;
     if (grid > items) grid = items;
     if (grid < 1) return CWX_OK;
-    k_gemv<FMT, KS, NT><<<(unsigned)grid, GEMV_THREADS, smem, st>>>(a);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(k_gemv<FMT, KS, NT>, dim3((unsigned)grid), dim3(GEMV_THREADS), smem, st, a);
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_gemv");
 }
 

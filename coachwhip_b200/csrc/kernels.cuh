@@ -77,6 +77,13 @@ int launch_prep(const PrepArgs& p, cudaStream_t st);
 int launch_prep2(const PrepArgs* p, int njobs, cudaStream_t st);  // up to two preparations in one launch
 int launch_combine(const float* rows, const float* w, int T, int K, int H, const float* shared, const float* sgate,
                    const float* residual, float* out, cudaStream_t st, const uint32_t* idx = nullptr);
+// sum = a + b (+ c), out = rms_norm(sum) * alpha per row of H (act.cu).
+int launch_add_norm(const float* a, const float* b, const float* c, const float* alpha, float eps, int64_t rows,
+                    int H, float* sum, float* out, cudaStream_t st);
+// launch_combine's sum into out, then norm_out = rms_norm(out) * alpha per token.
+int launch_combine_norm(const float* rows, const float* w, int T, int K, int H, const float* shared,
+                        const float* sgate, const float* residual, const float* alpha, float eps, float* out,
+                        float* norm_out, cudaStream_t st, const uint32_t* idx = nullptr);
 
 // Expert parallelism (ep.cu): units (token, destination rank) and their pick records.
 struct EpOffsets {  // received records of source s: [pstart[s], pstart[s+1]); its units from ustart[s]

@@ -54,6 +54,7 @@ __device__ __forceinline__ void dmma_8x8x4(double* c, double a, double b) {
 __global__ void __launch_bounds__(256) k_router(const float* __restrict__ x, const float* __restrict__ w,
                                                 const float* __restrict__ bias, int T, int H, int E,
                                                 float* __restrict__ logits) {
+    pdl_wait();
     __shared__ double red[8][64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e0 = blockIdx.x * 8, t0 = blockIdx.y * 8;
@@ -136,6 +137,7 @@ __global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits,
                                                uint32_t* __restrict__ ids, float* __restrict__ wout,
                                                const float* __restrict__ x, const float* __restrict__ g_inp,
                                                int H, float* __restrict__ sgate) {
+    pdl_wait();
     __shared__ float pv[1024];
     __shared__ float wred[8];
     __shared__ float s_sum;
@@ -287,6 +289,7 @@ constexpr int PERM_TILE = 1024;
 
 __global__ void __launch_bounds__(1024) k_perm_count(const uint32_t* __restrict__ ids, int64_t n, int E,
                                                      uint32_t* __restrict__ tile_counts, int* err) {
+    pdl_wait();
     extern __shared__ uint32_t hist[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
     __syncthreads();
@@ -305,6 +308,7 @@ __global__ void __launch_bounds__(1024) k_perm_count(const uint32_t* __restrict_
 __global__ void __launch_bounds__(1024) k_perm_scan(uint32_t* __restrict__ tile_counts, int ntiles, int E,
                                                     uint32_t* __restrict__ heads, uint32_t* __restrict__ used3,
                                                     uint32_t* __restrict__ n_used) {
+    pdl_wait();
     extern __shared__ uint32_t sm[];
     uint32_t* cnt = sm;       // E
     uint32_t* first = sm + E; // E
@@ -388,6 +392,7 @@ __global__ void __launch_bounds__(1024) k_perm_scan(uint32_t* __restrict__ tile_
 __global__ void __launch_bounds__(1024) k_perm_scatter(const uint32_t* __restrict__ ids, int64_t n, int E,
                                                        const uint32_t* __restrict__ tile_base,
                                                        uint32_t* __restrict__ pairs) {
+    pdl_wait();
     extern __shared__ uint32_t base[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) base[e] = tile_base[(int64_t)blockIdx.x * E + e];
     __syncthreads();
@@ -419,6 +424,7 @@ __global__ void __launch_bounds__(1024) k_perm_small(const uint32_t* __restrict_
                                                      uint32_t* __restrict__ pairs, uint32_t* __restrict__ heads,
                                                      uint32_t* __restrict__ used3, uint32_t* __restrict__ n_used,
                                                      int* err) {
+    pdl_wait();
     __shared__ uint32_t sid[PERM_SMALL_N];
     __shared__ uint32_t cnt[1024];
     __shared__ uint32_t wsum[32], wusum[32];
@@ -508,6 +514,7 @@ __device__ __forceinline__ void cp16_zfill(void* dst, const void* src, uint32_t 
 __global__ void __launch_bounds__(256) k_router_tiled(const float* __restrict__ x, const float* __restrict__ w,
                                                       const float* __restrict__ bias, int T, int H, int E,
                                                       float* __restrict__ logits) {
+    pdl_wait();
     __shared__ __align__(16) float ws[2][RT][RPAD];
     __shared__ __align__(16) float xs[2][RT][RPAD];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -577,20 +584,18 @@ int launch_router(const float* x, const float* w, const float* b, int T, int H, 
                   cudaStream_t st) {
     if (T == 0) return CWX_OK;
     if (T >= 1024 && H % 4 == 0) {
-        k_router_tiled<<<dim3((E + RT - 1) / RT, (T + RT - 1) / RT), 256, 0, st>>>(x, w, b, T, H, E, logits);
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e = launch_pdl(k_router_tiled, dim3((E + RT - 1) / RT, (T + RT - 1) / RT), dim3(256), 0, st, x, w,
+                                   b, T, H, E, logits);
         return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_router_tiled");
     }
-    k_router<<<dim3((E + 7) / 8, (T + 7) / 8), 256, 0, st>>>(x, w, b, T, H, E, logits);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(k_router, dim3((E + 7) / 8, (T + 7) / 8), dim3(256), 0, st, x, w, b, T, H, E, logits);
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_router");
 }
 
 int launch_route(const float* logits, int T, int E, int K, int norm, uint32_t* ids, float* w, const float* x,
                  const float* g_inp, int H, float* sgate, cudaStream_t st) {
     if (T == 0) return CWX_OK;
-    k_route<<<T, 256, 0, st>>>(logits, T, E, K, norm, ids, w, x, g_inp, H, sgate);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(k_route, dim3(T), dim3(256), 0, st, logits, T, E, K, norm, ids, w, x, g_inp, H, sgate);
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_route");
 }
 
@@ -604,17 +609,17 @@ size_t perm_scratch_bytes(int64_t n, int E) {
 int launch_permute(const uint32_t* ids, int64_t n, int E, uint32_t* pairs, uint32_t* heads, uint32_t* used3,
                    uint32_t* n_used, uint32_t* scratch, int* err, cudaStream_t st) {
     if (n <= PERM_SMALL_N && E <= 1024) {
-        k_perm_small<<<1, 1024, 0, st>>>(ids, (int)n, E, pairs, heads, used3, n_used, err);
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e = launch_pdl(k_perm_small, dim3(1), dim3(1024), 0, st, ids, (int)n, E, pairs, heads, used3, n_used,
+                                   err);
         return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_perm_small");
     }
     int ntiles = (int)((n + PERM_TILE - 1) / PERM_TILE);
     if (ntiles == 0) ntiles = 1;
     size_t sh = (size_t)E * 4;
-    k_perm_count<<<ntiles, 1024, sh, st>>>(ids, n, E, scratch, err);
-    k_perm_scan<<<1, 1024, 2 * sh, st>>>(scratch, ntiles, E, heads, used3, n_used);
-    k_perm_scatter<<<ntiles, 1024, sh, st>>>(ids, n, E, scratch, pairs);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(k_perm_count, dim3(ntiles), dim3(1024), sh, st, ids, n, E, scratch, err);
+    if (e == cudaSuccess)
+        e = launch_pdl(k_perm_scan, dim3(1), dim3(1024), 2 * sh, st, scratch, ntiles, E, heads, used3, n_used);
+    if (e == cudaSuccess) e = launch_pdl(k_perm_scatter, dim3(ntiles), dim3(1024), sh, st, ids, n, E, scratch, pairs);
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "permute kernels");
 }
 

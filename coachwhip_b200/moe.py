@@ -252,10 +252,56 @@ class StreamedMoe:
         check(_lib.lib().cwx_moe_forward(_lib.ctx(dev), ctypes.byref(self._layer), ctypes.byref(A), _stream(xs.device)))
         return out.reshape(b, s, h).to(dtype)
 
+    def forward_norm(self, xs: torch.Tensor, residual: torch.Tensor | None, norm_w: torch.Tensor,
+                     eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+        """forward() with the reference's residual step fused after the combine (add_norm,
+        crates/engine/src/model_next.rs:1432-1436): returns (out, rms_norm(out) * norm_w), out as
+        forward() gives it (f32), the second the next layer's normalised input."""
+        b, s, h = xs.shape
+        n = b * s
+        if norm_w.dtype != torch.float32 or norm_w.shape != (h,):
+            raise ValueError(f"add_norm: f32 ({h},) norm weight expected, got {norm_w.dtype} {tuple(norm_w.shape)}")
+        x = xs.reshape(n, h).to(torch.float32).contiguous()
+        out = torch.empty((n, h), dtype=torch.float32, device=xs.device)
+        normed = torch.empty((n, h), dtype=torch.float32, device=xs.device)
+        w = norm_w.contiguous()
+        A = _lib.MoeArgs()
+        A.x, A.tokens, A.out = x.data_ptr(), n, out.data_ptr()
+        res = None
+        if residual is not None:
+            res = residual.reshape(n, h).to(torch.float32).contiguous()
+            A.residual = res.data_ptr()
+        A.norm_w, A.norm_eps, A.norm_out = w.data_ptr(), float(eps), normed.data_ptr()
+        check(_lib.lib().cwx_moe_forward(_lib.ctx(_dev_index(xs)), ctypes.byref(self._layer), ctypes.byref(A),
+                                         _stream(xs.device)))
+        return out.reshape(b, s, h), normed.reshape(b, s, h)
+
     def reserve(self, tokens: int) -> None:
         """Size the workspace for `tokens` (before capturing forward() in a CUDA graph)."""
         check(_lib.lib().cwx_ctx_reserve(_lib.ctx(self.gate.device.index or 0), ctypes.byref(self._layer), tokens))
 
 
-__all__ = ["Bank", "route", "piles", "ExpertAct", "MoeMatvec", "ExpertStore", "SharedExpert", "StreamedMoe",
+def add_norm(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor | None, alpha: torch.Tensor,
+             eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """(a + b (+ c), rms_norm(a + b (+ c)) * alpha) in one launch: fuse_kernel::add_norm
+    (crates/engine/src/fuse_kernel.rs:433-471), with the same checks (f32 only, alpha the last
+    dimension's size)."""
+    ts = [a, b, alpha] + ([c] if c is not None else [])
+    if any(t.dtype != torch.float32 for t in ts):
+        raise ValueError("add_norm: f32 only")
+    h = a.shape[-1]
+    if b.shape != a.shape or (c is not None and c.shape != a.shape) or alpha.shape != (h,):
+        raise ValueError(f"add_norm: shapes {tuple(a.shape)}, {tuple(b.shape)}, alpha {tuple(alpha.shape)}")
+    if any(t.device != a.device for t in ts) or a.device.type != "cuda":
+        raise ValueError("add_norm: all tensors on one CUDA device")
+    a, b, alpha = a.contiguous(), b.contiguous(), alpha.contiguous()
+    c = c.contiguous() if c is not None else None
+    s = torch.empty_like(a)
+    o = torch.empty_like(a)
+    check(_lib.lib().cwx_add_rms_norm(a.data_ptr(), b.data_ptr(), _ptr(c), alpha.data_ptr(), float(eps),
+                                      a.numel() // h, h, s.data_ptr(), o.data_ptr(), _stream(a.device)))
+    return s, o
+
+
+__all__ = ["Bank", "route", "piles", "add_norm", "ExpertAct", "MoeMatvec", "ExpertStore", "SharedExpert", "StreamedMoe",
            "CwxError", "row_bytes"]

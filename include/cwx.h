@@ -211,10 +211,27 @@ typedef struct {
     float* weights_out;
     uint32_t* pairs_out;
     uint32_t* heads_out;
+    /* Optional: the next layer's RMSNorm fused after the combine, as the reference's residual
+     * step does with add_norm (crates/engine/src/model_next.rs:1432-1436): with norm_w set,
+     * norm_out (tokens, hidden) = rms_norm(out) * norm_w, norm_w (hidden) f32, norm_out a buffer
+     * of its own. NULL norm_w: no norm (norm_eps and norm_out ignored). */
+    const float* norm_w;
+    float norm_eps;
+    float* norm_out;
 } cwx_moe_args;
 
-/* out = routed experts (weighted) + shared expert * sigmoid(x . sh_gate_inp) (+ residual). */
+/* out = routed experts (weighted) + shared expert * sigmoid(x . sh_gate_inp) (+ residual)
+ * (+ norm_out = rms_norm(out) * norm_w when args->norm_w is set). */
 int cwx_moe_forward(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_moe_args* args, void* stream);
+
+/* add_norm (crates/engine/src/fuse_kernel.rs:433-471): per row of `hidden`, sum = a + b (+ c)
+ * and out = rms_norm(sum) * alpha, rms_norm as candle's RmsNorm (v / sqrt(mean(v^2) + eps)).
+ * a, b, c (NULL for none), sum, out: (rows, hidden) f32 device; alpha (hidden) f32. sum may be
+ * a, b or c (in place); out must be a buffer of its own. The reference's errors ("f32 only",
+ * "metal only") have no analogue here: CWX_EINVAL for null pointers, rows < 0, hidden <= 0 or
+ * out aliasing an input. */
+int cwx_add_rms_norm(const float* a, const float* b, const float* c, const float* alpha, float eps, int64_t rows,
+                     int32_t hidden, float* sum, float* out, void* stream);
 
 /* Expert parallelism (no counterpart in the reference, which runs one device): the experts are
  * split contiguously over `world` ranks, rank r owning experts [r*epr, (r+1)*epr); every rank

@@ -53,6 +53,7 @@ def lib() -> ctypes.CDLL:
             "cwo_permute": (I32, [P, I32, I32, I32, P, P]),
             "cwo_matmul": (I32, [I32, I32, P, I64, I64, I64, U32, P, I32, P]),
             "cwo_moe_forward": (I32, [P, P, I32, I32, P, P, P, P, P]),
+            "cwo_add_rms_norm": (I32, [P, P, P, P, F, I64, I32, P, P]),
             "cwo_set_threads": (None, [I32]),
             "cwo_get_threads": (I32, []),
         }
@@ -213,6 +214,21 @@ def moe_forward(layer: dict, x: np.ndarray, mode: int) -> dict:
     rc = lib().cwo_moe_forward(ctypes.byref(L), _p(x), T, mode, _p(out), _p(routed), _p(shared), _p(ids), _p(w))
     assert rc == 0, rc
     return {"out": out, "routed": routed, "shared": shared, "ids": ids, "w": w}
+
+
+def add_rms_norm(a: np.ndarray, b: np.ndarray, c: np.ndarray | None, alpha: np.ndarray,
+                 eps: float) -> tuple[np.ndarray, np.ndarray]:
+    """(a + b (+ c), rms_norm(a + b (+ c)) * alpha) per row: add_norm with candle's CPU RmsNorm."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    c = None if c is None else np.ascontiguousarray(c, dtype=np.float32)
+    alpha = np.ascontiguousarray(alpha, dtype=np.float32)
+    H = a.shape[-1]
+    rows = a.size // H
+    s = np.empty_like(a)
+    o = np.empty_like(a)
+    assert lib().cwo_add_rms_norm(_p(a), _p(b), _p(c), _p(alpha), float(eps), rows, H, _p(s), _p(o)) == 0
+    return s, o
 
 
 def set_threads(n: int) -> None:

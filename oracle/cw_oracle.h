@@ -100,6 +100,14 @@ typedef struct {
 int cwo_moe_forward(const cwo_moe_layer* L, const float* x, int T, int mode, float* out, float* routed,
                     float* shared, uint32_t* ids, float* w);
 
+// add_norm (crates/engine/src/fuse_kernel.rs:433-471, the residual step of model_next.rs:1432-1436
+// and its unfused form ((routed + shared) + h, then the next layer's RmsNorm)): per row of
+// `hidden`, sum = (a + b) + c (c may be NULL) and out = rms_norm(sum) * alpha with candle-nn's
+// CPU RmsNorm arithmetic: sum2 = sequential f32 sum of v * v, m = sqrt(sum2 / hidden + eps),
+// out = v / m * alpha.
+int cwo_add_rms_norm(const float* a, const float* b, const float* c, const float* alpha, float eps, int64_t rows,
+                     int hidden, float* sum, float* out);
+
 // Threads used by the OpenMP regions (0 = runtime default).
 void cwo_set_threads(int n);
 int cwo_get_threads(void);

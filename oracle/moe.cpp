@@ -279,4 +279,26 @@ int cwo_moe_forward(const cwo_moe_layer* L, const float* x, int T, int mode, flo
     return 0;
 }
 
+// add_norm (fuse_kernel.rs:433-471) with candle-nn's CPU RmsNorm: the sum of squares is a plain
+// left-to-right f32 sum (an iterator sum in the Rust source), then sqrt(sum2 / dim + eps) and
+// v / m * alpha, every operation rounded to f32.
+int cwo_add_rms_norm(const float* a, const float* b, const float* c, const float* alpha, float eps, int64_t rows,
+                     int hidden, float* sum, float* out) {
+    if (!a || !b || !alpha || !sum || !out || rows < 0 || hidden <= 0) return 1;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+        const size_t o = (size_t)r * hidden;
+        float sum2 = 0.0f;
+        for (int i = 0; i < hidden; ++i) {
+            float v = a[o + i] + b[o + i];
+            if (c) v = v + c[o + i];
+            sum[o + i] = v;
+            sum2 = sum2 + v * v;
+        }
+        const float m = sqrtf(sum2 / (float)hidden + eps);
+        for (int i = 0; i < hidden; ++i) out[o + i] = sum[o + i] / m * alpha[i];
+    }
+    return 0;
+}
+
 }  // extern "C"
