@@ -143,6 +143,35 @@ __global__ void __launch_bounds__(256) k_prep(PrepPair pp) {
     *reinterpret_cast<uint4*>(piece + 512 + 16 * ((ss * 2 + q) * 4 + c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
+// acc + sum_j w[t][j] * rows[pick j][c .. c+3] in pick order; the rows of up to 8 picks are
+// loaded before the first add, so their loads are in flight together.
+__device__ __forceinline__ float4 sum_picks4(const float* __restrict__ rows, const uint32_t* __restrict__ idx,
+                                             const float* __restrict__ w, int64_t t, int K, int H, int64_t c,
+                                             float4 acc) {
+    for (int j0 = 0; j0 < K; j0 += 8) {
+        float4 v[8];
+        float wj[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (j0 + u < K) {
+                const int64_t p = t * K + j0 + u, r = idx ? (int64_t)idx[p] : p;
+                v[u] = *reinterpret_cast<const float4*>(rows + r * H + c);
+                wj[u] = w[p];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (j0 + u < K) {
+                acc.x = __fadd_rn(acc.x, __fmul_rn(v[u].x, wj[u]));
+                acc.y = __fadd_rn(acc.y, __fmul_rn(v[u].y, wj[u]));
+                acc.z = __fadd_rn(acc.z, __fmul_rn(v[u].z, wj[u]));
+                acc.w = __fadd_rn(acc.w, __fmul_rn(v[u].w, wj[u]));
+            }
+        }
+    }
+    return acc;
+}
+
 // out[t] = sum_j w[t][j] * rows[t*K + j] (pick order, from 0) + sgate[t] * shared[t] + residual[t]
 // rows are indexed by pick (t*K + j), or through idx (row of pick p = idx[p]) when idx is set.
 __global__ void __launch_bounds__(256) k_combine(const float* __restrict__ rows, const uint32_t* __restrict__ idx,
@@ -172,16 +201,8 @@ __global__ void __launch_bounds__(256) k_combine4(const float* __restrict__ rows
     const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (i >= (int64_t)T * H) return;
     const int64_t t = i / H, c = i % H;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < K; ++j) {
-        const int64_t p = t * K + j, r = idx ? (int64_t)idx[p] : p;
-        const float4 v = *reinterpret_cast<const float4*>(rows + r * H + c);
-        const float wj = w[p];
-        acc.x = __fadd_rn(acc.x, __fmul_rn(v.x, wj));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(v.y, wj));
-        acc.z = __fadd_rn(acc.z, __fmul_rn(v.z, wj));
-        acc.w = __fadd_rn(acc.w, __fmul_rn(v.w, wj));
-    }
+    const float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 acc = sum_picks4(rows, idx, w, t, K, H, c, acc0);
     if (shared) {
         const float4 v = *reinterpret_cast<const float4*>(shared + t * H + c);
         const float g = sgate[t];
@@ -303,16 +324,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_combine_norm(const float* __re
     for (int q = threadIdx.x; q < nq; q += NORM_THREADS) {
         const int c = 4 * q;
         if (vec) {
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int j = 0; j < K; ++j) {
-                const int64_t p = t * K + j, r = idx ? (int64_t)idx[p] : p;
-                const float4 v = *reinterpret_cast<const float4*>(rows + r * H + c);
-                const float wj = w[p];
-                acc.x = __fadd_rn(acc.x, __fmul_rn(v.x, wj));
-                acc.y = __fadd_rn(acc.y, __fmul_rn(v.y, wj));
-                acc.z = __fadd_rn(acc.z, __fmul_rn(v.z, wj));
-                acc.w = __fadd_rn(acc.w, __fmul_rn(v.w, wj));
-            }
+            float4 acc = sum_picks4(rows, idx, w, t, K, H, c, make_float4(0.f, 0.f, 0.f, 0.f));
             if (shared) {
                 const float4 v = *reinterpret_cast<const float4*>(shared + o + c);
                 acc.x = __fadd_rn(acc.x, __fmul_rn(v.x, g));
