@@ -53,6 +53,7 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-prefill", action="store_true")
     p.add_argument("--no-ep", action="store_true")
+    p.add_argument("--no-c3", action="store_true", help="skip the config-3 (MXFP4, gpt-oss shape) runs")
     return p.parse_args()
 
 
@@ -359,6 +360,120 @@ def ep_runs(world, rank, local, a, maxall, barrier):
                          "per layer", "timing": f"CUDA events over {reps} eager passes of the 48 layers, max over ranks"}
 
 
+# config 3: gpt-oss-120b-shaped MoE (MXFP4 experts with per-expert biases, clamped SwiGLU, router
+# bias, top-4 renormalised, no shared expert)
+C3_H, C3_E, C3_K, C3_I, C3_LAYERS, C3_SEED, C3_T = 2880, 128, 4, 2880, 36, 4, 4096
+T_GB, T_UB, T_DB, T_RB = 9, 10, 11, 13
+
+
+def c3_layers(world, rank, local, layers=C3_LAYERS):
+    """This rank's config-3 layers: banks and biases of experts rank*epr .. (rank+1)*epr - 1."""
+    from coachwhip_b200 import TYPE_MXFP4
+    from coachwhip_b200.moe import Bank, ExpertAct
+
+    import torch
+
+    dev = torch.device(f"cuda:{local}")
+    epr = C3_E // world
+    out = []
+    for l in range(layers):
+        st = lambda t: stream(C3_SEED, l, t)  # noqa: E731
+        g = Bank.synth(TYPE_MXFP4, C3_I, C3_H, epr, st(T_GATE), 0.02, local, first=rank * epr)
+        u = Bank.synth(TYPE_MXFP4, C3_I, C3_H, epr, st(T_UP), 0.02, local, first=rank * epr)
+        d = Bank.synth(TYPE_MXFP4, C3_H, C3_I, epr, st(T_DOWN), 0.02, local, first=rank * epr)
+        gb = synth_f32(C3_E * C3_I, st(T_GB), 0.02, dev).view(C3_E, C3_I)[rank * epr:(rank + 1) * epr].contiguous()
+        ub = synth_f32(C3_E * C3_I, st(T_UB), 0.02, dev).view(C3_E, C3_I)[rank * epr:(rank + 1) * epr].contiguous()
+        db = synth_f32(C3_E * C3_H, st(T_DB), 0.02, dev).view(C3_E, C3_H)[rank * epr:(rank + 1) * epr].contiguous()
+        w = synth_f32(C3_E * C3_H, st(T_RW), 0.02, dev).view(C3_E, C3_H)
+        rb = synth_f32(C3_E, st(T_RB), 0.02, dev)
+        out.append(((g, u, d), ExpertAct.ClampedSwiglu(1.702, 7.0, gb, ub, db), w, rb))
+    return out
+
+
+def c3_runs(world, rank, local, a, pk, maxall, barrier):
+    """Config 3: decode batches 1 and 64 and prefill of 4096 tokens on one GPU (36-layer stack as
+    CUDA graphs); on N ranks, the 4096-token prefill expert-parallel (128 / N experts per rank)."""
+    import numpy as np
+    import torch
+
+    from coachwhip_b200 import _lib
+    from coachwhip_b200.moe import ExpertStore, StreamedMoe
+
+    dev = torch.device(f"cuda:{local}")
+    cfg = ("config 3: 36 x MoE(H2880, E128, top4, I2880, MXFP4 gate/up/down with per-expert biases, clamped "
+           "SwiGLU 1.702/7.0, router bias, no shared expert); candle activation policy (Q8_0 codes)")
+    t0 = time.time()
+    layers = c3_layers(world, rank, local)
+    torch.cuda.synchronize(dev)
+    synth_s = time.time() - t0
+    b_exp = 3 * C3_H * C3_I // 32 * 17 + (2 * C3_I + C3_H) * 4  # MXFP4 bytes of one expert + its biases
+    if world > 1:
+        from coachwhip_b200.ep import CudaEngine, ExpertParallelMoe
+
+        mods = []
+        for (banks, act, w, rb) in layers:
+            eng = CudaEngine(w, C3_K, True, act, banks, world, rank, gate_bias=rb)
+            eng._keep = (banks, act, w, rb)
+            mods.append(ExpertParallelMoe(eng))
+        per = C3_T // world
+        x = synth_f32(C3_T * C3_H, stream(C3_SEED + 1, 0, T_IN), 1.0, dev).view(C3_T, C3_H)[rank * per:(rank + 1) * per]
+        x = x.contiguous().view(1, per, C3_H)
+
+        def run():
+            h = x
+            for m in mods:
+                h = m.forward(h, residual=h)
+            return h
+
+        for _ in range(max(1, a.warmup // 2)):
+            run()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 2
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = maxall(e0.elapsed_time(e1) / reps)
+        _lib.status(local)
+        fl = C3_LAYERS * (2 * C3_T * C3_K * 3 * C3_H * C3_I + 2 * C3_T * C3_H * C3_E)
+        return {"config": cfg, "prefill": {"tokens": C3_T, "tokens_per_rank": per, "ranks": world,
+                                           "experts_per_rank": C3_E // world, "ms_per_step": ms,
+                                           "tokens_per_s": C3_T / (ms / 1e3), "tflops": fl / (ms / 1e3) / 1e12,
+                                           "timing": f"CUDA events over {reps} eager passes, max over ranks"},
+                "bank_synthesis_s": synth_s}
+    store = ExpertStore([b for (b, _, _, _) in layers])
+    mods = [StreamedMoe(l, w, C3_K, True, act, store, gate_bias=rb) for l, (_, act, w, rb) in enumerate(layers)]
+    for m in mods:
+        m.reserve(C3_T)
+    res = {"config": cfg, "bank_gb": C3_LAYERS * C3_E * b_exp / 1e9, "bank_synthesis_s": synth_s, "decode": {}}
+    for T in (1, 64):
+        x = synth_f32(T * C3_H, stream(C3_SEED + 1, 0, T_IN), 1.0, dev).view(1, T, C3_H)
+        g, _ = capture(mods, x, dev)
+        ms = time_graph(g, max(5, a.steps // 2), a.warmup, dev)
+        del g
+        us = used_experts(mods, x)
+        eb = sum(us) * b_exp + C3_LAYERS * C3_E * C3_H * 4  # experts read + router weights
+        res["decode"][str(T)] = {"tokens_per_s": T / (ms / 1e3), "ms_per_step": ms,
+                                 "unique_experts_mean": float(np.mean(us)),
+                                 "hbm_gbs_expert_bytes": eb / (ms / 1e3) / 1e9,
+                                 "hbm_frac": eb / (ms / 1e3) / 1e9 / pk["hbm_gbs"]}
+        print(f"[bench] config 3 decode {T}: {ms:.3f} ms/step, {T / (ms / 1e3):.1f} tokens/s", file=sys.stderr,
+              flush=True)
+    x = synth_f32(C3_T * C3_H, stream(C3_SEED + 1, 0, T_IN), 1.0, dev).view(1, C3_T, C3_H)
+    g, _ = capture(mods, x, dev)
+    ms = time_graph(g, 3, max(1, a.warmup // 2), dev)
+    del g
+    fl = C3_LAYERS * (2 * C3_T * C3_K * 3 * C3_H * C3_I + 2 * C3_T * C3_H * C3_E)
+    res["prefill"] = {"tokens": C3_T, "ms_per_step": ms, "tokens_per_s": C3_T / (ms / 1e3),
+                      "tflops": fl / (ms / 1e3) / 1e12,
+                      "path": "grouped mma.sync products (MXFP4 is not a tensor-core (tcgen05) format here)"}
+    print(f"[bench] config 3 prefill {C3_T}: {ms:.3f} ms/step", file=sys.stderr, flush=True)
+    _lib.status(local)
+    return res
+
+
 def layer_flops(T):
     """Multiply-add FLOPs of one config-1 layer on T tokens: routed gate/up/down, shared expert, router."""
     return 2 * T * K * 3 * H * I + 2 * T * 3 * H * I_S + 2 * T * H * E
@@ -552,6 +667,10 @@ def main():
     if world > 1 and not a.no_ep:
         graphs.clear()  # the decode graphs are not replayed again; release before the EP banks
         ep = ep_runs(world, rank, local, a, maxall, barrier)
+    c3 = None
+    if not a.no_c3:
+        graphs.clear()
+        c3 = c3_runs(world, rank, local, a, pk, maxall, barrier)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
@@ -569,7 +688,7 @@ def main():
                 "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
                 "gpu_launches": int(launches_per_step * a.steps),
                 "decode_sweep": {str(b): d for b, d in sweep.items()},
-                "prefill": prefill, "expert_parallel": ep}
+                "prefill": prefill, "expert_parallel": ep, "config3": c3}
         print(json.dumps(line), flush=True)
     graphs.clear()
     if world > 1:

@@ -273,6 +273,7 @@ static GemvJob job(const cwx_bank* b, int shared, const uint8_t* act, int mode, 
     j.ostride = ostride;
     j.split = split;
     j.bias = bias;
+    j.exact = b && b->mx_wide;
     return j;
 }
 

@@ -415,6 +415,46 @@ static int supported_type(int t) {
            t == F_IQ2_XXS || t == F_IQ3_XXS || t == F_IQ4_XS;
 }
 
+// MXFP4 banks: whether any row's whole 256-column piece has block scales e more than 24 apart
+// (one thread per (expert, row, piece); the piece's 8 scale bytes are contiguous in the tiled
+// layout).
+__global__ void k_mx_spread(const uint8_t* __restrict__ d, Layout L, int64_t ne, int* flag) {
+    const int full = L.last_kp_row_bytes == L.kp_row_bytes ? L.n_kp : L.n_kp - 1;
+    const int64_t per_e = L.n * full;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (full <= 0 || i >= ne * per_e) return;
+    const int64_t e = i / per_e, rem = i % per_e, r = rem / full;
+    const int kp = (int)(rem % full);
+    const uint8_t* p = d + e * L.expert_bytes + tiled_offset(L, r / TILE_ROWS, r % TILE_ROWS, kp, 0);
+    int mx = 0, mn = 255;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        mx = max(mx, (int)p[j]);
+        mn = min(mn, (int)p[j]);
+    }
+    if (mx - mn > 24) atomicOr(flag, 1);
+}
+
+// Sets b->mx_wide for an MXFP4 bank whose tiled bytes are on the device.
+static int mx_check(cwx_bank* b, int64_t ne) {
+    b->mx_wide = 0;
+    if (b->L.fmt != F_MXFP4 || ne <= 0) return CWX_OK;
+    int* flag = nullptr;
+    CWX_CUDA(cudaMalloc(&flag, sizeof(int)));
+    cudaError_t e = cudaMemset(flag, 0, sizeof(int));
+    const int64_t items = ne * b->L.n * b->L.n_kp;
+    if (e == cudaSuccess) {
+        k_mx_spread<<<(unsigned)((items + 255) / 256), 256>>>(b->d, b->L, ne, flag);
+        e = cudaGetLastError();
+    }
+    int h = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&h, flag, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(flag);
+    if (e != cudaSuccess) return cuda_fail(e, "MXFP4 scale check");
+    b->mx_wide = h;
+    return CWX_OK;
+}
+
 static int alloc_bank(int device, int type, int64_t n, int64_t k, int64_t ne, cwx_bank** out) {
     if (!out) return fail(CWX_EINVAL, "cwx_bank: null output pointer");
     *out = nullptr;
@@ -478,6 +518,11 @@ extern "C" int cwx_bank_create(int device, const cwx_matrix_desc* desc, cwx_bank
         *out = nullptr;
         return cuda_fail(e, "cwx_bank_create upload");
     }
+    if ((rc = mx_check(b, desc->n_experts))) {
+        cwx_bank_destroy(b);
+        *out = nullptr;
+        return rc;
+    }
     return CWX_OK;
 }
 
@@ -518,6 +563,11 @@ extern "C" int cwx_bank_synth_experts(cwx_ctx* ctx, int32_t type, int64_t n, int
         cwx_bank_destroy(b);
         *out = nullptr;
         return cuda_fail(e, "cwx_bank_synth");
+    }
+    if ((rc = mx_check(b, ne))) {
+        cwx_bank_destroy(b);
+        *out = nullptr;
+        return rc;
     }
     return CWX_OK;
 }

@@ -145,11 +145,22 @@ inline bool make_layout(int fmt, int64_t n, int64_t k, int64_t e, Layout* L) {
 //     d at 1536 + row*2.
 //   IQ4_XS group (16 x 136 = 2176 B): per (row, c4) the 32 nibble bytes (GGUF 8 + 32 c4 ..) at
 //     (row*4 + c4)*32; per row [d | scales_h | scales_l] (GGUF 0 .. 7) at 2048 + row*8.
+//   MXFP4 group (16 x 136 = 2176 B; a piece row is 8 GGUF blocks of 17 bytes, e then 16 nibble
+//     bytes): per (row, c4) the nibble bytes of blocks 2 c4 and 2 c4 + 1 at (row*4 + c4)*32; per
+//     row the 8 scale bytes e at 2048 + row*8.
 // GGUF blocks: IQ2_S = d(2) qs(32) signs(32) qh(8) scales(8); IQ3_S = d(2) qs(64) qh(8) signs(32)
 // scales(4); IQ2_XXS = d(2) 8 x [entries(4) signs/scale(4)]; IQ3_XXS = d(2) entries(64)
 // signs/scale(32); IQ4_XS = d(2) scales_h(2) scales_l(4) qs(128).
 __host__ __device__ inline bool fmt_soa(int fmt) {
-    return fmt == F_IQ2_S || fmt == F_IQ3_S || fmt == F_IQ2_XXS || fmt == F_IQ3_XXS || fmt == F_IQ4_XS;
+    return fmt == F_IQ2_S || fmt == F_IQ3_S || fmt == F_IQ2_XXS || fmt == F_IQ3_XXS || fmt == F_IQ4_XS ||
+           fmt == F_MXFP4;
+}
+
+// Whether a piece whose rows are prb bytes is stored in 16-row groups: every piece of the IQ
+// formats; the whole 256-column pieces of MXFP4 (a row's last piece of 2 to 7 blocks stays row
+// after row).
+__host__ __device__ inline bool soa_piece(int fmt, int64_t prb) {
+    return fmt_soa(fmt) && (fmt != F_MXFP4 || prb == 8 * 17);
 }
 
 // Offset inside a 16-row group of byte b of the GGUF block of row rg (0..15).
@@ -164,6 +175,11 @@ __host__ __device__ inline int soa_offset(int fmt, int rg, int b) {
         if (b < 66) { const int j = b - 2; return (rg * 4 + (j >> 4)) * 16 + (j & 15); }
         const int j = b - 66;
         return 1024 + (rg * 4 + (j >> 3)) * 8 + (j & 7);
+    }
+    if (fmt == F_MXFP4) {
+        const int blk = b / 17, o = b % 17;
+        if (o == 0) return 2048 + rg * 8 + blk;
+        return (rg * 4 + (blk >> 1)) * 32 + (blk & 1) * 16 + (o - 1);
     }
     if (fmt == F_IQ4_XS) {
         if (b < 8) return 2048 + rg * 8 + b;
@@ -189,7 +205,7 @@ __host__ __device__ inline int soa_offset(int fmt, int rg, int b) {
 __host__ __device__ inline int64_t tiled_offset(const Layout& L, int64_t rt, int64_t rr, int kp, int64_t b) {
     const int64_t prb = piece_row_bytes(L, kp);
     const int64_t base = piece_offset(L, rt, kp);
-    if (!fmt_soa(L.fmt)) return base + rr * prb + b;
+    if (!soa_piece(L.fmt, prb)) return base + rr * prb + b;
     return base + (rr / 16) * 16 * prb + soa_offset(L.fmt, (int)(rr % 16), (int)b);
 }
 
@@ -200,6 +216,9 @@ struct cwx_bank {
     cwx::Layout L;
     uint8_t* d;  // tiled bytes, E * expert_bytes
     int64_t bytes_per_expert_gguf;
+    // MXFP4: some row's 256-column piece has block scales more than 2^24 apart, beyond the f16
+    // range of the grouped products' fast path (its launches take the exact path)
+    int mx_wide;
 };
 
 struct cwx_ctx {

@@ -87,6 +87,14 @@ __device__ __forceinline__ uint32_t iq_u32(int fmt, const IqRow& r, int b) {
 template <bool SMEM>
 __device__ __forceinline__ void dec16_iq_exact(int fmt, const IqRow& r, int kofs, float* v, const HTables& t) {
     const int ib = kofs >> 5;
+    if (fmt == F_MXFP4) {  // GGUF block ib of the piece row: e at 17 ib, nibble bytes after it
+        const float dm = e8m0_to_f32_half(iq_byte(fmt, r, 17 * ib));
+        const int8_t kv[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+        const int sh = (kofs & 16) ? 4 : 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __fmul_rn((float)kv[(iq_byte(fmt, r, 17 * ib + 1 + i) >> sh) & 0xF], dm);
+        return;
+    }
     const float d = h2f_bits((uint16_t)(iq_byte(fmt, r, 0) | (iq_byte(fmt, r, 1) << 8)));
     if (fmt == F_IQ2_XXS) {  // 8 bytes per 32 columns: 4 grid entries, then signs and scale
         const uint32_t aux = iq_u32(fmt, r, 2 + 8 * ib + 4);
@@ -229,7 +237,7 @@ __device__ __forceinline__ void dec16_row_exact(int fmt, const uint8_t* b, int k
 template <bool SMEM>
 __device__ __forceinline__ void dec16_exact(int fmt, const uint8_t* piece, int rr, int64_t prb, int kofs, float* v,
                                             const HTables& t) {
-    if (fmt_soa(fmt)) dec16_iq_exact<SMEM>(fmt, iq_row_in(piece, rr, prb), kofs, v, t);
+    if (soa_piece(fmt, prb)) dec16_iq_exact<SMEM>(fmt, iq_row_in(piece, rr, prb), kofs, v, t);
     else dec16_row_exact(fmt, piece + (int64_t)rr * prb, kofs, v);
 }
 

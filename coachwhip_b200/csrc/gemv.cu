@@ -63,14 +63,17 @@ template <int FMT>
 struct Tbl {  // replicated codebook bytes in shared memory (128 bytes per entry)
     static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 128
                                  : FMT == F_IQ3_S ? 512 * 128
-                                 : (FMT == F_IQ2_XXS || FMT == F_IQ3_XXS || FMT == F_IQ4_XS) ? 256 * 128
+                                 : (FMT == F_IQ2_XXS || FMT == F_IQ3_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4)
+                                     ? 256 * 128
                                                                                                : 0;
 };
 // This lane's copy of the table: 8-value codebooks (IQ2_S, IQ2_XXS) keep 8 copies of 16 bytes per
 // entry, 4-value ones (IQ3_S, IQ3_XXS) 16 copies of 8 bytes, the IQ4_XS nibble-pair table (256
 // pairs of levels) 32 copies of 4 bytes.
 __device__ __forceinline__ int tbl_lane(int fmt, int lane) {
-    return (fmt == F_IQ2_S || fmt == F_IQ2_XXS) ? (lane & 7) * 16 : fmt == F_IQ4_XS ? (lane & 31) * 4 : (lane & 15) * 8;
+    return (fmt == F_IQ2_S || fmt == F_IQ2_XXS)    ? (lane & 7) * 16
+           : (fmt == F_IQ4_XS || fmt == F_MXFP4) ? (lane & 31) * 4
+                                                 : (lane & 15) * 8;
 }
 
 template <int KS>
@@ -432,9 +435,38 @@ __device__ __forceinline__ void iq4xs_pairs(const uint4& Q, __half2 sc, int nh, 
     }
 }
 
+// MXFP4 scales of blocks 2 c4 and 2 c4 + 1 of a row (its 8 scale bytes e in the piece): the f16
+// pair (2^(e0 - m), 2^(e1 - m)), m the largest of the 8, and the row's piece scale 2^(m - 128)
+// (e8m0 halved, as the reference's e8m0_to_fp32_half). Code value x 2^(e - m) is exact in f16
+// down to 2^-24 (codes are at most 12). A bank with a piece whose scales span more than 2^24 is
+// marked at creation (cwx_bank::mx_wide) and its launches take the exact path instead.
+__device__ __forceinline__ void mx_scales(uint2 e8, int c4, uint32_t* h, float* d) {
+    uint32_t m = __vmaxu4(e8.x, e8.y);
+    m = __vmaxu4(m, m >> 16);
+    m = __vmaxu4(m, m >> 8);
+    const int em = (int)(m & 0xFFu);
+    const uint32_t w = (c4 < 2 ? e8.x : e8.y) >> (16 * (c4 & 1));
+    uint32_t bits[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int k = (int)((w >> (8 * i)) & 0xFFu) - em;
+        bits[i] = k >= -14 ? (uint32_t)(k + 15) << 10 : k >= -24 ? 1u << (k + 24) : 0u;
+    }
+    *h = bits[0] | (bits[1] << 16);
+    *d = e8m0_to_f32_half((uint8_t)em);
+}
+
 template <int FMT>
 __device__ __forceinline__ void fast_load(const uint8_t* wsl, int mt, int g, int c4, FastIn& in) {
-    if (FMT == F_IQ4_XS) {
+    if (FMT == F_MXFP4) {
+        const uint8_t* grp = wsl + mt * (16 * 136);
+        in.QA = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 32);
+        in.QA2 = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 32 + 16);
+        in.QB = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 32);
+        in.QB2 = *reinterpret_cast<const uint4*>(grp + ((g + 8) * 4 + c4) * 32 + 16);
+        mx_scales(*reinterpret_cast<const uint2*>(grp + 2048 + 8 * g), c4, &in.HA, &in.dA);
+        mx_scales(*reinterpret_cast<const uint2*>(grp + 2048 + 8 * (g + 8)), c4, &in.HB, &in.dB);
+    } else if (FMT == F_IQ4_XS) {
         const uint8_t* grp = wsl + mt * (16 * 136);
         in.QA = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 32);
         in.QA2 = *reinterpret_cast<const uint4*>(grp + (g * 4 + c4) * 32 + 16);
@@ -494,7 +526,7 @@ __device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl
 #pragma unroll
     for (int ss = 0; ss < 4; ++ss) {
         uint32_t pa[8], pb[8];
-        if (FMT == F_IQ4_XS) {
+        if (FMT == F_IQ4_XS || FMT == F_MXFP4) {
             const __half2 sa = ss < 2 ? __low2half2(u2h2(in.HA)) : __high2half2(u2h2(in.HA));
             const __half2 sb = ss < 2 ? __low2half2(u2h2(in.HB)) : __high2half2(u2h2(in.HB));
             iq4xs_pairs(ss < 2 ? in.QA : in.QA2, sa, ss & 1, tl, pa);
@@ -731,6 +763,14 @@ __device__ __forceinline__ void build_tables(uint8_t* tbl, int tid) {
 #pragma unroll
             for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(tbl + e * 128 + c * 16) = q;
         }
+    } else if (FMT == F_MXFP4) {
+        // nibble pair -> pair of e2m1 codes times 2 (the reference's kvalues_mxfp4), signed
+        const int8_t kv[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+        for (int e = tid; e < 256; e += NCW * 32) {
+            const uint32_t q = h22u(__floats2half2_rn((float)kv[e & 15], (float)kv[e >> 4]));
+#pragma unroll
+            for (int c = 0; c < 32; ++c) *reinterpret_cast<uint32_t*>(tbl + e * 128 + c * 4) = q;
+        }
     } else if (FMT == F_IQ4_XS) {
         for (int e = tid; e < 256; e += NCW * 32) {
             const uint32_t q = h22u(__floats2half2_rn((float)cwx_iq4nl(e & 15), (float)cwx_iq4nl(e >> 4)));
@@ -927,7 +967,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
         const uint8_t* wsl = wslots + s * a.wslot_bytes + ks * a.slot_bytes;
         const uint8_t* brow = bslot + brow_off;
         if (!mbar_wait(&full_w[s], ph, a.err)) return;
-        if (FMT != 0 && fmt == FMT && !lo && !qi) {
+        if (FMT != 0 && FMT != F_MXFP4 && fmt == FMT && !lo && !qi) {
             FastIn in;
             if (active) fast_load<FMT>(wsl, mt, g, c4, in);
             __syncwarp();
@@ -938,11 +978,15 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
                 const Layout& L = a.job[jobi].m.L;
                 const DxAt dx{bslot + dx0_off, bslot + dx1_off};
                 // (late release; IQ4_XS weights above 2048 are not exact in f16, so its products
-                // that must carry ~22 bits take the exact path)
-                if (FMT != 0 && L.fmt == FMT && !qi && (FMT != F_IQ4_XS || !lo)) {
+                // that must carry ~22 bits take the exact path; MXFP4 weights are exact, and their
+                // products always take the activations' lo parts too, as Q8_0-rounded activations
+                // are not exact in f16; a row's last MXFP4 piece of fewer than 8 blocks is stored
+                // row after row and takes the exact path)
+                if (FMT != 0 && L.fmt == FMT && !qi && (FMT != F_IQ4_XS || !lo) &&
+                    (FMT != F_MXFP4 || kp + 1 < L.n_kp || L.last_kp_row_bytes == L.kp_row_bytes)) {
                     FastIn in;
                     fast_load<FMT>(wsl, mt, g, c4, in);
-                    fast_compute<FMT, NT>(in, tl, brow, bnt, lo, acc);
+                    fast_compute<FMT, NT>(in, tl, brow, bnt, lo || FMT == F_MXFP4, acc);
                 }
                 else if (L.fmt == F_Q4_K && L.kp_row_bytes == 144) q4k_step<NT>(wsl, mt, g, c4, brow, bnt, lo, qi, dx, acc);
                 else generic_step<NT>(L, kp, wsl, mt, g, c4, brow, bnt, lo, qi, dx, acc);
@@ -1016,12 +1060,14 @@ static int tbl_bytes(int fmt) {
         case F_IQ2_XXS: return Tbl<F_IQ2_XXS>::BYTES;
         case F_IQ3_XXS: return Tbl<F_IQ3_XXS>::BYTES;
         case F_IQ4_XS: return Tbl<F_IQ4_XS>::BYTES;
+        case F_MXFP4: return Tbl<F_MXFP4>::BYTES;
         default: return 0;
     }
 }
 // Routed formats with a fast path in k_gemv.
 static bool fast_fmt(int fmt) {
-    return fmt == F_IQ2_S || fmt == F_IQ3_S || fmt == F_IQ2_XXS || fmt == F_IQ3_XXS || fmt == F_IQ4_XS;
+    return fmt == F_IQ2_S || fmt == F_IQ3_S || fmt == F_IQ2_XXS || fmt == F_IQ3_XXS || fmt == F_IQ4_XS ||
+           fmt == F_MXFP4;
 }
 
 // Stage sizes of a launch with routed format fmt (0: none), ks K-slices and a.tokcap picks per
@@ -1043,7 +1089,7 @@ static int size_stages(GemvArgs& a, int fmt, int ks, int64_t experts_est, int64_
         // which products read the activations' lo halves: the exact path of any format, and
         // split products, unless the rows hold Q8_K codes
         const bool fast = fmt != 0 && L.fmt == fmt, q4 = L.fmt == F_Q4_K && L.kp_row_bytes == 144;
-        if (!jb.qint && (jb.split || !(fast || q4))) hi_only = false;
+        if (!jb.qint && (jb.split || !(fast || q4) || L.fmt == F_MXFP4)) hi_only = false;
     }
     a.slot_bytes = (int)slot;
     *items = 0;
@@ -1072,11 +1118,17 @@ static int size_stages(GemvArgs& a, int fmt, int ks, int64_t experts_est, int64_
 
 template <int FMT, int KS, int NT>
 static int launch_fk(const GemvArgs& a, int64_t items, int smem, int device, int sm_count, cudaStream_t st) {
-    constexpr int fi = FMT == 0 ? 0 : FMT == F_IQ2_S ? 1 : FMT == F_IQ3_S ? 2 : FMT == F_IQ2_XXS ? 3 : FMT == F_IQ3_XXS ? 4 : 5;
+    constexpr int fi = FMT == 0           ? 0
+                       : FMT == F_IQ2_S     ? 1
+                       : FMT == F_IQ3_S     ? 2
+                       : FMT == F_IQ2_XXS   ? 3
+                       : FMT == F_IQ3_XXS   ? 4
+                       : FMT == F_IQ4_XS    ? 5
+                                            : 6;
     constexpr int ki = (KS == 1 ? 0 : KS == 2 ? 1 : KS == 4 ? 2 : 3) + (NT == 2 ? 4 : NT == 4 ? 5 : 0);
     // the register split assumes the launch allocates LAUNCH_REGS per thread (allocation is in
     // steps of 8): a kernel compiled with fewer would make the consumers' increase wait forever
-    static int regs_ok[6][6] = {{0}};
+    static int regs_ok[7][6] = {{0}};
     if (!regs_ok[fi][ki]) {
         cudaFuncAttributes fa;
         cudaError_t e = cudaFuncGetAttributes(&fa, k_gemv<FMT, KS, NT>);
@@ -1086,7 +1138,7 @@ static int launch_fk(const GemvArgs& a, int64_t items, int smem, int device, int
                         fa.numRegs, LAUNCH_REGS);
         regs_ok[fi][ki] = 1;
     }
-    static int attr_set[64][6][6] = {{{0}}};
+    static int attr_set[64][7][6] = {{{0}}};
     if (device < 0 || device >= 64 || attr_set[device][fi][ki] < smem) {
         cudaError_t e = cudaFuncSetAttribute(k_gemv<FMT, KS, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_gemv)");
@@ -1120,6 +1172,7 @@ static int launch_fmt(int fmt, const GemvArgs& a, int ks, int nt, int64_t items,
         case F_IQ2_XXS: return launch_f<F_IQ2_XXS>(a, ks, nt, items, smem, device, sm_count, st);
         case F_IQ3_XXS: return launch_f<F_IQ3_XXS>(a, ks, nt, items, smem, device, sm_count, st);
         case F_IQ4_XS: return launch_f<F_IQ4_XS>(a, ks, nt, items, smem, device, sm_count, st);
+        case F_MXFP4: return launch_f<F_MXFP4>(a, ks, nt, items, smem, device, sm_count, st);
         default: return launch_f<0>(a, ks, nt, items, smem, device, sm_count, st);
     }
 }
@@ -1137,6 +1190,8 @@ int launch_gemv(const GemvArgs& in, int64_t experts_est, int device, int sm_coun
         rows += L.n;
     }
     if (!fast_fmt(fmt)) fmt = 0;
+    for (int j = 0; j < a.njobs; ++j)  // a bank only the exact path reads correctly
+        if (a.job[j].m.L.fmt == fmt && a.job[j].exact) fmt = 0;
     int64_t items = 0;
     int smem = 0;
     // large piles (on average 24 or 10 picks and more): 32 or 16 picks per pass (4 or 2 n-tiles of

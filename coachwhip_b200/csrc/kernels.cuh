@@ -24,6 +24,7 @@ struct GemvJob {
     int qint;           // activation rows hold Q8_K codes (f16 integers) and each piece's f32 scale
     const float* bias;  // (n_experts, n) added to the outputs, or NULL
     int rows;           // rows per work item (set by the launcher)
+    int exact;          // the bank needs the exact path (an MXFP4 bank with cwx_bank::mx_wide)
 };
 
 struct GemvArgs {

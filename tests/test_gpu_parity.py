@@ -185,6 +185,41 @@ def test_expert_matmul_matches_oracle(fmt, mode, rpe):
     assert err < RTOL, err
 
 
+@pytest.mark.parametrize("mode", [O.MODE_CANDLE, O.MODE_F32])
+@pytest.mark.parametrize("spread", [20, 40])
+def test_mxfp4_block_scales_far_apart(mode, spread):
+    # MXFP4 block scales within a row's 256 columns: the grouped products scale each block by
+    # 2^(e - max e) in f16, exact down to f16's smallest subnormal (2^-24); a bank with a piece
+    # whose scales span more than 2^24 is marked when it is made and takes the exact path. Here
+    # block 0 of every row has the largest e and zero codes, the row's other blocks of the first
+    # piece sit 2^-spread below it (20: subnormal f16 scales on the fast path; 40: the exact
+    # path), so the first piece's contribution rests on those blocks alone.
+    from coachwhip_b200.moe import Bank, MoeMatvec
+
+    fmt, E, n, k, T = O.MXFP4, 2, 128, 512, 5
+    q = O.synth_matrix(fmt, O.stream(3, fmt, 9), 0, E, n, k, 0.02).copy()
+    blocks = q.reshape(E, n, k // 32, 17)
+    blocks[:, :, 0, 0] = 140
+    blocks[:, :, 0, 1:] = 0
+    blocks[:, :, 1:8, 0] = 140 - spread
+    b = Bank.from_gguf_bytes(q, fmt, n, k, E)
+    ids = np.array([[i % E] for i in range(T)], dtype=np.uint32)
+    x = O.normal(O.stream(4, fmt, 9), 0, T * k, 1.0).reshape(T, k)
+    out = MoeMatvec(b, 1, False, act_mode=mode)(_t(x), _t(ids.view(np.int32))).cpu().numpy()
+    want = np.stack([O.matmul(fmt, mode, q, n, k, b.bytes_per_expert, int(ids[t, 0]), x[t][None, :])[0]
+                     for t in range(T)])[:, None, :]
+    tol = 1e-5 if mode == O.MODE_F32 else 1e-4  # (Q8_0 activation codes: the oracle's f32 block sums)
+    assert rel_l2(out, want) < tol
+    # the first piece alone: the second piece's blocks zeroed
+    q2 = q.copy()
+    q2.reshape(E, n, k // 32, 17)[:, :, 8:, 1:] = 0
+    b2 = Bank.from_gguf_bytes(q2, fmt, n, k, E)
+    out2 = MoeMatvec(b2, 1, False, act_mode=mode)(_t(x), _t(ids.view(np.int32))).cpu().numpy()
+    want2 = np.stack([O.matmul(fmt, mode, q2, n, k, b2.bytes_per_expert, int(ids[t, 0]), x[t][None, :])[0]
+                      for t in range(T)])[:, None, :]
+    assert np.abs(want2).max() > 0 and rel_l2(out2, want2) < tol
+
+
 def test_expert_matmul_shape_errors():
     from coachwhip_b200.moe import Bank, MoeMatvec
 
