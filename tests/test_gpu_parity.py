@@ -193,15 +193,16 @@ def test_mxfp4_block_scales_far_apart(mode, spread):
     # whose scales span more than 2^24 is marked when it is made and takes the exact path. Here
     # block 0 of every row has the largest e and zero codes, the row's other blocks of the first
     # piece sit 2^-spread below it (20: subnormal f16 scales on the fast path; 40: the exact
-    # path), so the first piece's contribution rests on those blocks alone.
+    # path), so the first piece's contribution rests on those blocks alone. Those blocks keep
+    # e = 120 (weights up to 12 * 2^-8), inside the f16 range every path rounds weights to.
     from coachwhip_b200.moe import Bank, MoeMatvec
 
     fmt, E, n, k, T = O.MXFP4, 2, 128, 512, 5
     q = O.synth_matrix(fmt, O.stream(3, fmt, 9), 0, E, n, k, 0.02).copy()
     blocks = q.reshape(E, n, k // 32, 17)
-    blocks[:, :, 0, 0] = 140
+    blocks[:, :, 0, 0] = 120 + spread
     blocks[:, :, 0, 1:] = 0
-    blocks[:, :, 1:8, 0] = 140 - spread
+    blocks[:, :, 1:8, 0] = 120
     b = Bank.from_gguf_bytes(q, fmt, n, k, E)
     ids = np.array([[i % E] for i in range(T)], dtype=np.uint32)
     x = O.normal(O.stream(4, fmt, 9), 0, T * k, 1.0).reshape(T, k)
