@@ -54,6 +54,7 @@ def parse():
     p.add_argument("--no-prefill", action="store_true")
     p.add_argument("--no-ep", action="store_true")
     p.add_argument("--no-c3", action="store_true", help="skip the config-3 (MXFP4, gpt-oss shape) runs")
+    p.add_argument("--c3-layers", type=int, default=C3_LAYERS, help="config-3 layers (36; fewer for profiling)")
     return p.parse_args()
 
 
@@ -403,9 +404,10 @@ def c3_runs(world, rank, local, a, pk, maxall, barrier):
     cfg = ("config 3: 36 x MoE(H2880, E128, top4, I2880, MXFP4 gate/up/down with per-expert biases, clamped "
            "SwiGLU 1.702/7.0, router bias, no shared expert); candle activation policy (Q8_0 codes)")
     t0 = time.time()
-    layers = c3_layers(world, rank, local)
+    layers = c3_layers(world, rank, local, a.c3_layers)
     torch.cuda.synchronize(dev)
     synth_s = time.time() - t0
+    nl = len(layers)
     b_exp = 3 * C3_H * C3_I // 32 * 17 + (2 * C3_I + C3_H) * 4  # MXFP4 bytes of one expert + its biases
     if world > 1:
         from coachwhip_b200.ep import CudaEngine, ExpertParallelMoe
@@ -437,8 +439,8 @@ def c3_runs(world, rank, local, a, pk, maxall, barrier):
         torch.cuda.synchronize(dev)
         ms = maxall(e0.elapsed_time(e1) / reps)
         _lib.status(local)
-        fl = C3_LAYERS * (2 * C3_T * C3_K * 3 * C3_H * C3_I + 2 * C3_T * C3_H * C3_E)
-        return {"config": cfg, "prefill": {"tokens": C3_T, "tokens_per_rank": per, "ranks": world,
+        fl = nl * (2 * C3_T * C3_K * 3 * C3_H * C3_I + 2 * C3_T * C3_H * C3_E)
+        return {"config": cfg, "layers": nl, "prefill": {"tokens": C3_T, "tokens_per_rank": per, "ranks": world,
                                            "experts_per_rank": C3_E // world, "ms_per_step": ms,
                                            "tokens_per_s": C3_T / (ms / 1e3), "tflops": fl / (ms / 1e3) / 1e12,
                                            "timing": f"CUDA events over {reps} eager passes, max over ranks"},
@@ -447,14 +449,14 @@ def c3_runs(world, rank, local, a, pk, maxall, barrier):
     mods = [StreamedMoe(l, w, C3_K, True, act, store, gate_bias=rb) for l, (_, act, w, rb) in enumerate(layers)]
     for m in mods:
         m.reserve(C3_T)
-    res = {"config": cfg, "bank_gb": C3_LAYERS * C3_E * b_exp / 1e9, "bank_synthesis_s": synth_s, "decode": {}}
+    res = {"config": cfg, "layers": nl, "bank_gb": nl * C3_E * b_exp / 1e9, "bank_synthesis_s": synth_s, "decode": {}}
     for T in (1, 64):
         x = synth_f32(T * C3_H, stream(C3_SEED + 1, 0, T_IN), 1.0, dev).view(1, T, C3_H)
         g, _ = capture(mods, x, dev)
         ms = time_graph(g, max(5, a.steps // 2), a.warmup, dev)
         del g
         us = used_experts(mods, x)
-        eb = sum(us) * b_exp + C3_LAYERS * C3_E * C3_H * 4  # experts read + router weights
+        eb = sum(us) * b_exp + nl * C3_E * C3_H * 4  # experts read + router weights
         res["decode"][str(T)] = {"tokens_per_s": T / (ms / 1e3), "ms_per_step": ms,
                                  "unique_experts_mean": float(np.mean(us)),
                                  "hbm_gbs_expert_bytes": eb / (ms / 1e3) / 1e9,
@@ -465,7 +467,7 @@ def c3_runs(world, rank, local, a, pk, maxall, barrier):
     g, _ = capture(mods, x, dev)
     ms = time_graph(g, 3, max(1, a.warmup // 2), dev)
     del g
-    fl = C3_LAYERS * (2 * C3_T * C3_K * 3 * C3_H * C3_I + 2 * C3_T * C3_H * C3_E)
+    fl = nl * (2 * C3_T * C3_K * 3 * C3_H * C3_I + 2 * C3_T * C3_H * C3_E)
     res["prefill"] = {"tokens": C3_T, "ms_per_step": ms, "tokens_per_s": C3_T / (ms / 1e3),
                       "tflops": fl / (ms / 1e3) / 1e12,
                       "path": "grouped mma.sync products (MXFP4 is not a tensor-core (tcgen05) format here)"}
