@@ -94,7 +94,9 @@ int cwx_ctx_status(cwx_ctx* ctx, void* stream);
  * usable. */
 int cwx_ctx_check_wait(cwx_ctx* ctx, int32_t limit_us, void* stream);
 
-/* Bank: copy a GGUF expert tensor into HBM (replaces ExpertStore::resident_op's exact_load). */
+/* Bank: copy a GGUF expert tensor into HBM (replaces ExpertStore::resident_op's exact_load).
+ * IQ2_S, IQ3_S, IQ2_XXS, IQ3_XXS, IQ4_XS and MXFP4 banks are stored in 16-row groups and need a
+ * multiple of 16 rows (CWX_EUNSUPPORTED otherwise). */
 int cwx_bank_create(int device, const cwx_matrix_desc* desc, cwx_bank** out);
 /* Bank filled on the device with the synthetic N(0, std^2) weights of stream `key`
  * (test and benchmark workloads; same values as the CPU generator). */
