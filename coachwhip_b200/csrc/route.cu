@@ -54,10 +54,19 @@ __device__ __forceinline__ void dmma_8x8x4(double* c, double a, double b) {
 __global__ void __launch_bounds__(256) k_router(const float* __restrict__ x, const float* __restrict__ w,
                                                 const float* __restrict__ bias, int T, int H, int E,
                                                 float* __restrict__ logits) {
-    pdl_wait();
     __shared__ double red[8][64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e0 = blockIdx.x * 8, t0 = blockIdx.y * 8;
+    {
+        // the router rows of this block's experts are weights no kernel writes: the first token
+        // tile asks L2 for them (one 128-byte line per request) before waiting for the kernel
+        // before, so the loop below finds them there
+        const char* wb = reinterpret_cast<const char*>(w + (int64_t)e0 * H);
+        const int64_t bytes = blockIdx.y == 0 ? (int64_t)min(8, E - e0) * H * 4 : 0;
+        for (int64_t o = (int64_t)threadIdx.x * 128; o < bytes; o += 256 * 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(wb + o));
+    }
+    pdl_wait();
     const int r = lane >> 2, kq = lane & 3;
     const int ks = (H + 7) / 8, k0 = warp * ks, k1 = min(H, k0 + ks);
     // A[r][k] = w[e0 + r][k], B[k][n] = x[t0 + n][k]: each lane reads row r at k = 4j + kq
