@@ -15,10 +15,15 @@ roofline: the expert-product kernel (k_gemv), algorithmic bytes (quantised weigh
          the measured HBM copy bandwidth in MEASURED_PEAKS.json.
 cpu_baseline: the CPU restatement of the reference's layer (oracle/, candle semantics) timed on
          the host cores on one full layer of the same bank at the same batch.
+prefill: config 2 (the config-1 layers at 1500 and 4096 tokens, tensor-core products).
+config3: the gpt-oss-shaped stack (36 MXFP4 layers): decode 1 and 64 and prefill of 4096 tokens
+         on one GPU; on N ranks the 4096-token prefill expert-parallel.
+expert_parallel (N > 1): config 4 (48 layers, 512 experts, 8192 tokens) expert-parallel.
 
 usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cwx|reference] [--batch T]
+                       [--no-sweep] [--no-prefill] [--no-ep] [--no-c3] [--no-cpu] [--c3-layers L]
 For N > 1 it runs under torchrun: config 1 does not shard (one process per GPU runs its own
-replica; scaling "weak").
+replica; scaling "weak"); configs 3 and 4 shard their experts over the ranks.
 """
 
 from __future__ import annotations
