@@ -69,9 +69,22 @@ class OracleEngine:
             xr = r[unit[sel]]
             g = O.matmul(L["gate_type"], self.mode, L["gate_bank"], I, H, expert_bytes(L, "gate"), e, xr)
             u = O.matmul(L["up_type"], self.mode, L["up_bank"], I, H, expert_bytes(L, "up"), e, xr)
-            h = (g / (np.float32(1) + np.exp(-g))) * u
+            if L.get("act", O.ACT_SILU) == O.ACT_CLAMPED_SWIGLU:
+                # gpt-oss: biases of expert e, gate clamped above, up clamped both ways
+                lim, alpha = np.float32(L.get("limit", 7.0)), np.float32(L.get("alpha", 1.702))
+                if L.get("gate_b") is not None:
+                    g = g + L["gate_b"][e]
+                if L.get("up_b") is not None:
+                    u = u + L["up_b"][e]
+                g = np.minimum(g, lim)
+                u = np.clip(u, -lim, lim)
+                h = (u + np.float32(1)) * (g / (np.exp(-g * alpha) + np.float32(1)))
+            else:
+                h = (g / (np.float32(1) + np.exp(-g))) * u
             y[sel] = O.matmul(L["down_type"], self.mode, L["down_bank"], H, I, expert_bytes(L, "down"), e,
                               h.astype(np.float32))
+            if L.get("act", O.ACT_SILU) == O.ACT_CLAMPED_SWIGLU and L.get("down_b") is not None:
+                y[sel] = y[sel] + L["down_b"][e]
         yu = np.zeros((r.shape[0], H), dtype=np.float32)
         for p in range(pk.shape[0]):  # each unit's weighted sum in record order
             yu[unit[p]] += wgt[p] * y[p]

@@ -12,10 +12,13 @@ from tests.layers import Spec, build_cpu, make_input, rel_l2
 
 SPEC = Spec(hidden=256, n_experts=8, top_k=2, inter=256, gate_type=O.Q4_K, up_type=O.Q4_K, down_type=O.Q4_K,
             shared_inter=256, seed=11)
+# the gpt-oss layer shape: MXFP4 experts with per-expert biases, clamped SwiGLU, router bias
+SPEC_GPTOSS = Spec(hidden=256, n_experts=8, top_k=4, inter=256, gate_type=O.MXFP4, up_type=O.MXFP4,
+                   down_type=O.MXFP4, act=O.ACT_CLAMPED_SWIGLU, router_bias=True, expert_bias=True, seed=12)
 T = 24
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, spec=SPEC):
     import torch
     import torch.distributed as dist
 
@@ -26,8 +29,8 @@ def _rank(rank, world, port, q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        L = build_cpu(SPEC)
-        x = make_input(SPEC, T)
+        L = build_cpu(spec)
+        x = make_input(spec, T)
         per = T // world
         xl = torch.from_numpy(np.ascontiguousarray(x[rank * per:(rank + 1) * per]))
         moe = ExpertParallelMoe(OracleEngine(L, world, rank, O.MODE_F32))
@@ -38,13 +41,13 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_expert_parallel_protocol_on_two_gloo_ranks():
+@pytest.mark.parametrize("spec,port", [(SPEC, 29611), (SPEC_GPTOSS, 29613)], ids=["qwen", "gptoss"])
+def test_expert_parallel_protocol_on_two_gloo_ranks(spec, port):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29611
-    ps = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, q, spec)) for r in range(2)]
     for p in ps:
         p.start()
     for p in ps:
