@@ -22,6 +22,7 @@ expert_parallel (N > 1): config 4 (48 layers, 512 experts, 8192 tokens) expert-p
 
 usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cwx|reference] [--batch T]
                        [--no-sweep] [--no-prefill] [--no-ep] [--no-c3] [--no-cpu] [--c3-layers L]
+                       [--prefill-tokens T ...]
 For N > 1 it runs under torchrun: config 1 does not shard (one process per GPU runs its own
 replica; scaling "weak"); configs 3 and 4 shard their experts over the ranks.
 """
@@ -60,6 +61,8 @@ def parse():
     p.add_argument("--no-ep", action="store_true")
     p.add_argument("--no-c3", action="store_true", help="skip the config-3 (MXFP4, gpt-oss shape) runs")
     p.add_argument("--c3-layers", type=int, default=C3_LAYERS, help="config-3 layers (36; fewer for profiling)")
+    p.add_argument("--prefill-tokens", type=int, nargs="*", default=None,
+                   help="config-2 prefill sizes (default 1500 4096; one size for profiling)")
     return p.parse_args()
 
 
@@ -557,7 +560,7 @@ def main():
         return float(t.item())
 
     batches = [a.batch] if a.no_sweep else sorted({1, 4, 16, 64, a.batch})
-    prefill_T = [] if a.no_prefill else PREFILL_T
+    prefill_T = [] if a.no_prefill else (a.prefill_tokens or PREFILL_T)
     for m in mods:
         m.reserve(max(batches + prefill_T))  # one workspace for every captured graph
     sweep, graphs = {}, {}
