@@ -31,8 +31,8 @@
 //     of the down products;
 //   plain: A rows are 128 consecutive rows of one matrix; the epilogue writes f32 rows per pick.
 //
-// Roles (18 warps): 0-3 epilogue (TMEM lanes 32w .. 32w+31), 4 MMA issue and TMEM allocation,
-// 5 quantised-piece copies, 6-9 activation gathers, 10-17 decode. Every wait is bounded; a role
+// Roles (22 warps): 0-3 epilogue (TMEM lanes 32w .. 32w+31), 4 MMA issue and TMEM allocation,
+// 5 quantised-piece copies, 6-9 activation gathers, 10-21 decode. Every wait is bounded; a role
 // that gives up records DE_TIMEOUT and leaves its loop, and the CTA still meets at the final
 // barrier, where the TMEM is freed.
 #include "cwx_common.cuh"
