@@ -14,6 +14,7 @@ TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_IQ3_S, TYPE_IQ2_S, TYPE_MXFP4 = 
 TYPE_IQ2_XXS, TYPE_IQ3_XXS, TYPE_IQ4_XS = 16, 18, 23
 ACT_MODE_CANDLE, ACT_MODE_F32 = 0, 1
 ACT_SILU, ACT_CLAMPED_SWIGLU = 0, 1
+NOALLOC_SCRATCH_WORDS = 262144  # CWX_NOALLOC_SCRATCH_WORDS: cwx_permute_noalloc's fixed scratch
 
 # Every entry point include/cwx.h declares.
 EXPORTS = [

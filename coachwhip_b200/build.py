@@ -11,6 +11,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
@@ -40,7 +41,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     headers.append(os.path.join(inc, "cwx.h"))
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
-    objs = []
+    objs, cmds = [], []
     for src in SOURCES:
         path = os.path.join(CSRC, src)
         obj = os.path.join(objdir, os.path.splitext(src)[0] + ".o")
@@ -54,7 +55,13 @@ def build(verbose: bool = False, force: bool = False) -> str:
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
+    # the sources compile independently: one nvcc per source, in parallel (the longest, gemv.cu
+    # with its per-format instantiations, sets the build time)
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as pool:
+        for r in list(pool.map(lambda c: subprocess.run(c, capture_output=not verbose, text=True), cmds)):
+            if r.returncode != 0:
+                raise RuntimeError(f"nvcc failed ({r.returncode}): {' '.join(r.args)}\n{r.stdout or ''}{r.stderr or ''}")
     if force or _stale(LIB, objs):
         subprocess.run([nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"], check=True)
     return LIB

@@ -1,11 +1,12 @@
 // cwx_permute_noalloc: the expert piles of cwx_permute for callers that must not allocate.
 //
 // cwx_permute keeps its scratch (per-tile expert counts, the used-expert list) in the context
-// workspace, which grows on demand with cudaMalloc. Some callers cannot allow that: a caller
-// inside CUDA stream capture (an allocation there fails), a caller with its own memory pool that
-// forbids hidden device allocations, or one without a cwx_ctx. This entry point runs the same
-// three kernels with the scratch in one fixed device array of this library (1 MiB per device),
-// so a call makes no allocation at all: no cudaMalloc, no cudaFree, no allocating library call.
+// workspace, which grows on demand with cudaMalloc. Some callers cannot allow that: an engine
+// that owns all device memory through its own pool and forbids hidden device allocations, a
+// latency-critical loop in which cudaMalloc's implicit device synchronisation is not acceptable,
+// or a caller without a cwx_ctx. This entry point runs the same kernels with the scratch in one
+// fixed device array of this library (1 MiB per device), so a call makes no allocation at all:
+// no cudaMalloc, no cudaFree, no allocating library call.
 //
 // Limits and rules:
 //   - scratch words needed = ceil(tokens*top_k / 1024) * n_experts + 3 * n_experts + 8 must be
@@ -25,7 +26,8 @@
 
 namespace cwx {
 
-constexpr size_t NOALLOC_WORDS = 262144;  // 1 MiB of uint32 per device
+constexpr size_t NOALLOC_WORDS = CWX_NOALLOC_SCRATCH_WORDS;  // 1 MiB of uint32 per device
+static_assert(NOALLOC_WORDS == 262144, "the header documents a 1 MiB scratch array");
 constexpr int NOALLOC_MAX_EXPERTS = 4096;
 
 static __device__ __align__(256) uint32_t g_noalloc_scratch[NOALLOC_WORDS];

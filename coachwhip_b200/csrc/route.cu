@@ -625,6 +625,12 @@ int launch_permute(const uint32_t* ids, int64_t n, int E, uint32_t* pairs, uint3
     int ntiles = (int)((n + PERM_TILE - 1) / PERM_TILE);
     if (ntiles == 0) ntiles = 1;
     size_t sh = (size_t)E * 4;
+    // the scan keeps two words per expert: above 48 KB (more than 6,144 experts) the kernel must
+    // be opted in to the larger dynamic shared memory (per device; repeated calls are cheap)
+    if (2 * sh > 48 * 1024) {
+        cudaError_t a = cudaFuncSetAttribute(k_perm_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(2 * sh));
+        if (a != cudaSuccess) return cuda_fail(a, "cudaFuncSetAttribute(k_perm_scan)");
+    }
     cudaError_t e = launch_pdl(k_perm_count, dim3(ntiles), dim3(1024), sh, st, ids, n, E, scratch, err);
     if (e == cudaSuccess)
         e = launch_pdl(k_perm_scan, dim3(1), dim3(1024), 2 * sh, st, scratch, ntiles, E, heads, used3, n_used);

@@ -161,8 +161,9 @@ int cwx_permute(cwx_ctx* ctx, const uint32_t* ids, int32_t tokens, int32_t top_k
                 uint32_t* pairs, uint32_t* heads, void* stream);
 
 /* cwx_permute for callers that must not allocate (no counterpart in the reference; it has no
- * such constraint). For code that cannot let a call allocate device memory: inside CUDA stream
- * capture, under a caller-owned memory pool, or without a cwx_ctx. Same pairs and heads as
+ * such constraint). For code that cannot let a call allocate device memory: an engine whose own
+ * pool owns all device memory, a loop that cannot take cudaMalloc's implicit device
+ * synchronisation, or a caller without a cwx_ctx. Same pairs and heads as
  * cwx_permute; the scratch is a fixed 1 MiB device array of this library, so the call makes no
  * allocation. Limits: n_experts <= 4096 and
  * ceil(tokens*top_k / 1024) * n_experts + 3 * n_experts + 8 <= CWX_NOALLOC_SCRATCH_WORDS;

@@ -50,6 +50,7 @@ def lib() -> ctypes.CDLL:
             "cwo_synth_matrix": (I32, [I32, U64, I64, I64, I64, I64, F, P]),
             "cwo_router": (None, [P, P, P, I32, I32, I32, P]),
             "cwo_route": (I32, [P, I32, I32, I32, I32, P, P]),
+            "cwo_router_f32": (I32, [P, P, P, I32, I32, I32, I32, P]),
             "cwo_permute": (I32, [P, I32, I32, I32, P, P]),
             "cwo_matmul": (I32, [I32, I32, P, I64, I64, I64, U32, P, I32, P]),
             "cwo_moe_forward": (I32, [P, P, I32, I32, P, P, P, P, P]),
@@ -128,6 +129,21 @@ def router(x: np.ndarray, w: np.ndarray, b: np.ndarray | None = None) -> np.ndar
     out = np.empty((T, E), dtype=np.float32)
     bb = None if b is None else np.ascontiguousarray(b, dtype=np.float32)
     lib().cwo_router(_p(x), _p(w), _p(bb), T, H, E, _p(out))
+    return out
+
+
+ROUTER_ORDERS = 6  # summation orders of cwo_router_f32
+
+
+def router_f32(x: np.ndarray, w: np.ndarray, b: np.ndarray | None, order: int) -> np.ndarray:
+    """Router logits rounded to f32 at every step, in summation order `order` (see cw_oracle.h)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    T, H = x.shape
+    E = w.shape[0]
+    out = np.empty((T, E), dtype=np.float32)
+    bb = None if b is None else np.ascontiguousarray(b, dtype=np.float32)
+    assert lib().cwo_router_f32(_p(x), _p(w), _p(bb), T, H, E, order, _p(out)) == 0
     return out
 
 

@@ -64,6 +64,13 @@ int cwo_synth_matrix(int type, uint64_t key, int64_t e0, int64_t ne, int64_t n, 
 
 // Router logits (T, E) = x (T, H) . W (E, H)^T (+ b), products exact, f64 accumulation.
 void cwo_router(const float* x, const float* w, const float* b, int T, int H, int E, float* logits);
+// Router logits with every product and sum rounded to f32, in one of the summation orders an f32
+// GEMV may use (the reference computes them with the gemm crate, whose order is not restated):
+//   0 sequential, 1 sequential fused multiply-add, 2 eight strided lanes (AVX2) then a lane tree,
+//   3 sixteen strided lanes (AVX-512) then a lane tree, 4 blocks of 256 columns with eight lanes
+//   each, the block sums added in order (a K-blocked GEMM), 5 pairwise (recursive halves).
+// Used by the routing-margin test, not by the layer oracle.
+int cwo_router_f32(const float* x, const float* w, const float* b, int T, int H, int E, int order, float* logits);
 // route(): softmax over all E, stable descending order, top k, renormalised when norm.
 int cwo_route(const float* logits, int T, int E, int k, int norm, uint32_t* ids, float* w);
 // Expert piles: pairs = flat pick indices i = t*k + j grouped stably by expert,

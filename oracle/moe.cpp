@@ -112,6 +112,75 @@ void cwo_router(const float* x, const float* w, const float* b, int T, int H, in
         }
 }
 
+static float lane_tree(float* a, int n) {  // halves added pairwise until one lane is left
+    for (int w = n / 2; w >= 1; w /= 2)
+        for (int i = 0; i < w; ++i) a[i] = a[i] + a[i + w];
+    return a[0];
+}
+
+static float pairwise_sum(const float* x, const float* w, int n) {
+    if (n <= 8) {
+        float s = 0.0f;
+        for (int i = 0; i < n; ++i) s = s + x[i] * w[i];
+        return s;
+    }
+    const int h = n / 2;
+    return pairwise_sum(x, w, h) + pairwise_sum(x + h, w + h, n - h);
+}
+
+static float dot_f32(const float* x, const float* w, int H, int order) {
+    switch (order) {
+        case 0: {
+            float s = 0.0f;
+            for (int i = 0; i < H; ++i) s = s + x[i] * w[i];
+            return s;
+        }
+        case 1: {
+            float s = 0.0f;
+            for (int i = 0; i < H; ++i) s = fmaf(x[i], w[i], s);
+            return s;
+        }
+        case 2:
+        case 3: {
+            const int L = order == 2 ? 8 : 16;
+            float acc[16] = {0};
+            int i = 0;
+            for (; i + L <= H; i += L)
+                for (int j = 0; j < L; ++j) acc[j] = fmaf(x[i + j], w[i + j], acc[j]);
+            float s = lane_tree(acc, L);
+            for (; i < H; ++i) s = fmaf(x[i], w[i], s);
+            return s;
+        }
+        case 4: {
+            float s = 0.0f;
+            for (int k0 = 0; k0 < H; k0 += 256) {
+                const int k1 = k0 + 256 < H ? k0 + 256 : H;
+                float acc[8] = {0};
+                int i = k0;
+                for (; i + 8 <= k1; i += 8)
+                    for (int j = 0; j < 8; ++j) acc[j] = fmaf(x[i + j], w[i + j], acc[j]);
+                float p = lane_tree(acc, 8);
+                for (; i < k1; ++i) p = fmaf(x[i], w[i], p);
+                s = s + p;
+            }
+            return s;
+        }
+        default:
+            return pairwise_sum(x, w, H);
+    }
+}
+
+int cwo_router_f32(const float* x, const float* w, const float* b, int T, int H, int E, int order, float* logits) {
+    if (order < 0 || order > 5 || T < 0 || H < 1 || E < 1) return -1;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int t = 0; t < T; ++t)
+        for (int e = 0; e < E; ++e) {
+            float l = dot_f32(x + (int64_t)t * H, w + (int64_t)e * H, H, order);
+            logits[(int64_t)t * E + e] = b ? l + b[e] : l;
+        }
+    return 0;
+}
+
 int cwo_route(const float* logits, int T, int E, int k, int norm, uint32_t* ids, float* w) {
     if (k < 1 || k > E) return -1;
     std::vector<float> p((size_t)E);

@@ -139,7 +139,10 @@ def test_route_nan_does_not_fail():
     assert ids.cpu().numpy().max() < 3
 
 
-@pytest.mark.parametrize("T,k,E", [(64, 8, 256), (1, 8, 256), (4096, 8, 256), (8192, 10, 512), (7, 3, 5)])
+# (300, 8, 12288): the largest expert count cwx_permute accepts, on the three-kernel path whose
+# scan holds two words per expert in shared memory (96 KB)
+@pytest.mark.parametrize("T,k,E", [(64, 8, 256), (1, 8, 256), (4096, 8, 256), (8192, 10, 512), (7, 3, 5),
+                                   (300, 8, 12288), (3000, 4, 6200)])
 def test_piles_match_oracle(T, k, E):
     from coachwhip_b200.moe import piles
 
