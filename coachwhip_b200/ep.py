@@ -39,6 +39,7 @@ class Dispatched:
     """What step 1 leaves for step 5 and what it sends."""
 
     x: torch.Tensor           # (T, H) f32 local tokens
+    ids: torch.Tensor | None  # (T, top_k) int32 expert ids of the local tokens (None: not kept)
     unit_of: torch.Tensor     # (T, world) int32: the token's unit in send_rows per rank, or -1
     sgate: torch.Tensor | None
     send_rows: torch.Tensor   # (units, H) f16 or f32, destinations in rank order
@@ -96,7 +97,7 @@ class CudaEngine:
                                          x.data_ptr(), T, ids.data_ptr(), w.data_ptr(), _ptr(sgate),
                                          unit_of.data_ptr(), rows.data_ptr(), picks.data_ptr(), counts.data_ptr(),
                                          _stream(dev)))
-        return Dispatched(x, unit_of, sgate, rows, picks, counts)
+        return Dispatched(x, ids.view(T, self.top_k), unit_of, sgate, rows, picks, counts)
 
     def experts(self, rows: torch.Tensor, picks: torch.Tensor, src_units: list[int],
                 src_picks: list[int]) -> torch.Tensor:
@@ -128,6 +129,11 @@ class ExpertParallelMoe:
 
         self.engine, self.group = engine, group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.timer = None  # optional: .mark(phase) called at the start of each phase (benchmarks)
+
+    def _mark(self, name: str) -> None:
+        if self.timer is not None:
+            self.timer.mark(name)
 
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int]) -> None:
         import torch.distributed as dist
@@ -137,12 +143,18 @@ class ExpertParallelMoe:
             return
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
-    def forward(self, xs: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
-        """xs (b, s, h) local tokens -> this rank's layer output, in the input's dtype."""
+    def forward(self, xs: torch.Tensor, residual: torch.Tensor | None = None,
+                taps: dict | None = None) -> torch.Tensor:
+        """xs (b, s, h) local tokens -> this rank's layer output, in the input's dtype. taps, when
+        given, receives the local tokens' expert ids ("ids", (tokens, top_k))."""
         b, s, h = xs.shape
         x = xs.reshape(b * s, h).to(torch.float32).contiguous()
         res = None if residual is None else residual.reshape(b * s, h).to(torch.float32).contiguous()
+        self._mark("dispatch")
         d = self.engine.dispatch(x)
+        if taps is not None and d.ids is not None:
+            taps["ids"] = d.ids
+        self._mark("counts_exchange_and_host_read")
         # counts first: every rank learns how many units and records each peer sends it
         recv_counts = torch.empty_like(d.send_counts)
         if self.world == 1:
@@ -156,12 +168,17 @@ class ExpertParallelMoe:
         ru, rp = [int(v[0]) for v in rc], [int(v[1]) for v in rc]
         rows = torch.empty((sum(ru), h), dtype=d.send_rows.dtype, device=x.device)
         picks = torch.empty((sum(rp), 3), dtype=torch.int32, device=x.device)
+        self._mark("row_exchange")
         self._a2a(rows, d.send_rows[:sum(su)], ru, su)
         self._a2a(picks, d.send_picks[:sum(sp)], rp, sp)
+        self._mark("experts")
         y = self.engine.experts(rows, picks, ru, rp)
         back = torch.empty((sum(su), h), dtype=torch.float32, device=x.device)
+        self._mark("return_exchange")
         self._a2a(back, y, su, ru)
+        self._mark("combine")
         out = self.engine.combine(d, back, res)
+        self._mark("end")
         return out.reshape(b, s, h).to(xs.dtype)
 
 

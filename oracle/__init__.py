@@ -55,6 +55,7 @@ def lib() -> ctypes.CDLL:
             "cwo_matmul": (I32, [I32, I32, P, I64, I64, I64, U32, P, I32, P]),
             "cwo_moe_forward": (I32, [P, P, I32, I32, P, P, P, P, P]),
             "cwo_add_rms_norm": (I32, [P, P, P, P, F, I64, I32, P, P]),
+            "cwo_moe_forward_fast": (I32, [P, P, I32, P]),
             "cwo_set_threads": (None, [I32]),
             "cwo_get_threads": (I32, []),
         }
@@ -189,9 +190,7 @@ class _Layer(ctypes.Structure):
     ]
 
 
-def moe_forward(layer: dict, x: np.ndarray, mode: int) -> dict:
-    """One MoE layer on the CPU. `layer` holds numpy arrays under the cw_oracle.h field names."""
-    keep = []
+def _layer_struct(layer: dict, keep: list) -> _Layer:
 
     def arr(name, dtype):
         a = layer.get(name)
@@ -219,6 +218,13 @@ def moe_forward(layer: dict, x: np.ndarray, mode: int) -> dict:
     L.sh_down_type = int(layer.get("sh_down_type", Q4_K))
     L.sh_gate, L.sh_up, L.sh_down = arr("sh_gate", np.uint8), arr("sh_up", np.uint8), arr("sh_down", np.uint8)
     L.sh_gate_inp = arr("sh_gate_inp", np.float32)
+    return L
+
+
+def moe_forward(layer: dict, x: np.ndarray, mode: int) -> dict:
+    """One MoE layer on the CPU. `layer` holds numpy arrays under the cw_oracle.h field names."""
+    keep = []
+    L = _layer_struct(layer, keep)
     x = np.ascontiguousarray(x, dtype=np.float32)
     T, H = x.shape
     k = L.top_k
@@ -230,6 +236,17 @@ def moe_forward(layer: dict, x: np.ndarray, mode: int) -> dict:
     rc = lib().cwo_moe_forward(ctypes.byref(L), _p(x), T, mode, _p(out), _p(routed), _p(shared), _p(ids), _p(w))
     assert rc == 0, rc
     return {"out": out, "routed": routed, "shared": shared, "ids": ids, "w": w}
+
+
+def moe_forward_fast(layer: dict, x: np.ndarray) -> np.ndarray:
+    """The vectorised CPU build of the layer (candle policy, SiLU layers): the timed CPU baseline."""
+    keep = []
+    L = _layer_struct(layer, keep)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    rc = lib().cwo_moe_forward_fast(ctypes.byref(L), _p(x), x.shape[0], _p(out))
+    assert rc == 0, rc
+    return out
 
 
 def add_rms_norm(a: np.ndarray, b: np.ndarray, c: np.ndarray | None, alpha: np.ndarray,

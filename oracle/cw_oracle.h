@@ -107,6 +107,10 @@ typedef struct {
 int cwo_moe_forward(const cwo_moe_layer* L, const float* x, int T, int mode, float* out, float* routed,
                     float* shared, uint32_t* ids, float* w);
 
+// The same layer (candle policy, SiLU layers) vectorised for speed: the timed CPU baseline, not
+// a checker (oracle/fast.cpp). out (T, H).
+int cwo_moe_forward_fast(const cwo_moe_layer* L, const float* x, int T, float* out);
+
 // add_norm (crates/engine/src/fuse_kernel.rs:433-471, the residual step of model_next.rs:1432-1436
 // and its unfused form ((routed + shared) + h, then the next layer's RmsNorm)): per row of
 // `hidden`, sum = (a + b) + c (c may be NULL) and out = rms_norm(sum) * alpha with candle-nn's

@@ -50,8 +50,8 @@ class OracleEngine:
                 counts[d, 1] += len(js)
         rows = np.array(rows, dtype=np.float32).reshape(-1, self.H)
         recs = np.array(recs, dtype=np.int32).reshape(-1, 3)
-        return Dispatched(x, torch.from_numpy(unit_of), None, torch.from_numpy(rows), torch.from_numpy(recs),
-                          torch.from_numpy(counts))
+        return Dispatched(x, torch.from_numpy(ids.astype(np.int32)), torch.from_numpy(unit_of), None,
+                          torch.from_numpy(rows), torch.from_numpy(recs), torch.from_numpy(counts))
 
     def experts(self, rows, picks, src_units, src_picks):
         import torch

@@ -177,3 +177,19 @@ def test_moe_forward_small_layer_modes():
     assert rel_l2(a["routed"], b["routed"]) < 1e-5  # IQ matrices use f32 activations in both
     assert rel_l2(a["shared"], b["shared"]) > 1e-4  # the Q4_K shared expert does not
     assert np.allclose(a["out"], a["routed"] + a["shared"])
+
+
+@pytest.mark.parametrize("types", [(O.IQ2_S, O.IQ2_S, O.IQ3_S), (O.Q4_K, O.Q4_K, O.Q4_K), (O.IQ3_S, O.IQ3_S, O.Q4_K)])
+def test_fast_cpu_layer_agrees_with_oracle(types):
+    # the vectorised CPU baseline computes the same layer as O1 (candle policy): same routing on
+    # these inputs, outputs within the layer bar (the reordered f32 sums can flip a Q8_K code of
+    # a down matrix's activations, ~1e-4)
+    from tests.layers import Spec, build_cpu, make_input, rel_l2
+
+    s = Spec(hidden=512, n_experts=16, top_k=4, inter=256, gate_type=types[0], up_type=types[1],
+             down_type=types[2], shared_inter=256, seed=3)
+    L = build_cpu(s)
+    x = make_input(s, 24)
+    ref = O.moe_forward(L, x, O.MODE_CANDLE)
+    got = O.moe_forward_fast(L, x)
+    assert rel_l2(got, ref["out"]) < 1e-3
