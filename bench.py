@@ -474,18 +474,19 @@ def c3_runs(world, rank, local, a, pk, maxall, barrier):
     b_exp = cfg.expert_bytes() + (2 * cfg.inter + cfg.hidden) * 4
     res = {"config": desc, "layers": nl}
     if world > 1:
-        from coachwhip_b200.ep import CudaEngine, ExpertParallelMoe
+        from coachwhip_b200.ep import CudaEngine, EpComm, LibraryExpertParallelMoe
 
+        T = 4096
+        per = T // world
+        comm = EpComm(local, world, rank)
         mods = []
         for l in range(nl):
             lay = W.build_layer(cfg, l, local, first=rank * epr, n_local=epr)
             eng = CudaEngine(lay.router_w, cfg.top_k, True, lay.act, lay.banks, world, rank, gate_bias=lay.router_b)
             eng._keep = lay
-            mods.append(ExpertParallelMoe(eng))
+            mods.append(LibraryExpertParallelMoe(eng, comm, per))
         torch.cuda.synchronize(dev)
         res["bank_synthesis_s"] = time.time() - t0
-        T = 4096
-        per = T // world
         x = W.make_input(cfg, T, local)[rank * per:(rank + 1) * per].contiguous().view(1, per, cfg.hidden)
         for _ in range(max(1, a.warmup // 2)):
             run_stack(mods, x)
@@ -502,7 +503,31 @@ def c3_runs(world, rank, local, a, pk, maxall, barrier):
         fl = nl * cfg.flops(T)
         res["prefill"] = {"tokens": T, "tokens_per_rank": per, "ranks": world, "experts_per_rank": epr,
                           "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3), "tflops": fl / (ms / 1e3) / 1e12,
+                          "transport": "cwx_ep_forward: NCCL inside libcwx, fixed-capacity exchanges, no host sync",
                           "timing": f"CUDA events over {reps} eager passes, max over ranks"}
+        # decode batches 1 and 64 spread over the ranks (a rank may hold no token: it still takes
+        # part in both exchanges and runs the picks the others send it)
+        res["decode"] = {}
+        for Td in (1, 64):
+            lo, hi = Td * rank // world, Td * (rank + 1) // world
+            capd = max(1, (Td + world - 1) // world)
+            for m in mods:
+                m.cap_tokens = capd
+            xd = W.make_input(cfg, Td, local)[lo:hi].contiguous().view(1, hi - lo, cfg.hidden)
+            for _ in range(3):
+                run_stack(mods, xd)
+            barrier()
+            e0.record()
+            for _ in range(5):
+                run_stack(mods, xd)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            msd = maxall(e0.elapsed_time(e1) / 5)
+            res["decode"][str(Td)] = {"ms_per_step": msd, "tokens_per_s": Td / (msd / 1e3),
+                                      "timing": "CUDA events over 5 eager passes, max over ranks"}
+        _lib.status(local)
+        del mods
+        comm.close()
         return res
     store = ExpertStore([])
     layers = [W.build_layer(cfg, l, local, store=store) for l in range(nl)]
@@ -540,39 +565,13 @@ def c3_runs(world, rank, local, a, pk, maxall, barrier):
     return res
 
 
-class EpTimer:
-    """CUDA events around the phases of ExpertParallelMoe.forward (summed over calls)."""
-
-    PH = ["dispatch", "counts_exchange_and_host_read", "row_exchange", "experts", "return_exchange", "combine"]
-
-    def __init__(self):
-        self.ev = []
-
-    def mark(self, name):
-        import torch
-
-        e = torch.cuda.Event(enable_timing=True)
-        e.record()
-        self.ev.append((name, e))
-
-    def totals(self):
-        import torch
-
-        torch.cuda.synchronize()
-        out = {p: 0.0 for p in self.PH}
-        for (n0, e0), (_, e1) in zip(self.ev, self.ev[1:]):
-            if n0 in out:
-                out[n0] += e0.elapsed_time(e1)
-        return out
-
-
 def ep_runs(world, rank, local, a, maxall, barrier):
     """Config 4 expert-parallel: 48 layers, 8192 tokens split over the ranks, f32 policy."""
     import torch
 
     from coachwhip_b200 import _lib
     from coachwhip_b200 import workloads as W
-    from coachwhip_b200.ep import CudaEngine, ExpertParallelMoe
+    from coachwhip_b200.ep import CudaEngine
     from coachwhip_b200.moe import ExpertStore
 
     cfg = W.CONFIGS["C4"]
@@ -596,35 +595,39 @@ def ep_runs(world, rank, local, a, maxall, barrier):
         return {"config": desc, "layers": nl, "tokens": T, "ranks": 1, "experts_per_rank": cfg.n_experts,
                 "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3), "tflops": fl / (ms / 1e3) / 1e12,
                 "path": "single-device cwx_moe_forward (no exchange), CUDA graph of the 48 layers"}
+    from coachwhip_b200.ep import EpComm, LibraryExpertParallelMoe
+
     epr = cfg.n_experts // world
+    comm = EpComm(local, world, rank)
     layers = []
     for l in range(nl):
         lay = W.build_layer(cfg, l, local, act_mode=_lib.ACT_MODE_F32, first=rank * epr, n_local=epr)
         eng = CudaEngine(lay.router_w, cfg.top_k, True, lay.act, lay.banks, world, rank, gate_bias=lay.router_b,
                          shared=lay.shared, act_mode=_lib.ACT_MODE_F32)
         eng._keep = lay
-        layers.append(ExpertParallelMoe(eng))
+        layers.append(LibraryExpertParallelMoe(eng, comm, per))
     x = W.make_input(cfg, T, local)[rank * per:(rank + 1) * per].contiguous().view(1, per, cfg.hidden)
     for _ in range(max(1, a.warmup // 2)):
         run_stack(layers, x)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 2
+    reps = 3
     e0.record()
     for _ in range(reps):
         run_stack(layers, x)
     e1.record()
     torch.cuda.synchronize(dev)
     ms = maxall(e0.elapsed_time(e1) / reps)
-    # per-phase breakdown of one more pass (events between the phases; max over ranks)
-    tm = EpTimer()
-    for m in layers:
-        m.timer = tm
+    # per-phase breakdown of one more pass: the library's phase events (max over ranks)
+    ctx = _lib.ctx(local)
+    _lib.lib().cwx_ctx_reset_profile(ctx)
+    _lib.lib().cwx_ctx_set_profiling(ctx, 1)
     barrier()
     run_stack(layers, x)
-    ph = {k: maxall(v) for k, v in tm.totals().items()}
-    for m in layers:
-        m.timer = None
+    _lib.lib().cwx_ctx_set_profiling(ctx, 0)
+    msv, _ = _lib.read_profile(local)
+    _lib.lib().cwx_ctx_reset_profile(ctx)
+    ph = {n: maxall(msv[i]) for i, n in enumerate(_lib.PHASES) if n.startswith("ep_")}
     # parity: layer 0 on this rank's tokens against the single-device layer (all 512 experts)
     taps = {}
     out_ep = layers[0].forward(x, taps=taps)[0]
@@ -636,13 +639,15 @@ def ep_runs(world, rank, local, a, maxall, barrier):
     ids_eq = bool(torch.equal(taps["ids"].view(-1), ftaps["ids"].view(-1)))
     rel = maxall(rel)
     ids_all = maxall(0.0 if ids_eq else 1.0) == 0.0
-    del full
+    del full, layers
+    comm.close()
     return {"config": desc, "layers": nl, "tokens": T, "tokens_per_rank": per, "ranks": world,
             "experts_per_rank": epr, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
             "tflops": fl / (ms / 1e3) / 1e12, "phase_ms_per_step": ph,
             "ep_parity": {"rel_l2": rel, "ids_equal": ids_all, "bar": 1e-3,
                           "what": "layer 0 on each rank's tokens vs the single-device layer; max over ranks"},
-            "transport": "NCCL all-to-all (torch.distributed all_to_all_single); counts read on the host per layer",
+            "transport": "cwx_ep_forward: NCCL inside libcwx, fixed-capacity exchanges (counts read on the "
+                         "device), no host synchronisation in a layer",
             "timing": f"CUDA events over {reps} eager passes of the {nl} layers, max over ranks"}
 
 

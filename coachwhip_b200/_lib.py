@@ -9,7 +9,7 @@ import threading
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libcwx.so")
 
-OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT, ENOMEM, EDEVICE = range(7)
+OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT, ENOMEM, EDEVICE, ECOMM = range(8)
 TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_IQ3_S, TYPE_IQ2_S, TYPE_MXFP4 = 0, 8, 12, 14, 21, 22, 39
 TYPE_IQ2_XXS, TYPE_IQ3_XXS, TYPE_IQ4_XS = 16, 18, 23
 ACT_MODE_CANDLE, ACT_MODE_F32 = 0, 1
@@ -25,9 +25,11 @@ EXPORTS = [
     "cwx_ctx_set_mma_min_pile", "cwx_ep_dispatch", "cwx_ep_experts", "cwx_ep_combine", "cwx_bank_synth_experts",
     "cwx_ep_rows_f16", "cwx_ctx_check_wait", "cwx_gguf_open", "cwx_gguf_close", "cwx_gguf_info",
     "cwx_gguf_tensor_info", "cwx_gguf_tensor", "cwx_bank_from_gguf", "cwx_gguf_tensor_f32", "cwx_gguf_meta_int",
-    "cwx_gguf_meta_f64", "cwx_gguf_meta_str", "cwx_add_rms_norm",
+    "cwx_gguf_meta_f64", "cwx_gguf_meta_str", "cwx_add_rms_norm", "cwx_ep_unique_id", "cwx_ep_comm_create",
+    "cwx_ep_comm_wrap", "cwx_ep_comm_abort", "cwx_ep_comm_destroy", "cwx_ep_forward",
 ]
-PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine"]
+PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine", "ep_dispatch", "ep_exchange",
+          "ep_experts", "ep_return", "ep_combine"]
 
 
 class CwxError(RuntimeError):
@@ -126,6 +128,13 @@ def lib() -> ctypes.CDLL:
             "cwx_gguf_meta_int": (I32, [P, ctypes.c_char_p, P]),
             "cwx_gguf_meta_f64": (I32, [P, ctypes.c_char_p, P]),
             "cwx_gguf_meta_str": (I32, [P, ctypes.c_char_p, P, I64, P]),
+            "cwx_ep_unique_id": (I32, [P, I64]),
+            "cwx_ep_comm_create": (I32, [I32, P, I32, I32, PP]),
+            "cwx_ep_comm_wrap": (I32, [P, I32, I32, I32, PP]),
+            "cwx_ep_comm_abort": (I32, [P]),
+            "cwx_ep_comm_destroy": (I32, [P]),
+            "cwx_ep_forward": (I32, [P, P, ctypes.POINTER(MoeLayer), ctypes.POINTER(EpGroup), P, I32, I32, P, P, P,
+                                     P]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)

@@ -16,7 +16,8 @@ from concurrent.futures import ThreadPoolExecutor
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libcwx.so")
-SOURCES = ["api.cu", "bank.cu", "route.cu", "gemv.cu", "act.cu", "noalloc.cu", "mma.cu", "ep.cu", "gguf.cpp"]
+SOURCES = ["api.cu", "bank.cu", "route.cu", "gemv.cu", "act.cu", "noalloc.cu", "mma.cu", "ep.cu", "ep_nccl.cu",
+           "gguf.cpp"]
 NO_FMA = {"bank.cu"}
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -63,7 +64,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
             if r.returncode != 0:
                 raise RuntimeError(f"nvcc failed ({r.returncode}): {' '.join(r.args)}\n{r.stdout or ''}{r.stderr or ''}")
     if force or _stale(LIB, objs):
-        subprocess.run([nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"], check=True)
+        subprocess.run([nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-ldl"], check=True)
     return LIB
 
 

@@ -1048,3 +1048,180 @@ extern "C" int cwx_ep_combine(cwx_ctx* c, const cwx_moe_layer* L, const cwx_ep_g
     c->launches += 1;
     return CWX_OK;
 }
+
+// A whole expert-parallel layer with the library's own transport: the three steps above with
+// fixed-capacity exchanges between them (ep_nccl.cu), so the receive sizes never travel through
+// the host. Buffers that live across the exchanges (the routing, the units' places, the send and
+// receive segments, the unit sums) are the communicator's; the workspace holds each step's
+// temporaries.
+extern "C" int cwx_ep_forward(cwx_ctx* c, cwx_ep_comm* comm, const cwx_moe_layer* L, const cwx_ep_group* g,
+                              const float* x, int32_t tokens, int32_t cap_tokens, const float* residual, float* out,
+                              uint32_t* ids_out, void* stream) {
+    if (!c || !comm) return fail(CWX_EINVAL, "cwx_ep_forward: null context or communicator");
+    int rc = ep_check(L, g, "cwx_ep_forward");
+    if (rc) return rc;
+    int cw = 0, cr = 0, cd = 0;
+    if ((rc = ep_comm_info(comm, &cw, &cr, &cd))) return rc;
+    if (cw != g->world || cr != g->rank || cd != c->device)
+        return fail(CWX_EINVAL,
+                    "cwx_ep_forward: the communicator is rank %d of %d on device %d, the group rank %d of %d and "
+                    "the context device %d",
+                    cr, cw, cd, g->rank, g->world, c->device);
+    if (!L->router_w || L->top_k < 1 || L->top_k > 16 || L->top_k > L->n_experts || L->n_experts > 1024)
+        return fail(CWX_EINVAL, "cwx_ep_forward: router or top_k out of range");
+    if (tokens < 0 || cap_tokens < 1 || tokens > cap_tokens)
+        return fail(CWX_EINVAL, "cwx_ep_forward: tokens %d with capacity %d", tokens, cap_tokens);
+    if (tokens && (!x || !out)) return fail(CWX_EINVAL, "cwx_ep_forward: null x or out");
+    if (L->hidden % 4 || ((uintptr_t)x & 15)) return fail(CWX_EINVAL, "cwx_ep_forward: x rows must be 16-byte aligned");
+    const bool shared = L->sh_gate != nullptr;
+    if (shared && (!L->sh_up || !L->sh_down || !L->sh_gate_inp))
+        return fail(CWX_EINVAL, "cwx_ep_forward: incomplete shared expert");
+    cwx_moe_layer lc = *L;  // this rank's experts as a layer of their own, one pick per record
+    lc.n_experts = g->experts_per_rank;
+    lc.top_k = 1;
+    lc.sh_gate = lc.sh_up = lc.sh_down = nullptr;
+    lc.sh_gate_inp = nullptr;
+    if ((rc = validate_layer(&lc))) return rc;
+    CWX_CUDA(cudaSetDevice(c->device));
+    cudaStream_t st = (cudaStream_t)stream;
+    const int T = tokens, cap = cap_tokens, H = L->hidden, E = L->n_experts, K = L->top_k, W = g->world;
+    const int epr = g->experts_per_rank;
+    const int cap_rec = cap * (K < epr ? K : epr);
+    const bool f16 = ep_rows_f16(L);
+    const size_t rb = f16 ? 2 : 4;
+    const int64_t U = (int64_t)W * cap, P = (int64_t)W * cap_rec;
+    if (P > INT32_MAX / 2) return fail(CWX_EUNSUPPORTED, "cwx_ep_forward: %lld record slots", (long long)P);
+
+    // the communicator's buffers (sized in a first pass, carved in the second)
+    uint32_t* ids = nullptr;
+    float *wts = nullptr, *sgate = nullptr, *yu = nullptr, *back = nullptr;
+    int32_t *unit_of = nullptr, *scnt = nullptr, *rcnt = nullptr, *spk = nullptr, *rpk = nullptr;
+    void *srows = nullptr, *rrows = nullptr;
+    size_t need = 0;
+    for (int pass = 0; pass < 2; ++pass) {
+        Carve b{nullptr, 0};
+        if (pass) {
+            void* base = nullptr;
+            if ((rc = ep_comm_buffer(comm, need, st, &base))) return rc;
+            b.base = static_cast<uint8_t*>(base);
+        }
+        ids = b.take<uint32_t>((size_t)cap * K);
+        wts = b.take<float>((size_t)cap * K);
+        sgate = b.take<float>((size_t)cap);
+        unit_of = b.take<int32_t>((size_t)cap * W);
+        scnt = b.take<int32_t>((size_t)2 * W);
+        rcnt = b.take<int32_t>((size_t)2 * W);
+        srows = b.take<uint8_t>((size_t)U * H * rb);
+        rrows = b.take<uint8_t>((size_t)U * H * rb);
+        spk = b.take<int32_t>((size_t)P * 3);
+        rpk = b.take<int32_t>((size_t)P * 3);
+        yu = b.take<float>((size_t)U * H);
+        back = b.take<float>((size_t)U * H);
+        need = b.off + 256;
+    }
+
+    // 1. dispatch into the fixed-capacity send segments
+    {
+        PhaseTimer t(c, st, CWX_PHASE_EP_DISPATCH);
+        Carve sz{nullptr, 0};
+        sz.take<float>((size_t)T * E + 1);
+        sz.take<int32_t>((size_t)T * W + 1);
+        sz.take<int32_t>((size_t)T * W + 1);
+        if ((rc = ensure_ws(c, sz.off + 256, st))) return rc;
+        Carve w{c->ws, 0};
+        float* logits = w.take<float>((size_t)T * E + 1);
+        int32_t* cnt = w.take<int32_t>((size_t)T * W + 1);
+        int32_t* pbase = w.take<int32_t>((size_t)T * W + 1);
+        if (T > 0) {
+            if ((rc = launch_router(x, L->router_w, L->router_b, T, H, E, logits, st))) return rc;
+            if ((rc = launch_route(logits, T, E, K, L->norm_topk_prob, ids, wts, x, shared ? L->sh_gate_inp : nullptr,
+                                   H, shared ? sgate : nullptr, st)))
+                return rc;
+            c->launches += 2;
+        }
+        if ((rc = launch_ep_units(x, T, H, K, W, epr, ids, wts, cnt, unit_of, pbase, scnt, f16, srows, spk, st, cap,
+                                  cap_rec)))
+            return rc;
+        c->launches += T > 0 ? 3 : 0;
+        t.end();
+    }
+    // 2. counts, unit rows and pick records to every peer, in one group
+    {
+        const void* snd[3] = {scnt, srows, spk};
+        void* rcv[3] = {rcnt, rrows, rpk};
+        const size_t bytes[3] = {8, (size_t)cap * H * rb, (size_t)cap_rec * 12};
+        PhaseTimer t(c, st, CWX_PHASE_EP_EXCHANGE);
+        if ((rc = ep_comm_exchange(comm, 3, snd, rcv, bytes, st))) return rc;
+        t.end();
+    }
+    // 3. this rank's experts over the received records; each unit's weighted sum
+    {
+        PhaseTimer t(c, st, CWX_PHASE_EP_EXPERTS);
+        // the product path from the expected picks per rank (tokens spread evenly over the ranks)
+        const int mma = mma_layer(c, &lc, cap * K) ? 1 : 0;
+        LayerPlan p;
+        plan_layer(&lc, (int)P, mma, nullptr, &p);
+        const size_t base = (p.bytes + 255) & ~(size_t)255;
+        Carve ex{nullptr, 0};
+        ex.take<uint32_t>((size_t)P);
+        ex.take<uint32_t>((size_t)P);
+        ex.take<float>((size_t)P);
+        ex.take<int32_t>((size_t)U);
+        ex.take<int32_t>((size_t)U);
+        ex.take<int32_t>(4);
+        if (f16) ex.take<float>((size_t)U * H);
+        if ((rc = ensure_ws(c, base + ex.off + 256, st))) return rc;
+        plan_layer(&lc, (int)P, mma, c->ws, &p);
+        Carve w{c->ws + base, 0};
+        uint32_t* rowmap = w.take<uint32_t>((size_t)P);
+        uint32_t* eid = w.take<uint32_t>((size_t)P);
+        float* wgt = w.take<float>((size_t)P);
+        int32_t* first = w.take<int32_t>((size_t)U);
+        int32_t* end = w.take<int32_t>((size_t)U);
+        int32_t* n_picks = w.take<int32_t>(4);
+        float* rows32 = f16 ? w.take<float>((size_t)U * H) : nullptr;
+        // pick slots past the received records still go through the hidden-row preparation, which
+        // reads each slot's expert (the clamped SwiGLU biases): they get expert 0, a valid index
+        CWX_CUDA(cudaMemsetAsync(eid, 0, (size_t)P * 4, st));
+        if ((rc = launch_ep_recv_cap(rpk, rcnt, W, cap, cap_rec, rowmap, eid, wgt, first, end, n_picks, st))) return rc;
+        const float* xr = reinterpret_cast<const float*>(rrows);
+        if (f16) {
+            if ((rc = launch_f16_to_f32(reinterpret_cast<const __half*>(rrows), U * H, rows32, st))) return rc;
+            xr = rows32;
+        }
+        p.xrows = U;
+        p.rowmap = rowmap;
+        p.ids = eid;  // per-pick expert (the clamped SwiGLU biases index it)
+        if ((rc = launch_permute(eid, P, epr, p.pairs, p.heads, p.used3, p.n_used, p.perm, c->d_err, st, n_picks)))
+            return rc;
+        c->launches += 1 + (f16 ? 1 : 0) + perm_launches(P, epr);
+        cwx_moe_args a;
+        memset(&a, 0, sizeof a);
+        a.x = xr;
+        a.tokens = (int32_t)U;
+        if ((rc = p.mma ? moe_mma(c, &lc, &a, p, st) : moe_gemv(c, &lc, &a, p, st))) return rc;
+        if ((rc = launch_ep_unit_sum_cap(p.y, wgt, first, end, rcnt, W, cap, H, yu, st))) return rc;
+        c->launches += 1;
+        t.end();
+    }
+    // 4. the unit sums back to their sources
+    {
+        const void* snd[1] = {yu};
+        void* rcv[1] = {back};
+        const size_t bytes[1] = {(size_t)cap * H * 4};
+        PhaseTimer t(c, st, CWX_PHASE_EP_RETURN);
+        if ((rc = ep_comm_exchange(comm, 1, snd, rcv, bytes, st))) return rc;
+        t.end();
+    }
+    // 5. combine: the returned units in rank order, the shared expert, the residual
+    if (T > 0) {
+        PhaseTimer t(c, st, CWX_PHASE_EP_COMBINE);
+        float* ys = nullptr;
+        if (shared && (rc = ep_shared(c, L, x, T, &ys, st))) return rc;
+        if ((rc = launch_ep_combine(back, unit_of, T, W, H, ys, sgate, residual, out, st))) return rc;
+        c->launches += 1;
+        if (ids_out) CWX_CUDA(cudaMemcpyAsync(ids_out, ids, (size_t)T * K * 4, cudaMemcpyDeviceToDevice, st));
+        t.end();
+    }
+    return CWX_OK;
+}

@@ -87,20 +87,22 @@ __global__ void __launch_bounds__(1024) k_ep_scan(const int32_t* __restrict__ cn
 // One block per token: its row to each destination it has picks on (f32, or f16 when the
 // destination's products take f16 activations), and its pick records. upos becomes the unit's
 // index in the whole send buffer (destination offsets added).
+// With cap > 0 (the fixed-capacity layout of the library's own exchange) destination d's units
+// start at row d * cap and its records at d * cap_rec, whatever the other destinations hold.
 template <bool F16>
 __global__ void __launch_bounds__(256) k_ep_pack_units(const float* __restrict__ x, int T, int H, int K, int W,
                                                        int epr, const uint32_t* __restrict__ ids,
                                                        const float* __restrict__ w, int32_t* __restrict__ upos,
                                                        const int32_t* __restrict__ pbase,
                                                        const int32_t* __restrict__ tot, void* __restrict__ send_rows,
-                                                       int32_t* __restrict__ send_picks) {
+                                                       int32_t* __restrict__ send_picks, int cap, int cap_rec) {
     const int t = blockIdx.x;
     __shared__ int32_t uoff[64], poff[64];
     if (threadIdx.x == 0) {
         int32_t a = 0, b = 0;
         for (int d = 0; d < W; ++d) {
-            uoff[d] = a;
-            poff[d] = b;
+            uoff[d] = cap > 0 ? d * cap : a;
+            poff[d] = cap > 0 ? d * cap_rec : b;
             a += tot[2 * d];
             b += tot[2 * d + 1];
         }
@@ -157,6 +159,54 @@ __global__ void k_ep_recv(const int32_t* __restrict__ picks, int64_t P, EpOffset
     if (p == off.pstart[s] || picks[3 * (p - 1)] != picks[3 * p]) first[u] = (int32_t)p;
 }
 
+// Receiver, fixed-capacity layout: source s's records in slots [s * cap_rec, s * cap_rec + n_s)
+// and its units in rows [s * cap, s * cap + u_s), the counts (u_s, n_s) in rcnt[2s], rcnt[2s + 1].
+// The records are packed into picks 0 .. P-1 in source order (P = the sum of the n_s, written to
+// n_picks): rowmap[p] = the unit's row, eid, wgt; each valid unit row r gets its run of records
+// [first[r], end[r]).
+__global__ void k_ep_recv_cap(const int32_t* __restrict__ picks, const int32_t* __restrict__ rcnt, int W, int cap,
+                              int cap_rec, uint32_t* __restrict__ rowmap, uint32_t* __restrict__ eid,
+                              float* __restrict__ wgt, int32_t* __restrict__ first, int32_t* __restrict__ end,
+                              int32_t* __restrict__ n_picks) {
+    const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (q == 0) {
+        int32_t tot = 0;
+        for (int s = 0; s < W; ++s) tot += rcnt[2 * s + 1];
+        *n_picks = tot;
+    }
+    if (q >= (int64_t)W * cap_rec) return;
+    const int s = (int)(q / cap_rec), i = (int)(q % cap_rec);
+    const int32_t ns = rcnt[2 * s + 1];
+    if (i >= ns) return;
+    int64_t p = i;
+    for (int r = 0; r < s; ++r) p += rcnt[2 * r + 1];
+    const int32_t u = picks[3 * q];
+    const uint32_t row = (uint32_t)((int64_t)s * cap + u);
+    rowmap[p] = row;
+    eid[p] = (uint32_t)picks[3 * q + 1];
+    wgt[p] = __int_as_float(picks[3 * q + 2]);
+    if (i == 0 || picks[3 * (q - 1)] != u) first[row] = (int32_t)p;
+    if (i == ns - 1 || picks[3 * (q + 1)] != u) end[row] = (int32_t)(p + 1);
+}
+
+// Fixed-capacity unit sums: row r = s * cap + u is a unit when u < rcnt[2s]; its sum is written in
+// place (other rows are left as they are: nothing reads them).
+__global__ void __launch_bounds__(256) k_ep_unit_sum_cap(const float* __restrict__ y, const float* __restrict__ wgt,
+                                                         const int32_t* __restrict__ first,
+                                                         const int32_t* __restrict__ end,
+                                                         const int32_t* __restrict__ rcnt, int cap, int H,
+                                                         float* __restrict__ yu) {
+    const int64_t r = blockIdx.x;
+    const int s = (int)(r / cap), u = (int)(r % cap);
+    if (u >= rcnt[2 * s]) return;
+    const int64_t p0 = first[r], p1 = end[r];
+    for (int c = threadIdx.x; c < H; c += blockDim.x) {
+        float acc = 0.f;
+        for (int64_t p = p0; p < p1; ++p) acc = __fadd_rn(acc, __fmul_rn(y[p * H + c], wgt[p]));
+        yu[r * H + c] = acc;
+    }
+}
+
 // yu[u] = sum over the unit's records p in order of wgt[p] * y[p].
 __global__ void __launch_bounds__(256) k_ep_unit_sum(const float* __restrict__ y, const float* __restrict__ wgt,
                                                      const int32_t* __restrict__ first, int64_t U, int64_t P, int H,
@@ -200,7 +250,7 @@ static int launched(const char* what) {
 
 int launch_ep_units(const float* x, int T, int H, int K, int W, int epr, const uint32_t* ids, const float* w,
                     int32_t* cnt, int32_t* upos, int32_t* pbase, int32_t* tot, bool f16, void* send_rows,
-                    int32_t* send_picks, cudaStream_t st) {
+                    int32_t* send_picks, cudaStream_t st, int cap, int cap_rec) {
     if (W > 64) return fail(CWX_EUNSUPPORTED, "expert parallelism over more than 64 ranks");
     if (T == 0) {
         CWX_CUDA(cudaMemsetAsync(tot, 0, (size_t)2 * W * 4, st));
@@ -209,9 +259,11 @@ int launch_ep_units(const float* x, int T, int H, int K, int W, int epr, const u
     k_ep_count<<<(T + 255) / 256, 256, 0, st>>>(ids, T, K, epr, W, cnt);
     k_ep_scan<<<W, 1024, 0, st>>>(cnt, T, W, upos, pbase, tot);
     if (f16)
-        k_ep_pack_units<true><<<T, 256, 0, st>>>(x, T, H, K, W, epr, ids, w, upos, pbase, tot, send_rows, send_picks);
+        k_ep_pack_units<true><<<T, 256, 0, st>>>(x, T, H, K, W, epr, ids, w, upos, pbase, tot, send_rows, send_picks,
+                                                 cap, cap_rec);
     else
-        k_ep_pack_units<false><<<T, 256, 0, st>>>(x, T, H, K, W, epr, ids, w, upos, pbase, tot, send_rows, send_picks);
+        k_ep_pack_units<false><<<T, 256, 0, st>>>(x, T, H, K, W, epr, ids, w, upos, pbase, tot, send_rows, send_picks,
+                                                  cap, cap_rec);
     return launched("expert-parallel dispatch kernels");
 }
 
@@ -226,6 +278,21 @@ int launch_ep_recv(const int32_t* picks, int64_t P, const EpOffsets& off, uint32
     if (P == 0) return CWX_OK;
     k_ep_recv<<<(unsigned)((P + 255) / 256), 256, 0, st>>>(picks, P, off, rowmap, eid, wgt, first);
     return launched("k_ep_recv");
+}
+
+int launch_ep_recv_cap(const int32_t* picks, const int32_t* rcnt, int W, int cap, int cap_rec, uint32_t* rowmap,
+                       uint32_t* eid, float* wgt, int32_t* first, int32_t* end, int32_t* n_picks, cudaStream_t st) {
+    const int64_t n = (int64_t)W * cap_rec;
+    const unsigned blocks = (unsigned)(n > 0 ? (n + 255) / 256 : 1);
+    k_ep_recv_cap<<<blocks, 256, 0, st>>>(picks, rcnt, W, cap, cap_rec, rowmap, eid, wgt, first, end, n_picks);
+    return launched("k_ep_recv_cap");
+}
+
+int launch_ep_unit_sum_cap(const float* y, const float* wgt, const int32_t* first, const int32_t* end,
+                           const int32_t* rcnt, int W, int cap, int H, float* yu, cudaStream_t st) {
+    if ((int64_t)W * cap == 0) return CWX_OK;
+    k_ep_unit_sum_cap<<<(unsigned)((int64_t)W * cap), 256, 0, st>>>(y, wgt, first, end, rcnt, cap, H, yu);
+    return launched("k_ep_unit_sum_cap");
 }
 
 int launch_ep_unit_sum(const float* y, const float* wgt, const int32_t* first, int64_t U, int64_t P, int H, float* yu,

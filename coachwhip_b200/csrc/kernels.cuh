@@ -56,8 +56,9 @@ int launch_route(const float* logits, int T, int E, int K, int norm, uint32_t* i
                  const float* g_inp, int H, float* sgate, cudaStream_t st);
 size_t perm_scratch_bytes(int64_t n, int E);
 int perm_launches(int64_t n, int E);  // kernels launch_permute issues
+// n_dev (optional, device): only the first *n_dev of the n pick slots are picks.
 int launch_permute(const uint32_t* ids, int64_t n, int E, uint32_t* pairs, uint32_t* heads, uint32_t* used3,
-                   uint32_t* n_used, uint32_t* scratch, int* err, cudaStream_t st);
+                   uint32_t* n_used, uint32_t* scratch, int* err, cudaStream_t st, const int32_t* n_dev = nullptr);
 
 // Activation preparation: rows (R, K) -> packed f16 hi/lo rows in the order the grouped products
 // read. With `up` set, the input is the activation of (gate, up): SiLU, or clamped SwiGLU with
@@ -94,9 +95,16 @@ struct EpOffsets {  // received records of source s: [pstart[s], pstart[s+1]); i
 };
 // Dispatch: cnt/upos/pbase are (T, W) scratch; upos ends as each unit's index in the send buffer
 // (-1: no picks there); tot (W, 2) = units and records per destination.
+// cap > 0: the fixed-capacity layout (destination d's units from row d * cap, records from
+// d * cap_rec); 0: destinations packed one after the other.
 int launch_ep_units(const float* x, int T, int H, int K, int W, int epr, const uint32_t* ids, const float* w,
                     int32_t* cnt, int32_t* upos, int32_t* pbase, int32_t* tot, bool f16, void* send_rows,
-                    int32_t* send_picks, cudaStream_t st);
+                    int32_t* send_picks, cudaStream_t st, int cap = 0, int cap_rec = 0);
+// The fixed-capacity receive side: records packed into picks (count into n_picks), unit runs.
+int launch_ep_recv_cap(const int32_t* picks, const int32_t* rcnt, int W, int cap, int cap_rec, uint32_t* rowmap,
+                       uint32_t* eid, float* wgt, int32_t* first, int32_t* end, int32_t* n_picks, cudaStream_t st);
+int launch_ep_unit_sum_cap(const float* y, const float* wgt, const int32_t* first, const int32_t* end,
+                           const int32_t* rcnt, int W, int cap, int H, float* yu, cudaStream_t st);
 int launch_ep_recv(const int32_t* picks, int64_t P, const EpOffsets& off, uint32_t* rowmap, uint32_t* eid,
                    float* wgt, int32_t* first, cudaStream_t st);
 int launch_ep_unit_sum(const float* y, const float* wgt, const int32_t* first, int64_t U, int64_t P, int H, float* yu,
@@ -104,6 +112,11 @@ int launch_ep_unit_sum(const float* y, const float* wgt, const int32_t* first, i
 int launch_ep_combine(const float* back, const int32_t* unit, int T, int W, int H, const float* shared,
                       const float* sgate, const float* residual, float* out, cudaStream_t st);
 int launch_f16_to_f32(const __half* x, int64_t n, float* y, cudaStream_t st);
+// The library's expert-parallel transport (ep_nccl.cu).
+int ep_comm_info(const cwx_ep_comm* c, int* world, int* rank, int* device);
+int ep_comm_buffer(cwx_ep_comm* c, size_t bytes, cudaStream_t st, void** out);
+int ep_comm_exchange(cwx_ep_comm* c, int nbuf, const void* const* send, void* const* recv, const size_t* bytes,
+                     cudaStream_t st);
 // experts_est: the number of experts expected to have picks (sizes the grid and the K split).
 int launch_gemv(const GemvArgs& a, int64_t experts_est, int device, int sm_count, cudaStream_t st);
 

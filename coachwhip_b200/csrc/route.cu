@@ -296,9 +296,18 @@ __global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits,
 // ---------------------------------------------------------------- piles
 constexpr int PERM_TILE = 1024;
 
+// n_dev (optional): the picks are the first *n_dev of the n slots (a count another kernel wrote)
+__device__ __forceinline__ int64_t picks_of(int64_t n, const int32_t* n_dev) {
+    if (!n_dev) return n;
+    const int64_t d = *n_dev;
+    return d < n ? (d > 0 ? d : 0) : n;
+}
+
 __global__ void __launch_bounds__(1024) k_perm_count(const uint32_t* __restrict__ ids, int64_t n, int E,
-                                                     uint32_t* __restrict__ tile_counts, int* err) {
+                                                     uint32_t* __restrict__ tile_counts, int* err,
+                                                     const int32_t* n_dev) {
     pdl_wait();
+    n = picks_of(n, n_dev);
     extern __shared__ uint32_t hist[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
     __syncthreads();
@@ -400,8 +409,9 @@ __global__ void __launch_bounds__(1024) k_perm_scan(uint32_t* __restrict__ tile_
 // same expert are ranked by lane.
 __global__ void __launch_bounds__(1024) k_perm_scatter(const uint32_t* __restrict__ ids, int64_t n, int E,
                                                        const uint32_t* __restrict__ tile_base,
-                                                       uint32_t* __restrict__ pairs) {
+                                                       uint32_t* __restrict__ pairs, const int32_t* n_dev) {
     pdl_wait();
+    n = picks_of(n, n_dev);
     extern __shared__ uint32_t base[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) base[e] = tile_base[(int64_t)blockIdx.x * E + e];
     __syncthreads();
@@ -432,8 +442,9 @@ constexpr int PERM_SMALL_N = 2048;
 __global__ void __launch_bounds__(1024) k_perm_small(const uint32_t* __restrict__ ids, int n, int E,
                                                      uint32_t* __restrict__ pairs, uint32_t* __restrict__ heads,
                                                      uint32_t* __restrict__ used3, uint32_t* __restrict__ n_used,
-                                                     int* err) {
+                                                     int* err, const int32_t* n_dev) {
     pdl_wait();
+    n = (int)picks_of(n, n_dev);
     __shared__ uint32_t sid[PERM_SMALL_N];
     __shared__ uint32_t cnt[1024];
     __shared__ uint32_t wsum[32], wusum[32];
@@ -616,10 +627,10 @@ size_t perm_scratch_bytes(int64_t n, int E) {
 }
 
 int launch_permute(const uint32_t* ids, int64_t n, int E, uint32_t* pairs, uint32_t* heads, uint32_t* used3,
-                   uint32_t* n_used, uint32_t* scratch, int* err, cudaStream_t st) {
+                   uint32_t* n_used, uint32_t* scratch, int* err, cudaStream_t st, const int32_t* n_dev) {
     if (n <= PERM_SMALL_N && E <= 1024) {
         cudaError_t e = launch_pdl(k_perm_small, dim3(1), dim3(1024), 0, st, ids, (int)n, E, pairs, heads, used3, n_used,
-                                   err);
+                                   err, n_dev);
         return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_perm_small");
     }
     int ntiles = (int)((n + PERM_TILE - 1) / PERM_TILE);
@@ -631,10 +642,11 @@ int launch_permute(const uint32_t* ids, int64_t n, int E, uint32_t* pairs, uint3
         cudaError_t a = cudaFuncSetAttribute(k_perm_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(2 * sh));
         if (a != cudaSuccess) return cuda_fail(a, "cudaFuncSetAttribute(k_perm_scan)");
     }
-    cudaError_t e = launch_pdl(k_perm_count, dim3(ntiles), dim3(1024), sh, st, ids, n, E, scratch, err);
+    cudaError_t e = launch_pdl(k_perm_count, dim3(ntiles), dim3(1024), sh, st, ids, n, E, scratch, err, n_dev);
     if (e == cudaSuccess)
         e = launch_pdl(k_perm_scan, dim3(1), dim3(1024), 2 * sh, st, scratch, ntiles, E, heads, used3, n_used);
-    if (e == cudaSuccess) e = launch_pdl(k_perm_scatter, dim3(ntiles), dim3(1024), sh, st, ids, n, E, scratch, pairs);
+    if (e == cudaSuccess)
+        e = launch_pdl(k_perm_scatter, dim3(ntiles), dim3(1024), sh, st, ids, n, E, scratch, pairs, n_dev);
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "permute kernels");
 }
 

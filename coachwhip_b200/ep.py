@@ -16,8 +16,11 @@ crates/engine/src/experts.rs:2539-2614) with the same output. Rank r owns expert
   5. combine (cwx_ep_combine): the units' rows summed in rank order + shared expert on the local
      tokens + residual.
 
-The exchanges use torch.distributed (NCCL between GPUs; the steps themselves run in libcwx.so).
-The count exchange is read on the host to size the row exchange, so a layer synchronises once.
+ExpertParallelMoe makes the exchanges with torch.distributed (NCCL between GPUs, gloo in the CPU
+protocol tests; the steps themselves run in libcwx.so); its count exchange is read on the host to
+size the row exchange, so a layer synchronises once. LibraryExpertParallelMoe runs the whole layer
+in cwx_ep_forward, with the library's own NCCL communicator (EpComm) and fixed-capacity exchanges
+whose counts stay on the device: no host synchronisation, and no PyTorch needed by a native host.
 `Engine` is the per-rank compute; `CudaEngine` is the product, and tests substitute a CPU engine
 built on the oracle to check the exchange protocol on gloo ranks.
 """
@@ -182,4 +185,70 @@ class ExpertParallelMoe:
         return out.reshape(b, s, h).to(xs.dtype)
 
 
-__all__ = ["CudaEngine", "Dispatched", "ExpertParallelMoe"]
+class EpComm:
+    """This rank's communicator of the library's own expert-parallel transport (cwx_ep_comm, NCCL
+    bound inside libcwx.so). Rank 0 makes the unique id; it reaches the other ranks through
+    `share(id_bytes) -> id_bytes` (by default a torch.distributed object broadcast); every rank then
+    creates its communicator (a collective call)."""
+
+    def __init__(self, device: int, world: int, rank: int, share=None):
+        uid = ctypes.create_string_buffer(128)
+        if rank == 0:
+            check(_lib.lib().cwx_ep_unique_id(uid, 128))
+        raw = bytes(uid.raw)
+        if share is None:
+            import torch.distributed as dist
+
+            box = [raw if rank == 0 else None]
+            dist.broadcast_object_list(box, src=0)
+            raw = box[0]
+        else:
+            raw = share(raw)
+        uid = ctypes.create_string_buffer(raw, 128)
+        h = ctypes.c_void_p()
+        check(_lib.lib().cwx_ep_comm_create(device, uid, world, rank, ctypes.byref(h)))
+        self.handle, self.device, self.world, self.rank = h, device, world, rank
+
+    def close(self) -> None:
+        if self.handle:
+            _lib.lib().cwx_ep_comm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class LibraryExpertParallelMoe:
+    """One expert-parallel layer run by cwx_ep_forward: dispatch, both exchanges (NCCL inside the
+    library, fixed per-peer sizes, counts read on the device) and the combine in one stream-ordered
+    call, no host synchronisation. Every rank calls forward with at most cap_tokens local tokens."""
+
+    def __init__(self, engine: CudaEngine, comm: EpComm, cap_tokens: int):
+        self.engine, self.comm, self.cap_tokens = engine, comm, cap_tokens
+
+    def forward(self, xs: torch.Tensor, residual: torch.Tensor | None = None,
+                taps: dict | None = None) -> torch.Tensor:
+        """xs (b, s, h) local tokens -> this rank's layer output, in the input's dtype. taps, when
+        given, receives the local tokens' expert ids ("ids", (tokens, top_k))."""
+        b, s, h = xs.shape
+        n = b * s
+        if n > self.cap_tokens:
+            raise ValueError(f"{n} tokens above the exchange capacity of {self.cap_tokens}")
+        x = xs.reshape(n, h).to(torch.float32).contiguous()
+        res = None if residual is None else residual.reshape(n, h).to(torch.float32).contiguous()
+        out = torch.empty((n, h), dtype=torch.float32, device=xs.device)
+        ids = None
+        if taps is not None:
+            ids = torch.empty((n, self.engine.top_k), dtype=torch.int32, device=xs.device)
+            taps["ids"] = ids
+        e = self.engine
+        check(_lib.lib().cwx_ep_forward(_lib.ctx(_dev_index(xs)), self.comm.handle, ctypes.byref(e._layer),
+                                        ctypes.byref(e._group), x.data_ptr(), n, self.cap_tokens, _ptr(res),
+                                        out.data_ptr(), _ptr(ids), _stream(xs.device)))
+        return out.reshape(b, s, h).to(xs.dtype)
+
+
+__all__ = ["CudaEngine", "Dispatched", "EpComm", "ExpertParallelMoe", "LibraryExpertParallelMoe"]

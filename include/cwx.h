@@ -38,6 +38,7 @@ extern "C" {
 #define CWX_ETIMEOUT 4     /* a bounded device-side wait gave up (see cwx_ctx_status) */
 #define CWX_ENOMEM 5       /* device or host allocation failed */
 #define CWX_EDEVICE 6      /* a kernel recorded an error (bad expert id, shape) */
+#define CWX_ECOMM 7        /* the expert-parallel transport (NCCL) failed */
 
 /* GGUF tensor type ids (ggml_type) of the supported expert formats. */
 #define CWX_TYPE_F32 0
@@ -272,6 +273,31 @@ int cwx_ep_combine(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_ep_group*
                    int32_t tokens, const int32_t* unit_of, const float* back_rows, const float* sgate,
                    const float* residual, float* out, void* stream);
 
+/* Expert parallelism with the transport inside the library (no counterpart in the reference): an
+ * NCCL communicator per rank (NCCL is bound at run time from libnccl.so.2; without it these calls
+ * return CWX_EUNSUPPORTED). Rank 0 makes a unique id (128 bytes) and shares it with the others by
+ * any host transport; every rank then creates its communicator (a collective call), or wraps an
+ * ncclComm_t the caller already has (cwx_ep_comm_wrap; the caller keeps ownership).
+ * cwx_ep_forward runs a whole expert-parallel layer on `stream`: dispatch (router, route, units),
+ * one NCCL group exchanging the per-peer counts, unit rows and pick records, this rank's experts,
+ * one NCCL group returning the unit sums, and the combine (+ shared expert on the local tokens,
+ * + residual); out (tokens, hidden) f32. Exchanges have fixed per-peer sizes (cap_tokens units,
+ * cap_tokens * min(top_k, experts per rank) records) and the receivers read the counts on the
+ * device, so a layer never waits on the host. Every rank calls it for the same layer with the same
+ * cap_tokens >= its own tokens (0 tokens allowed). ids_out (tokens, top_k), optional, receives the
+ * local tokens' expert ids. The layer's banks hold this rank's experts, as for cwx_ep_dispatch. A
+ * peer that stops calling makes the exchange wait: a watchdog thread may end it with
+ * cwx_ep_comm_abort (the communicator is unusable afterwards). */
+typedef struct cwx_ep_comm cwx_ep_comm;
+int cwx_ep_unique_id(void* out, int64_t cap);
+int cwx_ep_comm_create(int device, const void* unique_id, int32_t world, int32_t rank, cwx_ep_comm** out);
+int cwx_ep_comm_wrap(void* nccl_comm, int32_t world, int32_t rank, int device, cwx_ep_comm** out);
+int cwx_ep_comm_abort(cwx_ep_comm* comm);
+int cwx_ep_comm_destroy(cwx_ep_comm* comm);
+int cwx_ep_forward(cwx_ctx* ctx, cwx_ep_comm* comm, const cwx_moe_layer* layer, const cwx_ep_group* group,
+                   const float* x, int32_t tokens, int32_t cap_tokens, const float* residual, float* out,
+                   uint32_t* ids_out, void* stream);
+
 /* Per-phase timing of cwx_moe_forward, the analogue of the reference's --profile Stats
  * (crates/engine/src/experts.rs:2541-2552): with profiling on, each call records a CUDA event
  * pair around every phase on its stream (also inside stream capture, where the events become
@@ -283,7 +309,13 @@ int cwx_ep_combine(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_ep_group*
 #define CWX_PHASE_GATE_UP 4 /* gate/up expert products */
 #define CWX_PHASE_DOWN 5    /* down expert products */
 #define CWX_PHASE_COMBINE 6 /* weighted combine + shared expert + residual */
-#define CWX_N_PHASES 7
+/* phases of cwx_ep_forward (its expert products also record GATE_UP / DOWN / PREP) */
+#define CWX_PHASE_EP_DISPATCH 7  /* router, route and the units of every destination */
+#define CWX_PHASE_EP_EXCHANGE 8  /* counts, unit rows and pick records to the peers (NCCL) */
+#define CWX_PHASE_EP_EXPERTS 9   /* this rank's experts over the received records, unit sums */
+#define CWX_PHASE_EP_RETURN 10   /* the unit sums back to their sources (NCCL) */
+#define CWX_PHASE_EP_COMBINE 11  /* shared expert on the local tokens, combine, residual */
+#define CWX_N_PHASES 12
 int cwx_ctx_set_profiling(cwx_ctx* ctx, int enabled);
 /* Layers whose routed banks are all IQ2_S / IQ3_S (SiLU, hidden and inter multiples of 256) run
  * their routed products on the tensor cores (tcgen05) when the batch gives at least min_pile

@@ -114,3 +114,97 @@ def test_ep_nccl_two_ranks():
     assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
     res = dict(q.get(timeout=5) for _ in range(2))
     assert max(res.values()) < RTOL, res
+
+
+# ---------------------------------------------------------------- the library's own transport
+@pytest.mark.parametrize("name", ["iq_mix", "mxfp4_gptoss", "q4k"])
+@pytest.mark.parametrize("mode", [O.MODE_F32, O.MODE_CANDLE])
+def test_ep_forward_one_rank_matches_oracle(name, mode):
+    # cwx_ep_forward on a one-rank NCCL communicator: the whole layer (dispatch, both fixed-capacity
+    # exchanges, experts, combine) in one call, with a capacity above the tokens so the segments
+    # have unused rows
+    from coachwhip_b200 import _lib
+    from coachwhip_b200.ep import EpComm, LibraryExpertParallelMoe
+
+    s = SPECS[name]
+    L = build_cpu(s)
+    T = 96
+    x = make_input(s, T)
+    comm = EpComm(0, 1, 0, share=lambda b: b)
+    moe = LibraryExpertParallelMoe(gpu_engine(L, 1, 0, 0, mode), comm, T + 37)
+    taps = {}
+    out = moe.forward(torch.from_numpy(x).cuda()[None], taps=taps)[0].cpu().numpy()
+    _lib.status(0)
+    ref = O.moe_forward(L, x, mode)
+    assert np.array_equal(taps["ids"].cpu().numpy().astype(np.uint32), ref["ids"])
+    assert rel_l2(out, ref["out"]) < RTOL
+    # a second call with fewer tokens reuses the buffers; nothing of the first call shows through
+    out2 = moe.forward(torch.from_numpy(x[:40]).cuda()[None])[0].cpu().numpy()
+    _lib.status(0)
+    assert rel_l2(out2, O.moe_forward(L, x[:40], mode)["out"]) < RTOL
+    comm.close()
+
+
+def test_ep_forward_refuses_tokens_above_capacity():
+    import ctypes
+
+    from coachwhip_b200 import CwxError, _lib
+    from coachwhip_b200.ep import EpComm
+
+    s = SPECS["q4k"]
+    L = build_cpu(s)
+    eng = gpu_engine(L, 1, 0, 0, O.MODE_F32)
+    comm = EpComm(0, 1, 0, share=lambda b: b)
+    x = torch.zeros((8, s.hidden), device="cuda")
+    out = torch.empty_like(x)
+    with pytest.raises(CwxError, match="capacity"):
+        _lib.check(_lib.lib().cwx_ep_forward(_lib.ctx(0), comm.handle, ctypes.byref(eng._layer),
+                                             ctypes.byref(eng._group), x.data_ptr(), 8, 4, None, out.data_ptr(),
+                                             None, None))
+    comm.close()
+
+
+def _lib_rank(rank, world, port, q):
+    import torch.distributed as dist
+
+    from coachwhip_b200 import _lib
+    from coachwhip_b200.ep import EpComm, LibraryExpertParallelMoe
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        s = SPECS["iq_mix"]
+        L = build_cpu(s)
+        x = make_input(s, 228)
+        lo, hi = (0, 128) if rank == 0 else (128, 228)  # uneven token counts, capacity 128
+        comm = EpComm(rank, world, rank)
+        moe = LibraryExpertParallelMoe(gpu_engine(L, world, rank, rank, O.MODE_F32), comm, 128)
+        xl = torch.from_numpy(np.ascontiguousarray(x[lo:hi])).cuda(rank)
+        out = moe.forward(xl[None])[0].cpu().numpy()
+        _lib.status(rank)
+        want = O.moe_forward(L, x, O.MODE_F32)["out"][lo:hi]
+        q.put((rank, rel_l2(out, want)))
+        comm.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two devices")
+def test_ep_forward_two_ranks_nccl():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_lib_rank, args=(r, 2, 29643, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
+    res = dict(q.get(timeout=5) for _ in range(2))
+    assert max(res.values()) < RTOL, res
