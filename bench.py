@@ -721,9 +721,12 @@ def main():
                     "unique_experts_mean": float(np.mean(us)),
                     "hbm_gbs_expert_bytes": expert / (ms / 1e3) / 1e9,
                     "hbm_frac_expert_bytes": expert / (ms / 1e3) / 1e9 / pk["hbm_gbs"],
-                    "k_gemv_ms_per_pass": gemv_ms, "k_gemv_share": gemv_ms / ms,
-                    "k_gemv_hbm_frac": alg / (gemv_ms / 1e3) / 1e9 / pk["hbm_gbs"],
                     "phase_ms_per_pass": ph}
+        if gemv_ms > 0:  # the grouped products (the fused decode layer has no separate product launches)
+            sweep[T].update({"k_gemv_ms_per_pass": gemv_ms, "k_gemv_share": gemv_ms / ms,
+                             "k_gemv_hbm_frac": alg / (gemv_ms / 1e3) / 1e9 / pk["hbm_gbs"]})
+        if ph.get("decode_fused", 0) > 0:
+            sweep[T]["path"] = "fused decode layer (k_decode_layer, one cooperative launch per layer)"
         print(f"[bench] batch {T}: {ms:.3f} ms/pass, {sweep[T]['tokens_per_s']:.1f} tokens/s, "
               f"{np.mean(us):.1f} experts/layer, expert bytes {sweep[T]['hbm_frac_expert_bytes']:.3f} of HBM",
               file=sys.stderr, flush=True)

@@ -26,10 +26,10 @@ EXPORTS = [
     "cwx_ep_rows_f16", "cwx_ctx_check_wait", "cwx_gguf_open", "cwx_gguf_close", "cwx_gguf_info",
     "cwx_gguf_tensor_info", "cwx_gguf_tensor", "cwx_bank_from_gguf", "cwx_gguf_tensor_f32", "cwx_gguf_meta_int",
     "cwx_gguf_meta_f64", "cwx_gguf_meta_str", "cwx_add_rms_norm", "cwx_ep_unique_id", "cwx_ep_comm_create",
-    "cwx_ep_comm_wrap", "cwx_ep_comm_abort", "cwx_ep_comm_destroy", "cwx_ep_forward",
+    "cwx_ep_comm_wrap", "cwx_ep_comm_abort", "cwx_ep_comm_destroy", "cwx_ep_forward", "cwx_ctx_set_fused_decode",
 ]
 PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine", "ep_dispatch", "ep_exchange",
-          "ep_experts", "ep_return", "ep_combine"]
+          "ep_experts", "ep_return", "ep_combine", "decode_fused"]
 
 
 class CwxError(RuntimeError):
@@ -128,6 +128,7 @@ def lib() -> ctypes.CDLL:
             "cwx_gguf_meta_int": (I32, [P, ctypes.c_char_p, P]),
             "cwx_gguf_meta_f64": (I32, [P, ctypes.c_char_p, P]),
             "cwx_gguf_meta_str": (I32, [P, ctypes.c_char_p, P, I64, P]),
+            "cwx_ctx_set_fused_decode": (I32, [P, I32]),
             "cwx_ep_unique_id": (I32, [P, I64]),
             "cwx_ep_comm_create": (I32, [I32, P, I32, I32, PP]),
             "cwx_ep_comm_wrap": (I32, [P, I32, I32, I32, PP]),
@@ -171,6 +172,11 @@ def status(device: int, stream: int | None = None) -> None:
 def set_mma_min_pile(device: int, min_pile: int) -> None:
     """Average picks per expert from which IQ layers use the tensor-core products (0: never)."""
     check(lib().cwx_ctx_set_mma_min_pile(ctx(device), min_pile))
+
+
+def set_fused_decode(device: int, max_tokens: int) -> None:
+    """Batches up to max_tokens take the fused decode layer where it applies (0: never)."""
+    check(lib().cwx_ctx_set_fused_decode(ctx(device), max_tokens))
 
 
 def read_profile(device: int) -> tuple[list[float], list[int]]:

@@ -17,10 +17,9 @@
 // products sum code x weight per piece and scale the sum by d once.
 #include "cwx_common.cuh"
 #include "kernels.cuh"
+#include "products.cuh"
 
 namespace cwx {
-
-__device__ __forceinline__ float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
 
 // One warp per (row, 256 columns); lane l takes columns 8l..8l+7 of the block. Up to two
 // independent preparations per launch (blockIdx.y picks one).
@@ -63,84 +62,7 @@ __global__ void __launch_bounds__(256) k_prep(PrepPair pp) {
             }
         }
     }
-    if (p.mode == AM_Q8_K) {
-        // max |x| with the lowest index among equals, and the signed value there
-        float am = -1.f, mv = 0.f;
-        int ai = 1 << 30;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float f = fabsf(v[j]);
-            if (f > am) {
-                am = f;
-                ai = k0 + j;
-                mv = v[j];
-            }
-        }
-        for (int o = 16; o > 0; o >>= 1) {
-            const float oa = __shfl_xor_sync(0xffffffffu, am, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, ai, o);
-            const float ov = __shfl_xor_sync(0xffffffffu, mv, o);
-            if (oa > am || (oa == am && oi < ai)) {
-                am = oa;
-                ai = oi;
-                mv = ov;
-            }
-        }
-        float d = 0.f;
-        if (am == 0.f) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = 0.f;
-        } else {
-            const float iscale = __fdiv_rn(-127.f, mv);
-            d = __fdiv_rn(1.0f, iscale);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                float qv = roundf(__fmul_rn(iscale, v[j]));
-                v[j] = fminf(fmaxf(qv, -128.f), 127.f);
-            }
-        }
-        uint32_t hi[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-            hi[j] = *reinterpret_cast<const uint32_t*>(&h);
-        }
-        const int c = k0 >> 6, ss = (k0 >> 4) & 3, q = (k0 >> 3) & 1;
-        uint8_t* piece = p.out + r * packed_row_bytes(p.K) + b * 1024;
-        const int ch = (ss * 2 + q) * 4 + c;
-        *reinterpret_cast<uint4*>(piece + 16 * ch) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(piece + 512 + 16 * ch) = make_uint4(ch == 0 ? __float_as_uint(d) : 0u, 0u, 0u, 0u);
-        return;
-    } else if (p.mode == AM_Q8_0) {
-        // 32-column blocks: lanes 4i..4i+3 hold block i
-        float am = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(v[j]));
-        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-        const float d = __fdiv_rn(am, 127.f);
-        const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
-        const float dh = __half2float(__float2half_rn(d));
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float qv = roundf(__fmul_rn(v[j], id));
-            qv = fminf(fmaxf(qv, -128.f), 127.f);
-            v[j] = __fmul_rn(qv, dh);
-        }
-    }
-    uint32_t hi[4], lo[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-        const float2 hf = __half22float2(h);
-        const __half2 l = __floats2half2_rn(__fsub_rn(v[2 * j], hf.x), __fsub_rn(v[2 * j + 1], hf.y));
-        hi[j] = *reinterpret_cast<const uint32_t*>(&h);
-        lo[j] = *reinterpret_cast<const uint32_t*>(&l);
-    }
-    const int c = k0 >> 6, ss = (k0 >> 4) & 3, q = (k0 >> 3) & 1;
-    uint8_t* piece = p.out + r * packed_row_bytes(p.K) + b * 1024;
-    *reinterpret_cast<uint4*>(piece + 16 * ((ss * 2 + q) * 4 + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4*>(piece + 512 + 16 * ((ss * 2 + q) * 4 + c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    pack_piece(p.mode, v, p.out + r * packed_row_bytes(p.K) + b * 1024, lane);
 }
 
 // acc + sum_j w[t][j] * rows[pick j][c .. c+3] in pick order; the rows of up to 8 picks are
@@ -230,52 +152,6 @@ __global__ void __launch_bounds__(256) k_combine4(const float* __restrict__ rows
 // the warps in order), then rounded once: at least as accurate as the reference's f32 sums (a
 // left-to-right sum on the CPU, a tree in the Metal kernel), so the outputs agree with either to
 // the rounding of the reference's own sum. sqrt and the divide are correctly rounded, as in Rust.
-constexpr int NORM_THREADS = 256;
-
-__device__ __forceinline__ double norm_block_sum(double v, double* red) {
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    const int warp = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) red[warp] = v;
-    __syncthreads();
-    double s = red[0];
-#pragma unroll
-    for (int w = 1; w < NORM_THREADS / 32; ++w) s += red[w];
-    return s;
-}
-
-__device__ __forceinline__ double sq4(float4 v) {
-    double s = (double)v.x * (double)v.x;
-    s += (double)v.y * (double)v.y;
-    s += (double)v.z * (double)v.z;
-    s += (double)v.w * (double)v.w;
-    return s;
-}
-
-// Second pass over a summed row (this thread's own writes): out = v / m * alpha.
-__device__ __forceinline__ void norm_row(double ss, const float* __restrict__ sum, const float* __restrict__ alpha,
-                                         float eps, int H, bool vec, float* __restrict__ out) {
-    __shared__ double red[NORM_THREADS / 32];
-    const double tot = norm_block_sum(ss, red);
-    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn((float)tot, (float)H), eps));
-    const int nq = (H + 3) / 4;
-    for (int q = threadIdx.x; q < nq; q += NORM_THREADS) {
-        if (vec) {
-            const float4 v = *reinterpret_cast<const float4*>(sum + 4 * q);
-            const float4 al = __ldg(reinterpret_cast<const float4*>(alpha) + q);
-            float4 r;
-            r.x = __fmul_rn(__fdiv_rn(v.x, m), al.x);
-            r.y = __fmul_rn(__fdiv_rn(v.y, m), al.y);
-            r.z = __fmul_rn(__fdiv_rn(v.z, m), al.z);
-            r.w = __fmul_rn(__fdiv_rn(v.w, m), al.w);
-            *reinterpret_cast<float4*>(out + 4 * q) = r;
-        } else {
-            for (int j = 0; j < 4 && 4 * q + j < H; ++j)
-                out[4 * q + j] = __fmul_rn(__fdiv_rn(sum[4 * q + j], m), __ldg(alpha + 4 * q + j));
-        }
-    }
-}
-
-// (a, b or c may be the sum buffer itself: each element is read before the same thread writes it)
 __global__ void __launch_bounds__(NORM_THREADS) k_add_norm(const float* a, const float* b, const float* c,
                                                           const float* __restrict__ alpha, float eps, int H, int vec,
                                                           float* sum, float* out) {

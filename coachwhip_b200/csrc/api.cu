@@ -308,10 +308,11 @@ extern "C" int cwx_ctx_create(int device, cwx_ctx** out) {
     memset(c, 0, sizeof *c);
     c->device = device;
     c->mma_min_pile = 32;
+    c->fused_max_tokens = DL_MAX_T;
     c->prof = new ProfLog();
     cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
-    cudaError_t e = cudaMalloc(&c->d_err, 16);
-    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, 16);
+    cudaError_t e = cudaMalloc(&c->d_err, 64);
+    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, 64);
     if (e != cudaSuccess) {
         delete static_cast<ProfLog*>(c->prof);
         delete c;
@@ -359,6 +360,13 @@ extern "C" int cwx_ctx_set_mma_min_pile(cwx_ctx* c, int min_pile) {
     return CWX_OK;
 }
 
+extern "C" int cwx_ctx_set_fused_decode(cwx_ctx* c, int max_tokens) {
+    if (!c) return fail(CWX_EINVAL, "cwx_ctx_set_fused_decode: null context");
+    if (max_tokens < 0) return fail(CWX_EINVAL, "cwx_ctx_set_fused_decode: %d is negative", max_tokens);
+    c->fused_max_tokens = max_tokens;
+    return CWX_OK;
+}
+
 extern "C" int cwx_ctx_set_profiling(cwx_ctx* c, int enabled) {
     if (!c) return fail(CWX_EINVAL, "cwx_ctx_set_profiling: null context");
     c->profiling = enabled ? 1 : 0;
@@ -387,7 +395,7 @@ extern "C" int cwx_ctx_status(cwx_ctx* c, void* stream) {
     int h = 0;
     CWX_CUDA(cudaMemcpy(&h, c->d_err, 4, cudaMemcpyDeviceToHost));
     if (h == DE_OK) return CWX_OK;
-    CWX_CUDA(cudaMemset(c->d_err, 0, 4));
+    CWX_CUDA(cudaMemset(c->d_err, 0, 64));  // (a timed-out grid barrier leaves its counter off step)
     if (h == DE_TIMEOUT) return fail(CWX_ETIMEOUT, "a device-side wait gave up (bulk copy did not complete)");
     if (h == DE_BAD_ID) return fail(CWX_EDEVICE, "an expert id was out of range");
     return fail(CWX_EDEVICE, "device error %d", h);
@@ -726,6 +734,87 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
     return CWX_OK;
 }
 
+// Whether a call takes the fused decode layer (decode_layer.cu): a small batch of a layer whose
+// banks and shapes it handles.
+static bool fused_layer(const cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, int T) {
+    if (c->fused_max_tokens <= 0 || T < 1 || T > c->fused_max_tokens || T > DL_MAX_T) return false;
+    if ((int64_t)T * L->top_k > DL_MAX_PICKS || L->act != CWX_ACT_SILU) return false;
+    if (L->n_experts > DL_MAX_E || L->hidden % 256 || L->hidden > DL_MAX_H || L->inter % 256 ||
+        L->inter > DL_MAX_I)
+        return false;
+    if (L->gate->L.fmt != L->up->L.fmt || !decode_fused_formats(L->gate->L.fmt, L->down->L.fmt)) return false;
+    if ((((uintptr_t)A->x) | ((uintptr_t)L->router_w)) & 15) return false;
+    if (L->sh_gate) {
+        const Layout &g = L->sh_gate->L, &u = L->sh_up->L, &d = L->sh_down->L;
+        if (g.fmt != F_Q4_K || u.fmt != F_Q4_K || d.fmt != F_Q4_K || g.n % 256 || g.n > DL_MAX_I) return false;
+        if (act_mode_of(L->sh_gate, L->act_mode) != act_mode_of(L->sh_down, L->act_mode)) return false;
+    }
+    return true;
+}
+
+// The whole layer in one launch of the fused decode layer.
+static int moe_fused(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, cudaStream_t st) {
+    const int T = A->tokens, H = L->hidden, E = L->n_experts, K = L->top_k, I = L->inter;
+    const int Is = L->sh_gate ? (int)L->sh_gate->L.n : 0;
+    const bool qint = L->sh_gate && act_mode_of(L->sh_gate, L->act_mode) == AM_Q8_K;
+    (void)H;
+    Carve sz{nullptr, 0};
+    for (int pass = 0; pass < 2; ++pass) {
+        if (pass) {
+            int rc = ensure_ws(c, sz.off + 256, st);
+            if (rc) return rc;
+        }
+        Carve w{pass ? c->ws : nullptr, 0};
+        DecodeArgs a;
+        memset(&a, 0, sizeof a);
+        a.logits = w.take<float>((size_t)T * (E + 1));  // + the shared expert's gates
+        a.hpk = w.take<uint8_t>((size_t)((int64_t)T * K * (I / 256) * 512));
+        a.hs = Is ? w.take<float>((size_t)T * Is) : nullptr;
+        if (!pass) {
+            sz = w;
+            continue;
+        }
+        a.x = A->x;
+        a.residual = A->residual;
+        a.out = A->out;
+        a.norm_w = A->norm_w;
+        a.norm_eps = A->norm_eps;
+        a.norm_out = A->norm_out;
+        a.norm_vec = ((((uintptr_t)A->out) | ((uintptr_t)A->norm_w) | ((uintptr_t)A->norm_out)) & 15) == 0;
+        a.T = T;
+        a.H = H;
+        a.E = E;
+        a.K = K;
+        a.I = I;
+        a.Is = Is;
+        a.norm = L->norm_topk_prob;
+        a.router_w = L->router_w;
+        a.router_b = L->router_b;
+        a.gate = mref(L->gate);
+        a.up = mref(L->up);
+        a.down = mref(L->down);
+        if (L->sh_gate) {
+            a.sg = mref(L->sh_gate);
+            a.su = mref(L->sh_up);
+            a.sd = mref(L->sh_down);
+            a.sg_inp = L->sh_gate_inp;
+        }
+        a.sh_qint = qint ? 1 : 0;
+        a.err = c->d_err;
+        a.bar = reinterpret_cast<unsigned long long*>(c->d_err + 8);
+        a.ids_out = A->ids_out;
+        a.w_out = A->weights_out;
+        a.pairs_out = A->pairs_out;
+        a.heads_out = A->heads_out;
+        PhaseTimer t(c, st, CWX_PHASE_DECODE_FUSED);
+        int rc = launch_decode_layer(a, c->device, c->sm_count, st);
+        if (rc) return rc;
+        t.end();
+        c->launches += 1;
+    }
+    return CWX_OK;
+}
+
 extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, void* stream) {
     if (!c || !A) return fail(CWX_EINVAL, "cwx_moe_forward: null argument");
     int rc = validate_layer(L);
@@ -738,6 +827,7 @@ extern "C" int cwx_moe_forward(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe
         return fail(CWX_EINVAL, "cwx_moe_forward: norm_w needs a norm_out buffer of its own");
     CWX_CUDA(cudaSetDevice(c->device));
     cudaStream_t st = (cudaStream_t)stream;
+    if (fused_layer(c, L, A, T)) return moe_fused(c, L, A, st);
     LayerPlan p;
     const int mma = mma_layer(c, L, T) ? 1 : 0;
     plan_layer(L, T, mma, nullptr, &p);

@@ -226,7 +226,7 @@ struct cwx_ctx {
     int sm_count;
     uint8_t* ws;  // workspace
     size_t ws_bytes;
-    int* d_err;   // device error word (first error code wins)
+    int* d_err;   // device error word (first error code wins); d_err + 8: grid barrier words of the fused decode layer
     int* h_err;   // pinned mirror
     uint16_t* d_iq3s_map;  // encoder maps for synthetic banks (built on first use)
     uint16_t* d_iq2s_map;
@@ -236,6 +236,7 @@ struct cwx_ctx {
     void* prof;        // recorded (phase, start, end) events
     int64_t launches;  // kernel launches issued through this context
     int mma_min_pile;  // average picks per expert from which IQ layers take the tensor-core products (0: never)
+    int fused_max_tokens;  // batches up to this size take the fused decode layer when it applies (0: never)
     cudaStream_t side;  // forked work inside a layer (created on first use)
     cudaEvent_t ev_fork, ev_join;
 };

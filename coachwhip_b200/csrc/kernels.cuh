@@ -120,6 +120,46 @@ int ep_comm_exchange(cwx_ep_comm* c, int nbuf, const void* const* send, void* co
 // experts_est: the number of experts expected to have picks (sizes the grid and the K split).
 int launch_gemv(const GemvArgs& a, int64_t experts_est, int device, int sm_count, cudaStream_t st);
 
+// The fused decode layer (decode_layer.cu): the whole layer of a small batch in one cooperative
+// launch (router, route, piles, gate/up with the SiLU, down, combine), phases separated by two
+// bounded grid-wide barriers.
+constexpr int DL_MAX_T = 4;        // tokens
+constexpr int DL_MAX_PICKS = 32;   // tokens x top_k
+constexpr int DL_MAX_E = 512;      // routed experts
+constexpr int DL_MAX_H = 2048;     // hidden (a multiple of 1024)
+constexpr int DL_MAX_I = 1024;     // expert and shared intermediate
+struct DecodeArgs {
+    const float* x;         // (T, H)
+    const float* residual;  // (T, H) or null
+    float* out;             // (T, H)
+    const float* norm_w;    // (H) the next layer's RMSNorm fused after the combine, or null
+    float norm_eps;
+    float* norm_out;        // (T, H)
+    int norm_vec;           // out, norm_w and norm_out 16-byte aligned
+    int T, H, E, K, I, Is, norm;
+    const float* router_w;
+    const float* router_b;
+    MatRef gate, up, down;  // routed banks (IQ formats)
+    MatRef sg, su, sd;      // shared expert (Q4_K) or base == null
+    const float* sg_inp;
+    int sh_qint;            // shared products on Q8_K activation codes (candle policy), else f16
+    // workspace
+    float* logits;          // (T, E)
+    uint8_t* hpk;           // (T * K) hidden rows per pick: f16 (hi parts) in the packed order, 512 B per piece
+    float* hs;              // (T, Is) shared hidden rows
+    unsigned long long* bar;  // grid barrier counter: arrivals since it was zeroed (context creation, or
+                              // a status read after a device error)
+    int* err;
+    // optional taps
+    uint32_t* ids_out;
+    float* w_out;
+    uint32_t* pairs_out;
+    uint32_t* heads_out;
+};
+// Whether the fused layer has an instantiation for these routed formats.
+bool decode_fused_formats(int gate_fmt, int down_fmt);
+int launch_decode_layer(const DecodeArgs& a, int device, int sm_count, cudaStream_t st);
+
 // Tensor-core (tcgen05) expert products for large piles (mma.cu).
 struct MmaArgs {
     MatRef a0, a1;       // weights; a1: the up matrix of a fused gate/up launch

@@ -18,28 +18,11 @@
 // tiled form with operand reuse for prefill-sized batches).
 #include "cwx_common.cuh"
 #include "kernels.cuh"
+#include "products.cuh"
 
 namespace cwx {
 
-__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
-
 constexpr int SGATE_SMEM = 4096;  // hidden sizes up to this stage the shared gate's products
-
-// candle's AVX order for a sum whose 32-element steps live one per lane: lane L holds the sum of
-// elements 32*s + L over the whole steps, in step order. Returns the reduced value in all lanes.
-__device__ __forceinline__ float avx_lane_tree(float acc) {
-    float b = __shfl_down_sync(0xffffffffu, acc, 8);
-    float c = __shfl_down_sync(0xffffffffu, acc, 16);
-    float d = __shfl_down_sync(0xffffffffu, acc, 24);
-    float X = __fadd_rn(__fadd_rn(acc, b), __fadd_rn(c, d));  // valid in lanes 0..7
-    float X4 = __shfl_down_sync(0xffffffffu, X, 4);
-    float t0 = __fadd_rn(X, X4);  // valid in lanes 0..3
-    float t1 = __shfl_down_sync(0xffffffffu, t0, 1);
-    float t2 = __shfl_down_sync(0xffffffffu, t0, 2);
-    float t3 = __shfl_down_sync(0xffffffffu, t0, 3);
-    float r = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
-    return __shfl_sync(0xffffffffu, r, 0);
-}
 
 // Router logits on the FP64 tensor cores: block = 8 warps on a tile of 8 experts x 8 tokens,
 // warp w taking the w-th eighth of K; each warp accumulates its slice with mma m8n8k4 f64 (the

@@ -315,13 +315,22 @@ int cwx_ep_forward(cwx_ctx* ctx, cwx_ep_comm* comm, const cwx_moe_layer* layer, 
 #define CWX_PHASE_EP_EXPERTS 9   /* this rank's experts over the received records, unit sums */
 #define CWX_PHASE_EP_RETURN 10   /* the unit sums back to their sources (NCCL) */
 #define CWX_PHASE_EP_COMBINE 11  /* shared expert on the local tokens, combine, residual */
-#define CWX_N_PHASES 12
+#define CWX_PHASE_DECODE_FUSED 12 /* the fused decode layer (every phase of a small batch in one launch) */
+#define CWX_N_PHASES 13
 int cwx_ctx_set_profiling(cwx_ctx* ctx, int enabled);
 /* Layers whose routed banks are all IQ2_S / IQ3_S (SiLU, hidden and inter multiples of 256) run
  * their routed products on the tensor cores (tcgen05) when the batch gives at least min_pile
  * picks per expert on average (tokens * top_k / n_experts, rounded up); smaller batches use the
  * grouped mma.sync products. Default 32; 0 keeps every batch on the mma.sync products. */
 int cwx_ctx_set_mma_min_pile(cwx_ctx* ctx, int min_pile);
+/* Batches of up to max_tokens tokens (at most 4, and tokens * top_k <= 32) run the whole layer as
+ * one cooperative launch (router, route, piles, gate/up with SiLU, down, combine; phases separated
+ * by grid-wide barriers whose waits are bounded) when the layer allows it: SiLU, routed banks
+ * IQ2_S gate/up with IQ3_S down (or IQ3_S / IQ2_S, IQ2_XXS / IQ3_XXS, IQ3_XXS / IQ2_XXS), hidden a
+ * multiple of 256 up to 2048, inter and the shared expert's a multiple of 256 up to 1024, at most
+ * 512 experts, a Q4_K shared expert or none (a fused RMSNorm is included). Default 4; 0 turns it off. Same
+ * results as the general path within f32 rounding (ids, weights and piles identical). */
+int cwx_ctx_set_fused_decode(cwx_ctx* ctx, int max_tokens);
 /* Synchronises the device; adds each recorded phase's elapsed milliseconds into ms[phase] and
  * its occurrences into count[phase] (arrays of CWX_N_PHASES; either may be NULL); keeps the
  * recorded events, so a replayed graph can be read again after each replay. */
