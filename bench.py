@@ -454,7 +454,7 @@ def prefill_runs(cfg, mods, Ts, a, dev, local, pk, fp8, maxall, barrier, world):
     return out
 
 
-def c3_runs(world, rank, local, a, pk, maxall, barrier):
+def c3_runs(world, rank, local, a, pk, maxall, barrier, fp8=None):
     """Config 3: decode batches 1 and 64 and prefill of 4096 tokens on one GPU (36-layer stack as
     CUDA graphs); on N ranks the 4096-token prefill expert-parallel (128 / N experts per rank)."""
     import numpy as np
@@ -559,7 +559,11 @@ def c3_runs(world, rank, local, a, pk, maxall, barrier):
     fl = nl * cfg.flops(T)
     res["prefill"] = {"tokens": T, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
                       "tflops": fl / (ms / 1e3) / 1e12, "frac_fp8_nominal": fl / (ms / 1e3) / 1e12 / FP8_NOMINAL_TFLOPS,
-                      "path": "grouped mma.sync products (MXFP4 is not a tensor-core (tcgen05) format here)"}
+                      "path": ("tcgen05 grouped products (k_mma<MXFP4>: weights decoded to f16 A tiles, exact for "
+                               "banks whose block scales lie in [104, 140]; activations as f16 hi + lo under the "
+                               "Q8_0 policy; clamped-SwiGLU and bias epilogues)")}
+    if fp8 and fp8.get("tflops"):
+        res["prefill"]["frac_fp8_measured"] = res["prefill"]["tflops"] / fp8["tflops"]
     print(f"[bench] config 3 prefill {T}: {ms:.3f} ms/step", file=sys.stderr, flush=True)
     _lib.status(local)
     return res
@@ -787,7 +791,7 @@ def main():
     # path's semantics, checked against the O2 oracle); routed and shared products on the tensor cores
     from coachwhip_b200.moe import StreamedMoe
 
-    fp8 = fp8_peak(dev) if prefill_T else None
+    fp8 = fp8_peak(dev) if (prefill_T or not a.no_c3) else None
     prefill = None
     if prefill_T:
         mods_f32 = [StreamedMoe(m.layer, m.gate, m.top_k, True, m.act, store, shared=m.shared,
@@ -801,7 +805,7 @@ def main():
     torch.cuda.empty_cache()
     c3 = None
     if not a.no_c3:
-        c3 = c3_runs(world, rank, local, a, pk, maxall, barrier)
+        c3 = c3_runs(world, rank, local, a, pk, maxall, barrier, fp8)
         torch.cuda.empty_cache()
     ep = None
     if not a.no_ep:

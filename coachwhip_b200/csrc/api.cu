@@ -136,6 +136,7 @@ struct LayerPlan {
     int mma;           // routed products on the tensor cores (IQ banks, large piles)
     int sh_mma;        // the shared expert on the tensor cores too (f32 activations)
     __half* x16;       // (T, H) f16 rows of x
+    __half* x16lo;     // (T, H) their lo parts (MXFP4 under the Q8_0 policy), or null
     __half* h16;       // (n, I) f16 hidden rows per pick
     __half* hs16;      // (T, Is) f16 hidden rows of the shared expert
     uint32_t* spairs;  // the shared expert's pile (every token) and used list
@@ -162,20 +163,25 @@ static bool shared_mma_ok(const cwx_moe_layer* L) {
     return g.n % 256 == 0 && L->hidden % 256 == 0;
 }
 
-// Whether a layer's routed products run on the tensor cores: IQ banks (f32 activations
-// under every policy), SiLU, whole 256-column pieces, and piles large enough on average.
+// Whether a layer's routed products run on the tensor cores: IQ banks (f32 activations under
+// every policy), Q4_K under the f32 policy, MXFP4 banks whose weights are exact in f16 (f32, or
+// Q8_0 rounded activations); SiLU or the clamped SwiGLU; piles large enough on average.
 static bool mma_layer(const cwx_ctx* c, const cwx_moe_layer* L, int T) {
-    if (!c || c->mma_min_pile <= 0 || L->act != CWX_ACT_SILU) return false;
+    if (!c || c->mma_min_pile <= 0) return false;
+    if (L->act != CWX_ACT_SILU && L->act != CWX_ACT_CLAMPED_SWIGLU) return false;
     const int64_t pile = ((int64_t)T * L->top_k + L->n_experts - 1) / L->n_experts;
     if (pile < c->mma_min_pile) return false;
     const cwx_bank* bs[3] = {L->gate, L->up, L->down};
     for (const cwx_bank* b : bs) {
         const int f = b->L.fmt;
         // Q4_K only with f32 activations (its Q8_K codes carry a per-piece, per-token scale)
-        if (!iq_format(f) && !(f == F_Q4_K && act_mode_of(b, L->act_mode) == AM_F32)) return false;
+        if (!iq_format(f) && !(f == F_Q4_K && act_mode_of(b, L->act_mode) == AM_F32) && !(f == F_MXFP4 && b->mx_f16))
+            return false;
     }
     if (L->gate->L.fmt != L->up->L.fmt) return false;
-    return L->hidden % 256 == 0 && L->inter % 256 == 0;
+    // whole 256-column pieces, or (MXFP4) a tail of whole 64-column stages; 64-row tiles
+    const int kq = L->gate->L.fmt == F_MXFP4 ? 64 : 256, kd = L->down->L.fmt == F_MXFP4 ? 64 : 256;
+    return L->hidden % kq == 0 && L->inter % kd == 0 && L->hidden % 64 == 0 && L->inter % 64 == 0;
 }
 
 static int validate_layer(const cwx_moe_layer* L) {
@@ -249,6 +255,7 @@ static void plan_layer(const cwx_moe_layer* L, int T, int mma, uint8_t* base, La
     p->mma = mma;
     p->sh_mma = sh_mma;
     p->x16 = mma ? c.take<__half>((size_t)T * p->H) : nullptr;
+    p->x16lo = mma && p->mgu == AM_Q8_0 ? c.take<__half>((size_t)T * p->H) : nullptr;
     p->h16 = mma ? c.take<__half>((size_t)n * p->I) : nullptr;
     p->hs16 = sh_mma ? c.take<__half>((size_t)T * p->Is) : nullptr;
     p->spairs = sh_mma ? c.take<uint32_t>((size_t)T + 1) : nullptr;
@@ -642,7 +649,12 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
     int rc;
     {
         PhaseTimer t(c, st, CWX_PHASE_PREP);
-        if ((rc = launch_f16rows(A->x, p.xrows * H, p.x16, st))) return rc;
+        // (Q8_0 policy, MXFP4: the rows through Q8_0 first, as the reference's vec_dot_type, kept
+        // exactly as hi + lo: h goes through Q8_0 again, whose rounding an f16-only product would
+        // flip for some elements)
+        if ((rc = p.mgu == AM_Q8_0 ? launch_f16rows_q80(A->x, p.xrows * H, p.x16, p.x16lo, st)
+                                   : launch_f16rows(A->x, p.xrows * H, p.x16, st)))
+            return rc;
         c->launches += 1;
         if (shared && !p.sh_mma) {
             if ((rc = launch_prep(prep(A->x, nullptr, T, H, p.msgu, p.xpk[p.msgu]), st))) return rc;
@@ -667,12 +679,21 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
         g.a1 = mref(L->up);
         g.fused = 1;
         g.b = reinterpret_cast<const uint8_t*>(p.x16);
+        g.blo = reinterpret_cast<const uint8_t*>(p.x16lo);
         g.bstride = (int64_t)H * 2;
         g.bdiv = K;
         g.rowmap = p.rowmap;
         g.brows = p.xrows;
         g.hout = p.h16;
         g.ostride = I;
+        g.act = L->act;
+        g.alpha = L->alpha;
+        g.limit = L->limit;
+        if (L->act == CWX_ACT_CLAMPED_SWIGLU) {
+            g.gate_b = L->gate_b;
+            g.up_b = L->up_b;
+        }
+        g.h_q80 = p.md == AM_Q8_0;
         if ((rc = launch_mma(g, c->device, c->sm_count, st))) return rc;
         c->launches += 1;
         if (p.sh_mma) {
@@ -685,6 +706,10 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
             sg.bdiv = 1;
             sg.hout = p.hs16;
             sg.ostride = Is;
+            sg.blo = nullptr;
+            sg.act = CWX_ACT_SILU;
+            sg.gate_b = sg.up_b = nullptr;
+            sg.h_q80 = 0;
             if ((rc = launch_mma(sg, c->device, c->sm_count, st))) return rc;
             c->launches += 1;
         } else if (shared) {
@@ -705,11 +730,13 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
         d.a0 = mref(L->down);
         d.fused = 0;
         d.b = reinterpret_cast<const uint8_t*>(p.h16);
+        d.blo = nullptr;
         d.bstride = (int64_t)I * 2;
         d.brows = (int64_t)T * K;
         d.bdiv = 1;
         d.out = p.y;
         d.ostride = H;
+        d.bias = L->act == CWX_ACT_CLAMPED_SWIGLU ? L->down_b : nullptr;
         if ((rc = launch_mma(d, c->device, c->sm_count, st))) return rc;
         c->launches += 1;
         if (p.sh_mma) {
@@ -723,6 +750,7 @@ static int moe_mma(cwx_ctx* c, const cwx_moe_layer* L, const cwx_moe_args* A, co
             sd.brows = T;
             sd.out = p.ys;
             sd.ostride = H;
+            sd.bias = nullptr;
             if ((rc = launch_mma(sd, c->device, c->sm_count, st))) return rc;
             c->launches += 1;
         } else if (shared) {

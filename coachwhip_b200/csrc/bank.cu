@@ -415,29 +415,34 @@ static int supported_type(int t) {
            t == F_IQ2_XXS || t == F_IQ3_XXS || t == F_IQ4_XS;
 }
 
-// MXFP4 banks: whether any row's whole 256-column piece has block scales e more than 24 apart
-// (one thread per (expert, row, piece); the piece's 8 scale bytes are contiguous in the tiled
-// layout).
+// MXFP4 banks, one thread per (expert, row, piece): bit 0 of flag when a whole 256-column piece
+// has block scales e more than 24 apart (the grouped products' f16 fast path), bit 1 when any
+// block scale lies outside [104, 140] (the tensor-core products need every weight exact in f16).
+constexpr int MX_F16_MIN = 104, MX_F16_MAX = 140;
 __global__ void k_mx_spread(const uint8_t* __restrict__ d, Layout L, int64_t ne, int* flag) {
-    const int full = L.last_kp_row_bytes == L.kp_row_bytes ? L.n_kp : L.n_kp - 1;
-    const int64_t per_e = L.n * full;
+    const int64_t per_e = L.n * L.n_kp;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (full <= 0 || i >= ne * per_e) return;
-    const int64_t e = i / per_e, rem = i % per_e, r = rem / full;
-    const int kp = (int)(rem % full);
-    const uint8_t* p = d + e * L.expert_bytes + tiled_offset(L, r / TILE_ROWS, r % TILE_ROWS, kp, 0);
+    if (i >= ne * per_e) return;
+    const int64_t e = i / per_e, rem = i % per_e, r = rem / L.n_kp;
+    const int kp = (int)(rem % L.n_kp);
+    const int nb = (int)(piece_row_bytes(L, kp) / 17);
+    const uint8_t* x = d + e * L.expert_bytes;
     int mx = 0, mn = 255;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        mx = max(mx, (int)p[j]);
-        mn = min(mn, (int)p[j]);
+    for (int b = 0; b < nb; ++b) {
+        const int v = x[tiled_offset(L, r / TILE_ROWS, r % TILE_ROWS, kp, 17 * b)];
+        mx = max(mx, v);
+        mn = min(mn, v);
     }
-    if (mx - mn > 24) atomicOr(flag, 1);
+    int f = 0;
+    if (nb == 8 && mx - mn > 24) f |= 1;
+    if (mn < MX_F16_MIN || mx > MX_F16_MAX) f |= 2;
+    if (f) atomicOr(flag, f);
 }
 
-// Sets b->mx_wide for an MXFP4 bank whose tiled bytes are on the device.
+// Sets b->mx_wide and b->mx_f16 for an MXFP4 bank whose tiled bytes are on the device.
 static int mx_check(cwx_bank* b, int64_t ne) {
     b->mx_wide = 0;
+    b->mx_f16 = 0;
     if (b->L.fmt != F_MXFP4 || ne <= 0) return CWX_OK;
     int* flag = nullptr;
     CWX_CUDA(cudaMalloc(&flag, sizeof(int)));
@@ -451,7 +456,8 @@ static int mx_check(cwx_bank* b, int64_t ne) {
     if (e == cudaSuccess) e = cudaMemcpy(&h, flag, sizeof(int), cudaMemcpyDeviceToHost);
     cudaFree(flag);
     if (e != cudaSuccess) return cuda_fail(e, "MXFP4 scale check");
-    b->mx_wide = h;
+    b->mx_wide = h & 1;
+    b->mx_f16 = (h & 2) ? 0 : 1;
     return CWX_OK;
 }
 

@@ -219,6 +219,9 @@ struct cwx_bank {
     // MXFP4: some row's 256-column piece has block scales more than 2^24 apart, beyond the f16
     // range of the grouped products' fast path (its launches take the exact path)
     int mx_wide;
+    // MXFP4: every block scale e lies in [104, 140], so every weight (code times 2^(e - 128)) is
+    // exact in f16 and the tensor-core products can take the bank
+    int mx_f16;
 };
 
 struct cwx_ctx {

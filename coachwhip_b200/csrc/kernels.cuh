@@ -165,6 +165,7 @@ struct MmaArgs {
     MatRef a0, a1;       // weights; a1: the up matrix of a fused gate/up launch
     int fused;           // 1: gate/up rows side by side, SwiGLU epilogue writing f16 h rows
     const uint8_t* b;    // activation rows (f16), bstride bytes apart
+    const uint8_t* blo;  // or null: the rows' lo parts (MXFP4 under the Q8_0 policy: x = hi + lo)
     int64_t bstride;
     int64_t brows;       // activation rows (their offsets must fit 32 bits)
     int bdiv;            // activation row = pair / bdiv
@@ -177,10 +178,21 @@ struct MmaArgs {
     int64_t ostride;     // elements between output rows
     int* err;
     int mtiles;          // row tiles per expert (set by the launcher)
+    // fused: the activation (CWX_ACT_SILU, or the clamped SwiGLU with its expert biases), and
+    // whether h goes through Q8_0 (per 32 features) before f16, as the down products' input
+    int act;
+    float alpha, limit;
+    const float* gate_b;
+    const float* up_b;
+    int h_q80;
+    const float* bias;   // plain: expert bias added to each output row (E x n), or null
 };
 bool mma_supports(const MmaArgs& a);
 int launch_mma(const MmaArgs& a, int device, int sm_count, cudaStream_t st);
 int launch_f16rows(const float* x, int64_t n, __half* y, cudaStream_t st);
+// x (rows of K, K a multiple of 32) through Q8_0 per 32 columns, then f16 (y), and the rest of
+// each value as a second f16 (ylo, when not null; y + ylo is the Q8_0 value exactly).
+int launch_f16rows_q80(const float* x, int64_t n, __half* y, __half* ylo, cudaStream_t st);
 int launch_all_tokens(uint32_t* pairs, int T, uint32_t* used3, uint32_t* n_used, cudaStream_t st);
 
 }  // namespace cwx

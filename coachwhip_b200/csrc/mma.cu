@@ -60,13 +60,15 @@ constexpr int TMEM_COLS = 512;
 // Codebook as f16 values: IQ2_S and IQ2_XXS 8 per entry, two copies (entry e of copy j at
 // e*32 + j*16, the copy picked by the lane's parity, so fewer lanes of a wavefront meet on a bank);
 // IQ3_S and IQ3_XXS 4 per entry, four copies (e*32 + j*8); the 16 IQ4_XS levels as f32, one copy
-// per lane (level n of copy j at n*128 + j*4).
+// per lane (level n of copy j at n*128 + j*4); MXFP4: nibble pair p -> the f16 pair of codes
+// (twice the e2m1 values, the reference's kvalues_mxfp4), one copy per lane (p*128 + j*4).
 template <int FMT>
 struct Tab {
     static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 32
                                  : FMT == F_IQ3_S ? 512 * 32
                                  : (FMT == F_IQ2_XXS || FMT == F_IQ3_XXS) ? 256 * 32
                                  : FMT == F_IQ4_XS ? 16 * 128
+                                 : FMT == F_MXFP4  ? 256 * 128
                                                    : 0;
 };
 
@@ -175,7 +177,9 @@ struct MItem {
     int mt;
 };
 
-__device__ __forceinline__ bool next_item(const MmaArgs& a, Iter& st, uint32_t i, uint32_t n_used, MItem* o) {
+// nmax: picks per column tile (NMAX, or NMAX / 2 when the B tiles carry hi and lo parts).
+__device__ __forceinline__ bool next_item(const MmaArgs& a, Iter& st, uint32_t i, uint32_t n_used, MItem* o,
+                                          uint32_t nmax) {
     while (st.u == 0xFFFFFFFFu || i >= st.base + st.n_items) {
         if (st.u != 0xFFFFFFFFu) st.base += st.n_items;
         st.u = st.u == 0xFFFFFFFFu ? 0 : st.u + 1;
@@ -183,16 +187,16 @@ __device__ __forceinline__ bool next_item(const MmaArgs& a, Iter& st, uint32_t i
         st.e = a.used3[3 * st.u];
         st.first = a.used3[3 * st.u + 1];
         st.count = a.used3[3 * st.u + 2];
-        st.n_items = (st.count + NMAX - 1) / NMAX * (uint32_t)a.mtiles;
+        st.n_items = (st.count + nmax - 1) / nmax * (uint32_t)a.mtiles;
     }
     const uint32_t local = i - st.base;
     const uint32_t nt = local / (uint32_t)a.mtiles;
     o->mt = (int)(local % (uint32_t)a.mtiles);
     o->e = st.e;
     o->first = st.first;
-    o->n0 = nt * NMAX;
+    o->n0 = nt * nmax;
     const uint32_t left = st.count - o->n0;
-    o->ntok = left < (uint32_t)NMAX ? left : (uint32_t)NMAX;
+    o->ntok = left < nmax ? left : nmax;
     return true;
 }
 
@@ -218,9 +222,49 @@ __device__ __forceinline__ __half2 odd_h2(uint32_t n) {
     return __hsub2(h2_u(n * 0x00020002u + 0x64016401u), __floats2half2_rn(1024.f, 1024.f));
 }
 
+// 2^(e - 128) as an f16 pair (e in [104, 140]: a normal or subnormal f16, exact).
+__device__ __forceinline__ __half2 mx_scale_h2(uint32_t e) {
+    const int s = (int)e - 128;
+    const uint32_t bits = s >= -14 ? (uint32_t)(s + 15) << 10 : 1u << (s + 24);
+    return h2_u(bits | (bits << 16));
+}
+
+// prb: bytes of a staged row of this piece (MXFP4's last piece of 2 to 7 blocks is row-major).
 template <int FMT>
-__device__ __forceinline__ uint4 dec_chunk(const uint8_t* q, int r, int c4, int gi, const uint8_t* tab) {
-    if (FMT == F_Q4_K) {
+__device__ __forceinline__ uint4 dec_chunk(const uint8_t* q, int r, int c4, int gi, const uint8_t* tab, int prb) {
+    if (FMT == F_MXFP4) {
+        // chunk gi: block 2 c4 + gi / 4, its columns 8 (gi % 4) ..: the low (gi % 4 < 2) or high
+        // nibbles of bytes 8 (gi % 2) .. + 7; y = code * 2^(e - 128) (the reference's
+        // dequantize: kvalues_mxfp4 times e8m0_to_fp32_half), exact in f16 for the banks that
+        // take this path (cwx_bank::mx_f16)
+        uint2 b;
+        uint32_t e;
+        if (prb == 136) {
+            const uint8_t* grp = q + (r >> 4) * (16 * 136);
+            const int rg = r & 15;
+            b = *reinterpret_cast<const uint2*>(grp + (rg * 4 + c4) * 32 + 16 * (gi >> 2) + 8 * (gi & 1));
+            e = grp[2048 + rg * 8 + 2 * c4 + (gi >> 2)];
+        } else {  // GGUF blocks of 17 bytes, row after row
+            const uint8_t* blk = q + r * prb + 17 * (2 * c4 + (gi >> 2));
+            e = blk[0];
+            const uint8_t* nb = blk + 1 + 8 * (gi & 1);
+            b.x = (uint32_t)nb[0] | ((uint32_t)nb[1] << 8) | ((uint32_t)nb[2] << 16) | ((uint32_t)nb[3] << 24);
+            b.y = (uint32_t)nb[4] | ((uint32_t)nb[5] << 8) | ((uint32_t)nb[6] << 16) | ((uint32_t)nb[7] << 24);
+        }
+        const __half2 sc = mx_scale_h2(e);
+        const int sh = (gi & 2) ? 4 : 0;
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t y = ((h ? b.y : b.x) >> sh) & 0x0F0F0F0Fu;
+            const uint32_t z = y | (y >> 4);  // byte 0: nibbles 0, 1; byte 2: nibbles 2, 3
+            const uint32_t p0 = *reinterpret_cast<const uint32_t*>(tab + ((z & 0xFFu) << 7));
+            const uint32_t p1 = *reinterpret_cast<const uint32_t*>(tab + (((z >> 16) & 0xFFu) << 7));
+            w[2 * h] = u_h2(__hmul2(h2_u(p0), sc));
+            w[2 * h + 1] = u_h2(__hmul2(h2_u(p1), sc));
+        }
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    } else if (FMT == F_Q4_K) {
         // y = d * sc * q - dmin * m per 32-column sub-block (candle's to_float, each operation
         // rounded as there), then rounded to f16; sub-block 2 c4 + (gi >= 4) holds the low
         // (gi < 4) or high nibbles of bytes 32 c4 + 8 (gi % 4) .. + 7
@@ -347,11 +391,26 @@ __device__ __forceinline__ uint4 dec_chunk(const uint8_t* q, int r, int c4, int 
 
 __device__ __forceinline__ float silu(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
 
+// 64-column stages of piece kp (a tail piece of MXFP4 may hold fewer than four).
+__device__ __forceinline__ int piece_stages(const Layout& L, int kp) {
+    return kp < L.n_kp - 1 ? 4 : (int)((L.k - (int64_t)PIECE_K * (L.n_kp - 1)) / 64);
+}
+// Whether half 1 (A rows 64-127) of row tile mt exists: always for fused gate/up; for a plain
+// launch, unless the matrix ends with half a tile.
+__device__ __forceinline__ bool half1_exists(const MmaArgs& a, int mt) {
+    return a.fused || (int64_t)(2 * mt + 1) * 64 < a.a0.L.n;
+}
+
 }  // namespace mm
 
-template <int FMT>
+// LO: the activations come as f16 hi and lo parts (a.b, a.blo; x = hi + lo exactly for the
+// Q8_0-rounded rows of the candle policy): each B stage holds both for half as many picks, and
+// every A tile meets both, so the products carry f32-level activations.
+template <int FMT, bool LO>
 __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
     using namespace mm;
+    constexpr uint32_t TN = LO ? NMAX / 2 : NMAX;  // picks per column tile
+    constexpr int LO_OFF = TN * 128;               // the lo tile inside a B stage
     extern __shared__ uint8_t smem_raw[];
     // 1024-aligned base (the swizzled operand tiles need it)
     uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -391,6 +450,13 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
         } else if (FMT == F_IQ4_XS) {
             for (int e = t; e < 16 * 32; e += N_DEC * 32)
                 *reinterpret_cast<float*>(tab + (e >> 5) * 128 + (e & 31) * 4) = (float)cwx_iq4nl(e >> 5);
+        } else if (FMT == F_MXFP4) {
+            const int8_t kv[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+            for (int e = t; e < 256 * 32; e += N_DEC * 32) {
+                const int pr = e >> 5;
+                *reinterpret_cast<uint32_t*>(tab + pr * 128 + (e & 31) * 4) =
+                    u_h2(__floats2half2_rn((float)kv[pr & 15], (float)kv[pr >> 4]));
+            }
         } else if (FMT == F_IQ2_S || FMT == F_IQ2_XXS) {
             for (int e = t; e < (FMT == F_IQ2_S ? 1024 : 256); e += N_DEC * 32) {
                 const uint64_t v = cwx_iq2s_expand(FMT == F_IQ2_S ? d_iq2s_codes[e] : d_iq2xxs_codes[e]);
@@ -418,7 +484,7 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
     const uint32_t tmem = bars->tmem;
     const uint32_t n_used = *a.n_used;
     const int n_kp = a.a0.L.n_kp;
-    const int nks = 4 * n_kp;  // 64-column stages per item
+    const int nks = 4 * (n_kp - 1) + piece_stages(a.a0.L, n_kp - 1);  // 64-column stages per item
 
     if (warp == W_MMA) {
         // ---------------- MMA issue: the whole warp walks the stages (the descriptors stay
@@ -429,7 +495,7 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
         bool ok = true;
         int li = 0;
         const bool leader = elect_one();
-        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m); i += gridDim.x, ++li) {
+        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m, TN); i += gridDim.x, ++li) {
             const int buf = li & 1;
             const uint32_t use = (uint32_t)li >> 1;
             if (use > 0 && !mbar_wait(&bars->acc_empty[buf], (use - 1) & 1, a.err)) {
@@ -452,8 +518,10 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                 const uint64_t ad = sdesc(sa + s * A_BYTES), bd = sdesc(sb + s * B_BYTES);
                 if (leader) {
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)  // +32 bytes = +2 in the descriptor's address field
+                    for (int kk = 0; kk < 4; ++kk) {  // +32 bytes = +2 in the descriptor's address field
                         tc_mma(d, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
+                        if (LO) tc_mma(d, ad + 2 * kk, sdesc(sb + s * B_BYTES + LO_OFF) + 2 * kk, idesc, 1);
+                    }
                     tc_commit(&bars->empty_s[s]);
                 }
                 __syncwarp();
@@ -471,9 +539,8 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
         Iter it;
         MItem m;
         uint32_t p = 0;
-        const int64_t hb0 = 64 * a.a0.L.kp_row_bytes, hb1 = 64 * (a.fused ? a.a1 : a.a0).L.kp_row_bytes;
         bool ok = true;
-        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m); i += gridDim.x) {
+        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m, TN); i += gridDim.x) {
             for (int kp = 0; kp < n_kp; ++kp, ++p) {
                 const int s = (int)(p % NQ);
                 const uint32_t use = p / NQ;
@@ -481,11 +548,14 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                     ok = false;
                     break;
                 }
+                // (64 rows of a piece: a multiple of 16 bytes)
+                const int64_t hb0 = 64 * piece_row_bytes(a.a0.L, kp);
+                const int64_t hb1 = half1_exists(a, m.mt) ? 64 * piece_row_bytes((a.fused ? a.a1 : a.a0).L, kp) : 0;
                 if (lane == 0) mbar_expect_tx(&bars->full_q[s], (uint32_t)(hb0 + hb1));
                 __syncwarp();
                 uint8_t* dst = sq + s * Q_BYTES;
                 if (lane == 0) bulk_g2s(dst, half_src(a, 0, m.e, m.mt, kp), (uint32_t)hb0, &bars->full_q[s]);
-                if (lane == 1) bulk_g2s(dst + hb0, half_src(a, 1, m.e, m.mt, kp), (uint32_t)hb1, &bars->full_q[s]);
+                if (lane == 1 && hb1) bulk_g2s(dst + hb0, half_src(a, 1, m.e, m.mt, kp), (uint32_t)hb1, &bars->full_q[s]);
             }
         }
         // the copies in flight land before the CTA ends
@@ -498,11 +568,13 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
         MItem m;
         uint32_t c = 0;
         bool ok = true;
-        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m); i += gridDim.x) {
+        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m, TN); i += gridDim.x) {
+            // chunk slot j: pick (t / 8) + 16 j (LO: + 16 (j % 8), from the hi rows for j < 8 and
+            // the lo rows above)
             int row[GATHER_PER];
 #pragma unroll
             for (int j = 0; j < GATHER_PER; ++j) {
-                const uint32_t n = (uint32_t)(t >> 3) + 16 * j;
+                const uint32_t n = (uint32_t)(t >> 3) + 16 * (LO ? (j & 7) : j);
                 if (n < m.ntok) {
                     const uint32_t pk = a.pairs[m.first + m.n0 + n];
                     row[j] = (int)(a.rowmap ? a.rowmap[pk] : pk / (uint32_t)a.bdiv);
@@ -517,11 +589,14 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
                 uint8_t* bt = sb + s * B_BYTES;
-                const uint8_t* col = a.b + 16 * (t & 7) + (int64_t)ks * 128;
+                const int64_t co = 16 * (t & 7) + (int64_t)ks * 128;
 #pragma unroll
                 for (int j = 0; j < GATHER_PER; ++j) {
-                    const int n = (t >> 3) + 16 * j, ch = t & 7;
-                    if (row[j] >= 0) cp_async16(bt + n * 128 + ((ch ^ (n & 7)) << 4), col + (int64_t)row[j] * a.bstride);
+                    const bool lo = LO && j >= 8;
+                    const int n = (t >> 3) + 16 * (LO ? (j & 7) : j), ch = t & 7;
+                    if (row[j] >= 0)
+                        cp_async16(bt + (lo ? LO_OFF : 0) + n * 128 + ((ch ^ (n & 7)) << 4),
+                                   (lo ? a.blo : a.b) + co + (int64_t)row[j] * a.bstride);
                 }
                 cp_async_arrive(&bars->full_b[s]);
             }
@@ -532,13 +607,13 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
         const int t = tid - W_DEC * 32;
         // this lane's copy of the table
         const uint8_t* tl = tab + ((FMT == F_IQ2_S || FMT == F_IQ2_XXS) ? (lane & 1) * 16
-                                   : FMT == F_IQ4_XS                   ? lane * 4
-                                                                       : (lane & 3) * 8);
+                                   : (FMT == F_IQ4_XS || FMT == F_MXFP4) ? lane * 4
+                                                                         : (lane & 3) * 8);
         Iter it;
         MItem m;
         uint32_t c = 0, p = 0;
         bool ok = true;
-        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m); i += gridDim.x) {
+        for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m, TN); i += gridDim.x) {
             for (int kp = 0; kp < n_kp && ok; ++kp, ++p) {
                 const int qs = (int)(p % NQ);
                 if (!mbar_wait(&bars->full_q[qs], (p / NQ) & 1, a.err)) {
@@ -546,7 +621,11 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                     break;
                 }
                 const uint8_t* q = sq + qs * Q_BYTES;
-                for (int c4 = 0; c4 < 4; ++c4, ++c) {
+                const int prb = (int)piece_row_bytes(a.a0.L, kp);
+                const int rows = half1_exists(a, m.mt) ? 128 : 64;  // (the rows of a missing half stay unwritten:
+                                                                   // their outputs are never read)
+                const int nst = piece_stages(a.a0.L, kp);
+                for (int c4 = 0; c4 < nst; ++c4, ++c) {
                     const int s = (int)(c % NS);
                     const uint32_t use = c / NS;
                     if (lane == 0 && use > 0 && !mbar_wait(&bars->empty_s[s], (use - 1) & 1, a.err)) ok = false;
@@ -556,9 +635,9 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
 #pragma unroll
                     for (int j = 0; j < DEC_PER; ++j) {
                         const int ci = t + N_DEC * 32 * j;  // chunk: row ci / 8, 16-byte chunk ci % 8
-                        if (ci < DEC_CHUNKS) {
+                        if (ci < DEC_CHUNKS && (ci >> 3) < rows) {
                             const int r = ci >> 3, gi = ci & 7;
-                            const uint4 w = dec_chunk<FMT>(q, r, c4, gi, tl);
+                            const uint4 w = dec_chunk<FMT>(q, r, c4, gi, tl, prb);
                             *reinterpret_cast<uint4*>(at + r * 128 + ((gi ^ (r & 7)) << 4)) = w;
                         }
                     }
@@ -575,7 +654,7 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
         Iter it;
         MItem m;
         int li = 0;
-        for (uint32_t i = blockIdx.x; next_item(a, it, i, n_used, &m); i += gridDim.x, ++li) {
+        for (uint32_t i = blockIdx.x; next_item(a, it, i, n_used, &m, TN); i += gridDim.x, ++li) {
             const int buf = li & 1;
             if (!mbar_wait(&bars->acc_full[buf], ((uint32_t)li >> 1) & 1, a.err)) break;
             tc_after();
@@ -592,14 +671,35 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                         for (int j = 0; j < 32; ++j) xch[j * 64 + (warp - 2) * 32 + lane] = __uint_as_float(r[j]);
                     asm volatile("bar.sync 1, 128;" ::: "memory");
                     if (warp < 2) {
+                        // a warp's 32 features are one Q8_0 block of each pick's h row
                         const int64_t f = (int64_t)m.mt * 64 + warp * 32 + lane;
-#pragma unroll
+                        const int64_t fb = (int64_t)m.e * a.a0.L.n + f;  // expert bias index
+                        const float gb = a.gate_b ? a.gate_b[fb] : 0.f, ub = a.up_b ? a.up_b[fb] : 0.f;
+#pragma unroll 4
                         for (int j = 0; j < 32; ++j) {
                             const int col = cc * 32 + j;
-                            if (col < (int)m.ntok) {
+                            if (col < (int)m.ntok) {  // (the same for the whole warp)
                                 const float g = __uint_as_float(r[j]);
                                 const float u = xch[j * 64 + warp * 32 + lane];
-                                const float h = __fmul_rn(silu(g), u);
+                                float h;
+                                if (a.act == CWX_ACT_SILU) {
+                                    h = __fmul_rn(silu(g), u);
+                                } else {  // gpt-oss clamped SwiGLU, as k_prep (act.cu)
+                                    float gv = a.gate_b ? __fadd_rn(g, gb) : g, uv = a.up_b ? __fadd_rn(u, ub) : u;
+                                    gv = fminf(gv, a.limit);
+                                    uv = fminf(fmaxf(uv, -a.limit), a.limit);
+                                    const float z = __fmul_rn(gv, a.alpha);
+                                    const float sg = __fdiv_rn(1.0f, __fadd_rn(expf(-z), 1.0f));
+                                    h = __fmul_rn(__fadd_rn(uv, 1.0f), __fmul_rn(gv, sg));
+                                }
+                                if (a.h_q80) {  // BlockQ8_0::from_float over the warp's block, as pack_words
+                                    float am = fabsf(h);
+                                    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+                                    const float d = __fdiv_rn(am, 127.f);
+                                    const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
+                                    const float qv = fminf(fmaxf(roundf(__fmul_rn(h, id)), -128.f), 127.f);
+                                    h = __fmul_rn(qv, __half2float(__float2half_rn(d)));
+                                }
                                 a.hout[(int64_t)pk[col] * a.ostride + f] = __float2half_rn(h);
                             }
                         }
@@ -607,10 +707,15 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                     asm volatile("bar.sync 1, 128;" ::: "memory");
                 } else {
                     const int64_t f = (int64_t)m.mt * 128 + warp * 32 + lane;
+                    if (f < a.a0.L.n) {  // (the rows of a missing half tile are not outputs)
+                        const float bv = a.bias ? a.bias[(int64_t)m.e * a.a0.L.n + f] : 0.f;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int col = cc * 32 + j;
-                        if (col < (int)m.ntok) a.out[(int64_t)pk[col] * a.ostride + f] = __uint_as_float(r[j]);
+                        for (int j = 0; j < 32; ++j) {
+                            const int col = cc * 32 + j;
+                            float v = __uint_as_float(r[j]);
+                            if (a.bias) v = __fadd_rn(v, bv);
+                            if (col < (int)m.ntok) a.out[(int64_t)pk[col] * a.ostride + f] = v;
+                        }
                     }
                 }
             }
@@ -645,38 +750,75 @@ int launch_f16rows(const float* x, int64_t n, __half* y, cudaStream_t st) {
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_f16rows");
 }
 
-// Formats the tensor-core products decode.
-bool mma_format(int fmt) {
-    return fmt == F_IQ2_S || fmt == F_IQ3_S || fmt == F_IQ2_XXS || fmt == F_IQ3_XXS || fmt == F_IQ4_XS || fmt == F_Q4_K;
+// x (R, K) f32 -> f16 rows through Q8_0 per 32 columns (BlockQ8_0::from_float, as pack_words):
+// one warp per block, lane j holding column j.
+// The value q * d (d rounded to f16, q <= 127: at most 18 significant bits) is exactly hi + lo.
+__global__ void __launch_bounds__(256) k_f16rows_q80(const float* __restrict__ x, int64_t n, __half* __restrict__ y,
+                                                     __half* __restrict__ ylo) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const float v = i < n ? x[i] : 0.f;
+    float am = fabsf(v);
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const float d = __fdiv_rn(am, 127.f);
+    const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
+    const float qv = fminf(fmaxf(roundf(__fmul_rn(v, id)), -128.f), 127.f);
+    const float w = __fmul_rn(qv, __half2float(__float2half_rn(d)));
+    const __half h = __float2half_rn(w);
+    if (i < n) {
+        y[i] = h;
+        if (ylo) ylo[i] = __float2half_rn(__fsub_rn(w, __half2float(h)));
+    }
 }
 
-// Which launches can take the tensor-core path: weights of those formats in full 64-row tiles and
-// whole 256-column pieces, gate and up of one format and shape.
+int launch_f16rows_q80(const float* x, int64_t n, __half* y, __half* ylo, cudaStream_t st) {
+    if (n <= 0) return CWX_OK;
+    if (n % 32) return fail(CWX_EINVAL, "Q8_0 rows: %lld values is not a whole number of blocks", (long long)n);
+    k_f16rows_q80<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, n, y, ylo);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_f16rows_q80");
+}
+
+// Formats the tensor-core products decode.
+bool mma_format(int fmt) {
+    return fmt == F_IQ2_S || fmt == F_IQ3_S || fmt == F_IQ2_XXS || fmt == F_IQ3_XXS || fmt == F_IQ4_XS || fmt == F_Q4_K ||
+           fmt == F_MXFP4;
+}
+
+// Which launches can take the tensor-core path: weights of those formats in full 64-row tiles
+// (a plain launch may end with half of its 128-row tile), whole 256-column pieces or (MXFP4) a
+// tail piece of whole 64-column stages, gate and up of one format and shape.
 bool mma_supports(const MmaArgs& a) {
     const Layout& L = a.a0.L;
     if (!mma_format(L.fmt)) return false;
-    if (L.k % PIECE_K || L.n % (a.fused ? 64 : 128)) return false;
+    if (L.k % (L.fmt == F_MXFP4 ? 64 : PIECE_K) || L.n % 64) return false;
     if (a.fused) {
         const Layout& U = a.a1.L;
         if (U.fmt != L.fmt || U.n != L.n || U.k != L.k) return false;
     }
     if (a.bstride % 16 || ((uintptr_t)a.b & 15)) return false;
+    if (a.blo && (L.fmt != F_MXFP4 || ((uintptr_t)a.blo & 15))) return false;  // (hi + lo: the MXFP4 kernel)
     return true;
 }
 
-template <int FMT>
+template <int FMT, bool LO = false>
 static int launch_mma_f(const MmaArgs& a, int device, int sm_count, cudaStream_t st) {
-    constexpr int fi =
-        FMT == F_IQ2_S ? 0 : FMT == F_IQ3_S ? 1 : FMT == F_IQ2_XXS ? 2 : FMT == F_IQ3_XXS ? 3 : FMT == F_IQ4_XS ? 4 : 5;
+    constexpr int fi = FMT == F_IQ2_S    ? 0
+                       : FMT == F_IQ3_S  ? 1
+                       : FMT == F_IQ2_XXS ? 2
+                       : FMT == F_IQ3_XXS ? 3
+                       : FMT == F_IQ4_XS ? 4
+                       : FMT == F_MXFP4  ? 6
+                                         : 5;
     const int smem = mm::Smem::total<FMT>() + 1024;
-    static int attr_set[64][6] = {{0}};
-    if (device < 0 || device >= 64 || !attr_set[device][fi]) {
-        cudaError_t e = cudaFuncSetAttribute(k_mma<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    static int attr_set[64][8] = {{0}};
+    const int slot = LO ? 7 : fi;
+    if (device < 0 || device >= 64 || !attr_set[device][slot]) {
+        cudaError_t e = cudaFuncSetAttribute(k_mma<FMT, LO>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_mma)");
-        if (device >= 0 && device < 64) attr_set[device][fi] = 1;
+        if (device >= 0 && device < 64) attr_set[device][slot] = 1;
     }
     const unsigned grid = (unsigned)(sm_count > 0 ? sm_count : 1);
-    k_mma<FMT><<<grid, mm::THREADS, smem, st>>>(a);
+    k_mma<FMT, LO><<<grid, mm::THREADS, smem, st>>>(a);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, "k_mma");
 }
@@ -684,13 +826,16 @@ static int launch_mma_f(const MmaArgs& a, int device, int sm_count, cudaStream_t
 int launch_mma(const MmaArgs& in, int device, int sm_count, cudaStream_t st) {
     MmaArgs a = in;
     if (!mma_supports(a)) return fail(CWX_EUNSUPPORTED, "tensor-core expert products: unsupported layout");
-    a.mtiles = (int)(a.fused ? a.a0.L.n / 64 : a.a0.L.n / 128);
+    a.mtiles = (int)(a.fused ? a.a0.L.n / 64 : (a.a0.L.n + 127) / 128);
     switch (a.a0.L.fmt) {
         case F_IQ2_S: return launch_mma_f<F_IQ2_S>(a, device, sm_count, st);
         case F_IQ3_S: return launch_mma_f<F_IQ3_S>(a, device, sm_count, st);
         case F_IQ2_XXS: return launch_mma_f<F_IQ2_XXS>(a, device, sm_count, st);
         case F_IQ3_XXS: return launch_mma_f<F_IQ3_XXS>(a, device, sm_count, st);
         case F_IQ4_XS: return launch_mma_f<F_IQ4_XS>(a, device, sm_count, st);
+        case F_MXFP4:
+            return a.blo ? launch_mma_f<F_MXFP4, true>(a, device, sm_count, st)
+                         : launch_mma_f<F_MXFP4, false>(a, device, sm_count, st);
         default: return launch_mma_f<F_Q4_K>(a, device, sm_count, st);
     }
 }

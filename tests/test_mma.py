@@ -1,8 +1,9 @@
 """Tensor-core (tcgen05) expert products of large piles against the CPU oracle.
 
-Layers whose routed banks are codebook IQ formats (IQ2_S, IQ3_S, IQ2_XXS, IQ3_XXS) take these
-products once the batch gives enough picks per expert; here the threshold is dropped to 1 so every
-case below takes them. Same bar as the
+Layers whose routed banks are codebook IQ formats (IQ2_S, IQ3_S, IQ2_XXS, IQ3_XXS), Q4_K under the
+f32 policy, or MXFP4 with every block scale in the f16-exact range take these products once the
+batch gives enough picks per expert; here the threshold is dropped to 1 so every case below takes
+them. Same bar as the
 grouped mma.sync products: MoE output within relative L2 1e-3 of the oracle with the same
 activation semantics, expert ids and piles bit-exact.
 """
@@ -37,6 +38,11 @@ SPECS = {
     # mma.sync products beside the tensor-core ones)
     "iq_xxs": Spec(hidden=512, n_experts=32, top_k=8, inter=256, gate_type=O.IQ2_XXS, up_type=O.IQ2_XXS,
                    down_type=O.IQ3_XXS, shared_inter=256, sh_types=(O.IQ4_XS, O.IQ4_XS, O.IQ4_XS), seed=8),
+    # gpt-oss family (config 3): MXFP4 gate/up/down with expert biases and the clamped SwiGLU,
+    # router bias; hidden and inter of 2 whole pieces and a 64-column tail piece (row-major), and
+    # down rows ending with half a 128-row tile
+    "mxfp4_gptoss": Spec(hidden=576, n_experts=16, top_k=4, inter=576, gate_type=O.MXFP4, up_type=O.MXFP4,
+                         down_type=O.MXFP4, act=O.ACT_CLAMPED_SWIGLU, router_bias=True, expert_bias=True, seed=4),
     # IQ3_XXS gate/up, IQ2_XXS down, shared expert of the same formats on the tensor cores
     "iq3xxs_iq2xxs": Spec(hidden=768, n_experts=16, top_k=4, inter=512, gate_type=O.IQ3_XXS, up_type=O.IQ3_XXS,
                           down_type=O.IQ2_XXS, shared_inter=512, sh_types=(O.IQ3_XXS, O.IQ3_XXS, O.IQ2_XXS),
@@ -66,7 +72,8 @@ def _launches():
 
 
 @pytest.mark.parametrize("name,T", [("iq_mix", 256), ("iq_mix", 1500), ("iq3_iq2", 700), ("iq_wide", 1500),
-                                    ("iq3_q4k", 512), ("iq_xxs", 300), ("iq_xxs", 1500), ("iq3xxs_iq2xxs", 900)])
+                                    ("iq3_q4k", 512), ("iq_xxs", 300), ("iq_xxs", 1500), ("iq3xxs_iq2xxs", 900),
+                                    ("mxfp4_gptoss", 64), ("mxfp4_gptoss", 1200)])
 @pytest.mark.parametrize("mode", [O.MODE_CANDLE, O.MODE_F32])
 def test_mma_forward_matches_oracle(name, T, mode):
     from coachwhip_b200 import _lib
@@ -86,12 +93,13 @@ def test_mma_forward_matches_oracle(name, T, mode):
     assert err < RTOL, err
 
 
-def test_mma_path_is_taken_and_matches_mma_sync():
+@pytest.mark.parametrize("name", ["iq_mix", "mxfp4_gptoss"])
+def test_mma_path_is_taken_and_matches_mma_sync(name):
     """Same layer and batch through both product paths: different launch sequences, outputs
     within the bar of each other."""
     from coachwhip_b200 import _lib
 
-    s = SPECS["iq_mix"]
+    s = SPECS[name]
     L = build_cpu(s)
     x = _t(make_input(s, 512))[None]
     moe = build_gpu(L)
@@ -125,3 +133,26 @@ def test_mma_skewed_piles():
     out = moe.forward(_t(x)[None])[0].cpu().numpy()
     _lib.status(0)
     assert rel_l2(out, ref["out"]) < RTOL
+
+
+def test_mxfp4_outside_the_f16_range_stays_on_mma_sync():
+    # block scales far below 2^-24 (weights near 1e-12): code * 2^(e - 128) is not exact in f16,
+    # so the bank is not marked for the tensor cores and the layer keeps the grouped products
+    from coachwhip_b200 import _lib
+
+    s = Spec(hidden=512, n_experts=8, top_k=2, inter=256, gate_type=O.MXFP4, up_type=O.MXFP4,
+             down_type=O.MXFP4, act=O.ACT_CLAMPED_SWIGLU, expert_bias=True, seed=11, w_std=1e-12)
+    L = build_cpu(s)
+    x = _t(make_input(s, 512))[None]
+    moe = build_gpu(L)
+    launches = []
+    for pile in (1, 0):
+        _lib.set_mma_min_pile(0, pile)
+        moe.forward(x)
+        torch.cuda.synchronize()
+        n0 = _launches()
+        moe.forward(x)
+        launches.append(_launches() - n0)
+    _lib.set_mma_min_pile(0, 1)
+    _lib.status(0)
+    assert launches[0] == launches[1], launches
