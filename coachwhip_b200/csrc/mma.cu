@@ -61,28 +61,37 @@ constexpr int TMEM_COLS = 512;
 // e*32 + j*16, the copy picked by the lane's parity, so fewer lanes of a wavefront meet on a bank);
 // IQ3_S and IQ3_XXS 4 per entry, four copies (e*32 + j*8); the 16 IQ4_XS levels as f32, one copy
 // per lane (level n of copy j at n*128 + j*4); MXFP4: nibble pair p -> the f16 pair of codes
-// (twice the e2m1 values, the reference's kvalues_mxfp4), one copy per lane (p*128 + j*4).
+// (twice the e2m1 values, the reference's kvalues_mxfp4), 16 copies (p*64 + j*4, j = lane % 16).
 template <int FMT>
 struct Tab {
     static constexpr int BYTES = FMT == F_IQ2_S ? 1024 * 32
                                  : FMT == F_IQ3_S ? 512 * 32
                                  : (FMT == F_IQ2_XXS || FMT == F_IQ3_XXS) ? 256 * 32
                                  : FMT == F_IQ4_XS ? 16 * 128
-                                 : FMT == F_MXFP4  ? 256 * 128
+                                 : FMT == F_MXFP4  ? 256 * 64
                                                    : 0;
 };
 
+// Pipeline geometry: three operand stages of B tiles for NMAX picks; with hi + lo activations
+// (LO) two stages, each B stage holding the hi and the lo tile of NMAX picks.
+template <bool LO>
+struct Geo {
+    static constexpr int NSS = LO ? 2 : NS;                              // operand stages
+    static constexpr int B_STAGE = (LO ? 2 : 1) * B_BYTES;              // bytes of a B stage
+    static constexpr int GP = (LO ? 2 : 1) * NMAX * 8 / (N_GATHER * 32);  // B chunks per gather thread
+};
+
 // shared memory: barriers, then 1024-aligned A and B stages, quantised stages, codebook, exchange
+template <int FMT, bool LO>
 struct Smem {
     static constexpr int BAR = 0;
     static constexpr int A = 1024;
-    static constexpr int B = A + NS * A_BYTES;
-    static constexpr int Q = B + NS * B_BYTES;
+    static constexpr int B = A + Geo<LO>::NSS * A_BYTES;
+    static constexpr int Q = B + Geo<LO>::NSS * Geo<LO>::B_STAGE;
     static constexpr int TAB = Q + NQ * Q_BYTES;
-    template <int FMT>
-    static constexpr int xch() { return TAB + Tab<FMT>::BYTES; }
-    template <int FMT>
-    static constexpr int total() { return xch<FMT>() + XCH_BYTES; }
+    static constexpr int XCH = TAB + Tab<FMT>::BYTES;
+    static constexpr int TOTAL = XCH + XCH_BYTES;
+    static_assert(TOTAL + 1024 <= 227 * 1024, "k_mma: shared memory above a CTA's 227 KB");
 };
 
 struct Bars {
@@ -258,8 +267,8 @@ __device__ __forceinline__ uint4 dec_chunk(const uint8_t* q, int r, int c4, int 
         for (int h = 0; h < 2; ++h) {
             const uint32_t y = ((h ? b.y : b.x) >> sh) & 0x0F0F0F0Fu;
             const uint32_t z = y | (y >> 4);  // byte 0: nibbles 0, 1; byte 2: nibbles 2, 3
-            const uint32_t p0 = *reinterpret_cast<const uint32_t*>(tab + ((z & 0xFFu) << 7));
-            const uint32_t p1 = *reinterpret_cast<const uint32_t*>(tab + (((z >> 16) & 0xFFu) << 7));
+            const uint32_t p0 = *reinterpret_cast<const uint32_t*>(tab + ((z & 0xFFu) << 6));
+            const uint32_t p1 = *reinterpret_cast<const uint32_t*>(tab + (((z >> 16) & 0xFFu) << 6));
             w[2 * h] = u_h2(__hmul2(h2_u(p0), sc));
             w[2 * h + 1] = u_h2(__hmul2(h2_u(p1), sc));
         }
@@ -404,22 +413,27 @@ __device__ __forceinline__ bool half1_exists(const MmaArgs& a, int mt) {
 }  // namespace mm
 
 // LO: the activations come as f16 hi and lo parts (a.b, a.blo; x = hi + lo exactly for the
-// Q8_0-rounded rows of the candle policy): each B stage holds both for half as many picks, and
-// every A tile meets both, so the products carry f32-level activations.
+// Q8_0-rounded rows of the candle policy): each B stage holds both tiles (two stages instead of
+// three), and every A tile meets both, so the products carry f32-level activations.
 template <int FMT, bool LO>
 __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
     using namespace mm;
-    constexpr uint32_t TN = LO ? NMAX / 2 : NMAX;  // picks per column tile
-    constexpr int LO_OFF = TN * 128;               // the lo tile inside a B stage
+    using G = Geo<LO>;
+    using S = Smem<FMT, LO>;
+    constexpr uint32_t TN = NMAX;       // picks per column tile
+    constexpr int LO_OFF = NMAX * 128;  // the lo tile inside a B stage
+    constexpr int NS = G::NSS;          // (shadows mm::NS)
+    constexpr int B_BYTES = G::B_STAGE;
+    constexpr int GATHER_PER = G::GP;
     extern __shared__ uint8_t smem_raw[];
     // 1024-aligned base (the swizzled operand tiles need it)
     uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    Bars* bars = reinterpret_cast<Bars*>(smem + Smem::BAR);
-    uint8_t* sa = smem + Smem::A;
-    uint8_t* sb = smem + Smem::B;
-    uint8_t* sq = smem + Smem::Q;
-    uint8_t* tab = smem + Smem::TAB;
-    float* xch = reinterpret_cast<float*>(smem + Smem::xch<FMT>());
+    Bars* bars = reinterpret_cast<Bars*>(smem + S::BAR);
+    uint8_t* sa = smem + S::A;
+    uint8_t* sb = smem + S::B;
+    uint8_t* sq = smem + S::Q;
+    uint8_t* tab = smem + S::TAB;
+    float* xch = reinterpret_cast<float*>(smem + S::XCH);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
@@ -452,9 +466,9 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                 *reinterpret_cast<float*>(tab + (e >> 5) * 128 + (e & 31) * 4) = (float)cwx_iq4nl(e >> 5);
         } else if (FMT == F_MXFP4) {
             const int8_t kv[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
-            for (int e = t; e < 256 * 32; e += N_DEC * 32) {
-                const int pr = e >> 5;
-                *reinterpret_cast<uint32_t*>(tab + pr * 128 + (e & 31) * 4) =
+            for (int e = t; e < 256 * 16; e += N_DEC * 32) {
+                const int pr = e >> 4;
+                *reinterpret_cast<uint32_t*>(tab + pr * 64 + (e & 15) * 4) =
                     u_h2(__floats2half2_rn((float)kv[pr & 15], (float)kv[pr >> 4]));
             }
         } else if (FMT == F_IQ2_S || FMT == F_IQ2_XXS) {
@@ -569,12 +583,13 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
         uint32_t c = 0;
         bool ok = true;
         for (uint32_t i = blockIdx.x; ok && next_item(a, it, i, n_used, &m, TN); i += gridDim.x) {
-            // chunk slot j: pick (t / 8) + 16 j (LO: + 16 (j % 8), from the hi rows for j < 8 and
-            // the lo rows above)
-            int row[GATHER_PER];
+            // chunk slot j: pick (t / 8) + 16 j (LO: + 16 (j % 16), from the hi rows for j < 16 and
+            // the lo rows above; the row of slot j + 16 is the row of slot j)
+            constexpr int NP = LO ? GATHER_PER / 2 : GATHER_PER;  // picks per gather thread
+            int row[NP];
 #pragma unroll
-            for (int j = 0; j < GATHER_PER; ++j) {
-                const uint32_t n = (uint32_t)(t >> 3) + 16 * (LO ? (j & 7) : j);
+            for (int j = 0; j < NP; ++j) {
+                const uint32_t n = (uint32_t)(t >> 3) + 16 * j;
                 if (n < m.ntok) {
                     const uint32_t pk = a.pairs[m.first + m.n0 + n];
                     row[j] = (int)(a.rowmap ? a.rowmap[pk] : pk / (uint32_t)a.bdiv);
@@ -592,11 +607,12 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                 const int64_t co = 16 * (t & 7) + (int64_t)ks * 128;
 #pragma unroll
                 for (int j = 0; j < GATHER_PER; ++j) {
-                    const bool lo = LO && j >= 8;
-                    const int n = (t >> 3) + 16 * (LO ? (j & 7) : j), ch = t & 7;
-                    if (row[j] >= 0)
+                    const bool lo = LO && j >= NP;
+                    const int jj = lo ? j - NP : j;
+                    const int n = (t >> 3) + 16 * jj, ch = t & 7;
+                    if (row[jj] >= 0)
                         cp_async16(bt + (lo ? LO_OFF : 0) + n * 128 + ((ch ^ (n & 7)) << 4),
-                                   (lo ? a.blo : a.b) + co + (int64_t)row[j] * a.bstride);
+                                   (lo ? a.blo : a.b) + co + (int64_t)row[jj] * a.bstride);
                 }
                 cp_async_arrive(&bars->full_b[s]);
             }
@@ -607,8 +623,9 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
         const int t = tid - W_DEC * 32;
         // this lane's copy of the table
         const uint8_t* tl = tab + ((FMT == F_IQ2_S || FMT == F_IQ2_XXS) ? (lane & 1) * 16
-                                   : (FMT == F_IQ4_XS || FMT == F_MXFP4) ? lane * 4
-                                                                         : (lane & 3) * 8);
+                                   : FMT == F_IQ4_XS                   ? lane * 4
+                                   : FMT == F_MXFP4                    ? (lane & 15) * 4
+                                                                       : (lane & 3) * 8);
         Iter it;
         MItem m;
         uint32_t c = 0, p = 0;
@@ -665,43 +682,49 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mma(MmaArgs a) {
                 tc_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(buf * 256 + cc * 32), r);
                 tc_wait_ld();
                 if (a.fused) {
-                    // up rows (lanes 64-127) go through shared memory to the gate rows' threads
-                    if (warp >= 2)
+                    // Lanes 0-63 hold gate rows, 64-127 the up rows of the same 64 features. The
+                    // four warps split the chunk's 32 picks: warps 0-1 take picks 0-15 (their
+                    // up values from warps 2-3 through shared memory), warps 2-3 picks 16-31 (their
+                    // gate values from warps 0-1). A warp's 32 features are one Q8_0 block of each
+                    // pick's h row.
+                    const int hf = warp & 1;
+                    const bool gate_side = warp < 2;
+                    float* give = xch + (gate_side ? 0 : 1024);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) xch[j * 64 + (warp - 2) * 32 + lane] = __uint_as_float(r[j]);
+                    for (int jj = 0; jj < 16; ++jj)
+                        give[jj * 64 + hf * 32 + lane] = __uint_as_float(gate_side ? r[16 + jj] : r[jj]);
                     asm volatile("bar.sync 1, 128;" ::: "memory");
-                    if (warp < 2) {
-                        // a warp's 32 features are one Q8_0 block of each pick's h row
-                        const int64_t f = (int64_t)m.mt * 64 + warp * 32 + lane;
-                        const int64_t fb = (int64_t)m.e * a.a0.L.n + f;  // expert bias index
-                        const float gb = a.gate_b ? a.gate_b[fb] : 0.f, ub = a.up_b ? a.up_b[fb] : 0.f;
-#pragma unroll 4
-                        for (int j = 0; j < 32; ++j) {
-                            const int col = cc * 32 + j;
-                            if (col < (int)m.ntok) {  // (the same for the whole warp)
-                                const float g = __uint_as_float(r[j]);
-                                const float u = xch[j * 64 + warp * 32 + lane];
-                                float h;
-                                if (a.act == CWX_ACT_SILU) {
-                                    h = __fmul_rn(silu(g), u);
-                                } else {  // gpt-oss clamped SwiGLU, as k_prep (act.cu)
-                                    float gv = a.gate_b ? __fadd_rn(g, gb) : g, uv = a.up_b ? __fadd_rn(u, ub) : u;
-                                    gv = fminf(gv, a.limit);
-                                    uv = fminf(fmaxf(uv, -a.limit), a.limit);
-                                    const float z = __fmul_rn(gv, a.alpha);
-                                    const float sg = __fdiv_rn(1.0f, __fadd_rn(expf(-z), 1.0f));
-                                    h = __fmul_rn(__fadd_rn(uv, 1.0f), __fmul_rn(gv, sg));
-                                }
-                                if (a.h_q80) {  // BlockQ8_0::from_float over the warp's block, as pack_words
-                                    float am = fabsf(h);
-                                    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-                                    const float d = __fdiv_rn(am, 127.f);
-                                    const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
-                                    const float qv = fminf(fmaxf(roundf(__fmul_rn(h, id)), -128.f), 127.f);
-                                    h = __fmul_rn(qv, __half2float(__float2half_rn(d)));
-                                }
-                                a.hout[(int64_t)pk[col] * a.ostride + f] = __float2half_rn(h);
+                    const float* take = xch + (gate_side ? 1024 : 0);
+                    const int64_t f = (int64_t)m.mt * 64 + hf * 32 + lane;
+                    const int64_t fb = (int64_t)m.e * a.a0.L.n + f;  // expert bias index
+                    const float gb = a.gate_b ? a.gate_b[fb] : 0.f, ub = a.up_b ? a.up_b[fb] : 0.f;
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const int col = cc * 32 + (gate_side ? jj : 16 + jj);
+                        if (col < (int)m.ntok) {  // (the same for the whole warp)
+                            const float mine = __uint_as_float(gate_side ? r[jj] : r[16 + jj]);
+                            const float other = take[jj * 64 + hf * 32 + lane];
+                            const float g = gate_side ? mine : other, u = gate_side ? other : mine;
+                            float h;
+                            if (a.act == CWX_ACT_SILU) {
+                                h = __fmul_rn(silu(g), u);
+                            } else {  // gpt-oss clamped SwiGLU, as k_prep (act.cu)
+                                float gv = a.gate_b ? __fadd_rn(g, gb) : g, uv = a.up_b ? __fadd_rn(u, ub) : u;
+                                gv = fminf(gv, a.limit);
+                                uv = fminf(fmaxf(uv, -a.limit), a.limit);
+                                const float z = __fmul_rn(gv, a.alpha);
+                                const float sg = __fdiv_rn(1.0f, __fadd_rn(expf(-z), 1.0f));
+                                h = __fmul_rn(__fadd_rn(uv, 1.0f), __fmul_rn(gv, sg));
                             }
+                            if (a.h_q80) {  // BlockQ8_0::from_float over the warp's block, as pack_words
+                                float am = fabsf(h);
+                                for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+                                const float d = __fdiv_rn(am, 127.f);
+                                const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
+                                const float qv = fminf(fmaxf(roundf(__fmul_rn(h, id)), -128.f), 127.f);
+                                h = __fmul_rn(qv, __half2float(__float2half_rn(d)));
+                            }
+                            a.hout[(int64_t)pk[col] * a.ostride + f] = __float2half_rn(h);
                         }
                     }
                     asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -809,7 +832,7 @@ static int launch_mma_f(const MmaArgs& a, int device, int sm_count, cudaStream_t
                        : FMT == F_IQ4_XS ? 4
                        : FMT == F_MXFP4  ? 6
                                          : 5;
-    const int smem = mm::Smem::total<FMT>() + 1024;
+    const int smem = mm::Smem<FMT, LO>::TOTAL + 1024;
     static int attr_set[64][8] = {{0}};
     const int slot = LO ? 7 : fi;
     if (device < 0 || device >= 64 || !attr_set[device][slot]) {
