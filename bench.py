@@ -279,6 +279,13 @@ def gemv_bytes(cfg, us, T):
     return gu + d, expert
 
 
+def fused_bytes(cfg, us, T):
+    """Algorithmic bytes of the fused decode layer per pass: the router weights, the unique
+    experts' and the shared expert's quantised bytes, the input, residual and output rows."""
+    _, expert = gemv_bytes(cfg, us, T)
+    return expert + len(us) * (cfg.n_experts * cfg.hidden * 4 + 3 * T * cfg.hidden * 4)
+
+
 # ------------------------------------------------------------------------------ CPU baselines
 def cpu_layer(store_banks, shared, router_w):
     """Layer 0 of config 1 for the CPU builds (bank bytes downloaded from the GPU)."""
@@ -730,7 +737,10 @@ def main():
             sweep[T].update({"k_gemv_ms_per_pass": gemv_ms, "k_gemv_share": gemv_ms / ms,
                              "k_gemv_hbm_frac": alg / (gemv_ms / 1e3) / 1e9 / pk["hbm_gbs"]})
         if ph.get("decode_fused", 0) > 0:
-            sweep[T]["path"] = "fused decode layer (k_decode_layer, one cooperative launch per layer)"
+            fb = fused_bytes(cfg, us, T)
+            sweep[T].update({"path": "fused decode layer (k_decode_layer, one cooperative launch per layer)",
+                             "k_decode_layer_ms_per_pass": ph["decode_fused"],
+                             "k_decode_layer_hbm_frac": fb / (ph["decode_fused"] / 1e3) / 1e9 / pk["hbm_gbs"]})
         print(f"[bench] batch {T}: {ms:.3f} ms/pass, {sweep[T]['tokens_per_s']:.1f} tokens/s, "
               f"{np.mean(us):.1f} experts/layer, expert bytes {sweep[T]['hbm_frac_expert_bytes']:.3f} of HBM",
               file=sys.stderr, flush=True)
@@ -746,20 +756,33 @@ def main():
     launches_per_pass = _lib.lib().cwx_ctx_launches(ctx) - l0
 
     gemv_ms = phase_ms["gate_up"] + phase_ms["down"]
-    achieved = alg / (gemv_ms / 1e3) / 1e9
-    traffic, traffic_src = None, None
-    try:
-        prof = json.load(open(os.path.join(ROOT, "profiles", "k_gemv_traffic.json")))
-        traffic, traffic_src = prof.get("dram_bytes_per_launch"), prof.get("source")
-    except Exception:
-        pass
-    roofline = {"kernel": "k_gemv (gate/up + down expert products)", "bound": "hbm", "achieved": achieved,
-                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
-                "traffic_source": traffic_src,
-                "peak_source": "measured" if not pk.get("fallback") else "fallback",
-                "launches_per_pass": 2 * len(us), "algorithmic_bytes_per_launch": alg / (2 * len(us)),
-                "algorithmic_bytes_per_pass": alg, "kernel_ms_per_pass": gemv_ms,
-                "stack_hbm_frac_expert_bytes": sweep[T]["hbm_frac_expert_bytes"]}
+    if gemv_ms > 0:
+        achieved = alg / (gemv_ms / 1e3) / 1e9
+        traffic, traffic_src = None, None
+        try:
+            prof = json.load(open(os.path.join(ROOT, "profiles", "k_gemv_traffic.json")))
+            traffic, traffic_src = prof.get("dram_bytes_per_launch"), prof.get("source")
+        except Exception:
+            pass
+        roofline = {"kernel": "k_gemv (gate/up + down expert products)", "bound": "hbm", "achieved": achieved,
+                    "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
+                    "traffic_source": traffic_src,
+                    "peak_source": "measured" if not pk.get("fallback") else "fallback",
+                    "launches_per_pass": 2 * len(us), "algorithmic_bytes_per_launch": alg / (2 * len(us)),
+                    "algorithmic_bytes_per_pass": alg, "kernel_ms_per_pass": gemv_ms,
+                    "stack_hbm_frac_expert_bytes": sweep[T]["hbm_frac_expert_bytes"]}
+    else:  # the fused decode layer: one launch per layer does all of it
+        fb = fused_bytes(cfg, us, T)
+        fms = phase_ms["decode_fused"]
+        roofline = {"kernel": "k_decode_layer (the whole layer, one launch)", "bound": "hbm",
+                    "achieved": fb / (fms / 1e3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                    "frac": fb / (fms / 1e3) / 1e9 / pk["hbm_gbs"],
+                    "traffic": 13.0e6, "traffic_source": "ncu --set full capture of profiles/k_decode_layer_c1_b1.md "
+                                                         "(one layer at b = 1, dram bytes read + written)",
+                    "peak_source": "measured" if not pk.get("fallback") else "fallback",
+                    "launches_per_pass": len(us), "algorithmic_bytes_per_launch": fb / len(us),
+                    "algorithmic_bytes_per_pass": fb, "kernel_ms_per_pass": fms,
+                    "stack_hbm_frac_expert_bytes": sweep[T]["hbm_frac_expert_bytes"]}
 
     # end to end through the public API, host buffers, copies inside the timed region
     xh = x.detach().cpu().pin_memory()
