@@ -552,10 +552,12 @@ def c3_runs(world, rank, local, a, pk, maxall, barrier, fp8=None):
         del g
         us = used_experts(mods, x)
         eb = sum(us) * b_exp + nl * cfg.n_experts * cfg.hidden * 4  # experts read + router weights
+        ph = phase_profile(mods, x, dev, local)
         res["decode"][str(T)] = {"tokens_per_s": T / (ms / 1e3), "ms_per_step": ms,
                                  "unique_experts_mean": float(np.mean(us)),
                                  "hbm_gbs_expert_bytes": eb / (ms / 1e3) / 1e9,
-                                 "hbm_frac": eb / (ms / 1e3) / 1e9 / pk["hbm_gbs"]}
+                                 "hbm_frac": eb / (ms / 1e3) / 1e9 / pk["hbm_gbs"],
+                                 "phase_ms_per_step": {k: v for k, v in ph.items() if v > 0}}
         print(f"[bench] config 3 decode {T}: {ms:.3f} ms/step, {T / (ms / 1e3):.1f} tokens/s", file=sys.stderr,
               flush=True)
     T = 4096

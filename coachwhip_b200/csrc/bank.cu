@@ -416,7 +416,8 @@ static int supported_type(int t) {
 }
 
 // MXFP4 banks, one thread per (expert, row, piece): bit 0 of flag when a whole 256-column piece
-// has block scales e more than 24 apart (the grouped products' f16 fast path), bit 1 when any
+// or a 2-block tail piece has block scales e more than 24 apart (the grouped products' f16 fast
+// paths), bit 1 when any
 // block scale lies outside [104, 140] (the tensor-core products need every weight exact in f16).
 constexpr int MX_F16_MIN = 104, MX_F16_MAX = 140;
 __global__ void k_mx_spread(const uint8_t* __restrict__ d, Layout L, int64_t ne, int* flag) {
@@ -434,7 +435,7 @@ __global__ void k_mx_spread(const uint8_t* __restrict__ d, Layout L, int64_t ne,
         mn = min(mn, v);
     }
     int f = 0;
-    if (nb == 8 && mx - mn > 24) f |= 1;
+    if ((nb == 8 || nb == 2) && mx - mn > 24) f |= 1;  // (whole pieces and the 2-block tail: fast paths)
     if (mn < MX_F16_MIN || mx > MX_F16_MAX) f |= 2;
     if (f) atomicOr(flag, f);
 }

@@ -216,8 +216,9 @@ struct cwx_bank {
     cwx::Layout L;
     uint8_t* d;  // tiled bytes, E * expert_bytes
     int64_t bytes_per_expert_gguf;
-    // MXFP4: some row's 256-column piece has block scales more than 2^24 apart, beyond the f16
-    // range of the grouped products' fast path (its launches take the exact path)
+    // MXFP4: some row's 256-column piece (or 2-block tail piece) has block scales more than 2^24
+    // apart, beyond the f16 range of the grouped products' fast path (its launches take the exact
+    // path)
     int mx_wide;
     // MXFP4: every block scale e lies in [104, 140], so every weight (code times 2^(e - 128)) is
     // exact in f16 and the tensor-core products can take the bank

@@ -503,11 +503,14 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(GemvArgs a) {
                 // that must carry ~22 bits take the exact path; MXFP4 weights are exact, and their
                 // products always take the activations' lo parts too, as Q8_0-rounded activations
                 // are not exact in f16; a row's last MXFP4 piece of fewer than 8 blocks is stored
-                // row after row and takes the exact path)
+                // row after row: one of 2 blocks (K = 64 mod 256, as 2880) has its own loader,
+                // longer ones take the exact path)
+                const bool mx_tail = FMT == F_MXFP4 && kp + 1 == L.n_kp && L.last_kp_row_bytes != L.kp_row_bytes;
                 if (FMT != 0 && L.fmt == FMT && !qi && (FMT != F_IQ4_XS || !lo) &&
-                    (FMT != F_MXFP4 || kp + 1 < L.n_kp || L.last_kp_row_bytes == L.kp_row_bytes)) {
+                    (!mx_tail || L.last_kp_row_bytes == 2 * 17)) {
                     FastIn in;
-                    fast_load<FMT>(wsl, mt, g, c4, in);
+                    if (mx_tail) fast_load_mx_tail(wsl, L.last_kp_row_bytes, mt, g, c4, in);
+                    else fast_load<FMT>(wsl, mt, g, c4, in);
                     fast_compute<FMT, NT>(in, tl, brow, bnt, lo || FMT == F_MXFP4, acc);
                 }
                 else if (L.fmt == F_Q4_K && L.kp_row_bytes == 144) q4k_step<NT>(wsl, mt, g, c4, brow, bnt, lo, qi, dx, acc);

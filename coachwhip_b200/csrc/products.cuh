@@ -227,6 +227,40 @@ __device__ __forceinline__ void mx_scales(uint2 e8, int c4, uint32_t* h, float* 
     *d = e8m0_to_f32_half((uint8_t)em);
 }
 
+// MXFP4 tail piece (a row's last 64 columns, two GGUF blocks of 17 bytes: e, then 16 nibble
+// bytes), stored row after row (prb bytes a row): the fast path's inputs for rows 16 mt + g and
+// + 8. The 64 columns are quarter 0; the other quarters' threads get zero weights (the packed
+// activation rows hold zeros there too) but the same row scales, because every thread of a quad
+// scales its own output columns (picks) of the rows' sums. The two blocks' scales enter as
+// 2^(e - m), m the larger, exact in f16 while they are at most 24 apart (the bank is checked for
+// it when it is made).
+__device__ __forceinline__ void mx_tail_row(const uint8_t* p, uint4* q, uint4* q2, uint32_t* h, float* d) {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        w[i] = (uint32_t)p[1 + 4 * i] | ((uint32_t)p[2 + 4 * i] << 8) | ((uint32_t)p[3 + 4 * i] << 16) |
+               ((uint32_t)p[4 + 4 * i] << 24);
+        w[4 + i] = (uint32_t)p[18 + 4 * i] | ((uint32_t)p[19 + 4 * i] << 8) | ((uint32_t)p[20 + 4 * i] << 16) |
+                   ((uint32_t)p[21 + 4 * i] << 24);
+    }
+    *q = make_uint4(w[0], w[1], w[2], w[3]);
+    *q2 = make_uint4(w[4], w[5], w[6], w[7]);
+    const int e0 = p[0], e1 = p[17], m = e0 > e1 ? e0 : e1;
+    uint32_t bits[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int k = (i ? e1 : e0) - m;
+        bits[i] = k >= -14 ? (uint32_t)(k + 15) << 10 : k >= -24 ? 1u << (k + 24) : 0u;
+    }
+    *h = bits[0] | (bits[1] << 16);
+    *d = e8m0_to_f32_half((uint8_t)m);
+}
+__device__ __forceinline__ void fast_load_mx_tail(const uint8_t* wsl, int64_t prb, int mt, int g, int c4, FastIn& in) {
+    mx_tail_row(wsl + (int64_t)(16 * mt + g) * prb, &in.QA, &in.QA2, &in.HA, &in.dA);
+    mx_tail_row(wsl + (int64_t)(16 * mt + g + 8) * prb, &in.QB, &in.QB2, &in.HB, &in.dB);
+    if (c4 != 0) in.QA = in.QA2 = in.QB = in.QB2 = make_uint4(0u, 0u, 0u, 0u);
+}
+
 template <int FMT>
 __device__ __forceinline__ void fast_load(const uint8_t* wsl, int mt, int g, int c4, FastIn& in) {
     if (FMT == F_MXFP4) {
