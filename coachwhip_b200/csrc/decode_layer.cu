@@ -377,7 +377,7 @@ __device__ __forceinline__ void sh_compute(const DecodeArgs& a, const DlState* S
     const uint8_t* brow = src + (tg * np + kp) * DL_HALF + 16 * c4;
     const DxAt dx{reinterpret_cast<const uint8_t*>(&S->xqd[t0 * np + kp]),
                   reinterpret_cast<const uint8_t*>(&S->xqd[t1 * np + kp])};
-    q4k_rows<1, true>(q4_row_of(r.a, c4), q4_row_of(r.b, c4), brow, 0, false, a.sh_qint != 0, dx, acc);
+    q4k_rows<1>(q4_row_of(r.a, c4), q4_row_of(r.b, c4), brow, 0, false, a.sh_qint != 0, dx, acc);
 }
 
 // h = SiLU(gate) * up of a finished unit: f16 at the features' places of each pick's hidden
@@ -419,7 +419,7 @@ __device__ __forceinline__ void down_item(const DlState* S, const FastIn& in, in
     const uint32_t pick = S->pairs[first + ((uint32_t)g < cnt ? g : 0)];
     const uint8_t* brow = hrows + (pick * npd + kp) * DL_HALF + 16 * c4;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    fast_compute<FD, 1, true>(in, tl, brow, 0, false, acc);
+    fast_compute<FD, 1>(in, tl, brow, 0, false, acc);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const uint32_t slot = 2 * c4 + (i & 1);
@@ -577,7 +577,7 @@ __global__ void __launch_bounds__(DL_THREADS, 1) k_decode_layer(DecodeArgs a) {
                 float t[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) t[j] = up ? au[j] : ag[j];
-                fast_compute<FG, 1, true>(cur, tlG, ui.xr + (r >> 1) * DL_HALF, 0, false, t);
+                fast_compute<FG, 1>(cur, tlG, ui.xr + (r >> 1) * DL_HALF, 0, false, t);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     au[j] = up ? t[j] : au[j];
@@ -737,7 +737,7 @@ __global__ void __launch_bounds__(DL_THREADS, 1) k_decode_layer(DecodeArgs a) {
                 const DxAt dx{hsp + (int64_t)t0 * hsrow + (int64_t)kp * 1024 + 512,
                               hsp + (int64_t)t1 * hsrow + (int64_t)kp * 1024 + 512};
                 float acc[4] = {0.f, 0.f, 0.f, 0.f};
-                q4k_rows<1, true>(q4_row_of(ra, c4), q4_row_of(rb, c4), brow, 0, false, a.sh_qint != 0, dx, acc);
+                q4k_rows<1>(q4_row_of(ra, c4), q4_row_of(rb, c4), brow, 0, false, a.sh_qint != 0, dx, acc);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int slot = 2 * c4 + (i & 1);

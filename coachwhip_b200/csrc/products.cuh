@@ -322,15 +322,13 @@ __device__ __forceinline__ void fast_load(const uint8_t* wsl, int mt, int g, int
 // A fast-path step from its inputs: this warp's 16 rows x 256 columns against NT n-tiles of 8
 // activation rows (bnt bytes apart), hi activations plus the lo parts when `lo`; the piece's
 // partial sums are scaled by the rows' block scales and added to acc[nt * 4 + i].
-// ROLL keeps the four 16-column steps as a loop (a quarter of the code, for kernels that run each
-// routine a few times per launch and would otherwise fetch it cold from the instruction cache).
-template <int FMT, int NT, bool ROLL = false>
+template <int FMT, int NT>
 __device__ __forceinline__ void fast_compute(const FastIn& in, const uint8_t* tl, const uint8_t* brow, int bnt, bool lo,
                                              float* acc) {
     float t[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) t[nt][0] = t[nt][1] = t[nt][2] = t[nt][3] = 0.f;
-#pragma unroll(ROLL ? 1 : 4)
+#pragma unroll
     for (int ss = 0; ss < 4; ++ss) {
         uint32_t pa[8], pb[8];
         if (FMT == F_IQ4_XS || FMT == F_MXFP4) {
@@ -448,7 +446,7 @@ __device__ __forceinline__ float dx_of(const DxAt& x, int nt, int bnt, int i) {
     return *reinterpret_cast<const float*>(((i & 1) ? x.p1 : x.p0) + nt * bnt);
 }
 
-template <int NT, bool ROLL = false>
+template <int NT>
 __device__ __forceinline__ void q4k_rows(const Q4Row& A, const Q4Row& Bq, const uint8_t* brow, int bnt, bool lo, bool qi,
                                          const DxAt& dx, float* acc);
 template <int NT>
@@ -459,7 +457,7 @@ __device__ __forceinline__ void q4k_step(const uint8_t* wsl, int mt, int g, int 
 }
 
 // The two rows (g, g + 8) of a 16-row group of one piece against NT n-tiles of activation rows.
-template <int NT, bool ROLL>
+template <int NT>
 __device__ __forceinline__ void q4k_rows(const Q4Row& A, const Q4Row& Bq, const uint8_t* brow, int bnt, bool lo, bool qi,
                                          const DxAt& dx, float* acc) {
     float t1[NT][4], t2[NT][4];
@@ -467,7 +465,7 @@ __device__ __forceinline__ void q4k_rows(const Q4Row& A, const Q4Row& Bq, const 
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) t1[nt][i] = t2[nt][i] = 0.f;
-#pragma unroll(ROLL ? 1 : 4)
+#pragma unroll
     for (int ss = 0; ss < 4; ++ss) {
         uint32_t pa[8], pb[8];
         q4_pairs(A, ss, pa);
