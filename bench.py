@@ -608,15 +608,36 @@ def ep_runs(world, rank, local, a, maxall, barrier):
         return {"config": desc, "layers": nl, "tokens": T, "ranks": 1, "experts_per_rank": cfg.n_experts,
                 "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3), "tflops": fl / (ms / 1e3) / 1e12,
                 "path": "single-device cwx_moe_forward (no exchange), CUDA graph of the 48 layers"}
-    from coachwhip_b200.ep import EpComm, LibraryExpertParallelMoe
+    import numpy as np
+    import torch.distributed as dist
+
+    from coachwhip_b200.ep import EpComm, LibraryExpertParallelMoe, balanced_placement, expert_lists
 
     epr = cfg.n_experts // world
     comm = EpComm(local, world, rank)
     layers = []
+    # Expert placement per layer from a calibration batch (2048 tokens of another input stream):
+    # its picks per expert, spread over the ranks by balanced_placement (rank 0 decides, the
+    # others receive it). The Zipf bias sends two thirds of the picks to ten experts, so the
+    # contiguous ranges would leave one rank with about twice the mean load.
+    n_cal = 2048
+    xc = W.normal(n_cal * cfg.hidden, W.stream(cfg.input_seed + 101, 0, W.T_IN), 1.0, local).view(n_cal, cfg.hidden)
+    loads = {"contiguous": [], "balanced": []}
     for l in range(nl):
-        lay = W.build_layer(cfg, l, local, act_mode=_lib.ACT_MODE_F32, first=rank * epr, n_local=epr)
+        rw, rb = W.router(cfg, l, local)
+        lg = xc @ rw.t() + (rb if rb is not None else 0)
+        cnt = torch.bincount(lg.topk(cfg.top_k, dim=1).indices.reshape(-1), minlength=cfg.n_experts).cpu().numpy()
+        del rw, rb, lg
+        slot = torch.from_numpy(balanced_placement(cnt, world)).to(dev)
+        dist.broadcast(slot, 0)
+        slot = slot.cpu().numpy()
+        per_rank = np.zeros(world)
+        np.add.at(per_rank, slot // epr, cnt)
+        loads["balanced"].append(float(per_rank.max() / per_rank.mean()))
+        loads["contiguous"].append(float(cnt.reshape(world, epr).sum(1).max() / per_rank.mean()))
+        lay = W.build_layer(cfg, l, local, act_mode=_lib.ACT_MODE_F32, experts=expert_lists(slot, world)[rank])
         eng = CudaEngine(lay.router_w, cfg.top_k, True, lay.act, lay.banks, world, rank, gate_bias=lay.router_b,
-                         shared=lay.shared, act_mode=_lib.ACT_MODE_F32)
+                         shared=lay.shared, act_mode=_lib.ACT_MODE_F32, placement=slot)
         eng._keep = lay
         layers.append(LibraryExpertParallelMoe(eng, comm, per))
     x = W.make_input(cfg, T, local)[rank * per:(rank + 1) * per].contiguous().view(1, per, cfg.hidden)
@@ -661,6 +682,9 @@ def ep_runs(world, rank, local, a, maxall, barrier):
                           "what": "layer 0 on each rank's tokens vs the single-device layer; max over ranks"},
             "transport": "cwx_ep_forward: NCCL inside libcwx, fixed-capacity exchanges (counts read on the "
                          "device), no host synchronisation in a layer",
+            "placement": {"how": "balanced_placement of a 2048-token calibration batch's picks per expert, per "
+                                 "layer (equal experts per rank)",
+                          "max_over_mean_rank_picks": {k: float(np.mean(v)) for k, v in loads.items()}},
             "timing": f"CUDA events over {reps} eager passes of the {nl} layers, max over ranks"}
 
 

@@ -22,7 +22,7 @@ EXPORTS = [
     "cwx_bank_create", "cwx_bank_synth", "cwx_bank_destroy", "cwx_bank_desc", "cwx_bank_download",
     "cwx_bank_dequantize", "cwx_synth_normal", "cwx_route", "cwx_permute", "cwx_permute_noalloc", "cwx_expert_matmul", "cwx_moe_forward",
     "cwx_ctx_set_profiling", "cwx_ctx_read_profile", "cwx_ctx_reset_profile", "cwx_ctx_launches",
-    "cwx_ctx_set_mma_min_pile", "cwx_ep_dispatch", "cwx_ep_experts", "cwx_ep_combine", "cwx_bank_synth_experts",
+    "cwx_ctx_set_mma_min_pile", "cwx_ep_dispatch", "cwx_ep_experts", "cwx_ep_combine", "cwx_bank_synth_experts", "cwx_bank_synth_list",
     "cwx_ep_rows_f16", "cwx_ctx_check_wait", "cwx_gguf_open", "cwx_gguf_close", "cwx_gguf_info",
     "cwx_gguf_tensor_info", "cwx_gguf_tensor", "cwx_bank_from_gguf", "cwx_gguf_tensor_f32", "cwx_gguf_meta_int",
     "cwx_gguf_meta_f64", "cwx_gguf_meta_str", "cwx_add_rms_norm", "cwx_ep_unique_id", "cwx_ep_comm_create",
@@ -57,7 +57,8 @@ class MoeLayer(ctypes.Structure):
 
 
 class EpGroup(ctypes.Structure):
-    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("experts_per_rank", ctypes.c_int32)]
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("experts_per_rank", ctypes.c_int32),
+                ("placement", ctypes.c_void_p)]
 
 
 class MoeArgs(ctypes.Structure):
@@ -95,6 +96,7 @@ def lib() -> ctypes.CDLL:
             "cwx_bank_create": (I32, [I32, ctypes.POINTER(MatrixDesc), PP]),
             "cwx_bank_synth": (I32, [P, I32, I64, I64, I64, U64, F, PP]),
             "cwx_bank_synth_experts": (I32, [P, I32, I64, I64, I64, I64, U64, F, PP]),
+            "cwx_bank_synth_list": (I32, [P, I32, I64, I64, P, I64, U64, F, PP]),
             "cwx_bank_destroy": (I32, [P]),
             "cwx_bank_desc": (I32, [P, ctypes.POINTER(MatrixDesc)]),
             "cwx_bank_download": (I32, [P, I64, I64, P]),

@@ -990,8 +990,8 @@ extern "C" int cwx_ep_dispatch(cwx_ctx* c, const cwx_moe_layer* L, const cwx_ep_
             return rc;
         c->launches += 2;
     }
-    if ((rc = launch_ep_units(x, T, H, K, W, g->experts_per_rank, ids, weights, cnt, unit_of, pbase, send_counts,
-                              ep_rows_f16(L), send_rows, send_picks, st)))
+    if ((rc = launch_ep_units(x, T, H, K, W, g->experts_per_rank, g->placement, L->n_experts, ids, weights, cnt,
+                              unit_of, pbase, send_counts, ep_rows_f16(L), send_rows, send_picks, st)))
         return rc;
     c->launches += T > 0 ? 3 : 0;
     return CWX_OK;
@@ -1257,8 +1257,8 @@ extern "C" int cwx_ep_forward(cwx_ctx* c, cwx_ep_comm* comm, const cwx_moe_layer
                 return rc;
             c->launches += 2;
         }
-        if ((rc = launch_ep_units(x, T, H, K, W, epr, ids, wts, cnt, unit_of, pbase, scnt, f16, srows, spk, st, cap,
-                                  cap_rec)))
+        if ((rc = launch_ep_units(x, T, H, K, W, epr, g->placement, L->n_experts, ids, wts, cnt, unit_of, pbase, scnt,
+                                  f16, srows, spk, st, cap, cap_rec)))
             return rc;
         c->launches += T > 0 ? 3 : 0;
         t.end();

@@ -579,6 +579,44 @@ extern "C" int cwx_bank_synth_experts(cwx_ctx* ctx, int32_t type, int64_t n, int
     return CWX_OK;
 }
 
+extern "C" int cwx_bank_synth_list(cwx_ctx* ctx, int32_t type, int64_t n, int64_t k, const int64_t* experts,
+                                   int64_t count, uint64_t key, float std_, cwx_bank** out) {
+    if (!ctx || !experts || !out) return fail(CWX_EINVAL, "cwx_bank_synth_list: null argument");
+    for (int64_t i = 0; i < count; ++i)
+        if (experts[i] < 0) return fail(CWX_EINVAL, "cwx_bank_synth_list: expert %lld", (long long)experts[i]);
+    int rc = alloc_bank(ctx->device, type, n, k, count, out);
+    if (rc) return rc;
+    cwx_bank* b = *out;
+    if ((rc = ensure_maps(ctx))) {
+        cwx_bank_destroy(b);
+        *out = nullptr;
+        return rc;
+    }
+    // slot i holds global expert experts[i]: one launch per expert (k_synth's values follow the
+    // global index e0 + first, so slot i is its own one-expert bank with first = experts[i])
+    cudaError_t e = cudaSuccess;
+    const int threads = 128;
+    const int64_t items = n * b->L.n_kp;
+    for (int64_t i = 0; i < count && e == cudaSuccess; ++i) {
+        k_synth<<<(unsigned)((items + threads - 1) / threads), threads>>>(
+            b->d + i * b->L.expert_bytes, b->L, 0, 1, experts[i], key, std_,
+            SynthMaps{ctx->d_iq3s_map, ctx->d_iq2s_map, ctx->d_iq3xxs_map, ctx->d_iq2xxs_map});
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cwx_bank_destroy(b);
+        *out = nullptr;
+        return cuda_fail(e, "cwx_bank_synth_list");
+    }
+    if ((rc = mx_check(b, count))) {
+        cwx_bank_destroy(b);
+        *out = nullptr;
+        return rc;
+    }
+    return CWX_OK;
+}
+
 extern "C" int cwx_bank_destroy(cwx_bank* b) {
     if (!b) return CWX_OK;
     cudaSetDevice(b->device);

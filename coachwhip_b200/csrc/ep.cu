@@ -15,13 +15,22 @@
 
 namespace cwx {
 
+// Slot of expert e: rank slot / epr, local index slot % epr (the placement when there is one; a
+// slot out of range falls back to e, so no record can leave the valid ranks and experts).
+__device__ __forceinline__ uint32_t ep_slot(const int32_t* place, uint32_t e, int E) {
+    if (!place) return e;
+    const uint32_t s = (uint32_t)place[e];
+    return s < (uint32_t)E ? s : e;
+}
+
 // Picks of each token per destination rank: cnt[t * W + d].
-__global__ void k_ep_count(const uint32_t* __restrict__ ids, int T, int K, int epr, int W, int32_t* __restrict__ cnt) {
+__global__ void k_ep_count(const uint32_t* __restrict__ ids, int T, int K, int epr, int W,
+                           const int32_t* __restrict__ place, int E, int32_t* __restrict__ cnt) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= T) return;
     for (int d = 0; d < W; ++d) cnt[(int64_t)t * W + d] = 0;
     for (int j = 0; j < K; ++j) {
-        const int d = (int)(ids[(int64_t)t * K + j] / (uint32_t)epr);
+        const int d = (int)(ep_slot(place, ids[(int64_t)t * K + j], E) / (uint32_t)epr);
         cnt[(int64_t)t * W + d] += 1;
     }
 }
@@ -91,7 +100,8 @@ __global__ void __launch_bounds__(1024) k_ep_scan(const int32_t* __restrict__ cn
 // start at row d * cap and its records at d * cap_rec, whatever the other destinations hold.
 template <bool F16>
 __global__ void __launch_bounds__(256) k_ep_pack_units(const float* __restrict__ x, int T, int H, int K, int W,
-                                                       int epr, const uint32_t* __restrict__ ids,
+                                                       int epr, const int32_t* __restrict__ place, int E,
+                                                       const uint32_t* __restrict__ ids,
                                                        const float* __restrict__ w, int32_t* __restrict__ upos,
                                                        const int32_t* __restrict__ pbase,
                                                        const int32_t* __restrict__ tot, void* __restrict__ send_rows,
@@ -125,7 +135,7 @@ __global__ void __launch_bounds__(256) k_ep_pack_units(const float* __restrict__
         if (threadIdx.x == 0) {
             int32_t r = poff[d] + pbase[(int64_t)t * W + d];
             for (int j = 0; j < K; ++j) {
-                const uint32_t e = ids[(int64_t)t * K + j];
+                const uint32_t e = ep_slot(place, ids[(int64_t)t * K + j], E);
                 if ((int)(e / (uint32_t)epr) != d) continue;
                 send_picks[3 * (int64_t)r] = u;  // unit index within the message to d
                 send_picks[3 * (int64_t)r + 1] = (int32_t)(e % (uint32_t)epr);
@@ -248,21 +258,21 @@ static int launched(const char* what) {
     return e == cudaSuccess ? CWX_OK : cuda_fail(e, what);
 }
 
-int launch_ep_units(const float* x, int T, int H, int K, int W, int epr, const uint32_t* ids, const float* w,
-                    int32_t* cnt, int32_t* upos, int32_t* pbase, int32_t* tot, bool f16, void* send_rows,
-                    int32_t* send_picks, cudaStream_t st, int cap, int cap_rec) {
+int launch_ep_units(const float* x, int T, int H, int K, int W, int epr, const int32_t* place, int E,
+                    const uint32_t* ids, const float* w, int32_t* cnt, int32_t* upos, int32_t* pbase, int32_t* tot,
+                    bool f16, void* send_rows, int32_t* send_picks, cudaStream_t st, int cap, int cap_rec) {
     if (W > 64) return fail(CWX_EUNSUPPORTED, "expert parallelism over more than 64 ranks");
     if (T == 0) {
         CWX_CUDA(cudaMemsetAsync(tot, 0, (size_t)2 * W * 4, st));
         return CWX_OK;
     }
-    k_ep_count<<<(T + 255) / 256, 256, 0, st>>>(ids, T, K, epr, W, cnt);
+    k_ep_count<<<(T + 255) / 256, 256, 0, st>>>(ids, T, K, epr, W, place, E, cnt);
     k_ep_scan<<<W, 1024, 0, st>>>(cnt, T, W, upos, pbase, tot);
     if (f16)
-        k_ep_pack_units<true><<<T, 256, 0, st>>>(x, T, H, K, W, epr, ids, w, upos, pbase, tot, send_rows, send_picks,
+        k_ep_pack_units<true><<<T, 256, 0, st>>>(x, T, H, K, W, epr, place, E, ids, w, upos, pbase, tot, send_rows, send_picks,
                                                  cap, cap_rec);
     else
-        k_ep_pack_units<false><<<T, 256, 0, st>>>(x, T, H, K, W, epr, ids, w, upos, pbase, tot, send_rows, send_picks,
+        k_ep_pack_units<false><<<T, 256, 0, st>>>(x, T, H, K, W, epr, place, E, ids, w, upos, pbase, tot, send_rows, send_picks,
                                                   cap, cap_rec);
     return launched("expert-parallel dispatch kernels");
 }

@@ -97,9 +97,9 @@ struct EpOffsets {  // received records of source s: [pstart[s], pstart[s+1]); i
 // (-1: no picks there); tot (W, 2) = units and records per destination.
 // cap > 0: the fixed-capacity layout (destination d's units from row d * cap, records from
 // d * cap_rec); 0: destinations packed one after the other.
-int launch_ep_units(const float* x, int T, int H, int K, int W, int epr, const uint32_t* ids, const float* w,
-                    int32_t* cnt, int32_t* upos, int32_t* pbase, int32_t* tot, bool f16, void* send_rows,
-                    int32_t* send_picks, cudaStream_t st, int cap = 0, int cap_rec = 0);
+int launch_ep_units(const float* x, int T, int H, int K, int W, int epr, const int32_t* place, int E,
+                    const uint32_t* ids, const float* w, int32_t* cnt, int32_t* upos, int32_t* pbase, int32_t* tot,
+                    bool f16, void* send_rows, int32_t* send_picks, cudaStream_t st, int cap = 0, int cap_rec = 0);
 // The fixed-capacity receive side: records packed into picks (count into n_picks), unit runs.
 int launch_ep_recv_cap(const int32_t* picks, const int32_t* rcnt, int W, int cap, int cap_rec, uint32_t* rowmap,
                        uint32_t* eid, float* wgt, int32_t* first, int32_t* end, int32_t* n_picks, cudaStream_t st);

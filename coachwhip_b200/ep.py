@@ -30,6 +30,7 @@ from __future__ import annotations
 import ctypes
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -55,7 +56,11 @@ class CudaEngine:
 
     def __init__(self, gate: torch.Tensor, top_k: int, norm_topk_prob: bool, act, banks: tuple[Bank, Bank, Bank],
                  world: int, rank: int, gate_bias: torch.Tensor | None = None, shared: SharedExpert | None = None,
-                 act_mode: int = _lib.ACT_MODE_CANDLE):
+                 act_mode: int = _lib.ACT_MODE_CANDLE, placement=None):
+        """placement: None (rank r owns experts r*epr .. (r+1)*epr - 1), or the slot of every expert
+        (a permutation of 0 .. n_experts-1: expert e lives on rank slot // epr at local index
+        slot % epr; this rank's banks and expert biases then hold its experts in slot order, see
+        expert_lists)."""
         self.gate, self.gate_bias, self.shared = gate.contiguous(), gate_bias, shared
         self.n_experts, self.hidden = self.gate.shape
         if self.n_experts % world:
@@ -81,7 +86,13 @@ class CudaEngine:
             L.sh_gate_inp = shared.gate_inp.data_ptr()
         L.act_mode = act_mode
         self._layer = L
-        self._group = _lib.EpGroup(world, rank, self.epr)
+        self.placement = None
+        if placement is not None:
+            p = np.asarray(placement.cpu() if isinstance(placement, torch.Tensor) else placement, dtype=np.int64)
+            if p.shape != (self.n_experts,) or not np.array_equal(np.sort(p), np.arange(self.n_experts)):
+                raise ValueError("placement must be a permutation of the expert indices")
+            self.placement = torch.from_numpy(p.astype(np.int32)).to(self.gate.device)
+        self._group = _lib.EpGroup(world, rank, self.epr, _ptr(self.placement))
         self.row_dtype = torch.float16 if _lib.lib().cwx_ep_rows_f16(ctypes.byref(L)) else torch.float32
 
     def dispatch(self, x: torch.Tensor) -> Dispatched:
@@ -122,6 +133,34 @@ class CudaEngine:
                                         back.data_ptr(), _ptr(d.sgate), _ptr(residual), out.data_ptr(),
                                         _stream(d.x.device)))
         return out
+
+
+def balanced_placement(counts, world: int) -> np.ndarray:
+    """Slots of a placement that spreads the experts' expected picks (counts, e.g. of a calibration
+    batch) over `world` ranks of n_experts / world experts each: the experts in decreasing count,
+    each to the least loaded rank that still has room (ties to the lowest rank), in its next
+    local slot."""
+    counts = np.asarray(counts, dtype=np.float64)
+    E = counts.size
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    epr = E // world
+    load, used = np.zeros(world), np.zeros(world, dtype=np.int64)
+    slot = np.empty(E, dtype=np.int32)
+    for e in np.argsort(-counts, kind="stable"):
+        r = min((r for r in range(world) if used[r] < epr), key=lambda r: (load[r], r))
+        slot[e] = r * epr + used[r]
+        load[r] += counts[e]
+        used[r] += 1
+    return slot
+
+
+def expert_lists(slot, world: int) -> list[list[int]]:
+    """The experts of each rank in local-slot order under a placement."""
+    slot = np.asarray(slot)
+    epr = slot.size // world
+    order = np.argsort(slot)
+    return [order[r * epr:(r + 1) * epr].tolist() for r in range(world)]
 
 
 class ExpertParallelMoe:

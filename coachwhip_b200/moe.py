@@ -78,6 +78,15 @@ class Bank:
                                                 ctypes.byref(h)))
         return cls(h, ggml_type, n, k, n_experts, device)
 
+    @classmethod
+    def synth_list(cls, ggml_type: int, n: int, k: int, experts, key: int, std: float, device: int = 0) -> "Bank":
+        """Synthetic bank holding the listed experts of stream `key`, in list order."""
+        ids = np.ascontiguousarray(np.asarray(experts, dtype=np.int64))
+        h = ctypes.c_void_p()
+        check(_lib.lib().cwx_bank_synth_list(_lib.ctx(device), ggml_type, n, k, ids.ctypes.data, int(ids.size), key,
+                                             std, ctypes.byref(h)))
+        return cls(h, ggml_type, n, k, int(ids.size), device)
+
     @property
     def bytes_per_expert(self) -> int:
         return self.n * row_bytes(self.ggml_type, self.k)

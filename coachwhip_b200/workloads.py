@@ -130,15 +130,10 @@ class Layer:
     first: int = 0
 
 
-def build_layer(cfg: Config, layer: int, device: int = 0, act_mode: int = _lib.ACT_MODE_CANDLE,
-                first: int = 0, n_local: int | None = None, store: ExpertStore | None = None) -> Layer:
-    """Layer `layer` of configuration cfg, synthesised on `device`."""
-    E, H, I = cfg.n_experts, cfg.hidden, cfg.inter
-    ne = E if n_local is None else n_local
+def router(cfg: Config, layer: int, device: int = 0):
+    """The layer's router weight (E, H) and bias (E, or None: the router bias, plus the Zipf bias)."""
+    E, H = cfg.n_experts, cfg.hidden
     st = lambda t: stream(cfg.seed, layer, t)  # noqa: E731
-    g = Bank.synth(cfg.gate_type, I, H, ne, st(T_GATE), cfg.w_std, device, first=first)
-    u = Bank.synth(cfg.up_type, I, H, ne, st(T_UP), cfg.w_std, device, first=first)
-    d = Bank.synth(cfg.down_type, H, I, ne, st(T_DOWN), cfg.w_std, device, first=first)
     w = normal(E * H, st(T_RW), cfg.w_std, device).view(E, H)
     b = None
     if cfg.router_bias:
@@ -146,8 +141,34 @@ def build_layer(cfg: Config, layer: int, device: int = 0, act_mode: int = _lib.A
     if cfg.zipf:
         z = torch.from_numpy(zipf_bias(cfg)).to(f"cuda:{device}")
         b = z if b is None else b + z
+    return w, b
+
+
+def build_layer(cfg: Config, layer: int, device: int = 0, act_mode: int = _lib.ACT_MODE_CANDLE,
+                first: int = 0, n_local: int | None = None, store: ExpertStore | None = None,
+                experts=None) -> Layer:
+    """Layer `layer` of configuration cfg, synthesised on `device`. `experts` (a list of global
+    expert indices) makes an expert-parallel rank's layer under a placement: its banks and expert
+    biases hold those experts in list order."""
+    E, H, I = cfg.n_experts, cfg.hidden, cfg.inter
+    st = lambda t: stream(cfg.seed, layer, t)  # noqa: E731
+    if experts is not None:
+        experts = [int(e) for e in experts]
+        n_local = len(experts)
+        g = Bank.synth_list(cfg.gate_type, I, H, experts, st(T_GATE), cfg.w_std, device)
+        u = Bank.synth_list(cfg.up_type, I, H, experts, st(T_UP), cfg.w_std, device)
+        d = Bank.synth_list(cfg.down_type, H, I, experts, st(T_DOWN), cfg.w_std, device)
+    else:
+        ne = E if n_local is None else n_local
+        g = Bank.synth(cfg.gate_type, I, H, ne, st(T_GATE), cfg.w_std, device, first=first)
+        u = Bank.synth(cfg.up_type, I, H, ne, st(T_UP), cfg.w_std, device, first=first)
+        d = Bank.synth(cfg.down_type, H, I, ne, st(T_DOWN), cfg.w_std, device, first=first)
+    ne = E if n_local is None else n_local
+    w, b = router(cfg, layer, device)
     if cfg.act == _lib.ACT_CLAMPED_SWIGLU:
-        bias = lambda t, n: (normal(E * n, st(t), cfg.w_std, device).view(E, n)[first:first + ne].contiguous()  # noqa
+        rows = (slice(first, first + ne) if experts is None
+                else torch.tensor(experts, dtype=torch.long, device=f"cuda:{device}"))
+        bias = lambda t, n: (normal(E * n, st(t), cfg.w_std, device).view(E, n)[rows].contiguous()  # noqa
                              if cfg.expert_bias else None)
         act = ExpertAct.ClampedSwiglu(1.702, 7.0, bias(T_GB, I), bias(T_UB, I), bias(T_DB, H))
     else:

@@ -107,6 +107,11 @@ int cwx_bank_synth(cwx_ctx* ctx, int32_t ggml_type, int64_t n, int64_t k, int64_
  * the values follow the global expert index). */
 int cwx_bank_synth_experts(cwx_ctx* ctx, int32_t ggml_type, int64_t n, int64_t k, int64_t first, int64_t n_experts,
                            uint64_t key, float std_, cwx_bank** out);
+/* Synthetic bank of the listed experts (host array of count global expert indices), in list
+ * order: the same weights as cwx_bank_synth's bank of all experts holds for them (an
+ * expert-parallel rank's banks under a placement). */
+int cwx_bank_synth_list(cwx_ctx* ctx, int32_t ggml_type, int64_t n, int64_t k, const int64_t* experts, int64_t count,
+                        uint64_t key, float std_, cwx_bank** out);
 int cwx_bank_destroy(cwx_bank* bank);
 /* out[i] = std * N(0,1) element (offset + i) of stream `key`, i < n (synthetic router weights,
  * biases and inputs; same values as the CPU generator). */
@@ -238,8 +243,10 @@ int cwx_add_rms_norm(const float* a, const float* b, const float* c, const float
                      int32_t hidden, float* sum, float* out, void* stream);
 
 /* Expert parallelism (no counterpart in the reference, which runs one device): the experts are
- * split contiguously over `world` ranks, rank r owning experts [r*epr, (r+1)*epr); every rank
- * routes its own tokens. A token sends its row once to each rank that owns any of its picks (a
+ * split over `world` ranks, epr = n_experts / world each: contiguously (rank r owns experts
+ * [r*epr, (r+1)*epr)) or, when the group carries a placement, expert e on rank placement[e] / epr
+ * at local index placement[e] % epr (a permutation of 0 .. n_experts-1 in device memory, e.g. one
+ * that balances the ranks' expected picks); every rank routes its own tokens. A token sends its row once to each rank that owns any of its picks (a
  * unit), with one record per pick: (unit index in that message, the expert's index on that rank,
  * the pick's weight) as three int32 (the weight's f32 bits). A layer is three calls around two
  * all-to-all exchanges the caller makes (NCCL, or any transport):
@@ -261,6 +268,7 @@ int cwx_add_rms_norm(const float* a, const float* b, const float* c, const float
  * tokens * min(top_k, world) rows, send_picks tokens * top_k records. */
 typedef struct {
     int32_t world, rank, experts_per_rank;
+    const int32_t* placement; /* device array of n_experts slots, or NULL: contiguous ranges */
 } cwx_ep_group;
 int cwx_ep_rows_f16(const cwx_moe_layer* layer);
 int cwx_ep_dispatch(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_ep_group* group, const float* x,

@@ -106,24 +106,29 @@ class OracleEngine:
         return torch.from_numpy(out)
 
 
-def gpu_engine(L: dict, world: int, rank: int, device: int, act_mode: int):
-    """CudaEngine for rank `rank`: banks of its experts (and their bias rows) from the oracle's bytes."""
+def gpu_engine(L: dict, world: int, rank: int, device: int, act_mode: int, placement=None):
+    """CudaEngine for rank `rank`: banks of its experts (and their bias rows) from the oracle's bytes;
+    with a placement (every expert's slot), the experts it assigns to this rank in slot order."""
     import torch
 
-    from coachwhip_b200.ep import CudaEngine
+    from coachwhip_b200.ep import CudaEngine, expert_lists
     from coachwhip_b200.moe import Bank, ExpertAct, SharedExpert
 
     dev = f"cuda:{device}"
     H, E, I = L["hidden"], L["n_experts"], L["inter"]
     epr = E // world
-    e0, e1 = rank * epr, (rank + 1) * epr
-    sl = lambda name: L[f"{name}_bank"][e0 * expert_bytes(L, name):e1 * expert_bytes(L, name)]  # noqa: E731
+    mine = list(range(rank * epr, (rank + 1) * epr)) if placement is None else expert_lists(placement, world)[rank]
+
+    def sl(name):
+        b = expert_bytes(L, name)
+        return np.concatenate([L[f"{name}_bank"][e * b:(e + 1) * b] for e in mine])
+
     g = Bank.from_gguf_bytes(sl("gate"), L["gate_type"], I, H, epr, device)
     u = Bank.from_gguf_bytes(sl("up"), L["up_type"], I, H, epr, device)
     dn = Bank.from_gguf_bytes(sl("down"), L["down_type"], H, I, epr, device)
     t = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev)  # noqa
     if L.get("act", 0) == 1:
-        rows = lambda a: None if a is None else a[e0:e1]  # noqa: E731
+        rows = lambda a: None if a is None else a[mine]  # noqa: E731
         act = ExpertAct.ClampedSwiglu(L.get("alpha", 1.702), L.get("limit", 7.0), t(rows(L.get("gate_b"))),
                                       t(rows(L.get("up_b"))), t(rows(L.get("down_b"))))
     else:
@@ -136,7 +141,7 @@ def gpu_engine(L: dict, world: int, rank: int, device: int, act_mode: int):
                               Bank.from_gguf_bytes(L["sh_up"], L["sh_up_type"], Is, H, 1, device),
                               Bank.from_gguf_bytes(L["sh_down"], L["sh_down_type"], H, Is, 1, device))
     eng = CudaEngine(t(L["router_w"]), L["top_k"], bool(L["norm_topk_prob"]), act, (g, u, dn), world, rank,
-                     gate_bias=t(L.get("router_b")), shared=shared, act_mode=act_mode)
+                     gate_bias=t(L.get("router_b")), shared=shared, act_mode=act_mode, placement=placement)
     eng._keep = (act, shared, g, u, dn)
     return eng
 

@@ -98,3 +98,23 @@ def test_lost_peer_is_reported_not_waited_on():
     assert not any(alive)
     msg = q.get(timeout=5)
     assert msg.startswith("raised"), msg
+
+
+def test_balanced_placement():
+    # a permutation of the expert slots, equal experts per rank, and on skewed counts the busiest
+    # rank's load at most the mean plus the largest single count (the greedy bound)
+    from coachwhip_b200.ep import balanced_placement, expert_lists
+
+    rng = np.random.default_rng(0)
+    for E, W in ((16, 2), (512, 4), (512, 8), (8, 1)):
+        c = rng.zipf(1.3, E).astype(np.float64)
+        s = balanced_placement(c, W)
+        assert sorted(s.tolist()) == list(range(E))
+        lists = expert_lists(s, W)
+        assert [len(x) for x in lists] == [E // W] * W
+        for r, x in enumerate(lists):
+            assert [int(s[e]) for e in x] == [r * (E // W) + i for i in range(E // W)]
+        load = np.array([c[x].sum() for x in lists])
+        assert load.max() <= load.mean() + c.max() + 1e-9
+    with pytest.raises(ValueError):
+        balanced_placement(np.ones(10), 4)

@@ -45,6 +45,24 @@ def test_ep_emulated_ranks_match_oracle(name, T, world, mode):
     assert err < RTOL, err
 
 
+@pytest.mark.parametrize("name,T,world", [("iq_mix", 256, 4), ("mxfp4_gptoss", 64, 2), ("q4k", 24, 2)])
+def test_ep_emulated_ranks_under_a_placement(name, T, world):
+    # experts placed by a balanced placement of skewed counts (not contiguous ranges): each rank's
+    # banks and bias rows hold the experts the placement gives it, in slot order
+    from coachwhip_b200.ep import balanced_placement
+
+    s = SPECS[name]
+    L = build_cpu(s)
+    x = make_input(s, T)
+    counts = np.random.default_rng(5).zipf(1.5, s.n_experts).astype(np.float64)
+    place = balanced_placement(counts, world)
+    assert not np.array_equal(place, np.arange(s.n_experts))
+    for mode in (O.MODE_CANDLE, O.MODE_F32):
+        out = run_emulated([gpu_engine(L, world, r, 0, mode, placement=place) for r in range(world)], x)
+        err = rel_l2(out, O.moe_forward(L, x, mode)["out"])
+        assert err < RTOL, (mode, err)
+
+
 def test_ep_rank_with_no_tokens_and_no_picks():
     # every token routes to rank 0's experts: rank 1 receives nothing, and sends nothing back
     s = SPECS["q4k"]

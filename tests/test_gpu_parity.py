@@ -66,6 +66,11 @@ def test_synth_bank_matches_cpu_generator(fmt):
     # an expert-parallel rank's slice: experts 1 .. 2 of a 3-expert tensor equal those experts
     part = Bank.synth(fmt, n, k, 2, key, 0.02, first=1).download()
     assert np.array_equal(part, O.synth_matrix(fmt, key, 1, 2, n, k, 0.02))
+    # a rank's experts under a placement: a listed set, in list order
+    lst = Bank.synth_list(fmt, n, k, [4, 0, 2], key, 0.02).download()
+    bpe = lst.size // 3
+    for i, e in enumerate([4, 0, 2]):
+        assert np.array_equal(lst[i * bpe:(i + 1) * bpe], O.synth_matrix(fmt, key, e, 1, n, k, 0.02))
 
 
 def test_synth_normal_matches_cpu_generator():
