@@ -25,6 +25,9 @@ prefill:  config 2 (the config-1 weights at 1500 and 4096 tokens, bf16 input wid
           here (torch._scaled_mm, e4m3) and the nominal 4.5 PFLOP/s, and against sustained bf16.
 config3:  the gpt-oss-shaped stack (36 MXFP4 layers): decode 1 and 64 and prefill of 4096 tokens
           on one GPU; on N ranks the 4096-token prefill expert-parallel.
+gdn_word: the linear-attention step before the MoE block (cwx_gdn_word: conv, norms, gates, delta
+          rule, output norm and gate) over 30 layers of Qwen3-Next-shaped heads at 1 and 64
+          sequences, HBM roofline on its algorithmic bytes; CPU baseline the oracle's restatement.
 expert_parallel: config 4 (48 layers, 512 experts, Zipf-biased router, 8192 tokens): on one GPU
           the single-device layer (the anchor), on N ranks expert-parallel over NCCL with a per-phase
           breakdown and `ep_parity` (layer 0 on each rank's tokens against the single-device layer).
@@ -34,7 +37,7 @@ cpu_baseline: the vectorised CPU build of the same layer (oracle/fast.cpp: AVX2 
           the same bank per call; cpu_baseline_scalar: the step-for-step restatement (oracle/).
 
 usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cwx|reference] [--batch T]
-                       [--no-sweep] [--no-prefill] [--no-ep] [--no-c3] [--no-cpu] [--c3-layers L]
+                       [--no-sweep] [--no-prefill] [--no-ep] [--no-c3] [--no-gdn] [--no-cpu] [--c3-layers L]
                        [--prefill-tokens T ...] [--layers L]
 For N > 1 it runs under torchrun: config 1 does not shard (each rank runs its own replica;
 scaling "weak"); configs 3 and 4 shard their experts over the ranks (expert parallelism).
@@ -74,6 +77,9 @@ def parse():
     p.add_argument("--no-prefill", action="store_true")
     p.add_argument("--no-ep", action="store_true")
     p.add_argument("--no-c3", action="store_true", help="skip the config-3 (MXFP4, gpt-oss shape) runs")
+    p.add_argument("--no-gdn", action="store_true", help="skip the linear-attention word step before the MoE")
+    p.add_argument("--gdn-seqs", type=int, nargs="*", default=[1, 64],
+                   help="sequences per word step in the linear-attention runs (default 1 64)")
     p.add_argument("--c3-layers", type=int, default=36, help="config-3 layers (36; fewer for profiling)")
     p.add_argument("--c4-layers", type=int, default=48, help="config-4 layers (48; fewer for profiling)")
     p.add_argument("--prefill-tokens", type=int, nargs="*", default=None,
@@ -429,6 +435,116 @@ def fp8_peak(dev):
         return {"tflops": best, "how": "torch._scaled_mm e4m3 x e4m3 -> bf16, 8192^3, best of 5 x 5 (burst)"}
     except Exception as e:  # the roofline then uses the nominal figure only
         return {"tflops": None, "how": f"unavailable: {type(e).__name__}: {e}"[:200]}
+
+
+GDN_SHAPE = dict(n_k=16, n_v=32, dk=128, dv=128, taps=4, cycle=1)  # Qwen3-Next / Qwen3.6 linear attention
+GDN_LAYERS = 30  # the linear-attention layers of a 40-layer stack (every fourth layer is full attention)
+
+
+def gdn_bytes(n_seq, n_k, n_v, dk, dv, taps, **_):
+    """Algorithmic bytes of one word step over n_seq sequences: each head's memory read and
+    written, the conv window read and written, qkv, z, beta/alpha in, o out; the layer's conv
+    weights, dt_bias, a and norm_w once per launch."""
+    ch = 2 * n_k * dk + n_v * dv
+    per_seq = 4 * (2 * n_v * dk * dv + 2 * (taps - 1) * ch + ch + n_v * dv + 2 * n_v + n_v * dv)
+    return n_seq * per_seq + 4 * (ch * taps + 2 * n_v + dv)
+
+
+def gdn_runs(world, rank, local, a, pk, maxall, barrier):
+    """The Gated DeltaNet word step before the MoE block (cwx_gdn_word): GDN_LAYERS layers, each
+    with its own constants, memory and conv window, one word of n_seq sequences per layer, the
+    layers replayed as one CUDA graph; memory updated in place. Also the oracle's restatement of the
+    reference kernel on one host thread (one layer, one sequence), the CPU baseline of this step."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    from coachwhip_b200 import _lib
+    from coachwhip_b200 import workloads as W
+    from coachwhip_b200.gdn import GdnWord
+
+    dev = torch.device(f"cuda:{local}")
+    sh = GDN_SHAPE
+    n_k, n_v, dk, dv, taps = sh["n_k"], sh["n_v"], sh["dk"], sh["dv"], sh["taps"]
+    ch = 2 * n_k * dk + n_v * dv
+    out = {"config": f"{GDN_LAYERS} x GatedDeltaNet word step (n_k {n_k}, n_v {n_v}, dk {dk}, dv {dv}, {taps} taps, "
+                     "key heads cycled), f32; synthetic constants and inputs from the seeded generator",
+           "layers": GDN_LAYERS,
+           "kernel": "k_gdn_head (one CTA per head and sequence; other head shapes take k_gdn_word)"}
+    rng_key = lambda l, t: W.stream(7, l, t)  # noqa: E731
+    consts = []
+    for l in range(GDN_LAYERS):
+        consts.append(dict(conv_w=W.normal(ch * taps, rng_key(l, 0), 0.4, local).view(ch, taps),
+                           dt_bias=W.normal(n_v, rng_key(l, 1), 1.0, local),
+                           a=-torch.exp(W.normal(n_v, rng_key(l, 2), 1.0, local).abs()),
+                           norm_w=1.0 + W.normal(dv, rng_key(l, 3), 0.1, local)))
+    for n_seq in a.gdn_seqs:
+        ops, words = [], []
+        for l, c in enumerate(consts):
+            s = W.normal(n_seq * n_v * dk * dv, rng_key(l, 10 + n_seq), 0.1, local).view(n_seq, n_v, dk, dv)
+            cs = W.normal(n_seq * (taps - 1) * ch, rng_key(l, 11 + n_seq), 1.0, local).view(n_seq, taps - 1, ch)
+            ops.append(GdnWord(cs, c["conv_w"], c["dt_bias"], c["a"], c["norm_w"], s, n_k, n_v, dk, dv, taps, True,
+                               1e-6))
+            words.append(dict(qkv=W.normal(n_seq * ch, rng_key(l, 12 + n_seq), 1.0, local).view(n_seq, ch),
+                              z=W.normal(n_seq * n_v * dv, rng_key(l, 13 + n_seq), 1.0, local).view(n_seq, -1),
+                              ba=W.normal(n_seq * 2 * n_v, rng_key(l, 14 + n_seq), 1.0, local).view(n_seq, -1),
+                              o=torch.empty(n_seq, n_v * dv, device=dev),
+                              cv=torch.empty_like(cs)))
+        layers_c = [op.layer() for op in ops]
+
+        def step():
+            # the launches go to the stream being captured; the window moves to a buffer of its own
+            # (conv_out may not alias conv_state)
+            st = torch.cuda.current_stream(dev)
+            for op, w, L in zip(ops, words, layers_c):
+                _lib.check(_lib.lib().cwx_gdn_word(ctypes.byref(L), n_seq, w["qkv"].data_ptr(), w["z"].data_ptr(),
+                                                   w["ba"].data_ptr(), op.conv_state.data_ptr(), op.s.data_ptr(),
+                                                   w["o"].data_ptr(), op.s.data_ptr(), w["cv"].data_ptr(),
+                                                   st.cuda_stream))
+
+        g, _ = capture(step, dev)
+        barrier()
+        ms = maxall(time_graph(g, max(10, a.steps), a.warmup, dev))
+        del g
+        _lib.status(local)
+        alg = GDN_LAYERS * gdn_bytes(n_seq, **sh)
+        achieved = alg / (ms / 1e3) / 1e9
+        out[f"n_seq_{n_seq}"] = {"ms_per_stack": ms, "us_per_layer": ms * 1e3 / GDN_LAYERS,
+                                 "tokens_per_s": world * n_seq / (ms / 1e3),
+                                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
+                                              "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                                              "algorithmic_bytes_per_launch": alg / GDN_LAYERS,
+                                              "peak_source": "measured" if not pk.get("fallback") else "fallback"},
+                                 "l2": "each layer its own memory (2.1 MB per sequence, "
+                                       f"{GDN_LAYERS * n_seq * 2.1e-3:.2f} GB over the stack), read and written "
+                                       "once per word"}
+        print(f"[bench] gdn word, {n_seq} sequences: {ms * 1e3 / GDN_LAYERS:.2f} us/layer, "
+              f"{achieved:.0f} GB/s ({achieved / pk['hbm_gbs']:.3f} of HBM)", file=sys.stderr, flush=True)
+        del ops, words
+        torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and not a.no_cpu:
+        import oracle as O
+
+        rng = np.random.default_rng(0)
+        f = np.float32
+        args = [rng.standard_normal(ch).astype(f), rng.standard_normal(n_v * dv).astype(f),
+                rng.standard_normal(2 * n_v).astype(f), rng.standard_normal((taps - 1, ch)).astype(f),
+                (0.4 * rng.standard_normal((ch, taps))).astype(f), rng.standard_normal(n_v).astype(f),
+                -np.exp(np.abs(rng.standard_normal(n_v))).astype(f), (1 + 0.1 * rng.standard_normal(dv)).astype(f),
+                (0.1 * rng.standard_normal((n_v, dk, dv))).astype(f)]
+        O.gdn_word(n_k, n_v, dk, dv, taps, True, 1e-6, *args)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 3.0:
+            O.gdn_word(n_k, n_v, dk, dv, taps, True, 1e-6, *args)
+            n += 1
+        per = (time.perf_counter() - t0) / n
+        out["cpu_baseline"] = {"value": 1.0 / (GDN_LAYERS * per), "unit": "tokens/s (one sequence)", "cores": 1,
+                               "kind": "port", "per_layer_ms": per * 1e3,
+                               "sample": f"{n} calls of one layer's word step for one sequence through the oracle's "
+                                         "restatement of the reference kernel (oracle/gdn.cpp, one thread); "
+                                         f"tokens/s = 1 / ({GDN_LAYERS} x per-layer time)"}
+    return out
 
 
 def prefill_runs(cfg, mods, Ts, a, dev, local, pk, fp8, maxall, barrier, world):
@@ -852,6 +968,7 @@ def main():
         del mods_f32
     del mods, layers, store
     torch.cuda.empty_cache()
+    gdn = None if a.no_gdn else gdn_runs(world, rank, local, a, pk, maxall, barrier)
     c3 = None
     if not a.no_c3:
         c3 = c3_runs(world, rank, local, a, pk, maxall, barrier, fp8)
@@ -875,7 +992,7 @@ def main():
                 "cpu_baseline_scalar": cpu["scalar"] if cpu else None, "clocks": clocks,
                 "gpu_launches": int(launches_per_pass * DECODE_ITERS * a.steps),
                 "decode_sweep": {str(b): d for b, d in sweep.items()},
-                "prefill": prefill, "expert_parallel": ep, "config3": c3}
+                "prefill": prefill, "expert_parallel": ep, "config3": c3, "gdn_word": gdn}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -242,6 +242,43 @@ int cwx_moe_forward(cwx_ctx* ctx, const cwx_moe_layer* layer, const cwx_moe_args
 int cwx_add_rms_norm(const float* a, const float* b, const float* c, const float* alpha, float eps, int64_t rows,
                      int32_t hidden, float* sum, float* out, void* stream);
 
+/* The Gated DeltaNet mixer's middle for one word (the linear-attention step before the MoE block of
+ * Qwen3-Next / Qwen3.5 / Qwen3.6 layers). The layer's constants: n_k key heads and n_v value heads
+ * (n_v a multiple of n_k) of dims dk and dv; conv_w (channels, taps) with channels = 2 n_k dk +
+ * n_v dv (q of all key heads, k of all key heads, v of all value heads); dt_bias, a (n_v); norm_w
+ * (dv). cycle = 0: value head h reads key head h / (n_v / n_k) (Qwen3-Next's fused projection);
+ * cycle = 1: key head h % n_k (Qwen3.5 / 3.6). The fields of the reference's GdnWord
+ * (crates/engine/src/attn_kernel.rs:780-800) other than the per-word tensors. */
+typedef struct cwx_gdn_layer {
+    int32_t n_k, n_v, dk, dv, taps, cycle;
+    float eps;
+    const float* conv_w;
+    const float* dt_bias;
+    const float* a;
+    const float* norm_w;
+} cwx_gdn_layer;
+
+/* coachwhip_gdn_word / gdn_word (crates/engine/src/attn_kernel.rs:24-143, 880-895) for one word of
+ * each of n_seq independent sequences: conv over the window + SiLU, L2 norms of q and k, q scaled
+ * by 1/sqrt(dk), beta = sigmoid(b), g = exp(softplus(alpha + dt_bias) * a), the delta rule on each
+ * head's memory (S' = g S + k d^T, d = (v - g k.S) beta, o = q.S'), o RMS-normed times norm_w
+ * times silu(z). Per sequence: qkv (channels), z (n_v dv), ba (2 n_v: the raw beta of every value
+ * head, then the raw alpha), conv_state (taps - 1, channels), s (n_v, dk, dv); out: o (n_v dv),
+ * s_out (n_v, dk, dv), conv_out (taps - 1, channels); sequences follow one another in each array.
+ * All f32 device pointers. The reference's packed result is o | s_out | conv_out of one buffer.
+ * s_out may be s (the memory updated in place); conv_out must be a buffer of its own (CWX_EINVAL).
+ * CWX_EUNSUPPORTED for dk > 512 or dv > 256; CWX_EINVAL for bad dims, taps < 2, n_seq outside
+ * 0 .. 65535 or null pointers. */
+int cwx_gdn_word(const cwx_gdn_layer* layer, int32_t n_seq, const float* qkv, const float* z, const float* ba,
+                 const float* conv_state, const float* s, float* o, float* s_out, float* conv_out, void* stream);
+
+/* coachwhip_delta_word (crates/engine/src/delta_kernel.rs:20-50): the delta rule alone for one word,
+ * in the reference's layout: qk (heads, 2 dk) q then k (already normed and scaled), vbd (heads,
+ * dv + 2) v then beta then the decay g, s (heads, dk, dv); out (heads, dk dv + dv) the new memory
+ * then the read-out o. f32 device pointers; out must not be s. CWX_EUNSUPPORTED for dk > 512. */
+int cwx_delta_word(int32_t heads, int32_t dk, int32_t dv, const float* qk, const float* vbd, const float* s,
+                   float* out, void* stream);
+
 /* Expert parallelism (no counterpart in the reference, which runs one device): the experts are
  * split over `world` ranks, epr = n_experts / world each: contiguously (rank r owns experts
  * [r*epr, (r+1)*epr)) or, when the group carries a placement, expert e on rank placement[e] / epr

@@ -55,6 +55,9 @@ def lib() -> ctypes.CDLL:
             "cwo_matmul": (I32, [I32, I32, P, I64, I64, I64, U32, P, I32, P]),
             "cwo_moe_forward": (I32, [P, P, I32, I32, P, P, P, P, P]),
             "cwo_add_rms_norm": (I32, [P, P, P, P, F, I64, I32, P, P]),
+            "cwo_gdn_word": (I32, [I32] * 6 + [F] + [P] * 12),
+            "cwo_gdn_word_ops": (I32, [I32] * 6 + [F] + [P] * 12),
+            "cwo_delta_steps": (I32, [I32] * 4 + [P] * 7),
             "cwo_moe_forward_fast": (I32, [P, P, I32, P]),
             "cwo_set_threads": (None, [I32]),
             "cwo_get_threads": (I32, []),
@@ -262,6 +265,37 @@ def add_rms_norm(a: np.ndarray, b: np.ndarray, c: np.ndarray | None, alpha: np.n
     o = np.empty_like(a)
     assert lib().cwo_add_rms_norm(_p(a), _p(b), _p(c), _p(alpha), float(eps), rows, H, _p(s), _p(o)) == 0
     return s, o
+
+
+def gdn_word(n_k: int, n_v: int, dk: int, dv: int, taps: int, cycle: bool, eps: float, qkv, z, ba, conv_state,
+             conv_w, dt_bias, a, norm_w, s, ops: bool = False):
+    """One word of one sequence through the Gated DeltaNet step: the reference's fused kernel
+    (ops=False, attn_kernel.rs:24-143) or its op-by-op form (ops=True, model_next.rs:581-620).
+    ba = raw beta (n_v) then raw alpha (n_v). Returns (o (n_v*dv), s' (n_v, dk, dv),
+    conv_state' (taps-1, channels))."""
+    f = lambda x: np.ascontiguousarray(x, dtype=np.float32)  # noqa: E731
+    ch = 2 * n_k * dk + n_v * dv
+    ins = [f(t) for t in (qkv, z, ba, conv_state, conv_w, dt_bias, a, norm_w, s)]
+    o = np.empty(n_v * dv, np.float32)
+    s_out = np.empty((n_v, dk, dv), np.float32)
+    c_out = np.empty((taps - 1, ch), np.float32)
+    fn = lib().cwo_gdn_word_ops if ops else lib().cwo_gdn_word
+    assert fn(n_k, n_v, dk, dv, taps, int(bool(cycle)), float(eps), *[_p(t) for t in ins], _p(o), _p(s_out),
+              _p(c_out)) == 0
+    return o, s_out, c_out
+
+
+def delta_steps(q, k, v, beta, log_decay, s):
+    """The word-by-word delta rule (model_next.rs:17-38) over l words: q, k (l, n_v, dk), v (l, n_v,
+    dv), beta, log_decay (l, n_v), s (n_v, dk, dv). Returns (o (l, n_v, dv), s')."""
+    f = lambda x: np.ascontiguousarray(x, dtype=np.float32)  # noqa: E731
+    q, k, v, beta, log_decay = f(q), f(k), f(v), f(beta), f(log_decay)
+    s = np.array(s, dtype=np.float32, copy=True)
+    l, n_v, dk = q.shape
+    dv = v.shape[2]
+    o = np.empty((l, n_v, dv), np.float32)
+    assert lib().cwo_delta_steps(l, n_v, dk, dv, _p(q), _p(k), _p(v), _p(beta), _p(log_decay), _p(s), _p(o)) == 0
+    return o, s
 
 
 def set_threads(n: int) -> None:

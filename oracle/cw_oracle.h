@@ -116,6 +116,18 @@ int cwo_moe_forward_fast(const cwo_moe_layer* L, const float* x, int T, float* o
 // `hidden`, sum = (a + b) + c (c may be NULL) and out = rms_norm(sum) * alpha with candle-nn's
 // CPU RmsNorm arithmetic: sum2 = sequential f32 sum of v * v, m = sqrt(sum2 / hidden + eps),
 // out = v / m * alpha.
+/* Gated DeltaNet word step (gdn.cpp): the reference's one-kernel step (attn_kernel.rs:24-143) for
+ * one word of one sequence, its op-by-op form (model_next.rs:581-620), and the word-by-word delta
+ * rule (model_next.rs:17-38) over l words (s updated in place). */
+int cwo_gdn_word(int n_k, int n_v, int dk, int dv, int taps, int cycle, float eps, const float* qkv, const float* z,
+                 const float* ba, const float* conv_state, const float* conv_w, const float* dt_bias,
+                 const float* a_vec, const float* norm_w, const float* s, float* o, float* s_out, float* conv_out);
+int cwo_gdn_word_ops(int n_k, int n_v, int dk, int dv, int taps, int cycle, float eps, const float* qkv,
+                     const float* z, const float* ba, const float* conv_state, const float* conv_w,
+                     const float* dt_bias, const float* a_vec, const float* norm_w, const float* s, float* o,
+                     float* s_out, float* conv_out);
+int cwo_delta_steps(int l, int n_v, int dk, int dv, const float* q, const float* k, const float* v, const float* beta,
+                    const float* log_decay, float* s, float* o);
 int cwo_add_rms_norm(const float* a, const float* b, const float* c, const float* alpha, float eps, int64_t rows,
                      int hidden, float* sum, float* out);
 
