@@ -28,6 +28,8 @@ config3:  the gpt-oss-shaped stack (36 MXFP4 layers): decode 1 and 64 and prefil
 gdn_word: the linear-attention step before the MoE block (cwx_gdn_word: conv, norms, gates, delta
           rule, output norm and gate) over 30 layers of Qwen3-Next-shaped heads at 1 and 64
           sequences, HBM roofline on its algorithmic bytes; CPU baseline the oracle's restatement.
+attn_word: the gated full-attention step (cwx_attn_word: q/k norms, rope, cache append, split-K
+          softmax attention, gate) over 10 layers at 4096 cached rows, 1 and 64 sequences.
 expert_parallel: config 4 (48 layers, 512 experts, Zipf-biased router, 8192 tokens): on one GPU
           the single-device layer (the anchor), on N ranks expert-parallel over NCCL with a per-phase
           breakdown and `ep_parity` (layer 0 on each rank's tokens against the single-device layer).
@@ -77,7 +79,8 @@ def parse():
     p.add_argument("--no-prefill", action="store_true")
     p.add_argument("--no-ep", action="store_true")
     p.add_argument("--no-c3", action="store_true", help="skip the config-3 (MXFP4, gpt-oss shape) runs")
-    p.add_argument("--no-gdn", action="store_true", help="skip the linear-attention word step before the MoE")
+    p.add_argument("--no-gdn", action="store_true",
+                   help="skip the attention word steps before the MoE (linear and full attention)")
     p.add_argument("--gdn-seqs", type=int, nargs="*", default=[1, 64],
                    help="sequences per word step in the linear-attention runs (default 1 64)")
     p.add_argument("--c3-layers", type=int, default=36, help="config-3 layers (36; fewer for profiling)")
@@ -547,6 +550,108 @@ def gdn_runs(world, rank, local, a, pk, maxall, barrier):
     return out
 
 
+ATTN_SHAPE = dict(n_head=16, n_kv=2, hd=256, rot=64)  # Qwen3-Next / Qwen3.6 gated full attention
+ATTN_LAYERS = 10  # the full-attention layers of a 40-layer stack
+ATTN_CTX = 4096   # cached rows per sequence when the timed word arrives
+
+
+def attn_bytes(n_seq, ctx, n_head, n_kv, hd, **_):
+    """Algorithmic bytes of one full-attention word over n_seq sequences with ctx cached rows:
+    the K and V rows read (ctx + 1 each, the new row included), the new row written, qg, k, v in
+    and the output out."""
+    return n_seq * 4 * (2 * n_kv * (ctx + 1) * hd + 2 * n_kv * hd + 2 * n_head * hd + 2 * n_kv * hd + n_head * hd)
+
+
+def attn_runs(world, rank, local, a, pk, maxall, barrier):
+    """The gated full-attention word step (cwx_attn_word) at ATTN_CTX cached rows: ATTN_LAYERS layers,
+    each its own cache, one word of n_seq sequences per layer, replayed as one CUDA graph (the
+    cache lengths stay put: each replay writes the same row)."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    from coachwhip_b200 import _lib
+    from coachwhip_b200 import workloads as W
+    from coachwhip_b200.attn import FullAttn, KvCache
+
+    dev = torch.device(f"cuda:{local}")
+    sh = ATTN_SHAPE
+    n_head, n_kv, hd, rot = sh["n_head"], sh["n_kv"], sh["hd"], sh["rot"]
+    cap = ATTN_CTX + 64
+    out = {"config": f"{ATTN_LAYERS} x gated full-attention word step (n_head {n_head}, n_kv {n_kv}, hd {hd}, "
+                     f"rope on {rot}), {ATTN_CTX} cached rows per sequence, f32 caches; synthetic inputs",
+           "layers": ATTN_LAYERS,
+           "kernel": "k_attn_part (32 cache rows of one kv head per CTA, bulk copies) between k_attn_prep and "
+                     "k_attn_combine"}
+    key = lambda l, t: W.stream(8, l, t)  # noqa: E731
+    for n_seq in a.gdn_seqs:
+        layers = []
+        for l in range(ATTN_LAYERS):
+            att = FullAttn(1.0 + W.normal(hd, key(l, 0), 0.1, local), 1.0 + W.normal(hd, key(l, 1), 0.1, local),
+                           n_head, n_kv, hd, rot, 1e7, 1e-6)
+            cache = KvCache(n_seq, n_kv, cap, hd, dev)
+            cache.k.copy_(W.normal(cache.k.numel(), key(l, 2), 0.5, local).view_as(cache.k))
+            cache.v.copy_(W.normal(cache.v.numel(), key(l, 3), 1.0, local).view_as(cache.v))
+            cache.len.fill_(ATTN_CTX)
+            layers.append(dict(att=att, L=att.layer(), cache=cache,
+                               qg=W.normal(n_seq * n_head * 2 * hd, key(l, 4), 1.0, local),
+                               kn=W.normal(n_seq * n_kv * hd, key(l, 5), 1.0, local),
+                               vn=W.normal(n_seq * n_kv * hd, key(l, 6), 1.0, local),
+                               o=torch.empty(n_seq, n_head * hd, device=dev)))
+        ctx = _lib.ctx(local)
+
+        def step():
+            st = torch.cuda.current_stream(dev)  # (the stream being captured)
+            for y in layers:
+                c = y["cache"]
+                _lib.check(_lib.lib().cwx_attn_word(ctx, ctypes.byref(y["L"]), n_seq, c.cap, y["qg"].data_ptr(),
+                                                    y["kn"].data_ptr(), y["vn"].data_ptr(), c.k.data_ptr(),
+                                                    c.v.data_ptr(), c.len.data_ptr(), c.len.data_ptr(),
+                                                    y["o"].data_ptr(), st.cuda_stream))
+
+        g, _ = capture(step, dev)
+        barrier()
+        ms = maxall(time_graph(g, max(10, a.steps), a.warmup, dev))
+        del g
+        _lib.status(local)
+        alg = ATTN_LAYERS * attn_bytes(n_seq, ATTN_CTX, **sh)
+        achieved = alg / (ms / 1e3) / 1e9
+        out[f"n_seq_{n_seq}"] = {"ms_per_stack": ms, "us_per_layer": ms * 1e3 / ATTN_LAYERS,
+                                 "tokens_per_s": world * n_seq / (ms / 1e3),
+                                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
+                                              "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                                              "algorithmic_bytes_per_launch": alg / ATTN_LAYERS,
+                                              "peak_source": "measured" if not pk.get("fallback") else "fallback"},
+                                 "l2": f"each layer its own cache ({2 * n_kv * cap * hd * 4 * n_seq / 1e6:.0f} MB), "
+                                       f"{ATTN_LAYERS} layers per replay"}
+        print(f"[bench] attn word, {n_seq} sequences, {ATTN_CTX} rows: {ms * 1e3 / ATTN_LAYERS:.2f} us/layer, "
+              f"{achieved:.0f} GB/s ({achieved / pk['hbm_gbs']:.3f} of HBM)", file=sys.stderr, flush=True)
+        del layers
+        torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and not a.no_cpu:
+        import oracle as O
+
+        rng = np.random.default_rng(0)
+        f = np.float32
+        cap_c = ATTN_CTX + 1
+        args = [rng.standard_normal((n_head, 2 * hd)).astype(f), rng.standard_normal((n_kv, hd)).astype(f),
+                rng.standard_normal((n_kv, hd)).astype(f), np.ones(hd, f), np.ones(hd, f),
+                rng.standard_normal((n_kv, cap_c, hd)).astype(f), rng.standard_normal((n_kv, cap_c, hd)).astype(f)]
+        O.attn_word(n_head, n_kv, hd, rot, 1e-6, 1e7, ATTN_CTX, ATTN_CTX, *args)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 3.0:
+            O.attn_word(n_head, n_kv, hd, rot, 1e-6, 1e7, ATTN_CTX, ATTN_CTX, *args)
+            n += 1
+        per = (time.perf_counter() - t0) / n
+        out["cpu_baseline"] = {"value": 1.0 / (ATTN_LAYERS * per), "unit": "tokens/s (one sequence)", "cores": 1,
+                               "kind": "port", "per_layer_ms": per * 1e3,
+                               "sample": f"{n} calls of one layer's word step for one sequence at {ATTN_CTX} rows "
+                                         "through the oracle's restatement (oracle/gdn.cpp cwo_attn_word, one "
+                                         f"thread); tokens/s = 1 / ({ATTN_LAYERS} x per-layer time)"}
+    return out
+
+
 def prefill_runs(cfg, mods, Ts, a, dev, local, pk, fp8, maxall, barrier, world):
     """Config 2: one layer and the 40-layer stack at 1500 and 4096 tokens, bf16 input widened to
     f32 at entry (the reference casts to f32 at the layer's entry), f32 activation policy."""
@@ -969,6 +1074,7 @@ def main():
     del mods, layers, store
     torch.cuda.empty_cache()
     gdn = None if a.no_gdn else gdn_runs(world, rank, local, a, pk, maxall, barrier)
+    attn = None if a.no_gdn else attn_runs(world, rank, local, a, pk, maxall, barrier)
     c3 = None
     if not a.no_c3:
         c3 = c3_runs(world, rank, local, a, pk, maxall, barrier, fp8)
@@ -992,7 +1098,8 @@ def main():
                 "cpu_baseline_scalar": cpu["scalar"] if cpu else None, "clocks": clocks,
                 "gpu_launches": int(launches_per_pass * DECODE_ITERS * a.steps),
                 "decode_sweep": {str(b): d for b, d in sweep.items()},
-                "prefill": prefill, "expert_parallel": ep, "config3": c3, "gdn_word": gdn}
+                "prefill": prefill, "expert_parallel": ep, "config3": c3, "gdn_word": gdn,
+                "attn_word": attn}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -27,7 +27,7 @@ EXPORTS = [
     "cwx_gguf_tensor_info", "cwx_gguf_tensor", "cwx_bank_from_gguf", "cwx_gguf_tensor_f32", "cwx_gguf_meta_int",
     "cwx_gguf_meta_f64", "cwx_gguf_meta_str", "cwx_add_rms_norm", "cwx_ep_unique_id", "cwx_ep_comm_create",
     "cwx_ep_comm_wrap", "cwx_ep_comm_abort", "cwx_ep_comm_destroy", "cwx_ep_forward", "cwx_ctx_set_fused_decode",
-    "cwx_gdn_word", "cwx_delta_word",
+    "cwx_gdn_word", "cwx_delta_word", "cwx_attn_word",
 ]
 PHASES = ["router", "route", "piles", "prep", "gate_up", "down", "combine", "ep_dispatch", "ep_exchange",
           "ep_experts", "ep_return", "ep_combine", "decode_fused"]
@@ -67,6 +67,12 @@ class GdnLayer(ctypes.Structure):
                 ("taps", ctypes.c_int32), ("cycle", ctypes.c_int32), ("eps", ctypes.c_float),
                 ("conv_w", ctypes.c_void_p), ("dt_bias", ctypes.c_void_p), ("a", ctypes.c_void_p),
                 ("norm_w", ctypes.c_void_p)]
+
+
+class AttnLayer(ctypes.Structure):
+    _fields_ = [("n_head", ctypes.c_int32), ("n_kv", ctypes.c_int32), ("hd", ctypes.c_int32), ("rot", ctypes.c_int32),
+                ("eps", ctypes.c_float), ("freq_base", ctypes.c_double), ("q_norm_w", ctypes.c_void_p),
+                ("k_norm_w", ctypes.c_void_p)]
 
 
 class MoeArgs(ctypes.Structure):
@@ -141,6 +147,7 @@ def lib() -> ctypes.CDLL:
             "cwx_ctx_set_fused_decode": (I32, [P, I32]),
             "cwx_gdn_word": (I32, [ctypes.POINTER(GdnLayer), I32, P, P, P, P, P, P, P, P, P]),
             "cwx_delta_word": (I32, [I32, I32, I32, P, P, P, P, P]),
+            "cwx_attn_word": (I32, [P, ctypes.POINTER(AttnLayer), I32, I32, P, P, P, P, P, P, P, P, P]),
             "cwx_ep_unique_id": (I32, [P, I64]),
             "cwx_ep_comm_create": (I32, [I32, P, I32, I32, PP]),
             "cwx_ep_comm_wrap": (I32, [P, I32, I32, I32, PP]),

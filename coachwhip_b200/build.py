@@ -17,7 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libcwx.so")
 SOURCES = ["api.cu", "bank.cu", "route.cu", "gemv.cu", "act.cu", "noalloc.cu", "mma.cu", "ep.cu", "ep_nccl.cu",
-           "decode_layer.cu", "gdn.cu", "gguf.cpp"]
+           "decode_layer.cu", "gdn.cu", "attn.cu", "gguf.cpp"]
 NO_FMA = {"bank.cu"}
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -52,7 +52,7 @@ struct Carve {
     }
 };
 
-static int ensure_ws(cwx_ctx* ctx, size_t bytes, cudaStream_t st) {
+int ensure_ws(cwx_ctx* ctx, size_t bytes, cudaStream_t st) {
     if (bytes <= ctx->ws_bytes) return CWX_OK;
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(st, &cap);
@@ -405,6 +405,7 @@ extern "C" int cwx_ctx_status(cwx_ctx* c, void* stream) {
     CWX_CUDA(cudaMemset(c->d_err, 0, 64));  // (a timed-out grid barrier leaves its counter off step)
     if (h == DE_TIMEOUT) return fail(CWX_ETIMEOUT, "a device-side wait gave up (bulk copy did not complete)");
     if (h == DE_BAD_ID) return fail(CWX_EDEVICE, "an expert id was out of range");
+    if (h == DE_SHAPE) return fail(CWX_EDEVICE, "a length read on the device was out of range (attention cache row)");
     return fail(CWX_EDEVICE, "device error %d", h);
 }
 

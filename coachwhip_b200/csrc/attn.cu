@@ -1,0 +1,394 @@
+// The full-attention word step: the gated attention layers (one in four) of the Qwen3-Next /
+// Qwen3.5 / Qwen3.6 stacks, for one word of each of n_seq sequences, between the projections.
+//
+// Follows FullAttn::forward for one word (crates/engine/src/model_next.rs:666-720, rope :653-664,
+// the KV cache KvBuf::append :74-130 without its roll): q = q_norm(q part of the wq output),
+// gate = its second half, k = k_norm(wk output), rope on the first `rot` values of q and k at
+// the word's position (non-interleaved halves, inverse frequencies base^(-2i/rot) in f64 rounded
+// to f32), k and v appended to the sequence's cache at row len, then for every query head the
+// softmax of q.K^T / sqrt(hd) over rows 0 .. len of its kv head (head h reads kv head
+// h / (n_head / n_kv)) times V, times sigmoid(gate).
+//
+// Layout of the work (split-K decoding), three launches:
+//   k_attn_prep: one warp per query head (normalised, rotated into the workspace) and per kv head
+//     (the new k, normalised and rotated, and v written to the caches at row len);
+//   k_attn_part: a CTA takes 32 cache rows of one kv head of one sequence (grid = ceil(cap / 32) x
+//     n_kv x n_seq; CTAs past the sequence's length return at once). One thread starts three bulk
+//     copies (cp.async.bulk) into shared memory: the chunk's K rows, its V rows and the kv head's
+//     prepared query heads; the CTA scores the rows for all query heads at once (each warp 4 rows,
+//     each lane hd / 32 values of a row, the (head, row) sums finished by a reduce-scatter
+//     butterfly), takes the chunk's softmax (max, exp, sum) and the probabilities times V;
+//   k_attn_combine: per query head the chunks merged in parallel (max-rescaled) and the gate.
+// The rows of K and V are read once: HBM-bound at long caches.
+#include <math.h>
+
+#include "cwx_common.cuh"
+
+namespace cwx {
+
+namespace att {
+constexpr int W = 8;
+constexpr int T = W * 32;
+constexpr int CHUNK = 32;   // cache rows per CTA, 4 per warp
+constexpr int MAX_G = 16;   // query heads per kv head
+constexpr int MAX_HD = 256;
+constexpr int HG = 4;       // query heads per scoring pass (4 heads x 4 rows: one sum per half-warp lane)
+}  // namespace att
+
+struct AttnArgs {
+    int n_head, n_kv, hd, rot, n_split, cap;
+    float eps, scale;
+    double freq_base;
+    const float* qg;
+    const float* k_new;
+    const float* v_new;
+    float* k_cache;
+    float* v_cache;
+    const int32_t* len;
+    const int32_t* pos;
+    const float* q_norm_w;
+    const float* k_norm_w;
+    float* qn;    // workspace: the normalised, rotated query heads (n_seq, n_head, hd)
+    float* part;  // workspace: per chunk and query head the hd weighted sums (n_seq, n_kv, n_split, g, hd)
+    float* ml;    // workspace: per chunk and query head the chunk's max and exp total (.., g, 2)
+    float* out;
+    int* err;
+};
+
+__device__ __forceinline__ float att_warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float att_warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// One level of the reduce-scatter butterfly over N values per lane: the lanes with bit N/2 set
+// keep the upper half, the others the lower half, each adding its partner's copy.
+template <int N>
+__device__ __forceinline__ void rs_level(float* v, int lane) {
+    constexpr int H = N / 2;
+    const bool up = (lane & H) != 0;
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+        const float send = up ? v[i] : v[i + H];
+        const float keep = up ? v[i + H] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, H);
+    }
+}
+
+// RmsNorm of one head row (candle's: x / sqrt(mean(x^2) + eps) * w) then rope on its first rot
+// values at position p, by one warp, into y (shared memory).
+__device__ void norm_rope_row(const float* x, const float* w, int hd, int rot, float eps, double base, int p,
+                              float* y, int lane) {
+    float ss = 0.f;
+    for (int d = lane; d < hd; d += 32) ss += x[d] * x[d];
+    ss = att_warp_sum(ss);
+    const float r = sqrtf(ss / (float)hd + eps);
+    for (int d = lane; d < hd; d += 32) y[d] = x[d] / r * w[d];
+    __syncwarp();
+    const int half = rot / 2;
+    for (int i = lane; i < half; i += 32) {
+        const float inv = (float)(1.0 / pow(base, (2.0 * i) / (double)rot));
+        const float f = (float)p * inv;
+        const float c = cosf(f), s = sinf(f);
+        const float a = y[i], b = y[i + half];
+        y[i] = a * c - b * s;
+        y[i + half] = a * s + b * c;
+    }
+    __syncwarp();
+}
+
+// This lane's DPL values of a row (hd = 32 DPL floats at `row`): 16-byte pieces lane, lane + 32
+// (DPL 8), so a warp's loads cover consecutive 512-byte spans (no shared-memory bank conflicts);
+// q and k use the same mapping, which is all a dot product needs.
+template <int DPL>
+__device__ __forceinline__ void load_row(const float* row, int lane, float* k) {
+    if (DPL == 8) {
+        const float4 a = reinterpret_cast<const float4*>(row)[lane], b = reinterpret_cast<const float4*>(row)[lane + 32];
+        k[0] = a.x; k[1] = a.y; k[2] = a.z; k[3] = a.w;
+        k[4] = b.x; k[5] = b.y; k[6] = b.z; k[7] = b.w;
+    } else if (DPL == 4) {
+        const float4 a = reinterpret_cast<const float4*>(row)[lane];
+        k[0] = a.x; k[1] = a.y; k[2] = a.z; k[3] = a.w;
+    } else {
+        const float2 a = reinterpret_cast<const float2*>(row)[lane];
+        k[0] = a.x; k[1] = a.y;
+    }
+}
+
+// Value j of this lane's DPL values under load_row's mapping.
+template <int DPL>
+__device__ __forceinline__ int dim_of(int lane, int j) {
+    return DPL == 8 ? (j < 4 ? 4 * lane + j : 128 + 4 * lane + j - 4) : DPL * lane + j;
+}
+
+// Query head blockIdx.x < n_head of sequence blockIdx.y: normalised and rotated into the workspace;
+// blockIdx.x = n_head + j: kv head j's new k (normalised, rotated) and v into the caches at row len.
+// One warp each.
+__global__ void __launch_bounds__(32) k_attn_prep(AttnArgs p) {
+    __shared__ float y[att::MAX_HD];
+    const int lane = threadIdx.x, seq = blockIdx.y, hd = p.hd;
+    pdl_wait();
+    const int L = p.len[seq];
+    if (L < 0 || L >= p.cap) {
+        if (lane == 0 && blockIdx.x == 0) dev_error(p.err, DE_SHAPE);
+        return;
+    }
+    const int P = p.pos[seq];
+    if ((int)blockIdx.x < p.n_head) {
+        const int64_t h = (int64_t)seq * p.n_head + blockIdx.x;
+        norm_rope_row(p.qg + h * 2 * hd, p.q_norm_w, hd, p.rot, p.eps, p.freq_base, P, y, lane);
+        for (int d = lane; d < hd; d += 32) p.qn[h * hd + d] = y[d];
+    } else {
+        const int kvh = blockIdx.x - p.n_head;
+        const int64_t nr = ((int64_t)seq * p.n_kv + kvh) * hd;
+        norm_rope_row(p.k_new + nr, p.k_norm_w, hd, p.rot, p.eps, p.freq_base, P, y, lane);
+        const int64_t row = (((int64_t)seq * p.n_kv + kvh) * p.cap + L) * hd;
+        for (int d = lane; d < hd; d += 32) {
+            p.k_cache[row + d] = y[d];
+            p.v_cache[row + d] = p.v_new[nr + d];
+        }
+    }
+}
+
+// Rows 32 blockIdx.x .. of kv head blockIdx.y of sequence blockIdx.z; DPL = hd / 32. Dynamic
+// shared memory: the chunk's K rows, its V rows (32 hd floats each) and the kv head's g prepared
+// query heads (g hd), brought by three bulk copies.
+template <int DPL>
+__global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
+    using namespace att;
+    extern __shared__ __align__(16) float kv_sm[];
+    __shared__ float pr[CHUNK][MAX_G + 1];  // scores, then exp(s - m), per row
+    __shared__ float mh[MAX_G], lh[MAX_G];
+    __shared__ __align__(8) uint64_t bar;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+    constexpr int hd = 32 * DPL;
+    const int g = p.n_head / p.n_kv;
+    float* Ks = kv_sm;
+    float* Vs = kv_sm + CHUNK * hd;
+    float* Qs = kv_sm + 2 * CHUNK * hd;
+
+    pdl_wait();  // (the prep kernel's query heads and new cache row)
+    const int L = p.len[seq];
+    if (L < 0 || L >= p.cap) return;  // (recorded by k_attn_prep)
+    const int p0 = r * CHUNK;
+    if (p0 > L) return;
+    const int n = min(p0 + CHUNK, L + 1) - p0;
+    const int64_t kvrow0 = ((int64_t)seq * p.n_kv + kvh) * p.cap;  // first cache row of this kv head
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        const uint32_t bytes = (uint32_t)(n * hd * 4), qb = (uint32_t)(g * hd * 4);
+        mbar_expect_tx(&bar, 2 * bytes + qb);
+        bulk_g2s(Ks, p.k_cache + (kvrow0 + p0) * hd, bytes, &bar);
+        bulk_g2s(Vs, p.v_cache + (kvrow0 + p0) * hd, bytes, &bar);
+        bulk_g2s(Qs, p.qn + ((int64_t)seq * p.n_head + kvh * g) * hd, qb, &bar);
+    }
+    __syncthreads();  // (the barrier's init is visible to every waiting thread)
+    if (!mbar_wait(&bar, 0, p.err)) {  // a copy that did not complete in time (recorded): wait once
+        mbar_wait(&bar, 0, p.err);     // more, bounded, then leave
+        return;
+    }
+
+    // scores: warp rows 4 warp .. + 3 of the chunk, HG query heads per pass; 4 x 4 (head, row)
+    // sums per lane, finished by a reduce-scatter over 16 lanes and one exchange across the halves
+    constexpr int RW = CHUNK / W;  // rows per warp (4)
+    for (int hg = 0; hg < g; hg += HG) {
+        float q[HG][DPL];
+#pragma unroll
+        for (int hh = 0; hh < HG; ++hh) {
+            if (hg + hh < g) {
+                load_row<DPL>(Qs + (hg + hh) * hd, lane, q[hh]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < DPL; ++j) q[hh][j] = 0.f;
+            }
+        }
+        float v[HG * RW];
+#pragma unroll
+        for (int jp = 0; jp < RW; ++jp) {
+            float k[DPL];
+            load_row<DPL>(Ks + (warp * RW + jp) * hd, lane, k);  // (rows past n hold stale data: masked below)
+#pragma unroll
+            for (int hh = 0; hh < HG; ++hh) {
+                float s = 0.f;
+#pragma unroll
+                for (int j = 0; j < DPL; ++j) s += q[hh][j] * k[j];
+                v[hh * RW + jp] = s;
+            }
+        }
+        rs_level<16>(v, lane);
+        rs_level<8>(v, lane);
+        rs_level<4>(v, lane);
+        rs_level<2>(v, lane);
+        const float sum = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 16);
+        const int hh = (lane & 15) >> 2, jp = lane & 3;  // the (head, row) whose sum this lane holds
+        const int row = warp * RW + jp;
+        if (lane < 16 && hg + hh < g) pr[row][hg + hh] = row < n ? sum * p.scale : -INFINITY;
+    }
+    __syncthreads();
+
+    // the chunk's softmax per query head (lane = row)
+    for (int hh = warp; hh < g; hh += W) {
+        const float a = pr[lane][hh];
+        const float m = att_warp_max(a);
+        const float ea = expf(a - m);
+        const float l = att_warp_sum(ea);
+        pr[lane][hh] = ea;
+        if (lane == 0) {
+            mh[hh] = m;
+            lh[hh] = l;
+        }
+    }
+    __syncthreads();
+
+    // exp-weighted sum of the V rows: thread d holds value d for every query head
+    const int64_t chunk = ((int64_t)seq * p.n_kv + kvh) * p.n_split + r;
+    if (tid < hd) {
+        float acc[MAX_G];
+#pragma unroll
+        for (int hh = 0; hh < MAX_G; ++hh) acc[hh] = 0.f;
+        for (int row = 0; row < n; ++row) {
+            const float vv = Vs[row * hd + tid];
+#pragma unroll
+            for (int hh = 0; hh < MAX_G; ++hh)
+                if (hh < g) acc[hh] += pr[row][hh] * vv;
+        }
+        float* part = p.part + chunk * g * hd;
+#pragma unroll
+        for (int hh = 0; hh < MAX_G; ++hh)
+            if (hh < g) part[hh * hd + tid] = acc[hh];
+    }
+    if (tid < g) {
+        p.ml[(chunk * g + tid) * 2] = mh[tid];
+        p.ml[(chunk * g + tid) * 2 + 1] = lh[tid];
+    }
+}
+
+// Query head blockIdx.x of sequence blockIdx.y: the chunks merged (warp w takes chunks w, w + 8,
+// ..; the warps' sums then added in warp order), each rescaled by exp(m_chunk - M), divided by the
+// softmax total, times sigmoid(gate).
+template <int DPL>
+__global__ void __launch_bounds__(att::T) k_attn_combine(AttnArgs p) {
+    using namespace att;
+    __shared__ float red[W][MAX_HD + 1];
+    __shared__ float dred[W], mx[W];
+    const int h = blockIdx.x, seq = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int hd = 32 * DPL;
+    pdl_wait();
+    const int L = p.len[seq];
+    if (L < 0 || L >= p.cap) return;  // (recorded by k_attn_prep)
+    const int g = p.n_head / p.n_kv, kvh = h / g, hh = h % g;
+    const int n_act = L / CHUNK + 1;
+    const int64_t c0 = ((int64_t)seq * p.n_kv + kvh) * p.n_split;  // first chunk of this kv head
+    const float* ml = p.ml + (c0 * g + hh) * 2;                     // chunk r at ml[2 g r]
+    const float* sums = p.part + (c0 * g + hh) * hd;                // chunk r at sums[g hd r]
+    float m = -INFINITY;
+    for (int r = tid; r < n_act; r += T) m = fmaxf(m, ml[(int64_t)r * 2 * g]);
+    m = att_warp_max(m);
+    if (lane == 0) mx[warp] = m;
+    __syncthreads();
+    float M = mx[0];
+#pragma unroll
+    for (int w = 1; w < W; ++w) M = fmaxf(M, mx[w]);
+    float num[DPL], den = 0.f;
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) num[j] = 0.f;
+    for (int r = warp; r < n_act; r += W) {
+        const float e = expf(ml[(int64_t)r * 2 * g] - M);
+        den += e * ml[(int64_t)r * 2 * g + 1];
+        float v[DPL];
+        load_row<DPL>(sums + (int64_t)r * g * hd, lane, v);
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) num[j] += e * v[j];
+    }
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) red[warp][dim_of<DPL>(lane, j)] = num[j];
+    if (lane == 0) dred[warp] = den;
+    __syncthreads();
+    if (tid < hd) {
+        float o = 0.f, D = 0.f;
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+            o += red[w][tid];
+            D += dred[w];
+        }
+        const float gt = p.qg[((int64_t)seq * p.n_head + h) * 2 * hd + hd + tid];
+        p.out[((int64_t)seq * p.n_head + h) * hd + tid] = (o / D) * (1.0f / (1.0f + expf(-gt)));
+    }
+}
+
+template <int DPL>
+static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const AttnArgs& a) {
+    static bool attr = false;  // (the dynamic shared memory limit, once per instantiation)
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_part<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (2 * att::CHUNK + att::MAX_G) * 32 * DPL * (int)sizeof(float));
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    cudaError_t e = launch_pdl(k_attn_prep, dim3(a.n_head + a.n_kv, grid.z), dim3(32), 0, st, a);
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(k_attn_part<DPL>, grid, dim3(att::T), smem, st, a);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_attn_combine<DPL>, dim3(a.n_head, grid.z), dim3(att::T), 0, st, a);
+}
+
+}  // namespace cwx
+
+using namespace cwx;
+
+extern "C" int cwx_attn_word(cwx_ctx* c, const cwx_attn_layer* L, int32_t n_seq, int32_t cap, const float* qg,
+                             const float* k_new, const float* v_new, float* k_cache, float* v_cache,
+                             const int32_t* len, const int32_t* pos, float* out, void* stream) {
+    if (!L) return fail(CWX_EINVAL, "cwx_attn_word: null layer");
+    if (L->n_head < 1 || L->n_kv < 1 || L->n_head % L->n_kv != 0 || L->n_kv > 65535)
+        return fail(CWX_EINVAL, "cwx_attn_word: %d query heads over %d kv heads", L->n_head, L->n_kv);
+    if (L->n_head / L->n_kv > att::MAX_G)
+        return fail(CWX_EUNSUPPORTED, "cwx_attn_word: %d query heads per kv head (at most %d)", L->n_head / L->n_kv,
+                    att::MAX_G);
+    if (L->hd != 64 && L->hd != 128 && L->hd != 256)
+        return fail(CWX_EUNSUPPORTED, "cwx_attn_word: head dim %d (64, 128 or 256)", L->hd);
+    if (L->rot < 0 || L->rot > L->hd || L->rot % 2 != 0)
+        return fail(CWX_EINVAL, "cwx_attn_word: rotary dims %d for head dim %d", L->rot, L->hd);
+    if (!(L->eps >= 0.f) || !(L->freq_base > 0.0))
+        return fail(CWX_EINVAL, "cwx_attn_word: eps %g, freq_base %g", (double)L->eps, L->freq_base);
+    if (n_seq < 0 || n_seq > 65535 || cap < 1) return fail(CWX_EINVAL, "cwx_attn_word: n_seq %d, cap %d", n_seq, cap);
+    if (!L->q_norm_w || !L->k_norm_w) return fail(CWX_EINVAL, "cwx_attn_word: null norm weights");
+    if (!c) return fail(CWX_EINVAL, "cwx_attn_word: null context");
+    if (n_seq == 0) return CWX_OK;
+    if (!qg || !k_new || !v_new || !k_cache || !v_cache || !len || !pos || !out)
+        return fail(CWX_EINVAL, "cwx_attn_word: null argument");
+    if ((((uintptr_t)k_cache | (uintptr_t)v_cache) & 15) != 0)
+        return fail(CWX_EINVAL, "cwx_attn_word: the caches must be 16-byte aligned");
+    CWX_CUDA(cudaSetDevice(c->device));
+    const cudaStream_t st = (cudaStream_t)stream;
+    const int g = L->n_head / L->n_kv;
+    const int n_split = (cap + att::CHUNK - 1) / att::CHUNK;
+    const size_t f4 = sizeof(float);
+    const size_t qn_b = (((size_t)n_seq * L->n_head * L->hd * f4) + 255) & ~(size_t)255;
+    const size_t part_b = (((size_t)n_seq * L->n_kv * n_split * g * L->hd * f4) + 255) & ~(size_t)255;
+    const size_t ml_b = (size_t)n_seq * L->n_kv * n_split * g * 2 * f4;
+    int rc = ensure_ws(c, qn_b + part_b + ml_b, st);
+    if (rc) return rc;
+    float* ws = reinterpret_cast<float*>(c->ws);
+    AttnArgs a{L->n_head, L->n_kv, L->hd, L->rot, n_split, cap, L->eps, (float)(1.0 / sqrt((double)L->hd)),
+               L->freq_base, qg, k_new, v_new, k_cache, v_cache, len, pos, L->q_norm_w, L->k_norm_w,
+               ws, ws + qn_b / f4, ws + (qn_b + part_b) / f4, out, c->d_err};
+    const dim3 grid(n_split, L->n_kv, n_seq);
+    const size_t smem = (2 * att::CHUNK + g) * L->hd * f4;
+    cudaError_t e;
+    switch (L->hd) {
+        case 64: e = launch_attn<2>(grid, smem, st, a); break;
+        case 128: e = launch_attn<4>(grid, smem, st, a); break;
+        default: e = launch_attn<8>(grid, smem, st, a); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cwx_attn_word launch");
+    c->launches += 3;
+    return CWX_OK;
+}

@@ -251,6 +251,8 @@ namespace cwx {
 void set_error(const char* fmt, ...);
 int fail(int code, const char* fmt, ...);
 int cuda_fail(cudaError_t e, const char* what);
+// Grows the context workspace to at least `bytes` (refused while `st` is capturing a graph).
+int ensure_ws(cwx_ctx* ctx, size_t bytes, cudaStream_t st);
 
 #define CWX_CUDA(call)                                 \
     do {                                               \

@@ -272,6 +272,35 @@ typedef struct cwx_gdn_layer {
 int cwx_gdn_word(const cwx_gdn_layer* layer, int32_t n_seq, const float* qkv, const float* z, const float* ba,
                  const float* conv_state, const float* s, float* o, float* s_out, float* conv_out, void* stream);
 
+/* The gated full-attention layer's constants (FullAttn, crates/engine/src/model_next.rs:636-650):
+ * n_head query heads over n_kv kv heads (n_head a multiple of n_kv, at most 16 per kv head), head
+ * dim hd (64, 128 or 256), rope on the first rot values of each head (even, <= hd) with base
+ * freq_base, q_norm_w and k_norm_w (hd) the per-head RmsNorm weights with eps. */
+typedef struct cwx_attn_layer {
+    int32_t n_head, n_kv, hd, rot;
+    float eps;
+    double freq_base;
+    const float* q_norm_w;
+    const float* k_norm_w;
+} cwx_attn_layer;
+
+/* FullAttn::forward for one word (crates/engine/src/model_next.rs:666-720, rope :653-664, KvBuf
+ * append :74-130 without its roll) of each of n_seq sequences, between the projections:
+ * q = q_norm(qg's first hd values per head), gate = its second hd values, k = k_norm(k_new), rope
+ * (non-interleaved halves) on q and k at position pos[s], k and v_new appended to the caches at row
+ * len[s], per query head softmax(q.K^T / sqrt(hd)) over rows 0 .. len[s] of its kv head (head h reads
+ * kv head h / (n_head / n_kv)) times V, times sigmoid(gate). Per sequence: qg (n_head, 2 hd), k_new
+ * and v_new (n_kv, hd), k_cache and v_cache (n_kv, cap, hd) 16-byte aligned, out (n_head hd); len and
+ * pos (n_seq) int32 in device memory (read on the device, so a captured graph can replay with
+ * moving lengths; the caller advances len). f32 device pointers; uses the context's workspace
+ * (about n_seq (n_head hd + n_head ceil(cap/32) (hd + 2)) floats: call once outside a graph capture
+ * so that it is there). Three launches (prep, chunks of 32 cache rows, merge). A len outside
+ * 0 .. cap-1 skips that sequence and is reported by cwx_ctx_status as CWX_EDEVICE.
+ * CWX_EUNSUPPORTED for other head dims or more than 16 query heads per kv head. */
+int cwx_attn_word(cwx_ctx* ctx, const cwx_attn_layer* layer, int32_t n_seq, int32_t cap, const float* qg,
+                  const float* k_new, const float* v_new, float* k_cache, float* v_cache, const int32_t* len,
+                  const int32_t* pos, float* out, void* stream);
+
 /* coachwhip_delta_word (crates/engine/src/delta_kernel.rs:20-50): the delta rule alone for one word,
  * in the reference's layout: qk (heads, 2 dk) q then k (already normed and scaled), vbd (heads,
  * dv + 2) v then beta then the decay g, s (heads, dk, dv); out (heads, dk dv + dv) the new memory

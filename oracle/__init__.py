@@ -58,6 +58,7 @@ def lib() -> ctypes.CDLL:
             "cwo_gdn_word": (I32, [I32] * 6 + [F] + [P] * 12),
             "cwo_gdn_word_ops": (I32, [I32] * 6 + [F] + [P] * 12),
             "cwo_delta_steps": (I32, [I32] * 4 + [P] * 7),
+            "cwo_attn_word": (I32, [I32] * 4 + [F, ctypes.c_double] + [I32] * 3 + [P] * 8),
             "cwo_moe_forward_fast": (I32, [P, P, I32, P]),
             "cwo_set_threads": (None, [I32]),
             "cwo_get_threads": (I32, []),
@@ -296,6 +297,22 @@ def delta_steps(q, k, v, beta, log_decay, s):
     o = np.empty((l, n_v, dv), np.float32)
     assert lib().cwo_delta_steps(l, n_v, dk, dv, _p(q), _p(k), _p(v), _p(beta), _p(log_decay), _p(s), _p(o)) == 0
     return o, s
+
+
+def attn_word(n_head: int, n_kv: int, hd: int, rot: int, eps: float, freq_base: float, len_: int, pos: int, qg,
+              k_new, v_new, q_norm_w, k_norm_w, k_cache, v_cache):
+    """One word of one sequence through the gated full attention (FullAttn::forward between the
+    projections). k_cache, v_cache (n_kv, cap, hd) are copied, the new row written at len_.
+    Returns (out (n_head*hd), k_cache', v_cache')."""
+    f = lambda x: np.ascontiguousarray(x, dtype=np.float32)  # noqa: E731
+    qg, k_new, v_new, q_norm_w, k_norm_w = f(qg), f(k_new), f(v_new), f(q_norm_w), f(k_norm_w)
+    kc = np.array(k_cache, dtype=np.float32, copy=True)
+    vc = np.array(v_cache, dtype=np.float32, copy=True)
+    cap = kc.shape[1]
+    out = np.empty(n_head * hd, np.float32)
+    assert lib().cwo_attn_word(n_head, n_kv, hd, rot, float(eps), float(freq_base), cap, len_, pos, _p(qg), _p(k_new),
+                               _p(v_new), _p(q_norm_w), _p(k_norm_w), _p(kc), _p(vc), _p(out)) == 0
+    return out, kc, vc
 
 
 def set_threads(n: int) -> None:

@@ -128,6 +128,11 @@ int cwo_gdn_word_ops(int n_k, int n_v, int dk, int dv, int taps, int cycle, floa
                      float* s_out, float* conv_out);
 int cwo_delta_steps(int l, int n_v, int dk, int dv, const float* q, const float* k, const float* v, const float* beta,
                     const float* log_decay, float* s, float* o);
+/* Full-attention word step (gdn.cpp): FullAttn::forward for one word of one sequence
+ * (model_next.rs:666-720); k_cache / v_cache (n_kv, cap, hd) get the new row at len. */
+int cwo_attn_word(int n_head, int n_kv, int hd, int rot, float eps, double freq_base, int cap, int len, int pos,
+                  const float* qg, const float* k_new, const float* v_new, const float* q_norm_w,
+                  const float* k_norm_w, float* k_cache, float* v_cache, float* out);
 int cwo_add_rms_norm(const float* a, const float* b, const float* c, const float* alpha, float eps, int64_t rows,
                      int hidden, float* sum, float* out);
 

@@ -1,5 +1,5 @@
-// CPU oracle of the Gated DeltaNet word step -- TEST INFRASTRUCTURE ONLY (the checker of
-// cwx_gdn_word / cwx_delta_word; the product library never links it).
+// CPU oracle of the attention steps before the MoE block -- TEST INFRASTRUCTURE ONLY (the checker
+// of cwx_gdn_word / cwx_delta_word / cwx_attn_word; the product library never links it).
 //
 // cwo_gdn_word restates the reference's one-kernel word step, coachwhip_gdn_word
 // (crates/engine/src/attn_kernel.rs:24-143), as its threadgroups compute it, one value head after
@@ -19,7 +19,9 @@
 // SiLU gate. The reference states that its fused kernel keeps the op-by-op arithmetic; the tests
 // check the two restatements against each other.
 //
-// Parity unpinned at the bit level: the reference holds no vectors for this step and its kernels
+// cwo_attn_word (below) restates the gated full-attention word step.
+//
+// Parity unpinned at the bit level: the reference holds no vectors for these steps and its kernels
 // run on Metal only.
 #include <math.h>
 #include <string.h>
@@ -203,6 +205,72 @@ extern "C" int cwo_gdn_word_ops(int n_k, int n_v, int dk, int dv, int taps, int 
         for (int j = 0; j < dv; ++j) ss += x[j] * x[j];
         const float r = sqrtf(ss / (float)dv + eps);
         for (int j = 0; j < dv; ++j) x[j] = (x[j] / r) * norm_w[j] * silu_f(z[(size_t)h * dv + j]);
+    }
+    return 0;
+}
+
+// ---------------------------------------------------------------- full attention, one word
+// FullAttn::forward for one word of one sequence (crates/engine/src/model_next.rs:666-720): the
+// per-head RmsNorm of q and k (candle's x / sqrt(mean(x^2) + eps) * w, the squares summed in
+// order), rope on the first rot values (rope :653-664: inverse frequencies 1 / base^(2i/rot) in f64
+// rounded to f32, angle pos * inv in f32, candle's non-interleaved rope: x1 cos - x2 sin,
+// x1 sin + x2 cos), the new row appended to the cache (KvBuf::append without its roll), then per
+// query head the scores q.k in order times 1/sqrt(hd) (an f32 scalar), softmax (max, exp(s - max),
+// sum in order, divide), the probabilities times V summed over the rows in order, times
+// sigmoid(gate). k_cache, v_cache (n_kv, cap, hd) are updated at row len.
+static void norm_rope(const float* x, const float* w, int hd, int rot, float eps, double base, int pos, float* y) {
+    float ss = 0.0f;
+    for (int d = 0; d < hd; ++d) ss += x[d] * x[d];
+    const float m = sqrtf(ss / (float)hd + eps);
+    for (int d = 0; d < hd; ++d) y[d] = x[d] / m * w[d];
+    const int half = rot / 2;
+    for (int i = 0; i < half; ++i) {
+        const float inv = (float)(1.0 / pow(base, 2.0 * i / (double)rot));
+        const float f = (float)pos * inv;
+        const float c = cosf(f), s = sinf(f);
+        const float a = y[i], b = y[i + half];
+        y[i] = a * c - b * s;
+        y[i + half] = a * s + b * c;
+    }
+}
+
+extern "C" int cwo_attn_word(int n_head, int n_kv, int hd, int rot, float eps, double freq_base, int cap, int len,
+                             int pos, const float* qg, const float* k_new, const float* v_new, const float* q_norm_w,
+                             const float* k_norm_w, float* k_cache, float* v_cache, float* out) {
+    if (n_head < 1 || n_kv < 1 || n_head % n_kv || hd < 1 || rot < 0 || rot > hd || rot % 2 || len < 0 || len >= cap)
+        return 1;
+    const int g = n_head / n_kv;
+    const float scale = (float)(1.0 / sqrt((double)hd));
+    std::vector<float> q(hd), sc(len + 1);
+    for (int kv = 0; kv < n_kv; ++kv) {
+        float* kr = k_cache + ((size_t)kv * cap + len) * hd;
+        norm_rope(k_new + (size_t)kv * hd, k_norm_w, hd, rot, eps, freq_base, pos, kr);
+        memcpy(v_cache + ((size_t)kv * cap + len) * hd, v_new + (size_t)kv * hd, sizeof(float) * hd);
+    }
+    for (int h = 0; h < n_head; ++h) {
+        const int kv = h / g;
+        norm_rope(qg + (size_t)h * 2 * hd, q_norm_w, hd, rot, eps, freq_base, pos, q.data());
+        const float* K = k_cache + (size_t)kv * cap * hd;
+        const float* V = v_cache + (size_t)kv * cap * hd;
+        float m = -INFINITY;
+        for (int p = 0; p <= len; ++p) {
+            float s = 0.0f;
+            for (int d = 0; d < hd; ++d) s += q[d] * K[(size_t)p * hd + d];
+            sc[p] = s * scale;
+            m = fmaxf(m, sc[p]);
+        }
+        float sum = 0.0f;
+        for (int p = 0; p <= len; ++p) {
+            sc[p] = expf(sc[p] - m);
+            sum += sc[p];
+        }
+        for (int p = 0; p <= len; ++p) sc[p] = sc[p] / sum;
+        const float* gate = qg + (size_t)h * 2 * hd + hd;
+        for (int d = 0; d < hd; ++d) {
+            float acc = 0.0f;
+            for (int p = 0; p <= len; ++p) acc += sc[p] * V[(size_t)p * hd + d];
+            out[(size_t)h * hd + d] = acc * (1.0f / (1.0f + expf(-gate[d])));
+        }
     }
     return 0;
 }
