@@ -12,12 +12,13 @@
 // Layout of the work (split-K decoding), three launches:
 //   k_attn_prep: one warp per query head (normalised, rotated into the workspace) and per kv head
 //     (the new k, normalised and rotated, and v written to the caches at row len);
-//   k_attn_part: a CTA takes 32 cache rows of one kv head of one sequence (grid = ceil(cap / 32) x
-//     n_kv x n_seq; CTAs past the sequence's length return at once). One thread starts three bulk
-//     copies (cp.async.bulk) into shared memory: the chunk's K rows, its V rows and the kv head's
-//     prepared query heads; the CTA scores the rows for all query heads at once (each warp 4 rows,
-//     each lane hd / 32 values of a row, the (head, row) sums finished by a reduce-scatter
-//     butterfly), takes the chunk's softmax (max, exp, sum) and the probabilities times V;
+//   k_attn_part: a CTA takes rpc cache rows of one kv head of one sequence (32 to 256: more when the
+//     grid is many waves deep; grid = ceil(cap / rpc) x n_kv x n_seq; CTAs past the sequence's
+//     length return at once), 32 rows at a time: one thread starts bulk copies (cp.async.bulk) into
+//     shared memory of the chunk's K rows, its V rows and (first) the kv head's prepared query heads;
+//     the CTA scores the rows for all query heads at once (each warp 4 rows, each lane hd / 32 values
+//     of a row, the (head, row) sums finished by a reduce-scatter butterfly), updates the online
+//     softmax (running max and total, earlier sums rescaled) and adds the probabilities times V;
 //   k_attn_combine: per query head the chunks merged in parallel (max-rescaled) and the gate.
 // The rows of K and V are read once: HBM-bound at long caches.
 #include <math.h>
@@ -29,7 +30,7 @@ namespace cwx {
 namespace att {
 constexpr int W = 8;
 constexpr int T = W * 32;
-constexpr int CHUNK = 32;   // cache rows per CTA, 4 per warp
+constexpr int CHUNK = 32;   // cache rows per step of a chunk CTA, 4 per warp
 constexpr int MAX_G = 16;   // query heads per kv head
 constexpr int MAX_HD = 256;
 constexpr int HG = 4;       // query heads per scoring pass (4 heads x 4 rows: one sum per half-warp lane)
@@ -37,6 +38,7 @@ constexpr int HG = 4;       // query heads per scoring pass (4 heads x 4 rows: o
 
 struct AttnArgs {
     int n_head, n_kv, hd, rot, n_split, cap;
+    int rpc;  // cache rows per k_attn_part CTA (a multiple of CHUNK)
     float eps, scale;
     double freq_base;
     const float* qg;
@@ -155,20 +157,24 @@ __global__ void __launch_bounds__(32) k_attn_prep(AttnArgs p) {
     }
 }
 
-// Rows 32 blockIdx.x .. of kv head blockIdx.y of sequence blockIdx.z; DPL = hd / 32. Dynamic
-// shared memory: the chunk's K rows, its V rows (32 hd floats each) and the kv head's g prepared
-// query heads (g hd), brought by three bulk copies.
-template <int DPL>
+// Rows rpc blockIdx.x .. of kv head blockIdx.y of sequence blockIdx.z, 32 at a time; DPL = hd / 32.
+// Dynamic shared memory: a chunk's K rows, its V rows (32 hd floats each) and the kv head's g
+// prepared query heads (g hd), brought by bulk copies; the softmax runs online over the chunks
+// (running max and total per query head, earlier sums rescaled), one partial result per CTA.
+// G: the query heads per kv head (EXACT) or a bound on them (g <= G, checked at run time).
+template <int DPL, int G, bool EXACT>
 __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
     using namespace att;
     extern __shared__ __align__(16) float kv_sm[];
-    __shared__ float pr[CHUNK][MAX_G + 1];  // scores, then exp(s - m), per row
-    __shared__ float mh[MAX_G], lh[MAX_G];
+    __shared__ float pr[CHUNK][G + 1];          // scores (stride G + 1: the softmax reads a column)
+    __shared__ __align__(16) float pw[CHUNK][G < 4 ? 4 : G];  // exp(s - m), per row (16-byte rows)
+    __shared__ float mh[G], lh[G];
+    __shared__ __align__(16) float sc[G < 4 ? 4 : G];  // rescale of the earlier chunks' sums, per head
     __shared__ __align__(8) uint64_t bar;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
     constexpr int hd = 32 * DPL;
-    const int g = p.n_head / p.n_kv;
+    const int g = EXACT ? G : p.n_head / p.n_kv;
     float* Ks = kv_sm;
     float* Vs = kv_sm + CHUNK * hd;
     float* Qs = kv_sm + 2 * CHUNK * hd;
@@ -176,97 +182,136 @@ __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
     pdl_wait();  // (the prep kernel's query heads and new cache row)
     const int L = p.len[seq];
     if (L < 0 || L >= p.cap) return;  // (recorded by k_attn_prep)
-    const int p0 = r * CHUNK;
+    const int p0 = r * p.rpc;
     if (p0 > L) return;
-    const int n = min(p0 + CHUNK, L + 1) - p0;
+    const int pend = min(p0 + p.rpc, L + 1);
     const int64_t kvrow0 = ((int64_t)seq * p.n_kv + kvh) * p.cap;  // first cache row of this kv head
     if (tid == 0) {
         mbar_init(&bar, 1);
         fence_mbar_init();
-        const uint32_t bytes = (uint32_t)(n * hd * 4), qb = (uint32_t)(g * hd * 4);
-        mbar_expect_tx(&bar, 2 * bytes + qb);
-        bulk_g2s(Ks, p.k_cache + (kvrow0 + p0) * hd, bytes, &bar);
-        bulk_g2s(Vs, p.v_cache + (kvrow0 + p0) * hd, bytes, &bar);
-        bulk_g2s(Qs, p.qn + ((int64_t)seq * p.n_head + kvh * g) * hd, qb, &bar);
     }
+    if (tid < G) {
+        mh[tid] = -INFINITY;  // running max and exp total of each query head over the CTA's chunks
+        lh[tid] = 0.f;
+    }
+    constexpr int G4 = G < 4 ? 4 : G;
+    float acc[G4];  // thread d: value d of every query head's running weighted sum
+#pragma unroll
+    for (int hh = 0; hh < G4; ++hh) acc[hh] = 0.f;
     __syncthreads();  // (the barrier's init is visible to every waiting thread)
-    if (!mbar_wait(&bar, 0, p.err)) {  // a copy that did not complete in time (recorded): wait once
-        mbar_wait(&bar, 0, p.err);     // more, bounded, then leave
-        return;
-    }
 
-    // scores: warp rows 4 warp .. + 3 of the chunk, HG query heads per pass; 4 x 4 (head, row)
-    // sums per lane, finished by a reduce-scatter over 16 lanes and one exchange across the halves
-    constexpr int RW = CHUNK / W;  // rows per warp (4)
-    for (int hg = 0; hg < g; hg += HG) {
-        float q[HG][DPL];
-#pragma unroll
-        for (int hh = 0; hh < HG; ++hh) {
-            if (hg + hh < g) {
-                load_row<DPL>(Qs + (hg + hh) * hd, lane, q[hh]);
-            } else {
-#pragma unroll
-                for (int j = 0; j < DPL; ++j) q[hh][j] = 0.f;
-            }
+    uint32_t phase = 0;
+    for (int c0 = p0; c0 < pend; c0 += CHUNK, phase ^= 1) {
+        const int n = min(CHUNK, pend - c0);
+        if (tid == 0) {  // this chunk's K and V rows (and, with the first, the query heads)
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // (earlier reads of the buffers first)
+            const uint32_t bytes = (uint32_t)(n * hd * 4), qb = c0 == p0 ? (uint32_t)(g * hd * 4) : 0u;
+            mbar_expect_tx(&bar, 2 * bytes + qb);
+            bulk_g2s(Ks, p.k_cache + (kvrow0 + c0) * hd, bytes, &bar);
+            bulk_g2s(Vs, p.v_cache + (kvrow0 + c0) * hd, bytes, &bar);
+            if (qb) bulk_g2s(Qs, p.qn + ((int64_t)seq * p.n_head + kvh * g) * hd, qb, &bar);
         }
-        float v[HG * RW];
+        if (!mbar_wait(&bar, phase, p.err)) {  // a copy that did not complete in time (recorded): wait
+            mbar_wait(&bar, phase, p.err);     // once more, bounded, then leave
+            return;
+        }
+
+        // scores: warp rows 4 warp .. + 3 of the chunk, HG query heads per pass; 4 x 4 (head, row)
+        // sums per lane, finished by a reduce-scatter over 16 lanes and one exchange across the halves
+        constexpr int RW = CHUNK / W;  // rows per warp (4)
 #pragma unroll
-        for (int jp = 0; jp < RW; ++jp) {
-            float k[DPL];
-            load_row<DPL>(Ks + (warp * RW + jp) * hd, lane, k);  // (rows past n hold stale data: masked below)
+        for (int hg = 0; hg < G; hg += HG) {
+            if (!EXACT && hg >= g) break;
+            float q[HG][DPL];
 #pragma unroll
             for (int hh = 0; hh < HG; ++hh) {
-                float s = 0.f;
+                if (hg + hh < g) {
+                    load_row<DPL>(Qs + (hg + hh) * hd, lane, q[hh]);
+                } else {
 #pragma unroll
-                for (int j = 0; j < DPL; ++j) s += q[hh][j] * k[j];
-                v[hh * RW + jp] = s;
+                    for (int j = 0; j < DPL; ++j) q[hh][j] = 0.f;
+                }
+            }
+            float v[HG * RW];
+#pragma unroll
+            for (int jp = 0; jp < RW; ++jp) {
+                float k[DPL];
+                load_row<DPL>(Ks + (warp * RW + jp) * hd, lane, k);  // (rows past n hold stale data: masked)
+#pragma unroll
+                for (int hh = 0; hh < HG; ++hh) {
+                    float s = 0.f;
+#pragma unroll
+                    for (int j = 0; j < DPL; ++j) s += q[hh][j] * k[j];
+                    v[hh * RW + jp] = s;
+                }
+            }
+            rs_level<16>(v, lane);
+            rs_level<8>(v, lane);
+            rs_level<4>(v, lane);
+            rs_level<2>(v, lane);
+            const float sum = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 16);
+            const int hh = (lane & 15) >> 2, jp = lane & 3;  // the (head, row) whose sum this lane holds
+            const int row = warp * RW + jp;
+            if (lane < 16 && hg + hh < g) pr[row][hg + hh] = row < n ? sum * p.scale : -INFINITY;
+        }
+        __syncthreads();
+
+        // the softmax so far per query head (lane = row): the new running max, the chunk's exp
+        // weights against it, the earlier sums' rescale factor
+        for (int hh = warp; hh < g; hh += W) {
+            const float a = pr[lane][hh];
+            const float m_old = mh[hh];
+            const float m = fmaxf(m_old, att_warp_max(a));
+            const float ea = expf(a - m);
+            const float l = att_warp_sum(ea);
+            pw[lane][hh] = ea;
+            __syncwarp();
+            if (lane == 0) {
+                const float so = expf(m_old - m);  // (0 for the first chunk)
+                sc[hh] = so;
+                mh[hh] = m;
+                lh[hh] = lh[hh] * so + l;
             }
         }
-        rs_level<16>(v, lane);
-        rs_level<8>(v, lane);
-        rs_level<4>(v, lane);
-        rs_level<2>(v, lane);
-        const float sum = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 16);
-        const int hh = (lane & 15) >> 2, jp = lane & 3;  // the (head, row) whose sum this lane holds
-        const int row = warp * RW + jp;
-        if (lane < 16 && hg + hh < g) pr[row][hg + hh] = row < n ? sum * p.scale : -INFINITY;
-    }
-    __syncthreads();
+        __syncthreads();
 
-    // the chunk's softmax per query head (lane = row)
-    for (int hh = warp; hh < g; hh += W) {
-        const float a = pr[lane][hh];
-        const float m = att_warp_max(a);
-        const float ea = expf(a - m);
-        const float l = att_warp_sum(ea);
-        pr[lane][hh] = ea;
-        if (lane == 0) {
-            mh[hh] = m;
-            lh[hh] = l;
+        // exp-weighted sum of the V rows: thread d holds value d for every query head
+        if (tid < hd) {
+            const float4* s4 = reinterpret_cast<const float4*>(sc);
+#pragma unroll
+            for (int q4 = 0; q4 < G4 / 4; ++q4) {
+                const float4 f = s4[q4];
+                acc[4 * q4 + 0] *= f.x;
+                acc[4 * q4 + 1] *= f.y;
+                acc[4 * q4 + 2] *= f.z;
+                acc[4 * q4 + 3] *= f.w;
+            }
+            for (int row = 0; row < n; ++row) {
+                const float vv = Vs[row * hd + tid];
+                const float4* w4 = reinterpret_cast<const float4*>(pw[row]);
+#pragma unroll
+                for (int q4 = 0; q4 < G4 / 4; ++q4) {  // (columns past g hold stale values: never stored)
+                    const float4 w = w4[q4];
+                    acc[4 * q4 + 0] += w.x * vv;
+                    acc[4 * q4 + 1] += w.y * vv;
+                    acc[4 * q4 + 2] += w.z * vv;
+                    acc[4 * q4 + 3] += w.w * vv;
+                }
+            }
         }
+        __syncthreads();  // (the buffers, pr, pw and sc are reused by the next chunk)
     }
-    __syncthreads();
 
-    // exp-weighted sum of the V rows: thread d holds value d for every query head
-    const int64_t chunk = ((int64_t)seq * p.n_kv + kvh) * p.n_split + r;
+    const int64_t part_i = ((int64_t)seq * p.n_kv + kvh) * p.n_split + r;
     if (tid < hd) {
-        float acc[MAX_G];
+        float* part = p.part + part_i * g * hd;
 #pragma unroll
-        for (int hh = 0; hh < MAX_G; ++hh) acc[hh] = 0.f;
-        for (int row = 0; row < n; ++row) {
-            const float vv = Vs[row * hd + tid];
-#pragma unroll
-            for (int hh = 0; hh < MAX_G; ++hh)
-                if (hh < g) acc[hh] += pr[row][hh] * vv;
-        }
-        float* part = p.part + chunk * g * hd;
-#pragma unroll
-        for (int hh = 0; hh < MAX_G; ++hh)
-            if (hh < g) part[hh * hd + tid] = acc[hh];
+        for (int hh = 0; hh < G; ++hh)
+            if (EXACT || hh < g) part[hh * hd + tid] = acc[hh];
     }
     if (tid < g) {
-        p.ml[(chunk * g + tid) * 2] = mh[tid];
-        p.ml[(chunk * g + tid) * 2 + 1] = lh[tid];
+        p.ml[(part_i * g + tid) * 2] = mh[tid];
+        p.ml[(part_i * g + tid) * 2 + 1] = lh[tid];
     }
 }
 
@@ -284,7 +329,7 @@ __global__ void __launch_bounds__(att::T) k_attn_combine(AttnArgs p) {
     const int L = p.len[seq];
     if (L < 0 || L >= p.cap) return;  // (recorded by k_attn_prep)
     const int g = p.n_head / p.n_kv, kvh = h / g, hh = h % g;
-    const int n_act = L / CHUNK + 1;
+    const int n_act = L / p.rpc + 1;
     const int64_t c0 = ((int64_t)seq * p.n_kv + kvh) * p.n_split;  // first chunk of this kv head
     const float* ml = p.ml + (c0 * g + hh) * 2;                     // chunk r at ml[2 g r]
     const float* sums = p.part + (c0 * g + hh) * hd;                // chunk r at sums[g hd r]
@@ -299,7 +344,8 @@ __global__ void __launch_bounds__(att::T) k_attn_combine(AttnArgs p) {
     float num[DPL], den = 0.f;
 #pragma unroll
     for (int j = 0; j < DPL; ++j) num[j] = 0.f;
-    for (int r = warp; r < n_act; r += W) {
+#pragma unroll 4
+    for (int r = warp; r < n_act; r += W) {  // (unrolled: several chunks' loads in flight)
         const float e = expf(ml[(int64_t)r * 2 * g] - M);
         den += e * ml[(int64_t)r * 2 * g + 1];
         float v[DPL];
@@ -323,18 +369,30 @@ __global__ void __launch_bounds__(att::T) k_attn_combine(AttnArgs p) {
     }
 }
 
-template <int DPL>
-static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const AttnArgs& a) {
+template <int DPL, int G, bool EXACT>
+static cudaError_t launch_part(dim3 grid, size_t smem, cudaStream_t st, const AttnArgs& a) {
     static bool attr = false;  // (the dynamic shared memory limit, once per instantiation)
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_attn_part<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (2 * att::CHUNK + att::MAX_G) * 32 * DPL * (int)sizeof(float));
+        cudaError_t e = cudaFuncSetAttribute(k_attn_part<DPL, G, EXACT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (2 * att::CHUNK + G) * 32 * DPL * (int)sizeof(float));
         if (e != cudaSuccess) return e;
         attr = true;
     }
+    return launch_pdl(k_attn_part<DPL, G, EXACT>, grid, dim3(att::T), smem, st, a);
+}
+
+template <int DPL>
+static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const AttnArgs& a) {
     cudaError_t e = launch_pdl(k_attn_prep, dim3(a.n_head + a.n_kv, grid.z), dim3(32), 0, st, a);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(k_attn_part<DPL>, grid, dim3(att::T), smem, st, a);
+    switch (a.n_head / a.n_kv) {  // the query heads per kv head: exact variants, else a bound of 16
+        case 1: e = launch_part<DPL, 1, true>(grid, smem, st, a); break;
+        case 2: e = launch_part<DPL, 2, true>(grid, smem, st, a); break;
+        case 4: e = launch_part<DPL, 4, true>(grid, smem, st, a); break;
+        case 8: e = launch_part<DPL, 8, true>(grid, smem, st, a); break;
+        case 16: e = launch_part<DPL, 16, true>(grid, smem, st, a); break;
+        default: e = launch_part<DPL, 16, false>(grid, smem, st, a); break;
+    }
     if (e != cudaSuccess) return e;
     return launch_pdl(k_attn_combine<DPL>, dim3(a.n_head, grid.z), dim3(att::T), 0, st, a);
 }
@@ -369,7 +427,13 @@ extern "C" int cwx_attn_word(cwx_ctx* c, const cwx_attn_layer* L, int32_t n_seq,
     CWX_CUDA(cudaSetDevice(c->device));
     const cudaStream_t st = (cudaStream_t)stream;
     const int g = L->n_head / L->n_kv;
-    const int n_split = (cap + att::CHUNK - 1) / att::CHUNK;
+    // rows per chunk CTA: 32, or more when the grid would otherwise run more than 4 waves of 2
+    // CTAs per SM (fewer partial results to write and merge), at most 256
+    const int64_t chunks = (int64_t)n_seq * L->n_kv * ((cap + att::CHUNK - 1) / att::CHUNK);
+    int nch = (int)(chunks / (8 * (int64_t)c->sm_count));
+    nch = nch < 1 ? 1 : nch > 8 ? 8 : nch;
+    const int rpc = att::CHUNK * nch;
+    const int n_split = (cap + rpc - 1) / rpc;
     const size_t f4 = sizeof(float);
     const size_t qn_b = (((size_t)n_seq * L->n_head * L->hd * f4) + 255) & ~(size_t)255;
     const size_t part_b = (((size_t)n_seq * L->n_kv * n_split * g * L->hd * f4) + 255) & ~(size_t)255;
@@ -377,7 +441,7 @@ extern "C" int cwx_attn_word(cwx_ctx* c, const cwx_attn_layer* L, int32_t n_seq,
     int rc = ensure_ws(c, qn_b + part_b + ml_b, st);
     if (rc) return rc;
     float* ws = reinterpret_cast<float*>(c->ws);
-    AttnArgs a{L->n_head, L->n_kv, L->hd, L->rot, n_split, cap, L->eps, (float)(1.0 / sqrt((double)L->hd)),
+    AttnArgs a{L->n_head, L->n_kv, L->hd, L->rot, n_split, cap, rpc, L->eps, (float)(1.0 / sqrt((double)L->hd)),
                L->freq_base, qg, k_new, v_new, k_cache, v_cache, len, pos, L->q_norm_w, L->k_norm_w,
                ws, ws + qn_b / f4, ws + (qn_b + part_b) / f4, out, c->d_err};
     const dim3 grid(n_split, L->n_kv, n_seq);

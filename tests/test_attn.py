@@ -3,8 +3,8 @@
 CPU: the oracle's restatement (model_next.rs:666-720) against a float64 evaluation of the same
 formulas, and the C ABI's argument checks (no device call). GPU: cwx_attn_word against the oracle
 at Qwen3-Next's shape (16 query heads over 2 kv heads of 256, rope on 64) and others, cache
-lengths on both sides of the 32-row chunks, several sequences of different lengths, a run of words
-appended one after another.
+lengths on both sides of the 32-row chunks, several sequences of different lengths, a grid large
+enough that each CTA walks several chunks, a run of words appended one after another.
 
 Tolerance: the split-K softmax merges 32-row chunks (exp(s - m_chunk) rescaled by exp(m_chunk - M))
 where the reference normalises once, and sums in another order: outputs within 2e-5 of the largest
@@ -108,6 +108,8 @@ SHAPES = [
     (8, 2, 128, 128, 300, [5, 130, 299]),
     (16, 1, 64, 32, 128, [127, 1]),
     (2, 2, 64, 0, 64, [40]),
+    # a grid of 8 x 2 x 256 chunks: several 32-row chunks per CTA (online softmax across them)
+    (16, 2, 256, 64, 8192, [8191, 96, 95, 0, 4000, 97, 191, 192]),
 ]
 
 
