@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
     __shared__ __align__(16) float pw[CHUNK][G < 4 ? 4 : G];  // exp(s - m), per row (16-byte rows)
     __shared__ float mh[G], lh[G];
     __shared__ __align__(16) float sc[G < 4 ? 4 : G];  // rescale of the earlier chunks' sums, per head
-    __shared__ __align__(8) uint64_t bar;
+    __shared__ __align__(8) uint64_t bar[2];  // K rows (and the query heads), V rows
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
     constexpr int hd = 32 * DPL;
@@ -186,9 +186,26 @@ __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
     if (p0 > L) return;
     const int pend = min(p0 + p.rpc, L + 1);
     const int64_t kvrow0 = ((int64_t)seq * p.n_kv + kvh) * p.cap;  // first cache row of this kv head
+    auto issue_k = [&](int c, bool with_q) {  // (thread 0) chunk c's K rows, and the query heads
+        const int m = min(CHUNK, pend - c);
+        const uint32_t bytes = (uint32_t)(m * hd * 4), qb = with_q ? (uint32_t)(g * hd * 4) : 0u;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // (earlier reads of the buffer first)
+        mbar_expect_tx(&bar[0], bytes + qb);
+        bulk_g2s(Ks, p.k_cache + (kvrow0 + c) * hd, bytes, &bar[0]);
+        if (with_q) bulk_g2s(Qs, p.qn + ((int64_t)seq * p.n_head + kvh * g) * hd, qb, &bar[0]);
+    };
+    auto issue_v = [&](int c) {  // (thread 0) chunk c's V rows
+        const uint32_t bytes = (uint32_t)(min(CHUNK, pend - c) * hd * 4);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(&bar[1], bytes);
+        bulk_g2s(Vs, p.v_cache + (kvrow0 + c) * hd, bytes, &bar[1]);
+    };
     if (tid == 0) {
-        mbar_init(&bar, 1);
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
         fence_mbar_init();
+        issue_k(p0, true);
+        issue_v(p0);
     }
     if (tid < G) {
         mh[tid] = -INFINITY;  // running max and exp total of each query head over the CTA's chunks
@@ -200,19 +217,16 @@ __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
     for (int hh = 0; hh < G4; ++hh) acc[hh] = 0.f;
     __syncthreads();  // (the barrier's init is visible to every waiting thread)
 
-    uint32_t phase = 0;
-    for (int c0 = p0; c0 < pend; c0 += CHUNK, phase ^= 1) {
+    // chunk i: wait for its K rows, score them, start chunk i+1's K rows; softmax; wait for its V
+    // rows, weight them, start chunk i+1's V rows. A bounded wait that gives up in any thread makes
+    // the whole CTA wait once more for what it has in flight and leave.
+    uint32_t ph = 0;
+    for (int c0 = p0; c0 < pend; c0 += CHUNK, ph ^= 1) {
         const int n = min(CHUNK, pend - c0);
-        if (tid == 0) {  // this chunk's K and V rows (and, with the first, the query heads)
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // (earlier reads of the buffers first)
-            const uint32_t bytes = (uint32_t)(n * hd * 4), qb = c0 == p0 ? (uint32_t)(g * hd * 4) : 0u;
-            mbar_expect_tx(&bar, 2 * bytes + qb);
-            bulk_g2s(Ks, p.k_cache + (kvrow0 + c0) * hd, bytes, &bar);
-            bulk_g2s(Vs, p.v_cache + (kvrow0 + c0) * hd, bytes, &bar);
-            if (qb) bulk_g2s(Qs, p.qn + ((int64_t)seq * p.n_head + kvh * g) * hd, qb, &bar);
-        }
-        if (!mbar_wait(&bar, phase, p.err)) {  // a copy that did not complete in time (recorded): wait
-            mbar_wait(&bar, phase, p.err);     // once more, bounded, then leave
+        const int c1 = c0 + CHUNK;
+        if (!__syncthreads_and(mbar_wait(&bar[0], ph, p.err))) {
+            mbar_wait(&bar[0], ph, p.err);
+            mbar_wait(&bar[1], ph, p.err);
             return;
         }
 
@@ -255,6 +269,7 @@ __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
             if (lane < 16 && hg + hh < g) pr[row][hg + hh] = row < n ? sum * p.scale : -INFINITY;
         }
         __syncthreads();
+        if (tid == 0 && c1 < pend) issue_k(c1, false);  // (the K buffer is free: scores are done)
 
         // the softmax so far per query head (lane = row): the new running max, the chunk's exp
         // weights against it, the earlier sums' rescale factor
@@ -276,6 +291,11 @@ __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
         __syncthreads();
 
         // exp-weighted sum of the V rows: thread d holds value d for every query head
+        if (!__syncthreads_and(mbar_wait(&bar[1], ph, p.err))) {
+            mbar_wait(&bar[1], ph, p.err);
+            if (c1 < pend) mbar_wait(&bar[0], ph ^ 1, p.err);
+            return;
+        }
         if (tid < hd) {
             const float4* s4 = reinterpret_cast<const float4*>(sc);
 #pragma unroll
@@ -299,7 +319,8 @@ __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
                 }
             }
         }
-        __syncthreads();  // (the buffers, pr, pw and sc are reused by the next chunk)
+        __syncthreads();  // (the V buffer, pw and sc are reused by the next chunk)
+        if (tid == 0 && c1 < pend) issue_v(c1);
     }
 
     const int64_t part_i = ((int64_t)seq * p.n_kv + kvh) * p.n_split + r;
