@@ -213,18 +213,22 @@ __global__ void __launch_bounds__(gdn::T, RPW <= 16 ? 3 : RPW <= 32 ? 2 : 1) k_g
 }
 
 // The same word step with one CTA per head, for dk <= 128 and dv <= 128 with dv % 4 == 0 (the
-// models' 128 x 128 heads): lane l owns memory columns 4l .. 4l+3 (16-byte loads and stores, a
-// warp covers a 512-byte row), warp w rows 16w .. 16w+15; the conv of the head's q, k and v
-// channels is one pass over all threads; the column sums and the RMS norm stay inside the CTA.
+// models' 128 x 128 heads): the head's memory (64 KB) comes into shared memory by one bulk copy
+// started at the kernel's start, under the conv pass; lane l owns memory columns 4l .. 4l+3
+// (16-byte shared-memory reads and global stores, a warp covers a 512-byte row), warp w rows
+// 16w .. 16w+15; the conv of the head's q, k and v channels is one pass over all threads; the
+// column sums and the RMS norm stay inside the CTA. Three CTAs per SM: 192 KB of memory in flight.
 namespace gdnh {
 constexpr int RPW = 16;                // rows per warp
 constexpr int MAX_DK = gdn::W * RPW;   // 128
 constexpr int MAX_DV = 128;
 }  // namespace gdnh
 
-__global__ void __launch_bounds__(gdn::T, 2) k_gdn_head(GdnArgs p) {
+__global__ void __launch_bounds__(gdn::T, 3) k_gdn_head(GdnArgs p) {
     using namespace gdn;
     using gdnh::RPW;
+    extern __shared__ __align__(16) float st_sm[];  // the head's memory, dk x dv, by one bulk copy
+    __shared__ __align__(8) uint64_t sbar;
     __shared__ float xc[2 * gdnh::MAX_DK + gdnh::MAX_DV];  // silu(conv): q | k | v of this head
     __shared__ __align__(16) float part[W][gdnh::MAX_DV];
     __shared__ __align__(16) float d_sh[gdnh::MAX_DV];
@@ -247,11 +251,11 @@ __global__ void __launch_bounds__(gdn::T, 2) k_gdn_head(GdnArgs p) {
     float* CO = p.conv_out + (int64_t)seq * (taps - 1) * channels;
 
     pdl_wait();
-    float4 col[RPW];
-#pragma unroll
-    for (int ii = 0; ii < RPW; ++ii) {
-        const int i = r0 + ii;
-        col[ii] = (jok && i < dk) ? *reinterpret_cast<const float4*>(S + i * dv + j0) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tid == 0) {  // the memory first: its copy is the long pole and runs under the conv pass
+        mbar_init(&sbar, 1);
+        fence_mbar_init();
+        mbar_expect_tx(&sbar, (uint32_t)(dk * dv * 4));
+        bulk_g2s(st_sm, S, (uint32_t)(dk * dv * 4), &sbar);
     }
 
     // conv + SiLU of q, k (key head kh) and v (this head) in one pass; the window moves one word
@@ -297,15 +301,27 @@ __global__ void __launch_bounds__(gdn::T, 2) k_gdn_head(GdnArgs p) {
     const float beta = 1.0f / (1.0f + expf(-ba[h]));
     const float g = expf(logf(expf(ba[p.n_v + h] + p.dt_bias[h]) + 1.0f) * p.a[h]);
 
-    // sk = k . S over this warp's rows, then over the warps in order
+    // sk = k . S over this warp's rows, then over the warps in order (a copy that did not arrive
+    // in time, in any thread: the CTA waits once more, bounded, writes NaN for the head's read-out,
+    // so that the failure shows, and leaves; this entry point has no context to record it in)
+    if (!__syncthreads_and(mbar_wait(&sbar, 0, nullptr))) {
+        mbar_wait(&sbar, 0, nullptr);
+        if (tid < dv) p.o[head * dv + tid] = __int_as_float(0x7fc00000);
+        return;
+    }
+    auto col = [&](int ii) {  // this thread's 4 columns of row r0 + ii
+        const int i = r0 + ii;
+        return (jok && i < dk) ? *reinterpret_cast<const float4*>(st_sm + i * dv + j0) : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
     float4 sp = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int ii = 0; ii < RPW; ++ii) {
         const float kv = (r0 + ii < dk ? xc[dk + r0 + ii] : 0.f) * kscale;
-        sp.x += kv * col[ii].x;
-        sp.y += kv * col[ii].y;
-        sp.z += kv * col[ii].z;
-        sp.w += kv * col[ii].w;
+        const float4 c = col(ii);
+        sp.x += kv * c.x;
+        sp.y += kv * c.y;
+        sp.z += kv * c.z;
+        sp.w += kv * c.w;
     }
     if (jok) *reinterpret_cast<float4*>(&part[warp][j0]) = sp;
     __syncthreads();
@@ -326,11 +342,12 @@ __global__ void __launch_bounds__(gdn::T, 2) k_gdn_head(GdnArgs p) {
         const bool iok = i < dk;
         const float kv = (iok ? xc[dk + i] : 0.f) * kscale;
         const float qv = (iok ? xc[i] : 0.f) * qscale;
+        const float4 c = col(ii);
         float4 ns;
-        ns.x = g * col[ii].x + kv * d.x;
-        ns.y = g * col[ii].y + kv * d.y;
-        ns.z = g * col[ii].z + kv * d.z;
-        ns.w = g * col[ii].w + kv * d.w;
+        ns.x = g * c.x + kv * d.x;
+        ns.y = g * c.y + kv * d.y;
+        ns.z = g * c.z + kv * d.z;
+        ns.w = g * c.w + kv * d.w;
         if (jok && iok) *reinterpret_cast<float4*>(SO + i * dv + j0) = ns;
         ac.x += qv * ns.x;
         ac.y += qv * ns.y;
@@ -468,7 +485,14 @@ extern "C" int cwx_gdn_word(const cwx_gdn_layer* L, int32_t n_seq, const float* 
     cudaError_t e;
     if (L->dk <= gdnh::MAX_DK && L->dv <= gdnh::MAX_DV && L->dv % 4 == 0 && ((uintptr_t)s & 15) == 0 &&
         ((uintptr_t)s_out & 15) == 0) {
-        e = launch_pdl(k_gdn_head, dim3(L->n_v, n_seq), dim3(gdn::T), 0, st, p);
+        static bool attr = false;  // (the dynamic shared memory limit, once)
+        if (!attr) {
+            e = cudaFuncSetAttribute(k_gdn_head, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     gdnh::MAX_DK * gdnh::MAX_DV * (int)sizeof(float));
+            if (e != cudaSuccess) return cuda_fail(e, "cwx_gdn_word attribute");
+            attr = true;
+        }
+        e = launch_pdl(k_gdn_head, dim3(L->n_v, n_seq), dim3(gdn::T), (size_t)L->dk * L->dv * sizeof(float), st, p);
         return e == cudaSuccess ? CWX_OK : cuda_fail(e, "cwx_gdn_word launch");
     }
     switch (rows_per_warp(L->dk)) {
