@@ -257,22 +257,47 @@ __global__ void __launch_bounds__(gdn::T, 3) k_gdn_head(GdnArgs p) {
         mbar_expect_tx(&sbar, (uint32_t)(dk * dv * 4));
         bulk_g2s(st_sm, S, (uint32_t)(dk * dv * 4), &sbar);
     }
+    // the head's gate inputs and this thread's output-gate values, requested now so that they
+    // arrive under the conv pass
+    const float* ba = p.ba + (int64_t)seq * 2 * p.n_v;
+    const float b_raw = ba[h], a_raw = ba[p.n_v + h], dtb = p.dt_bias[h], a_h = p.a[h];
+    const float zv = tid < dv ? p.z[head * dv + tid] : 0.f, nw = tid < dv ? p.norm_w[tid] : 0.f;
 
     // conv + SiLU of q, k (key head kh) and v (this head) in one pass; the window moves one word
     // on (q, k by the key head's first value head)
     const bool qk_writer = p.cycle ? h < p.n_k : h % per_group == 0;
+    // (at most 384 channels over 256 threads: a thread's two channels load together, then compute,
+    // then move their windows, so that no load waits behind a store it might alias)
     const int nc = 2 * dk + dv;
-    for (int c = tid; c < nc; c += T) {
-        const int ch = c < dk ? kh * dk + c : c < 2 * dk ? p.n_k * dk + kh * dk + (c - dk) : 2 * p.n_k * dk + h * dv + (c - 2 * dk);
-        const float* w = p.conv_w + (int64_t)ch * taps;
-        float x = 0.f;
-        for (int t = 0; t + 1 < taps; ++t) x += w[t] * CS[t * channels + ch];
-        x += w[taps - 1] * X[ch];
-        xc[c] = gdn_silu(x);
-        if (c >= 2 * dk || qk_writer) {
-            for (int t = 0; t + 2 < taps; ++t) CO[t * channels + ch] = CS[(t + 1) * channels + ch];
-            CO[(taps - 2) * channels + ch] = X[ch];
-        }
+    auto chan = [&](int c) {
+        return c < dk ? kh * dk + c : c < 2 * dk ? p.n_k * dk + kh * dk + (c - dk) : 2 * p.n_k * dk + h * dv + (c - 2 * dk);
+    };
+    const int ca = tid, cb = tid + T;
+    const bool ha = ca < nc, hb = cb < nc;
+    const int cha = ha ? chan(ca) : 0, chb = hb ? chan(cb) : 0;
+    const float* wa = p.conv_w + (int64_t)cha * taps;
+    const float* wb = p.conv_w + (int64_t)chb * taps;
+    float xa = 0.f, xb = 0.f;
+    for (int t = 0; t + 1 < taps; ++t) {
+        if (ha) xa += wa[t] * CS[t * channels + cha];
+        if (hb) xb += wb[t] * CS[t * channels + chb];
+    }
+    const float na = ha ? X[cha] : 0.f, nb = hb ? X[chb] : 0.f;
+    if (ha) {
+        xa += wa[taps - 1] * na;
+        xc[ca] = gdn_silu(xa);
+    }
+    if (hb) {
+        xb += wb[taps - 1] * nb;
+        xc[cb] = gdn_silu(xb);
+    }
+    if (ha && (ca >= 2 * dk || qk_writer)) {
+        for (int t = 0; t + 2 < taps; ++t) CO[t * channels + cha] = CS[(t + 1) * channels + cha];
+        CO[(taps - 2) * channels + cha] = na;
+    }
+    if (hb && (cb >= 2 * dk || qk_writer)) {
+        for (int t = 0; t + 2 < taps; ++t) CO[t * channels + chb] = CS[(t + 1) * channels + chb];
+        CO[(taps - 2) * channels + chb] = nb;
     }
     __syncthreads();
     {
@@ -297,9 +322,8 @@ __global__ void __launch_bounds__(gdn::T, 3) k_gdn_head(GdnArgs p) {
     }
     const float qscale = 1.0f / (sqrtf(tq + p.eps) * sqrtf((float)dk));
     const float kscale = 1.0f / sqrtf(tk + p.eps);
-    const float* ba = p.ba + (int64_t)seq * 2 * p.n_v;
-    const float beta = 1.0f / (1.0f + expf(-ba[h]));
-    const float g = expf(logf(expf(ba[p.n_v + h] + p.dt_bias[h]) + 1.0f) * p.a[h]);
+    const float beta = 1.0f / (1.0f + expf(-b_raw));
+    const float g = expf(logf(expf(a_raw + dtb) + 1.0f) * a_h);
 
     // sk = k . S over this warp's rows, then over the warps in order (a copy that did not arrive
     // in time, in any thread: the CTA waits once more, bounded, writes NaN for the head's read-out,
@@ -368,9 +392,8 @@ __global__ void __launch_bounds__(gdn::T, 3) k_gdn_head(GdnArgs p) {
     if (tid < dv) {
         const float total = ((red[0] + red[1]) + red[2]) + red[3];
         const float rms = 1.0f / sqrtf(total / (float)dv + p.eps);
-        const int64_t oi = head * dv + tid;
-        const float x = o * rms * p.norm_w[tid];
-        p.o[oi] = x * gdn_silu(p.z[oi]);
+        const float x = o * rms * nw;
+        p.o[head * dv + tid] = x * gdn_silu(zv);
     }
 }
 
