@@ -336,14 +336,15 @@ __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
     }
 }
 
-// Query head blockIdx.x of sequence blockIdx.y: the chunks merged (warp w takes chunks w, w + 8,
-// ..; the warps' sums then added in warp order), each rescaled by exp(m_chunk - M), divided by the
+// Query head blockIdx.x of sequence blockIdx.y: the chunks merged (warp w of CW takes chunks w,
+// w + CW, ..; the warps' sums then added in warp order), each rescaled by exp(m_chunk - M), divided by the
 // softmax total, times sigmoid(gate).
-template <int DPL>
-__global__ void __launch_bounds__(att::T) k_attn_combine(AttnArgs p) {
+template <int DPL, int CW>
+__global__ void __launch_bounds__(CW * 32) k_attn_combine(AttnArgs p) {
     using namespace att;
-    __shared__ float red[W][MAX_HD + 1];
-    __shared__ float dred[W], mx[W];
+    constexpr int CT = CW * 32;
+    __shared__ float red[CW][MAX_HD + 1];
+    __shared__ float dred[CW], mx[CW];
     const int h = blockIdx.x, seq = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr int hd = 32 * DPL;
     pdl_wait();
@@ -355,18 +356,18 @@ __global__ void __launch_bounds__(att::T) k_attn_combine(AttnArgs p) {
     const float* ml = p.ml + (c0 * g + hh) * 2;                     // chunk r at ml[2 g r]
     const float* sums = p.part + (c0 * g + hh) * hd;                // chunk r at sums[g hd r]
     float m = -INFINITY;
-    for (int r = tid; r < n_act; r += T) m = fmaxf(m, ml[(int64_t)r * 2 * g]);
+    for (int r = tid; r < n_act; r += CT) m = fmaxf(m, ml[(int64_t)r * 2 * g]);
     m = att_warp_max(m);
     if (lane == 0) mx[warp] = m;
     __syncthreads();
     float M = mx[0];
 #pragma unroll
-    for (int w = 1; w < W; ++w) M = fmaxf(M, mx[w]);
+    for (int w = 1; w < CW; ++w) M = fmaxf(M, mx[w]);
     float num[DPL], den = 0.f;
 #pragma unroll
     for (int j = 0; j < DPL; ++j) num[j] = 0.f;
 #pragma unroll 4
-    for (int r = warp; r < n_act; r += W) {  // (unrolled: several chunks' loads in flight)
+    for (int r = warp; r < n_act; r += CW) {  // (unrolled: several chunks' loads in flight)
         const float e = expf(ml[(int64_t)r * 2 * g] - M);
         den += e * ml[(int64_t)r * 2 * g + 1];
         float v[DPL];
@@ -381,7 +382,7 @@ __global__ void __launch_bounds__(att::T) k_attn_combine(AttnArgs p) {
     if (tid < hd) {
         float o = 0.f, D = 0.f;
 #pragma unroll
-        for (int w = 0; w < W; ++w) {
+        for (int w = 0; w < CW; ++w) {
             o += red[w][tid];
             D += dred[w];
         }
@@ -415,7 +416,9 @@ static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const At
         default: e = launch_part<DPL, 16, false>(grid, smem, st, a); break;
     }
     if (e != cudaSuccess) return e;
-    return launch_pdl(k_attn_combine<DPL>, dim3(a.n_head, grid.z), dim3(att::T), 0, st, a);
+    // the merge: 32 warps when a head has many chunk results (their loads in flight together), else 8
+    if (a.n_split >= 64) return launch_pdl(k_attn_combine<DPL, 32>, dim3(a.n_head, grid.z), dim3(32 * 32), 0, st, a);
+    return launch_pdl(k_attn_combine<DPL, 8>, dim3(a.n_head, grid.z), dim3(8 * 32), 0, st, a);
 }
 
 }  // namespace cwx
