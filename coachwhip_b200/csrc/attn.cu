@@ -82,16 +82,8 @@ __device__ __forceinline__ void rs_level(float* v, int lane) {
     }
 }
 
-// RmsNorm of one head row (candle's: x / sqrt(mean(x^2) + eps) * w) then rope on its first rot
-// values at position p, by one warp, into y (shared memory).
-__device__ void norm_rope_row(const float* x, const float* w, int hd, int rot, float eps, double base, int p,
-                              float* y, int lane) {
-    float ss = 0.f;
-    for (int d = lane; d < hd; d += 32) ss += x[d] * x[d];
-    ss = att_warp_sum(ss);
-    const float r = sqrtf(ss / (float)hd + eps);
-    for (int d = lane; d < hd; d += 32) y[d] = x[d] / r * w[d];
-    __syncwarp();
+// Rope on the first rot values of y (shared memory) at position p, by one warp.
+__device__ void rope_row(float* y, int hd, int rot, double base, int p, int lane) {
     const int half = rot / 2;
     for (int i = lane; i < half; i += 32) {
         const float inv = (float)(1.0 / pow(base, (2.0 * i) / (double)rot));
@@ -128,27 +120,49 @@ __device__ __forceinline__ int dim_of(int lane, int j) {
     return DPL == 8 ? (j < 4 ? 4 * lane + j : 128 + 4 * lane + j - 4) : DPL * lane + j;
 }
 
-// Query head blockIdx.x < n_head of sequence blockIdx.y: normalised and rotated into the workspace;
+// Query head blockIdx.x < n_head of sequence blockIdx.y: normalised (candle's RmsNorm:
+// x / sqrt(mean(x^2) + eps) * w, the squares summed per lane then by a butterfly) and rotated into
+// the workspace;
 // blockIdx.x = n_head + j: kv head j's new k (normalised, rotated) and v into the caches at row len.
 // One warp each.
 __global__ void __launch_bounds__(32) k_attn_prep(AttnArgs p) {
     __shared__ float y[att::MAX_HD];
     const int lane = threadIdx.x, seq = blockIdx.y, hd = p.hd;
     pdl_wait();
+    // the length, the position, the head's row and its norm weights all requested at once (the row
+    // does not depend on the length; a length out of range still leaves before any write)
+    const bool qhead = (int)blockIdx.x < p.n_head;
+    const int kvh = qhead ? 0 : blockIdx.x - p.n_head;
+    const int64_t h = (int64_t)seq * p.n_head + (qhead ? blockIdx.x : 0);
+    const int64_t nr = ((int64_t)seq * p.n_kv + kvh) * hd;
+    const float* x = qhead ? p.qg + h * 2 * hd : p.k_new + nr;
+    const float* w = qhead ? p.q_norm_w : p.k_norm_w;
+    float xv[att::MAX_HD / 32], wv[att::MAX_HD / 32];
+#pragma unroll
+    for (int i = 0; i < att::MAX_HD / 32; ++i) {
+        const int d = lane + 32 * i;
+        xv[i] = d < hd ? x[d] : 0.f;
+        wv[i] = d < hd ? w[d] : 0.f;
+    }
     const int L = p.len[seq];
+    const int P = p.pos[seq];
     if (L < 0 || L >= p.cap) {
         if (lane == 0 && blockIdx.x == 0) dev_error(p.err, DE_SHAPE);
         return;
     }
-    const int P = p.pos[seq];
-    if ((int)blockIdx.x < p.n_head) {
-        const int64_t h = (int64_t)seq * p.n_head + blockIdx.x;
-        norm_rope_row(p.qg + h * 2 * hd, p.q_norm_w, hd, p.rot, p.eps, p.freq_base, P, y, lane);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < att::MAX_HD / 32; ++i) ss += xv[i] * xv[i];
+    ss = att_warp_sum(ss);
+    const float r = sqrtf(ss / (float)hd + p.eps);
+#pragma unroll
+    for (int i = 0; i < att::MAX_HD / 32; ++i)
+        if (lane + 32 * i < hd) y[lane + 32 * i] = xv[i] / r * wv[i];
+    __syncwarp();
+    rope_row(y, hd, p.rot, p.freq_base, P, lane);
+    if (qhead) {
         for (int d = lane; d < hd; d += 32) p.qn[h * hd + d] = y[d];
     } else {
-        const int kvh = blockIdx.x - p.n_head;
-        const int64_t nr = ((int64_t)seq * p.n_kv + kvh) * hd;
-        norm_rope_row(p.k_new + nr, p.k_norm_w, hd, p.rot, p.eps, p.freq_base, P, y, lane);
         const int64_t row = (((int64_t)seq * p.n_kv + kvh) * p.cap + L) * hd;
         for (int d = lane; d < hd; d += 32) {
             p.k_cache[row + d] = y[d];
