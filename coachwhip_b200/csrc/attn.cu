@@ -362,6 +362,8 @@ __global__ void __launch_bounds__(CW * 32) k_attn_combine(AttnArgs p) {
     const int h = blockIdx.x, seq = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr int hd = 32 * DPL;
     pdl_wait();
+    // (the gate value of this thread's output, requested with the length)
+    const float gt = tid < hd ? p.qg[((int64_t)seq * p.n_head + h) * 2 * hd + hd + tid] : 0.f;
     const int L = p.len[seq];
     if (L < 0 || L >= p.cap) return;  // (recorded by k_attn_prep)
     const int g = p.n_head / p.n_kv, kvh = h / g, hh = h % g;
@@ -400,7 +402,6 @@ __global__ void __launch_bounds__(CW * 32) k_attn_combine(AttnArgs p) {
             o += red[w][tid];
             D += dred[w];
         }
-        const float gt = p.qg[((int64_t)seq * p.n_head + h) * 2 * hd + hd + tid];
         p.out[((int64_t)seq * p.n_head + h) * hd + tid] = (o / D) * (1.0f / (1.0f + expf(-gt)));
     }
 }
