@@ -226,9 +226,18 @@ __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
         lh[tid] = 0.f;
     }
     constexpr int G4 = G < 4 ? 4 : G;
-    float acc[G4];  // thread d: value d of every query head's running weighted sum
+    // the weighted sum of V: thread t takes DPT values d0 .. of the rows of its row group (all
+    // threads busy at every head dim; the groups' sums are added once, after the last chunk)
+    constexpr int DPT = DPL == 8 ? 2 : 1;      // values per thread
+    constexpr int TPR = 32 * DPL / DPT;        // threads per row group (hd / DPT)
+    constexpr int NRG = T / TPR;               // row groups: 2 (hd 256, 128) or 4 (hd 64)
+    constexpr int RG = CHUNK / NRG;            // rows per group
+    const int rg = tid / TPR, d0 = (tid % TPR) * DPT;
+    float acc[G4][DPT];  // the running weighted sums of its values, per query head
 #pragma unroll
-    for (int hh = 0; hh < G4; ++hh) acc[hh] = 0.f;
+    for (int hh = 0; hh < G4; ++hh)
+#pragma unroll
+        for (int k = 0; k < DPT; ++k) acc[hh][k] = 0.f;
     __syncthreads();  // (the barrier's init is visible to every waiting thread)
 
     // chunk i: wait for its K rows, score them, start chunk i+1's K rows; softmax; wait for its V
@@ -310,26 +319,40 @@ __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
             if (c1 < pend) mbar_wait(&bar[0], ph ^ 1, p.err);
             return;
         }
-        if (tid < hd) {
+        {
             const float4* s4 = reinterpret_cast<const float4*>(sc);
 #pragma unroll
             for (int q4 = 0; q4 < G4 / 4; ++q4) {
                 const float4 f = s4[q4];
-                acc[4 * q4 + 0] *= f.x;
-                acc[4 * q4 + 1] *= f.y;
-                acc[4 * q4 + 2] *= f.z;
-                acc[4 * q4 + 3] *= f.w;
+#pragma unroll
+                for (int k = 0; k < DPT; ++k) {
+                    acc[4 * q4 + 0][k] *= f.x;
+                    acc[4 * q4 + 1][k] *= f.y;
+                    acc[4 * q4 + 2][k] *= f.z;
+                    acc[4 * q4 + 3][k] *= f.w;
+                }
             }
-            for (int row = 0; row < n; ++row) {
-                const float vv = Vs[row * hd + tid];
+            const int row1 = min(n, (rg + 1) * RG);
+            for (int row = rg * RG; row < row1; ++row) {
+                float vv[DPT];
+                if (DPT == 2) {
+                    const float2 t2 = *reinterpret_cast<const float2*>(Vs + row * hd + d0);
+                    vv[0] = t2.x;
+                    vv[DPT - 1] = t2.y;
+                } else {
+                    vv[0] = Vs[row * hd + d0];
+                }
                 const float4* w4 = reinterpret_cast<const float4*>(pw[row]);
 #pragma unroll
                 for (int q4 = 0; q4 < G4 / 4; ++q4) {  // (columns past g hold stale values: never stored)
                     const float4 w = w4[q4];
-                    acc[4 * q4 + 0] += w.x * vv;
-                    acc[4 * q4 + 1] += w.y * vv;
-                    acc[4 * q4 + 2] += w.z * vv;
-                    acc[4 * q4 + 3] += w.w * vv;
+#pragma unroll
+                    for (int k = 0; k < DPT; ++k) {
+                        acc[4 * q4 + 0][k] += w.x * vv[k];
+                        acc[4 * q4 + 1][k] += w.y * vv[k];
+                        acc[4 * q4 + 2][k] += w.z * vv[k];
+                        acc[4 * q4 + 3][k] += w.w * vv[k];
+                    }
                 }
             }
         }
@@ -337,12 +360,30 @@ __global__ void __launch_bounds__(att::T, 2) k_attn_part(AttnArgs p) {
         if (tid == 0 && c1 < pend) issue_v(c1);
     }
 
-    const int64_t part_i = ((int64_t)seq * p.n_kv + kvh) * p.n_split + r;
-    if (tid < hd) {
-        float* part = p.part + part_i * g * hd;
+    // the row groups' sums, added in group order (the K and V buffers, contiguous, are free: no copy
+    // is in flight)
+    static_assert((NRG - 1) * G <= 2 * CHUNK, "row-group sums fit in the K and V buffers");
+    float* red = Ks;
+    if (rg > 0) {
 #pragma unroll
         for (int hh = 0; hh < G; ++hh)
-            if (EXACT || hh < g) part[hh * hd + tid] = acc[hh];
+#pragma unroll
+            for (int k = 0; k < DPT; ++k) red[((rg - 1) * G + hh) * hd + d0 + k] = acc[hh][k];
+    }
+    __syncthreads();
+    const int64_t part_i = ((int64_t)seq * p.n_kv + kvh) * p.n_split + r;
+    if (rg == 0) {
+        float* part = p.part + part_i * g * hd;
+#pragma unroll
+        for (int hh = 0; hh < G; ++hh) {
+            if (!EXACT && hh >= g) break;
+#pragma unroll
+            for (int k = 0; k < DPT; ++k) {
+                float v = acc[hh][k];
+                for (int r2 = 1; r2 < NRG; ++r2) v += red[((r2 - 1) * G + hh) * hd + d0 + k];
+                part[hh * hd + d0 + k] = v;
+            }
+        }
     }
     if (tid < g) {
         p.ml[(part_i * g + tid) * 2] = mh[tid];
